@@ -1,0 +1,455 @@
+#!/usr/bin/env python
+"""Benchmark of the KV offload/reload hot path (config C1, Llama-3-8B KV tier).
+
+One step = offload one 512-block batch (extract kernel HBM pages -> HBM
+staging, copy-engine DMA -> pinned host tier) and reload another 512-block
+batch (DMA host tier -> staging, insert kernel -> HBM pages), both directions
+in flight together.  A block is 2 MiB (32 layers x K/V x 16 tokens x 8 heads x
+128 x bf16), so a step moves 1 GiB each way over PCIe.
+
+  value      offload + reload bytes of all ranks / device time (CUDA events,
+             max over ranks), through the C ABI manager with the pool resident
+             in HBM and block lists prepared before the timed region
+  e2e        the same through the Python KVCacheManager.d2h/h2d API from
+             Python lists, Await() on each step, host wall clock
+  roofline   the extract kernel (dominant kernel): algorithmic bytes
+             (read + write of every moved block) / its device time, timed live
+             with CUDA events around every launch in the timed region
+  pcie       achieved D2H / H2D GB/s of the step against pinned-memcpy peaks
+             measured in this run and the Gen5 x16 spec (64 GB/s)
+  cpu_baseline  the reference's host copy loops restated in C (oracle/cpu_ref.c)
+             on this box's host cores, on a bounded sample of the workload
+
+`--impl reference` times that CPU restatement alone (rank 0; other ranks exit).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "KV offload/reload GB/s per GPU vs PCIe peak; extract HBM GB/s; 8B weight-sync s"
+GIB = 1 << 30
+PCIE_SPEC_GBS = 64.0
+
+
+def parse():
+  p = argparse.ArgumentParser()
+  p.add_argument("--gpus", type=int, default=1)
+  p.add_argument("--steps", type=int, default=10)
+  p.add_argument("--warmup", type=int, default=3)
+  p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+  p.add_argument("--batch", type=int, default=512)
+  p.add_argument("--pool-blocks", type=int, default=32768)
+  p.add_argument("--host-blocks", type=int, default=0, help="0 = size to host RAM")
+  p.add_argument("--cpu-sample-s", type=float, default=10.0)
+  p.add_argument("--no-cpu-baseline", action="store_true")
+  return p.parse_args()
+
+
+def peaks():
+  try:
+    return json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+  except Exception:
+    return {}
+
+
+def mem_available_bytes() -> int:
+  try:
+    for line in open("/proc/meminfo"):
+      if line.startswith("MemAvailable:"):
+        return int(line.split()[1]) * 1024
+  except OSError:
+    pass
+  return 64 * GIB
+
+
+def cpu_model() -> str:
+  try:
+    for line in open("/proc/cpuinfo"):
+      if line.startswith("model name"):
+        return line.split(":", 1)[1].strip()
+  except OSError:
+    pass
+  return "unknown"
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+  QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+           "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+           "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+  def __init__(self, device_index: int):
+    self.dev = device_index
+    self.proc = None
+    self.lines = []
+
+  def start(self):
+    try:
+      self.proc = subprocess.Popen(
+          ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+           "-lms", "200", "-i", str(self.dev)], stdout=subprocess.PIPE,
+          stderr=subprocess.DEVNULL, text=True)
+      self.thread = threading.Thread(target=self._read, daemon=True)
+      self.thread.start()
+    except OSError:
+      self.proc = None
+
+  def _read(self):
+    for line in self.proc.stdout:
+      self.lines.append(line.strip())
+
+  def stop(self):
+    if self.proc is None:
+      return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+    self.proc.terminate()
+    try:
+      self.proc.wait(timeout=5)
+    except subprocess.TimeoutExpired:
+      self.proc.kill()
+    sm, smax, reasons = [], None, set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for line in self.lines:
+      f = [x.strip() for x in line.split(",")]
+      if len(f) < 9:
+        continue
+      try:
+        sm.append(float(f[1]))
+        smax = float(f[2])
+      except ValueError:
+        continue
+      for name, val in zip(names, f[5:9]):
+        if val.lower() == "active":
+          reasons.add(name)
+    return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+            "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU arms (oracle restatement of the reference host loops)
+# ---------------------------------------------------------------------------
+
+def cpu_offload_reload(batch: int, seconds: float, steps: int = 0, warmup: int = 0):
+  """Times the reference host loops (restated in C) for offload + reload of
+  `batch` C1 blocks between a host "device" pool and a host tier."""
+  from oracle import cpu_ref
+  from tpu_sync_b200 import workloads
+  g = workloads.C1
+  S, bb = g.storages, g.storage_block_bytes
+  pool_blocks = max(2 * batch, 256)
+  threads = cpu_ref.host_threads()
+  rng = np.random.default_rng(10)
+  dev = [np.empty(pool_blocks * bb, np.uint8) for _ in range(S)]
+  host = [np.empty(pool_blocks * bb, np.uint8) for _ in range(S)]
+  for a in dev + host:
+    a.fill(1)
+  half = pool_blocks // 2
+
+  def one_step():
+    src = np.sort(rng.choice(half, batch, replace=False))
+    dst = rng.choice(pool_blocks, batch, replace=False)
+    ones = np.ones(batch, np.int64)
+    cpu_ref.copy_runs(host, dev, [bb] * S, src, dst, ones, threads)      # D2H
+    hs = rng.choice(pool_blocks, batch, replace=False)
+    ds = half + rng.choice(pool_blocks - half, batch, replace=False)
+    cpu_ref.copy_runs(dev, host, [bb] * S, hs, ds, ones, threads)        # H2D
+
+  for _ in range(warmup):
+    one_step()
+  times = []
+  t_end = time.perf_counter() + seconds
+  while (steps and len(times) < steps) or (not steps and (time.perf_counter() < t_end or
+                                                          len(times) < 2)):
+    t0 = time.perf_counter()
+    one_step()
+    times.append(time.perf_counter() - t0)
+  step_bytes = 2 * batch * g.block_bytes
+  per_step = statistics.mean(times)
+  return {"value": round(step_bytes / per_step / 1e9, 3), "unit": "GB/s", "cores": threads,
+          "ms_per_step": per_step * 1e3, "steps": len(times),
+          "sample": (f"offload {batch} + reload {batch} C1 blocks (2 MiB each) per step "
+                     f"between a {pool_blocks}-block host-resident pool and host tier, "
+                     f"{len(times)} steps, memcpy per (storage, run) as "
+                     f"DispatchD2hWork/DispatchH2dWork on the CPU client"),
+          "cpu": cpu_model()}
+
+
+def run_reference(args):
+  rank = int(os.environ.get("RANK", "0"))
+  if rank != 0:
+    return
+  r = cpu_offload_reload(args.batch, 0.0, steps=args.steps, warmup=args.warmup)
+  line = {"impl": "reference", "metric": METRIC, "value": r["value"], "unit": "GB/s",
+          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+          "ms_per_step": round(r["ms_per_step"], 3), "higher_is_better": True,
+          "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+          "data": "synthetic (host-resident pool standing in for the CPU client's device)",
+          "config": {"workload": "C1 Llama-3-8B KV tier offload/reload (CPU restatement)",
+                     "batch": args.batch},
+          "cpu_baseline": {"value": r["value"], "unit": "GB/s", "cores": r["cores"],
+                           "kind": "port", "sample": r["sample"]},
+          "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
+                  "d2h_bytes_per_step": 0}}
+  print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def measure_pcie(torch, device, nbytes=GIB):
+  """Best-of-3 pinned cudaMemcpyAsync D2H, H2D and both at once (GB/s)."""
+  d = torch.empty(nbytes, dtype=torch.uint8, device=device)
+  d2 = torch.empty(nbytes, dtype=torch.uint8, device=device)
+  h = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+  h2 = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+  s1, s2 = torch.cuda.Stream(device), torch.cuda.Stream(device)
+  out = {}
+  for name in ("d2h", "h2d", "duplex"):
+    best = 0.0
+    for _ in range(3):
+      torch.cuda.synchronize(device)
+      e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+      e2 = torch.cuda.Event(enable_timing=True)
+      e0.record(s1)
+      s2.wait_event(e0)
+      if name in ("d2h", "duplex"):
+        with torch.cuda.stream(s1):
+          h.copy_(d, non_blocking=True)
+      if name in ("h2d", "duplex"):
+        with torch.cuda.stream(s2):
+          d2.copy_(h2, non_blocking=True)
+      e2.record(s2)
+      s1.wait_event(e2)
+      e1.record(s1)
+      torch.cuda.synchronize(device)
+      ms = e0.elapsed_time(e1)
+      moved = nbytes * (2 if name == "duplex" else 1)
+      best = max(best, moved / (ms * 1e-3) / 1e9)
+    out[name] = round(best, 2)
+  del d, d2, h, h2
+  return out
+
+
+def run_ours(args):
+  import torch
+  import torch.distributed as dist
+
+  from tpu_sync_b200 import KVCacheManager, ops, workloads
+
+  world = int(os.environ.get("WORLD_SIZE", "1"))
+  rank = int(os.environ.get("RANK", "0"))
+  local = int(os.environ.get("LOCAL_RANK", "0"))
+  torch.cuda.set_device(local)
+  device = torch.device("cuda", local)
+  if world > 1:
+    from datetime import timedelta
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                            device_id=device)
+
+  def barrier():
+    if world > 1:
+      dist.barrier()
+
+  def max_over_ranks(x: float) -> float:
+    if world == 1:
+      return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+  g = workloads.C1
+  B = args.batch
+  pool_blocks = args.pool_blocks
+  # Pool: [layers, K/V, blocks, 16, 8, 128] bf16, N(0,1) generated on device.
+  gen = torch.Generator(device=device).manual_seed(10 + rank)
+  full = torch.empty((g.layers, g.kv, pool_blocks, g.block_tokens, g.heads, g.head_dim),
+                     dtype=torch.bfloat16, device=device)
+  for l in range(g.layers):
+    full[l].normal_(generator=gen)
+  storages = [full[l, k] for l in range(g.layers) for k in range(g.kv)]
+
+  # Host tier: as large as requested, bounded by this box's RAM share.
+  pitch = g.block_bytes
+  want_host = args.host_blocks or 8192
+  local_ranks = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+  fit = int(0.45 * mem_available_bytes() / max(local_ranks, 1) // pitch)
+  host_blocks = max(4 * B, min(want_host, fit))
+  mgr = KVCacheManager([[t] for t in storages], host_blocks_to_allocate=host_blocks)
+
+  pcie = measure_pcie(torch, device)
+
+  # Step plans: offload from the first half of the pool into the first half
+  # of the host tier; reload from the second half of the tier into the second
+  # half of the pool (disjoint sets, as evicted and admitted blocks are).
+  rng = np.random.default_rng(100 + rank)
+  half_pool, half_host = pool_blocks // 2, host_blocks // 2
+  plans = []
+  for _ in range(args.warmup + args.steps):
+    plans.append((rng.choice(half_pool, B, replace=False),
+                  rng.choice(half_host, B, replace=False),
+                  half_host + rng.choice(host_blocks - half_host, B, replace=False),
+                  half_pool + rng.choice(pool_blocks - half_pool, B, replace=False)))
+  step_bytes = 2 * B * pitch
+  bench_stream = torch.cuda.Stream(device)
+
+  def step(plan, stream):
+    f1 = mgr.d2h(plan[0], plan[1], stream=stream)
+    f2 = mgr.h2d(plan[2], plan[3], stream=stream)
+    f1.stream_wait(stream)
+    f2.stream_wait(stream)
+    return f1, f2
+
+  # ---- device-timed steps (value) ----
+  for i in range(args.warmup):
+    for f in step(plans[i], bench_stream):
+      f.Await()
+  torch.cuda.synchronize(device)
+  barrier()
+  torch.cuda.synchronize(device)
+  mgr.set_profiling(True)
+  mgr.kernel_stats("extract")
+  mgr.kernel_stats("insert")
+  clocks = ClockSampler(device.index)
+  clocks.start()
+  e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+  e0.record(bench_stream)
+  futs = []
+  for i in range(args.warmup, args.warmup + args.steps):
+    futs.extend(step(plans[i], bench_stream))
+  e1.record(bench_stream)
+  torch.cuda.synchronize(device)
+  clock_info = clocks.stop()
+  barrier()
+  for f in futs:
+    f.Await()
+  dev_ms = e0.elapsed_time(e1)
+  mgr.set_profiling(False)
+  ext = mgr.kernel_stats("extract")
+  ins = mgr.kernel_stats("insert")
+  max_ms = max_over_ranks(dev_ms)
+  ms_per_step = max_ms / args.steps
+  value = world * step_bytes * args.steps / (max_ms * 1e-3) / 1e9
+
+  # ---- standalone extract of a whole batch in one launch (HBM GB/s) ----
+  table = ops.StorageTable(storages)
+  staging = table.new_staging(B)
+  big_ids = torch.from_numpy(plans[0][0].astype(np.int64)).to(device)
+  for _ in range(3):
+    ops.kv_extract(table, big_ids, staging)
+  torch.cuda.synchronize(device)
+  xs = []
+  for i in range(5):
+    ids_i = torch.from_numpy(plans[i % len(plans)][0].astype(np.int64)).to(device)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    ops.kv_extract(table, ids_i, staging)
+    b.record()
+    torch.cuda.synchronize(device)
+    xs.append(a.elapsed_time(b))
+  extract_one_launch_gbs = 2 * B * pitch / (statistics.median(xs) * 1e-3) / 1e9
+  del staging
+
+  # ---- end to end through the public Python API ----
+  barrier()
+  lists = [[p[0].tolist(), p[1].tolist(), p[2].tolist(), p[3].tolist()] for p in plans]
+  torch.cuda.synchronize(device)
+  t0 = time.perf_counter()
+  for i in range(args.warmup, args.warmup + args.steps):
+    a = mgr.d2h(lists[i][0], lists[i][1])
+    b = mgr.h2d(lists[i][2], lists[i][3])
+    a.Await()
+    b.Await()
+  wall = time.perf_counter() - t0
+  wall = max_over_ranks(wall)
+  e2e_value = world * step_bytes * args.steps / wall / 1e9
+  idx_bytes = 2 * 2 * B * 8  # two int64 lists per direction
+
+  # ---- roofline of the dominant kernel (extract) ----
+  pk = peaks()
+  hbm_peak = pk.get("hbm_gbs")
+  peak_src = "measured (MEASURED_PEAKS.json hbm_gbs)"
+  if not hbm_peak:
+    hbm_peak, peak_src = 6650.0, "fallback"
+  achieved = ext["bytes"] / (ext["ms"] * 1e-3) / 1e9 if ext["ms"] > 0 else 0.0
+  per_launch_bytes = ext["bytes"] / max(ext["launches"], 1)
+
+  # ---- CPU baseline (rank 0, N=1) ----
+  cpu = None
+  if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    cpu = cpu_offload_reload(B, args.cpu_sample_s)
+
+  d2h_gbs = B * pitch / (ms_per_step * 1e-3) / 1e9
+  if rank == 0:
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic N(0,1) bf16 KV pool generated on device (seed 10+rank)",
+        "config": {
+            "workload": ("C1 Llama-3-8B KV tier: 32 layers x K/V, 16-token blocks of "
+                         "8 heads x 128 bf16 (2 MiB per block), offload 512 + reload 512 "
+                         "blocks per step, both directions in flight"),
+            "pool_blocks": pool_blocks, "pool_gib": round(full.numel() * 2 / GIB, 1),
+            "host_tier_blocks": host_blocks,
+            "host_tier_gib": round(host_blocks * pitch / GIB, 1),
+            "batch": B, "l2": "inputs larger than L2 (1 GiB of random blocks per direction per step)",
+            "parallelism": f"replicas x{world}"},
+        "per_gpu_gbs": round(value / world, 3),
+        "pcie": {"offload_d2h_gbs": round(d2h_gbs, 2), "reload_h2d_gbs": round(d2h_gbs, 2),
+                 "measured_peak": pcie, "spec_gbs_per_dir": PCIE_SPEC_GBS,
+                 "frac_of_measured_duplex": round(2 * d2h_gbs / pcie["duplex"], 3)
+                 if pcie.get("duplex") else None,
+                 "frac_of_spec": round(d2h_gbs / PCIE_SPEC_GBS, 3)},
+        "roofline": {"bound": "hbm", "kernel": "extract (block_copy_vec_kernel, to staging)",
+                     "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 3), "peak_source": peak_src,
+                     "launches": ext["launches"],
+                     "bytes_per_launch": int(per_launch_bytes),
+                     "avg_launch_us": round(ext["ms"] * 1e3 / max(ext["launches"], 1), 2),
+                     "traffic": None,
+                     "insert_achieved": round(ins["bytes"] / (ins["ms"] * 1e-3) / 1e9, 1)
+                     if ins["ms"] > 0 else None},
+        "extract_hbm_gbs_one_launch": round(extract_one_launch_gbs, 1),
+        "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
+                "h2d_bytes_per_step": B * pitch + idx_bytes,
+                "d2h_bytes_per_step": B * pitch,
+                "how": "KVCacheManager.d2h/h2d from Python lists, Await() per step, wall clock"},
+        "gpu_launches": ext["launches"] + ins["launches"],
+        "clocks": clock_info,
+        "cpu_baseline": None if cpu is None else {
+            "value": cpu["value"], "unit": "GB/s", "cores": cpu["cores"], "kind": "port",
+            "sample": cpu["sample"], "cpu": cpu["cpu"]},
+    }
+    print(json.dumps(line), flush=True)
+  mgr.close()
+  if world > 1:
+    dist.destroy_process_group()
+
+
+def main():
+  args = parse()
+  if args.impl == "reference":
+    run_reference(args)
+  else:
+    run_ours(args)
+
+
+if __name__ == "__main__":
+  main()

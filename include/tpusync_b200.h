@@ -1,0 +1,293 @@
+/*
+ * tpusync_b200.h -- C ABI of the B200-native tpu_sync data-movement hot path.
+ *
+ * Every entry point is `extern "C"`, takes plain pointers and sizes, never
+ * throws and returns a status code (ts_status).  The last error message of
+ * the calling thread is available through ts_last_error().
+ *
+ * Units follow the reference: block offsets are "major-dim" units (one block of
+ * one (layer, shard) storage = its dim-0 slice), byte offsets are bytes.
+ *
+ * Device pointers are CUDA device addresses of the device given in the call;
+ * `stream` arguments are cudaStream_t handles (NULL = legacy default stream).
+ */
+#ifndef TPUSYNC_B200_H_
+#define TPUSYNC_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TS_API __attribute__((visibility("default")))
+#else
+#define TS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes: the absl::StatusCode values the reference returns
+ * (tpu_sync/kv_cache/kv_cache_manager_base.cc:72-102, :2005-2012, :2096-2103). */
+typedef enum ts_status {
+  TS_OK = 0,
+  TS_CANCELLED = 1,
+  TS_UNKNOWN = 2,
+  TS_INVALID_ARGUMENT = 3,
+  TS_DEADLINE_EXCEEDED = 4,
+  TS_NOT_FOUND = 5,
+  TS_ALREADY_EXISTS = 6,
+  TS_RESOURCE_EXHAUSTED = 8,
+  TS_FAILED_PRECONDITION = 9,
+  TS_OUT_OF_RANGE = 11,
+  TS_UNIMPLEMENTED = 12,
+  TS_INTERNAL = 13,
+  TS_UNAVAILABLE = 14,
+  /* not an error: returned by ts_event_query while the work is in flight */
+  TS_PENDING = 100
+} ts_status;
+
+/* Thread-local message of the last failed call on this thread ("" if none). */
+TS_API const char* ts_last_error(void);
+
+/* Library version string. */
+TS_API const char* ts_version(void);
+
+/* ------------------------------------------------------------------------ */
+/* Pure host logic (no CUDA calls; usable on a machine without a GPU).       */
+/* ------------------------------------------------------------------------ */
+
+/* Replaces ValidateOffsetsAndSizes (tpu_sync/kv_cache/kv_cache_manager_base.cc:72-102).
+ * n_dst / n_sizes may be 0 (= "not given", as in the reference). */
+TS_API int ts_validate_copy_spec(const int64_t* src, int64_t n_src, const int64_t* dst,
+                          int64_t n_dst, const int64_t* sizes, int64_t n_sizes);
+
+/* Replaces CoalesceMajorDimCopies (tpu_sync/kv_cache/kv_cache_manager_base.cc:121-141):
+ * merges copy i into the previous run when both its src and dst continue it.
+ * Outputs must hold n entries; *n_out receives the run count. */
+TS_API int ts_coalesce_runs(const int64_t* src, const int64_t* dst, const int64_t* sizes,
+                     int64_t n, int64_t* out_src, int64_t* out_dst,
+                     int64_t* out_sizes, int64_t* n_out);
+
+/* ------------------------------------------------------------------------ */
+/* Block-movement kernels (manager-free).                                    */
+/* ------------------------------------------------------------------------ */
+
+/* One (layer, shard) storage as the kernels see it: a device buffer whose
+ * dim-0 slices are blocks of `block_bytes` bytes, and the byte offset of this
+ * storage's slot inside one staging block.  Lives in DEVICE memory when passed
+ * to the kernels below (an array of n_storages entries, 16-byte aligned). */
+typedef struct ts_block_storage {
+  uint64_t dev_ptr;      /* device address of block 0 */
+  uint64_t block_bytes;  /* bytes of one block of this storage */
+  uint64_t dev_bytes;    /* bytes of the storage on the device (bounds check) */
+  uint64_t stage_off;    /* byte offset of this storage inside a staging block */
+} ts_block_storage;
+
+/* Extract (gather): staging[k*stage_pitch + st[s].stage_off + b] =
+ *   storage s block ids[k], byte b; for every k < n_blocks, s < n_storages.
+ * `ids` is a device array of n_blocks int64.  The staging layout is
+ * block-major: one staging block holds that block of every storage
+ * (the "[blocks, layers, K/V, ...]" staging of the reference's configs).
+ * Replaces the per-(storage, run) DMA loop of DispatchD2hWork
+ * (tpu_sync/kv_cache/kv_cache_manager_base.cc:2036-2124) on the device side.
+ * `err_flag` (device or host-mapped int, may be 0) receives 1 when an id is
+ * out of the storage's bounds (that block is skipped). */
+TS_API int ts_kv_extract(int device, const ts_block_storage* d_storages, int n_storages,
+                  const int64_t* d_ids, int64_t n_blocks, void* d_staging,
+                  uint64_t stage_pitch, int* err_flag, void* stream);
+
+/* Insert (scatter), the inverse of ts_kv_extract; replaces DispatchH2dWork's
+ * per-run copies (tpu_sync/kv_cache/kv_cache_manager_base.cc:1945-2033). */
+TS_API int ts_kv_insert(int device, const ts_block_storage* d_storages, int n_storages,
+                 const int64_t* d_ids, int64_t n_blocks, const void* d_staging,
+                 uint64_t stage_pitch, int* err_flag, void* stream);
+
+/* Fused extract + bf16 -> fp8 e4m3 cast.  Storages hold bf16; per (block,
+ * storage) one fp32 scale = absmax/448 (1 if absmax is 0) is written to
+ * staging[k*stage_pitch + scale_off + 4*s] and the payload
+ * e4m3_rn_satfinite(x / scale) to staging[k*stage_pitch + st[s].stage_off ...]
+ * (block_bytes/2 bytes).  No reference counterpart (new in this build). */
+TS_API int ts_kv_extract_fp8(int device, const ts_block_storage* d_storages,
+                      int n_storages, const int64_t* d_ids, int64_t n_blocks,
+                      void* d_staging, uint64_t stage_pitch, uint64_t scale_off,
+                      int* err_flag, void* stream);
+
+/* Inverse of ts_kv_extract_fp8: x = bf16_rn(float(q) * scale). */
+TS_API int ts_kv_insert_fp8(int device, const ts_block_storage* d_storages,
+                     int n_storages, const int64_t* d_ids, int64_t n_blocks,
+                     const void* d_staging, uint64_t stage_pitch,
+                     uint64_t scale_off, int* err_flag, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Strided chunk copy (weight-sync reshard executor).                        */
+/* ------------------------------------------------------------------------ */
+
+/* One strided chunk of the reshard plan, in ELEMENTS of the source/dest
+ * tensors: count rows of `size` elements from src + src_off + c*src_stride to
+ * dst + dst_off + c*dst_stride.  The reference's ShardPushEntryProto carries the
+ * same six numbers in bytes of one dtype (tpu_sync/rpc/raiden_service.proto:105-131,
+ * expansion in tpu_sync/weight_sync/weight_synchronizer_base.cc:606-667);
+ * elements are used so a chunk can change dtype on the way. */
+typedef struct ts_reshard_chunk {
+  uint64_t src_ptr;     /* device address of the source tensor (element 0) */
+  uint64_t dst_ptr;     /* device address (local or peer) of the destination */
+  int64_t src_off;
+  int64_t dst_off;
+  int64_t size;
+  int64_t src_stride;
+  int64_t dst_stride;
+  int64_t count;
+} ts_reshard_chunk;
+
+typedef enum ts_dtype {
+  TS_DTYPE_U8 = 0,   /* raw bytes */
+  TS_DTYPE_BF16 = 1,
+  TS_DTYPE_F32 = 2,
+  TS_DTYPE_F16 = 3
+} ts_dtype;
+
+/* Executes n_chunks chunks (device array `d_chunks`) on `device`, converting
+ * src_dtype -> dst_dtype (identity, or F32 -> BF16 round-to-nearest-even).
+ * Destinations may be peer-GPU addresses (P2P stores over NVLink).
+ * `d_row_prefix` is a device int64 array of n_chunks+1 entries: the prefix sum
+ * of the per-chunk work items as computed by ts_reshard_work_items(). */
+TS_API int ts_reshard_work_items(const ts_reshard_chunk* h_chunks, int64_t n_chunks,
+                          int src_dtype, int dst_dtype, int64_t* h_prefix_out);
+TS_API int ts_reshard_copy(int device, const ts_reshard_chunk* d_chunks,
+                    const int64_t* d_item_prefix, int64_t n_chunks,
+                    int64_t n_items, int src_dtype, int dst_dtype, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Paged KV relayout (disaggregated prefill -> decode hand-off).             */
+/* ------------------------------------------------------------------------ */
+
+/* Geometry of one paged KV storage.  A block holds `block_tokens` tokens of
+ * `heads` heads of `head_bytes` bytes, ordered head-major ([heads][tokens])
+ * when head_major != 0 else token-major ([tokens][heads]). */
+typedef struct ts_page_geometry {
+  int64_t block_tokens;
+  int64_t heads;
+  int64_t head_bytes;
+  int32_t head_major;
+  int32_t pad_;
+} ts_page_geometry;
+
+/* For every storage s (n_storages pairs of device base addresses, src_bases[s]
+ * and dst_bases[s], device arrays of uint64), every sequence q < n_seqs and
+ * token t < seq_tokens: copies each head vector of token t from source block
+ * src_table[q*src_table_stride + t/src.block_tokens] to destination block
+ * dst_table[q*dst_table_stride + t/dst.block_tokens] in the destination order.
+ * src.heads == dst.heads and src.head_bytes == dst.head_bytes are required.
+ * Destination addresses may be a peer GPU's (P2P stores). */
+TS_API int ts_kv_relayout(int device, const uint64_t* d_src_bases,
+                   const uint64_t* d_dst_bases, int n_storages,
+                   ts_page_geometry src, ts_page_geometry dst,
+                   const int32_t* d_src_table, int64_t src_table_stride,
+                   const int32_t* d_dst_table, int64_t dst_table_stride,
+                   int64_t n_seqs, int64_t seq_tokens, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Pinned host tier.                                                         */
+/* ------------------------------------------------------------------------ */
+
+typedef struct ts_host_tier ts_host_tier;
+
+/* Allocates `bytes` of DMA-registered host memory: anonymous mmap, or a
+ * /dev/shm segment when shm_name is non-empty, registered with
+ * cudaHostRegister (Portable|Mapped).  Replaces XlaHostMemoryAllocator /
+ * SharedMemoryHostMemoryAllocator (tpu_sync/core/host_memory_allocator.cc:125-196,
+ * :217-407).  `register_with_cuda` = 0 skips the CUDA registration (CPU use).
+ * *warm_out = 1 when an existing /dev/shm segment with the same name,
+ * model_uid and geometry was attached (warm boot). */
+TS_API int ts_host_tier_create(uint64_t bytes, const char* shm_name,
+                        const char* model_uid, uint64_t geometry_tag,
+                        int register_with_cuda, ts_host_tier** out,
+                        int* warm_out);
+TS_API void* ts_host_tier_ptr(ts_host_tier* tier);
+TS_API uint64_t ts_host_tier_bytes(ts_host_tier* tier);
+TS_API int ts_host_tier_destroy(ts_host_tier* tier, int unlink_shm);
+
+/* ------------------------------------------------------------------------ */
+/* KV cache manager (replaces KVCacheManagerBase's device path).            */
+/* ------------------------------------------------------------------------ */
+
+typedef struct ts_manager ts_manager;
+typedef struct ts_event ts_event;
+
+typedef struct ts_storage_desc {
+  uint64_t dev_ptr;   /* device address of the (layer, shard) storage */
+  uint64_t nbytes;    /* its on-device size in bytes */
+  int64_t dim0;       /* its dim-0 extent (number of blocks) */
+  int32_t device;     /* CUDA device ordinal */
+  int32_t pad_;
+} ts_storage_desc;
+
+typedef struct ts_manager_opts {
+  int64_t host_blocks;         /* host tier capacity in blocks (reference default 64) */
+  int64_t chunk_blocks;        /* blocks per pipelined staging chunk (0 = default) */
+  const char* shm_name;        /* "" / NULL = anonymous pinned memory */
+  const char* model_uid;       /* stored in the /dev/shm header */
+  int32_t fp8;                 /* 1: host tier holds fp8 e4m3 + per-block scales */
+  int32_t pad_;
+} ts_manager_opts;
+
+/* Creates a manager over num_layers x num_shards storages (row-major
+ * [layer][shard]).  Replaces the device-backed KVCacheManagerBase constructor
+ * (tpu_sync/kv_cache/kv_cache_manager_base.cc:223-372): block bytes of layer l
+ * = nbytes(l) / dim0(layer 0) (layer_block_byte_size, kv_cache_manager_base.h:434-439),
+ * host mirror of host_blocks blocks per storage. */
+TS_API int ts_mgr_create(const ts_storage_desc* storages, int num_layers,
+                  int num_shards, const ts_manager_opts* opts,
+                  ts_manager** out);
+TS_API int ts_mgr_destroy(ts_manager* mgr);
+
+/* Device -> host tier: KVCacheManagerBase::D2h
+ * (tpu_sync/kv_cache/kv_cache_manager_base.cc:2616 -> :792 -> :652 -> :2036).
+ * n == 0 means "whole storages" as in the reference.  layer_idx / shard_idx
+ * = -1 mean all.  The copy is ordered after the work already queued on
+ * `stream`.  *out receives an event handle to query/wait/release. */
+TS_API int ts_d2h(ts_manager* mgr, const int64_t* src, const int64_t* dst,
+           const int64_t* sizes, int64_t n_src, int64_t n_dst, int64_t n_sizes,
+           int64_t layer_idx, int64_t shard_idx, void* stream, ts_event** out);
+
+/* Host tier -> device: KVCacheManagerBase::H2d
+ * (tpu_sync/kv_cache/kv_cache_manager_base.cc:2575 -> :518 -> :1945). */
+TS_API int ts_h2d(ts_manager* mgr, const int64_t* src, const int64_t* dst,
+           const int64_t* sizes, int64_t n_src, int64_t n_dst, int64_t n_sizes,
+           int64_t layer_idx, int64_t shard_idx, void* stream, ts_event** out);
+
+/* Host address of (layer, shard, host block) and the layout of the tier.
+ * Replaces GetBlockHostPointerValue (kv_cache/kv_cache_manager_base.h:358-362). */
+TS_API int ts_mgr_host_block_ptr(ts_manager* mgr, int64_t layer_idx, int64_t shard_idx,
+                          int64_t block_id, uint64_t* ptr_out,
+                          uint64_t* bytes_out);
+TS_API int ts_mgr_info(ts_manager* mgr, int64_t* host_blocks, uint64_t* host_block_pitch,
+                int64_t* major_dim, uint64_t* bytes_per_block);
+
+/* Per-launch timing of the manager's kernels (CUDA events around every
+ * extract / insert launch on its kernel streams).  ts_mgr_kernel_stats
+ * returns and resets the launches, their summed device time and their
+ * algorithmic HBM bytes (read + write) for which = 0 (extract) or 1 (insert).
+ * Plays the role of the reference's per-op duration telemetry
+ * (JoinAndRecordTelemetry, tpu_sync/kv_cache/kv_cache_manager_base.cc:205-219). */
+TS_API int ts_mgr_set_profiling(ts_manager* mgr, int on);
+TS_API int ts_mgr_kernel_stats(ts_manager* mgr, int which, int64_t* launches,
+                               double* total_ms, uint64_t* bytes);
+
+/* Completion handles (replace PjRtCopyFuture / RaidenFuture,
+ * tpu_sync/core/raw_transfer_core.h:379-621,
+ * tpu_sync/frameworks/torch/tpu_raiden_torch_module.cc:179-211). */
+TS_API int ts_event_query(ts_event* ev);               /* TS_OK, TS_PENDING or error */
+TS_API int ts_event_wait(ts_event* ev, int64_t timeout_ms); /* <0: no timeout */
+TS_API int ts_event_error(ts_event* ev, char* buf, size_t len);
+/* Makes `stream` wait for the event on the device (no host synchronisation). */
+TS_API int ts_event_stream_wait(ts_event* ev, void* stream);
+TS_API int ts_event_elapsed_ms(ts_event* ev, float* ms);
+TS_API void ts_event_release(ts_event* ev);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* TPUSYNC_B200_H_ */

@@ -1,0 +1,137 @@
+"""Pins the CPU oracle before it is trusted as the checker.
+
+* fp8 e4m3 encoder (written from the format definition) against ml_dtypes and
+  torch on every finite fp32 value representable as bf16 in range;
+* the byte-level manager model on the reference's own heterogeneous
+  block-size scenario (tpu_sync/frameworks/torch/kv_cache_manager_test.py:206-275)
+  and round trip (tpu_sync/benchmarks/perf_core.py:112-142);
+* the planner restatement against plans produced by the reference planner
+  (tests/golden/reshard_plans.json, made by tests/golden/make_golden.py).
+"""
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import fp8 as ofp8
+from oracle import kv_blocks as ref
+from oracle import reshard as ors
+
+GOLDEN = Path(__file__).resolve().parent / "golden" / "reshard_plans.json"
+
+
+def all_bf16_finite():
+  bits = np.arange(1 << 16, dtype=np.uint32).astype(np.uint16)
+  v = ofp8.bf16_bits_to_f32(bits)
+  return v[np.isfinite(v)]
+
+
+def test_e4m3_encoder_matches_ml_dtypes_in_range():
+  ml_dtypes = pytest.importorskip("ml_dtypes")
+  v = all_bf16_finite()
+  v = v[np.abs(v) <= 448]
+  ours = ofp8.e4m3_encode(v)
+  theirs = v.astype(ml_dtypes.float8_e4m3fn).view(np.uint8)
+  # ml_dtypes keeps the sign of zero results; so do we
+  np.testing.assert_array_equal(ours, theirs)
+
+
+def test_e4m3_encoder_matches_torch_in_range():
+  v = all_bf16_finite()
+  v = v[np.abs(v) <= 448]
+  theirs = torch.from_numpy(v).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+  np.testing.assert_array_equal(ofp8.e4m3_encode(v), theirs)
+
+
+def test_e4m3_saturates_and_decodes():
+  big = np.array([448.0, 449.0, 463.9, 464.0, 1e6, np.inf, -np.inf, -500.0], np.float32)
+  enc = ofp8.e4m3_encode(big)
+  assert list(enc) == [0x7E, 0x7E, 0x7E, 0x7E, 0x7E, 0x7E, 0xFE, 0xFE]
+  assert ofp8.e4m3_encode(np.array([np.nan], np.float32))[0] & 0x7F == 0x7F
+  codes = np.arange(256, dtype=np.uint8)
+  dec = ofp8.e4m3_decode(codes)
+  finite = ~np.isnan(dec)
+  np.testing.assert_array_equal(ofp8.e4m3_encode(dec[finite]), codes[finite])
+
+
+def test_fp8_unit_roundtrip_error_bound():
+  rng = np.random.default_rng(0)
+  x = torch.from_numpy(rng.standard_normal(8192).astype(np.float32)).to(torch.bfloat16)
+  bits = x.view(torch.int16).numpy().view(np.uint16)
+  q, scale = ofp8.quantize_unit(bits)
+  assert scale == np.float32(np.abs(x.float().numpy()).max()) / np.float32(448)
+  back = ofp8.bf16_bits_to_f32(ofp8.dequantize_unit(q, scale))
+  # e4m3 has 3 mantissa bits: relative error <= 2^-4 for normals
+  err = np.abs(back - x.float().numpy())
+  assert np.all(err <= np.abs(x.float().numpy()) * 2.0 ** -4 * 1.01 + scale * 2.0 ** -9)
+
+
+def test_zero_unit_scale_is_one():
+  q, scale = ofp8.quantize_unit(np.zeros(64, np.uint16))
+  assert scale == 1.0 and not q.any()
+
+
+def test_bf16_rne_matches_torch():
+  rng = np.random.default_rng(1)
+  v = np.concatenate([rng.standard_normal(100000).astype(np.float32) * 1e3,
+                      np.array([0.0, -0.0, 1e38, -1e-38, np.inf, -np.inf], np.float32)])
+  ours = ofp8.f32_to_bf16_bits_rne(v)
+  theirs = torch.from_numpy(v).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+  np.testing.assert_array_equal(ours, theirs)
+
+
+def pattern(shape, layer):
+  n = int(np.prod(shape))
+  return (np.arange(n, dtype=np.float32).reshape(shape) + 1000.0 * (layer + 1))
+
+
+def test_heterogeneous_block_sizes_model():
+  """kv_cache_manager_test.py:206-275 on the byte model."""
+  shapes = [(4, 128, 8), (4, 128, 2)]
+  src = ref.RefKVManager([[pattern(s, l).view(np.uint8).reshape(-1)] for l, s in
+                          enumerate(shapes)], dim0=4, host_blocks=4)
+  dst_dev = [[np.zeros(int(np.prod(s)) * 4, np.uint8)] for s in shapes]
+  dst = ref.RefKVManager(dst_dev, dim0=4, host_blocks=4)
+  assert src.d2h([2], [2], [2]) == (ref.OK, "")
+  for l in range(2):  # H2hWrite: copy host blocks 2..3 to the peer's host 0..1
+    bb = src.layer_block_bytes(l)
+    dst.host[l][0][:2 * bb] = src.host[l][0][2 * bb:4 * bb]
+  assert dst.h2d([0], [2], [2]) == (ref.OK, "")
+  for l, s in enumerate(shapes):
+    got = dst.device[l][0].view(np.float32).reshape(s)
+    np.testing.assert_array_equal(got[2:4], pattern(s, l)[2:4])
+    np.testing.assert_array_equal(got[0:2], 0)
+
+
+def test_round_trip_and_errors_model():
+  dev = [[np.arange(8 * 64, dtype=np.uint8).copy()] for _ in range(2)]
+  m = ref.RefKVManager(dev, dim0=8, host_blocks=8)
+  assert m.d2h([0, 1, 2, 3], [0, 1, 2, 3]) == (ref.OK, "")
+  assert m.h2d([0, 1, 2, 3], [4, 5, 6, 7]) == (ref.OK, "")
+  np.testing.assert_array_equal(dev[0][0][:256], dev[0][0][256:])
+  assert m.d2h([7], [8])[0] == ref.INVALID_ARGUMENT
+  assert m.d2h([8], [0])[1] == "Copy range exceeds source device buffer size"
+  assert m.h2d([0], [0], layer_idx=2) == (ref.OUT_OF_RANGE, ref.LAYER_RANGE)
+  assert m.d2h([], []) == (ref.OK, "")
+
+
+def test_planner_oracle_matches_reference_goldens():
+  data = json.loads(GOLDEN.read_text())
+  for case in data["slices"]:
+    got = ors.compute_nd_shard_slices(case["global_shape"], case["mesh_shape"])
+    assert [[list(d) for d in s] for s in got] == case["slices"]
+  for case in data["plans"]:
+    s_sl = ors.compute_nd_shard_slices(case["shape"], case["src_mesh"])
+    d_sl = ors.compute_nd_shard_slices(case["shape"], case["dst_mesh"])
+    pairs = []
+    for i, s in enumerate(s_sl):
+      for j, d in enumerate(d_sl):
+        inter = ors.intersect_nd_slices(s, d)
+        if inter is None:
+          continue
+        pairs.append({"src": i, "dst": j, "chunks": [list(c) for c in
+                      ors.generate_strided_copy_chunks(s, d, inter, case["itemsize"])]})
+    assert pairs == case["pairs"], case["param"]

@@ -1,0 +1,273 @@
+"""GPU parity of the block extract/insert kernels and the KVCacheManager
+offload/reload path against the CPU oracle (bit-exact)."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import fp8 as ofp8
+from oracle import kv_blocks as ref
+from tpu_sync_b200 import KVCacheManager, ops, workloads
+
+pytestmark = pytest.mark.gpu
+
+
+def u8(t: torch.Tensor) -> np.ndarray:
+  return t.contiguous().view(torch.uint8).cpu().numpy().reshape(t.shape[0], -1)
+
+
+def small_pool(geom, blocks, seed, device):
+  return workloads.kv_pool(geom, blocks, seed, device)
+
+
+def test_c0_extract_insert_round_trip(cuda):
+  """Config 0: extract 128 ids (seed 1) into block-major staging, insert at 128
+  other ids (seed 2); bit-exact against the oracle, round trip exact."""
+  g = workloads.C0
+  pool = small_pool(g, workloads.C0_BLOCKS, 0, cuda)
+  ids_x = workloads.distinct_ids(workloads.C0_IDS, workloads.C0_BLOCKS, 1)
+  ids_i = workloads.distinct_ids(workloads.C0_IDS, workloads.C0_BLOCKS, 2)
+  host_pool = [u8(t) for t in pool]
+  table = ops.StorageTable(pool)
+  staging = table.new_staging(len(ids_x))
+  err = torch.zeros(1, dtype=torch.int32, device=cuda)
+  ops.kv_extract(table, ids_x, staging, err_flag=err)
+  torch.cuda.synchronize()
+  want = ref.extract_to_padded_staging(host_pool, ids_x)
+  np.testing.assert_array_equal(staging.cpu().numpy(), want)
+  # contiguous staging [128, 4, 2, 16, 8, 128] bf16 (no padding at these sizes)
+  assert table.pitch == g.block_bytes
+  st6 = staging.view(torch.bfloat16).view(len(ids_x), g.layers, g.kv, g.block_tokens,
+                                          g.heads, g.head_dim)
+  full = torch.stack([torch.stack(pool[l * 2:l * 2 + 2]) for l in range(g.layers)])
+  torch.testing.assert_close(st6[5], full[:, :, int(ids_x[5])], rtol=0, atol=0)
+  ops.kv_insert(table, ids_i, staging, err_flag=err)
+  torch.cuda.synchronize()
+  ref.insert_from_staging(host_pool, ids_i, want)
+  for t, h in zip(pool, host_pool):
+    np.testing.assert_array_equal(u8(t), h)
+  assert int(err.item()) == 0
+
+
+@pytest.mark.parametrize("block_tokens,heads,head_dim,n_st", [
+    (16, 8, 128, 3),   # 32 KiB blocks: two 16 KiB pieces
+    (1, 1, 8, 5),      # 16-byte blocks
+    (3, 1, 40, 2),     # 240-byte blocks: 16-aligned, single partial piece
+    (64, 1, 136, 2),   # 17 KiB blocks: partial second piece
+])
+def test_extract_insert_shapes(cuda, block_tokens, heads, head_dim, n_st):
+  geom = workloads.KVGeometry(layers=n_st, kv=1, block_tokens=block_tokens, heads=heads,
+                              head_dim=head_dim)
+  pool = small_pool(geom, 37, 11, cuda)
+  ids = [36, 0, 5, 5, 17]
+  table = ops.StorageTable(pool)
+  staging = table.new_staging(len(ids))
+  ops.kv_extract(table, ids, staging)
+  torch.cuda.synchronize()
+  want = ref.extract_to_padded_staging([u8(t) for t in pool], ids)
+  np.testing.assert_array_equal(staging.cpu().numpy(), want)
+
+
+def test_unaligned_block_bytes_use_byte_path(cuda):
+  # 6-byte blocks (3 x bf16): vector path impossible, byte kernel must be exact
+  pool = [torch.arange(30 * 3, dtype=torch.int16, device=cuda).view(30, 3) + 100 * s
+          for s in range(3)]
+  ids = [29, 3, 0, 14]
+  table = ops.StorageTable(pool)
+  staging = table.new_staging(len(ids))
+  staging.zero_()
+  ops.kv_extract(table, ids, staging)
+  torch.cuda.synchronize()
+  want = ref.extract_to_padded_staging([u8(t) for t in pool], ids)
+  np.testing.assert_array_equal(staging.cpu().numpy(), want)
+
+
+def test_out_of_bounds_id_sets_error_flag(cuda):
+  pool = small_pool(workloads.KVGeometry(2, 1, 4, 1, 64), 8, 3, cuda)
+  table = ops.StorageTable(pool)
+  staging = table.new_staging(2)
+  err = torch.zeros(1, dtype=torch.int32, device=cuda)
+  ops.kv_extract(table, [1, 8], staging, err_flag=err)
+  torch.cuda.synchronize()
+  assert int(err.item()) == 1
+  np.testing.assert_array_equal(staging[0].cpu().numpy(),
+                                ref.extract_to_padded_staging([u8(t) for t in pool], [1])[0])
+
+
+# ---------------------------------------------------------------------------
+# fp8 fused cast
+# ---------------------------------------------------------------------------
+
+def fp8_oracle(pool, ids):
+  bits = [t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16).reshape(
+      t.shape[0], -1) for t in pool]
+  return ofp8.extract_fp8(bits, ids), bits
+
+
+@pytest.mark.parametrize("block_tokens,heads,n_blocks", [(64, 1, 40), (16, 8, 9), (256, 4, 3)])
+def test_fp8_extract_insert_matches_oracle(cuda, block_tokens, heads, n_blocks):
+  geom = workloads.KVGeometry(layers=3, kv=2, block_tokens=block_tokens, heads=heads,
+                              head_dim=128)
+  pool = small_pool(geom, n_blocks + 4, 20, cuda)
+  # edge units: all zero, a huge value (saturation path), tiny values
+  pool[0][1].zero_()
+  pool[1][2].mul_(1e4)
+  pool[2][3].mul_(1e-30)
+  ids = list(range(n_blocks))
+  table = ops.StorageTable(pool, fp8=True)
+  staging = table.new_staging(len(ids))
+  ops.kv_extract(table, ids, staging)
+  torch.cuda.synchronize()
+  (payload, scales), bits = fp8_oracle(pool, ids)
+  st = staging.cpu().numpy()
+  for s in range(len(pool)):
+    off = table.stage_offs[s]
+    np.testing.assert_array_equal(st[:, off:off + payload.shape[2]], payload[:, s])
+  got_scales = st[:, table.scale_off:table.scale_off + 4 * len(pool)].copy().view(np.float32)
+  np.testing.assert_array_equal(got_scales, scales)
+  assert got_scales[1, 0] == 1.0  # zero unit
+  # dequant into other blocks
+  dst_ids = [n_blocks + 3 - (i % 4) for i in range(len(ids))][:4]
+  ops.kv_insert(table, dst_ids, staging[:4])
+  torch.cuda.synchronize()
+  ofp8.insert_fp8(payload[:4], scales[:4], dst_ids, bits)
+  for t, b in zip(pool, bits):
+    np.testing.assert_array_equal(
+        t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16).reshape(b.shape), b)
+
+
+# ---------------------------------------------------------------------------
+# KVCacheManager (pinned host tier, pipelined gather + DMA)
+# ---------------------------------------------------------------------------
+
+def make_pair(geom, blocks, host_blocks, seed, cuda, chunk_blocks=0):
+  pool = small_pool(geom, blocks, seed, cuda)
+  grid = [[t] for t in pool]
+  mgr = KVCacheManager(grid, host_blocks_to_allocate=host_blocks, chunk_blocks=chunk_blocks)
+  model = ref.RefKVManager([[u8(t).reshape(-1).copy()] for t in pool], dim0=blocks,
+                           host_blocks=host_blocks)
+  return pool, mgr, model
+
+
+def assert_same(pool, mgr, model, host_ids):
+  for l, t in enumerate(pool):
+    np.testing.assert_array_equal(u8(t).reshape(-1), model.device[l][0])
+    for h in host_ids:
+      assert mgr.read_block_bytes(l, h) == model.host_block(l, h), (l, h)
+
+
+@pytest.mark.parametrize("chunk_blocks", [0, 3])
+def test_manager_offload_reload_matches_model(cuda, chunk_blocks):
+  geom = workloads.KVGeometry(layers=4, kv=2, block_tokens=16, heads=2, head_dim=128)
+  pool, mgr, model = make_pair(geom, 64, 96, 5, cuda, chunk_blocks)
+  rng = np.random.default_rng(3)
+  for step in range(6):
+    n = int(rng.integers(1, 40))
+    src = list(rng.choice(64, n, replace=False))
+    dst = list(rng.choice(96, n, replace=False))
+    if step == 2:  # coalescible runs with sizes
+      src, dst, sizes = [0, 4, 10], [50, 54, 70], [4, 3, 6]
+    else:
+      sizes = None
+    f = mgr.d2h(src, dst, sizes)
+    assert model.d2h(src, dst, sizes) == (ref.OK, "")
+    f.Await()
+    assert f.is_ready() and f.ok() and f.error_message() == ""
+    hs = list(rng.choice(96, n, replace=False))
+    ds = list(rng.choice(64, n, replace=False))
+    g = mgr.h2d(hs, ds)
+    assert model.h2d(hs, ds) == (ref.OK, "")
+    g.Await()
+  torch.cuda.synchronize()
+  assert_same(pool, mgr, model, range(96))
+
+
+def test_manager_back_to_back_calls_are_ordered(cuda):
+  """Offload then reload of the same host blocks without waiting in between."""
+  geom = workloads.KVGeometry(layers=2, kv=2, block_tokens=16, heads=8, head_dim=128)
+  pool, mgr, model = make_pair(geom, 128, 128, 9, cuda, chunk_blocks=8)
+  futs = []
+  for i in range(4):
+    src = list(range(i * 20, i * 20 + 20))
+    futs.append(mgr.d2h(src, list(range(20))))
+    model.d2h(src, list(range(20)))
+    futs.append(mgr.h2d(list(range(20)), list(range(100, 120))))
+    model.h2d(list(range(20)), list(range(100, 120)))
+  for f in futs:
+    f.Await()
+  assert_same(pool, mgr, model, range(128))
+
+
+def test_manager_whole_storage_and_layer_restricted(cuda):
+  geom = workloads.KVGeometry(layers=3, kv=1, block_tokens=4, heads=2, head_dim=64)
+  pool, mgr, model = make_pair(geom, 16, 16, 2, cuda)
+  mgr.d2h([], []).Await()
+  assert model.d2h([], []) == (ref.OK, "")
+  f = mgr.h2d([3, 4], [9, 10], layer_idx=1)
+  assert model.h2d([3, 4], [9, 10], layer_idx=1) == (ref.OK, "")
+  f.Await()
+  f = mgr.d2h([0, 1, 2], [13, 14, 15], layer_idx=2, shard_idx=0)
+  assert model.d2h([0, 1, 2], [13, 14, 15], layer_idx=2, shard_idx=0) == (ref.OK, "")
+  f.Await()
+  assert_same(pool, mgr, model, range(16))
+
+
+def test_manager_errors_match_reference(cuda):
+  geom = workloads.KVGeometry(layers=2, kv=1, block_tokens=4, heads=1, head_dim=64)
+  pool, mgr, model = make_pair(geom, 8, 4, 2, cuda)
+  cases = [
+      ("d2h", dict(src=[0], dst=[0, 1], sizes=[1])),
+      ("h2d", dict(src=[-1], dst=[0], sizes=[1])),
+      ("d2h", dict(src=[7], dst=[4], sizes=[1])),
+      ("d2h", dict(src=[8], dst=[0], sizes=[1])),
+      ("h2d", dict(src=[3], dst=[0], sizes=[2])),
+      ("h2d", dict(src=[0], dst=[7], sizes=[2])),
+      ("d2h", dict(src=[], dst=[], sizes=[])),          # whole storage > host tier
+      ("h2d", dict(src=[], dst=[], sizes=[])),
+      ("h2d", dict(src=[0], dst=[0], sizes=[1], layer_idx=2)),
+  ]
+  for op, kw in cases:
+    code, msg = getattr(model, op)(kw["src"], kw["dst"], kw["sizes"], kw.get("layer_idx"))
+    assert code != ref.OK, (op, kw)
+    with pytest.raises(RuntimeError) as e:
+      getattr(mgr, op)(kw["src"], kw["dst"], kw["sizes"], layer_idx=kw.get("layer_idx"))
+    prefix = "KVCacheManager D2h failed: " if op == "d2h" else "KVCacheManager H2d failed: "
+    assert str(e.value) == prefix + msg
+
+
+def test_heterogeneous_layer_block_sizes_transfer(cuda):
+  """Port of tpu_sync/frameworks/torch/kv_cache_manager_test.py:206-275."""
+  shapes = [(4, 128, 8), (4, 128, 2)]
+  src_t, dst_t = [], []
+  for l, s in enumerate(shapes):
+    n = int(np.prod(s))
+    src_t.append([(torch.arange(n, dtype=torch.float32).reshape(s) + 1000.0 * (l + 1)).to(cuda)])
+    dst_t.append([torch.zeros(s, dtype=torch.float32, device=cuda)])
+  ws_src = KVCacheManager(src_t, 0, host_blocks_to_allocate=4, parallelism=1)
+  ws_dst = KVCacheManager(dst_t, 0, host_blocks_to_allocate=4, parallelism=1)
+  ws_src.D2h([2], [2], [2]).Await()
+  for l in range(2):  # H2hWrite stand-in: the peer's host blocks 0..1
+    for b in range(2):
+      ws_dst.write_block_bytes(l, b, ws_src.read_block_bytes(l, 2 + b))
+  ws_dst.H2d([0], [2], [2]).Await()
+  for l in range(2):
+    got, want = dst_t[l][0].cpu(), src_t[l][0].cpu()
+    torch.testing.assert_close(got[2:4], want[2:4], rtol=0, atol=0)
+    assert torch.count_nonzero(got[0:2]) == 0
+
+
+def test_fp8_manager_round_trip(cuda):
+  geom = workloads.KVGeometry(layers=4, kv=2, block_tokens=64, heads=1, head_dim=128)
+  pool = small_pool(geom, 32, 21, cuda)
+  mgr = KVCacheManager([[t] for t in pool], host_blocks_to_allocate=32, fp8=True)
+  ids = [3, 9, 27, 30]
+  mgr.d2h(ids, [0, 1, 2, 3]).Await()
+  (payload, scales), bits = fp8_oracle(pool, ids)
+  for s in range(len(pool)):
+    for k in range(len(ids)):
+      assert mgr.read_block_bytes(s, k) == payload[k, s].tobytes()
+  mgr.h2d([0, 1, 2, 3], [0, 1, 2, 4]).Await()
+  ofp8.insert_fp8(payload, scales, [0, 1, 2, 4], bits)
+  for t, b in zip(pool, bits):
+    np.testing.assert_array_equal(
+        t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16).reshape(b.shape), b)

@@ -1,0 +1,195 @@
+"""ctypes binding of the C ABI in ``include/tpusync_b200.h``.
+
+The library is loaded from ``tpu_sync_b200/_lib/libtpusync_b200.so`` (built
+in-tree by ``tpu_sync_b200.build``).  There is no fallback: if the library is
+missing every entry point raises, so a missing build can never silently turn
+into a CPU path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import numpy as np
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libtpusync_b200.so"
+
+# ts_status values
+OK = 0
+CANCELLED = 1
+UNKNOWN = 2
+INVALID_ARGUMENT = 3
+DEADLINE_EXCEEDED = 4
+NOT_FOUND = 5
+ALREADY_EXISTS = 6
+RESOURCE_EXHAUSTED = 8
+FAILED_PRECONDITION = 9
+OUT_OF_RANGE = 11
+UNIMPLEMENTED = 12
+INTERNAL = 13
+UNAVAILABLE = 14
+PENDING = 100
+
+STATUS_NAMES = {
+    OK: "OK", CANCELLED: "CANCELLED", UNKNOWN: "UNKNOWN",
+    INVALID_ARGUMENT: "INVALID_ARGUMENT", DEADLINE_EXCEEDED: "DEADLINE_EXCEEDED",
+    NOT_FOUND: "NOT_FOUND", ALREADY_EXISTS: "ALREADY_EXISTS",
+    RESOURCE_EXHAUSTED: "RESOURCE_EXHAUSTED",
+    FAILED_PRECONDITION: "FAILED_PRECONDITION", OUT_OF_RANGE: "OUT_OF_RANGE",
+    UNIMPLEMENTED: "UNIMPLEMENTED", INTERNAL: "INTERNAL",
+    UNAVAILABLE: "UNAVAILABLE", PENDING: "PENDING",
+}
+
+DTYPE_U8, DTYPE_BF16, DTYPE_F32, DTYPE_F16 = 0, 1, 2, 3
+
+c_i64_p = ctypes.POINTER(ctypes.c_int64)
+c_u64_p = ctypes.POINTER(ctypes.c_uint64)
+c_i32_p = ctypes.POINTER(ctypes.c_int32)
+
+
+class BlockStorage(ctypes.Structure):
+  _fields_ = [("dev_ptr", ctypes.c_uint64), ("block_bytes", ctypes.c_uint64),
+              ("dev_bytes", ctypes.c_uint64), ("stage_off", ctypes.c_uint64)]
+
+
+class ReshardChunk(ctypes.Structure):
+  _fields_ = [("src_ptr", ctypes.c_uint64), ("dst_ptr", ctypes.c_uint64),
+              ("src_off", ctypes.c_int64), ("dst_off", ctypes.c_int64),
+              ("size", ctypes.c_int64), ("src_stride", ctypes.c_int64),
+              ("dst_stride", ctypes.c_int64), ("count", ctypes.c_int64)]
+
+
+class PageGeometry(ctypes.Structure):
+  _fields_ = [("block_tokens", ctypes.c_int64), ("heads", ctypes.c_int64),
+              ("head_bytes", ctypes.c_int64), ("head_major", ctypes.c_int32),
+              ("pad_", ctypes.c_int32)]
+
+
+class StorageDesc(ctypes.Structure):
+  _fields_ = [("dev_ptr", ctypes.c_uint64), ("nbytes", ctypes.c_uint64),
+              ("dim0", ctypes.c_int64), ("device", ctypes.c_int32),
+              ("pad_", ctypes.c_int32)]
+
+
+class ManagerOpts(ctypes.Structure):
+  _fields_ = [("host_blocks", ctypes.c_int64), ("chunk_blocks", ctypes.c_int64),
+              ("shm_name", ctypes.c_char_p), ("model_uid", ctypes.c_char_p),
+              ("fp8", ctypes.c_int32), ("pad_", ctypes.c_int32)]
+
+
+# name -> (restype, argtypes); every symbol declared in include/tpusync_b200.h
+_V = ctypes.c_void_p
+_SIGS = {
+    "ts_last_error": (ctypes.c_char_p, []),
+    "ts_version": (ctypes.c_char_p, []),
+    "ts_validate_copy_spec": (ctypes.c_int, [c_i64_p, ctypes.c_int64, c_i64_p,
+                                             ctypes.c_int64, c_i64_p, ctypes.c_int64]),
+    "ts_coalesce_runs": (ctypes.c_int, [c_i64_p, c_i64_p, c_i64_p, ctypes.c_int64,
+                                        c_i64_p, c_i64_p, c_i64_p, c_i64_p]),
+    "ts_kv_extract": (ctypes.c_int, [ctypes.c_int, _V, ctypes.c_int, _V,
+                                     ctypes.c_int64, _V, ctypes.c_uint64, _V, _V]),
+    "ts_kv_insert": (ctypes.c_int, [ctypes.c_int, _V, ctypes.c_int, _V,
+                                    ctypes.c_int64, _V, ctypes.c_uint64, _V, _V]),
+    "ts_kv_extract_fp8": (ctypes.c_int, [ctypes.c_int, _V, ctypes.c_int, _V,
+                                         ctypes.c_int64, _V, ctypes.c_uint64,
+                                         ctypes.c_uint64, _V, _V]),
+    "ts_kv_insert_fp8": (ctypes.c_int, [ctypes.c_int, _V, ctypes.c_int, _V,
+                                        ctypes.c_int64, _V, ctypes.c_uint64,
+                                        ctypes.c_uint64, _V, _V]),
+    "ts_reshard_work_items": (ctypes.c_int, [ctypes.POINTER(ReshardChunk),
+                                             ctypes.c_int64, ctypes.c_int,
+                                             ctypes.c_int, c_i64_p]),
+    "ts_reshard_copy": (ctypes.c_int, [ctypes.c_int, _V, _V, ctypes.c_int64,
+                                       ctypes.c_int64, ctypes.c_int, ctypes.c_int, _V]),
+    "ts_kv_relayout": (ctypes.c_int, [ctypes.c_int, _V, _V, ctypes.c_int,
+                                      PageGeometry, PageGeometry, _V, ctypes.c_int64,
+                                      _V, ctypes.c_int64, ctypes.c_int64,
+                                      ctypes.c_int64, _V]),
+    "ts_host_tier_create": (ctypes.c_int, [ctypes.c_uint64, ctypes.c_char_p,
+                                           ctypes.c_char_p, ctypes.c_uint64,
+                                           ctypes.c_int, ctypes.POINTER(_V),
+                                           ctypes.POINTER(ctypes.c_int)]),
+    "ts_host_tier_ptr": (_V, [_V]),
+    "ts_host_tier_bytes": (ctypes.c_uint64, [_V]),
+    "ts_host_tier_destroy": (ctypes.c_int, [_V, ctypes.c_int]),
+    "ts_mgr_create": (ctypes.c_int, [ctypes.POINTER(StorageDesc), ctypes.c_int,
+                                     ctypes.c_int, ctypes.POINTER(ManagerOpts),
+                                     ctypes.POINTER(_V)]),
+    "ts_mgr_destroy": (ctypes.c_int, [_V]),
+    "ts_d2h": (ctypes.c_int, [_V, c_i64_p, c_i64_p, c_i64_p, ctypes.c_int64,
+                              ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                              ctypes.c_int64, _V, ctypes.POINTER(_V)]),
+    "ts_h2d": (ctypes.c_int, [_V, c_i64_p, c_i64_p, c_i64_p, ctypes.c_int64,
+                              ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                              ctypes.c_int64, _V, ctypes.POINTER(_V)]),
+    "ts_mgr_host_block_ptr": (ctypes.c_int, [_V, ctypes.c_int64, ctypes.c_int64,
+                                             ctypes.c_int64, c_u64_p, c_u64_p]),
+    "ts_mgr_info": (ctypes.c_int, [_V, c_i64_p, c_u64_p, c_i64_p, c_u64_p]),
+    "ts_mgr_set_profiling": (ctypes.c_int, [_V, ctypes.c_int]),
+    "ts_mgr_kernel_stats": (ctypes.c_int, [_V, ctypes.c_int, c_i64_p,
+                                           ctypes.POINTER(ctypes.c_double), c_u64_p]),
+    "ts_event_query": (ctypes.c_int, [_V]),
+    "ts_event_wait": (ctypes.c_int, [_V, ctypes.c_int64]),
+    "ts_event_error": (ctypes.c_int, [_V, ctypes.c_char_p, ctypes.c_size_t]),
+    "ts_event_stream_wait": (ctypes.c_int, [_V, _V]),
+    "ts_event_elapsed_ms": (ctypes.c_int, [_V, ctypes.POINTER(ctypes.c_float)]),
+    "ts_event_release": (None, [_V]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class NativeError(RuntimeError):
+  """A ts_status error from the native library."""
+
+  def __init__(self, code: int, message: str):
+    super().__init__(message)
+    self.code = code
+    self.status = STATUS_NAMES.get(code, str(code))
+
+
+def lib() -> ctypes.CDLL:
+  """Returns the loaded library (loads it on first use; raises if missing)."""
+  global _lib
+  if _lib is not None:
+    return _lib
+  with _lock:
+    if _lib is None:
+      if not LIB_PATH.exists():
+        raise ImportError(
+            f"tpu_sync_b200 native library not built: {LIB_PATH} is missing. "
+            "Run `python -m tpu_sync_b200.build` (nvcc required).")
+      l = ctypes.CDLL(str(LIB_PATH), mode=os.RTLD_NOW | ctypes.RTLD_LOCAL)
+      for name, (res, args) in _SIGS.items():
+        fn = getattr(l, name)
+        fn.restype = res
+        fn.argtypes = args
+      _lib = l
+  return _lib
+
+
+def last_error() -> str:
+  msg = lib().ts_last_error()
+  return msg.decode() if msg else ""
+
+
+def check(rc: int, prefix: str = "") -> None:
+  if rc != OK:
+    msg = last_error()
+    raise NativeError(rc, f"{prefix}{msg}" if prefix else msg)
+
+
+def i64_array(values) -> np.ndarray:
+  return np.ascontiguousarray(np.asarray(values, dtype=np.int64).reshape(-1))
+
+
+def i64_ptr(arr: np.ndarray):
+  return arr.ctypes.data_as(c_i64_p) if arr.size else None
+
+
+def declared_symbols() -> list[str]:
+  return sorted(_SIGS)

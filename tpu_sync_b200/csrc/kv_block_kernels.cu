@@ -1,0 +1,533 @@
+// Block extract (gather) / insert (scatter) kernels between paged KV storages
+// in HBM and a block-major staging buffer, plus the fused bf16 <-> fp8 e4m3
+// variants.
+//
+// Semantics: the reference copies, per (layer, shard) storage and per
+// coalesced run, bytes [src*bb, +n*bb) of the device buffer to host offset
+// dst*bb (tpu_sync/kv_cache/kv_cache_manager_base.cc:2036-2124, inverse at
+// :1945-2033).  Here one launch moves whole blocks of every storage at once:
+// work unit = (block k, storage s) = one contiguous run of bb_s bytes, split
+// into 16 KiB pieces; one CTA copies one piece with 16-byte vector accesses,
+// all loads of a thread issued before its stores (64 B in flight per thread).
+// The grid is persistent: a multiple of the SM count, grid-striding over the
+// pieces.  Nothing here is a contraction, so no tensor cores are used; the
+// bound is HBM bandwidth (read bb + write bb per unit).
+
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "ts_internal.h"
+
+namespace tsb {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kVecPerThread = 4;
+constexpr uint64_t kPieceBytes = uint64_t(kThreads) * kVecPerThread * 16;  // 16 KiB
+constexpr int kCtasPerSm = 8;
+
+// Block ids come from a device array (manager-free entry points) or by value
+// inside the kernel parameters (the manager's pipelined chunks: the launch
+// snapshots them, so no device id buffer or host->device id copy is needed).
+struct DevIds {
+  const int64_t* p;
+  __device__ __forceinline__ int64_t operator[](int64_t k) const { return p[k]; }
+};
+
+__device__ __forceinline__ int4 ld_stream(const void* p) {
+  int4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void st_vec(void* p, const int4& v) {
+  asm volatile("st.global.v4.s32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x),
+               "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Resolves work item w into (block k, storage s, piece).  Returns false when
+// the piece lies past the end of the storage's block (heterogeneous storages)
+// or the block id is out of bounds (err_flag set).
+struct Unit {
+  uint8_t* dev;
+  uint8_t* stg;
+  uint64_t nbytes;
+};
+
+template <typename Ids>
+__device__ __forceinline__ bool resolve(const ts_block_storage* __restrict__ st,
+                                        int n_st, const Ids& ids,
+                                        uint8_t* staging, uint64_t pitch,
+                                        uint32_t ppu, int64_t w, int* err_flag,
+                                        Unit* u) {
+  const int64_t unit = w / ppu;
+  const uint64_t piece = uint64_t(w - unit * ppu);
+  const int64_t k = unit / n_st;
+  const int s = int(unit - k * n_st);
+  const uint64_t bb = st[s].block_bytes;
+  const uint64_t off = piece * kPieceBytes;
+  if (off >= bb) return false;
+  const int64_t id = ids[k];
+  const uint64_t dev_off = uint64_t(id) * bb;
+  if (id < 0 || dev_off + bb > st[s].dev_bytes) {
+    if (err_flag != nullptr && threadIdx.x == 0) *reinterpret_cast<volatile int*>(err_flag) = 1;
+    return false;
+  }
+  u->dev = reinterpret_cast<uint8_t*>(st[s].dev_ptr) + dev_off + off;
+  u->stg = staging + uint64_t(k) * pitch + st[s].stage_off + off;
+  const uint64_t rem = bb - off;
+  u->nbytes = rem < kPieceBytes ? rem : kPieceBytes;
+  return true;
+}
+
+// 16-byte vector path: every block_bytes, stage_off, pitch and base address is
+// a multiple of 16 (checked on the host before choosing this kernel).
+template <bool kToStaging, typename Ids>
+__global__ void __launch_bounds__(kThreads)
+    block_copy_vec_kernel(const ts_block_storage* __restrict__ st, int n_st,
+                          const __grid_constant__ Ids ids, int64_t n_blocks,
+                          uint8_t* staging, uint64_t pitch, uint32_t ppu,
+                          int* err_flag) {
+  const int64_t items = n_blocks * int64_t(n_st) * ppu;
+  for (int64_t w = blockIdx.x; w < items; w += gridDim.x) {
+    Unit u;
+    if (!resolve(st, n_st, ids, staging, pitch, ppu, w, err_flag, &u)) continue;
+    const uint8_t* src = kToStaging ? u.dev : u.stg;
+    uint8_t* dst = kToStaging ? u.stg : u.dev;
+    const int nvec = int(u.nbytes >> 4);
+    int4 v[kVecPerThread];
+#pragma unroll
+    for (int i = 0; i < kVecPerThread; ++i) {
+      const int idx = threadIdx.x + i * kThreads;
+      if (idx < nvec) v[i] = ld_stream(src + (uint64_t(idx) << 4));
+    }
+#pragma unroll
+    for (int i = 0; i < kVecPerThread; ++i) {
+      const int idx = threadIdx.x + i * kThreads;
+      if (idx < nvec) st_vec(dst + (uint64_t(idx) << 4), v[i]);
+    }
+  }
+}
+
+// Byte path for storages whose sizes or addresses are not 16-byte multiples.
+template <bool kToStaging, typename Ids>
+__global__ void __launch_bounds__(kThreads)
+    block_copy_byte_kernel(const ts_block_storage* __restrict__ st, int n_st,
+                           const __grid_constant__ Ids ids, int64_t n_blocks,
+                           uint8_t* staging, uint64_t pitch, uint32_t ppu,
+                           int* err_flag) {
+  const int64_t items = n_blocks * int64_t(n_st) * ppu;
+  for (int64_t w = blockIdx.x; w < items; w += gridDim.x) {
+    Unit u;
+    if (!resolve(st, n_st, ids, staging, pitch, ppu, w, err_flag, &u)) continue;
+    const uint8_t* src = kToStaging ? u.dev : u.stg;
+    uint8_t* dst = kToStaging ? u.stg : u.dev;
+    for (uint64_t b = threadIdx.x; b < u.nbytes; b += kThreads) dst[b] = src[b];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// fp8 e4m3 fused cast.  One CTA per (block, storage) unit of bf16 values.
+// scale = amax / 448 (IEEE round-to-nearest division; 1 when amax == 0),
+// q = cvt.rn.satfinite.e4m3(x / scale) with x / scale an IEEE RN division,
+// dequant x' = bf16_rn(float(q) * scale).
+// ---------------------------------------------------------------------------
+
+constexpr int kFp8MaxVec = 8;  // register path: up to 8 x 16 B per thread (32 KiB unit)
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();  // red[] may still be read by a previous unit
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float r = red[0];
+#pragma unroll
+  for (int i = 1; i < kThreads / 32; ++i) r = fmaxf(r, red[i]);
+  return r;
+}
+
+__device__ __forceinline__ float bf16_bits_to_float(uint32_t h) {
+  return __uint_as_float(h << 16);
+}
+
+__device__ __forceinline__ float amax8(const int4& v, float m) {
+  const uint32_t w[4] = {uint32_t(v.x), uint32_t(v.y), uint32_t(v.z), uint32_t(v.w)};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    m = fmaxf(m, fabsf(bf16_bits_to_float(w[j] & 0xffffu)));
+    m = fmaxf(m, fabsf(bf16_bits_to_float(w[j] >> 16)));
+  }
+  return m;
+}
+
+// 8 bf16 -> 8 e4m3 bytes (packed in a uint2).
+__device__ __forceinline__ uint2 quant8(const int4& v, float scale) {
+  const uint32_t w[4] = {uint32_t(v.x), uint32_t(v.y), uint32_t(v.z), uint32_t(v.w)};
+  uint32_t out[2] = {0u, 0u};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float lo = __fdiv_rn(bf16_bits_to_float(w[j] & 0xffffu), scale);
+    const float hi = __fdiv_rn(bf16_bits_to_float(w[j] >> 16), scale);
+    const __nv_fp8x2_storage_t p =
+        __nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE, __NV_E4M3);
+    out[j >> 1] |= uint32_t(p) << (16 * (j & 1));
+  }
+  return make_uint2(out[0], out[1]);
+}
+
+// 8 e4m3 bytes -> 8 bf16 (packed in an int4).
+__device__ __forceinline__ int4 dequant8(uint2 q, float scale) {
+  const uint32_t in[2] = {q.x, q.y};
+  uint32_t w[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const __nv_fp8x2_storage_t p =
+        __nv_fp8x2_storage_t((in[j >> 1] >> (16 * (j & 1))) & 0xffffu);
+    const __half2_raw h2 = __nv_cvt_fp8x2_to_halfraw2(p, __NV_E4M3);
+    // e4m3 -> f16 is exact; f16 -> f32 is exact.
+    const float lo = __half2float(__half(__half_raw{h2.x}));
+    const float hi = __half2float(__half(__half_raw{h2.y}));
+    const __nv_bfloat16 blo = __float2bfloat16_rn(__fmul_rn(lo, scale));
+    const __nv_bfloat16 bhi = __float2bfloat16_rn(__fmul_rn(hi, scale));
+    w[j] = uint32_t(__bfloat16_as_ushort(blo)) | (uint32_t(__bfloat16_as_ushort(bhi)) << 16);
+  }
+  return make_int4(int(w[0]), int(w[1]), int(w[2]), int(w[3]));
+}
+
+template <typename Ids>
+__device__ __forceinline__ bool unit_addr(const ts_block_storage* __restrict__ st,
+                                          int n_st, const Ids& ids,
+                                          int64_t unit, int* err_flag, int* s_out,
+                                          int64_t* k_out, uint8_t** dev_out,
+                                          uint64_t* bb_out) {
+  const int64_t k = unit / n_st;
+  const int s = int(unit - k * n_st);
+  const uint64_t bb = st[s].block_bytes;
+  const int64_t id = ids[k];
+  const uint64_t dev_off = uint64_t(id) * bb;
+  if (id < 0 || dev_off + bb > st[s].dev_bytes) {
+    if (err_flag != nullptr && threadIdx.x == 0) *reinterpret_cast<volatile int*>(err_flag) = 1;
+    return false;
+  }
+  *s_out = s;
+  *k_out = k;
+  *dev_out = reinterpret_cast<uint8_t*>(st[s].dev_ptr) + dev_off;
+  *bb_out = bb;
+  return true;
+}
+
+template <typename Ids>
+__global__ void __launch_bounds__(kThreads)
+    extract_fp8_kernel(const ts_block_storage* __restrict__ st, int n_st,
+                       const __grid_constant__ Ids ids, int64_t n_blocks,
+                       uint8_t* staging, uint64_t pitch, uint64_t scale_off,
+                       int* err_flag) {
+  __shared__ float red[kThreads / 32];
+  const int64_t units = n_blocks * int64_t(n_st);
+  for (int64_t unit = blockIdx.x; unit < units; unit += gridDim.x) {
+    int s;
+    int64_t k;
+    uint8_t* dev;
+    uint64_t bb;
+    if (!unit_addr(st, n_st, ids, unit, err_flag, &s, &k, &dev, &bb)) continue;
+    uint8_t* stg_blk = staging + uint64_t(k) * pitch;
+    uint8_t* q_out = stg_blk + st[s].stage_off;
+    const int64_t nvec = int64_t(bb >> 4);  // 8 bf16 per vector
+    float m = 0.f;
+    if (nvec <= int64_t(kThreads) * kFp8MaxVec) {
+      int4 v[kFp8MaxVec];
+#pragma unroll
+      for (int i = 0; i < kFp8MaxVec; ++i) {
+        const int64_t idx = threadIdx.x + int64_t(i) * kThreads;
+        if (idx < nvec) {
+          v[i] = ld_stream(dev + (idx << 4));
+          m = amax8(v[i], m);
+        }
+      }
+      const float amax = block_max(m, red);
+      const float scale = amax == 0.f ? 1.f : __fdiv_rn(amax, 448.f);
+#pragma unroll
+      for (int i = 0; i < kFp8MaxVec; ++i) {
+        const int64_t idx = threadIdx.x + int64_t(i) * kThreads;
+        if (idx < nvec) *reinterpret_cast<uint2*>(q_out + (idx << 3)) = quant8(v[i], scale);
+      }
+      if (threadIdx.x == 0) *reinterpret_cast<float*>(stg_blk + scale_off + 4u * s) = scale;
+    } else {
+      // Large blocks: pass 1 reduces, pass 2 re-reads (L2-resident) and casts.
+      for (int64_t idx = threadIdx.x; idx < nvec; idx += kThreads)
+        m = amax8(ld_stream(dev + (idx << 4)), m);
+      const float amax = block_max(m, red);
+      const float scale = amax == 0.f ? 1.f : __fdiv_rn(amax, 448.f);
+      for (int64_t idx = threadIdx.x; idx < nvec; idx += kThreads)
+        *reinterpret_cast<uint2*>(q_out + (idx << 3)) =
+            quant8(*reinterpret_cast<const int4*>(dev + (idx << 4)), scale);
+      if (threadIdx.x == 0) *reinterpret_cast<float*>(stg_blk + scale_off + 4u * s) = scale;
+    }
+  }
+}
+
+template <typename Ids>
+__global__ void __launch_bounds__(kThreads)
+    insert_fp8_kernel(const ts_block_storage* __restrict__ st, int n_st,
+                      const __grid_constant__ Ids ids, int64_t n_blocks,
+                      const uint8_t* staging, uint64_t pitch, uint64_t scale_off,
+                      int* err_flag) {
+  const int64_t units = n_blocks * int64_t(n_st);
+  for (int64_t unit = blockIdx.x; unit < units; unit += gridDim.x) {
+    int s;
+    int64_t k;
+    uint8_t* dev;
+    uint64_t bb;
+    if (!unit_addr(st, n_st, ids, unit, err_flag, &s, &k, &dev, &bb)) continue;
+    const uint8_t* stg_blk = staging + uint64_t(k) * pitch;
+    const uint8_t* q_in = stg_blk + st[s].stage_off;
+    const float scale = *reinterpret_cast<const float*>(stg_blk + scale_off + 4u * s);
+    const int64_t nvec = int64_t(bb >> 4);
+    for (int64_t base = 0; base < nvec; base += int64_t(kThreads) * kVecPerThread) {
+      uint2 q[kVecPerThread];
+#pragma unroll
+      for (int i = 0; i < kVecPerThread; ++i) {
+        const int64_t idx = base + threadIdx.x + int64_t(i) * kThreads;
+        if (idx < nvec) q[i] = *reinterpret_cast<const uint2*>(q_in + (idx << 3));
+      }
+#pragma unroll
+      for (int i = 0; i < kVecPerThread; ++i) {
+        const int64_t idx = base + threadIdx.x + int64_t(i) * kThreads;
+        if (idx < nvec) st_vec(dev + (idx << 4), dequant8(q[i], scale));
+      }
+    }
+  }
+}
+
+bool aligned16(uint64_t v) { return (v & 15u) == 0; }
+
+int launch_grid(int device, int64_t items) {
+  const int64_t cap = int64_t(sm_count(device)) * kCtasPerSm;
+  return int(items < cap ? items : cap);
+}
+
+template <bool kToStaging, typename Ids>
+int block_copy(int device, const ts_block_storage* d_st, int n_st,
+               const Ids& d_ids, int64_t n_blocks, uint8_t* staging,
+               uint64_t pitch, int* err_flag, void* stream, bool vec_ok,
+               uint64_t max_block_bytes) {
+  if (n_blocks == 0 || n_st == 0) return TS_OK;
+  const uint32_t ppu = uint32_t((max_block_bytes + kPieceBytes - 1) / kPieceBytes);
+  if (ppu == 0) return TS_OK;
+  const int64_t items = n_blocks * int64_t(n_st) * ppu;
+  DeviceGuard g(device);
+  const int grid = launch_grid(device, items);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (vec_ok) {
+    block_copy_vec_kernel<kToStaging, Ids><<<grid, kThreads, 0, s>>>(
+        d_st, n_st, d_ids, n_blocks, staging, pitch, ppu, err_flag);
+  } else {
+    block_copy_byte_kernel<kToStaging, Ids><<<grid, kThreads, 0, s>>>(
+        d_st, n_st, d_ids, n_blocks, staging, pitch, ppu, err_flag);
+  }
+  TS_CUDA_RET(cudaGetLastError(), "block copy launch");
+  return TS_OK;
+}
+
+// Reads the device storage table back to decide alignment and piece count.
+int inspect_storages(const ts_block_storage* d_st, int n_st, uint64_t pitch,
+                     const void* staging, bool* vec_ok, uint64_t* max_bb) {
+  if (n_st < 0) return set_error(TS_INVALID_ARGUMENT, "n_storages must be >= 0");
+  ts_block_storage h[512];
+  *vec_ok = aligned16(pitch) && aligned16(reinterpret_cast<uint64_t>(staging));
+  *max_bb = 0;
+  for (int base = 0; base < n_st; base += 512) {
+    const int n = n_st - base < 512 ? n_st - base : 512;
+    TS_CUDA_RET(cudaMemcpy(h, d_st + base, sizeof(ts_block_storage) * n,
+                           cudaMemcpyDeviceToHost),
+                "read storage table");
+    for (int i = 0; i < n; ++i) {
+      *vec_ok = *vec_ok && aligned16(h[i].dev_ptr) && aligned16(h[i].block_bytes) &&
+                aligned16(h[i].stage_off);
+      if (h[i].block_bytes > *max_bb) *max_bb = h[i].block_bytes;
+    }
+  }
+  return TS_OK;
+}
+
+
+// Launchers used by the manager and the C entry points (storage table
+// already inspected on the host).
+template <typename Ids>
+int launch_extract(int device, const ts_block_storage* d_st, int n_st,
+                   const Ids& ids, int64_t n_blocks, void* staging,
+                   uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
+                   uint64_t max_bb) {
+  return block_copy<true>(device, d_st, n_st, ids, n_blocks,
+                          static_cast<uint8_t*>(staging), pitch, err_flag, s,
+                          vec_ok, max_bb);
+}
+
+template <typename Ids>
+int launch_insert(int device, const ts_block_storage* d_st, int n_st,
+                  const Ids& ids, int64_t n_blocks, const void* staging,
+                  uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
+                  uint64_t max_bb) {
+  return block_copy<false>(device, d_st, n_st, ids, n_blocks,
+                           static_cast<uint8_t*>(const_cast<void*>(staging)),
+                           pitch, err_flag, s, vec_ok, max_bb);
+}
+
+template <typename Ids>
+int launch_extract_fp8(int device, const ts_block_storage* d_st, int n_st,
+                       const Ids& ids, int64_t n_blocks, void* staging,
+                       uint64_t pitch, uint64_t scale_off, int* err_flag,
+                       cudaStream_t s) {
+  if (n_blocks == 0 || n_st == 0) return TS_OK;
+  DeviceGuard g(device);
+  const int grid = launch_grid(device, n_blocks * int64_t(n_st));
+  extract_fp8_kernel<Ids><<<grid, kThreads, 0, s>>>(d_st, n_st, ids, n_blocks,
+                                                    static_cast<uint8_t*>(staging),
+                                                    pitch, scale_off, err_flag);
+  TS_CUDA_RET(cudaGetLastError(), "extract_fp8 launch");
+  return TS_OK;
+}
+
+template <typename Ids>
+int launch_insert_fp8(int device, const ts_block_storage* d_st, int n_st,
+                      const Ids& ids, int64_t n_blocks, const void* staging,
+                      uint64_t pitch, uint64_t scale_off, int* err_flag,
+                      cudaStream_t s) {
+  if (n_blocks == 0 || n_st == 0) return TS_OK;
+  DeviceGuard g(device);
+  const int grid = launch_grid(device, n_blocks * int64_t(n_st));
+  insert_fp8_kernel<Ids><<<grid, kThreads, 0, s>>>(
+      d_st, n_st, ids, n_blocks, static_cast<const uint8_t*>(staging), pitch,
+      scale_off, err_flag);
+  TS_CUDA_RET(cudaGetLastError(), "insert_fp8 launch");
+  return TS_OK;
+}
+
+}  // namespace
+
+// Entry points for the manager (ids by value, at most kMaxParamIds blocks).
+int mgr_extract(int device, const ts_block_storage* d_st, int n_st,
+                const ParamIds& ids, int64_t n_blocks, void* staging,
+                uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
+                uint64_t max_bb, bool fp8, uint64_t scale_off) {
+  if (fp8)
+    return launch_extract_fp8(device, d_st, n_st, ids, n_blocks, staging, pitch,
+                              scale_off, err_flag, s);
+  return launch_extract(device, d_st, n_st, ids, n_blocks, staging, pitch,
+                        err_flag, s, vec_ok, max_bb);
+}
+
+int mgr_insert(int device, const ts_block_storage* d_st, int n_st,
+               const ParamIds& ids, int64_t n_blocks, const void* staging,
+               uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
+               uint64_t max_bb, bool fp8, uint64_t scale_off) {
+  if (fp8)
+    return launch_insert_fp8(device, d_st, n_st, ids, n_blocks, staging, pitch,
+                             scale_off, err_flag, s);
+  return launch_insert(device, d_st, n_st, ids, n_blocks, staging, pitch,
+                       err_flag, s, vec_ok, max_bb);
+}
+
+}  // namespace tsb
+
+using tsb::set_error;
+
+extern "C" int ts_kv_extract(int device, const ts_block_storage* d_storages,
+                             int n_storages, const int64_t* d_ids,
+                             int64_t n_blocks, void* d_staging,
+                             uint64_t stage_pitch, int* err_flag, void* stream) {
+  tsb::clear_error();
+  if (n_blocks < 0) return set_error(TS_INVALID_ARGUMENT, "n_blocks must be >= 0");
+  if (n_blocks == 0 || n_storages == 0) return TS_OK;
+  if (!d_storages || !d_ids || !d_staging)
+    return set_error(TS_INVALID_ARGUMENT, "null pointer argument");
+  bool vec_ok;
+  uint64_t max_bb;
+  tsb::DeviceGuard g(device);
+  int rc = tsb::inspect_storages(d_storages, n_storages, stage_pitch, d_staging,
+                                 &vec_ok, &max_bb);
+  if (rc != TS_OK) return rc;
+  return tsb::launch_extract(device, d_storages, n_storages, tsb::DevIds{d_ids}, n_blocks,
+                             d_staging, stage_pitch, err_flag,
+                             reinterpret_cast<cudaStream_t>(stream), vec_ok, max_bb);
+}
+
+extern "C" int ts_kv_insert(int device, const ts_block_storage* d_storages,
+                            int n_storages, const int64_t* d_ids,
+                            int64_t n_blocks, const void* d_staging,
+                            uint64_t stage_pitch, int* err_flag, void* stream) {
+  tsb::clear_error();
+  if (n_blocks < 0) return set_error(TS_INVALID_ARGUMENT, "n_blocks must be >= 0");
+  if (n_blocks == 0 || n_storages == 0) return TS_OK;
+  if (!d_storages || !d_ids || !d_staging)
+    return set_error(TS_INVALID_ARGUMENT, "null pointer argument");
+  bool vec_ok;
+  uint64_t max_bb;
+  tsb::DeviceGuard g(device);
+  int rc = tsb::inspect_storages(d_storages, n_storages, stage_pitch, d_staging,
+                                 &vec_ok, &max_bb);
+  if (rc != TS_OK) return rc;
+  return tsb::launch_insert(device, d_storages, n_storages, tsb::DevIds{d_ids}, n_blocks,
+                            d_staging, stage_pitch, err_flag,
+                            reinterpret_cast<cudaStream_t>(stream), vec_ok, max_bb);
+}
+
+namespace {
+int check_fp8_table(const ts_block_storage* d_st, int n_st, uint64_t pitch,
+                    uint64_t scale_off, const void* staging) {
+  bool vec_ok;
+  uint64_t max_bb;
+  int rc = tsb::inspect_storages(d_st, n_st, pitch, staging, &vec_ok, &max_bb);
+  if (rc != TS_OK) return rc;
+  // The fp8 kernels move 16 B of bf16 / 8 B of fp8 per vector.
+  if (!vec_ok || (scale_off & 3u) != 0)
+    return set_error(TS_INVALID_ARGUMENT,
+                     "fp8 path needs 16-byte aligned storages, block sizes, "
+                     "stage offsets and pitch, and a 4-byte aligned scale offset");
+  return TS_OK;
+}
+}  // namespace
+
+extern "C" int ts_kv_extract_fp8(int device, const ts_block_storage* d_storages,
+                                 int n_storages, const int64_t* d_ids,
+                                 int64_t n_blocks, void* d_staging,
+                                 uint64_t stage_pitch, uint64_t scale_off,
+                                 int* err_flag, void* stream) {
+  tsb::clear_error();
+  if (n_blocks < 0) return set_error(TS_INVALID_ARGUMENT, "n_blocks must be >= 0");
+  if (n_blocks == 0 || n_storages == 0) return TS_OK;
+  if (!d_storages || !d_ids || !d_staging)
+    return set_error(TS_INVALID_ARGUMENT, "null pointer argument");
+  tsb::DeviceGuard g(device);
+  int rc = check_fp8_table(d_storages, n_storages, stage_pitch, scale_off, d_staging);
+  if (rc != TS_OK) return rc;
+  return tsb::launch_extract_fp8(device, d_storages, n_storages, tsb::DevIds{d_ids}, n_blocks,
+                                 d_staging, stage_pitch, scale_off, err_flag,
+                                 reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ts_kv_insert_fp8(int device, const ts_block_storage* d_storages,
+                                int n_storages, const int64_t* d_ids,
+                                int64_t n_blocks, const void* d_staging,
+                                uint64_t stage_pitch, uint64_t scale_off,
+                                int* err_flag, void* stream) {
+  tsb::clear_error();
+  if (n_blocks < 0) return set_error(TS_INVALID_ARGUMENT, "n_blocks must be >= 0");
+  if (n_blocks == 0 || n_storages == 0) return TS_OK;
+  if (!d_storages || !d_ids || !d_staging)
+    return set_error(TS_INVALID_ARGUMENT, "null pointer argument");
+  tsb::DeviceGuard g(device);
+  int rc = check_fp8_table(d_storages, n_storages, stage_pitch, scale_off, d_staging);
+  if (rc != TS_OK) return rc;
+  return tsb::launch_insert_fp8(device, d_storages, n_storages, tsb::DevIds{d_ids}, n_blocks,
+                                d_staging, stage_pitch, scale_off, err_flag,
+                                reinterpret_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,849 @@
+// KV cache manager: the device path of KVCacheManagerBase on one B200.
+//
+// Reference behaviour kept (tpu_sync/kv_cache/kv_cache_manager_base.cc):
+//  * storages are a [layer][shard] grid of device buffers whose dim-0 slices
+//    are blocks; block bytes of layer l = physical_size(l) / dim0(layer 0)
+//    (layer_block_byte_size, kv_cache_manager_base.h:434-439);
+//  * D2h/H2d take block-unit (src, dst, size) lists, validated
+//    (ValidateOffsetsAndSizes :72-102), coalesced (:121-141), bounds-checked
+//    per storage and run in (layer, shard, run) order with the reference's
+//    codes and messages (:1994-2012, :2089-2103), and an empty list means
+//    "whole storage" (:1984-1993, :2078-2088);
+//  * optional layer / shard restriction (:540-545);
+//  * a future per call (PjRtCopyFuture -> ts_event).
+//
+// B200 design:
+//  * the host tier is block-major: host block h holds block h of every
+//    storage contiguously (pitch = sum of block bytes), so a KV block of all
+//    layers is one contiguous host range and one DMA;
+//  * offload = extract kernel (HBM pages -> HBM staging slot, block-major)
+//    on a kernel stream, then copy-engine D2H DMAs of whole host blocks on a
+//    copy stream; reload = H2D DMAs into a staging slot, then the insert
+//    kernel.  Two staging slots per direction double-buffer chunks of up to
+//    kMaxParamIds blocks, so the next chunk's gather overlaps the current
+//    chunk's DMA, and offload and reload use separate slots and streams so
+//    both PCIe directions run at once;
+//  * block-level hazard tracking orders a reload after an in-flight offload
+//    of the same host/device blocks (and vice versa) without serialising
+//    independent calls.
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstring>
+#include <deque>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "ts_internal.h"
+
+struct ts_host_tier;
+
+namespace tsb {
+namespace {
+
+constexpr int kSlots = 2;
+constexpr int kEventRing = 256;
+constexpr int kErrWords = 4096;
+
+struct Storage {
+  uint64_t dev_ptr = 0;
+  uint64_t nbytes = 0;
+  int64_t dim0 = 0;
+  uint64_t bb = 0;        // layer_block_byte_size
+  uint64_t host_off = 0;  // offset inside a host block (and a staging block)
+  uint64_t host_bytes = 0;  // bytes of this storage in one host block
+};
+
+struct Slot {
+  uint8_t* buf = nullptr;
+  cudaEvent_t ready = nullptr;
+  cudaEvent_t free = nullptr;
+};
+
+// Completion record of one call, kept so later calls can wait on it.
+struct CallRec {
+  uint64_t seq = 0;
+  cudaEvent_t done = nullptr;
+};
+
+}  // namespace
+}  // namespace tsb
+
+struct ts_manager;
+
+struct ts_event {
+  ts_manager* mgr = nullptr;
+  int device = 0;
+  cudaEvent_t start = nullptr;
+  cudaEvent_t done = nullptr;
+  int* err_word = nullptr;  // mapped pinned int (host view)
+  int err_index = -1;
+  bool finished = false;
+  int status = TS_PENDING;
+  std::string message;
+};
+
+struct ts_manager {
+  int device = 0;
+  int num_layers = 0;
+  int num_shards = 0;
+  int64_t major_dim = 0;
+  uint64_t bytes_per_block = 0;  // slice byte size of layer 0 (reference bytes_per_block)
+  std::vector<tsb::Storage> st;
+  int64_t host_blocks = 0;
+  uint64_t host_pitch = 0;
+  uint64_t scale_off = 0;  // fp8: offset of the per-storage scales in a block
+  bool fp8 = false;
+  ts_host_tier* tier = nullptr;
+  uint8_t* host = nullptr;
+
+  ts_block_storage* d_table = nullptr;
+  bool vec_ok = true;
+  uint64_t max_bb = 0;
+  int64_t chunk_blocks = tsb::kMaxParamIds;
+
+  cudaStream_t s_out_kernel = nullptr, s_out_copy = nullptr;
+  cudaStream_t s_in_copy = nullptr, s_in_kernel = nullptr;
+  cudaEvent_t ev_user = nullptr;
+  cudaEvent_t ev_link = nullptr;
+  tsb::Slot out_slots[tsb::kSlots];
+  tsb::Slot in_slots[tsb::kSlots];
+  int next_out = 0, next_in = 0;
+
+  // hazard tracking: sequence numbers of the last offload (d2h) / reload
+  // (h2d) call touching each host block and device block.
+  std::vector<uint64_t> host_d2h_seq, host_h2d_seq, dev_d2h_seq, dev_h2d_seq;
+  uint64_t d2h_seq = 0, h2d_seq = 0;
+  tsb::CallRec d2h_ring[tsb::kEventRing];
+  tsb::CallRec h2d_ring[tsb::kEventRing];
+
+  // optional per-launch timing of the extract (0) / insert (1) kernels
+  bool profiling = false;
+  std::vector<cudaEvent_t> prof_ev[2];  // start/stop pairs, in launch order
+  std::vector<uint64_t> prof_bytes[2];
+  std::vector<cudaEvent_t> prof_free;
+
+  // mapped pinned error words, one per outstanding event
+  int* err_host = nullptr;
+  std::vector<int> err_free;
+
+  std::mutex mu;
+};
+
+namespace tsb {
+namespace {
+
+// Returns the index of a free error word, or -1 (error recorded).
+int alloc_err_word(ts_manager* m, int** word) {
+  if (m->err_free.empty()) {
+    set_error(TS_RESOURCE_EXHAUSTED, "too many outstanding transfer events");
+    return -1;
+  }
+  const int i = m->err_free.back();
+  m->err_free.pop_back();
+  m->err_host[i] = 0;
+  *word = m->err_host + i;
+  return i;
+}
+
+uint64_t round16(uint64_t v) { return (v + 15) & ~uint64_t(15); }
+
+// Waits (on `stream`) for the call `seq` of the ring if it may still run.
+int wait_for_call(CallRec* ring, uint64_t seq, cudaStream_t stream) {
+  if (seq == 0) return TS_OK;
+  CallRec& r = ring[seq % kEventRing];
+  if (r.seq != seq || r.done == nullptr) return TS_OK;  // recycled => long done
+  TS_CUDA_RET(cudaStreamWaitEvent(stream, r.done, 0), "cross-direction ordering");
+  return TS_OK;
+}
+
+int record_call(CallRec* ring, uint64_t seq, cudaStream_t stream) {
+  CallRec& r = ring[seq % kEventRing];
+  if (r.done == nullptr) {
+    TS_CUDA_RET(cudaEventCreateWithFlags(&r.done, cudaEventDisableTiming), "event create");
+  } else if (r.seq != 0) {
+    // The slot's previous call is kEventRing calls old; make sure it is done
+    // before its record is dropped (later calls may no longer wait on it).
+    TS_CUDA_RET(cudaEventSynchronize(r.done), "event ring recycle");
+  }
+  r.seq = seq;
+  TS_CUDA_RET(cudaEventRecord(r.done, stream), "event record");
+  return TS_OK;
+}
+
+struct Plan {
+  std::vector<int> storages;  // storage indices touched
+  std::vector<int64_t> src, dst;  // per-block ids
+  bool whole = false;             // all storages of the grid
+};
+
+// Validation, coalescing and bounds checks in the reference's order.
+// `to_host` = D2H direction.
+int build_plan(ts_manager* m, bool to_host, const int64_t* src, const int64_t* dst,
+               const int64_t* sizes, int64_t n_src, int64_t n_dst, int64_t n_sizes,
+               int64_t layer_idx, int64_t shard_idx, Plan* plan) {
+  int rc = ts_validate_copy_spec(src, n_src, dst, n_dst, sizes, n_sizes);
+  if (rc != TS_OK) return rc;
+  if (n_src > 0 && n_dst == 0)
+    return set_error(TS_INVALID_ARGUMENT,
+                     "src_offsets, dst_offsets, and sizes must have the same length");
+  if (layer_idx >= m->num_layers || shard_idx >= m->num_shards)
+    return set_error(TS_OUT_OF_RANGE, "layer or shard index out of range");
+  std::vector<int64_t> ones;
+  if (n_src > 0 && n_sizes == 0) {
+    ones.assign(size_t(n_src), 1);
+    sizes = ones.data();
+  }
+  std::vector<int64_t> cs(n_src), cd(n_src), cn(n_src);
+  int64_t runs = 0;
+  ts_coalesce_runs(src, dst, sizes, n_src, cs.data(), cd.data(), cn.data(), &runs);
+  const bool partial = runs > 0;
+
+  plan->storages.clear();
+  for (int l = 0; l < m->num_layers; ++l) {
+    if (layer_idx >= 0 && l != layer_idx) continue;
+    for (int s = 0; s < m->num_shards; ++s) {
+      if (shard_idx >= 0 && s != shard_idx) continue;
+      plan->storages.push_back(l * m->num_shards + s);
+    }
+  }
+  plan->whole = int(plan->storages.size()) == int(m->st.size());
+  if (!plan->whole && m->fp8)
+    return set_error(TS_UNIMPLEMENTED,
+                     "layer / shard restricted copies are not supported on an fp8 host tier");
+
+  // Reference host mirror size per storage: host_blocks * bytes_per_block().
+  const int64_t ref_host_size = m->host_blocks * int64_t(m->bytes_per_block);
+  for (int si : plan->storages) {
+    const Storage& sd = m->st[si];
+    const int64_t bb = int64_t(sd.bb);
+    if (!partial) {
+      // whole-storage copy: physical size against the host mirror
+      if (int64_t(sd.nbytes) > ref_host_size ||
+          (bb > 0 && int64_t(sd.nbytes) / bb > m->host_blocks)) {
+        if (to_host)
+          return set_error(TS_OUT_OF_RANGE, "Copy range exceeds destination host buffer size");
+        return set_error(TS_INVALID_ARGUMENT, "Source host buffer is too small");
+      }
+      continue;
+    }
+    for (int64_t r = 0; r < runs; ++r) {
+      const int64_t so = cs[r] * bb, dof = cd[r] * bb, n = cn[r] * bb;
+      const int64_t host_id_end = (to_host ? cd[r] : cs[r]) + cn[r];
+      if (to_host) {
+        if (so + n > int64_t(sd.nbytes))
+          return set_error(TS_INVALID_ARGUMENT, "Copy range exceeds source device buffer size");
+        if (dof + n > ref_host_size || host_id_end > m->host_blocks)
+          return set_error(TS_INVALID_ARGUMENT, "Copy range exceeds destination host buffer size");
+      } else {
+        if (so + n > ref_host_size || host_id_end > m->host_blocks)
+          return set_error(TS_INVALID_ARGUMENT, "Copy range exceeds source host buffer size");
+        if (dof + n > int64_t(sd.nbytes))
+          return set_error(TS_INVALID_ARGUMENT, "Copy range exceeds destination device buffer size");
+      }
+    }
+  }
+
+  plan->src.clear();
+  plan->dst.clear();
+  if (!partial) {
+    // Whole storages: every block of the largest storage (the kernels skip
+    // ids past a smaller storage's end only when they are out of its bounds,
+    // so restrict to the common block count).
+    int64_t nb = INT64_MAX;
+    for (int si : plan->storages) {
+      const Storage& sd = m->st[si];
+      nb = std::min<int64_t>(nb, sd.bb ? int64_t(sd.nbytes / sd.bb) : 0);
+    }
+    if (nb == INT64_MAX) nb = 0;
+    for (int64_t b = 0; b < nb; ++b) {
+      plan->src.push_back(b);
+      plan->dst.push_back(b);
+    }
+  } else {
+    for (int64_t r = 0; r < runs; ++r)
+      for (int64_t j = 0; j < cn[r]; ++j) {
+        plan->src.push_back(cs[r] + j);
+        plan->dst.push_back(cd[r] + j);
+      }
+  }
+  return TS_OK;
+}
+
+// Frees an event whose work has drained, with the manager lock held.
+void drop_event_locked(ts_event* ev) {
+  if (ev->err_index >= 0) ev->mgr->err_free.push_back(ev->err_index);
+  cudaEventDestroy(ev->start);
+  cudaEventDestroy(ev->done);
+  delete ev;
+}
+
+int make_event(ts_manager* m, ts_event** out) {
+  auto* ev = new ts_event();
+  ev->mgr = m;
+  ev->device = m->device;
+  cudaError_t e = cudaEventCreate(&ev->start);
+  if (e == cudaSuccess) e = cudaEventCreate(&ev->done);
+  if (e != cudaSuccess) {
+    delete ev;
+    return cuda_error(e, "event create");
+  }
+  const int idx = alloc_err_word(m, &ev->err_word);
+  if (idx < 0) {
+    cudaEventDestroy(ev->start);
+    cudaEventDestroy(ev->done);
+    delete ev;
+    return TS_RESOURCE_EXHAUSTED;
+  }
+  ev->err_index = idx;
+  *out = ev;
+  return TS_OK;
+}
+
+// Storage-subset copies (layer / shard restricted): one strided 2-D DMA per
+// run between the device storage and that storage's slot in the host blocks.
+int enqueue_subset(ts_manager* m, bool to_host, const Plan& p, cudaStream_t s) {
+  for (int si : p.storages) {
+    const Storage& sd = m->st[si];
+    size_t i = 0;
+    while (i < p.src.size()) {
+      size_t j = i + 1;
+      while (j < p.src.size() && p.src[j] == p.src[j - 1] + 1 && p.dst[j] == p.dst[j - 1] + 1) ++j;
+      const int64_t n = int64_t(j - i);
+      const int64_t dev_id = to_host ? p.src[i] : p.dst[i];
+      const int64_t host_id = to_host ? p.dst[i] : p.src[i];
+      uint8_t* dev = reinterpret_cast<uint8_t*>(sd.dev_ptr) + uint64_t(dev_id) * sd.bb;
+      uint8_t* host = m->host + uint64_t(host_id) * m->host_pitch + sd.host_off;
+      if (to_host) {
+        TS_CUDA_RET(cudaMemcpy2DAsync(host, m->host_pitch, dev, sd.bb, sd.bb, size_t(n),
+                                      cudaMemcpyDeviceToHost, s),
+                    "D2H storage copy");
+      } else {
+        TS_CUDA_RET(cudaMemcpy2DAsync(dev, sd.bb, host, m->host_pitch, sd.bb, size_t(n),
+                                      cudaMemcpyHostToDevice, s),
+                    "H2D storage copy");
+      }
+      i = j;
+    }
+  }
+  return TS_OK;
+}
+
+cudaEvent_t prof_event(ts_manager* m) {
+  if (!m->prof_free.empty()) {
+    cudaEvent_t e = m->prof_free.back();
+    m->prof_free.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+// Algorithmic HBM bytes of one kernel launch over `cn` blocks.
+uint64_t kernel_bytes(const ts_manager* m, int64_t cn, bool extract) {
+  uint64_t dev = 0, stage = 0;
+  for (const Storage& s : m->st) {
+    dev += s.bb;
+    stage += s.host_bytes;
+  }
+  if (m->fp8) stage += 4 * m->st.size();
+  (void)extract;
+  return uint64_t(cn) * (dev + stage);
+}
+
+int enqueue_transfer(ts_manager* m, bool to_host, const Plan& p, void* user_stream,
+                     ts_event* ev) {
+  cudaStream_t user = reinterpret_cast<cudaStream_t>(user_stream);
+  cudaStream_t ks = to_host ? m->s_out_kernel : m->s_in_kernel;
+  cudaStream_t cs = to_host ? m->s_out_copy : m->s_in_copy;
+  cudaStream_t first = to_host ? ks : cs;
+  cudaStream_t last = to_host ? cs : ks;
+  int* err_dev = nullptr;
+  TS_CUDA_RET(cudaHostGetDevicePointer(reinterpret_cast<void**>(&err_dev), ev->err_word, 0),
+              "error word mapping");
+
+  // Order after the producer's queued work (device data written by the user)
+  TS_CUDA_RET(cudaEventRecord(m->ev_user, user), "event record");
+  TS_CUDA_RET(cudaStreamWaitEvent(first, m->ev_user, 0), "stream wait");
+  if (!to_host) TS_CUDA_RET(cudaStreamWaitEvent(ks, m->ev_user, 0), "stream wait");
+
+  // Cross-direction hazards at block granularity.
+  uint64_t need = 0;
+  if (to_host) {
+    for (size_t i = 0; i < p.src.size(); ++i) {
+      need = std::max(need, m->dev_h2d_seq[size_t(p.src[i])]);
+      need = std::max(need, m->host_h2d_seq[size_t(p.dst[i])]);
+    }
+    int rc = wait_for_call(m->h2d_ring, need, first);
+    if (rc != TS_OK) return rc;
+  } else {
+    for (size_t i = 0; i < p.src.size(); ++i) {
+      need = std::max(need, m->host_d2h_seq[size_t(p.src[i])]);
+      need = std::max(need, m->dev_d2h_seq[size_t(p.dst[i])]);
+    }
+    int rc = wait_for_call(m->d2h_ring, need, first);
+    if (rc != TS_OK) return rc;
+    rc = wait_for_call(m->d2h_ring, need, ks);
+    if (rc != TS_OK) return rc;
+  }
+  TS_CUDA_RET(cudaEventRecord(ev->start, first), "event record");
+
+  if (!p.whole) {
+    int rc = enqueue_subset(m, to_host, p, first);
+    if (rc != TS_OK) return rc;
+    if (last != first) {  // keep `last` the stream that completes every call
+      TS_CUDA_RET(cudaEventRecord(m->ev_link, first), "event record");
+      TS_CUDA_RET(cudaStreamWaitEvent(last, m->ev_link, 0), "stream wait");
+    }
+    TS_CUDA_RET(cudaEventRecord(ev->done, last), "event record");
+    return TS_OK;
+  }
+
+  const int64_t nblk = int64_t(p.src.size());
+  for (int64_t c0 = 0; c0 < nblk; c0 += m->chunk_blocks) {
+    const int64_t cn = std::min<int64_t>(m->chunk_blocks, nblk - c0);
+    Slot& slot = to_host ? m->out_slots[m->next_out] : m->in_slots[m->next_in];
+    if (to_host) m->next_out = (m->next_out + 1) % kSlots;
+    else m->next_in = (m->next_in + 1) % kSlots;
+    ParamIds ids;
+    const std::vector<int64_t>& dev_ids = to_host ? p.src : p.dst;
+    const std::vector<int64_t>& host_ids = to_host ? p.dst : p.src;
+    for (int64_t k = 0; k < cn; ++k) ids.v[k] = dev_ids[size_t(c0 + k)];
+    if (to_host) {
+      TS_CUDA_RET(cudaStreamWaitEvent(ks, slot.free, 0), "stream wait");
+      cudaEvent_t e0 = nullptr, e1 = nullptr;
+      if (m->profiling) {
+        e0 = prof_event(m);
+        e1 = prof_event(m);
+        TS_CUDA_RET(cudaEventRecord(e0, ks), "event record");
+      }
+      int rc = mgr_extract(m->device, m->d_table, int(m->st.size()), ids, cn, slot.buf,
+                           m->host_pitch, err_dev, ks, m->vec_ok, m->max_bb, m->fp8,
+                           m->scale_off);
+      if (rc != TS_OK) return rc;
+      if (m->profiling) {
+        TS_CUDA_RET(cudaEventRecord(e1, ks), "event record");
+        m->prof_ev[0].push_back(e0);
+        m->prof_ev[0].push_back(e1);
+        m->prof_bytes[0].push_back(kernel_bytes(m, cn, true));
+      }
+      TS_CUDA_RET(cudaEventRecord(slot.ready, ks), "event record");
+      TS_CUDA_RET(cudaStreamWaitEvent(cs, slot.ready, 0), "stream wait");
+    } else {
+      TS_CUDA_RET(cudaStreamWaitEvent(cs, slot.free, 0), "stream wait");
+    }
+    // DMAs of maximal runs of consecutive host block ids
+    int64_t k = 0;
+    while (k < cn) {
+      int64_t e = k + 1;
+      while (e < cn && host_ids[size_t(c0 + e)] == host_ids[size_t(c0 + e - 1)] + 1) ++e;
+      uint8_t* h = m->host + uint64_t(host_ids[size_t(c0 + k)]) * m->host_pitch;
+      uint8_t* d = slot.buf + uint64_t(k) * m->host_pitch;
+      const size_t bytes = size_t(e - k) * m->host_pitch;
+      if (to_host) {
+        TS_CUDA_RET(cudaMemcpyAsync(h, d, bytes, cudaMemcpyDeviceToHost, cs), "D2H DMA");
+      } else {
+        TS_CUDA_RET(cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, cs), "H2D DMA");
+      }
+      k = e;
+    }
+    if (to_host) {
+      TS_CUDA_RET(cudaEventRecord(slot.free, cs), "event record");
+    } else {
+      TS_CUDA_RET(cudaEventRecord(slot.ready, cs), "event record");
+      TS_CUDA_RET(cudaStreamWaitEvent(ks, slot.ready, 0), "stream wait");
+      cudaEvent_t e0 = nullptr, e1 = nullptr;
+      if (m->profiling) {
+        e0 = prof_event(m);
+        e1 = prof_event(m);
+        TS_CUDA_RET(cudaEventRecord(e0, ks), "event record");
+      }
+      int rc = mgr_insert(m->device, m->d_table, int(m->st.size()), ids, cn, slot.buf,
+                          m->host_pitch, err_dev, ks, m->vec_ok, m->max_bb, m->fp8,
+                          m->scale_off);
+      if (rc != TS_OK) return rc;
+      if (m->profiling) {
+        TS_CUDA_RET(cudaEventRecord(e1, ks), "event record");
+        m->prof_ev[1].push_back(e0);
+        m->prof_ev[1].push_back(e1);
+        m->prof_bytes[1].push_back(kernel_bytes(m, cn, false));
+      }
+      TS_CUDA_RET(cudaEventRecord(slot.free, ks), "event record");
+    }
+  }
+  TS_CUDA_RET(cudaEventRecord(ev->done, last), "event record");
+  return TS_OK;
+}
+
+int transfer(ts_manager* m, bool to_host, const int64_t* src, const int64_t* dst,
+             const int64_t* sizes, int64_t n_src, int64_t n_dst, int64_t n_sizes,
+             int64_t layer_idx, int64_t shard_idx, void* stream, ts_event** out) {
+  clear_error();
+  if (!m || !out) return set_error(TS_INVALID_ARGUMENT, "null manager or output");
+  *out = nullptr;
+  Plan p;
+  int rc = build_plan(m, to_host, src, dst, sizes, n_src, n_dst, n_sizes, layer_idx,
+                      shard_idx, &p);
+  if (rc != TS_OK) return rc;
+  std::lock_guard<std::mutex> lock(m->mu);
+  DeviceGuard g(m->device);
+  ts_event* ev = nullptr;
+  rc = make_event(m, &ev);
+  if (rc != TS_OK) return rc;
+  rc = enqueue_transfer(m, to_host, p, stream, ev);
+  if (rc != TS_OK) {
+    // Work already queued stays ordered on the manager's streams; drain it so
+    // the error word can be recycled safely.
+    cudaStreamSynchronize(m->s_out_copy);
+    cudaStreamSynchronize(m->s_in_kernel);
+    cudaStreamSynchronize(m->s_out_kernel);
+    cudaStreamSynchronize(m->s_in_copy);
+    std::string msg = ts_last_error();
+    drop_event_locked(ev);
+    return set_error(rc, msg);
+  }
+  cudaStream_t last = to_host ? m->s_out_copy : m->s_in_kernel;
+  const uint64_t seq = to_host ? ++m->d2h_seq : ++m->h2d_seq;
+  rc = record_call(to_host ? m->d2h_ring : m->h2d_ring, seq, last);
+  if (rc != TS_OK) {
+    cudaEventSynchronize(ev->done);
+    drop_event_locked(ev);
+    return rc;
+  }
+  for (size_t i = 0; i < p.src.size(); ++i) {
+    if (to_host) {
+      m->dev_d2h_seq[size_t(p.src[i])] = seq;
+      m->host_d2h_seq[size_t(p.dst[i])] = seq;
+    } else {
+      m->host_h2d_seq[size_t(p.src[i])] = seq;
+      m->dev_h2d_seq[size_t(p.dst[i])] = seq;
+    }
+  }
+  *out = ev;
+  return TS_OK;
+}
+
+void destroy_resources(ts_manager* m) {
+  DeviceGuard g(m->device);
+  for (cudaStream_t s : {m->s_out_kernel, m->s_out_copy, m->s_in_copy, m->s_in_kernel})
+    if (s) cudaStreamSynchronize(s);
+  for (Slot* slots : {m->out_slots, m->in_slots})
+    for (int i = 0; i < kSlots; ++i) {
+      if (slots[i].buf) cudaFree(slots[i].buf);
+      if (slots[i].ready) cudaEventDestroy(slots[i].ready);
+      if (slots[i].free) cudaEventDestroy(slots[i].free);
+    }
+  for (CallRec* ring : {m->d2h_ring, m->h2d_ring})
+    for (int i = 0; i < kEventRing; ++i)
+      if (ring[i].done) cudaEventDestroy(ring[i].done);
+  for (cudaStream_t s : {m->s_out_kernel, m->s_out_copy, m->s_in_copy, m->s_in_kernel})
+    if (s) cudaStreamDestroy(s);
+  for (int k = 0; k < 2; ++k)
+    for (cudaEvent_t e : m->prof_ev[k]) cudaEventDestroy(e);
+  for (cudaEvent_t e : m->prof_free) cudaEventDestroy(e);
+  if (m->ev_user) cudaEventDestroy(m->ev_user);
+  if (m->ev_link) cudaEventDestroy(m->ev_link);
+  if (m->d_table) cudaFree(m->d_table);
+  if (m->err_host) cudaFreeHost(m->err_host);
+  if (m->tier) ts_host_tier_destroy(m->tier, 0);
+}
+
+}  // namespace
+}  // namespace tsb
+
+using tsb::set_error;
+using tsb::set_errorf;
+
+extern "C" int ts_mgr_create(const ts_storage_desc* storages, int num_layers,
+                             int num_shards, const ts_manager_opts* opts,
+                             ts_manager** out) {
+  tsb::clear_error();
+  if (!out) return set_error(TS_INVALID_ARGUMENT, "out must not be null");
+  *out = nullptr;
+  if (num_layers <= 0 || num_shards <= 0 || !storages)
+    return set_error(TS_INVALID_ARGUMENT, "need at least one layer and one shard");
+  auto* m = new ts_manager();
+  m->num_layers = num_layers;
+  m->num_shards = num_shards;
+  m->device = storages[0].device;
+  m->major_dim = storages[0].dim0;
+  if (m->major_dim <= 0) {
+    delete m;
+    return set_error(TS_INVALID_ARGUMENT, "storage dim 0 must be positive");
+  }
+  m->host_blocks = opts && opts->host_blocks > 0 ? opts->host_blocks : 64;
+  m->fp8 = opts && opts->fp8;
+  if (opts && opts->chunk_blocks > 0)
+    m->chunk_blocks = std::min<int64_t>(opts->chunk_blocks, tsb::kMaxParamIds);
+  const int n = num_layers * num_shards;
+  m->st.resize(size_t(n));
+  // reference: slice_byte_size from layer 0, shard 0 (GetMajorSliceByteSize)
+  m->bytes_per_block = storages[0].nbytes / uint64_t(m->major_dim);
+  uint64_t off = 0;
+  int64_t max_dev_blocks = 0;
+  for (int i = 0; i < n; ++i) {
+    const ts_storage_desc& d = storages[i];
+    if (d.device != m->device) {
+      delete m;
+      return set_error(TS_INVALID_ARGUMENT,
+                       "all storages of one manager must live on one CUDA device "
+                       "(create one manager per GPU)");
+    }
+    const int layer = i / num_shards;
+    const ts_storage_desc& shard0 = storages[layer * num_shards];
+    if (d.nbytes < shard0.nbytes) {
+      delete m;
+      return set_error(TS_INVALID_ARGUMENT, "Device buffer shard size smaller than physical size");
+    }
+    tsb::Storage& s = m->st[size_t(i)];
+    s.dev_ptr = d.dev_ptr;
+    s.nbytes = d.nbytes;
+    s.dim0 = d.dim0;
+    s.bb = shard0.nbytes / uint64_t(m->major_dim);
+    s.host_bytes = m->fp8 ? s.bb / 2 : s.bb;
+    if (m->fp8 && (s.bb % 32) != 0) {
+      delete m;
+      return set_error(TS_INVALID_ARGUMENT, "fp8 tier needs block bytes that are a multiple of 32");
+    }
+    s.host_off = off;
+    off += tsb::round16(s.host_bytes);
+    if (s.bb) max_dev_blocks = std::max<int64_t>(max_dev_blocks, int64_t(s.nbytes / s.bb));
+    m->max_bb = std::max(m->max_bb, s.bb);
+    m->vec_ok = m->vec_ok && (s.dev_ptr % 16 == 0) && (s.bb % 16 == 0);
+  }
+  if (m->fp8) {
+    m->scale_off = off;
+    off += tsb::round16(uint64_t(n) * 4);
+  }
+  m->host_pitch = tsb::round16(off);
+
+  tsb::DeviceGuard g(m->device);
+  int rc = TS_OK;
+  auto fail = [&](int code) {
+    tsb::destroy_resources(m);
+    delete m;
+    return code;
+  };
+  const char* shm = opts ? opts->shm_name : nullptr;
+  const char* uid = opts && opts->model_uid ? opts->model_uid : "";
+  uint64_t geometry = m->host_pitch * 1000003ull ^ uint64_t(n) * 7919ull ^ (m->fp8 ? 1 : 0);
+  int warm = 0;
+  rc = ts_host_tier_create(uint64_t(m->host_blocks) * m->host_pitch, shm, uid, geometry, 1,
+                           &m->tier, &warm);
+  if (rc != TS_OK) return fail(rc);
+  m->host = static_cast<uint8_t*>(ts_host_tier_ptr(m->tier));
+  if (!warm && (shm == nullptr || shm[0] == '\0')) {
+    // reference zero-fills its mirrors (posix_memalign + memset); anonymous
+    // mmap pages are already zero.
+  }
+
+  // device table
+  std::vector<ts_block_storage> table(static_cast<size_t>(n));
+  for (int i = 0; i < n; ++i) {
+    table[size_t(i)] = {m->st[size_t(i)].dev_ptr, m->st[size_t(i)].bb, m->st[size_t(i)].nbytes,
+                        m->st[size_t(i)].host_off};
+  }
+  cudaError_t e = cudaMalloc(&m->d_table, sizeof(ts_block_storage) * size_t(n));
+  if (e == cudaSuccess)
+    e = cudaMemcpy(m->d_table, table.data(), sizeof(ts_block_storage) * size_t(n),
+                   cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return fail(tsb::cuda_error(e, "storage table upload"));
+
+  for (cudaStream_t* s : {&m->s_out_kernel, &m->s_out_copy, &m->s_in_copy, &m->s_in_kernel}) {
+    e = cudaStreamCreateWithFlags(s, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return fail(tsb::cuda_error(e, "stream create"));
+  }
+  e = cudaEventCreateWithFlags(&m->ev_user, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&m->ev_link, cudaEventDisableTiming);
+  if (e != cudaSuccess) return fail(tsb::cuda_error(e, "event create"));
+  const size_t slot_bytes = size_t(m->chunk_blocks) * m->host_pitch;
+  for (tsb::Slot* slots : {m->out_slots, m->in_slots})
+    for (int i = 0; i < tsb::kSlots; ++i) {
+      e = cudaMalloc(&slots[i].buf, slot_bytes);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&slots[i].ready, cudaEventDisableTiming);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&slots[i].free, cudaEventDisableTiming);
+      if (e != cudaSuccess) return fail(tsb::cuda_error(e, "staging slot"));
+    }
+  e = cudaHostAlloc(reinterpret_cast<void**>(&m->err_host), sizeof(int) * tsb::kErrWords,
+                    cudaHostAllocMapped | cudaHostAllocPortable);
+  if (e != cudaSuccess) return fail(tsb::cuda_error(e, "error words"));
+  for (int i = tsb::kErrWords - 1; i >= 0; --i) m->err_free.push_back(i);
+  m->host_d2h_seq.assign(size_t(m->host_blocks), 0);
+  m->host_h2d_seq.assign(size_t(m->host_blocks), 0);
+  m->dev_d2h_seq.assign(size_t(max_dev_blocks), 0);
+  m->dev_h2d_seq.assign(size_t(max_dev_blocks), 0);
+  *out = m;
+  return TS_OK;
+}
+
+extern "C" int ts_mgr_destroy(ts_manager* mgr) {
+  tsb::clear_error();
+  if (!mgr) return TS_OK;
+  tsb::destroy_resources(mgr);
+  delete mgr;
+  return TS_OK;
+}
+
+extern "C" int ts_d2h(ts_manager* mgr, const int64_t* src, const int64_t* dst,
+                      const int64_t* sizes, int64_t n_src, int64_t n_dst,
+                      int64_t n_sizes, int64_t layer_idx, int64_t shard_idx,
+                      void* stream, ts_event** out) {
+  return tsb::transfer(mgr, true, src, dst, sizes, n_src, n_dst, n_sizes, layer_idx,
+                       shard_idx, stream, out);
+}
+
+extern "C" int ts_h2d(ts_manager* mgr, const int64_t* src, const int64_t* dst,
+                      const int64_t* sizes, int64_t n_src, int64_t n_dst,
+                      int64_t n_sizes, int64_t layer_idx, int64_t shard_idx,
+                      void* stream, ts_event** out) {
+  return tsb::transfer(mgr, false, src, dst, sizes, n_src, n_dst, n_sizes, layer_idx,
+                       shard_idx, stream, out);
+}
+
+extern "C" int ts_mgr_host_block_ptr(ts_manager* mgr, int64_t layer_idx, int64_t shard_idx,
+                                     int64_t block_id, uint64_t* ptr_out,
+                                     uint64_t* bytes_out) {
+  tsb::clear_error();
+  if (!mgr) return set_error(TS_INVALID_ARGUMENT, "null manager");
+  if (layer_idx < 0 || layer_idx >= mgr->num_layers || shard_idx < 0 ||
+      shard_idx >= mgr->num_shards)
+    return set_error(TS_OUT_OF_RANGE, "layer or shard index out of range");
+  if (block_id < 0 || block_id >= mgr->host_blocks)
+    return set_errorf(TS_OUT_OF_RANGE, "Invalid host block ID: %lld", (long long)block_id);
+  const tsb::Storage& s = mgr->st[size_t(layer_idx * mgr->num_shards + shard_idx)];
+  if (ptr_out)
+    *ptr_out = reinterpret_cast<uint64_t>(mgr->host + uint64_t(block_id) * mgr->host_pitch +
+                                          s.host_off);
+  if (bytes_out) *bytes_out = s.host_bytes;
+  return TS_OK;
+}
+
+extern "C" int ts_mgr_info(ts_manager* mgr, int64_t* host_blocks, uint64_t* host_block_pitch,
+                           int64_t* major_dim, uint64_t* bytes_per_block) {
+  tsb::clear_error();
+  if (!mgr) return set_error(TS_INVALID_ARGUMENT, "null manager");
+  if (host_blocks) *host_blocks = mgr->host_blocks;
+  if (host_block_pitch) *host_block_pitch = mgr->host_pitch;
+  if (major_dim) *major_dim = mgr->major_dim;
+  if (bytes_per_block) *bytes_per_block = mgr->bytes_per_block;
+  return TS_OK;
+}
+
+extern "C" int ts_mgr_set_profiling(ts_manager* mgr, int on) {
+  tsb::clear_error();
+  if (!mgr) return set_error(TS_INVALID_ARGUMENT, "null manager");
+  std::lock_guard<std::mutex> lock(mgr->mu);
+  mgr->profiling = on != 0;
+  return TS_OK;
+}
+
+extern "C" int ts_mgr_kernel_stats(ts_manager* mgr, int which, int64_t* launches,
+                                   double* total_ms, uint64_t* bytes) {
+  tsb::clear_error();
+  if (!mgr || which < 0 || which > 1) return set_error(TS_INVALID_ARGUMENT, "bad arguments");
+  std::lock_guard<std::mutex> lock(mgr->mu);
+  tsb::DeviceGuard g(mgr->device);
+  double ms = 0;
+  uint64_t b = 0;
+  std::vector<cudaEvent_t>& ev = mgr->prof_ev[which];
+  for (size_t i = 0; i + 1 < ev.size(); i += 2) {
+    TS_CUDA_RET(cudaEventSynchronize(ev[i + 1]), "profiling event");
+    float t = 0;
+    TS_CUDA_RET(cudaEventElapsedTime(&t, ev[i], ev[i + 1]), "profiling event");
+    ms += t;
+  }
+  for (uint64_t x : mgr->prof_bytes[which]) b += x;
+  if (launches) *launches = int64_t(ev.size() / 2);
+  if (total_ms) *total_ms = ms;
+  if (bytes) *bytes = b;
+  for (cudaEvent_t e : ev) mgr->prof_free.push_back(e);
+  ev.clear();
+  mgr->prof_bytes[which].clear();
+  return TS_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Events
+// ---------------------------------------------------------------------------
+
+extern "C" int ts_event_query(ts_event* ev) {
+  tsb::clear_error();
+  if (!ev) return set_error(TS_INVALID_ARGUMENT, "null event");
+  if (ev->finished) {
+    if (ev->status != TS_OK) tsb::set_error(ev->status, ev->message);
+    return ev->status;
+  }
+  tsb::DeviceGuard g(ev->device);
+  cudaError_t e = cudaEventQuery(ev->done);
+  if (e == cudaErrorNotReady) return TS_PENDING;
+  ev->finished = true;
+  if (e != cudaSuccess) {
+    ev->status = tsb::cuda_error(e, "transfer");
+    ev->message = ts_last_error();
+    return ev->status;
+  }
+  const int word = *reinterpret_cast<volatile int*>(ev->err_word);
+  if (word != 0) {
+    ev->status = TS_INTERNAL;
+    ev->message = "block id out of the storage bounds in the transfer kernel";
+    return set_error(ev->status, ev->message);
+  }
+  ev->status = TS_OK;
+  return TS_OK;
+}
+
+extern "C" int ts_event_wait(ts_event* ev, int64_t timeout_ms) {
+  if (!ev) return set_error(TS_INVALID_ARGUMENT, "null event");
+  const auto t0 = std::chrono::steady_clock::now();
+  int sleep_us = 2;
+  for (;;) {
+    const int rc = ts_event_query(ev);
+    if (rc != TS_PENDING) return rc;
+    if (timeout_ms >= 0 &&
+        std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms))
+      return set_error(TS_DEADLINE_EXCEEDED, "transfer did not complete before the timeout");
+    std::this_thread::sleep_for(std::chrono::microseconds(sleep_us));
+    sleep_us = std::min(sleep_us * 2, 200);
+  }
+}
+
+extern "C" int ts_event_error(ts_event* ev, char* buf, size_t len) {
+  if (!ev || !buf || len == 0) return TS_INVALID_ARGUMENT;
+  const std::string msg = ev->finished && ev->status != TS_OK ? ev->message : std::string();
+  std::snprintf(buf, len, "%s", msg.c_str());
+  return TS_OK;
+}
+
+extern "C" int ts_event_stream_wait(ts_event* ev, void* stream) {
+  tsb::clear_error();
+  if (!ev) return set_error(TS_INVALID_ARGUMENT, "null event");
+  TS_CUDA_RET(cudaStreamWaitEvent(reinterpret_cast<cudaStream_t>(stream), ev->done, 0),
+              "stream wait");
+  return TS_OK;
+}
+
+extern "C" int ts_event_elapsed_ms(ts_event* ev, float* ms) {
+  tsb::clear_error();
+  if (!ev || !ms) return set_error(TS_INVALID_ARGUMENT, "null argument");
+  TS_CUDA_RET(cudaEventElapsedTime(ms, ev->start, ev->done), "elapsed time");
+  return TS_OK;
+}
+
+extern "C" void ts_event_release(ts_event* ev) {
+  if (!ev) return;
+  tsb::DeviceGuard g(ev->device);
+  // The kernels of a pending transfer may still write its error word.
+  if (!ev->finished) cudaEventSynchronize(ev->done);
+  if (ev->mgr && ev->err_index >= 0) {
+    std::lock_guard<std::mutex> lock(ev->mgr->mu);
+    ev->mgr->err_free.push_back(ev->err_index);
+  }
+  cudaEventDestroy(ev->start);
+  cudaEventDestroy(ev->done);
+  delete ev;
+}

@@ -1,0 +1,110 @@
+// Error plumbing, device queries and the pure host copy-spec logic.
+//
+// ts_validate_copy_spec restates ValidateOffsetsAndSizes
+// (tpu_sync/kv_cache/kv_cache_manager_base.cc:72-102) with the same checks,
+// order, codes and messages; ts_coalesce_runs restates CoalesceMajorDimCopies
+// (tpu_sync/kv_cache/kv_cache_manager_base.cc:121-141).
+
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "ts_internal.h"
+
+namespace tsb {
+namespace {
+thread_local std::string g_last_error;
+}
+
+int set_error(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int set_errorf(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+void clear_error() { g_last_error.clear(); }
+
+int cuda_error(cudaError_t e, const char* what) {
+  const int code = e == cudaErrorMemoryAllocation ? TS_RESOURCE_EXHAUSTED : TS_INTERNAL;
+  return set_errorf(code, "%s: CUDA error %d (%s)", what, int(e), cudaGetErrorString(e));
+}
+
+int sm_count(int device) {
+  static std::mutex mu;
+  static std::vector<int> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  if (device < 0) device = 0;
+  if (size_t(device) >= cache.size()) cache.resize(device + 1, 0);
+  if (cache[device] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[device] = n;
+  }
+  return cache[device];
+}
+
+}  // namespace tsb
+
+extern "C" const char* ts_last_error(void) { return tsb::g_last_error.c_str(); }
+
+extern "C" const char* ts_version(void) { return "tpusync_b200 0.1.0 (sm_100a)"; }
+
+extern "C" int ts_validate_copy_spec(const int64_t* src, int64_t n_src,
+                                     const int64_t* dst, int64_t n_dst,
+                                     const int64_t* sizes, int64_t n_sizes) {
+  tsb::clear_error();
+  if (n_src < 0 || n_dst < 0 || n_sizes < 0)
+    return tsb::set_error(TS_INVALID_ARGUMENT, "list lengths must be non-negative");
+  if (n_dst != 0 && n_src != n_dst)
+    return tsb::set_error(TS_INVALID_ARGUMENT,
+                          "src_offsets, dst_offsets, and sizes must have the same length");
+  if (n_sizes != 0 && n_src != n_sizes)
+    return tsb::set_error(TS_INVALID_ARGUMENT,
+                          "src_offsets, dst_offsets, and sizes must have the same length");
+  for (int64_t i = 0; i < n_src; ++i)
+    if (src[i] < 0)
+      return tsb::set_error(TS_INVALID_ARGUMENT, "copy offsets and sizes must be non-negative");
+  for (int64_t i = 0; i < n_dst; ++i)
+    if (dst[i] < 0)
+      return tsb::set_error(TS_INVALID_ARGUMENT, "copy offsets and sizes must be non-negative");
+  for (int64_t i = 0; i < n_sizes; ++i)
+    if (sizes[i] < 0)
+      return tsb::set_error(TS_INVALID_ARGUMENT, "copy offsets and sizes must be non-negative");
+  return TS_OK;
+}
+
+extern "C" int ts_coalesce_runs(const int64_t* src, const int64_t* dst,
+                                const int64_t* sizes, int64_t n, int64_t* out_src,
+                                int64_t* out_dst, int64_t* out_sizes,
+                                int64_t* n_out) {
+  tsb::clear_error();
+  if (!n_out) return tsb::set_error(TS_INVALID_ARGUMENT, "n_out must not be null");
+  int64_t m = 0;
+  for (int64_t i = 0; i < n; ++i) {
+    if (m > 0 && src[i] == out_src[m - 1] + out_sizes[m - 1] &&
+        dst[i] == out_dst[m - 1] + out_sizes[m - 1]) {
+      out_sizes[m - 1] += sizes[i];
+    } else {
+      out_src[m] = src[i];
+      out_dst[m] = dst[i];
+      out_sizes[m] = sizes[i];
+      ++m;
+    }
+  }
+  *n_out = m;
+  return TS_OK;
+}

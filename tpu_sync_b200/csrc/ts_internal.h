@@ -1,0 +1,68 @@
+// Internal helpers shared by the C-ABI translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "tpusync_b200.h"
+
+namespace tsb {
+
+// Records `msg` as the calling thread's last error and returns `code`.
+int set_error(int code, const std::string& msg);
+int set_errorf(int code, const char* fmt, ...);
+void clear_error();
+
+// Maps a CUDA runtime error to a ts_status (and records the message).
+int cuda_error(cudaError_t e, const char* what);
+
+// Number of SMs of `device` (cached).
+int sm_count(int device);
+
+// Block ids passed by value in kernel parameters (one pipelined chunk).
+constexpr int kMaxParamIds = 64;
+struct ParamIds {
+  int64_t v[kMaxParamIds];
+#ifdef __CUDACC__
+  __device__ __forceinline__ int64_t operator[](int64_t k) const { return v[k]; }
+#endif
+};
+
+// Chunk launchers of kv_block_kernels.cu used by the manager.
+int mgr_extract(int device, const ts_block_storage* d_st, int n_st,
+                const ParamIds& ids, int64_t n_blocks, void* staging,
+                uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
+                uint64_t max_bb, bool fp8, uint64_t scale_off);
+int mgr_insert(int device, const ts_block_storage* d_st, int n_st,
+               const ParamIds& ids, int64_t n_blocks, const void* staging,
+               uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
+               uint64_t max_bb, bool fp8, uint64_t scale_off);
+
+// Scoped switch of the current CUDA device.
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int device) {
+    cudaGetDevice(&prev_);
+    if (prev_ != device) cudaSetDevice(device);
+    dev_ = device;
+  }
+  ~DeviceGuard() {
+    if (prev_ != dev_) cudaSetDevice(prev_);
+  }
+
+ private:
+  int prev_ = 0;
+  int dev_ = 0;
+};
+
+}  // namespace tsb
+
+#define TS_CUDA_RET(expr, what)                      \
+  do {                                               \
+    cudaError_t _e = (expr);                         \
+    if (_e != cudaSuccess) return tsb::cuda_error(_e, what); \
+  } while (0)

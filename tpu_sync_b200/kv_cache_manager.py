@@ -1,0 +1,329 @@
+"""KVCacheManager / RaidenFuture over the B200 C ABI.
+
+Mirrors the reference's torch surface (tpu_sync/api/torch/kv_cache_manager.py:55-448
+and the nanobind binding tpu_sync/frameworks/torch/tpu_raiden_torch_module.cc:179-496):
+same class names, method names, argument meaning, block-unit offsets, the
+``copy_sizes=[1]*n`` default, RuntimeError messages prefixed
+"KVCacheManager D2h failed: " / "KVCacheManager H2d failed: " and futures
+whose ``Await()`` raises "Async copy failed: ...".
+
+Data enters as torch CUDA tensors: each (layer, shard) storage is a contiguous
+CUDA tensor whose dim 0 indexes blocks.  The manager owns a pinned host tier
+of ``host_blocks_to_allocate`` blocks (block-major: host block h holds block
+h of every storage contiguously).
+
+The control-plane arguments of the reference constructor (ports, controller
+address, worker id, staging slots for the TCP hand-off) are accepted for
+signature compatibility and have no effect: there is no network path here.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Any, Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+import torch
+
+from tpu_sync_b200 import _native
+
+
+def _storage_grid(kv_caches) -> List[List[torch.Tensor]]:
+  if isinstance(kv_caches, torch.Tensor):
+    raise TypeError("kv_caches must be a list of tensors or a list of lists")
+  grid = []
+  for layer in kv_caches:
+    if isinstance(layer, torch.Tensor):
+      grid.append([layer])
+    else:
+      grid.append(list(layer))
+  if not grid or not grid[0]:
+    raise ValueError("kv_caches must hold at least one storage")
+  nshards = len(grid[0])
+  for layer in grid:
+    if len(layer) != nshards:
+      raise RuntimeError("Number of shards mismatch across layers")
+    for t in layer:
+      if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError("every storage must be a CUDA tensor")
+      if not t.is_contiguous():
+        raise ValueError("every storage must be contiguous")
+      if t.dim() == 0:
+        raise ValueError("storages need a block dimension (dim 0)")
+  return grid
+
+
+class RaidenFuture:
+  """Completion handle of one transfer (reference RaidenFuture)."""
+
+  def __init__(self, handle: int, keepalive: Any = None):
+    self._handle = ctypes.c_void_p(handle)
+    self._keepalive = keepalive
+
+  def _h(self):
+    if not self._handle:
+      raise RuntimeError("future already released")
+    return self._handle
+
+  def Await(self, timeout_s: Optional[float] = None) -> None:
+    timeout_ms = -1 if timeout_s is None else int(timeout_s * 1000)
+    rc = _native.lib().ts_event_wait(self._h(), timeout_ms)
+    if rc != _native.OK:
+      raise RuntimeError("Async copy failed: " + _native.last_error())
+
+  wait = Await
+
+  def IsReady(self) -> bool:
+    return _native.lib().ts_event_query(self._h()) != _native.PENDING
+
+  is_ready = IsReady
+
+  def ok(self) -> bool:
+    rc = _native.lib().ts_event_query(self._h())
+    return rc in (_native.OK, _native.PENDING)
+
+  def error_message(self) -> str:
+    rc = _native.lib().ts_event_query(self._h())
+    if rc in (_native.OK, _native.PENDING):
+      return ""
+    buf = ctypes.create_string_buffer(1024)
+    _native.lib().ts_event_error(self._h(), buf, 1024)
+    return buf.value.decode()
+
+  def stream_wait(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+    """Makes `stream` (default: current) wait for the transfer on the device."""
+    s = stream if stream is not None else torch.cuda.current_stream()
+    _native.check(_native.lib().ts_event_stream_wait(self._h(), ctypes.c_void_p(s.cuda_stream)))
+
+  def elapsed_ms(self) -> float:
+    """Device time from the transfer's first queued operation to its end."""
+    self.Await()
+    ms = ctypes.c_float()
+    _native.check(_native.lib().ts_event_elapsed_ms(self._h(), ctypes.byref(ms)))
+    return float(ms.value)
+
+  def release(self) -> None:
+    if self._handle:
+      _native.lib().ts_event_release(self._handle)
+      self._handle = ctypes.c_void_p(0)
+      self._keepalive = None
+
+  def __del__(self):
+    try:
+      self.release()
+    except Exception:  # interpreter shutdown
+      pass
+
+
+class KVCacheManager:
+  """Paged KV block offload / reload between HBM and a pinned host tier."""
+
+  def __init__(
+      self,
+      kv_caches: List[Any],
+      local_control_port: int = 0,
+      max_blocks: Optional[int] = None,
+      num_slots: Optional[int] = None,
+      timeout_s: float = 120.0,
+      unsafe_skip_buffer_lock: bool = True,
+      host_blocks_to_allocate: Optional[int] = None,
+      parallelism: int = 4,
+      node_id: int = 0,
+      listener_port: Optional[int] = None,
+      raiden_worker_port: int = 0,
+      raiden_controller_address: Optional[str] = None,
+      worker_id: Optional[str] = None,
+      *,
+      shm_name: str = "",
+      model_uid: str = "",
+      fp8: bool = False,
+      chunk_blocks: int = 0,
+  ):
+    if host_blocks_to_allocate is None:
+      if max_blocks is None or num_slots is None:
+        raise ValueError(
+            "Must specify either (max_blocks, num_slots) or"
+            " host_blocks_to_allocate.")
+      host_blocks_to_allocate = int(max_blocks) * int(num_slots)
+    grid = _storage_grid(kv_caches)
+    self._grid = grid
+    self._node_id = node_id
+    self._timeout_s = timeout_s
+    self.num_layers = len(grid)
+    self.num_shards = len(grid[0])
+    descs = (_native.StorageDesc * (self.num_layers * self.num_shards))()
+    i = 0
+    for layer in grid:
+      for t in layer:
+        descs[i].dev_ptr = t.data_ptr()
+        descs[i].nbytes = t.numel() * t.element_size()
+        descs[i].dim0 = t.shape[0]
+        descs[i].device = t.device.index
+        i += 1
+    opts = _native.ManagerOpts(
+        host_blocks=int(host_blocks_to_allocate), chunk_blocks=int(chunk_blocks),
+        shm_name=shm_name.encode(), model_uid=model_uid.encode(), fp8=int(fp8))
+    handle = ctypes.c_void_p()
+    rc = _native.lib().ts_mgr_create(descs, self.num_layers, self.num_shards,
+                                     ctypes.byref(opts), ctypes.byref(handle))
+    if rc != _native.OK:
+      raise RuntimeError(_native.last_error())
+    self._mgr = handle
+    self.device = grid[0][0].device
+    hb, pitch, major, bpb = (ctypes.c_int64(), ctypes.c_uint64(), ctypes.c_int64(),
+                             ctypes.c_uint64())
+    _native.check(_native.lib().ts_mgr_info(self._mgr, ctypes.byref(hb),
+                                            ctypes.byref(pitch), ctypes.byref(major),
+                                            ctypes.byref(bpb)))
+    self.host_blocks = hb.value
+    self.host_block_pitch = pitch.value
+    self.major_dim = major.value
+    self.bytes_per_block = bpb.value
+    self.slice_byte_size = bpb.value
+    self.fp8 = fp8
+
+  # -- reference properties ------------------------------------------------
+  @property
+  def node_id(self) -> int:
+    return self._node_id
+
+  @property
+  def local_port(self) -> Optional[int]:
+    return None
+
+  def close(self) -> None:
+    if getattr(self, "_mgr", None):
+      _native.lib().ts_mgr_destroy(self._mgr)
+      self._mgr = None
+
+  def __del__(self):
+    try:
+      self.close()
+    except Exception:
+      pass
+
+  # -- transfers -----------------------------------------------------------
+  def _transfer(self, fn, what, src_offsets, dst_offsets, copy_sizes, layer_idx,
+                shard_idx, stream):
+    if copy_sizes is None:
+      copy_sizes = [1] * len(src_offsets)
+    src = _native.i64_array(src_offsets)
+    dst = _native.i64_array(dst_offsets)
+    sizes = _native.i64_array(copy_sizes)
+    if stream is None:
+      stream = torch.cuda.current_stream(self.device)
+    ev = ctypes.c_void_p()
+    rc = fn(self._mgr, _native.i64_ptr(src), _native.i64_ptr(dst),
+            _native.i64_ptr(sizes), src.size, dst.size, sizes.size,
+            -1 if layer_idx is None else int(layer_idx),
+            -1 if shard_idx is None else int(shard_idx),
+            ctypes.c_void_p(stream.cuda_stream), ctypes.byref(ev))
+    if rc != _native.OK:
+      raise RuntimeError(f"KVCacheManager {what} failed: " + _native.last_error())
+    return RaidenFuture(ev.value, keepalive=self)
+
+  def d2h(self, src_offsets: List[int], dst_offsets: List[int],
+          copy_sizes: Optional[List[int]] = None, *, layer_idx: Optional[int] = None,
+          shard_idx: Optional[int] = None,
+          stream: Optional[torch.cuda.Stream] = None) -> RaidenFuture:
+    """Device-to-host copy of blocks (block units); returns a future."""
+    return self._transfer(_native.lib().ts_d2h, "D2h", src_offsets, dst_offsets,
+                          copy_sizes, layer_idx, shard_idx, stream)
+
+  def h2d(self, src_offsets: List[int], dst_offsets: List[int],
+          copy_sizes: Optional[List[int]] = None, *, layer_idx: Optional[int] = None,
+          shard_idx: Optional[int] = None,
+          stream: Optional[torch.cuda.Stream] = None) -> RaidenFuture:
+    """Host-to-device copy of blocks (block units); returns a future."""
+    return self._transfer(_native.lib().ts_h2d, "H2d", src_offsets, dst_offsets,
+                          copy_sizes, layer_idx, shard_idx, stream)
+
+  # nanobind-style spellings of the reference binding
+  def D2h(self, src_offsets_major_dim=(), dst_offsets_major_dim=(),
+          copy_sizes_major_dim=()):
+    return self._transfer(_native.lib().ts_d2h, "D2h", list(src_offsets_major_dim),
+                          list(dst_offsets_major_dim), list(copy_sizes_major_dim),
+                          None, None, None)
+
+  def H2d(self, src_offsets_major_dim=(), dst_offsets_major_dim=(),
+          copy_sizes_major_dim=()):
+    return self._transfer(_native.lib().ts_h2d, "H2d", list(src_offsets_major_dim),
+                          list(dst_offsets_major_dim), list(copy_sizes_major_dim),
+                          None, None, None)
+
+  # -- kernel timing -------------------------------------------------------
+  def set_profiling(self, on: bool = True) -> None:
+    """Times every extract / insert kernel launch with CUDA events."""
+    _native.check(_native.lib().ts_mgr_set_profiling(self._mgr, int(bool(on))))
+
+  def kernel_stats(self, which: str = "extract") -> Dict[str, float]:
+    """Launches, summed device ms and algorithmic bytes since the last call."""
+    n, ms, b = ctypes.c_int64(), ctypes.c_double(), ctypes.c_uint64()
+    _native.check(_native.lib().ts_mgr_kernel_stats(
+        self._mgr, 0 if which == "extract" else 1, ctypes.byref(n), ctypes.byref(ms),
+        ctypes.byref(b)))
+    return {"launches": n.value, "ms": ms.value, "bytes": b.value}
+
+  # -- host tier access ----------------------------------------------------
+  def _host_block(self, layer_idx: int, block_id: int, shard_idx: int = 0):
+    ptr, nbytes = ctypes.c_uint64(), ctypes.c_uint64()
+    rc = _native.lib().ts_mgr_host_block_ptr(self._mgr, int(layer_idx), int(shard_idx),
+                                             int(block_id), ctypes.byref(ptr),
+                                             ctypes.byref(nbytes))
+    return rc, ptr.value, nbytes.value
+
+  def read_block_bytes(self, layer_idx: int, block_id: int, shard_idx: int = 0) -> bytes:
+    """Returns one host block of one storage as bytes."""
+    rc, ptr, nbytes = self._host_block(layer_idx, block_id, shard_idx)
+    if rc != _native.OK:
+      raise RuntimeError("KVCacheManager read_block_bytes failed: " + _native.last_error())
+    return ctypes.string_at(ptr, nbytes)
+
+  def write_block_bytes(self, layer_idx: int, block_id: int, payload: bytes,
+                        shard_idx: int = 0) -> None:
+    """Overwrites one host block of one storage with bytes."""
+    rc, ptr, nbytes = self._host_block(layer_idx, block_id, shard_idx)
+    if rc != _native.OK:
+      raise RuntimeError("KVCacheManager write_block_bytes failed: " + _native.last_error())
+    if len(payload) > nbytes:
+      raise RuntimeError("KVCacheManager write_block_bytes failed: payload exceeds block size")
+    ctypes.memmove(ptr, payload, len(payload))
+
+  def host_tier_view(self) -> np.ndarray:
+    """Zero-copy uint8 view [host_blocks, host_block_pitch] of the host tier."""
+    rc, ptr, _ = self._host_block(0, 0, 0)
+    _native.check(rc)
+    buf = (ctypes.c_uint8 * (self.host_blocks * self.host_block_pitch)).from_address(ptr)
+    return np.frombuffer(buf, dtype=np.uint8).reshape(self.host_blocks, self.host_block_pitch)
+
+  def block_bytes(self, layer_idx: int) -> int:
+    t = self._grid[layer_idx][0]
+    return t.numel() * t.element_size() // self.major_dim
+
+  # -- pool surface over the implicit pools --------------------------------
+  def num_pools(self) -> int:
+    """Implicit pools: one per storage (tag "opaque"), as before RegisterPools."""
+    return self.num_layers
+
+  def pool_spec(self, pool_idx: int) -> Dict[str, Any]:
+    if not 0 <= pool_idx < self.num_layers:
+      raise RuntimeError(f"pool index {pool_idx} out of range")
+    bb = self.block_bytes(pool_idx)
+    return {"tag": "opaque", "storage_index": pool_idx, "base_offset_bytes": 0,
+            "block_stride_bytes": bb, "num_blocks": self.major_dim,
+            "regions": [{"name": "block", "offset_bytes": 0, "stride_bytes": bb,
+                         "unit_bytes": bb, "num_units": 1, "units_per_stride": 1}]}
+
+  def d2h_pool_blocks(self, pool_idx: int, block_ids: Sequence[int],
+                      shard_idx: Optional[int] = None) -> RaidenFuture:
+    """Partial D2H of whole pool blocks into the host mirror (same ids)."""
+    ids = list(block_ids)
+    return self._transfer(_native.lib().ts_d2h, "D2hPoolBlocks", ids, ids, None,
+                          pool_idx, shard_idx, None)
+
+  def h2d_pool_blocks(self, pool_idx: int, block_ids: Sequence[int],
+                      shard_idx: Optional[int] = None) -> RaidenFuture:
+    """Partial H2D of whole pool blocks from the host mirror (same ids)."""
+    ids = list(block_ids)
+    return self._transfer(_native.lib().ts_h2d, "H2dPoolBlocks", ids, ids, None,
+                          pool_idx, shard_idx, None)

@@ -1,0 +1,191 @@
+"""Tensor-level wrappers of the manager-free kernels of the C ABI.
+
+These take torch CUDA tensors, build the small device-side descriptor tables
+the kernels read, and launch on the current stream.  They are what the
+manager, the weight synchronizer and the hand-off executor are made of, and
+what the parity tests and the benchmark call directly.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import List, Optional, Sequence
+
+import numpy as np
+import torch
+
+from tpu_sync_b200 import _native
+
+
+def _stream(stream: Optional[torch.cuda.Stream], device) -> ctypes.c_void_p:
+  s = stream if stream is not None else torch.cuda.current_stream(device)
+  return ctypes.c_void_p(s.cuda_stream)
+
+
+def _nbytes(t: torch.Tensor) -> int:
+  return t.numel() * t.element_size()
+
+
+def _to_device_bytes(arr: ctypes.Array, device) -> torch.Tensor:
+  raw = np.frombuffer(bytes(arr), dtype=np.uint8).copy()
+  return torch.from_numpy(raw).to(device)
+
+
+class StorageTable:
+  """Device table of (layer, shard) storages for the block kernels.
+
+  stage_off of storage s = sum of the (16-byte rounded) slot bytes of the
+  storages before it, so a staging block is [storage 0 | storage 1 | ...].
+  `slot_scale` = 0.5 lays out fp8 payload slots (half the bf16 bytes).
+  """
+
+  def __init__(self, storages: Sequence[torch.Tensor], fp8: bool = False):
+    if not storages:
+      raise ValueError("need at least one storage")
+    self.storages = list(storages)
+    self.device = self.storages[0].device
+    n = len(self.storages)
+    arr = (_native.BlockStorage * n)()
+    off = 0
+    self.block_bytes = []
+    self.stage_offs = []
+    for i, t in enumerate(self.storages):
+      if not t.is_cuda or not t.is_contiguous():
+        raise ValueError("storages must be contiguous CUDA tensors")
+      if t.device != self.device:
+        raise ValueError("all storages must live on one device")
+      bb = _nbytes(t) // t.shape[0]
+      arr[i].dev_ptr = t.data_ptr()
+      arr[i].block_bytes = bb
+      arr[i].dev_bytes = _nbytes(t)
+      arr[i].stage_off = off
+      self.block_bytes.append(bb)
+      self.stage_offs.append(off)
+      slot = bb // 2 if fp8 else bb
+      off += (slot + 15) // 16 * 16
+    self.scale_off = off if fp8 else 0
+    if fp8:
+      off += (4 * n + 15) // 16 * 16
+    self.pitch = (off + 15) // 16 * 16
+    self.fp8 = fp8
+    self.d_table = _to_device_bytes(arr, self.device)
+    self.n = n
+
+  def new_staging(self, n_blocks: int) -> torch.Tensor:
+    return torch.empty((n_blocks, self.pitch), dtype=torch.uint8, device=self.device)
+
+
+def _ids(ids, device) -> torch.Tensor:
+  if isinstance(ids, torch.Tensor):
+    t = ids.to(device=device, dtype=torch.int64).contiguous()
+  else:
+    t = torch.tensor(list(ids), dtype=torch.int64, device=device)
+  return t
+
+
+def kv_extract(table: StorageTable, ids, staging: torch.Tensor,
+               err_flag: Optional[torch.Tensor] = None,
+               stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+  """staging[k] <- block ids[k] of every storage (block-major)."""
+  d_ids = _ids(ids, table.device)
+  fn = _native.lib().ts_kv_extract_fp8 if table.fp8 else _native.lib().ts_kv_extract
+  args = [table.device.index, ctypes.c_void_p(table.d_table.data_ptr()), table.n,
+          ctypes.c_void_p(d_ids.data_ptr()), d_ids.numel(),
+          ctypes.c_void_p(staging.data_ptr()), table.pitch]
+  if table.fp8:
+    args.append(table.scale_off)
+  args += [ctypes.c_void_p(err_flag.data_ptr() if err_flag is not None else 0),
+           _stream(stream, table.device)]
+  _native.check(fn(*args), "kv_extract: ")
+  return staging
+
+
+def kv_insert(table: StorageTable, ids, staging: torch.Tensor,
+              err_flag: Optional[torch.Tensor] = None,
+              stream: Optional[torch.cuda.Stream] = None) -> None:
+  """block ids[k] of every storage <- staging[k]."""
+  d_ids = _ids(ids, table.device)
+  fn = _native.lib().ts_kv_insert_fp8 if table.fp8 else _native.lib().ts_kv_insert
+  args = [table.device.index, ctypes.c_void_p(table.d_table.data_ptr()), table.n,
+          ctypes.c_void_p(d_ids.data_ptr()), d_ids.numel(),
+          ctypes.c_void_p(staging.data_ptr()), table.pitch]
+  if table.fp8:
+    args.append(table.scale_off)
+  args += [ctypes.c_void_p(err_flag.data_ptr() if err_flag is not None else 0),
+           _stream(stream, table.device)]
+  _native.check(fn(*args), "kv_insert: ")
+
+
+_TORCH_TO_TS = {torch.uint8: _native.DTYPE_U8, torch.bfloat16: _native.DTYPE_BF16,
+                torch.float32: _native.DTYPE_F32, torch.float16: _native.DTYPE_F16}
+
+
+class ReshardProgram:
+  """A list of strided chunks compiled for one launch of ts_reshard_copy.
+
+  chunks: iterables (src_tensor, dst_tensor_or_ptr, src_off, dst_off, size,
+  src_stride, dst_stride, count) in elements.  All sources must be on
+  `device`; destinations may be local or peer-GPU addresses.
+  """
+
+  def __init__(self, chunks, src_dtype: torch.dtype, dst_dtype: torch.dtype,
+               device: torch.device):
+    self.device = torch.device(device)
+    self.src_dtype = _TORCH_TO_TS[src_dtype]
+    self.dst_dtype = _TORCH_TO_TS[dst_dtype]
+    chunks = list(chunks)
+    n = len(chunks)
+    arr = (_native.ReshardChunk * max(n, 1))()
+    for i, (sp, dp, so, do, size, ss, ds, cnt) in enumerate(chunks):
+      arr[i].src_ptr = sp.data_ptr() if isinstance(sp, torch.Tensor) else int(sp)
+      arr[i].dst_ptr = dp.data_ptr() if isinstance(dp, torch.Tensor) else int(dp)
+      arr[i].src_off, arr[i].dst_off, arr[i].size = int(so), int(do), int(size)
+      arr[i].src_stride, arr[i].dst_stride, arr[i].count = int(ss), int(ds), int(cnt)
+    prefix = np.zeros(n + 1, dtype=np.int64)
+    _native.check(_native.lib().ts_reshard_work_items(
+        arr, n, self.src_dtype, self.dst_dtype,
+        prefix.ctypes.data_as(_native.c_i64_p)), "reshard plan: ")
+    self.n_chunks = n
+    self.n_items = int(prefix[-1])
+    self.d_chunks = _to_device_bytes(arr, self.device)
+    self.d_prefix = torch.from_numpy(prefix).to(self.device)
+
+  def launch(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+    _native.check(_native.lib().ts_reshard_copy(
+        self.device.index, ctypes.c_void_p(self.d_chunks.data_ptr()),
+        ctypes.c_void_p(self.d_prefix.data_ptr()), self.n_chunks, self.n_items,
+        self.src_dtype, self.dst_dtype, _stream(stream, self.device)), "reshard: ")
+
+
+def kv_relayout(src_storages: Sequence, dst_storages: Sequence, src_geom: dict,
+                dst_geom: dict, src_table: torch.Tensor, dst_table: torch.Tensor,
+                seq_tokens: int, device=None,
+                stream: Optional[torch.cuda.Stream] = None) -> None:
+  """Copies every token of every sequence between two page geometries.
+
+  src_storages / dst_storages: tensors or raw device addresses (destinations
+  may be peer-GPU addresses).  Geometries are dicts with block_tokens, heads,
+  head_bytes, head_major.  Tables are int32 [n_seqs, blocks_per_seq].
+  """
+  device = torch.device(device) if device is not None else src_table.device
+  n = len(src_storages)
+  if len(dst_storages) != n:
+    raise ValueError("source and destination storage counts differ")
+  ptr = lambda x: x.data_ptr() if isinstance(x, torch.Tensor) else int(x)
+  d_src = torch.tensor([ptr(x) for x in src_storages], dtype=torch.int64,
+                       device=device)
+  d_dst = torch.tensor([ptr(x) for x in dst_storages], dtype=torch.int64,
+                       device=device)
+  sg = _native.PageGeometry(int(src_geom["block_tokens"]), int(src_geom["heads"]),
+                            int(src_geom["head_bytes"]), int(src_geom["head_major"]), 0)
+  dg = _native.PageGeometry(int(dst_geom["block_tokens"]), int(dst_geom["heads"]),
+                            int(dst_geom["head_bytes"]), int(dst_geom["head_major"]), 0)
+  st = src_table.to(device=device, dtype=torch.int32).contiguous()
+  dt = dst_table.to(device=device, dtype=torch.int32).contiguous()
+  _native.check(_native.lib().ts_kv_relayout(
+      device.index, ctypes.c_void_p(d_src.data_ptr()), ctypes.c_void_p(d_dst.data_ptr()),
+      n, sg, dg, ctypes.c_void_p(st.data_ptr()), st.shape[1],
+      ctypes.c_void_p(dt.data_ptr()), dt.shape[1], st.shape[0], int(seq_tokens),
+      _stream(stream, device)), "kv_relayout: ")
+  # keep the address tables alive until the kernel has consumed them
+  torch.cuda.current_stream(device).synchronize() if stream is None else stream.synchronize()
