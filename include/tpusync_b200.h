@@ -225,11 +225,15 @@ typedef struct ts_storage_desc {
 
 typedef struct ts_manager_opts {
   int64_t host_blocks;         /* host tier capacity in blocks (reference default 64) */
-  int64_t chunk_blocks;        /* blocks per pipelined staging chunk (0 = default) */
+  int64_t chunk_blocks;        /* blocks per pipelined chunk (0 = default 64) */
   const char* shm_name;        /* "" / NULL = anonymous pinned memory */
   const char* model_uid;       /* stored in the /dev/shm header */
   int32_t fp8;                 /* 1: host tier holds fp8 e4m3 + per-block scales */
-  int32_t pad_;
+  int32_t mode;                /* 0: extract/insert kernels + copy-engine DMAs via
+                                  HBM staging; 1: direct -- the kernels read and
+                                  write the mapped host tier over PCIe themselves */
+  int32_t copy_streams;        /* staged mode: copy streams per direction (1..4) */
+  int32_t max_ctas;            /* grid cap of the kernels (0 = every SM) */
 } ts_manager_opts;
 
 /* Creates a manager over num_layers x num_shards storages (row-major

@@ -140,10 +140,15 @@ def test_fp8_extract_insert_matches_oracle(cuda, block_tokens, heads, n_blocks):
 # KVCacheManager (pinned host tier, pipelined gather + DMA)
 # ---------------------------------------------------------------------------
 
-def make_pair(geom, blocks, host_blocks, seed, cuda, chunk_blocks=0):
+MODES = [dict(mode="staged", copy_streams=1), dict(mode="staged", copy_streams=2),
+         dict(mode="direct", max_ctas=64)]
+
+
+def make_pair(geom, blocks, host_blocks, seed, cuda, chunk_blocks=0, **kw):
   pool = small_pool(geom, blocks, seed, cuda)
   grid = [[t] for t in pool]
-  mgr = KVCacheManager(grid, host_blocks_to_allocate=host_blocks, chunk_blocks=chunk_blocks)
+  mgr = KVCacheManager(grid, host_blocks_to_allocate=host_blocks, chunk_blocks=chunk_blocks,
+                       **kw)
   model = ref.RefKVManager([[u8(t).reshape(-1).copy()] for t in pool], dim0=blocks,
                            host_blocks=host_blocks)
   return pool, mgr, model
@@ -156,10 +161,11 @@ def assert_same(pool, mgr, model, host_ids):
       assert mgr.read_block_bytes(l, h) == model.host_block(l, h), (l, h)
 
 
+@pytest.mark.parametrize("mode", MODES)
 @pytest.mark.parametrize("chunk_blocks", [0, 3])
-def test_manager_offload_reload_matches_model(cuda, chunk_blocks):
+def test_manager_offload_reload_matches_model(cuda, chunk_blocks, mode):
   geom = workloads.KVGeometry(layers=4, kv=2, block_tokens=16, heads=2, head_dim=128)
-  pool, mgr, model = make_pair(geom, 64, 96, 5, cuda, chunk_blocks)
+  pool, mgr, model = make_pair(geom, 64, 96, 5, cuda, chunk_blocks, **mode)
   rng = np.random.default_rng(3)
   for step in range(6):
     n = int(rng.integers(1, 40))
@@ -182,10 +188,11 @@ def test_manager_offload_reload_matches_model(cuda, chunk_blocks):
   assert_same(pool, mgr, model, range(96))
 
 
-def test_manager_back_to_back_calls_are_ordered(cuda):
+@pytest.mark.parametrize("mode", MODES)
+def test_manager_back_to_back_calls_are_ordered(cuda, mode):
   """Offload then reload of the same host blocks without waiting in between."""
   geom = workloads.KVGeometry(layers=2, kv=2, block_tokens=16, heads=8, head_dim=128)
-  pool, mgr, model = make_pair(geom, 128, 128, 9, cuda, chunk_blocks=8)
+  pool, mgr, model = make_pair(geom, 128, 128, 9, cuda, chunk_blocks=8, **mode)
   futs = []
   for i in range(4):
     src = list(range(i * 20, i * 20 + 20))
@@ -198,9 +205,10 @@ def test_manager_back_to_back_calls_are_ordered(cuda):
   assert_same(pool, mgr, model, range(128))
 
 
-def test_manager_whole_storage_and_layer_restricted(cuda):
+@pytest.mark.parametrize("mode", MODES)
+def test_manager_whole_storage_and_layer_restricted(cuda, mode):
   geom = workloads.KVGeometry(layers=3, kv=1, block_tokens=4, heads=2, head_dim=64)
-  pool, mgr, model = make_pair(geom, 16, 16, 2, cuda)
+  pool, mgr, model = make_pair(geom, 16, 16, 2, cuda, **mode)
   mgr.d2h([], []).Await()
   assert model.d2h([], []) == (ref.OK, "")
   f = mgr.h2d([3, 4], [9, 10], layer_idx=1)
@@ -256,10 +264,11 @@ def test_heterogeneous_layer_block_sizes_transfer(cuda):
     assert torch.count_nonzero(got[0:2]) == 0
 
 
-def test_fp8_manager_round_trip(cuda):
+@pytest.mark.parametrize("mode", MODES)
+def test_fp8_manager_round_trip(cuda, mode):
   geom = workloads.KVGeometry(layers=4, kv=2, block_tokens=64, heads=1, head_dim=128)
   pool = small_pool(geom, 32, 21, cuda)
-  mgr = KVCacheManager([[t] for t in pool], host_blocks_to_allocate=32, fp8=True)
+  mgr = KVCacheManager([[t] for t in pool], host_blocks_to_allocate=32, fp8=True, **mode)
   ids = [3, 9, 27, 30]
   mgr.d2h(ids, [0, 1, 2, 3]).Await()
   (payload, scales), bits = fp8_oracle(pool, ids)

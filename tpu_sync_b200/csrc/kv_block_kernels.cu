@@ -34,7 +34,8 @@ constexpr int kCtasPerSm = 8;
 // snapshots them, so no device id buffer or host->device id copy is needed).
 struct DevIds {
   const int64_t* p;
-  __device__ __forceinline__ int64_t operator[](int64_t k) const { return p[k]; }
+  __device__ __forceinline__ int64_t dev(int64_t k) const { return p[k]; }
+  __device__ __forceinline__ int64_t stage(int64_t k) const { return k; }
 };
 
 __device__ __forceinline__ int4 ld_stream(const void* p) {
@@ -73,14 +74,14 @@ __device__ __forceinline__ bool resolve(const ts_block_storage* __restrict__ st,
   const uint64_t bb = st[s].block_bytes;
   const uint64_t off = piece * kPieceBytes;
   if (off >= bb) return false;
-  const int64_t id = ids[k];
+  const int64_t id = ids.dev(k);
   const uint64_t dev_off = uint64_t(id) * bb;
   if (id < 0 || dev_off + bb > st[s].dev_bytes) {
     if (err_flag != nullptr && threadIdx.x == 0) *reinterpret_cast<volatile int*>(err_flag) = 1;
     return false;
   }
   u->dev = reinterpret_cast<uint8_t*>(st[s].dev_ptr) + dev_off + off;
-  u->stg = staging + uint64_t(k) * pitch + st[s].stage_off + off;
+  u->stg = staging + uint64_t(ids.stage(k)) * pitch + st[s].stage_off + off;
   const uint64_t rem = bb - off;
   u->nbytes = rem < kPieceBytes ? rem : kPieceBytes;
   return true;
@@ -211,14 +212,14 @@ __device__ __forceinline__ bool unit_addr(const ts_block_storage* __restrict__ s
   const int64_t k = unit / n_st;
   const int s = int(unit - k * n_st);
   const uint64_t bb = st[s].block_bytes;
-  const int64_t id = ids[k];
+  const int64_t id = ids.dev(k);
   const uint64_t dev_off = uint64_t(id) * bb;
   if (id < 0 || dev_off + bb > st[s].dev_bytes) {
     if (err_flag != nullptr && threadIdx.x == 0) *reinterpret_cast<volatile int*>(err_flag) = 1;
     return false;
   }
   *s_out = s;
-  *k_out = k;
+  *k_out = ids.stage(k);
   *dev_out = reinterpret_cast<uint8_t*>(st[s].dev_ptr) + dev_off;
   *bb_out = bb;
   return true;
@@ -309,8 +310,9 @@ __global__ void __launch_bounds__(kThreads)
 
 bool aligned16(uint64_t v) { return (v & 15u) == 0; }
 
-int launch_grid(int device, int64_t items) {
-  const int64_t cap = int64_t(sm_count(device)) * kCtasPerSm;
+int launch_grid(int device, int64_t items, int max_ctas = 0) {
+  int64_t cap = int64_t(sm_count(device)) * kCtasPerSm;
+  if (max_ctas > 0 && max_ctas < cap) cap = max_ctas;
   return int(items < cap ? items : cap);
 }
 
@@ -318,13 +320,13 @@ template <bool kToStaging, typename Ids>
 int block_copy(int device, const ts_block_storage* d_st, int n_st,
                const Ids& d_ids, int64_t n_blocks, uint8_t* staging,
                uint64_t pitch, int* err_flag, void* stream, bool vec_ok,
-               uint64_t max_block_bytes) {
+               uint64_t max_block_bytes, int max_ctas = 0) {
   if (n_blocks == 0 || n_st == 0) return TS_OK;
   const uint32_t ppu = uint32_t((max_block_bytes + kPieceBytes - 1) / kPieceBytes);
   if (ppu == 0) return TS_OK;
   const int64_t items = n_blocks * int64_t(n_st) * ppu;
   DeviceGuard g(device);
-  const int grid = launch_grid(device, items);
+  const int grid = launch_grid(device, items, max_ctas);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (vec_ok) {
     block_copy_vec_kernel<kToStaging, Ids><<<grid, kThreads, 0, s>>>(
@@ -365,30 +367,30 @@ template <typename Ids>
 int launch_extract(int device, const ts_block_storage* d_st, int n_st,
                    const Ids& ids, int64_t n_blocks, void* staging,
                    uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
-                   uint64_t max_bb) {
+                   uint64_t max_bb, int max_ctas = 0) {
   return block_copy<true>(device, d_st, n_st, ids, n_blocks,
                           static_cast<uint8_t*>(staging), pitch, err_flag, s,
-                          vec_ok, max_bb);
+                          vec_ok, max_bb, max_ctas);
 }
 
 template <typename Ids>
 int launch_insert(int device, const ts_block_storage* d_st, int n_st,
                   const Ids& ids, int64_t n_blocks, const void* staging,
                   uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
-                  uint64_t max_bb) {
+                  uint64_t max_bb, int max_ctas = 0) {
   return block_copy<false>(device, d_st, n_st, ids, n_blocks,
                            static_cast<uint8_t*>(const_cast<void*>(staging)),
-                           pitch, err_flag, s, vec_ok, max_bb);
+                           pitch, err_flag, s, vec_ok, max_bb, max_ctas);
 }
 
 template <typename Ids>
 int launch_extract_fp8(int device, const ts_block_storage* d_st, int n_st,
                        const Ids& ids, int64_t n_blocks, void* staging,
                        uint64_t pitch, uint64_t scale_off, int* err_flag,
-                       cudaStream_t s) {
+                       cudaStream_t s, int max_ctas = 0) {
   if (n_blocks == 0 || n_st == 0) return TS_OK;
   DeviceGuard g(device);
-  const int grid = launch_grid(device, n_blocks * int64_t(n_st));
+  const int grid = launch_grid(device, n_blocks * int64_t(n_st), max_ctas);
   extract_fp8_kernel<Ids><<<grid, kThreads, 0, s>>>(d_st, n_st, ids, n_blocks,
                                                     static_cast<uint8_t*>(staging),
                                                     pitch, scale_off, err_flag);
@@ -400,10 +402,10 @@ template <typename Ids>
 int launch_insert_fp8(int device, const ts_block_storage* d_st, int n_st,
                       const Ids& ids, int64_t n_blocks, const void* staging,
                       uint64_t pitch, uint64_t scale_off, int* err_flag,
-                      cudaStream_t s) {
+                      cudaStream_t s, int max_ctas = 0) {
   if (n_blocks == 0 || n_st == 0) return TS_OK;
   DeviceGuard g(device);
-  const int grid = launch_grid(device, n_blocks * int64_t(n_st));
+  const int grid = launch_grid(device, n_blocks * int64_t(n_st), max_ctas);
   insert_fp8_kernel<Ids><<<grid, kThreads, 0, s>>>(
       d_st, n_st, ids, n_blocks, static_cast<const uint8_t*>(staging), pitch,
       scale_off, err_flag);
@@ -417,23 +419,23 @@ int launch_insert_fp8(int device, const ts_block_storage* d_st, int n_st,
 int mgr_extract(int device, const ts_block_storage* d_st, int n_st,
                 const ParamIds& ids, int64_t n_blocks, void* staging,
                 uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
-                uint64_t max_bb, bool fp8, uint64_t scale_off) {
+                uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas) {
   if (fp8)
     return launch_extract_fp8(device, d_st, n_st, ids, n_blocks, staging, pitch,
-                              scale_off, err_flag, s);
+                              scale_off, err_flag, s, max_ctas);
   return launch_extract(device, d_st, n_st, ids, n_blocks, staging, pitch,
-                        err_flag, s, vec_ok, max_bb);
+                        err_flag, s, vec_ok, max_bb, max_ctas);
 }
 
 int mgr_insert(int device, const ts_block_storage* d_st, int n_st,
                const ParamIds& ids, int64_t n_blocks, const void* staging,
                uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
-               uint64_t max_bb, bool fp8, uint64_t scale_off) {
+               uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas) {
   if (fp8)
     return launch_insert_fp8(device, d_st, n_st, ids, n_blocks, staging, pitch,
-                             scale_off, err_flag, s);
+                             scale_off, err_flag, s, max_ctas);
   return launch_insert(device, d_st, n_st, ids, n_blocks, staging, pitch,
-                       err_flag, s, vec_ok, max_bb);
+                       err_flag, s, vec_ok, max_bb, max_ctas);
 }
 
 }  // namespace tsb

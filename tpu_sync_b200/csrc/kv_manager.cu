@@ -45,7 +45,7 @@ struct ts_host_tier;
 namespace tsb {
 namespace {
 
-constexpr int kSlots = 2;
+constexpr int kMaxCopyStreams = 4;
 constexpr int kEventRing = 256;
 constexpr int kErrWords = 4096;
 
@@ -106,12 +106,17 @@ struct ts_manager {
   uint64_t max_bb = 0;
   int64_t chunk_blocks = tsb::kMaxParamIds;
 
-  cudaStream_t s_out_kernel = nullptr, s_out_copy = nullptr;
-  cudaStream_t s_in_copy = nullptr, s_in_kernel = nullptr;
+  int mode = 0;       // 0 staged (kernel + copy engine), 1 direct (kernel <-> mapped host)
+  int ncs = 2;        // copy streams per direction (staged)
+  int max_ctas = 0;   // grid cap of the kernels
+  uint8_t* host_dev = nullptr;  // device address of the mapped host tier
+
+  cudaStream_t s_out_kernel = nullptr, s_in_kernel = nullptr;
+  cudaStream_t out_cs[tsb::kMaxCopyStreams] = {};
+  cudaStream_t in_cs[tsb::kMaxCopyStreams] = {};
+  cudaEvent_t out_join[tsb::kMaxCopyStreams] = {};
   cudaEvent_t ev_user = nullptr;
-  cudaEvent_t ev_link = nullptr;
-  tsb::Slot out_slots[tsb::kSlots];
-  tsb::Slot in_slots[tsb::kSlots];
+  std::vector<tsb::Slot> out_slots, in_slots;
   int next_out = 0, next_in = 0;
 
   // hazard tracking: sequence numbers of the last offload (d2h) / reload
@@ -356,88 +361,121 @@ uint64_t kernel_bytes(const ts_manager* m, int64_t cn, bool extract) {
   return uint64_t(cn) * (dev + stage);
 }
 
+// The stream on which every call of a direction completes.
+cudaStream_t last_stream(const ts_manager* m, bool to_host) {
+  if (!to_host) return m->s_in_kernel;
+  return m->mode == 1 ? m->s_out_kernel : m->out_cs[0];
+}
+
+int launch_chunk(ts_manager* m, bool to_host, const ParamIds& ids, int64_t cn,
+                 void* staging, int* err_dev, cudaStream_t ks) {
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (m->profiling) {
+    e0 = prof_event(m);
+    e1 = prof_event(m);
+    TS_CUDA_RET(cudaEventRecord(e0, ks), "event record");
+  }
+  int rc = to_host
+               ? mgr_extract(m->device, m->d_table, int(m->st.size()), ids, cn, staging,
+                             m->host_pitch, err_dev, ks, m->vec_ok, m->max_bb, m->fp8,
+                             m->scale_off, m->max_ctas)
+               : mgr_insert(m->device, m->d_table, int(m->st.size()), ids, cn, staging,
+                            m->host_pitch, err_dev, ks, m->vec_ok, m->max_bb, m->fp8,
+                            m->scale_off, m->max_ctas);
+  if (rc != TS_OK) return rc;
+  if (m->profiling) {
+    TS_CUDA_RET(cudaEventRecord(e1, ks), "event record");
+    const int w = to_host ? 0 : 1;
+    m->prof_ev[w].push_back(e0);
+    m->prof_ev[w].push_back(e1);
+    m->prof_bytes[w].push_back(kernel_bytes(m, cn, to_host));
+  }
+  return TS_OK;
+}
+
 int enqueue_transfer(ts_manager* m, bool to_host, const Plan& p, void* user_stream,
                      ts_event* ev) {
   cudaStream_t user = reinterpret_cast<cudaStream_t>(user_stream);
   cudaStream_t ks = to_host ? m->s_out_kernel : m->s_in_kernel;
-  cudaStream_t cs = to_host ? m->s_out_copy : m->s_in_copy;
-  cudaStream_t first = to_host ? ks : cs;
-  cudaStream_t last = to_host ? cs : ks;
+  cudaStream_t* cs = to_host ? m->out_cs : m->in_cs;
+  const bool direct = m->mode == 1 && p.whole;
+  const cudaStream_t last = last_stream(m, to_host);
+  std::vector<cudaStream_t> streams{ks};
+  if (m->mode == 0)
+    for (int i = 0; i < m->ncs; ++i) streams.push_back(cs[i]);
   int* err_dev = nullptr;
   TS_CUDA_RET(cudaHostGetDevicePointer(reinterpret_cast<void**>(&err_dev), ev->err_word, 0),
               "error word mapping");
 
-  // Order after the producer's queued work (device data written by the user)
+  // Order after the producer's queued work, and after in-flight calls of the
+  // other direction that touch the same host or device blocks.
   TS_CUDA_RET(cudaEventRecord(m->ev_user, user), "event record");
-  TS_CUDA_RET(cudaStreamWaitEvent(first, m->ev_user, 0), "stream wait");
-  if (!to_host) TS_CUDA_RET(cudaStreamWaitEvent(ks, m->ev_user, 0), "stream wait");
-
-  // Cross-direction hazards at block granularity.
   uint64_t need = 0;
   if (to_host) {
     for (size_t i = 0; i < p.src.size(); ++i) {
       need = std::max(need, m->dev_h2d_seq[size_t(p.src[i])]);
       need = std::max(need, m->host_h2d_seq[size_t(p.dst[i])]);
     }
-    int rc = wait_for_call(m->h2d_ring, need, first);
-    if (rc != TS_OK) return rc;
   } else {
     for (size_t i = 0; i < p.src.size(); ++i) {
       need = std::max(need, m->host_d2h_seq[size_t(p.src[i])]);
       need = std::max(need, m->dev_d2h_seq[size_t(p.dst[i])]);
     }
-    int rc = wait_for_call(m->d2h_ring, need, first);
-    if (rc != TS_OK) return rc;
-    rc = wait_for_call(m->d2h_ring, need, ks);
+  }
+  for (cudaStream_t s : streams) {
+    TS_CUDA_RET(cudaStreamWaitEvent(s, m->ev_user, 0), "stream wait");
+    int rc = wait_for_call(to_host ? m->h2d_ring : m->d2h_ring, need, s);
     if (rc != TS_OK) return rc;
   }
-  TS_CUDA_RET(cudaEventRecord(ev->start, first), "event record");
+  TS_CUDA_RET(cudaEventRecord(ev->start, ks), "event record");
 
   if (!p.whole) {
-    int rc = enqueue_subset(m, to_host, p, first);
+    int rc = enqueue_subset(m, to_host, p, last);
     if (rc != TS_OK) return rc;
-    if (last != first) {  // keep `last` the stream that completes every call
-      TS_CUDA_RET(cudaEventRecord(m->ev_link, first), "event record");
-      TS_CUDA_RET(cudaStreamWaitEvent(last, m->ev_link, 0), "stream wait");
-    }
     TS_CUDA_RET(cudaEventRecord(ev->done, last), "event record");
     return TS_OK;
   }
 
   const int64_t nblk = int64_t(p.src.size());
-  for (int64_t c0 = 0; c0 < nblk; c0 += m->chunk_blocks) {
+  const std::vector<int64_t>& dev_ids = to_host ? p.src : p.dst;
+  const std::vector<int64_t>& host_ids = to_host ? p.dst : p.src;
+  if (direct) {
+    for (int64_t c0 = 0; c0 < nblk; c0 += m->chunk_blocks) {
+      const int64_t cn = std::min<int64_t>(m->chunk_blocks, nblk - c0);
+      ParamIds ids;
+      ids.direct = 1;
+      for (int64_t k = 0; k < cn; ++k) {
+        ids.v[k] = dev_ids[size_t(c0 + k)];
+        ids.s[k] = host_ids[size_t(c0 + k)];
+      }
+      int rc = launch_chunk(m, to_host, ids, cn, m->host_dev, err_dev, ks);
+      if (rc != TS_OK) return rc;
+    }
+    TS_CUDA_RET(cudaEventRecord(ev->done, ks), "event record");
+    return TS_OK;
+  }
+
+  std::vector<Slot>& slots = to_host ? m->out_slots : m->in_slots;
+  int& next = to_host ? m->next_out : m->next_in;
+  int chunk = 0;
+  for (int64_t c0 = 0; c0 < nblk; c0 += m->chunk_blocks, ++chunk) {
     const int64_t cn = std::min<int64_t>(m->chunk_blocks, nblk - c0);
-    Slot& slot = to_host ? m->out_slots[m->next_out] : m->in_slots[m->next_in];
-    if (to_host) m->next_out = (m->next_out + 1) % kSlots;
-    else m->next_in = (m->next_in + 1) % kSlots;
+    Slot& slot = slots[size_t(next)];
+    next = (next + 1) % int(slots.size());
+    cudaStream_t cc = cs[chunk % m->ncs];
     ParamIds ids;
-    const std::vector<int64_t>& dev_ids = to_host ? p.src : p.dst;
-    const std::vector<int64_t>& host_ids = to_host ? p.dst : p.src;
+    ids.direct = 0;
     for (int64_t k = 0; k < cn; ++k) ids.v[k] = dev_ids[size_t(c0 + k)];
     if (to_host) {
       TS_CUDA_RET(cudaStreamWaitEvent(ks, slot.free, 0), "stream wait");
-      cudaEvent_t e0 = nullptr, e1 = nullptr;
-      if (m->profiling) {
-        e0 = prof_event(m);
-        e1 = prof_event(m);
-        TS_CUDA_RET(cudaEventRecord(e0, ks), "event record");
-      }
-      int rc = mgr_extract(m->device, m->d_table, int(m->st.size()), ids, cn, slot.buf,
-                           m->host_pitch, err_dev, ks, m->vec_ok, m->max_bb, m->fp8,
-                           m->scale_off);
+      int rc = launch_chunk(m, true, ids, cn, slot.buf, err_dev, ks);
       if (rc != TS_OK) return rc;
-      if (m->profiling) {
-        TS_CUDA_RET(cudaEventRecord(e1, ks), "event record");
-        m->prof_ev[0].push_back(e0);
-        m->prof_ev[0].push_back(e1);
-        m->prof_bytes[0].push_back(kernel_bytes(m, cn, true));
-      }
       TS_CUDA_RET(cudaEventRecord(slot.ready, ks), "event record");
-      TS_CUDA_RET(cudaStreamWaitEvent(cs, slot.ready, 0), "stream wait");
+      TS_CUDA_RET(cudaStreamWaitEvent(cc, slot.ready, 0), "stream wait");
     } else {
-      TS_CUDA_RET(cudaStreamWaitEvent(cs, slot.free, 0), "stream wait");
+      TS_CUDA_RET(cudaStreamWaitEvent(cc, slot.free, 0), "stream wait");
     }
-    // DMAs of maximal runs of consecutive host block ids
+    // one DMA per maximal run of consecutive host block ids
     int64_t k = 0;
     while (k < cn) {
       int64_t e = k + 1;
@@ -446,38 +484,39 @@ int enqueue_transfer(ts_manager* m, bool to_host, const Plan& p, void* user_stre
       uint8_t* d = slot.buf + uint64_t(k) * m->host_pitch;
       const size_t bytes = size_t(e - k) * m->host_pitch;
       if (to_host) {
-        TS_CUDA_RET(cudaMemcpyAsync(h, d, bytes, cudaMemcpyDeviceToHost, cs), "D2H DMA");
+        TS_CUDA_RET(cudaMemcpyAsync(h, d, bytes, cudaMemcpyDeviceToHost, cc), "D2H DMA");
       } else {
-        TS_CUDA_RET(cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, cs), "H2D DMA");
+        TS_CUDA_RET(cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, cc), "H2D DMA");
       }
       k = e;
     }
     if (to_host) {
-      TS_CUDA_RET(cudaEventRecord(slot.free, cs), "event record");
+      TS_CUDA_RET(cudaEventRecord(slot.free, cc), "event record");
     } else {
-      TS_CUDA_RET(cudaEventRecord(slot.ready, cs), "event record");
+      TS_CUDA_RET(cudaEventRecord(slot.ready, cc), "event record");
       TS_CUDA_RET(cudaStreamWaitEvent(ks, slot.ready, 0), "stream wait");
-      cudaEvent_t e0 = nullptr, e1 = nullptr;
-      if (m->profiling) {
-        e0 = prof_event(m);
-        e1 = prof_event(m);
-        TS_CUDA_RET(cudaEventRecord(e0, ks), "event record");
-      }
-      int rc = mgr_insert(m->device, m->d_table, int(m->st.size()), ids, cn, slot.buf,
-                          m->host_pitch, err_dev, ks, m->vec_ok, m->max_bb, m->fp8,
-                          m->scale_off);
+      int rc = launch_chunk(m, false, ids, cn, slot.buf, err_dev, ks);
       if (rc != TS_OK) return rc;
-      if (m->profiling) {
-        TS_CUDA_RET(cudaEventRecord(e1, ks), "event record");
-        m->prof_ev[1].push_back(e0);
-        m->prof_ev[1].push_back(e1);
-        m->prof_bytes[1].push_back(kernel_bytes(m, cn, false));
-      }
       TS_CUDA_RET(cudaEventRecord(slot.free, ks), "event record");
+    }
+  }
+  if (to_host) {  // join the other copy streams into the completing one
+    for (int i = 1; i < m->ncs && i < chunk; ++i) {
+      TS_CUDA_RET(cudaEventRecord(m->out_join[i], cs[i]), "event record");
+      TS_CUDA_RET(cudaStreamWaitEvent(last, m->out_join[i], 0), "stream wait");
     }
   }
   TS_CUDA_RET(cudaEventRecord(ev->done, last), "event record");
   return TS_OK;
+}
+
+void sync_all(ts_manager* m) {
+  for (cudaStream_t s : {m->s_out_kernel, m->s_in_kernel})
+    if (s) cudaStreamSynchronize(s);
+  for (int i = 0; i < kMaxCopyStreams; ++i) {
+    if (m->out_cs[i]) cudaStreamSynchronize(m->out_cs[i]);
+    if (m->in_cs[i]) cudaStreamSynchronize(m->in_cs[i]);
+  }
 }
 
 int transfer(ts_manager* m, bool to_host, const int64_t* src, const int64_t* dst,
@@ -499,15 +538,12 @@ int transfer(ts_manager* m, bool to_host, const int64_t* src, const int64_t* dst
   if (rc != TS_OK) {
     // Work already queued stays ordered on the manager's streams; drain it so
     // the error word can be recycled safely.
-    cudaStreamSynchronize(m->s_out_copy);
-    cudaStreamSynchronize(m->s_in_kernel);
-    cudaStreamSynchronize(m->s_out_kernel);
-    cudaStreamSynchronize(m->s_in_copy);
+    sync_all(m);
     std::string msg = ts_last_error();
     drop_event_locked(ev);
     return set_error(rc, msg);
   }
-  cudaStream_t last = to_host ? m->s_out_copy : m->s_in_kernel;
+  cudaStream_t last = last_stream(m, to_host);
   const uint64_t seq = to_host ? ++m->d2h_seq : ++m->h2d_seq;
   rc = record_call(to_host ? m->d2h_ring : m->h2d_ring, seq, last);
   if (rc != TS_OK) {
@@ -530,24 +566,27 @@ int transfer(ts_manager* m, bool to_host, const int64_t* src, const int64_t* dst
 
 void destroy_resources(ts_manager* m) {
   DeviceGuard g(m->device);
-  for (cudaStream_t s : {m->s_out_kernel, m->s_out_copy, m->s_in_copy, m->s_in_kernel})
-    if (s) cudaStreamSynchronize(s);
-  for (Slot* slots : {m->out_slots, m->in_slots})
-    for (int i = 0; i < kSlots; ++i) {
-      if (slots[i].buf) cudaFree(slots[i].buf);
-      if (slots[i].ready) cudaEventDestroy(slots[i].ready);
-      if (slots[i].free) cudaEventDestroy(slots[i].free);
+  sync_all(m);
+  for (std::vector<Slot>* slots : {&m->out_slots, &m->in_slots})
+    for (Slot& sl : *slots) {
+      if (sl.buf) cudaFree(sl.buf);
+      if (sl.ready) cudaEventDestroy(sl.ready);
+      if (sl.free) cudaEventDestroy(sl.free);
     }
   for (CallRec* ring : {m->d2h_ring, m->h2d_ring})
     for (int i = 0; i < kEventRing; ++i)
       if (ring[i].done) cudaEventDestroy(ring[i].done);
-  for (cudaStream_t s : {m->s_out_kernel, m->s_out_copy, m->s_in_copy, m->s_in_kernel})
+  for (cudaStream_t s : {m->s_out_kernel, m->s_in_kernel})
     if (s) cudaStreamDestroy(s);
+  for (int i = 0; i < kMaxCopyStreams; ++i) {
+    if (m->out_cs[i]) cudaStreamDestroy(m->out_cs[i]);
+    if (m->in_cs[i]) cudaStreamDestroy(m->in_cs[i]);
+    if (m->out_join[i]) cudaEventDestroy(m->out_join[i]);
+  }
   for (int k = 0; k < 2; ++k)
     for (cudaEvent_t e : m->prof_ev[k]) cudaEventDestroy(e);
   for (cudaEvent_t e : m->prof_free) cudaEventDestroy(e);
   if (m->ev_user) cudaEventDestroy(m->ev_user);
-  if (m->ev_link) cudaEventDestroy(m->ev_link);
   if (m->d_table) cudaFree(m->d_table);
   if (m->err_host) cudaFreeHost(m->err_host);
   if (m->tier) ts_host_tier_destroy(m->tier, 0);
@@ -580,6 +619,13 @@ extern "C" int ts_mgr_create(const ts_storage_desc* storages, int num_layers,
   m->fp8 = opts && opts->fp8;
   if (opts && opts->chunk_blocks > 0)
     m->chunk_blocks = std::min<int64_t>(opts->chunk_blocks, tsb::kMaxParamIds);
+  m->mode = opts ? opts->mode : 0;
+  if (m->mode != 0 && m->mode != 1) {
+    delete m;
+    return set_error(TS_INVALID_ARGUMENT, "mode must be 0 (staged) or 1 (direct)");
+  }
+  m->ncs = opts && opts->copy_streams > 0 ? std::min(opts->copy_streams, tsb::kMaxCopyStreams) : 2;
+  m->max_ctas = opts && opts->max_ctas > 0 ? opts->max_ctas : 0;
   const int n = num_layers * num_shards;
   m->st.resize(size_t(n));
   // reference: slice_byte_size from layer 0, shard 0 (GetMajorSliceByteSize)
@@ -654,21 +700,35 @@ extern "C" int ts_mgr_create(const ts_storage_desc* storages, int num_layers,
                    cudaMemcpyHostToDevice);
   if (e != cudaSuccess) return fail(tsb::cuda_error(e, "storage table upload"));
 
-  for (cudaStream_t* s : {&m->s_out_kernel, &m->s_out_copy, &m->s_in_copy, &m->s_in_kernel}) {
+  for (cudaStream_t* s : {&m->s_out_kernel, &m->s_in_kernel}) {
     e = cudaStreamCreateWithFlags(s, cudaStreamNonBlocking);
     if (e != cudaSuccess) return fail(tsb::cuda_error(e, "stream create"));
   }
-  e = cudaEventCreateWithFlags(&m->ev_user, cudaEventDisableTiming);
-  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&m->ev_link, cudaEventDisableTiming);
-  if (e != cudaSuccess) return fail(tsb::cuda_error(e, "event create"));
-  const size_t slot_bytes = size_t(m->chunk_blocks) * m->host_pitch;
-  for (tsb::Slot* slots : {m->out_slots, m->in_slots})
-    for (int i = 0; i < tsb::kSlots; ++i) {
-      e = cudaMalloc(&slots[i].buf, slot_bytes);
-      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&slots[i].ready, cudaEventDisableTiming);
-      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&slots[i].free, cudaEventDisableTiming);
-      if (e != cudaSuccess) return fail(tsb::cuda_error(e, "staging slot"));
+  if (m->mode == 0) {
+    for (int i = 0; i < m->ncs; ++i) {
+      e = cudaStreamCreateWithFlags(&m->out_cs[i], cudaStreamNonBlocking);
+      if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&m->in_cs[i], cudaStreamNonBlocking);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&m->out_join[i], cudaEventDisableTiming);
+      if (e != cudaSuccess) return fail(tsb::cuda_error(e, "copy stream create"));
     }
+  }
+  e = cudaEventCreateWithFlags(&m->ev_user, cudaEventDisableTiming);
+  if (e != cudaSuccess) return fail(tsb::cuda_error(e, "event create"));
+  if (m->mode == 0) {
+    const size_t slot_bytes = size_t(m->chunk_blocks) * m->host_pitch;
+    m->out_slots.resize(size_t(2 * m->ncs));
+    m->in_slots.resize(size_t(2 * m->ncs));
+    for (std::vector<tsb::Slot>* slots : {&m->out_slots, &m->in_slots})
+      for (tsb::Slot& sl : *slots) {
+        e = cudaMalloc(&sl.buf, slot_bytes);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sl.ready, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sl.free, cudaEventDisableTiming);
+        if (e != cudaSuccess) return fail(tsb::cuda_error(e, "staging slot"));
+      }
+  } else {
+    e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&m->host_dev), m->host, 0);
+    if (e != cudaSuccess) return fail(tsb::cuda_error(e, "host tier mapping"));
+  }
   e = cudaHostAlloc(reinterpret_cast<void**>(&m->err_host), sizeof(int) * tsb::kErrWords,
                     cudaHostAllocMapped | cudaHostAllocPortable);
   if (e != cudaSuccess) return fail(tsb::cuda_error(e, "error words"));

@@ -23,24 +23,31 @@ int cuda_error(cudaError_t e, const char* what);
 // Number of SMs of `device` (cached).
 int sm_count(int device);
 
-// Block ids passed by value in kernel parameters (one pipelined chunk).
+// Block ids passed by value in kernel parameters (one pipelined chunk):
+// dev(k) = device block id of the k-th block, stage(k) = its block index in
+// the staging buffer (k) or, in direct mode, its host-tier block id (the
+// kernel then reads / writes the mapped host tier itself).
 constexpr int kMaxParamIds = 64;
 struct ParamIds {
   int64_t v[kMaxParamIds];
+  int64_t s[kMaxParamIds];
+  int32_t direct;
 #ifdef __CUDACC__
-  __device__ __forceinline__ int64_t operator[](int64_t k) const { return v[k]; }
+  __device__ __forceinline__ int64_t dev(int64_t k) const { return v[k]; }
+  __device__ __forceinline__ int64_t stage(int64_t k) const { return direct ? s[k] : k; }
 #endif
 };
 
-// Chunk launchers of kv_block_kernels.cu used by the manager.
+// Chunk launchers of kv_block_kernels.cu used by the manager.  max_ctas caps
+// the grid (0 = a full wave of every SM).
 int mgr_extract(int device, const ts_block_storage* d_st, int n_st,
                 const ParamIds& ids, int64_t n_blocks, void* staging,
                 uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
-                uint64_t max_bb, bool fp8, uint64_t scale_off);
+                uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas);
 int mgr_insert(int device, const ts_block_storage* d_st, int n_st,
                const ParamIds& ids, int64_t n_blocks, const void* staging,
                uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
-               uint64_t max_bb, bool fp8, uint64_t scale_off);
+               uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas);
 
 // Scoped switch of the current CUDA device.
 class DeviceGuard {

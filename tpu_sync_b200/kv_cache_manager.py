@@ -12,6 +12,12 @@ CUDA tensor whose dim 0 indexes blocks.  The manager owns a pinned host tier
 of ``host_blocks_to_allocate`` blocks (block-major: host block h holds block
 h of every storage contiguously).
 
+Two transfer modes: "staged" (default) gathers blocks into an HBM staging
+slot with the extract kernel and moves them with copy-engine DMAs on
+`copy_streams` streams per direction; "direct" lets the extract / insert
+kernels read and write the mapped pinned host tier over PCIe themselves
+(`max_ctas` caps their grid so most SMs stay free).
+
 The control-plane arguments of the reference constructor (ports, controller
 address, worker id, staging slots for the TCP hand-off) are accepted for
 signature compatibility and have no effect: there is no network path here.
@@ -138,6 +144,9 @@ class KVCacheManager:
       model_uid: str = "",
       fp8: bool = False,
       chunk_blocks: int = 0,
+      mode: str = "staged",
+      copy_streams: int = 2,
+      max_ctas: int = 0,
   ):
     if host_blocks_to_allocate is None:
       if max_blocks is None or num_slots is None:
@@ -160,9 +169,13 @@ class KVCacheManager:
         descs[i].dim0 = t.shape[0]
         descs[i].device = t.device.index
         i += 1
+    if mode not in ("staged", "direct"):
+      raise ValueError("mode must be 'staged' or 'direct'")
     opts = _native.ManagerOpts(
         host_blocks=int(host_blocks_to_allocate), chunk_blocks=int(chunk_blocks),
-        shm_name=shm_name.encode(), model_uid=model_uid.encode(), fp8=int(fp8))
+        shm_name=shm_name.encode(), model_uid=model_uid.encode(), fp8=int(fp8),
+        mode=0 if mode == "staged" else 1, copy_streams=int(copy_streams),
+        max_ctas=int(max_ctas))
     handle = ctypes.c_void_p()
     rc = _native.lib().ts_mgr_create(descs, self.num_layers, self.num_shards,
                                      ctypes.byref(opts), ctypes.byref(handle))
