@@ -56,6 +56,9 @@ def parse():
   p.add_argument("--host-blocks", type=int, default=0, help="0 = size to host RAM")
   p.add_argument("--cpu-sample-s", type=float, default=10.0)
   p.add_argument("--no-cpu-baseline", action="store_true")
+  p.add_argument("--kernel-case", default="",
+                 choices=["", "extract", "insert", "extract_fp8", "insert_fp8"],
+                 help="run a few launches of one kernel on a small case (for ncu)")
   return p.parse_args()
 
 
@@ -443,8 +446,42 @@ def run_ours(args):
     dist.destroy_process_group()
 
 
+def run_kernel_case(args):
+  """A few launches of one kernel on a case of a few GB (inputs > L2), for
+  ncu captures: 1024-block C1 pool (2 GiB), 256 blocks per launch
+  (512 MiB read + 512 MiB written), 4 launches."""
+  import torch
+
+  from tpu_sync_b200 import ops, workloads
+  device = torch.device("cuda", 0)
+  g = workloads.C1 if not args.kernel_case.endswith("fp8") else workloads.C2
+  blocks = 1024 if g is workloads.C1 else 2048
+  full = torch.empty((g.layers, g.kv, blocks, g.block_tokens, g.heads, g.head_dim),
+                     dtype=torch.bfloat16, device=device)
+  full.normal_(generator=torch.Generator(device=device).manual_seed(1))
+  storages = [full[l, k] for l in range(g.layers) for k in range(g.kv)]
+  table = ops.StorageTable(storages, fp8=args.kernel_case.endswith("fp8"))
+  n = 256
+  staging = table.new_staging(n)
+  rng = np.random.default_rng(5)
+  for i in range(4):
+    ids = torch.from_numpy(rng.choice(blocks, n, replace=False).astype(np.int64)).to(device)
+    if args.kernel_case.startswith("extract"):
+      ops.kv_extract(table, ids, staging)
+    else:
+      if i == 0:
+        ops.kv_extract(table, ids, staging) if not table.fp8 else None
+      ops.kv_insert(table, ids, staging)
+  torch.cuda.synchronize()
+  print(json.dumps({"kernel_case": args.kernel_case, "blocks_per_launch": n,
+                    "bytes_per_block": table.pitch}))
+
+
 def main():
   args = parse()
+  if args.kernel_case:
+    run_kernel_case(args)
+    return
   if args.impl == "reference":
     run_reference(args)
   else:
