@@ -30,6 +30,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <chrono>
 #include <cstring>
 #include <deque>
@@ -104,7 +105,7 @@ struct ts_manager {
   ts_block_storage* d_table = nullptr;
   bool vec_ok = true;
   uint64_t max_bb = 0;
-  int64_t chunk_blocks = tsb::kMaxParamIds;
+  int64_t chunk_blocks = 64;
 
   int mode = 0;       // 0 staged (kernel + copy engine), 1 direct (kernel <-> mapped host)
   int ncs = 2;        // copy streams per direction (staged)
@@ -137,6 +138,11 @@ struct ts_manager {
   std::vector<int> err_free;
 
   std::mutex mu;
+  // 1 for the owner + 1 per live event; the struct (its mutex and error
+  // words) is freed when the last reference goes, so events released after
+  // ts_mgr_destroy stay valid.
+  std::atomic<int> refs{1};
+  bool closed = false;
 };
 
 namespace tsb {
@@ -279,11 +285,20 @@ int build_plan(ts_manager* m, bool to_host, const int64_t* src, const int64_t* d
   return TS_OK;
 }
 
-// Frees an event whose work has drained, with the manager lock held.
+void unref_manager(ts_manager* m) {
+  if (m->refs.fetch_sub(1) == 1) {
+    if (m->err_host) cudaFreeHost(m->err_host);
+    delete m;
+  }
+}
+
+// Frees an event whose work has drained, with the manager lock held (the
+// owner's reference is still held, so this never frees the manager).
 void drop_event_locked(ts_event* ev) {
   if (ev->err_index >= 0) ev->mgr->err_free.push_back(ev->err_index);
   cudaEventDestroy(ev->start);
   cudaEventDestroy(ev->done);
+  ev->mgr->refs.fetch_sub(1);
   delete ev;
 }
 
@@ -305,6 +320,7 @@ int make_event(ts_manager* m, ts_event** out) {
     return TS_RESOURCE_EXHAUSTED;
   }
   ev->err_index = idx;
+  m->refs.fetch_add(1);
   *out = ev;
   return TS_OK;
 }
@@ -530,6 +546,7 @@ int transfer(ts_manager* m, bool to_host, const int64_t* src, const int64_t* dst
                       shard_idx, &p);
   if (rc != TS_OK) return rc;
   std::lock_guard<std::mutex> lock(m->mu);
+  if (m->closed) return set_error(TS_FAILED_PRECONDITION, "manager already destroyed");
   DeviceGuard g(m->device);
   ts_event* ev = nullptr;
   rc = make_event(m, &ev);
@@ -588,8 +605,9 @@ void destroy_resources(ts_manager* m) {
   for (cudaEvent_t e : m->prof_free) cudaEventDestroy(e);
   if (m->ev_user) cudaEventDestroy(m->ev_user);
   if (m->d_table) cudaFree(m->d_table);
-  if (m->err_host) cudaFreeHost(m->err_host);
   if (m->tier) ts_host_tier_destroy(m->tier, 0);
+  m->d_table = nullptr;
+  m->tier = nullptr;
 }
 
 }  // namespace
@@ -672,7 +690,7 @@ extern "C" int ts_mgr_create(const ts_storage_desc* storages, int num_layers,
   int rc = TS_OK;
   auto fail = [&](int code) {
     tsb::destroy_resources(m);
-    delete m;
+    tsb::unref_manager(m);
     return code;
   };
   const char* shm = opts ? opts->shm_name : nullptr;
@@ -744,8 +762,12 @@ extern "C" int ts_mgr_create(const ts_storage_desc* storages, int num_layers,
 extern "C" int ts_mgr_destroy(ts_manager* mgr) {
   tsb::clear_error();
   if (!mgr) return TS_OK;
-  tsb::destroy_resources(mgr);
-  delete mgr;
+  {
+    std::lock_guard<std::mutex> lock(mgr->mu);
+    tsb::destroy_resources(mgr);  // drains every stream first
+    mgr->closed = true;
+  }
+  tsb::unref_manager(mgr);
   return TS_OK;
 }
 
@@ -899,11 +921,13 @@ extern "C" void ts_event_release(ts_event* ev) {
   tsb::DeviceGuard g(ev->device);
   // The kernels of a pending transfer may still write its error word.
   if (!ev->finished) cudaEventSynchronize(ev->done);
-  if (ev->mgr && ev->err_index >= 0) {
-    std::lock_guard<std::mutex> lock(ev->mgr->mu);
-    ev->mgr->err_free.push_back(ev->err_index);
+  ts_manager* m = ev->mgr;
+  if (m && ev->err_index >= 0) {
+    std::lock_guard<std::mutex> lock(m->mu);
+    m->err_free.push_back(ev->err_index);
   }
   cudaEventDestroy(ev->start);
   cudaEventDestroy(ev->done);
   delete ev;
+  if (m) tsb::unref_manager(m);
 }

@@ -27,7 +27,7 @@ int sm_count(int device);
 // dev(k) = device block id of the k-th block, stage(k) = its block index in
 // the staging buffer (k) or, in direct mode, its host-tier block id (the
 // kernel then reads / writes the mapped host tier itself).
-constexpr int kMaxParamIds = 64;
+constexpr int kMaxParamIds = 256;
 struct ParamIds {
   int64_t v[kMaxParamIds];
   int64_t s[kMaxParamIds];
