@@ -229,9 +229,11 @@ typedef struct ts_manager_opts {
   const char* shm_name;        /* "" / NULL = anonymous pinned memory */
   const char* model_uid;       /* stored in the /dev/shm header */
   int32_t fp8;                 /* 1: host tier holds fp8 e4m3 + per-block scales */
-  int32_t mode;                /* 0: extract/insert kernels + copy-engine DMAs via
-                                  HBM staging; 1: direct -- the kernels read and
-                                  write the mapped host tier over PCIe themselves */
+  int32_t mode;                /* per direction (bit 0 offload, bit 1 reload):
+                                  0 = staged: extract/insert kernels + copy-engine
+                                  DMAs via HBM staging slots; 1 = direct: the
+                                  kernels read / write the mapped host tier over
+                                  PCIe themselves */
   int32_t copy_streams;        /* staged mode: copy streams per direction (1..4) */
   int32_t max_ctas;            /* grid cap of the kernels (0 = every SM) */
 } ts_manager_opts;

@@ -107,7 +107,7 @@ struct ts_manager {
   uint64_t max_bb = 0;
   int64_t chunk_blocks = 64;
 
-  int mode = 0;       // 0 staged (kernel + copy engine), 1 direct (kernel <-> mapped host)
+  int mode = 0;       // bit 0: offload direct, bit 1: reload direct (else staged)
   int ncs = 2;        // copy streams per direction (staged)
   int max_ctas = 0;   // grid cap of the kernels
   uint8_t* host_dev = nullptr;  // device address of the mapped host tier
@@ -377,10 +377,14 @@ uint64_t kernel_bytes(const ts_manager* m, int64_t cn, bool extract) {
   return uint64_t(cn) * (dev + stage);
 }
 
+bool is_direct(const ts_manager* m, bool to_host) {
+  return (m->mode & (to_host ? 1 : 2)) != 0;
+}
+
 // The stream on which every call of a direction completes.
 cudaStream_t last_stream(const ts_manager* m, bool to_host) {
   if (!to_host) return m->s_in_kernel;
-  return m->mode == 1 ? m->s_out_kernel : m->out_cs[0];
+  return is_direct(m, true) ? m->s_out_kernel : m->out_cs[0];
 }
 
 int launch_chunk(ts_manager* m, bool to_host, const ParamIds& ids, int64_t cn,
@@ -414,10 +418,10 @@ int enqueue_transfer(ts_manager* m, bool to_host, const Plan& p, void* user_stre
   cudaStream_t user = reinterpret_cast<cudaStream_t>(user_stream);
   cudaStream_t ks = to_host ? m->s_out_kernel : m->s_in_kernel;
   cudaStream_t* cs = to_host ? m->out_cs : m->in_cs;
-  const bool direct = m->mode == 1 && p.whole;
+  const bool direct = is_direct(m, to_host) && p.whole;
   const cudaStream_t last = last_stream(m, to_host);
   std::vector<cudaStream_t> streams{ks};
-  if (m->mode == 0)
+  if (!is_direct(m, to_host))
     for (int i = 0; i < m->ncs; ++i) streams.push_back(cs[i]);
   int* err_dev = nullptr;
   TS_CUDA_RET(cudaHostGetDevicePointer(reinterpret_cast<void**>(&err_dev), ev->err_word, 0),
@@ -638,9 +642,9 @@ extern "C" int ts_mgr_create(const ts_storage_desc* storages, int num_layers,
   if (opts && opts->chunk_blocks > 0)
     m->chunk_blocks = std::min<int64_t>(opts->chunk_blocks, tsb::kMaxParamIds);
   m->mode = opts ? opts->mode : 0;
-  if (m->mode != 0 && m->mode != 1) {
+  if (m->mode < 0 || m->mode > 3) {
     delete m;
-    return set_error(TS_INVALID_ARGUMENT, "mode must be 0 (staged) or 1 (direct)");
+    return set_error(TS_INVALID_ARGUMENT, "mode must be in 0..3");
   }
   m->ncs = opts && opts->copy_streams > 0 ? std::min(opts->copy_streams, tsb::kMaxCopyStreams) : 2;
   m->max_ctas = opts && opts->max_ctas > 0 ? opts->max_ctas : 0;
@@ -722,31 +726,28 @@ extern "C" int ts_mgr_create(const ts_storage_desc* storages, int num_layers,
     e = cudaStreamCreateWithFlags(s, cudaStreamNonBlocking);
     if (e != cudaSuccess) return fail(tsb::cuda_error(e, "stream create"));
   }
-  if (m->mode == 0) {
-    for (int i = 0; i < m->ncs; ++i) {
-      e = cudaStreamCreateWithFlags(&m->out_cs[i], cudaStreamNonBlocking);
-      if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&m->in_cs[i], cudaStreamNonBlocking);
-      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&m->out_join[i], cudaEventDisableTiming);
-      if (e != cudaSuccess) return fail(tsb::cuda_error(e, "copy stream create"));
-    }
+  for (int i = 0; i < m->ncs; ++i) {
+    e = cudaStreamCreateWithFlags(&m->out_cs[i], cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&m->in_cs[i], cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&m->out_join[i], cudaEventDisableTiming);
+    if (e != cudaSuccess) return fail(tsb::cuda_error(e, "copy stream create"));
   }
   e = cudaEventCreateWithFlags(&m->ev_user, cudaEventDisableTiming);
   if (e != cudaSuccess) return fail(tsb::cuda_error(e, "event create"));
-  if (m->mode == 0) {
-    const size_t slot_bytes = size_t(m->chunk_blocks) * m->host_pitch;
-    m->out_slots.resize(size_t(2 * m->ncs));
-    m->in_slots.resize(size_t(2 * m->ncs));
-    for (std::vector<tsb::Slot>* slots : {&m->out_slots, &m->in_slots})
-      for (tsb::Slot& sl : *slots) {
-        e = cudaMalloc(&sl.buf, slot_bytes);
-        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sl.ready, cudaEventDisableTiming);
-        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sl.free, cudaEventDisableTiming);
-        if (e != cudaSuccess) return fail(tsb::cuda_error(e, "staging slot"));
-      }
-  } else {
-    e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&m->host_dev), m->host, 0);
-    if (e != cudaSuccess) return fail(tsb::cuda_error(e, "host tier mapping"));
+  const size_t slot_bytes = size_t(m->chunk_blocks) * m->host_pitch;
+  for (int dir = 0; dir < 2; ++dir) {
+    if (tsb::is_direct(m, dir == 0)) continue;
+    std::vector<tsb::Slot>& slots = dir == 0 ? m->out_slots : m->in_slots;
+    slots.resize(size_t(2 * m->ncs));
+    for (tsb::Slot& sl : slots) {
+      e = cudaMalloc(&sl.buf, slot_bytes);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sl.ready, cudaEventDisableTiming);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sl.free, cudaEventDisableTiming);
+      if (e != cudaSuccess) return fail(tsb::cuda_error(e, "staging slot"));
+    }
   }
+  e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&m->host_dev), m->host, 0);
+  if (e != cudaSuccess) return fail(tsb::cuda_error(e, "host tier mapping"));
   e = cudaHostAlloc(reinterpret_cast<void**>(&m->err_host), sizeof(int) * tsb::kErrWords,
                     cudaHostAllocMapped | cudaHostAllocPortable);
   if (e != cudaSuccess) return fail(tsb::cuda_error(e, "error words"));

@@ -12,11 +12,12 @@ CUDA tensor whose dim 0 indexes blocks.  The manager owns a pinned host tier
 of ``host_blocks_to_allocate`` blocks (block-major: host block h holds block
 h of every storage contiguously).
 
-Two transfer modes: "staged" (default) gathers blocks into an HBM staging
-slot with the extract kernel and moves them with copy-engine DMAs on
-`copy_streams` streams per direction; "direct" lets the extract / insert
-kernels read and write the mapped pinned host tier over PCIe themselves
-(`max_ctas` caps their grid so most SMs stay free).
+Transfer modes, chosen per direction: "staged" gathers blocks into an HBM
+staging slot with the extract kernel and moves them with copy-engine DMAs on
+`copy_streams` streams per direction (and the reverse for reload); "direct"
+lets the extract / insert kernels read and write the mapped pinned host tier
+over PCIe themselves (`max_ctas` caps their grid so most SMs stay free);
+"direct_d2h" / "direct_h2d" use direct for one direction only.
 
 The control-plane arguments of the reference constructor (ports, controller
 address, worker id, staging slots for the TCP hand-off) are accepted for
@@ -169,12 +170,13 @@ class KVCacheManager:
         descs[i].dim0 = t.shape[0]
         descs[i].device = t.device.index
         i += 1
-    if mode not in ("staged", "direct"):
-      raise ValueError("mode must be 'staged' or 'direct'")
+    modes = {"staged": 0, "direct_d2h": 1, "direct_h2d": 2, "direct": 3}
+    if mode not in modes:
+      raise ValueError(f"mode must be one of {sorted(modes)}")
     opts = _native.ManagerOpts(
         host_blocks=int(host_blocks_to_allocate), chunk_blocks=int(chunk_blocks),
         shm_name=shm_name.encode(), model_uid=model_uid.encode(), fp8=int(fp8),
-        mode=0 if mode == "staged" else 1, copy_streams=int(copy_streams),
+        mode=modes[mode], copy_streams=int(copy_streams),
         max_ctas=int(max_ctas))
     handle = ctypes.c_void_p()
     rc = _native.lib().ts_mgr_create(descs, self.num_layers, self.num_shards,
