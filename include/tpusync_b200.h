@@ -158,6 +158,11 @@ TS_API int ts_reshard_copy(int device, const ts_reshard_chunk* d_chunks,
                     const int64_t* d_item_prefix, int64_t n_chunks,
                     int64_t n_items, int src_dtype, int dst_dtype, void* stream);
 
+/* Lets kernels running on `device` load and store `peer`'s memory through
+ * plain device pointers (NVLink P2P); idempotent.  The in-process
+ * counterpart of the reference's peer connection set-up. */
+TS_API int ts_enable_peer_access(int device, int peer);
+
 /* ------------------------------------------------------------------------ */
 /* Paged KV relayout (disaggregated prefill -> decode hand-off).             */
 /* ------------------------------------------------------------------------ */

@@ -135,3 +135,56 @@ def test_planner_oracle_matches_reference_goldens():
         pairs.append({"src": i, "dst": j, "chunks": [list(c) for c in
                       ors.generate_strided_copy_chunks(s, d, inter, case["itemsize"])]})
     assert pairs == case["pairs"], case["param"]
+
+
+def test_product_planner_matches_reference_goldens():
+  from tpu_sync_b200 import reshard_plan as rp
+  data = json.loads(GOLDEN.read_text())
+  for case in data["slices"]:
+    got = rp.shard_boxes(case["global_shape"], case["mesh_shape"])
+    assert [[list(d) for d in b] for b in got] == case["slices"]
+  for case in data["plans"]:
+    sb = rp.shard_boxes(case["shape"], case["src_mesh"])
+    db = rp.shard_boxes(case["shape"], case["dst_mesh"])
+    pairs = []
+    for i, s in enumerate(sb):
+      for j, d in enumerate(db):
+        inter = rp.box_intersection(s, d)
+        if inter is not None:
+          pairs.append({"src": i, "dst": j, "chunks": [list(c) for c in
+                        rp.plan_bytes(s, d, inter, case["itemsize"])]})
+    assert pairs == case["pairs"], case["param"]
+
+
+def test_planner_covers_every_destination_element_once():
+  from tpu_sync_b200 import reshard_plan as rp, workloads
+  for name, shape, split in workloads.llama3_8b_params()[:12]:
+    small = tuple(max(8, d // 64) for d in shape)
+    v = rp.VariableSpec(name, small, workloads.mesh_for(small, "fsdp", 4),
+                        workloads.mesh_for(small, split, 4))
+    plan = rp.build_plan([v])
+    dboxes = rp.shard_boxes(small, v.dst_mesh)
+    for d, box in enumerate(dboxes):
+      n = int(np.prod(rp.local_shape(box)))
+      hits = np.zeros(n, np.int64)
+      for (vi, s, dd), chunks in plan.chunks.items():
+        if dd != d:
+          continue
+        for (so, do, size, ss, ds, cnt) in chunks:
+          for c in range(cnt):
+            hits[do + c * ds: do + c * ds + size] += 1
+      assert (hits == 1).all(), (name, d)
+
+
+def test_normalized_plan_moves_same_elements():
+  from tpu_sync_b200 import reshard_plan as rp
+  v = rp.VariableSpec("x", (64, 48), (4, 1), (1, 1))
+  raw = rp.build_plan([v], normalize_runs=False)
+  norm = rp.build_plan([v])
+  src = np.arange(64 * 48, dtype=np.float32)
+  for key in raw.chunks:
+    a = np.zeros(64 * 48, np.float32)
+    b = np.zeros(64 * 48, np.float32)
+    ors.apply_element_chunks(src, a, raw.chunks[key], False)
+    ors.apply_element_chunks(src, b, norm.chunks[key], False)
+    np.testing.assert_array_equal(a, b)

@@ -1,0 +1,131 @@
+"""GPU parity of the weight-sync reshard executor and the KV hand-off relayout
+kernel against the CPU oracle (bit-exact, fp32 -> bf16 round-to-nearest-even)."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import fp8 as ofp8
+from oracle import reshard as ors
+from tpu_sync_b200 import ops, workloads
+from tpu_sync_b200 import reshard_plan as rp
+from tpu_sync_b200.weight_synchronizer import WeightSynchronizer
+
+pytestmark = pytest.mark.gpu
+
+
+def small_llama(hidden=256, ffn=640, vocab=1000, layers=2, kv=64):
+  """Llama-3-8B-shaped parameter list scaled down (same splits)."""
+  out = [("embed_tokens", (vocab, hidden), "vocab")]
+  for i in range(layers):
+    p = f"layers.{i}."
+    out += [(p + "q_proj", (hidden, hidden), "col"), (p + "k_proj", (kv, hidden), "col"),
+            (p + "v_proj", (kv, hidden), "col"), (p + "o_proj", (hidden, hidden), "row"),
+            (p + "gate_proj", (ffn, hidden), "col"), (p + "up_proj", (ffn, hidden), "col"),
+            (p + "down_proj", (hidden, ffn), "row"),
+            (p + "input_layernorm", (hidden,), "rep"),
+            (p + "post_attention_layernorm", (hidden,), "rep")]
+  out += [("norm", (hidden,), "rep"), ("lm_head", (vocab, hidden), "vocab")]
+  return out
+
+
+def run_reshard(cuda, n_src, n_dst, params, src_dtype=torch.float32, dst_dtype=torch.bfloat16):
+  g = torch.Generator().manual_seed(3)
+  specs, globals_ = [], []
+  for li, (name, shape, split) in enumerate(params):
+    specs.append(rp.VariableSpec(name, shape, workloads.mesh_for(shape, "fsdp", n_src),
+                                 workloads.mesh_for(shape, split, n_dst), layer_idx=li))
+    globals_.append((torch.randn(shape, generator=g) * 0.02).to(src_dtype))
+  plan = rp.build_plan(specs)
+  # trainer: one synchronizer with n_src shards per layer (all on cuda:0)
+  grid = []
+  for v, full in zip(specs, globals_):
+    boxes = rp.shard_boxes(v.shape, v.src_mesh)
+    grid.append([full[tuple(slice(a, b) for a, b in box)].contiguous().to(cuda)
+                 for box in boxes])
+  ws = WeightSynchronizer(grid)
+  dest = {}
+  for vi, v in enumerate(specs):
+    for d, box in enumerate(rp.shard_boxes(v.shape, v.dst_mesh)):
+      dest[(vi, d)] = torch.zeros(rp.local_shape(box), dtype=dst_dtype, device=cuda)
+  fut = ws.push_weights_resharded(plan, {s: s for s in range(n_src)}, dest)
+  fut.Await()
+  torch.cuda.synchronize()
+  for vi, v in enumerate(specs):
+    want_full = globals_[vi].to(dst_dtype)
+    for d, box in enumerate(rp.shard_boxes(v.shape, v.dst_mesh)):
+      want = want_full[tuple(slice(a, b) for a, b in box)]
+      got = dest[(vi, d)].cpu()
+      assert torch.equal(got.view(torch.int16) if dst_dtype == torch.bfloat16 else got,
+                         want.view(torch.int16) if dst_dtype == torch.bfloat16 else want), \
+          (v.name, d)
+  return plan
+
+
+@pytest.mark.parametrize("n_src,n_dst", [(4, 4), (1, 1), (1, 2), (2, 4)])
+def test_llama_shaped_reshard_fp32_to_bf16(cuda, n_src, n_dst):
+  run_reshard(cuda, n_src, n_dst, small_llama())
+
+
+def test_reshard_identity_dtype_odd_shapes(cuda):
+  params = [("a", (37, 29), "col"), ("b", (13, 51), "row"), ("c", (7,), "rep"),
+            ("d", (9, 4, 6), "col")]
+  run_reshard(cuda, 3, 2, params, torch.float32, torch.float32)
+  run_reshard(cuda, 2, 3, params, torch.bfloat16, torch.bfloat16)
+
+
+def test_bf16_cast_matches_oracle_rne(cuda):
+  v = np.concatenate([np.random.default_rng(4).standard_normal(4097).astype(np.float32),
+                      np.array([0.0, -0.0, 3.4e38, 1e-40, np.inf, -np.inf], np.float32)])
+  src = torch.from_numpy(v).to(cuda)
+  dst = torch.empty(v.size, dtype=torch.bfloat16, device=cuda)
+  prog = ops.ReshardProgram([(src, dst, 0, 0, v.size, 0, 0, 1)], torch.float32,
+                            torch.bfloat16, cuda)
+  prog.launch()
+  torch.cuda.synchronize()
+  np.testing.assert_array_equal(dst.view(torch.int16).cpu().numpy().view(np.uint16),
+                                ofp8.f32_to_bf16_bits_rne(v))
+
+
+GEOM_SRC = dict(block_tokens=16, heads=2, head_bytes=256, head_major=1)
+GEOM_DST = dict(block_tokens=64, heads=2, head_bytes=256, head_major=0)
+
+
+@pytest.mark.parametrize("seq_tokens", [256, 200, 17])
+def test_relayout_head_major16_to_token_major64(cuda, seq_tokens):
+  n_seqs, n_st = 3, 4
+  rng = np.random.default_rng(7)
+  sbps = (seq_tokens + 15) // 16
+  dbps = (seq_tokens + 63) // 64
+  n_src_blocks, n_dst_blocks = n_seqs * sbps + 5, n_seqs * dbps + 3
+  src_table = rng.permutation(n_src_blocks)[:n_seqs * sbps].reshape(n_seqs, sbps).astype(np.int32)
+  dst_table = rng.permutation(n_dst_blocks)[:n_seqs * dbps].reshape(n_seqs, dbps).astype(np.int32)
+  sbb, dbb = 16 * 2 * 256, 64 * 2 * 256
+  srcs = [torch.from_numpy(rng.integers(0, 256, (n_src_blocks, sbb), dtype=np.uint8)).to(cuda)
+          for _ in range(n_st)]
+  dsts = [torch.zeros((n_dst_blocks, dbb), dtype=torch.uint8, device=cuda) for _ in range(n_st)]
+  ops.kv_relayout(srcs, dsts, GEOM_SRC, GEOM_DST, torch.from_numpy(src_table),
+                  torch.from_numpy(dst_table), seq_tokens, device=cuda)
+  torch.cuda.synchronize()
+  for s, d in zip(srcs, dsts):
+    want = np.zeros((n_dst_blocks, dbb), np.uint8)
+    ors.relayout(s.cpu().numpy(), want, GEOM_SRC, GEOM_DST, src_table, dst_table, seq_tokens)
+    np.testing.assert_array_equal(d.cpu().numpy(), want)
+
+
+def test_relayout_round_trip(cuda):
+  """token-major 64 -> head-major 16 inverts the forward relayout."""
+  n_seqs, T = 2, 128
+  rng = np.random.default_rng(8)
+  st = rng.permutation(20)[:16].reshape(2, 8).astype(np.int32)
+  dt = rng.permutation(6)[:4].reshape(2, 2).astype(np.int32)
+  src = torch.from_numpy(rng.integers(0, 256, (20, 16 * 2 * 256), dtype=np.uint8)).to(cuda)
+  mid = torch.zeros((6, 64 * 2 * 256), dtype=torch.uint8, device=cuda)
+  back = torch.zeros_like(src)
+  ops.kv_relayout([src], [mid], GEOM_SRC, GEOM_DST, torch.from_numpy(st), torch.from_numpy(dt),
+                  T, device=cuda)
+  ops.kv_relayout([mid], [back], GEOM_DST, GEOM_SRC, torch.from_numpy(dt), torch.from_numpy(st),
+                  T, device=cuda)
+  torch.cuda.synchronize()
+  used = st.reshape(-1)
+  assert torch.equal(back[used], src[used])

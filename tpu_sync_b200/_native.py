@@ -105,6 +105,7 @@ _SIGS = {
                                              ctypes.c_int, c_i64_p]),
     "ts_reshard_copy": (ctypes.c_int, [ctypes.c_int, _V, _V, ctypes.c_int64,
                                        ctypes.c_int64, ctypes.c_int, ctypes.c_int, _V]),
+    "ts_enable_peer_access": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
     "ts_kv_relayout": (ctypes.c_int, [ctypes.c_int, _V, _V, ctypes.c_int,
                                       PageGeometry, PageGeometry, _V, ctypes.c_int64,
                                       _V, ctypes.c_int64, ctypes.c_int64,

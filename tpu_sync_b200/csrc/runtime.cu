@@ -108,3 +108,19 @@ extern "C" int ts_coalesce_runs(const int64_t* src, const int64_t* dst,
   *n_out = m;
   return TS_OK;
 }
+
+extern "C" int ts_enable_peer_access(int device, int peer) {
+  tsb::clear_error();
+  if (device == peer) return TS_OK;
+  int can = 0;
+  TS_CUDA_RET(cudaDeviceCanAccessPeer(&can, device, peer), "peer query");
+  if (!can) return tsb::set_errorf(TS_UNAVAILABLE, "device %d cannot access device %d", device, peer);
+  tsb::DeviceGuard g(device);
+  cudaError_t e = cudaDeviceEnablePeerAccess(peer, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    cudaGetLastError();  // clear the sticky-free "already enabled" status
+    return TS_OK;
+  }
+  TS_CUDA_RET(e, "enable peer access");
+  return TS_OK;
+}

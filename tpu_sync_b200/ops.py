@@ -75,6 +75,13 @@ class StorageTable:
     return torch.empty((n_blocks, self.pitch), dtype=torch.uint8, device=self.device)
 
 
+def _keep(tensors, stream: Optional[torch.cuda.Stream]) -> None:
+  """Keeps temporaries alive for kernels queued on a non-current stream."""
+  if stream is not None:
+    for t in tensors:
+      t.record_stream(stream)
+
+
 def _ids(ids, device) -> torch.Tensor:
   if isinstance(ids, torch.Tensor):
     t = ids.to(device=device, dtype=torch.int64).contiguous()
@@ -97,6 +104,7 @@ def kv_extract(table: StorageTable, ids, staging: torch.Tensor,
   args += [ctypes.c_void_p(err_flag.data_ptr() if err_flag is not None else 0),
            _stream(stream, table.device)]
   _native.check(fn(*args), "kv_extract: ")
+  _keep([d_ids], stream)
   return staging
 
 
@@ -114,6 +122,7 @@ def kv_insert(table: StorageTable, ids, staging: torch.Tensor,
   args += [ctypes.c_void_p(err_flag.data_ptr() if err_flag is not None else 0),
            _stream(stream, table.device)]
   _native.check(fn(*args), "kv_insert: ")
+  _keep([d_ids], stream)
 
 
 _TORCH_TO_TS = {torch.uint8: _native.DTYPE_U8, torch.bfloat16: _native.DTYPE_BF16,
@@ -187,5 +196,4 @@ def kv_relayout(src_storages: Sequence, dst_storages: Sequence, src_geom: dict,
       n, sg, dg, ctypes.c_void_p(st.data_ptr()), st.shape[1],
       ctypes.c_void_p(dt.data_ptr()), dt.shape[1], st.shape[0], int(seq_tokens),
       _stream(stream, device)), "kv_relayout: ")
-  # keep the address tables alive until the kernel has consumed them
-  torch.cuda.current_stream(device).synchronize() if stream is None else stream.synchronize()
+  _keep([d_src, d_dst, st, dt], stream)

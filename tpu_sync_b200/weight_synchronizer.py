@@ -1,0 +1,218 @@
+"""WeightSynchronizer: trainer -> sampler weight reshard on B200 GPUs.
+
+Keeps the reference surface (tpu_sync/api/torch/weight_synchronizer.py:36-123:
+``WeightSynchronizer(device_tensors[layers][shards], ...)``, ``d2h()``,
+``h2d()``, ``get_host_buffer(layer, shard)``, ``push_weights(peers)``) and
+replaces the resharded push (WeightSynchronizerBase::PushWeightsResharded,
+tpu_sync/weight_sync/weight_synchronizer_base.cc:558-760: per-layer D2H, TCP
+push of strided chunks into the peers' host buffers, H2D on the receiver)
+with one kernel per source GPU that reads the trainer shard in HBM, converts
+fp32 -> bf16 on the way when the sampler is bf16, and stores straight into the
+sampler tensors -- on the same GPU or on a peer GPU over NVLink (peer pointers
+within a process, CUDA IPC mappings across processes).
+
+Destinations are described by a ``{(var_index, dst_shard): tensor}`` map; in a
+multi-process job the sampler ranks export theirs with
+``export_destinations`` and the trainer ranks map them with
+``import_destinations``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Any, Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from tpu_sync_b200 import _native, ops
+from tpu_sync_b200.reshard_plan import ReshardPlan
+
+
+def enable_peer_access(device: int, peer: int) -> None:
+  """Lets kernels on `device` load / store `peer`'s memory (idempotent)."""
+  if device == peer:
+    return
+  _native.check(_native.lib().ts_enable_peer_access(int(device), int(peer)),
+                "enable_peer_access: ")
+
+
+class PushFuture:
+  """Completion of one resharded push (device-side event on the source)."""
+
+  def __init__(self, event: torch.cuda.Event, programs):
+    self._event = event
+    self._programs = programs  # keep device tables alive until completion
+
+  def is_ready(self) -> bool:
+    return self._event.query()
+
+  def Await(self) -> None:
+    self._event.synchronize()
+
+  wait = Await
+
+  def stream_wait(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+    (stream or torch.cuda.current_stream()).wait_event(self._event)
+
+
+class WeightSynchronizer:
+  """Zero-copy trainer -> sampler weight movement."""
+
+  def __init__(
+      self,
+      device_tensors: List[List[torch.Tensor]],
+      local_port: Optional[int] = None,
+      parallelism: int = 1,
+      listener_port: Optional[int] = None,
+      bind_ip: Optional[str] = None,
+      unsafe_skip_buffer_lock: bool = True,
+      auto_h2d: bool = False,
+      *,
+      layer_names: Optional[Sequence[str]] = None,
+  ):
+    grid = [[t] if isinstance(t, torch.Tensor) else list(t) for t in device_tensors]
+    if not grid or not grid[0]:
+      raise ValueError("device_tensors must hold at least one tensor")
+    n_sh = len(grid[0])
+    for layer in grid:
+      if len(layer) != n_sh:
+        raise RuntimeError("Number of shards mismatch across layers")
+      for t in layer:
+        if not t.is_cuda or not t.is_contiguous():
+          raise ValueError("device tensors must be contiguous CUDA tensors")
+    self._grid = grid
+    self.layer_names = list(layer_names) if layer_names else [str(i) for i in range(len(grid))]
+    self._host: Dict[Tuple[int, int], torch.Tensor] = {}
+    self.auto_h2d = auto_h2d
+
+  # -- reference properties --------------------------------------------------
+  @property
+  def num_layers(self) -> int:
+    return len(self._grid)
+
+  @property
+  def num_shards(self) -> int:
+    return len(self._grid[0])
+
+  @property
+  def slice_byte_size(self) -> int:
+    t = self._grid[0][0]
+    return t.numel() * t.element_size() // max(t.shape[0], 1) if t.dim() else t.element_size()
+
+  @property
+  def local_port(self) -> Optional[int]:
+    return None
+
+  @property
+  def listener_port(self) -> Optional[int]:
+    return None
+
+  @property
+  def is_listener_active(self) -> bool:
+    return False
+
+  # -- host staging (reference d2h / h2d / get_host_buffer) -----------------
+  def _host_buf(self, l: int, s: int) -> torch.Tensor:
+    key = (l, s)
+    if key not in self._host:
+      t = self._grid[l][s]
+      self._host[key] = torch.empty(t.numel() * t.element_size(), dtype=torch.uint8,
+                                    pin_memory=True)
+    return self._host[key]
+
+  def d2h(self) -> None:
+    """Copies every (layer, shard) tensor into its pinned host buffer."""
+    for l, layer in enumerate(self._grid):
+      for s, t in enumerate(layer):
+        self._host_buf(l, s).copy_(t.view(-1).view(torch.uint8), non_blocking=True)
+    for layer in self._grid:
+      for t in layer:
+        torch.cuda.current_stream(t.device).synchronize()
+
+  def h2d(self) -> None:
+    """Copies every pinned host buffer back into its device tensor."""
+    for l, layer in enumerate(self._grid):
+      for s, t in enumerate(layer):
+        t.view(-1).view(torch.uint8).copy_(self._host_buf(l, s), non_blocking=True)
+    for layer in self._grid:
+      for t in layer:
+        torch.cuda.current_stream(t.device).synchronize()
+
+  def get_host_buffer(self, layer_idx: int = 0, shard_idx: int = 0) -> torch.Tensor:
+    """Zero-copy uint8 host view of one (layer, shard) staging buffer."""
+    if not (0 <= layer_idx < self.num_layers and 0 <= shard_idx < self.num_shards):
+      raise RuntimeError("layer or shard index out of range")
+    return self._host_buf(layer_idx, shard_idx)
+
+  def push_weights(self, peers: Sequence[Any]) -> None:
+    """Whole-buffer push to peer synchronizers with the same layout.
+
+    ``peers`` are WeightSynchronizer objects (or [layers][shards] tensor
+    grids) of identical shapes; replaces PushWeights' D2H + TCP push of every
+    host buffer (weight_synchronizer_base.cc:541-556) with device copies.
+    """
+    if not peers:
+      raise RuntimeError("Peer list cannot be empty for trainer weights sync")
+    for p in peers:
+      grid = p._grid if isinstance(p, WeightSynchronizer) else p
+      for l, layer in enumerate(self._grid):
+        for s, t in enumerate(layer):
+          grid[l][s].copy_(t, non_blocking=True)
+    torch.cuda.synchronize()
+
+  # -- resharded push -------------------------------------------------------
+  def push_weights_resharded(self, plan: ReshardPlan, src_shards: Dict[int, int],
+                             destinations: Dict[Tuple[int, int], torch.Tensor],
+                             stream: Optional[torch.cuda.Stream] = None) -> PushFuture:
+    """Executes every chunk of `plan` whose source shard lives here.
+
+    src_shards: local shard index -> plan source shard index.
+    destinations: (var index, plan dst shard) -> destination tensor (local,
+      peer-device, or an IPC-imported tensor).  Variable v reads layer
+      ``plan.variables[v].layer_idx`` of this synchronizer.
+    """
+    programs = []
+    last_event = None
+    for local, src_shard in src_shards.items():
+      by_kind: Dict[Tuple[torch.dtype, torch.dtype], List] = {}
+      device = None
+      for (vi, d), chunks in plan.for_source(src_shard).items():
+        var = plan.variables[vi]
+        src = self._grid[var.layer_idx][local]
+        dst = destinations.get((vi, d))
+        if dst is None:
+          continue
+        device = src.device
+        if dst.device != src.device and dst.device.type == "cuda":
+          enable_peer_access(src.device.index, dst.device.index)
+        kind = (src.dtype, dst.dtype)
+        for (so, do, size, ss, ds, cnt) in chunks:
+          by_kind.setdefault(kind, []).append((src, dst, so, do, size, ss, ds, cnt))
+      if device is None:
+        continue
+      s = stream if stream is not None else torch.cuda.current_stream(device)
+      for (sd, dd), chunk_list in by_kind.items():
+        prog = ops.ReshardProgram(chunk_list, sd, dd, device)
+        prog.launch(s)
+        programs.append(prog)
+      ev = torch.cuda.Event()
+      ev.record(s)
+      last_event = ev
+    if last_event is None:
+      last_event = torch.cuda.Event()
+      last_event.record()
+    return PushFuture(last_event, programs)
+
+
+def export_destinations(dest: Dict[Tuple[int, int], torch.Tensor]) -> Dict:
+  """Picklable CUDA-IPC descriptors of destination tensors (sampler side)."""
+  from torch.multiprocessing.reductions import reduce_tensor
+  return {k: reduce_tensor(t) for k, t in dest.items()}
+
+
+def import_destinations(desc: Dict) -> Dict[Tuple[int, int], torch.Tensor]:
+  """Maps exported destination tensors into this process (trainer side)."""
+  out = {}
+  for k, (fn, args) in desc.items():
+    out[k] = fn(*args)
+  return out
