@@ -119,6 +119,26 @@ TS_API int ts_kv_insert_fp8(int device, const ts_block_storage* d_storages,
                      const void* d_staging, uint64_t stage_pitch,
                      uint64_t scale_off, int* err_flag, void* stream);
 
+/* Offload without device allocation: for callers that cannot cudaMalloc
+ * (an engine that has handed nearly all HBM to its own KV pool or
+ * allocator, where an extra cudaMalloc fails or fragments that pool, and
+ * cudaMalloc / cudaFree may synchronise the device under its running work).
+ * No counterpart in the reference.  For k < n_blocks and every storage s:
+ *   host_dst[dst_ids[k]*host_pitch + st[s].stage_off + b] = storage s block
+ *   src_ids[k], byte b
+ * (the block-major layout of the manager's host tier).  src_ids / dst_ids are
+ * HOST arrays; host_dst is pinned (or registered) host memory of host_blocks
+ * blocks.  Staging is a file-scope device array of 64 MiB: host_pitch above
+ * that is rejected (TS_OUT_OF_RANGE).  Allocates nothing; everything is
+ * queued on `stream` (synchronise it to know the copy landed).  The first
+ * call on a device looks up the array's device address (make it before any
+ * stream capture); calls that overlap on the GPU race on the shared array. */
+TS_API int ts_kv_offload_noalloc(int device, const ts_block_storage* d_storages,
+                                 int n_storages, const int64_t* src_ids,
+                                 const int64_t* dst_ids, int64_t n_blocks,
+                                 void* host_dst, uint64_t host_pitch,
+                                 int64_t host_blocks, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Strided chunk copy (weight-sync reshard executor).                        */
 /* ------------------------------------------------------------------------ */

@@ -100,6 +100,9 @@ _SIGS = {
     "ts_kv_insert_fp8": (ctypes.c_int, [ctypes.c_int, _V, ctypes.c_int, _V,
                                         ctypes.c_int64, _V, ctypes.c_uint64,
                                         ctypes.c_uint64, _V, _V]),
+    "ts_kv_offload_noalloc": (ctypes.c_int, [ctypes.c_int, _V, ctypes.c_int, c_i64_p,
+                                             c_i64_p, ctypes.c_int64, _V, ctypes.c_uint64,
+                                             ctypes.c_int64, _V]),
     "ts_reshard_work_items": (ctypes.c_int, [ctypes.POINTER(ReshardChunk),
                                              ctypes.c_int64, ctypes.c_int,
                                              ctypes.c_int, c_i64_p]),
