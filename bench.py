@@ -56,6 +56,8 @@ def parse():
   p.add_argument("--host-blocks", type=int, default=0, help="0 = size to host RAM")
   p.add_argument("--cpu-sample-s", type=float, default=10.0)
   p.add_argument("--no-cpu-baseline", action="store_true")
+  p.add_argument("--no-exchange", action="store_true",
+                 help="skip the N>=2 weight-sync and hand-off measurements")
   p.add_argument("--kernel-case", default="",
                  choices=["", "extract", "insert", "extract_fp8", "insert_fp8"],
                  help="run a few launches of one kernel on a small case (for ncu)")
@@ -250,6 +252,144 @@ def measure_pcie(torch, device, nbytes=GIB):
   return out
 
 
+def _cumsum(sizes):
+  out, acc = [], 0
+  for n in sizes:
+    out.append(acc)
+    acc += n
+  return out, acc
+
+
+def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
+  """C4: Llama-3-8B fp32 FSDP shards on ranks [0, half) -> TP bf16 shards on
+  ranks [half, 2*half), one reshard kernel per trainer rank storing straight
+  into the sampler ranks' memory (CUDA IPC mappings, NVLink P2P stores)."""
+  import math
+  from tpu_sync_b200 import ops, reshard_plan as rp, workloads
+  from tpu_sync_b200.weight_synchronizer import export_destinations, import_destinations
+  half = world // 2
+  is_src = rank < half
+  idx = rank if is_src else rank - half
+  params = workloads.llama3_8b_params()
+  specs = [rp.VariableSpec(n, s, workloads.mesh_for(s, "fsdp", half),
+                           workloads.mesh_for(s, split, half), layer_idx=i)
+           for i, (n, s, split) in enumerate(params)]
+  plan = rp.build_plan(specs)
+  src_sizes = [[math.prod(rp.local_shape(b)) for b in rp.shard_boxes(v.shape, v.src_mesh)]
+               for v in specs]
+  dst_sizes = [[math.prod(rp.local_shape(b)) for b in rp.shard_boxes(v.shape, v.dst_mesh)]
+               for v in specs]
+  src_off, src_total = _cumsum([src_sizes[v][idx] for v in range(len(specs))]) if is_src else ([], 0)
+  dst_offs = [_cumsum([dst_sizes[v][d] for v in range(len(specs))]) for d in range(half)]
+  if is_src:
+    flat = torch.empty(src_total, dtype=torch.float32, device=device)
+    flat.normal_(0.0, 0.02, generator=torch.Generator(device=device).manual_seed(3 + idx))
+    desc = None
+  else:
+    flat = torch.zeros(dst_offs[idx][1], dtype=torch.bfloat16, device=device)
+    desc = export_destinations({0: flat})
+  descs = [None] * world
+  dist.all_gather_object(descs, desc)
+  per_push_ms, prog = 0.0, None
+  if is_src:
+    dsts = {d: import_destinations(descs[half + d])[0] for d in range(half)}
+    chunks = []
+    for (vi, d), cs in plan.for_source(idx).items():
+      sp = flat.data_ptr() + 4 * src_off[vi]
+      dp = dsts[d].data_ptr() + 2 * dst_offs[d][0][vi]
+      for (so, do, size, ss, ds, cnt) in cs:
+        chunks.append((sp, dp, so, do, size, ss, ds, cnt))
+    prog = ops.ReshardProgram(chunks, torch.float32, torch.bfloat16, device)
+    for _ in range(warmup):
+      prog.launch()
+    torch.cuda.synchronize(device)
+  dist.barrier()
+  if is_src:
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+      prog.launch()
+    e1.record()
+    torch.cuda.synchronize(device)
+    per_push_ms = e0.elapsed_time(e1) / steps
+  dist.barrier()
+  t = torch.tensor([per_push_ms], dtype=torch.float64, device=device)
+  dist.all_reduce(t, op=dist.ReduceOp.MAX)
+  push_s = float(t.item()) / 1e3
+  recv_bytes = max(2 * plan.elements_to(d) for d in range(half))
+  total_params = sum(math.prod(v.shape) for v in specs)
+  del prog
+  if is_src:
+    dsts = None
+  dist.barrier()
+  return {"config": f"C4 Llama-3-8B fp32 FSDP {half} ranks -> bf16 TP={half} ({half}->{half})",
+          "params": total_params, "seconds": round(push_s, 5),
+          "bytes_per_dst_gpu": recv_bytes,
+          "nvlink_gbs_per_dst_gpu": round(recv_bytes / push_s / 1e9, 1) if push_s else None,
+          "frac_of_nvlink_770": round(recv_bytes / push_s / 1e9 / 770.0, 3) if push_s else None,
+          "chunks_per_src": len(plan.for_source(0))}
+
+
+def run_handoff(torch, dist, rank, world, device, steps, warmup):
+  """C3: 8 sequences x 32768 tokens of Llama-3-8B KV (2 heads per GPU) move
+  from rank i (16-token head-major pages) to rank i+half (64-token
+  token-major pages): one relayout kernel per producer storing into the
+  consumer's pages (CUDA IPC mapping, NVLink P2P stores)."""
+  import numpy as np
+  from tpu_sync_b200 import ops
+  from tpu_sync_b200.weight_synchronizer import export_destinations, import_destinations
+  half = world // 2
+  is_src = rank < half
+  n_st, n_seqs, T, H, HB = 64, 8, 32768, 2, 256
+  sg = dict(block_tokens=16, heads=H, head_bytes=HB, head_major=1)
+  dg = dict(block_tokens=64, heads=H, head_bytes=HB, head_major=0)
+  sbps, dbps = T // 16, T // 64
+  rng = np.random.default_rng(30 + (rank % half))
+  st_tab = rng.permutation(n_seqs * sbps).reshape(n_seqs, sbps).astype(np.int32)
+  dt_tab = rng.permutation(n_seqs * dbps).reshape(n_seqs, dbps).astype(np.int32)
+  sbb, dbb = 16 * H * HB, 64 * H * HB
+  if is_src:
+    pages = torch.empty((n_st, n_seqs * sbps, sbb // 2), dtype=torch.bfloat16, device=device)
+    pages.normal_(generator=torch.Generator(device=device).manual_seed(40 + rank))
+    desc = None
+  else:
+    pages = torch.zeros((n_st, n_seqs * dbps, dbb // 2), dtype=torch.bfloat16, device=device)
+    desc = export_destinations({0: pages})
+  descs = [None] * world
+  dist.all_gather_object(descs, desc)
+  ms = 0.0
+  if is_src:
+    peer = import_destinations(descs[rank + half])[0]
+    srcs = [pages[s] for s in range(n_st)]
+    dsts = [peer.data_ptr() + s * peer.stride(0) * 2 for s in range(n_st)]
+    st_t, dt_t = torch.from_numpy(st_tab), torch.from_numpy(dt_tab)
+    for _ in range(warmup):
+      ops.kv_relayout(srcs, dsts, sg, dg, st_t, dt_t, T, device=device)
+    torch.cuda.synchronize(device)
+  dist.barrier()
+  if is_src:
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+      ops.kv_relayout(srcs, dsts, sg, dg, st_t, dt_t, T, device=device)
+    e1.record()
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1) / steps
+  dist.barrier()
+  t = torch.tensor([ms], dtype=torch.float64, device=device)
+  dist.all_reduce(t, op=dist.ReduceOp.MAX)
+  ms = float(t.item())
+  moved = n_st * n_seqs * T * H * HB
+  if is_src:
+    peer = None
+  dist.barrier()
+  return {"config": "C3 8 seqs x 32768 tok, 2 KV heads/GPU, 16-tok head-major -> 64-tok "
+                    f"token-major, {half} pairs (GPU i -> i+{half})",
+          "bytes_per_pair": moved, "ms": round(ms, 3),
+          "nvlink_gbs_per_pair": round(moved / (ms * 1e-3) / 1e9, 1) if ms else None,
+          "frac_of_nvlink_770": round(moved / (ms * 1e-3) / 1e9 / 770.0, 3) if ms else None}
+
+
 def run_ours(args):
   import torch
   import torch.distributed as dist
@@ -399,6 +539,7 @@ def run_ours(args):
     cpu = cpu_offload_reload(B, args.cpu_sample_s)
 
   d2h_gbs = B * pitch / (ms_per_step * 1e-3) / 1e9
+  line = None
   if rank == 0:
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
@@ -440,9 +581,20 @@ def run_ours(args):
             "value": cpu["value"], "unit": "GB/s", "cores": cpu["cores"], "kind": "port",
             "sample": cpu["sample"], "cpu": cpu["cpu"]},
     }
-    print(json.dumps(line), flush=True)
   mgr.close()
+  del mgr, full, storages, table
+  torch.cuda.empty_cache()
+  exchange = {}
+  if world >= 2 and world % 2 == 0 and not args.no_exchange:
+    exchange["weight_sync"] = run_weight_sync(torch, dist, rank, world, device, 3, 2)
+    torch.cuda.empty_cache()
+    exchange["handoff"] = run_handoff(torch, dist, rank, world, device, 3, 2)
+    torch.cuda.empty_cache()
+  if rank == 0:
+    line.update(exchange)
+    print(json.dumps(line), flush=True)
   if world > 1:
+    dist.barrier()
     dist.destroy_process_group()
 
 

@@ -1,0 +1,121 @@
+"""Two-GPU parity of the NVLink paths (skipped with fewer than two GPUs).
+
+* in one process: reshard and relayout kernels on cuda:0 store into
+  tensors on cuda:1 through peer pointers;
+* across two processes: the sampler process exports its destination
+  tensors (CUDA IPC), the trainer process maps them and pushes its fp32
+  shards as bf16; the sampler checks every element bit-exact.
+"""
+
+import multiprocessing as mp
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import reshard as ors
+from tpu_sync_b200 import ops, workloads
+from tpu_sync_b200 import reshard_plan as rp
+
+pytestmark = pytest.mark.gpu
+
+
+def two_gpus():
+  if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+    pytest.skip("needs two GPUs")
+
+
+def small_params():
+  return [("embed", (320, 64), "vocab"), ("q", (64, 64), "col"), ("o", (64, 64), "row"),
+          ("down", (64, 160), "row"), ("norm", (64,), "rep")]
+
+
+def globals_for(params):
+  g = torch.Generator().manual_seed(3)
+  return [(torch.randn(shape, generator=g) * 0.02) for _, shape, _ in params]
+
+
+def test_peer_reshard_and_relayout_in_process():
+  two_gpus()
+  from tpu_sync_b200.weight_synchronizer import WeightSynchronizer
+  params = small_params()
+  specs = [rp.VariableSpec(n, s, workloads.mesh_for(s, "fsdp", 2), workloads.mesh_for(s, sp, 2),
+                           layer_idx=i) for i, (n, s, sp) in enumerate(params)]
+  plan = rp.build_plan(specs)
+  full = globals_for(params)
+  grid = [[full[i][tuple(slice(a, b) for a, b in box)].contiguous().cuda(0)
+           for box in rp.shard_boxes(v.shape, v.src_mesh)] for i, v in enumerate(specs)]
+  dest = {(vi, d): torch.zeros(rp.local_shape(box), dtype=torch.bfloat16, device="cuda:1")
+          for vi, v in enumerate(specs) for d, box in enumerate(rp.shard_boxes(v.shape, v.dst_mesh))}
+  WeightSynchronizer(grid).push_weights_resharded(plan, {0: 0, 1: 1}, dest).Await()
+  torch.cuda.synchronize(1)
+  for (vi, d), t in dest.items():
+    box = rp.shard_boxes(specs[vi].shape, specs[vi].dst_mesh)[d]
+    want = full[vi].to(torch.bfloat16)[tuple(slice(a, b) for a, b in box)]
+    assert torch.equal(t.cpu().view(torch.int16), want.view(torch.int16))
+  # relayout into the peer
+  sg = dict(block_tokens=16, heads=2, head_bytes=256, head_major=1)
+  dg = dict(block_tokens=64, heads=2, head_bytes=256, head_major=0)
+  rng = np.random.default_rng(1)
+  st = rng.permutation(16).reshape(2, 8).astype(np.int32)
+  dt = rng.permutation(4).reshape(2, 2).astype(np.int32)
+  src = torch.from_numpy(rng.integers(0, 256, (16, 8192), dtype=np.uint8)).cuda(0)
+  dst = torch.zeros((4, 32768), dtype=torch.uint8, device="cuda:1")
+  from tpu_sync_b200.weight_synchronizer import enable_peer_access
+  enable_peer_access(0, 1)
+  ops.kv_relayout([src], [dst], sg, dg, torch.from_numpy(st), torch.from_numpy(dt), 128,
+                  device="cuda:0")
+  torch.cuda.synchronize(0)
+  want = np.zeros((4, 32768), np.uint8)
+  ors.relayout(src.cpu().numpy(), want, sg, dg, st, dt, 128)
+  np.testing.assert_array_equal(dst.cpu().numpy(), want)
+
+
+def _sampler(q_out, q_in, result):
+  import torch
+  from tpu_sync_b200 import reshard_plan as rp, workloads
+  from tpu_sync_b200.weight_synchronizer import export_destinations
+  torch.cuda.set_device(1)
+  params = small_params()
+  specs = [rp.VariableSpec(n, s, workloads.mesh_for(s, "fsdp", 1), workloads.mesh_for(s, sp, 1),
+                           layer_idx=i) for i, (n, s, sp) in enumerate(params)]
+  dest = {(vi, 0): torch.zeros(v.shape, dtype=torch.bfloat16, device="cuda:1")
+          for vi, v in enumerate(specs)}
+  q_out.put(export_destinations(dest))
+  q_in.get(timeout=120)  # trainer finished its push
+  full = globals_for(params)
+  ok = all(torch.equal(dest[(vi, 0)].cpu().view(torch.int16),
+                       full[vi].to(torch.bfloat16).view(torch.int16)) for vi in range(len(specs)))
+  result.put(ok)
+
+
+def _trainer(q_in, q_out):
+  import torch
+  from tpu_sync_b200 import reshard_plan as rp, workloads
+  from tpu_sync_b200.weight_synchronizer import WeightSynchronizer, import_destinations
+  torch.cuda.set_device(0)
+  params = small_params()
+  specs = [rp.VariableSpec(n, s, workloads.mesh_for(s, "fsdp", 1), workloads.mesh_for(s, sp, 1),
+                           layer_idx=i) for i, (n, s, sp) in enumerate(params)]
+  plan = rp.build_plan(specs)
+  full = globals_for(params)
+  grid = [[t.cuda(0)] for t in full]
+  dest = import_destinations(q_in.get(timeout=120))
+  WeightSynchronizer(grid).push_weights_resharded(plan, {0: 0}, dest).Await()
+  torch.cuda.synchronize(0)
+  q_out.put("done")
+
+
+def test_cross_process_ipc_reshard():
+  two_gpus()
+  ctx = mp.get_context("spawn")
+  to_trainer, to_sampler, result = ctx.Queue(), ctx.Queue(), ctx.Queue()
+  ps = ctx.Process(target=_sampler, args=(to_trainer, to_sampler, result))
+  pt = ctx.Process(target=_trainer, args=(to_trainer, to_sampler))
+  ps.start()
+  pt.start()
+  pt.join(timeout=180)
+  ok = result.get(timeout=180)
+  ps.join(timeout=60)
+  assert pt.exitcode == 0 and ps.exitcode == 0
+  assert ok
