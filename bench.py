@@ -266,7 +266,8 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
   into the sampler ranks' memory (CUDA IPC mappings, NVLink P2P stores)."""
   import math
   from tpu_sync_b200 import ops, reshard_plan as rp, workloads
-  from tpu_sync_b200.weight_synchronizer import export_destinations, import_destinations
+  from tpu_sync_b200.weight_synchronizer import (close_imports, export_destinations,
+                                                 import_destinations)
   half = world // 2
   is_src = rank < half
   idx = rank if is_src else rank - half
@@ -292,7 +293,8 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
   dist.all_gather_object(descs, desc)
   per_push_ms, prog = 0.0, None
   if is_src:
-    dsts = {d: import_destinations(descs[half + d])[0] for d in range(half)}
+    dsts = {d: import_destinations(descs[half + d], kernel_device=device.index)[0]
+            for d in range(half)}
     chunks = []
     for (vi, d), cs in plan.for_source(idx).items():
       sp = flat.data_ptr() + 4 * src_off[vi]
@@ -321,6 +323,7 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
   del prog
   if is_src:
     dsts = None
+    close_imports(device.index)
   dist.barrier()
   return {"config": f"C4 Llama-3-8B fp32 FSDP {half} ranks -> bf16 TP={half} ({half}->{half})",
           "params": total_params, "seconds": round(push_s, 5),
@@ -337,7 +340,8 @@ def run_handoff(torch, dist, rank, world, device, steps, warmup):
   consumer's pages (CUDA IPC mapping, NVLink P2P stores)."""
   import numpy as np
   from tpu_sync_b200 import ops
-  from tpu_sync_b200.weight_synchronizer import export_destinations, import_destinations
+  from tpu_sync_b200.weight_synchronizer import (close_imports, export_destinations,
+                                                 import_destinations)
   half = world // 2
   is_src = rank < half
   n_st, n_seqs, T, H, HB = 64, 8, 32768, 2, 256
@@ -359,9 +363,10 @@ def run_handoff(torch, dist, rank, world, device, steps, warmup):
   dist.all_gather_object(descs, desc)
   ms = 0.0
   if is_src:
-    peer = import_destinations(descs[rank + half])[0]
+    peer = import_destinations(descs[rank + half], kernel_device=device.index)[0]
     srcs = [pages[s] for s in range(n_st)]
-    dsts = [peer.data_ptr() + s * peer.stride(0) * 2 for s in range(n_st)]
+    storage_bytes = n_seqs * dbps * dbb
+    dsts = [peer.data_ptr() + s * storage_bytes for s in range(n_st)]
     st_t, dt_t = torch.from_numpy(st_tab), torch.from_numpy(dt_tab)
     for _ in range(warmup):
       ops.kv_relayout(srcs, dsts, sg, dg, st_t, dt_t, T, device=device)
@@ -382,6 +387,7 @@ def run_handoff(torch, dist, rank, world, device, steps, warmup):
   moved = n_st * n_seqs * T * H * HB
   if is_src:
     peer = None
+    close_imports(device.index)
   dist.barrier()
   return {"config": "C3 8 seqs x 32768 tok, 2 KV heads/GPU, 16-tok head-major -> 64-tok "
                     f"token-major, {half} pairs (GPU i -> i+{half})",

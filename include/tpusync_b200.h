@@ -183,6 +183,15 @@ TS_API int ts_reshard_copy(int device, const ts_reshard_chunk* d_chunks,
  * counterpart of the reference's peer connection set-up. */
 TS_API int ts_enable_peer_access(int device, int peer);
 
+/* Maps another process's device allocation (a 64-byte cudaIpcMemHandle_t)
+ * into this process FOR KERNELS RUNNING ON `device`: the handle is opened
+ * with `device` current and lazy peer access, so `device`'s kernels can
+ * store into the peer GPU's memory over NVLink.  Replaces the TCP push of
+ * the reference's cross-host transfers on one NVSwitch box.  A handle may be
+ * opened once per device per process; ts_ipc_close unmaps it. */
+TS_API int ts_ipc_open(int device, const void* handle_bytes, void** base_out);
+TS_API int ts_ipc_close(int device, void* base);
+
 /* ------------------------------------------------------------------------ */
 /* Paged KV relayout (disaggregated prefill -> decode hand-off).             */
 /* ------------------------------------------------------------------------ */

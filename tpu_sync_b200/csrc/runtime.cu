@@ -9,6 +9,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -122,5 +123,25 @@ extern "C" int ts_enable_peer_access(int device, int peer) {
     return TS_OK;
   }
   TS_CUDA_RET(e, "enable peer access");
+  return TS_OK;
+}
+
+extern "C" int ts_ipc_open(int device, const void* handle_bytes, void** base_out) {
+  tsb::clear_error();
+  if (!handle_bytes || !base_out) return tsb::set_error(TS_INVALID_ARGUMENT, "null pointer argument");
+  cudaIpcMemHandle_t h;
+  static_assert(sizeof(h) == 64, "cudaIpcMemHandle_t is 64 bytes");
+  std::memcpy(&h, handle_bytes, sizeof(h));
+  tsb::DeviceGuard g(device);
+  void* p = nullptr;
+  TS_CUDA_RET(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+  *base_out = p;
+  return TS_OK;
+}
+
+extern "C" int ts_ipc_close(int device, void* base) {
+  tsb::clear_error();
+  tsb::DeviceGuard g(device);
+  TS_CUDA_RET(cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle");
   return TS_OK;
 }

@@ -146,8 +146,8 @@ class ReshardProgram:
     n = len(chunks)
     arr = (_native.ReshardChunk * max(n, 1))()
     for i, (sp, dp, so, do, size, ss, ds, cnt) in enumerate(chunks):
-      arr[i].src_ptr = sp.data_ptr() if isinstance(sp, torch.Tensor) else int(sp)
-      arr[i].dst_ptr = dp.data_ptr() if isinstance(dp, torch.Tensor) else int(dp)
+      arr[i].src_ptr = sp.data_ptr() if hasattr(sp, "data_ptr") else int(sp)
+      arr[i].dst_ptr = dp.data_ptr() if hasattr(dp, "data_ptr") else int(dp)
       arr[i].src_off, arr[i].dst_off, arr[i].size = int(so), int(do), int(size)
       arr[i].src_stride, arr[i].dst_stride, arr[i].count = int(ss), int(ds), int(cnt)
     prefix = np.zeros(n + 1, dtype=np.int64)
@@ -180,7 +180,7 @@ def kv_relayout(src_storages: Sequence, dst_storages: Sequence, src_geom: dict,
   n = len(src_storages)
   if len(dst_storages) != n:
     raise ValueError("source and destination storage counts differ")
-  ptr = lambda x: x.data_ptr() if isinstance(x, torch.Tensor) else int(x)
+  ptr = lambda x: x.data_ptr() if hasattr(x, "data_ptr") else int(x)
   d_src = torch.tensor([ptr(x) for x in src_storages], dtype=torch.int64,
                        device=device)
   d_dst = torch.tensor([ptr(x) for x in dst_storages], dtype=torch.int64,

@@ -167,8 +167,9 @@ class WeightSynchronizer:
     """Executes every chunk of `plan` whose source shard lives here.
 
     src_shards: local shard index -> plan source shard index.
-    destinations: (var index, plan dst shard) -> destination tensor (local,
-      peer-device, or an IPC-imported tensor).  Variable v reads layer
+    destinations: (var index, plan dst shard) -> destination tensor (local or
+      on a peer GPU of this process) or PeerBuffer (another process's memory,
+      from import_destinations with this source's device).  Variable v reads layer
       ``plan.variables[v].layer_idx`` of this synchronizer.
     """
     programs = []
@@ -183,7 +184,7 @@ class WeightSynchronizer:
         if dst is None:
           continue
         device = src.device
-        if dst.device != src.device and dst.device.type == "cuda":
+        if isinstance(dst, torch.Tensor) and dst.device != src.device:
           enable_peer_access(src.device.index, dst.device.index)
         kind = (src.dtype, dst.dtype)
         for (so, do, size, ss, ds, cnt) in chunks:
@@ -204,15 +205,67 @@ class WeightSynchronizer:
     return PushFuture(last_event, programs)
 
 
-def export_destinations(dest: Dict[Tuple[int, int], torch.Tensor]) -> Dict:
-  """Picklable CUDA-IPC descriptors of destination tensors (sampler side)."""
-  from torch.multiprocessing.reductions import reduce_tensor
-  return {k: reduce_tensor(t) for k, t in dest.items()}
+class PeerBuffer:
+  """Another process's device memory, mapped for kernels on `kernel_device`.
+
+  Exposes what the reshard path reads from a destination: data_ptr(),
+  device (the GPU that holds the memory), dtype and shape.
+  """
+
+  def __init__(self, ptr: int, device_index: int, dtype: torch.dtype, shape):
+    self._ptr = ptr
+    self.device = torch.device("cuda", device_index)
+    self.dtype = dtype
+    self.shape = tuple(shape)
+
+  def data_ptr(self) -> int:
+    return self._ptr
 
 
-def import_destinations(desc: Dict) -> Dict[Tuple[int, int], torch.Tensor]:
-  """Maps exported destination tensors into this process (trainer side)."""
+# (kernel device, handle bytes) -> mapped base address; a handle may be opened
+# once per device per process, and several tensors can share one allocation.
+_IPC_BASES: Dict[Tuple[int, bytes], int] = {}
+
+
+def export_destinations(dest: Dict[Any, torch.Tensor]) -> Dict:
+  """Picklable CUDA-IPC descriptors of destination tensors (sampler side).
+
+  The tensors must stay alive until every importer has finished with them.
+  """
   out = {}
-  for k, (fn, args) in desc.items():
-    out[k] = fn(*args)
+  for k, t in dest.items():
+    if not t.is_cuda or not t.is_contiguous():
+      raise ValueError("destinations must be contiguous CUDA tensors")
+    info = t.untyped_storage()._share_cuda_()
+    device_index, handle, _size, storage_offset = info[0], info[1], info[2], info[3]
+    offset = storage_offset + t.storage_offset() * t.element_size()
+    out[k] = (int(device_index), bytes(handle), int(offset), t.dtype, tuple(t.shape))
   return out
+
+
+def import_destinations(desc: Dict, kernel_device: Optional[int] = None) -> Dict[Any, PeerBuffer]:
+  """Maps exported destinations for kernels on `kernel_device` (trainer side).
+
+  The IPC handle is opened with the kernel's device current (lazy peer
+  access), which is what lets that device's kernels store into the peer's
+  memory; a mapping opened under the peer's own device would not be visible
+  to them.
+  """
+  dev = torch.cuda.current_device() if kernel_device is None else int(kernel_device)
+  out = {}
+  for k, (peer_dev, handle, offset, dtype, shape) in desc.items():
+    key = (dev, handle)
+    if key not in _IPC_BASES:
+      base = ctypes.c_void_p()
+      _native.check(_native.lib().ts_ipc_open(dev, handle, ctypes.byref(base)), "ipc open: ")
+      _IPC_BASES[key] = base.value
+    out[k] = PeerBuffer(_IPC_BASES[key] + offset, peer_dev, dtype, shape)
+  return out
+
+
+def close_imports(kernel_device: Optional[int] = None) -> None:
+  """Unmaps every destination imported for `kernel_device` (all if None)."""
+  for (dev, handle), base in list(_IPC_BASES.items()):
+    if kernel_device is None or dev == kernel_device:
+      _native.lib().ts_ipc_close(dev, ctypes.c_void_p(base))
+      del _IPC_BASES[(dev, handle)]
