@@ -190,6 +190,10 @@ TS_API int ts_enable_peer_access(int device, int peer);
  * the reference's cross-host transfers on one NVSwitch box.  A handle may be
  * opened once per device per process; ts_ipc_close unmaps it. */
 TS_API int ts_ipc_open(int device, const void* handle_bytes, void** base_out);
+/* The exporting side: the 64-byte handle of the allocation holding dev_ptr and
+ * dev_ptr's byte offset inside it (cudaMalloc'ed memory, e.g. torch's default
+ * caching allocator; not virtual-memory-mapped segments). */
+TS_API int ts_ipc_export(const void* dev_ptr, void* handle_out, uint64_t* offset_out);
 TS_API int ts_ipc_close(int device, void* base);
 
 /* ------------------------------------------------------------------------ */

@@ -111,6 +111,7 @@ _SIGS = {
     "ts_enable_peer_access": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
     "ts_ipc_open": (ctypes.c_int, [ctypes.c_int, ctypes.c_char_p, ctypes.POINTER(_V)]),
     "ts_ipc_close": (ctypes.c_int, [ctypes.c_int, _V]),
+    "ts_ipc_export": (ctypes.c_int, [_V, ctypes.c_char_p, c_u64_p]),
     "ts_kv_relayout": (ctypes.c_int, [ctypes.c_int, _V, _V, ctypes.c_int,
                                       PageGeometry, PageGeometry, _V, ctypes.c_int64,
                                       _V, ctypes.c_int64, ctypes.c_int64,

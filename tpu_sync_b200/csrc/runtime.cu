@@ -5,6 +5,7 @@
 // order, codes and messages; ts_coalesce_runs restates CoalesceMajorDimCopies
 // (tpu_sync/kv_cache/kv_cache_manager_base.cc:121-141).
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdarg>
@@ -143,5 +144,38 @@ extern "C" int ts_ipc_close(int device, void* base) {
   tsb::clear_error();
   tsb::DeviceGuard g(device);
   TS_CUDA_RET(cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle");
+  return TS_OK;
+}
+
+extern "C" int ts_ipc_export(const void* dev_ptr, void* handle_out, uint64_t* offset_out) {
+  tsb::clear_error();
+  if (!dev_ptr || !handle_out || !offset_out)
+    return tsb::set_error(TS_INVALID_ARGUMENT, "null pointer argument");
+  // Allocation base through the driver entry point (no link-time libcuda).
+  using AddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static AddressRangeFn range_fn = nullptr;
+  if (range_fn == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    TS_CUDA_RET(cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q),
+                "driver entry point");
+    if (q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return tsb::set_error(TS_UNAVAILABLE, "cuMemGetAddressRange is not available");
+    range_fn = reinterpret_cast<AddressRangeFn>(fn);
+  }
+  cudaPointerAttributes attr;
+  TS_CUDA_RET(cudaPointerGetAttributes(&attr, dev_ptr), "pointer attributes");
+  if (attr.type != cudaMemoryTypeDevice)
+    return tsb::set_error(TS_INVALID_ARGUMENT, "ipc export needs device memory");
+  tsb::DeviceGuard g(attr.device);
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  const CUresult r = range_fn(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr));
+  if (r != CUDA_SUCCESS)
+    return tsb::set_errorf(TS_INTERNAL, "cuMemGetAddressRange failed (%d)", int(r));
+  cudaIpcMemHandle_t h;
+  TS_CUDA_RET(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)), "cudaIpcGetMemHandle");
+  std::memcpy(handle_out, &h, sizeof(h));
+  *offset_out = uint64_t(reinterpret_cast<uintptr_t>(dev_ptr) - uintptr_t(base));
   return TS_OK;
 }

@@ -230,16 +230,19 @@ _IPC_BASES: Dict[Tuple[int, bytes], int] = {}
 def export_destinations(dest: Dict[Any, torch.Tensor]) -> Dict:
   """Picklable CUDA-IPC descriptors of destination tensors (sampler side).
 
-  The tensors must stay alive until every importer has finished with them.
+  Each descriptor is (device, 64-byte cudaIpcMemHandle of the allocation,
+  byte offset, dtype, shape).  The tensors must stay alive until every
+  importer has finished with them.
   """
   out = {}
   for k, t in dest.items():
     if not t.is_cuda or not t.is_contiguous():
       raise ValueError("destinations must be contiguous CUDA tensors")
-    info = t.untyped_storage()._share_cuda_()
-    device_index, handle, _size, storage_offset = info[0], info[1], info[2], info[3]
-    offset = storage_offset + t.storage_offset() * t.element_size()
-    out[k] = (int(device_index), bytes(handle), int(offset), t.dtype, tuple(t.shape))
+    handle = ctypes.create_string_buffer(64)
+    offset = ctypes.c_uint64()
+    _native.check(_native.lib().ts_ipc_export(ctypes.c_void_p(t.data_ptr()), handle,
+                                              ctypes.byref(offset)), "ipc export: ")
+    out[k] = (t.device.index, handle.raw, int(offset.value), t.dtype, tuple(t.shape))
   return out
 
 
