@@ -436,7 +436,7 @@ def run_ours(args):
 
   # Host tier: as large as requested, bounded by this box's RAM share.
   pitch = g.block_bytes
-  want_host = args.host_blocks or 8192
+  want_host = args.host_blocks or 32768
   local_ranks = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
   fit = int(0.45 * mem_available_bytes() / max(local_ranks, 1) // pitch)
   host_blocks = max(4 * B, min(want_host, fit))
@@ -444,17 +444,33 @@ def run_ours(args):
 
   pcie = measure_pcie(torch, device)
 
-  # Step plans: offload from the first half of the pool into the first half
-  # of the host tier; reload from the second half of the tier into the second
-  # half of the pool (disjoint sets, as evicted and admitted blocks are).
-  rng = np.random.default_rng(100 + rank)
-  half_pool, half_host = pool_blocks // 2, host_blocks // 2
+  # Step plans from the C1 access trace: 100k accesses Zipf(1.1) over 200k
+  # prefix ids run through the tier-2 store (LRU index + host block
+  # allocator with the reference's policies) over this host tier; its save
+  # (offload) and load (reload) streams are cut into 512-block batches and a
+  # step pairs one of each, taken from the second half of the trace (tier
+  # full, evicting).  Device ids: offloads read the first half of the pool,
+  # reloads write the second half (disjoint, as evicted and admitted blocks
+  # are).
+  trace = workloads.zipf_trace(seed=10 + rank)
+  saves, loads, trace_stats = workloads.store_transfer_streams(trace, host_blocks, pool_blocks, B)
+  half_pool = pool_blocks // 2
+  n_steps = args.warmup + args.steps
+  s0, l0 = len(saves) // 2, len(loads) // 2
+  if s0 + n_steps * B > len(saves):
+    s0 = max(0, len(saves) - n_steps * B)
+  if l0 + n_steps * B > len(loads):
+    l0 = max(0, len(loads) - n_steps * B)
   plans = []
-  for _ in range(args.warmup + args.steps):
-    plans.append((rng.choice(half_pool, B, replace=False),
-                  rng.choice(half_host, B, replace=False),
-                  half_host + rng.choice(host_blocks - half_host, B, replace=False),
-                  half_pool + rng.choice(pool_blocks - half_pool, B, replace=False)))
+  for i in range(n_steps):
+    sv = saves[s0 + i * B:s0 + (i + 1) * B]
+    ld = loads[l0 + i * B:l0 + (i + 1) * B]
+    if len(sv) < B or len(ld) < B:
+      raise RuntimeError("access trace too short for the requested steps")
+    plans.append((np.array([d % half_pool for d, _ in sv], np.int64),
+                  np.array([h for _, h in sv], np.int64),
+                  np.array([h for h, _ in ld], np.int64),
+                  np.array([half_pool + d % half_pool for _, d in ld], np.int64)))
   step_bytes = 2 * B * pitch
   bench_stream = torch.cuda.Stream(device)
 
@@ -559,7 +575,11 @@ def run_ours(args):
             "pool_blocks": pool_blocks, "pool_gib": round(full.numel() * 2 / GIB, 1),
             "host_tier_blocks": host_blocks,
             "host_tier_gib": round(host_blocks * pitch / GIB, 1),
-            "batch": B, "l2": "inputs larger than L2 (1 GiB of random blocks per direction per step)",
+            "batch": B, "l2": "inputs larger than L2 (1 GiB of scattered blocks per direction per step)",
+            "trace": ("100k accesses Zipf(1.1) over 200k prefix ids (seed 10+rank) through the "
+                      "tier-2 store (reference LRU + host block allocator); steady-state "
+                      "512-block offload and reload batches"),
+            "trace_hit_rate": trace_stats["hit_rate"],
             "parallelism": f"replicas x{world}"},
         "per_gpu_gbs": round(value / world, 3),
         "pcie": {"offload_d2h_gbs": round(d2h_gbs, 2), "reload_h2d_gbs": round(d2h_gbs, 2),

@@ -330,6 +330,87 @@ TS_API int ts_event_stream_wait(ts_event* ev, void* stream);
 TS_API int ts_event_elapsed_ms(ts_event* ev, float* ms);
 TS_API void ts_event_release(ts_event* ev);
 
+/* ------------------------------------------------------------------------ */
+/* Tier-2 prefix cache (KVCacheStore, local paths).                          */
+/* ------------------------------------------------------------------------ */
+
+/* BlockStatus of tpu_sync/kv_cache/kv_cache_store_backend.h:39-45. */
+enum {
+  TS_BLOCK_INIT = 0,
+  TS_BLOCK_REMOTE = 1,
+  TS_BLOCK_HBM = 2,
+  TS_BLOCK_HOST = 3,
+  TS_BLOCK_HOST_AND_HBM = 4
+};
+
+/* RaidenBlockId without the RaidenId strings (local blocks only). */
+typedef struct ts_block_info {
+  int32_t host_block_id;
+  int32_t device_block_id;
+  int32_t status;
+  int32_t pad_;
+} ts_block_info;
+
+typedef struct ts_store ts_store;
+
+/* Block hashes are byte strings packed back to back in `keys`, key i being
+ * keys[offs[i] .. offs[i+1]).  The store's Save / Load move bytes through
+ * `mgr` (ts_d2h / ts_h2d); with mgr == NULL transfers complete at once
+ * (host-only state machine).  capacity = LRU entries; host_blocks = host
+ * tier blocks the allocator hands out.
+ * Replaces KVCacheStore + HostOffloadBackend + LRUCache + LogicalBlockManager
+ * local paths: tpu_sync/kv_cache/kv_cache_store.h:100-808,
+ * tpu_sync/kv_cache/host_offload_backend.cc:154-470,
+ * tpu_sync/kv_cache/lru_cache.h:41-364,
+ * tpu_sync/kv_cache/logical_block_manager.cc:32-224. */
+TS_API int ts_store_create(ts_manager* mgr, int64_t capacity, int64_t host_blocks,
+                           ts_store** out);
+TS_API int ts_store_destroy(ts_store* store);
+/* KVCacheStore::Lookup (kv_cache_store.cc:837-904): hits up to the first miss,
+ * pinned when pin_found != 0. */
+TS_API int ts_store_lookup(ts_store* store, const uint8_t* keys, const int64_t* offs,
+                           int64_t n, int pin_found, ts_block_info* out,
+                           int64_t* n_found);
+/* KVCacheStore::Insert (kv_cache_store.cc:906-939), all-or-nothing, pins. */
+TS_API int ts_store_insert(ts_store* store, const uint8_t* keys, const int64_t* offs,
+                           int64_t n, const ts_block_info* slices, int64_t n_slices,
+                           int on_host);
+TS_API int ts_store_release(ts_store* store, const uint8_t* keys, const int64_t* offs,
+                            int64_t n);
+TS_API int ts_store_pin_count(ts_store* store, const uint8_t* key, int64_t len, int* out);
+/* KVCacheStore::SaveLocal (kv_cache_store.cc:977-1058): HBM -> host tier. */
+TS_API int ts_store_save(ts_store* store, const uint8_t* keys, const int64_t* offs,
+                         int64_t n, void* stream);
+/* KVCacheStore::Load (kv_cache_store.cc:1060-1140): host tier -> HBM. */
+TS_API int ts_store_load(ts_store* store, const uint8_t* keys, const int64_t* offs,
+                         int64_t n, const int32_t* device_block_ids, int64_t n_ids,
+                         void* stream);
+/* PollSaveStatus (which = 0: done, failed, pending, existing, unregistered) /
+ * PollLoadStatus (which = 1: done, failed, pending), kv_cache_store.cc:1453-1521.
+ * counts[] receives the list sizes, the keys are packed into buf / offs.
+ * TS_RESOURCE_EXHAUSTED (nothing consumed) when buf_len < *need_bytes or
+ * offs_len < *need_keys + 1. */
+TS_API int ts_store_poll(ts_store* store, int which, int64_t* counts, uint8_t* buf,
+                         int64_t buf_len, int64_t* offs, int64_t offs_len,
+                         int64_t* need_bytes, int64_t* need_keys);
+/* capacity, size, available space, host blocks total, free, locked. */
+TS_API int ts_store_stats(ts_store* store, int64_t* stats6);
+/* Test hooks: LRU order (which 0 = active MRU-first, 1 = candidates,
+ * 2 = GetEvictableKeys order) and direct allocator operations
+ * (op 0 deallocate, 1 allocate_target, 2 unlock, 3 access one id). */
+TS_API int ts_store_lru_order(ts_store* store, int which, uint8_t* buf, int64_t buf_len,
+                              int64_t* offs, int64_t offs_len, int64_t* need_bytes,
+                              int64_t* need_keys);
+TS_API int ts_store_allocate_host_blocks(ts_store* store, int n, int lock, int32_t* out);
+TS_API int ts_store_host_block_op(ts_store* store, int op, const int32_t* ids, int64_t n);
+/* Test hook: one raw operation on the LRU index (0 put, 1 pin, 2 unpin,
+ * 3 peek, 4 peek including candidates, 5 pin count, 6 erase, 7 contains,
+ * 8 available space, 9 size); put reports a demoted key in out_key. */
+TS_API int ts_store_lru_op(ts_store* store, int op, const uint8_t* key, int64_t len,
+                           const ts_block_info* in, ts_block_info* out_info,
+                           int64_t* out_val, uint8_t* out_key, int64_t out_key_cap,
+                           int64_t* out_key_len);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

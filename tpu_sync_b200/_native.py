@@ -81,6 +81,11 @@ class ManagerOpts(ctypes.Structure):
               ("copy_streams", ctypes.c_int32), ("max_ctas", ctypes.c_int32)]
 
 
+class BlockInfo(ctypes.Structure):
+  _fields_ = [("host_block_id", ctypes.c_int32), ("device_block_id", ctypes.c_int32),
+              ("status", ctypes.c_int32), ("pad_", ctypes.c_int32)]
+
+
 # name -> (restype, argtypes); every symbol declared in include/tpusync_b200.h
 _V = ctypes.c_void_p
 _SIGS = {
@@ -139,6 +144,28 @@ _SIGS = {
     "ts_mgr_set_profiling": (ctypes.c_int, [_V, ctypes.c_int]),
     "ts_mgr_kernel_stats": (ctypes.c_int, [_V, ctypes.c_int, c_i64_p,
                                            ctypes.POINTER(ctypes.c_double), c_u64_p]),
+    "ts_store_create": (ctypes.c_int, [_V, ctypes.c_int64, ctypes.c_int64, ctypes.POINTER(_V)]),
+    "ts_store_destroy": (ctypes.c_int, [_V]),
+    "ts_store_lookup": (ctypes.c_int, [_V, ctypes.c_char_p, c_i64_p, ctypes.c_int64, ctypes.c_int,
+                                       ctypes.POINTER(BlockInfo), c_i64_p]),
+    "ts_store_insert": (ctypes.c_int, [_V, ctypes.c_char_p, c_i64_p, ctypes.c_int64,
+                                       ctypes.POINTER(BlockInfo), ctypes.c_int64, ctypes.c_int]),
+    "ts_store_release": (ctypes.c_int, [_V, ctypes.c_char_p, c_i64_p, ctypes.c_int64]),
+    "ts_store_pin_count": (ctypes.c_int, [_V, ctypes.c_char_p, ctypes.c_int64,
+                                          ctypes.POINTER(ctypes.c_int)]),
+    "ts_store_save": (ctypes.c_int, [_V, ctypes.c_char_p, c_i64_p, ctypes.c_int64, _V]),
+    "ts_store_load": (ctypes.c_int, [_V, ctypes.c_char_p, c_i64_p, ctypes.c_int64, c_i32_p,
+                                     ctypes.c_int64, _V]),
+    "ts_store_poll": (ctypes.c_int, [_V, ctypes.c_int, c_i64_p, ctypes.c_char_p, ctypes.c_int64,
+                                     c_i64_p, ctypes.c_int64, c_i64_p, c_i64_p]),
+    "ts_store_stats": (ctypes.c_int, [_V, c_i64_p]),
+    "ts_store_lru_order": (ctypes.c_int, [_V, ctypes.c_int, ctypes.c_char_p, ctypes.c_int64,
+                                          c_i64_p, ctypes.c_int64, c_i64_p, c_i64_p]),
+    "ts_store_allocate_host_blocks": (ctypes.c_int, [_V, ctypes.c_int, ctypes.c_int, c_i32_p]),
+    "ts_store_host_block_op": (ctypes.c_int, [_V, ctypes.c_int, c_i32_p, ctypes.c_int64]),
+    "ts_store_lru_op": (ctypes.c_int, [_V, ctypes.c_int, ctypes.c_char_p, ctypes.c_int64,
+                                       ctypes.POINTER(BlockInfo), ctypes.POINTER(BlockInfo),
+                                       c_i64_p, ctypes.c_char_p, ctypes.c_int64, c_i64_p]),
     "ts_event_query": (ctypes.c_int, [_V]),
     "ts_event_wait": (ctypes.c_int, [_V, ctypes.c_int64]),
     "ts_event_error": (ctypes.c_int, [_V, ctypes.c_char_p, ctypes.c_size_t]),

@@ -15,9 +15,12 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <cerrno>
 #include <cstring>
 #include <string>
+#include <thread>
+#include <vector>
 
 #include "ts_internal.h"
 
@@ -65,6 +68,23 @@ struct ts_host_tier {
 using tsb::set_error;
 using tsb::set_errorf;
 
+namespace {
+// Zero-fills a large pinned range with several threads (first touch of many
+// GiB is otherwise single-core bound).
+void parallel_zero(uint8_t* p, uint64_t n) {
+  const unsigned hw = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+  const uint64_t per = ((n / hw) + 4095) & ~uint64_t(4095);
+  std::vector<std::thread> ts;
+  for (unsigned i = 0; i < hw; ++i) {
+    const uint64_t a = uint64_t(i) * per;
+    if (a >= n) break;
+    const uint64_t b = std::min(n, a + per);
+    ts.emplace_back([p, a, b] { std::memset(p + a, 0, b - a); });
+  }
+  for (auto& t : ts) t.join();
+}
+}  // namespace
+
 extern "C" int ts_host_tier_create(uint64_t bytes, const char* shm_name,
                                    const char* model_uid, uint64_t geometry_tag,
                                    int register_with_cuda, ts_host_tier** out,
@@ -87,7 +107,7 @@ extern "C" int ts_host_tier_create(uint64_t bytes, const char* shm_name,
         delete t;
         return tsb::cuda_error(e, "cudaHostAlloc of the host tier");
       }
-      std::memset(p, 0, payload);
+      parallel_zero(static_cast<uint8_t*>(p), payload);
       t->payload = static_cast<uint8_t*>(p);
       t->cuda_alloc = true;
     }

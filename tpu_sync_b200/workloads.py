@@ -134,3 +134,73 @@ def mesh_for(shape, split: str, n: int) -> Tuple[int, ...]:
   if split == "row":
     return (1, n) + (1,) * (len(shape) - 2)
   return (1,) * len(shape)
+
+
+# ---------------------------------------------------------------------------
+# C1 access trace driving the tier-2 store
+# ---------------------------------------------------------------------------
+
+def zipf_trace(n_access: int = 100_000, n_ids: int = 200_000, s: float = 1.1,
+               seed: int = 10) -> np.ndarray:
+  """n_access block accesses drawn Zipf(s) over n_ids prefix ids.
+
+  Rank r (1-based) has probability proportional to r^-s; ranks map to ids
+  through a seeded permutation, so popularity is not correlated with id.
+  """
+  rng = np.random.default_rng(seed)
+  p = np.arange(1, n_ids + 1, dtype=np.float64) ** (-s)
+  p /= p.sum()
+  ranks = rng.choice(n_ids, size=n_access, p=p)
+  return rng.permutation(n_ids)[ranks].astype(np.int64)
+
+
+def store_transfer_streams(trace: np.ndarray, host_blocks: int, device_blocks: int,
+                           batch: int = 512):
+  """Runs the access trace through a host-only KVCacheStore.
+
+  Every access gets a device block (a ring over the HBM pool); a hit is
+  looked up and loaded into it, a miss is inserted from it and saved.  The
+  store's LRU and host block allocator (the reference's policies) choose the
+  host ids.  Returns (saves, loads, stats): saves = [(device id, host id)],
+  loads = [(host id, device id)] in issue order.
+  """
+  from tpu_sync_b200.kv_cache_store import BlockStatus, KVCacheStore, RaidenBlockId
+  store = KVCacheStore(capacity=host_blocks, host_blocks=host_blocks)
+  saves, loads = [], []
+  ring = 0
+  hits = misses = 0
+  for b0 in range(0, len(trace), batch):
+    seen, hit_h, hit_dev, miss_h, miss_dev = set(), [], [], [], []
+    for x in trace[b0:b0 + batch]:
+      h = int(x).to_bytes(8, "little")
+      if h in seen:
+        continue
+      seen.add(h)
+      d = ring % device_blocks
+      ring += 1
+      r = store.lookup([h])
+      if r:
+        hit_h.append(h)
+        hit_dev.append(d)
+        loads.append((r[0][1].host_block_id, d))
+      else:
+        miss_h.append(h)
+        miss_dev.append(d)
+    hits += len(hit_h)
+    misses += len(miss_h)
+    if hit_h:
+      store.load(hit_h, hit_dev)
+    if miss_h and store.insert(miss_h, [RaidenBlockId(device_block_id=d, status=BlockStatus.HBM)
+                                        for d in miss_dev]):
+      if store.save(miss_h):
+        store.poll_save_status()
+        for h, d in zip(miss_h, miss_dev):
+          saves.append((d, store.lookup([h], pin_found=False)[0][1].host_block_id))
+      else:
+        store.release(miss_h)
+    store.poll_load_status()
+    store.poll_save_status()
+  stats = {"accesses": int(len(trace)), "hits": hits, "misses": misses,
+           "hit_rate": round(hits / max(hits + misses, 1), 4)}
+  store.close()
+  return saves, loads, stats
