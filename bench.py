@@ -150,48 +150,69 @@ class ClockSampler:
 # CPU arms (oracle restatement of the reference host loops)
 # ---------------------------------------------------------------------------
 
-def cpu_offload_reload(batch: int, seconds: float, steps: int = 0, warmup: int = 0):
-  """Times the reference host loops (restated in C) for offload + reload of
-  `batch` C1 blocks between a host "device" pool and a host tier."""
+def c1_plans(rank: int, host_blocks: int, pool_blocks: int, batch: int, n_steps: int):
+  """Step plans of the C1 trace (see run_ours): per step (offload device ids,
+  offload host ids, reload host ids, reload device ids)."""
+  from tpu_sync_b200 import workloads
+  trace = workloads.zipf_trace(seed=10 + rank)
+  batches, stats = workloads.store_transfer_streams(trace, host_blocks, pool_blocks, batch)
+  half_pool = pool_blocks // 2
+  b0 = min(len(batches) // 2, len(batches) - n_steps)
+  plans = []
+  for sv, ld in batches[b0:b0 + n_steps]:
+    plans.append((np.array([d % half_pool for d, _ in sv], np.int64),
+                  np.array([h for _, h in sv], np.int64),
+                  np.array([h for h, _ in ld], np.int64),
+                  np.array([half_pool + d % half_pool for _, d in ld], np.int64)))
+  return plans, stats
+
+
+def cpu_offload_reload(plans, seconds: float, steps: int = 0, warmup: int = 0):
+  """Times the reference host loops (restated in C) on the C1 step plans.
+
+  The reference's CPU client keeps its "device" buffers in host memory, so a
+  host-resident pool stands in for HBM; block ids are folded into a
+  2048-block pool and a 2048-block host tier (every copy stays a 32 KiB run
+  per storage, as in the real layout).
+  """
   from oracle import cpu_ref
   from tpu_sync_b200 import workloads
   g = workloads.C1
   S, bb = g.storages, g.storage_block_bytes
-  pool_blocks = max(2 * batch, 256)
+  nb = 2048
   threads = cpu_ref.host_threads()
-  rng = np.random.default_rng(10)
-  dev = [np.empty(pool_blocks * bb, np.uint8) for _ in range(S)]
-  host = [np.empty(pool_blocks * bb, np.uint8) for _ in range(S)]
+  dev = [np.empty(nb * bb, np.uint8) for _ in range(S)]
+  host = [np.empty(nb * bb, np.uint8) for _ in range(S)]
   for a in dev + host:
     a.fill(1)
-  half = pool_blocks // 2
+  folded = [tuple(np.asarray(x) % nb for x in p) for p in plans]
 
-  def one_step():
-    src = np.sort(rng.choice(half, batch, replace=False))
-    dst = rng.choice(pool_blocks, batch, replace=False)
-    ones = np.ones(batch, np.int64)
-    cpu_ref.copy_runs(host, dev, [bb] * S, src, dst, ones, threads)      # D2H
-    hs = rng.choice(pool_blocks, batch, replace=False)
-    ds = half + rng.choice(pool_blocks - half, batch, replace=False)
-    cpu_ref.copy_runs(dev, host, [bb] * S, hs, ds, ones, threads)        # H2D
+  def one_step(p):
+    ones_s = np.ones(len(p[0]), np.int64)
+    ones_l = np.ones(len(p[2]), np.int64)
+    cpu_ref.copy_runs(host, dev, [bb] * S, p[0], p[1], ones_s, threads)   # D2H
+    cpu_ref.copy_runs(dev, host, [bb] * S, p[2], p[3], ones_l, threads)   # H2D
 
-  for _ in range(warmup):
-    one_step()
-  times = []
+  for i in range(warmup):
+    one_step(folded[i % len(folded)])
+  times, moved = [], 0
   t_end = time.perf_counter() + seconds
+  i = 0
   while (steps and len(times) < steps) or (not steps and (time.perf_counter() < t_end or
                                                           len(times) < 2)):
+    p = folded[(warmup + i) % len(folded)]
     t0 = time.perf_counter()
-    one_step()
+    one_step(p)
     times.append(time.perf_counter() - t0)
-  step_bytes = 2 * batch * g.block_bytes
-  per_step = statistics.mean(times)
-  return {"value": round(step_bytes / per_step / 1e9, 3), "unit": "GB/s", "cores": threads,
-          "ms_per_step": per_step * 1e3, "steps": len(times),
-          "sample": (f"offload {batch} + reload {batch} C1 blocks (2 MiB each) per step "
-                     f"between a {pool_blocks}-block host-resident pool and host tier, "
-                     f"{len(times)} steps, memcpy per (storage, run) as "
-                     f"DispatchD2hWork/DispatchH2dWork on the CPU client"),
+    moved += (len(p[0]) + len(p[2])) * g.block_bytes
+    i += 1
+  total = sum(times)
+  return {"value": round(moved / total / 1e9, 3), "unit": "GB/s", "cores": threads,
+          "ms_per_step": total / len(times) * 1e3, "steps": len(times),
+          "sample": (f"{len(times)} steps of the C1 trace plans (offloads + reloads of one "
+                     f"512-access batch each, 2 MiB blocks) between a {nb}-block "
+                     f"host-resident pool and a {nb}-block host tier, memcpy per (storage, "
+                     f"run) as DispatchD2hWork/DispatchH2dWork on the CPU client"),
           "cpu": cpu_model()}
 
 
@@ -199,7 +220,8 @@ def run_reference(args):
   rank = int(os.environ.get("RANK", "0"))
   if rank != 0:
     return
-  r = cpu_offload_reload(args.batch, 0.0, steps=args.steps, warmup=args.warmup)
+  plans, _ = c1_plans(0, 32768, args.pool_blocks, args.batch, args.warmup + args.steps)
+  r = cpu_offload_reload(plans, 0.0, steps=args.steps, warmup=args.warmup)
   line = {"impl": "reference", "metric": METRIC, "value": r["value"], "unit": "GB/s",
           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
           "ms_per_step": round(r["ms_per_step"], 3), "higher_is_better": True,
@@ -445,33 +467,14 @@ def run_ours(args):
   pcie = measure_pcie(torch, device)
 
   # Step plans from the C1 access trace: 100k accesses Zipf(1.1) over 200k
-  # prefix ids run through the tier-2 store (LRU index + host block
-  # allocator with the reference's policies) over this host tier; its save
-  # (offload) and load (reload) streams are cut into 512-block batches and a
-  # step pairs one of each, taken from the second half of the trace (tier
-  # full, evicting).  Device ids: offloads read the first half of the pool,
-  # reloads write the second half (disjoint, as evicted and admitted blocks
-  # are).
-  trace = workloads.zipf_trace(seed=10 + rank)
-  saves, loads, trace_stats = workloads.store_transfer_streams(trace, host_blocks, pool_blocks, B)
-  half_pool = pool_blocks // 2
-  n_steps = args.warmup + args.steps
-  s0, l0 = len(saves) // 2, len(loads) // 2
-  if s0 + n_steps * B > len(saves):
-    s0 = max(0, len(saves) - n_steps * B)
-  if l0 + n_steps * B > len(loads):
-    l0 = max(0, len(loads) - n_steps * B)
-  plans = []
-  for i in range(n_steps):
-    sv = saves[s0 + i * B:s0 + (i + 1) * B]
-    ld = loads[l0 + i * B:l0 + (i + 1) * B]
-    if len(sv) < B or len(ld) < B:
-      raise RuntimeError("access trace too short for the requested steps")
-    plans.append((np.array([d % half_pool for d, _ in sv], np.int64),
-                  np.array([h for _, h in sv], np.int64),
-                  np.array([h for h, _ in ld], np.int64),
-                  np.array([half_pool + d % half_pool for _, d in ld], np.int64)))
-  step_bytes = 2 * B * pitch
+  # prefix ids, in batches of 512, run through the tier-2 store (LRU index +
+  # host block allocator with the reference's policies) over this host tier.
+  # A step moves what one access batch needs: its misses offloaded (saved)
+  # and its hits reloaded, both directions in flight; steps follow the trace
+  # from its middle (tier full, evicting).  Device ids: offloads read the
+  # first half of the pool, reloads write the second half.
+  plans, trace_stats = c1_plans(rank, host_blocks, pool_blocks, B, args.warmup + args.steps)
+  plan_bytes = [(len(p[0]) + len(p[2])) * pitch for p in plans]
   bench_stream = torch.cuda.Stream(device)
 
   def step(plan, stream):
@@ -510,7 +513,10 @@ def run_ours(args):
   ins = mgr.kernel_stats("insert")
   max_ms = max_over_ranks(dev_ms)
   ms_per_step = max_ms / args.steps
-  value = world * step_bytes * args.steps / (max_ms * 1e-3) / 1e9
+  timed_bytes = sum(plan_bytes[args.warmup:])
+  timed_d2h = sum(len(p[0]) for p in plans[args.warmup:]) * pitch
+  timed_h2d = sum(len(p[2]) for p in plans[args.warmup:]) * pitch
+  value = world * timed_bytes / (max_ms * 1e-3) / 1e9
 
   # ---- standalone extract of a whole batch in one launch (HBM GB/s) ----
   table = ops.StorageTable(storages)
@@ -543,8 +549,7 @@ def run_ours(args):
     b.Await()
   wall = time.perf_counter() - t0
   wall = max_over_ranks(wall)
-  e2e_value = world * step_bytes * args.steps / wall / 1e9
-  idx_bytes = 2 * 2 * B * 8  # two int64 lists per direction
+  e2e_value = world * timed_bytes / wall / 1e9
 
   # ---- roofline of the dominant kernel (extract) ----
   pk = peaks()
@@ -558,9 +563,10 @@ def run_ours(args):
   # ---- CPU baseline (rank 0, N=1) ----
   cpu = None
   if rank == 0 and world == 1 and not args.no_cpu_baseline:
-    cpu = cpu_offload_reload(B, args.cpu_sample_s)
+    cpu = cpu_offload_reload(plans, args.cpu_sample_s)
 
-  d2h_gbs = B * pitch / (ms_per_step * 1e-3) / 1e9
+  d2h_gbs = timed_d2h / (max_ms * 1e-3) / 1e9
+  h2d_gbs = timed_h2d / (max_ms * 1e-3) / 1e9
   line = None
   if rank == 0:
     line = {
@@ -570,23 +576,28 @@ def run_ours(args):
         "data": "synthetic N(0,1) bf16 KV pool generated on device (seed 10+rank)",
         "config": {
             "workload": ("C1 Llama-3-8B KV tier: 32 layers x K/V, 16-token blocks of "
-                         "8 heads x 128 bf16 (2 MiB per block), offload 512 + reload 512 "
-                         "blocks per step, both directions in flight"),
+                         "8 heads x 128 bf16 (2 MiB per block); per step the offloads "
+                         "(misses) and reloads (hits) of one 512-access batch of the "
+                         "Zipf trace, both directions in flight"),
+            "blocks_per_step": round(sum(len(p[0]) + len(p[2]) for p in plans[args.warmup:])
+                                     / args.steps, 1),
             "pool_blocks": pool_blocks, "pool_gib": round(full.numel() * 2 / GIB, 1),
             "host_tier_blocks": host_blocks,
             "host_tier_gib": round(host_blocks * pitch / GIB, 1),
-            "batch": B, "l2": "inputs larger than L2 (1 GiB of scattered blocks per direction per step)",
-            "trace": ("100k accesses Zipf(1.1) over 200k prefix ids (seed 10+rank) through the "
-                      "tier-2 store (reference LRU + host block allocator); steady-state "
-                      "512-block offload and reload batches"),
+            "batch": B, "l2": "inputs larger than L2 (~1 GiB of scattered 2 MiB blocks per step)",
+            "trace": ("100k accesses Zipf(1.1) over 200k prefix ids (seed 10+rank), batches "
+                      "of 512, through the tier-2 store (reference LRU + host block "
+                      "allocator); steps from the middle of the trace"),
             "trace_hit_rate": trace_stats["hit_rate"],
             "parallelism": f"replicas x{world}"},
         "per_gpu_gbs": round(value / world, 3),
-        "pcie": {"offload_d2h_gbs": round(d2h_gbs, 2), "reload_h2d_gbs": round(d2h_gbs, 2),
+        "pcie": {"offload_d2h_gbs": round(d2h_gbs, 2), "reload_h2d_gbs": round(h2d_gbs, 2),
                  "measured_peak": pcie, "spec_gbs_per_dir": PCIE_SPEC_GBS,
-                 "frac_of_measured_duplex": round(2 * d2h_gbs / pcie["duplex"], 3)
+                 "frac_of_measured_duplex": round((d2h_gbs + h2d_gbs) / pcie["duplex"], 3)
                  if pcie.get("duplex") else None,
-                 "frac_of_spec": round(d2h_gbs / PCIE_SPEC_GBS, 3)},
+                 "reload_frac_of_measured_h2d": round(h2d_gbs / pcie["h2d"], 3)
+                 if pcie.get("h2d") else None,
+                 "frac_of_spec_busier_dir": round(max(d2h_gbs, h2d_gbs) / PCIE_SPEC_GBS, 3)},
         "roofline": {"bound": "hbm", "kernel": "extract (block_copy_vec_kernel, to staging)",
                      "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 3), "peak_source": peak_src,
@@ -598,8 +609,8 @@ def run_ours(args):
                      if ins["ms"] > 0 else None},
         "extract_hbm_gbs_one_launch": round(extract_one_launch_gbs, 1),
         "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
-                "h2d_bytes_per_step": B * pitch + idx_bytes,
-                "d2h_bytes_per_step": B * pitch,
+                "h2d_bytes_per_step": int(timed_h2d / args.steps),
+                "d2h_bytes_per_step": int(timed_d2h / args.steps),
                 "how": "KVCacheManager.d2h/h2d from Python lists, Await() per step, wall clock"},
         "gpu_launches": ext["launches"] + ins["launches"],
         "clocks": clock_info,

@@ -161,16 +161,20 @@ def store_transfer_streams(trace: np.ndarray, host_blocks: int, device_blocks: i
   Every access gets a device block (a ring over the HBM pool); a hit is
   looked up and loaded into it, a miss is inserted from it and saved.  The
   store's LRU and host block allocator (the reference's policies) choose the
-  host ids.  Returns (saves, loads, stats): saves = [(device id, host id)],
-  loads = [(host id, device id)] in issue order.
+  host ids.  Returns (batches, stats): per access batch, (saves, loads) with
+  saves = [(device id, host id)] and loads = [(host id, device id)].  Within a
+  batch the two lists never share a host block (loaded blocks are pinned, so
+  the save's allocator cannot evict them); a load can depend on an earlier
+  batch's save.
   """
   from tpu_sync_b200.kv_cache_store import BlockStatus, KVCacheStore, RaidenBlockId
   store = KVCacheStore(capacity=host_blocks, host_blocks=host_blocks)
-  saves, loads = [], []
+  batches = []
   ring = 0
   hits = misses = 0
   for b0 in range(0, len(trace), batch):
     seen, hit_h, hit_dev, miss_h, miss_dev = set(), [], [], [], []
+    saves, loads = [], []
     for x in trace[b0:b0 + batch]:
       h = int(x).to_bytes(8, "little")
       if h in seen:
@@ -200,7 +204,8 @@ def store_transfer_streams(trace: np.ndarray, host_blocks: int, device_blocks: i
         store.release(miss_h)
     store.poll_load_status()
     store.poll_save_status()
+    batches.append((saves, loads))
   stats = {"accesses": int(len(trace)), "hits": hits, "misses": misses,
            "hit_rate": round(hits / max(hits + misses, 1), 4)}
   store.close()
-  return saves, loads, stats
+  return batches, stats
