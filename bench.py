@@ -157,9 +157,21 @@ def c1_plans(rank: int, host_blocks: int, pool_blocks: int, batch: int, n_steps:
   trace = workloads.zipf_trace(seed=10 + rank)
   batches, stats = workloads.store_transfer_streams(trace, host_blocks, pool_blocks, batch)
   half_pool = pool_blocks // 2
-  b0 = min(len(batches) // 2, len(batches) - n_steps)
+  # A step gathers consecutive access batches, in trace order, until `batch`
+  # reloads (or offloads) are pending: its offloads and reloads go out
+  # together (a reload that depends on an offload of the same step waits for
+  # it inside the manager).
+  steps, cur_s, cur_l = [], [], []
+  for sv, ld in batches[len(batches) // 2:]:
+    cur_s += sv
+    cur_l += ld
+    if len(cur_l) >= batch or len(cur_s) >= batch:
+      steps.append((cur_s, cur_l))
+      cur_s, cur_l = [], []
+  if len(steps) < n_steps:
+    raise RuntimeError(f"C1 trace yields {len(steps)} steps, {n_steps} requested")
   plans = []
-  for sv, ld in batches[b0:b0 + n_steps]:
+  for sv, ld in steps[:n_steps]:
     plans.append((np.array([d % half_pool for d, _ in sv], np.int64),
                   np.array([h for _, h in sv], np.int64),
                   np.array([h for h, _ in ld], np.int64),
@@ -521,13 +533,15 @@ def run_ours(args):
   # ---- standalone extract of a whole batch in one launch (HBM GB/s) ----
   table = ops.StorageTable(storages)
   staging = table.new_staging(B)
-  big_ids = torch.from_numpy(plans[0][0].astype(np.int64)).to(device)
+  one_rng = np.random.default_rng(7)
+  one_ids = [one_rng.choice(pool_blocks, B, replace=False).astype(np.int64) for _ in range(5)]
+  big_ids = torch.from_numpy(one_ids[0]).to(device)
   for _ in range(3):
     ops.kv_extract(table, big_ids, staging)
   torch.cuda.synchronize(device)
   xs = []
   for i in range(5):
-    ids_i = torch.from_numpy(plans[i % len(plans)][0].astype(np.int64)).to(device)
+    ids_i = torch.from_numpy(one_ids[i]).to(device)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     ops.kv_extract(table, ids_i, staging)
@@ -577,8 +591,9 @@ def run_ours(args):
         "config": {
             "workload": ("C1 Llama-3-8B KV tier: 32 layers x K/V, 16-token blocks of "
                          "8 heads x 128 bf16 (2 MiB per block); per step the offloads "
-                         "(misses) and reloads (hits) of one 512-access batch of the "
-                         "Zipf trace, both directions in flight"),
+                         "(misses) and reloads (hits) of consecutive 512-access batches "
+                         "of the Zipf trace until 512 reloads are pending, both "
+                         "directions in flight"),
             "blocks_per_step": round(sum(len(p[0]) + len(p[2]) for p in plans[args.warmup:])
                                      / args.steps, 1),
             "pool_blocks": pool_blocks, "pool_gib": round(full.numel() * 2 / GIB, 1),

@@ -207,6 +207,34 @@ def test_manager_back_to_back_calls_are_ordered(cuda, mode):
 
 
 @pytest.mark.parametrize("mode", MODES)
+def test_manager_partial_hazards_reorder(cuda, mode):
+  """A reload whose host blocks are partly written by an in-flight offload,
+  and an offload whose device blocks are partly written by an in-flight
+  reload: dependent blocks wait, independent ones do not, result as if
+  the calls ran in program order."""
+  geom = workloads.KVGeometry(layers=2, kv=2, block_tokens=16, heads=4, head_dim=128)
+  pool, mgr, model = make_pair(geom, 256, 128, 13, cuda, chunk_blocks=8, **mode)
+  futs = []
+  for rep in range(3):
+    d_src = list(range(rep * 40, rep * 40 + 40))
+    h_dst = list(range(0, 40))
+    futs.append(mgr.d2h(d_src, h_dst))
+    model.d2h(d_src, h_dst)
+    h_src = list(range(20, 60))          # 20 conflicting + 20 independent
+    d_dst = list(range(200, 240))
+    futs.append(mgr.h2d(h_src, d_dst))
+    model.h2d(h_src, d_dst)
+    d_src2 = list(range(220, 250))       # 20 written by the reload above
+    h_dst2 = list(range(80, 110))
+    futs.append(mgr.d2h(d_src2, h_dst2))
+    model.d2h(d_src2, h_dst2)
+  for f in futs:
+    f.Await()
+  torch.cuda.synchronize()
+  assert_same(pool, mgr, model, range(128))
+
+
+@pytest.mark.parametrize("mode", MODES)
 def test_manager_whole_storage_and_layer_restricted(cuda, mode):
   geom = workloads.KVGeometry(layers=3, kv=1, block_tokens=4, heads=2, head_dim=64)
   pool, mgr, model = make_pair(geom, 16, 16, 2, cuda, **mode)

@@ -37,6 +37,8 @@
 #include <mutex>
 #include <string>
 #include <thread>
+#include <unordered_map>
+#include <unordered_set>
 #include <vector>
 
 #include "ts_internal.h"
@@ -427,24 +429,61 @@ int enqueue_transfer(ts_manager* m, bool to_host, const Plan& p, void* user_stre
   TS_CUDA_RET(cudaHostGetDevicePointer(reinterpret_cast<void**>(&err_dev), ev->err_word, 0),
               "error word mapping");
 
-  // Order after the producer's queued work, and after in-flight calls of the
-  // other direction that touch the same host or device blocks.
+  // Order after the producer's queued work.
   TS_CUDA_RET(cudaEventRecord(m->ev_user, user), "event record");
-  uint64_t need = 0;
-  if (to_host) {
-    for (size_t i = 0; i < p.src.size(); ++i) {
-      need = std::max(need, m->dev_h2d_seq[size_t(p.src[i])]);
-      need = std::max(need, m->host_h2d_seq[size_t(p.dst[i])]);
-    }
-  } else {
-    for (size_t i = 0; i < p.src.size(); ++i) {
-      need = std::max(need, m->host_d2h_seq[size_t(p.src[i])]);
-      need = std::max(need, m->dev_d2h_seq[size_t(p.dst[i])]);
-    }
-  }
-  for (cudaStream_t s : streams) {
+  for (cudaStream_t s : streams)
     TS_CUDA_RET(cudaStreamWaitEvent(s, m->ev_user, 0), "stream wait");
-    int rc = wait_for_call(to_host ? m->h2d_ring : m->d2h_ring, need, s);
+
+  // Cross-direction hazards, per block: the latest in-flight call of the
+  // other direction that wrote what this call reads (or reads what it
+  // writes).  Independent blocks go first; dependent ones follow in order of
+  // the call they wait for, and each chunk waits only for what its own
+  // blocks need, so a few conflicting blocks do not hold back the rest.
+  CallRec* ring = to_host ? m->h2d_ring : m->d2h_ring;
+  const size_t nb = p.src.size();
+  std::vector<uint64_t> need(nb, 0);
+  std::unordered_map<uint64_t, bool> finished;
+  auto still_running = [&](uint64_t seq) {
+    if (seq == 0) return false;
+    auto it = finished.find(seq);
+    if (it != finished.end()) return !it->second;
+    const CallRec& r = ring[seq % kEventRing];
+    const bool done = r.seq != seq || r.done == nullptr || cudaEventQuery(r.done) == cudaSuccess;
+    finished.emplace(seq, done);
+    return !done;
+  };
+  for (size_t i = 0; i < nb; ++i) {
+    const uint64_t a = to_host ? m->dev_h2d_seq[size_t(p.src[i])] : m->host_d2h_seq[size_t(p.src[i])];
+    const uint64_t b = to_host ? m->host_h2d_seq[size_t(p.dst[i])] : m->dev_d2h_seq[size_t(p.dst[i])];
+    const uint64_t x = std::max(still_running(a) ? a : 0, still_running(b) ? b : 0);
+    need[i] = x;
+  }
+  cudaGetLastError();  // cudaEventQuery's "not ready" is not an error
+  std::vector<size_t> order(nb);
+  for (size_t i = 0; i < nb; ++i) order[i] = i;
+  bool dup_dst = false;
+  {
+    std::unordered_set<int64_t> seen;
+    for (int64_t d : p.dst)
+      if (!seen.insert(d).second) { dup_dst = true; break; }
+  }
+  if (!dup_dst)  // reordering is only safe when no destination repeats
+    std::stable_sort(order.begin(), order.end(),
+                     [&](size_t a, size_t b) { return need[a] < need[b]; });
+  uint64_t waited = 0;
+  auto wait_upto = [&](uint64_t seq) -> int {
+    if (seq <= waited) return TS_OK;
+    for (cudaStream_t s : streams) {
+      int rc = wait_for_call(ring, seq, s);
+      if (rc != TS_OK) return rc;
+    }
+    waited = seq;
+    return TS_OK;
+  };
+  if (dup_dst || !p.whole) {
+    uint64_t all = 0;
+    for (uint64_t x : need) all = std::max(all, x);
+    int rc = wait_upto(all);
     if (rc != TS_OK) return rc;
   }
   TS_CUDA_RET(cudaEventRecord(ev->start, ks), "event record");
@@ -456,19 +495,32 @@ int enqueue_transfer(ts_manager* m, bool to_host, const Plan& p, void* user_stre
     return TS_OK;
   }
 
-  const int64_t nblk = int64_t(p.src.size());
-  const std::vector<int64_t>& dev_ids = to_host ? p.src : p.dst;
-  const std::vector<int64_t>& host_ids = to_host ? p.dst : p.src;
+  const int64_t nblk = int64_t(nb);
+  std::vector<int64_t> dev_ids(nb), host_ids(nb);
+  std::vector<uint64_t> need_o(nb);
+  for (size_t k = 0; k < nb; ++k) {
+    const size_t i = order[k];
+    dev_ids[k] = to_host ? p.src[i] : p.dst[i];
+    host_ids[k] = to_host ? p.dst[i] : p.src[i];
+    need_o[k] = need[i];
+  }
+  auto chunk_need = [&](int64_t c0, int64_t cn) {
+    uint64_t x = 0;
+    for (int64_t k = 0; k < cn; ++k) x = std::max(x, need_o[size_t(c0 + k)]);
+    return x;
+  };
   if (direct) {
     for (int64_t c0 = 0; c0 < nblk; c0 += m->chunk_blocks) {
       const int64_t cn = std::min<int64_t>(m->chunk_blocks, nblk - c0);
+      int rc = wait_upto(chunk_need(c0, cn));
+      if (rc != TS_OK) return rc;
       ParamIds ids;
       ids.direct = 1;
       for (int64_t k = 0; k < cn; ++k) {
         ids.v[k] = dev_ids[size_t(c0 + k)];
         ids.s[k] = host_ids[size_t(c0 + k)];
       }
-      int rc = launch_chunk(m, to_host, ids, cn, m->host_dev, err_dev, ks);
+      rc = launch_chunk(m, to_host, ids, cn, m->host_dev, err_dev, ks);
       if (rc != TS_OK) return rc;
     }
     TS_CUDA_RET(cudaEventRecord(ev->done, ks), "event record");
@@ -480,6 +532,8 @@ int enqueue_transfer(ts_manager* m, bool to_host, const Plan& p, void* user_stre
   int chunk = 0;
   for (int64_t c0 = 0; c0 < nblk; c0 += m->chunk_blocks, ++chunk) {
     const int64_t cn = std::min<int64_t>(m->chunk_blocks, nblk - c0);
+    int rc0 = wait_upto(chunk_need(c0, cn));
+    if (rc0 != TS_OK) return rc0;
     Slot& slot = slots[size_t(next)];
     next = (next + 1) % int(slots.size());
     cudaStream_t cc = cs[chunk % m->ncs];
