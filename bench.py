@@ -43,6 +43,9 @@ sys.path.insert(0, str(ROOT))
 METRIC = "KV offload/reload GB/s per GPU vs PCIe peak; extract HBM GB/s; 8B weight-sync s"
 GIB = 1 << 30
 PCIE_SPEC_GBS = 64.0
+# DRAM bytes per 2 MiB block moved by the insert kernel, from
+# profiles/insert_kernel_c1_256blocks.md (None until captured).
+INSERT_TRAFFIC_PER_BLOCK = None
 
 
 def parse():
@@ -565,15 +568,30 @@ def run_ours(args):
   wall = max_over_ranks(wall)
   e2e_value = world * timed_bytes / wall / 1e9
 
-  # ---- roofline of the dominant kernel (extract) ----
+  # ---- roofline of the dominant kernel (by live device time) ----
   pk = peaks()
   hbm_peak = pk.get("hbm_gbs")
   peak_src = "measured (MEASURED_PEAKS.json hbm_gbs)"
   if not hbm_peak:
     hbm_peak, peak_src = 6650.0, "fallback"
-  achieved = ext["bytes"] / (ext["ms"] * 1e-3) / 1e9 if ext["ms"] > 0 else 0.0
-  per_launch_bytes = ext["bytes"] / max(ext["launches"], 1)
-
+  kern = {}
+  for name, st in (("extract", ext), ("insert", ins)):
+    kern[name] = {
+        "kernel": f"block_copy_vec_kernel<{'true' if name == 'extract' else 'false'}> ({name})",
+        "launches": st["launches"], "total_ms": round(st["ms"], 3),
+        "bytes_per_launch": int(st["bytes"] / max(st["launches"], 1)),
+        "avg_launch_us": round(st["ms"] * 1e3 / max(st["launches"], 1), 2),
+        "achieved_gbs": round(st["bytes"] / (st["ms"] * 1e-3) / 1e9, 1) if st["ms"] > 0 else 0.0}
+  tot_ms = sum(k["total_ms"] for k in kern.values()) or 1.0
+  for k in kern.values():
+    k["share"] = round(k["total_ms"] / tot_ms, 3)
+  dom = max(kern, key=lambda n: kern[n]["total_ms"])
+  # DRAM traffic per block from ncu captures of the same kernels on the
+  # small kernel case (profiles/*_kernel_c1_256blocks.md), scaled to this
+  # run's launches by the blocks they move.
+  traffic_per_block = {"extract": 1018413568 / 256, "insert": INSERT_TRAFFIC_PER_BLOCK}
+  blocks_per_launch = kern[dom]["bytes_per_launch"] / (2 * pitch)
+  tpb = traffic_per_block.get(dom)
   # ---- CPU baseline (rank 0, N=1) ----
   cpu = None
   if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -613,15 +631,16 @@ def run_ours(args):
                  "reload_frac_of_measured_h2d": round(h2d_gbs / pcie["h2d"], 3)
                  if pcie.get("h2d") else None,
                  "frac_of_spec_busier_dir": round(max(d2h_gbs, h2d_gbs) / PCIE_SPEC_GBS, 3)},
-        "roofline": {"bound": "hbm", "kernel": "extract (block_copy_vec_kernel, to staging)",
-                     "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-                     "frac": round(achieved / hbm_peak, 3), "peak_source": peak_src,
-                     "launches": ext["launches"],
-                     "bytes_per_launch": int(per_launch_bytes),
-                     "avg_launch_us": round(ext["ms"] * 1e3 / max(ext["launches"], 1), 2),
-                     "traffic": None,
-                     "insert_achieved": round(ins["bytes"] / (ins["ms"] * 1e-3) / 1e9, 1)
-                     if ins["ms"] > 0 else None},
+        "roofline": {"bound": "hbm", "kernel": kern[dom]["kernel"],
+                     "achieved": kern[dom]["achieved_gbs"], "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(kern[dom]["achieved_gbs"] / hbm_peak, 3),
+                     "peak_source": peak_src,
+                     "traffic": int(tpb * blocks_per_launch) if tpb else None,
+                     "traffic_source": "ncu capture of the small kernel case, scaled per block"
+                     if tpb else None,
+                     "note": ("live: launched in 64-block chunks concurrently with the other "
+                              "direction's kernel and the DMAs"),
+                     "kernels": kern},
         "extract_hbm_gbs_one_launch": round(extract_one_launch_gbs, 1),
         "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
                 "h2d_bytes_per_step": int(timed_h2d / args.steps),
