@@ -692,8 +692,8 @@ def run_kernel_case(args):
     if args.kernel_case.startswith("extract"):
       ops.kv_extract(table, ids, staging)
     else:
-      if i == 0:
-        ops.kv_extract(table, ids, staging) if not table.fp8 else None
+      if i == 0:  # fill the staging with real blocks (and fp8 scales)
+        ops.kv_extract(table, ids, staging)
       ops.kv_insert(table, ids, staging)
   torch.cuda.synchronize()
   print(json.dumps({"kernel_case": args.kernel_case, "blocks_per_launch": n,
