@@ -309,3 +309,36 @@ def test_fp8_manager_round_trip(cuda, mode):
   for t, b in zip(pool, bits):
     np.testing.assert_array_equal(
         t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16).reshape(b.shape), b)
+
+
+def test_fp8_quantizer_exact_over_bf16_domain(cuda):
+  """The in-kernel x / scale (Markstein-corrected reciprocal product, IEEE
+  division for units whose scale or reciprocal is not normal) must equal the
+  IEEE round-to-nearest division of the oracle: every finite bf16 value, and
+  2000 units of random magnitudes below random maxima (tiny ones included)."""
+  rng = np.random.default_rng(17)
+  bits = np.arange(1 << 16, dtype=np.uint32).astype(np.uint16)
+  finite = bits[(bits & 0x7FFF) < 0x7F80]
+  units = [np.zeros(8192, np.uint16) for _ in range(8)]
+  for i, chunk in enumerate(np.array_split(finite, 8)):
+    units[i][:chunk.size] = chunk
+  for _ in range(2000):
+    amax_bits = int(rng.integers(1, 0x7F80))
+    mag = rng.integers(0, amax_bits + 1, 8192, dtype=np.uint32).astype(np.uint16)
+    sign = (rng.integers(0, 2, 8192, dtype=np.uint32) << 15).astype(np.uint16)
+    u = mag | sign
+    u[0] = amax_bits
+    units.append(u)
+  host = np.stack(units)                      # [n_units, 8192] bf16 bit patterns
+  store = torch.from_numpy(host.view(np.int16)).to(cuda).view(torch.bfloat16)
+  store = store.view(host.shape[0], 64, 1, 128)
+  table = ops.StorageTable([store], fp8=True)
+  ids = list(range(host.shape[0]))
+  staging = table.new_staging(len(ids))
+  ops.kv_extract(table, ids, staging)
+  torch.cuda.synchronize()
+  payload, scales = ofp8.extract_fp8([host], ids)
+  st = staging.cpu().numpy()
+  np.testing.assert_array_equal(st[:, 0:8192], payload[:, 0])
+  got_scales = st[:, table.scale_off:table.scale_off + 4].copy().view(np.float32)[:, 0]
+  np.testing.assert_array_equal(got_scales, scales[:, 0])

@@ -140,7 +140,6 @@ __global__ void __launch_bounds__(kThreads)
 // dequant x' = bf16_rn(float(q) * scale).
 // ---------------------------------------------------------------------------
 
-constexpr int kFp8MaxVec = 8;  // register path: up to 8 x 16 B per thread (32 KiB unit)
 
 __device__ __forceinline__ float block_max(float v, float* red) {
 #pragma unroll
@@ -169,14 +168,38 @@ __device__ __forceinline__ float amax8(const int4& v, float m) {
   return m;
 }
 
+// Correctly rounded quotient x / scale.  Markstein's method (P. Markstein,
+// "Computation of elementary functions on the IBM RISC System/6000 processor",
+// IBM J. Res. Dev. 1990; Muller et al., Handbook of Floating-Point Arithmetic,
+// Markstein's theorem): with r = RN(1/scale) and q = RN(x*r) within one ulp of
+// x/scale, the FMA residual e = x - q*scale is exact and RN(q + e*r) is the
+// correctly rounded quotient.  e == 0 keeps q (exact, and keeps the sign of
+// a zero).  Units whose scale or reciprocal is not a normal finite number take
+// the IEEE division instead (use_div, uniform per unit).
+struct Divider {
+  float scale, r;
+  bool use_div;
+  __device__ __forceinline__ explicit Divider(float s) : scale(s) {
+    r = __frcp_rn(s);
+    use_div = !(s >= 1.17549435e-38f && s <= 3.40282347e38f && r >= 1.17549435e-38f &&
+                r <= 3.40282347e38f);
+  }
+  __device__ __forceinline__ float operator()(float x) const {
+    if (use_div) return __fdiv_rn(x, scale);
+    const float q = __fmul_rn(x, r);
+    const float e = __fmaf_rn(-q, scale, x);
+    return e == 0.f ? q : __fmaf_rn(e, r, q);
+  }
+};
+
 // 8 bf16 -> 8 e4m3 bytes (packed in a uint2).
-__device__ __forceinline__ uint2 quant8(const int4& v, float scale) {
+__device__ __forceinline__ uint2 quant8(const int4& v, const Divider& div) {
   const uint32_t w[4] = {uint32_t(v.x), uint32_t(v.y), uint32_t(v.z), uint32_t(v.w)};
   uint32_t out[2] = {0u, 0u};
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const float lo = __fdiv_rn(bf16_bits_to_float(w[j] & 0xffffu), scale);
-    const float hi = __fdiv_rn(bf16_bits_to_float(w[j] >> 16), scale);
+    const float lo = div(bf16_bits_to_float(w[j] & 0xffffu));
+    const float hi = div(bf16_bits_to_float(w[j] >> 16));
     const __nv_fp8x2_storage_t p =
         __nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE, __NV_E4M3);
     out[j >> 1] |= uint32_t(p) << (16 * (j & 1));
@@ -225,7 +248,9 @@ __device__ __forceinline__ bool unit_addr(const ts_block_storage* __restrict__ s
   return true;
 }
 
-template <typename Ids>
+// V = 16-byte vectors per thread held in registers (V*4 KiB per unit); a
+// unit larger than that takes the two-pass path.
+template <typename Ids, int V>
 __global__ void __launch_bounds__(kThreads)
     extract_fp8_kernel(const ts_block_storage* __restrict__ st, int n_st,
                        const __grid_constant__ Ids ids, int64_t n_blocks,
@@ -243,10 +268,10 @@ __global__ void __launch_bounds__(kThreads)
     uint8_t* q_out = stg_blk + st[s].stage_off;
     const int64_t nvec = int64_t(bb >> 4);  // 8 bf16 per vector
     float m = 0.f;
-    if (nvec <= int64_t(kThreads) * kFp8MaxVec) {
-      int4 v[kFp8MaxVec];
+    if (nvec <= int64_t(kThreads) * V) {
+      int4 v[V];
 #pragma unroll
-      for (int i = 0; i < kFp8MaxVec; ++i) {
+      for (int i = 0; i < V; ++i) {
         const int64_t idx = threadIdx.x + int64_t(i) * kThreads;
         if (idx < nvec) {
           v[i] = ld_stream(dev + (idx << 4));
@@ -255,10 +280,11 @@ __global__ void __launch_bounds__(kThreads)
       }
       const float amax = block_max(m, red);
       const float scale = amax == 0.f ? 1.f : __fdiv_rn(amax, 448.f);
+      const Divider div(scale);
 #pragma unroll
-      for (int i = 0; i < kFp8MaxVec; ++i) {
+      for (int i = 0; i < V; ++i) {
         const int64_t idx = threadIdx.x + int64_t(i) * kThreads;
-        if (idx < nvec) *reinterpret_cast<uint2*>(q_out + (idx << 3)) = quant8(v[i], scale);
+        if (idx < nvec) *reinterpret_cast<uint2*>(q_out + (idx << 3)) = quant8(v[i], div);
       }
       if (threadIdx.x == 0) *reinterpret_cast<float*>(stg_blk + scale_off + 4u * s) = scale;
     } else {
@@ -267,9 +293,10 @@ __global__ void __launch_bounds__(kThreads)
         m = amax8(ld_stream(dev + (idx << 4)), m);
       const float amax = block_max(m, red);
       const float scale = amax == 0.f ? 1.f : __fdiv_rn(amax, 448.f);
+      const Divider div(scale);
       for (int64_t idx = threadIdx.x; idx < nvec; idx += kThreads)
         *reinterpret_cast<uint2*>(q_out + (idx << 3)) =
-            quant8(*reinterpret_cast<const int4*>(dev + (idx << 4)), scale);
+            quant8(*reinterpret_cast<const int4*>(dev + (idx << 4)), div);
       if (threadIdx.x == 0) *reinterpret_cast<float*>(stg_blk + scale_off + 4u * s) = scale;
     }
   }
@@ -387,13 +414,22 @@ template <typename Ids>
 int launch_extract_fp8(int device, const ts_block_storage* d_st, int n_st,
                        const Ids& ids, int64_t n_blocks, void* staging,
                        uint64_t pitch, uint64_t scale_off, int* err_flag,
-                       cudaStream_t s, int max_ctas = 0) {
+                       cudaStream_t s, uint64_t max_bb, int max_ctas = 0) {
   if (n_blocks == 0 || n_st == 0) return TS_OK;
   DeviceGuard g(device);
   const int grid = launch_grid(device, n_blocks * int64_t(n_st), max_ctas);
-  extract_fp8_kernel<Ids><<<grid, kThreads, 0, s>>>(d_st, n_st, ids, n_blocks,
-                                                    static_cast<uint8_t*>(staging),
-                                                    pitch, scale_off, err_flag);
+  uint8_t* stg = static_cast<uint8_t*>(staging);
+  // register tile sized to the largest unit (16-byte vectors per thread)
+  const uint64_t vecs = (max_bb / 16 + kThreads - 1) / kThreads;
+  if (vecs <= 2)
+    extract_fp8_kernel<Ids, 2><<<grid, kThreads, 0, s>>>(d_st, n_st, ids, n_blocks, stg, pitch,
+                                                         scale_off, err_flag);
+  else if (vecs <= 4)
+    extract_fp8_kernel<Ids, 4><<<grid, kThreads, 0, s>>>(d_st, n_st, ids, n_blocks, stg, pitch,
+                                                         scale_off, err_flag);
+  else
+    extract_fp8_kernel<Ids, 8><<<grid, kThreads, 0, s>>>(d_st, n_st, ids, n_blocks, stg, pitch,
+                                                         scale_off, err_flag);
   TS_CUDA_RET(cudaGetLastError(), "extract_fp8 launch");
   return TS_OK;
 }
@@ -422,7 +458,7 @@ int mgr_extract(int device, const ts_block_storage* d_st, int n_st,
                 uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas) {
   if (fp8)
     return launch_extract_fp8(device, d_st, n_st, ids, n_blocks, staging, pitch,
-                              scale_off, err_flag, s, max_ctas);
+                              scale_off, err_flag, s, max_bb, max_ctas);
   return launch_extract(device, d_st, n_st, ids, n_blocks, staging, pitch,
                         err_flag, s, vec_ok, max_bb, max_ctas);
 }
@@ -484,10 +520,11 @@ extern "C" int ts_kv_insert(int device, const ts_block_storage* d_storages,
 
 namespace {
 int check_fp8_table(const ts_block_storage* d_st, int n_st, uint64_t pitch,
-                    uint64_t scale_off, const void* staging) {
+                    uint64_t scale_off, const void* staging, uint64_t* max_bb_out) {
   bool vec_ok;
   uint64_t max_bb;
   int rc = tsb::inspect_storages(d_st, n_st, pitch, staging, &vec_ok, &max_bb);
+  if (max_bb_out) *max_bb_out = max_bb;
   if (rc != TS_OK) return rc;
   // The fp8 kernels move 16 B of bf16 / 8 B of fp8 per vector.
   if (!vec_ok || (scale_off & 3u) != 0)
@@ -509,11 +546,12 @@ extern "C" int ts_kv_extract_fp8(int device, const ts_block_storage* d_storages,
   if (!d_storages || !d_ids || !d_staging)
     return set_error(TS_INVALID_ARGUMENT, "null pointer argument");
   tsb::DeviceGuard g(device);
-  int rc = check_fp8_table(d_storages, n_storages, stage_pitch, scale_off, d_staging);
+  uint64_t max_bb = 0;
+  int rc = check_fp8_table(d_storages, n_storages, stage_pitch, scale_off, d_staging, &max_bb);
   if (rc != TS_OK) return rc;
   return tsb::launch_extract_fp8(device, d_storages, n_storages, tsb::DevIds{d_ids}, n_blocks,
                                  d_staging, stage_pitch, scale_off, err_flag,
-                                 reinterpret_cast<cudaStream_t>(stream));
+                                 reinterpret_cast<cudaStream_t>(stream), max_bb);
 }
 
 extern "C" int ts_kv_insert_fp8(int device, const ts_block_storage* d_storages,
@@ -527,7 +565,7 @@ extern "C" int ts_kv_insert_fp8(int device, const ts_block_storage* d_storages,
   if (!d_storages || !d_ids || !d_staging)
     return set_error(TS_INVALID_ARGUMENT, "null pointer argument");
   tsb::DeviceGuard g(device);
-  int rc = check_fp8_table(d_storages, n_storages, stage_pitch, scale_off, d_staging);
+  int rc = check_fp8_table(d_storages, n_storages, stage_pitch, scale_off, d_staging, nullptr);
   if (rc != TS_OK) return rc;
   return tsb::launch_insert_fp8(device, d_storages, n_storages, tsb::DevIds{d_ids}, n_blocks,
                                 d_staging, stage_pitch, scale_off, err_flag,
