@@ -173,9 +173,11 @@ __device__ __forceinline__ float amax8(const int4& v, float m) {
 // IBM J. Res. Dev. 1990; Muller et al., Handbook of Floating-Point Arithmetic,
 // Markstein's theorem): with r = RN(1/scale) and q = RN(x*r) within one ulp of
 // x/scale, the FMA residual e = x - q*scale is exact and RN(q + e*r) is the
-// correctly rounded quotient.  e == 0 keeps q (exact, and keeps the sign of
-// a zero).  Units whose scale or reciprocal is not a normal finite number take
-// the IEEE division instead (use_div, uniform per unit).
+// correctly rounded quotient.  The residual is a multiple of 2^(exp(x) - 46),
+// so it is exactly representable (no underflow) when |x| >= 2^-96; smaller x
+// take the IEEE division, as do units whose scale or reciprocal is not a
+// normal finite number (use_div, uniform per unit).  e == 0 keeps q (exact,
+// and keeps the sign of a zero).
 struct Divider {
   float scale, r;
   bool use_div;
@@ -185,7 +187,7 @@ struct Divider {
                 r <= 3.40282347e38f);
   }
   __device__ __forceinline__ float operator()(float x) const {
-    if (use_div) return __fdiv_rn(x, scale);
+    if (use_div || fabsf(x) < 1.2621774e-29f /* 2^-96 */) return __fdiv_rn(x, scale);
     const float q = __fmul_rn(x, r);
     const float e = __fmaf_rn(-q, scale, x);
     return e == 0.f ? q : __fmaf_rn(e, r, q);
