@@ -158,14 +158,24 @@ __device__ __forceinline__ float bf16_bits_to_float(uint32_t h) {
   return __uint_as_float(h << 16);
 }
 
-__device__ __forceinline__ float amax8(const int4& v, float m) {
+// Running |x| maximum of 8 bf16 values on packed pairs: clearing the sign
+// bits gives |x|, and the bf16x2 maximum ignores NaN like fmaxf.
+__device__ __forceinline__ __nv_bfloat162 amax8_pairs(const int4& v, __nv_bfloat162 m) {
   const uint32_t w[4] = {uint32_t(v.x), uint32_t(v.y), uint32_t(v.z), uint32_t(v.w)};
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    m = fmaxf(m, fabsf(bf16_bits_to_float(w[j] & 0xffffu)));
-    m = fmaxf(m, fabsf(bf16_bits_to_float(w[j] >> 16)));
+    const uint32_t a = w[j] & 0x7fff7fffu;
+    m = __hmax2(m, *reinterpret_cast<const __nv_bfloat162*>(&a));
   }
   return m;
+}
+
+__device__ __forceinline__ float pair_max(__nv_bfloat162 m) {
+  return fmaxf(__bfloat162float(m.x), __bfloat162float(m.y));
+}
+
+__device__ __forceinline__ float amax8(const int4& v, float m) {
+  return fmaxf(m, pair_max(amax8_pairs(v, __floats2bfloat162_rn(0.f, 0.f))));
 }
 
 // Correctly rounded quotient x / scale.  Markstein's method (P. Markstein,
@@ -176,8 +186,8 @@ __device__ __forceinline__ float amax8(const int4& v, float m) {
 // correctly rounded quotient.  The residual is a multiple of 2^(exp(x) - 46),
 // so it is exactly representable (no underflow) when |x| >= 2^-96; smaller x
 // take the IEEE division, as do units whose scale or reciprocal is not a
-// normal finite number (use_div, uniform per unit).  e == 0 keeps q (exact,
-// and keeps the sign of a zero).
+// normal finite number (use_div, uniform per unit).  The quotient's sign is
+// x's (scale > 0), which copysign restores for zero results.
 struct Divider {
   float scale, r;
   bool use_div;
@@ -190,7 +200,7 @@ struct Divider {
     if (use_div || fabsf(x) < 1.2621774e-29f /* 2^-96 */) return __fdiv_rn(x, scale);
     const float q = __fmul_rn(x, r);
     const float e = __fmaf_rn(-q, scale, x);
-    return e == 0.f ? q : __fmaf_rn(e, r, q);
+    return copysignf(__fmaf_rn(e, r, q), x);  // scale > 0: sign of x (also for zeros)
   }
 };
 
@@ -272,14 +282,16 @@ __global__ void __launch_bounds__(kThreads)
     float m = 0.f;
     if (nvec <= int64_t(kThreads) * V) {
       int4 v[V];
+      __nv_bfloat162 mp = __floats2bfloat162_rn(0.f, 0.f);
 #pragma unroll
       for (int i = 0; i < V; ++i) {
         const int64_t idx = threadIdx.x + int64_t(i) * kThreads;
         if (idx < nvec) {
           v[i] = ld_stream(dev + (idx << 4));
-          m = amax8(v[i], m);
+          mp = amax8_pairs(v[i], mp);
         }
       }
+      m = pair_max(mp);
       const float amax = block_max(m, red);
       const float scale = amax == 0.f ? 1.f : __fdiv_rn(amax, 448.f);
       const Divider div(scale);
