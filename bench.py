@@ -44,8 +44,8 @@ METRIC = "KV offload/reload GB/s per GPU vs PCIe peak; extract HBM GB/s; 8B weig
 GIB = 1 << 30
 PCIE_SPEC_GBS = 64.0
 # DRAM bytes per 2 MiB block moved by the insert kernel, from
-# profiles/insert_kernel_c1_256blocks.md (None until captured).
-INSERT_TRAFFIC_PER_BLOCK = None
+# profiles/insert_kernel_c1_256blocks.md (mean of the two captured launches).
+INSERT_TRAFFIC_PER_BLOCK = 1019588608 / 256
 
 
 def parse():
