@@ -170,24 +170,6 @@ __device__ __forceinline__ __nv_bfloat162 amax8_pairs(const int4& v, __nv_bfloat
   return m;
 }
 
-// Running minimum of the nonzero |x| of 8 bf16 values (zeros count as +inf:
-// they take the fast path exactly).
-__device__ __forceinline__ __nv_bfloat162 amin8_pairs(const int4& v, __nv_bfloat162 m) {
-  const uint32_t w[4] = {uint32_t(v.x), uint32_t(v.y), uint32_t(v.z), uint32_t(v.w)};
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    uint32_t a = w[j] & 0x7fff7fffu;
-    if ((a & 0xffffu) == 0) a |= 0x7f80u;          // +inf in the low half
-    if ((a >> 16) == 0) a |= 0x7f800000u;          // +inf in the high half
-    m = __hmin2(m, *reinterpret_cast<const __nv_bfloat162*>(&a));
-  }
-  return m;
-}
-
-__device__ __forceinline__ float pair_min(__nv_bfloat162 m) {
-  return fminf(__bfloat162float(m.x), __bfloat162float(m.y));
-}
-
 __device__ __forceinline__ float pair_max(__nv_bfloat162 m) {
   return fmaxf(__bfloat162float(m.x), __bfloat162float(m.y));
 }
@@ -214,32 +196,22 @@ struct Divider {
     use_div = !(s >= 1.17549435e-38f && s <= 3.40282347e38f && r >= 1.17549435e-38f &&
                 r <= 3.40282347e38f);
   }
-  // Any |x|; per-element choice of method.
   __device__ __forceinline__ float operator()(float x) const {
-    if (use_div || fabsf(x) < kMarksteinMinAbs) return __fdiv_rn(x, scale);
-    return fast(x);
-  }
-  // Only for |x| >= kMarksteinMinAbs (or 0) and !use_div.
-  __device__ __forceinline__ float fast(float x) const {
+    if (use_div || fabsf(x) < 1.2621774e-29f /* 2^-96 */) return __fdiv_rn(x, scale);
     const float q = __fmul_rn(x, r);
     const float e = __fmaf_rn(-q, scale, x);
     return copysignf(__fmaf_rn(e, r, q), x);  // scale > 0: sign of x (also for zeros)
   }
-  static constexpr float kMarksteinMinAbs = 1.2621774e-29f;  // 2^-96
 };
 
-// 8 bf16 -> 8 e4m3 bytes (packed in a uint2).  kFast: every nonzero |x| of
-// the calling thread is >= 2^-96 and the unit's scale is normal.
-template <bool kFast>
+// 8 bf16 -> 8 e4m3 bytes (packed in a uint2).
 __device__ __forceinline__ uint2 quant8(const int4& v, const Divider& div) {
   const uint32_t w[4] = {uint32_t(v.x), uint32_t(v.y), uint32_t(v.z), uint32_t(v.w)};
   uint32_t out[2] = {0u, 0u};
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const float xl = bf16_bits_to_float(w[j] & 0xffffu);
-    const float xh = bf16_bits_to_float(w[j] >> 16);
-    const float lo = kFast ? div.fast(xl) : div(xl);
-    const float hi = kFast ? div.fast(xh) : div(xh);
+    const float lo = div(bf16_bits_to_float(w[j] & 0xffffu));
+    const float hi = div(bf16_bits_to_float(w[j] >> 16));
     const __nv_fp8x2_storage_t p =
         __nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE, __NV_E4M3);
     out[j >> 1] |= uint32_t(p) << (16 * (j & 1));
@@ -311,35 +283,22 @@ __global__ void __launch_bounds__(kThreads)
     if (nvec <= int64_t(kThreads) * V) {
       int4 v[V];
       __nv_bfloat162 mp = __floats2bfloat162_rn(0.f, 0.f);
-      __nv_bfloat162 np = __floats2bfloat162_rn(INFINITY, INFINITY);
 #pragma unroll
       for (int i = 0; i < V; ++i) {
         const int64_t idx = threadIdx.x + int64_t(i) * kThreads;
         if (idx < nvec) {
           v[i] = ld_stream(dev + (idx << 4));
           mp = amax8_pairs(v[i], mp);
-          np = amin8_pairs(v[i], np);
         }
       }
       m = pair_max(mp);
       const float amax = block_max(m, red);
       const float scale = amax == 0.f ? 1.f : __fdiv_rn(amax, 448.f);
       const Divider div(scale);
-      // NaN minima compare false: such a thread takes the general path.
-      if (!div.use_div && pair_min(np) >= Divider::kMarksteinMinAbs) {
 #pragma unroll
-        for (int i = 0; i < V; ++i) {
-          const int64_t idx = threadIdx.x + int64_t(i) * kThreads;
-          if (idx < nvec)
-            *reinterpret_cast<uint2*>(q_out + (idx << 3)) = quant8<true>(v[i], div);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < V; ++i) {
-          const int64_t idx = threadIdx.x + int64_t(i) * kThreads;
-          if (idx < nvec)
-            *reinterpret_cast<uint2*>(q_out + (idx << 3)) = quant8<false>(v[i], div);
-        }
+      for (int i = 0; i < V; ++i) {
+        const int64_t idx = threadIdx.x + int64_t(i) * kThreads;
+        if (idx < nvec) *reinterpret_cast<uint2*>(q_out + (idx << 3)) = quant8(v[i], div);
       }
       if (threadIdx.x == 0) *reinterpret_cast<float*>(stg_blk + scale_off + 4u * s) = scale;
     } else {
@@ -351,7 +310,7 @@ __global__ void __launch_bounds__(kThreads)
       const Divider div(scale);
       for (int64_t idx = threadIdx.x; idx < nvec; idx += kThreads)
         *reinterpret_cast<uint2*>(q_out + (idx << 3)) =
-            quant8<false>(*reinterpret_cast<const int4*>(dev + (idx << 4)), div);
+            quant8(*reinterpret_cast<const int4*>(dev + (idx << 4)), div);
       if (threadIdx.x == 0) *reinterpret_cast<float*>(stg_blk + scale_off + 4u * s) = scale;
     }
   }
