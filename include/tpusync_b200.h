@@ -69,6 +69,82 @@ TS_API int ts_coalesce_runs(const int64_t* src, const int64_t* dst, const int64_
                      int64_t n, int64_t* out_src, int64_t* out_dst,
                      int64_t* out_sizes, int64_t* n_out);
 
+/* Pool layouts: byte-level descriptions of block pools inside a storage.
+ * Replace RegionSpec / PoolSpec (tpu_sync/kv_cache/pool_layout.h:34-74); the
+ * same fields and meaning (tag / dtype_tag are opaque strings). */
+typedef struct ts_region_spec {
+  const char* name;
+  int64_t offset_bytes;      /* first unit's offset inside a block */
+  int64_t stride_bytes;      /* distance between units */
+  int64_t unit_bytes;
+  int64_t num_units;
+  int64_t units_per_stride;  /* units packed back to back at each stride */
+} ts_region_spec;
+
+typedef struct ts_pool_spec {
+  const char* tag;
+  int64_t storage_index;       /* which storage (layer) of the manager */
+  int64_t base_offset_bytes;
+  int64_t block_stride_bytes;
+  int64_t num_blocks;
+  const ts_region_spec* regions;
+  int64_t num_regions;
+  const char* dtype_tag;
+} ts_pool_spec;
+
+typedef struct ts_pool_extent {   /* PoolBlockCopyExtent (pool_layout.h:84-87) */
+  int64_t offset_bytes;
+  int64_t size_bytes;
+} ts_pool_extent;
+
+typedef struct ts_live_segment {  /* PoolLiveSegment (pool_layout.h:99-110) */
+  int64_t logical_offset;
+  int64_t physical_offset;
+  int64_t size;
+} ts_live_segment;
+
+typedef struct ts_live_copy_chunk {  /* LiveCopyChunk (pool_layout.h:127-137) */
+  int64_t src_physical;
+  int64_t dst_physical;
+  int64_t size;
+} ts_live_copy_chunk;
+
+/* RegionSpec::Validate / PoolSpec::Validate
+ * (tpu_sync/kv_cache/pool_layout.cc:120-185, :187-229); storage_bytes < 0
+ * checks internal consistency only.  Same codes and messages. */
+TS_API int ts_region_validate(const ts_region_spec* region, int64_t slot_bytes);
+TS_API int ts_pool_validate(const ts_pool_spec* pool, int64_t storage_bytes);
+/* PoolSpec::storage_extent_end_bytes (pool_layout.cc:231-254), the largest
+ * region extent end in one block and live_bytes_per_block
+ * (tpu_sync/api/torch/pool_layout.py:129-156); INT64_MAX on overflow. */
+TS_API int ts_pool_geometry(const ts_pool_spec* pool, int64_t* storage_extent_end,
+                            int64_t* block_live_end, int64_t* live_bytes_per_block);
+/* RegionsCoverRange (pool_layout.cc:256-272). */
+TS_API int ts_regions_cover_range(const ts_region_spec* regions, int64_t n, uint64_t start,
+                                  uint64_t end, int* covered);
+
+/* Output arrays below follow one protocol: *n_out receives the number of
+ * results; when it exceeds `cap` nothing is written and the call returns
+ * TS_RESOURCE_EXHAUSTED (call again with cap >= *n_out). */
+
+/* ComputePoolBlockCopyExtents (pool_layout.cc:274-374): declared-live byte
+ * extents of the given blocks, sorted and merged where they touch. */
+TS_API int ts_pool_copy_extents(const ts_pool_spec* pool, const int64_t* block_ids,
+                                int64_t n_ids, ts_pool_extent* out, int64_t cap,
+                                int64_t* n_out);
+/* ExpandPoolLiveSegments (pool_layout.cc:376-472). */
+TS_API int ts_pool_live_segments(const ts_pool_spec* pool, ts_live_segment* out, int64_t cap,
+                                 int64_t* n_out);
+/* PhysicalLiveRangeToLogical (pool_layout.cc:474-493). */
+TS_API int ts_pool_physical_to_logical(const ts_live_segment* segments, int64_t n,
+                                       int64_t physical_offset, int64_t size,
+                                       int64_t* logical_start, int64_t* logical_end);
+/* TranslateLiveCopy (pool_layout.cc:554-602). */
+TS_API int ts_pool_translate_live_copy(const ts_live_segment* src, int64_t n_src,
+                                       const ts_live_segment* dst, int64_t n_dst,
+                                       int64_t src_offset, int64_t dst_offset, int64_t size,
+                                       ts_live_copy_chunk* out, int64_t cap, int64_t* n_out);
+
 /* ------------------------------------------------------------------------ */
 /* Block-movement kernels (manager-free).                                    */
 /* ------------------------------------------------------------------------ */
@@ -308,6 +384,39 @@ TS_API int ts_mgr_host_block_ptr(ts_manager* mgr, int64_t layer_idx, int64_t sha
                           uint64_t* bytes_out);
 TS_API int ts_mgr_info(ts_manager* mgr, int64_t* host_blocks, uint64_t* host_block_pitch,
                 int64_t* major_dim, uint64_t* bytes_per_block);
+
+/* Explicit block pools: KVCacheManagerBase::RegisterPools
+ * (tpu_sync/kv_cache/kv_cache_manager_base.cc:1653-1712).  Until it is
+ * called the manager has implicit pools, one per storage (layer) whose
+ * block bytes are positive (EnsureImplicitPools, :1554-1590).  The host
+ * mirror of storage s shares its byte offsets: device byte x of the storage
+ * lives in host block x / bb(s) at offset x % bb(s) of that storage's slot.
+ * Pools whose live extent reaches past host_blocks * bb(s) are rejected
+ * (the host tier is one allocation and is not regrown).  Not available on an
+ * fp8 host tier. */
+TS_API int ts_mgr_register_pools(ts_manager* mgr, const ts_pool_spec* pools, int64_t n);
+TS_API int ts_mgr_num_pools(ts_manager* mgr, int64_t* n, int* explicit_pools);
+/* Geometry of pool `pool_idx` (strings are not returned: the caller keeps
+ * the specs it registered; implicit pools are tagged "opaque" with one region
+ * "block"). */
+TS_API int ts_mgr_pool_geometry(ts_manager* mgr, int64_t pool_idx, int64_t* storage_index,
+                                int64_t* block_stride_bytes, int64_t* num_blocks);
+
+/* CopyPoolBlocks (kv_cache_manager_base.cc:1789-1858): copies the declared-
+ * live extents of the given pool blocks between the device storage and its
+ * host mirror (same byte offsets); shard_idx = -1 copies every shard.
+ * Whole aligned blocks move as strided DMAs, partial regions with one
+ * segment-copy kernel over the mapped host tier. */
+TS_API int ts_d2h_pool_blocks(ts_manager* mgr, int64_t pool_idx, const int64_t* block_ids,
+                              int64_t n_ids, int64_t shard_idx, void* stream, ts_event** out);
+TS_API int ts_h2d_pool_blocks(ts_manager* mgr, int64_t pool_idx, const int64_t* block_ids,
+                              int64_t n_ids, int64_t shard_idx, void* stream, ts_event** out);
+/* GetPoolBlockRef (kv_cache_manager_base.cc:1714-1760): host address of one
+ * pool block (the block's live bytes must sit inside one host block of the
+ * block-major tier, which holds whenever the pool's blocks are the storage's
+ * blocks). */
+TS_API int ts_mgr_pool_block_ref(ts_manager* mgr, int64_t pool_idx, int64_t shard_idx,
+                                 int64_t block_id, uint64_t* host_ptr);
 
 /* Per-launch timing of the manager's kernels (CUDA events around every
  * extract / insert launch on its kernel streams).  ts_mgr_kernel_stats

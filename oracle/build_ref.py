@@ -1,12 +1,18 @@
-"""Compiles the reference's header-only LRUCache into a test oracle binary.
+"""Compiles reference sources into test oracle binaries.
 
-    python oracle/build_ref.py     # -> oracle/_ref/lru_ref
+    python oracle/build_ref.py     # -> oracle/_ref/lru_ref, oracle/_ref/pool_ref
 
-g++ builds oracle/ref_lru_driver.cc against tpu_sync/kv_cache/lru_cache.h
-where it lies in the reference checkout (REFERENCE_ROOT, default
-/root/reference), with oracle/shim standing in for absl's flat_hash_map.
-Nothing is copied from the reference; the binary goes to oracle/_ref/ only.
-Test infrastructure: tests/ use the binary to pin the product's LRU.
+* lru_ref: oracle/ref_lru_driver.cc over the header-only LRUCache
+  (tpu_sync/kv_cache/lru_cache.h);
+* pool_ref: oracle/ref_pool_driver.cc linked with tpu_sync/kv_cache/pool_layout.cc.
+
+g++ compiles them where they lie in the reference checkout (REFERENCE_ROOT,
+default /root/reference); oracle/shim stands in for the few absl types they
+use (flat_hash_map, Status, StatusOr, StrCat, Span) and for the two proto
+message classes pool_layout.h names.  Nothing is copied from the reference;
+the binaries go to oracle/_ref/ only.  Test infrastructure: tests/ use them to
+pin the product's LRU and pool geometry (and tests/golden/make_pool_golden.py
+records pool_ref's answers as fixtures).
 """
 
 from __future__ import annotations
@@ -40,5 +46,25 @@ def build(force: bool = False) -> Path | None:
   return OUT
 
 
+POOL_OUT = HERE / "_ref" / "pool_ref"
+
+
+def build_pool(force: bool = False) -> Path | None:
+  """Builds pool_ref if the reference checkout is present; returns its path."""
+  ref = reference_root()
+  cc = ref / "tpu_sync" / "kv_cache" / "pool_layout.cc"
+  src = HERE / "ref_pool_driver.cc"
+  if POOL_OUT.exists() and not force and POOL_OUT.stat().st_mtime >= src.stat().st_mtime:
+    return POOL_OUT
+  if not cc.exists():
+    return POOL_OUT if POOL_OUT.exists() else None
+  POOL_OUT.parent.mkdir(parents=True, exist_ok=True)
+  cxx = shutil.which("g++") or "c++"
+  subprocess.run([cxx, "-std=c++17", "-O1", f"-I{HERE / 'shim'}", f"-I{ref}", str(src), str(cc),
+                  "-o", str(POOL_OUT)], check=True)
+  return POOL_OUT
+
+
 if __name__ == "__main__":
   print(build(force=True))
+  print(build_pool(force=True))

@@ -86,6 +86,33 @@ class BlockInfo(ctypes.Structure):
               ("status", ctypes.c_int32), ("pad_", ctypes.c_int32)]
 
 
+class RegionSpecC(ctypes.Structure):
+  _fields_ = [("name", ctypes.c_char_p), ("offset_bytes", ctypes.c_int64),
+              ("stride_bytes", ctypes.c_int64), ("unit_bytes", ctypes.c_int64),
+              ("num_units", ctypes.c_int64), ("units_per_stride", ctypes.c_int64)]
+
+
+class PoolSpecC(ctypes.Structure):
+  _fields_ = [("tag", ctypes.c_char_p), ("storage_index", ctypes.c_int64),
+              ("base_offset_bytes", ctypes.c_int64), ("block_stride_bytes", ctypes.c_int64),
+              ("num_blocks", ctypes.c_int64), ("regions", ctypes.POINTER(RegionSpecC)),
+              ("num_regions", ctypes.c_int64), ("dtype_tag", ctypes.c_char_p)]
+
+
+class PoolExtent(ctypes.Structure):
+  _fields_ = [("offset_bytes", ctypes.c_int64), ("size_bytes", ctypes.c_int64)]
+
+
+class LiveSegmentC(ctypes.Structure):
+  _fields_ = [("logical_offset", ctypes.c_int64), ("physical_offset", ctypes.c_int64),
+              ("size", ctypes.c_int64)]
+
+
+class LiveCopyChunkC(ctypes.Structure):
+  _fields_ = [("src_physical", ctypes.c_int64), ("dst_physical", ctypes.c_int64),
+              ("size", ctypes.c_int64)]
+
+
 # name -> (restype, argtypes); every symbol declared in include/tpusync_b200.h
 _V = ctypes.c_void_p
 _SIGS = {
@@ -95,6 +122,25 @@ _SIGS = {
                                              ctypes.c_int64, c_i64_p, ctypes.c_int64]),
     "ts_coalesce_runs": (ctypes.c_int, [c_i64_p, c_i64_p, c_i64_p, ctypes.c_int64,
                                         c_i64_p, c_i64_p, c_i64_p, c_i64_p]),
+    "ts_region_validate": (ctypes.c_int, [ctypes.POINTER(RegionSpecC), ctypes.c_int64]),
+    "ts_pool_validate": (ctypes.c_int, [ctypes.POINTER(PoolSpecC), ctypes.c_int64]),
+    "ts_pool_geometry": (ctypes.c_int, [ctypes.POINTER(PoolSpecC), c_i64_p, c_i64_p, c_i64_p]),
+    "ts_regions_cover_range": (ctypes.c_int, [ctypes.POINTER(RegionSpecC), ctypes.c_int64,
+                                              ctypes.c_uint64, ctypes.c_uint64,
+                                              ctypes.POINTER(ctypes.c_int)]),
+    "ts_pool_copy_extents": (ctypes.c_int, [ctypes.POINTER(PoolSpecC), c_i64_p, ctypes.c_int64,
+                                            ctypes.POINTER(PoolExtent), ctypes.c_int64, c_i64_p]),
+    "ts_pool_live_segments": (ctypes.c_int, [ctypes.POINTER(PoolSpecC),
+                                             ctypes.POINTER(LiveSegmentC), ctypes.c_int64,
+                                             c_i64_p]),
+    "ts_pool_physical_to_logical": (ctypes.c_int, [ctypes.POINTER(LiveSegmentC), ctypes.c_int64,
+                                                   ctypes.c_int64, ctypes.c_int64, c_i64_p,
+                                                   c_i64_p]),
+    "ts_pool_translate_live_copy": (ctypes.c_int, [ctypes.POINTER(LiveSegmentC), ctypes.c_int64,
+                                                   ctypes.POINTER(LiveSegmentC), ctypes.c_int64,
+                                                   ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                                   ctypes.POINTER(LiveCopyChunkC),
+                                                   ctypes.c_int64, c_i64_p]),
     "ts_kv_extract": (ctypes.c_int, [ctypes.c_int, _V, ctypes.c_int, _V,
                                      ctypes.c_int64, _V, ctypes.c_uint64, _V, _V]),
     "ts_kv_insert": (ctypes.c_int, [ctypes.c_int, _V, ctypes.c_int, _V,
@@ -141,6 +187,15 @@ _SIGS = {
     "ts_mgr_host_block_ptr": (ctypes.c_int, [_V, ctypes.c_int64, ctypes.c_int64,
                                              ctypes.c_int64, c_u64_p, c_u64_p]),
     "ts_mgr_info": (ctypes.c_int, [_V, c_i64_p, c_u64_p, c_i64_p, c_u64_p]),
+    "ts_mgr_register_pools": (ctypes.c_int, [_V, ctypes.POINTER(PoolSpecC), ctypes.c_int64]),
+    "ts_mgr_num_pools": (ctypes.c_int, [_V, c_i64_p, ctypes.POINTER(ctypes.c_int)]),
+    "ts_mgr_pool_geometry": (ctypes.c_int, [_V, ctypes.c_int64, c_i64_p, c_i64_p, c_i64_p]),
+    "ts_d2h_pool_blocks": (ctypes.c_int, [_V, ctypes.c_int64, c_i64_p, ctypes.c_int64,
+                                          ctypes.c_int64, _V, ctypes.POINTER(_V)]),
+    "ts_h2d_pool_blocks": (ctypes.c_int, [_V, ctypes.c_int64, c_i64_p, ctypes.c_int64,
+                                          ctypes.c_int64, _V, ctypes.POINTER(_V)]),
+    "ts_mgr_pool_block_ref": (ctypes.c_int, [_V, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                             c_u64_p]),
     "ts_mgr_set_profiling": (ctypes.c_int, [_V, ctypes.c_int]),
     "ts_mgr_kernel_stats": (ctypes.c_int, [_V, ctypes.c_int, c_i64_p,
                                            ctypes.POINTER(ctypes.c_double), c_u64_p]),

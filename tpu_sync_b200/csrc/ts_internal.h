@@ -49,6 +49,21 @@ int mgr_insert(int device, const ts_block_storage* d_st, int n_st,
                uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
                uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas);
 
+// Strided byte runs for seg_copy (seg_copy.cu): row r of `count` rows of
+// `bytes` bytes goes from src + r*src_stride to dst + r*dst_stride.  src / dst
+// are addresses the launching device can access (its memory, mapped host
+// memory, or a peer's memory with peer access enabled).
+struct SegTask {
+  uint64_t src;
+  uint64_t dst;
+  int64_t src_stride;
+  int64_t dst_stride;
+  uint32_t bytes;
+  uint32_t count;
+};
+constexpr int kMaxSegTasks = 512;  // tasks per launch (kernel parameters)
+int seg_copy(int device, const SegTask* tasks, int64_t n, cudaStream_t s, int max_ctas);
+
 // Scoped switch of the current CUDA device.
 class DeviceGuard {
  public:

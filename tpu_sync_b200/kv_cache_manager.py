@@ -315,30 +315,123 @@ class KVCacheManager:
     t = self._grid[layer_idx][0]
     return t.numel() * t.element_size() // self.major_dim
 
-  # -- pool surface over the implicit pools --------------------------------
+  # -- pools (RegisterPools / CopyPoolBlocks) -------------------------------
+  def register_pools(self, pools: Sequence[Any]) -> Dict[str, Any]:
+    """Registers explicit block pools over the wrapped storages.
+
+    ``pools``: PoolSpec objects or equivalent mappings, in the caller's
+    canonical order (pool indices are positions in it).  Returns the admission
+    summary (tpu_sync/api/torch/kv_cache_manager.py:239-283).
+    """
+    from tpu_sync_b200 import pool_layout
+    coerced = tuple(pool_layout.coerce_pool_spec(p) for p in pools)
+    if not coerced:
+      raise ValueError("pool table must be non-empty")
+    for i, p in enumerate(coerced):
+      try:
+        p.validate()
+      except ValueError as exc:
+        raise ValueError(f"invalid pool {i}: {exc}") from exc
+      if p.storage_index >= self.num_layers:
+        raise ValueError(f"pool {i} ({p.tag}) storage_index {p.storage_index} out of range: "
+                         f"manager wraps {self.num_layers} storages")
+    arr, keep = pool_layout.pools_c(coerced)
+    rc = _native.lib().ts_mgr_register_pools(self._mgr, arr, len(coerced))
+    del keep
+    if rc != _native.OK:
+      raise RuntimeError("KVCacheManager register_pools failed: " + _native.last_error())
+    self._pools = coerced
+    tags: Dict[str, int] = {}
+    for p in coerced:
+      tags[p.tag] = tags.get(p.tag, 0) + 1
+    self._admission_summary = {"admitted": True, "pools": len(coerced),
+                               "storages": len({p.storage_index for p in coerced}), "tags": tags}
+    return dict(self._admission_summary)
+
+  def admission_summary(self) -> Dict[str, Any]:
+    summary = getattr(self, "_admission_summary", None)
+    return dict(summary) if summary else {"admitted": False}
+
+  def has_explicit_pools(self) -> bool:
+    n, ex = ctypes.c_int64(), ctypes.c_int()
+    _native.check(_native.lib().ts_mgr_num_pools(self._mgr, ctypes.byref(n), ctypes.byref(ex)))
+    return bool(ex.value)
+
   def num_pools(self) -> int:
-    """Implicit pools: one per storage (tag "opaque"), as before RegisterPools."""
-    return self.num_layers
+    """Pools (implicit: one per storage with positive block bytes; or explicit)."""
+    n = ctypes.c_int64()
+    _native.check(_native.lib().ts_mgr_num_pools(self._mgr, ctypes.byref(n), None))
+    return n.value
 
   def pool_spec(self, pool_idx: int) -> Dict[str, Any]:
-    if not 0 <= pool_idx < self.num_layers:
-      raise RuntimeError(f"pool index {pool_idx} out of range")
-    bb = self.block_bytes(pool_idx)
-    return {"tag": "opaque", "storage_index": pool_idx, "base_offset_bytes": 0,
-            "block_stride_bytes": bb, "num_blocks": self.major_dim,
+    """One pool's descriptor as a dict (implicit pools: tag "opaque", region "block")."""
+    if getattr(self, "_pools", None) is not None:
+      if not 0 <= pool_idx < len(self._pools):
+        raise IndexError(f"pool index out of range: {pool_idx}")
+      return self._pools[pool_idx].to_dict()
+    si, stride, nb = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+    rc = _native.lib().ts_mgr_pool_geometry(self._mgr, int(pool_idx), ctypes.byref(si),
+                                            ctypes.byref(stride), ctypes.byref(nb))
+    if rc != _native.OK:
+      raise IndexError(f"pool index out of range: {pool_idx}")
+    bb = stride.value
+    return {"tag": "opaque", "storage_index": si.value, "base_offset_bytes": 0,
+            "block_stride_bytes": bb, "num_blocks": nb.value,
             "regions": [{"name": "block", "offset_bytes": 0, "stride_bytes": bb,
-                         "unit_bytes": bb, "num_units": 1, "units_per_stride": 1}]}
+                         "unit_bytes": bb, "num_units": 1, "units_per_stride": 1}],
+            "dtype_tag": ""}
+
+  def pool_ids_with_tag(self, tag: str) -> List[int]:
+    return [i for i in range(self.num_pools()) if self.pool_spec(i)["tag"] == tag]
+
+  def get_block_ref(self, pool_idx: int, block_id: int, shard_idx: int = 0) -> Dict[str, Any]:
+    """Host-side reference to one pool block (pointer into the host tier)."""
+    ptr = ctypes.c_uint64()
+    rc = _native.lib().ts_mgr_pool_block_ref(self._mgr, int(pool_idx), int(shard_idx),
+                                             int(block_id), ctypes.byref(ptr))
+    if rc != _native.OK:
+      raise RuntimeError("KVCacheManager get_pool_block_ref failed: " + _native.last_error())
+    spec = self.pool_spec(pool_idx)
+    return {"ptr": ptr.value, "block_stride_bytes": spec["block_stride_bytes"],
+            "tag": spec["tag"], "dtype_tag": spec.get("dtype_tag", ""), "pool_idx": pool_idx,
+            "shard_idx": shard_idx, "block_id": block_id, "regions": spec["regions"]}
+
+  def _pool_copy(self, fn, what, pool_idx, block_ids, shard_idx, stream):
+    ids = _native.i64_array(list(block_ids))
+    if stream is None:
+      stream = torch.cuda.current_stream(self.device)
+    ev = ctypes.c_void_p()
+    rc = fn(self._mgr, int(pool_idx), _native.i64_ptr(ids), ids.size,
+            -1 if shard_idx is None else int(shard_idx), ctypes.c_void_p(stream.cuda_stream),
+            ctypes.byref(ev))
+    if rc != _native.OK:
+      raise RuntimeError(f"KVCacheManager {what} failed: " + _native.last_error())
+    return RaidenFuture(ev.value, keepalive=self)
 
   def d2h_pool_blocks(self, pool_idx: int, block_ids: Sequence[int],
-                      shard_idx: Optional[int] = None) -> RaidenFuture:
-    """Partial D2H of whole pool blocks into the host mirror (same ids)."""
-    ids = list(block_ids)
-    return self._transfer(_native.lib().ts_d2h, "D2hPoolBlocks", ids, ids, None,
-                          pool_idx, shard_idx, None)
+                      shard_idx: Optional[int] = None, *,
+                      stream: Optional[torch.cuda.Stream] = None) -> RaidenFuture:
+    """Partial D2H of the declared-live bytes of pool blocks into the host mirror."""
+    return self._pool_copy(_native.lib().ts_d2h_pool_blocks, "d2h_pool_blocks", pool_idx,
+                           block_ids, shard_idx, stream)
 
   def h2d_pool_blocks(self, pool_idx: int, block_ids: Sequence[int],
-                      shard_idx: Optional[int] = None) -> RaidenFuture:
-    """Partial H2D of whole pool blocks from the host mirror (same ids)."""
-    ids = list(block_ids)
-    return self._transfer(_native.lib().ts_h2d, "H2dPoolBlocks", ids, ids, None,
-                          pool_idx, shard_idx, None)
+                      shard_idx: Optional[int] = None, *,
+                      stream: Optional[torch.cuda.Stream] = None) -> RaidenFuture:
+    """Partial H2D of the declared-live bytes of pool blocks from the host mirror."""
+    return self._pool_copy(_native.lib().ts_h2d_pool_blocks, "h2d_pool_blocks", pool_idx,
+                           block_ids, shard_idx, stream)
+
+  def read_storage_bytes(self, layer_idx: int, offset: int, size: int,
+                         shard_idx: int = 0) -> bytes:
+    """Bytes [offset, offset + size) of one storage's host mirror (byte offsets
+    as on the device, across host blocks)."""
+    bb = self.block_bytes(layer_idx)
+    out = bytearray()
+    x, end = int(offset), int(offset) + int(size)
+    while x < end:
+      blk, inb = divmod(x, bb)
+      take = min(bb - inb, end - x)
+      out += self.read_block_bytes(layer_idx, blk, shard_idx)[inb:inb + take]
+      x += take
+    return bytes(out)
