@@ -145,6 +145,114 @@ TS_API int ts_pool_translate_live_copy(const ts_live_segment* src, int64_t n_src
                                        int64_t src_offset, int64_t dst_offset, int64_t size,
                                        ts_live_copy_chunk* out, int64_t cap, int64_t* n_out);
 
+/* Pool reshard planning (prefill -> decode KV hand-off).  Replaces the data
+ * part of BuildPoolReshardPlan
+ * (tpu_sync/kv_cache/reshard/pool_reshard_planner.cc:132-859) with the span
+ * declarations of tpu_sync/kv_cache/reshard/declaration_types.h:17-58. */
+typedef struct ts_byte_span {        /* PoolByteSpan */
+  int64_t src_block_ordinal;         /* index into the declaration's block_ids */
+  int64_t src_offset_bytes;          /* compact-live offset in the source block */
+  int64_t dst_block_index;           /* index into the tag's destination block list */
+  int64_t dst_offset_bytes;          /* compact-live offset (v1: request-global) */
+  int64_t size_bytes;
+  int64_t src_stride_bytes;
+  int64_t dst_stride_bytes;
+  int32_t count;                     /* repeats at the strides */
+  int32_t pad_;
+} ts_byte_span;
+
+typedef struct ts_span_decl {        /* PoolSpanRegistration of one source unit */
+  int64_t src_unit;                  /* index of the declaring source unit */
+  const char* tag;
+  const int64_t* block_ids;
+  int64_t n_block_ids;
+  const ts_byte_span* spans;
+  int64_t n_spans;
+  int64_t declared_bytes;
+  int32_t dst_space_version;         /* 0: page-indexed, 1: request-global */
+  int32_t pad_;
+} ts_span_decl;
+
+typedef struct ts_pool_reshard_request {  /* PlanRequest (data-plane fields) */
+  int64_t n_src_units;
+  const ts_pool_spec* const* src_pools;   /* per unit: its pool manifest */
+  const int64_t* n_src_pools;             /* per unit */
+  const ts_pool_spec* dst_pools;          /* the destination unit's manifest */
+  int64_t n_dst_pools;
+  const int32_t* transfer_ranks;          /* per unit (NULL: unit index) */
+  const int32_t* transfer_parallelism;    /* per unit (NULL: 1) */
+  int32_t parallelism;                    /* 0: the units' admitted value */
+  int32_t pad_;
+  const char* const* tags;                /* transfer_pool_tags */
+  int64_t n_tags;
+  const int64_t* dst_block_ids;
+  int64_t n_dst_block_ids;
+  const int64_t* dst_block_counts;        /* per tag, or n = 0 */
+  int64_t n_dst_block_counts;
+  const int64_t* dst_skip_bytes;          /* per tag, or n = 0 */
+  int64_t n_dst_skip_bytes;
+  const ts_span_decl* decls;
+  int64_t n_decls;
+  const char* const* unit_names;          /* per unit names for messages, or NULL */
+} ts_pool_reshard_request;
+
+typedef struct ts_schedule_entry {   /* ScheduleEntry (pool_reshard_planner.h:20-33) */
+  int64_t src_block_id;
+  int64_t dst_block_id;
+  int64_t src_offset_bytes;          /* physical offset inside the source pool block */
+  int64_t dst_offset_bytes;          /* physical offset inside the destination pool block */
+  int64_t size_bytes;
+  int32_t pool_group;
+  int32_t pad_;
+} ts_schedule_entry;
+
+typedef struct ts_pool_reshard_plan ts_pool_reshard_plan;
+typedef struct ts_pool_reshard_program ts_pool_reshard_program;
+
+TS_API int ts_pool_reshard_plan_build(const ts_pool_reshard_request* request,
+                                      ts_pool_reshard_plan** out);
+TS_API void ts_pool_reshard_plan_destroy(ts_pool_reshard_plan* plan);
+/* info[8] = {groups, active source units, expected_block_count, parallelism,
+ * expected_pushes_per_pool, transfer pool count, entries (all units), units}. */
+TS_API int ts_pool_reshard_plan_info(const ts_pool_reshard_plan* plan, int64_t* info);
+/* One source unit's schedule (capacity protocol as above). */
+TS_API int ts_pool_reshard_plan_entries(const ts_pool_reshard_plan* plan, int64_t src_unit,
+                                        ts_schedule_entry* out, int64_t cap, int64_t* n_out);
+/* Active source units in rank order (info[1] of them) and the transfer pool
+ * indices (info[5]); either pointer may be NULL. */
+TS_API int ts_pool_reshard_plan_units(const ts_pool_reshard_plan* plan, int64_t* units,
+                                      int32_t* pool_indices);
+/* sizes[4] = {pools, destination blocks, expected pushes, order rank}; the
+ * arrays (may be NULL) receive the pool indices, destination block ids and
+ * expected extent bytes per destination block. */
+TS_API int ts_pool_reshard_plan_group(const ts_pool_reshard_plan* plan, int64_t group,
+                                      int64_t* sizes, int32_t* pool_indices, int64_t* dst_ids,
+                                      int64_t* extents);
+
+/* Pool reshard execution: replaces PoolReshardPush / StartPoolReshardPush /
+ * OnPoolReceived + H2dPoolBlocks (D2H, TCP push, H2D;
+ * tpu_sync/core/kv_cache_manager_with_transfer.cc:1152-1335, :2665-2805) by
+ * one kernel on the source GPU that stores every entry of `src_unit`, for
+ * every pool of its group, into the destination storages.  Storage pointers
+ * are indexed by pool storage_index: the source unit's device storages and
+ * the destination's storages as this device addresses them (its own memory,
+ * a peer pointer with peer access enabled, or a CUDA IPC mapping opened on
+ * this device), with their sizes in bytes: every transferred pool must fit
+ * its storages (checked), so no copy reaches outside them.  create uploads
+ * two small tables per pool group (device allocations owned by the program);
+ * launch queues one kernel per group on `stream`. */
+TS_API int ts_pool_reshard_program_create(const ts_pool_reshard_plan* plan, int64_t src_unit,
+                                          int device, const uint64_t* src_storage_ptrs,
+                                          const uint64_t* dst_storage_ptrs,
+                                          const uint64_t* src_storage_bytes,
+                                          const uint64_t* dst_storage_bytes, int64_t n_storages,
+                                          ts_pool_reshard_program** out);
+TS_API int ts_pool_reshard_program_info(const ts_pool_reshard_program* prog, int64_t* n_tasks,
+                                        uint64_t* bytes);
+TS_API int ts_pool_reshard_program_launch(ts_pool_reshard_program* prog, void* stream,
+                                          int max_ctas);
+TS_API void ts_pool_reshard_program_destroy(ts_pool_reshard_program* prog);
+
 /* ------------------------------------------------------------------------ */
 /* Block-movement kernels (manager-free).                                    */
 /* ------------------------------------------------------------------------ */

@@ -119,3 +119,29 @@ def test_cross_process_ipc_reshard():
   ps.join(timeout=60)
   assert pt.exitcode == 0 and ps.exitcode == 0
   assert ok
+
+
+def test_pool_reshard_plan_into_peer_gpu():
+  """C3-shaped pool plan executed on cuda:0, storing into cuda:1's pages."""
+  two_gpus()
+  from tpu_sync_b200.pool_reshard import PoolReshardProgram, build_pool_reshard_plan
+  rng = np.random.default_rng(4)
+  n_st, n_seqs, T, H, HB = 3, 2, 512, 2, 256
+  sbps, dbps = T // 16, T // 64
+  st = rng.permutation(n_seqs * sbps).reshape(n_seqs, sbps).astype(np.int32)
+  dt = rng.permutation(n_seqs * dbps).reshape(n_seqs, dbps).astype(np.int32)
+  src_pools, dst_pools, dst_ids, r = workloads.handoff_pool_plan_inputs(n_st, st, dt, H, HB)
+  plan = build_pool_reshard_plan([src_pools], dst_pools, ["kv"], dst_ids, [(0, r)])
+  g = torch.Generator().manual_seed(2)
+  src = [torch.randint(0, 256, (n_seqs * sbps, 16 * H * HB), generator=g,
+                       dtype=torch.uint8).cuda(0) for _ in range(n_st)]
+  dst = [torch.zeros((n_seqs * dbps, 64 * H * HB), dtype=torch.uint8, device="cuda:1")
+         for _ in range(n_st)]
+  PoolReshardProgram(plan, 0, src, dst).launch()
+  torch.cuda.synchronize(0)
+  sg = dict(block_tokens=16, heads=H, head_bytes=HB, head_major=1)
+  dg = dict(block_tokens=64, heads=H, head_bytes=HB, head_major=0)
+  for s in range(n_st):
+    want = np.zeros((n_seqs * dbps, 64 * H * HB), np.uint8)
+    ors.relayout(src[s].cpu().numpy(), want, sg, dg, st, dt, T)
+    np.testing.assert_array_equal(dst[s].cpu().numpy(), want)

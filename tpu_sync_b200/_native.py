@@ -113,6 +113,43 @@ class LiveCopyChunkC(ctypes.Structure):
               ("size", ctypes.c_int64)]
 
 
+class ByteSpanC(ctypes.Structure):
+  _fields_ = [("src_block_ordinal", ctypes.c_int64), ("src_offset_bytes", ctypes.c_int64),
+              ("dst_block_index", ctypes.c_int64), ("dst_offset_bytes", ctypes.c_int64),
+              ("size_bytes", ctypes.c_int64), ("src_stride_bytes", ctypes.c_int64),
+              ("dst_stride_bytes", ctypes.c_int64), ("count", ctypes.c_int32),
+              ("pad_", ctypes.c_int32)]
+
+
+class SpanDeclC(ctypes.Structure):
+  _fields_ = [("src_unit", ctypes.c_int64), ("tag", ctypes.c_char_p),
+              ("block_ids", c_i64_p), ("n_block_ids", ctypes.c_int64),
+              ("spans", ctypes.POINTER(ByteSpanC)), ("n_spans", ctypes.c_int64),
+              ("declared_bytes", ctypes.c_int64), ("dst_space_version", ctypes.c_int32),
+              ("pad_", ctypes.c_int32)]
+
+
+class PoolReshardRequestC(ctypes.Structure):
+  _fields_ = [("n_src_units", ctypes.c_int64),
+              ("src_pools", ctypes.POINTER(ctypes.POINTER(PoolSpecC))),
+              ("n_src_pools", c_i64_p), ("dst_pools", ctypes.POINTER(PoolSpecC)),
+              ("n_dst_pools", ctypes.c_int64), ("transfer_ranks", c_i32_p),
+              ("transfer_parallelism", c_i32_p), ("parallelism", ctypes.c_int32),
+              ("pad_", ctypes.c_int32), ("tags", ctypes.POINTER(ctypes.c_char_p)),
+              ("n_tags", ctypes.c_int64), ("dst_block_ids", c_i64_p),
+              ("n_dst_block_ids", ctypes.c_int64), ("dst_block_counts", c_i64_p),
+              ("n_dst_block_counts", ctypes.c_int64), ("dst_skip_bytes", c_i64_p),
+              ("n_dst_skip_bytes", ctypes.c_int64), ("decls", ctypes.POINTER(SpanDeclC)),
+              ("n_decls", ctypes.c_int64), ("unit_names", ctypes.POINTER(ctypes.c_char_p))]
+
+
+class ScheduleEntryC(ctypes.Structure):
+  _fields_ = [("src_block_id", ctypes.c_int64), ("dst_block_id", ctypes.c_int64),
+              ("src_offset_bytes", ctypes.c_int64), ("dst_offset_bytes", ctypes.c_int64),
+              ("size_bytes", ctypes.c_int64), ("pool_group", ctypes.c_int32),
+              ("pad_", ctypes.c_int32)]
+
+
 # name -> (restype, argtypes); every symbol declared in include/tpusync_b200.h
 _V = ctypes.c_void_p
 _SIGS = {
@@ -141,6 +178,22 @@ _SIGS = {
                                                    ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                                    ctypes.POINTER(LiveCopyChunkC),
                                                    ctypes.c_int64, c_i64_p]),
+    "ts_pool_reshard_plan_build": (ctypes.c_int, [ctypes.POINTER(PoolReshardRequestC),
+                                                  ctypes.POINTER(_V)]),
+    "ts_pool_reshard_plan_destroy": (None, [_V]),
+    "ts_pool_reshard_plan_info": (ctypes.c_int, [_V, c_i64_p]),
+    "ts_pool_reshard_plan_entries": (ctypes.c_int, [_V, ctypes.c_int64,
+                                                    ctypes.POINTER(ScheduleEntryC),
+                                                    ctypes.c_int64, c_i64_p]),
+    "ts_pool_reshard_plan_units": (ctypes.c_int, [_V, c_i64_p, c_i32_p]),
+    "ts_pool_reshard_plan_group": (ctypes.c_int, [_V, ctypes.c_int64, c_i64_p, c_i32_p, c_i64_p,
+                                                  c_i64_p]),
+    "ts_pool_reshard_program_create": (ctypes.c_int, [_V, ctypes.c_int64, ctypes.c_int, c_u64_p,
+                                                      c_u64_p, c_u64_p, c_u64_p, ctypes.c_int64,
+                                                      ctypes.POINTER(_V)]),
+    "ts_pool_reshard_program_info": (ctypes.c_int, [_V, c_i64_p, c_u64_p]),
+    "ts_pool_reshard_program_launch": (ctypes.c_int, [_V, _V, ctypes.c_int]),
+    "ts_pool_reshard_program_destroy": (None, [_V]),
     "ts_kv_extract": (ctypes.c_int, [ctypes.c_int, _V, ctypes.c_int, _V,
                                      ctypes.c_int64, _V, ctypes.c_uint64, _V, _V]),
     "ts_kv_insert": (ctypes.c_int, [ctypes.c_int, _V, ctypes.c_int, _V,

@@ -209,3 +209,47 @@ def store_transfer_streams(trace: np.ndarray, host_blocks: int, device_blocks: i
            "hit_rate": round(hits / max(hits + misses, 1), 4)}
   store.close()
   return batches, stats
+
+
+# ---------------------------------------------------------------------------
+# C3 hand-off as pools + byte-span declarations
+# ---------------------------------------------------------------------------
+
+def handoff_pool_plan_inputs(n_storages: int, src_table: np.ndarray, dst_table: np.ndarray,
+                             heads: int, head_bytes: int, src_tokens: int = 16,
+                             dst_tokens: int = 64):
+  """Pools and span declarations of the prefill -> decode KV hand-off.
+
+  One pool per (layer, K/V) storage, all tagged "kv": source pages of
+  `src_tokens` tokens, head-major ([head][token][head_bytes]); destination
+  pages of `dst_tokens` tokens, token-major ([token][head][head_bytes]).
+  src_table[q, p] / dst_table[q, P] are sequence q's page ids.  The single
+  source unit declares, per source page and head, one span of src_tokens
+  rows (one head vector each) at the head-major source stride and the
+  token-major destination stride, page-indexed (dst_space_version 0).
+  Returns (src_pools, dst_pools, dst_block_ids, registration).
+  """
+  from tpu_sync_b200.pool_layout import PoolSpec, RegionSpec
+  from tpu_sync_b200.pool_reshard import PoolByteSpan, PoolSpanRegistration
+  n_seqs, sbps = src_table.shape
+  dbps = dst_table.shape[1]
+  per = dst_tokens // src_tokens
+  sbb, dbb = src_tokens * heads * head_bytes, dst_tokens * heads * head_bytes
+  n_src_blocks = int(src_table.max()) + 1
+  n_dst_blocks = int(dst_table.max()) + 1
+  src_pools = [PoolSpec("kv", s, 0, sbb, n_src_blocks, (RegionSpec("page", 0, sbb, sbb, 1),))
+               for s in range(n_storages)]
+  dst_pools = [PoolSpec("kv", s, 0, dbb, n_dst_blocks, (RegionSpec("page", 0, dbb, dbb, 1),))
+               for s in range(n_storages)]
+  spans = []
+  for q in range(n_seqs):
+    for p in range(sbps):
+      for h in range(heads):
+        spans.append(PoolByteSpan(
+            src_block_ordinal=q * sbps + p, src_offset_bytes=h * src_tokens * head_bytes,
+            dst_block_index=q * dbps + p // per,
+            dst_offset_bytes=(p % per) * src_tokens * heads * head_bytes + h * head_bytes,
+            size_bytes=head_bytes, src_stride_bytes=head_bytes,
+            dst_stride_bytes=heads * head_bytes, count=src_tokens))
+  reg = PoolSpanRegistration("kv", [int(x) for x in src_table.reshape(-1)], spans)
+  return src_pools, dst_pools, [int(x) for x in dst_table.reshape(-1)], reg
