@@ -422,7 +422,51 @@ def run_handoff(torch, dist, rank, world, device, steps, warmup):
   dist.all_reduce(t, op=dist.ReduceOp.MAX)
   ms = float(t.item())
   moved = n_st * n_seqs * T * H * HB
+
+  # The same hand-off through the pool reshard planner: pools + span
+  # declarations -> plan entries -> one program launch per source GPU.
+  plan_ms = prog_ms = 0.0
+  n_tasks = 0
   if is_src:
+    from tpu_sync_b200 import pool_reshard, workloads
+    t0 = time.perf_counter()
+    src_pools, dst_pools, dst_ids, reg = workloads.handoff_pool_plan_inputs(
+        n_st, st_tab, dt_tab, H, HB)
+    plan = pool_reshard.build_pool_reshard_plan([src_pools], dst_pools, ["kv"], dst_ids,
+                                                [(0, reg)])
+    plan_ms = (time.perf_counter() - t0) * 1e3
+
+    class _Peer:  # one destination storage inside the imported mapping
+      def __init__(self, ptr, dev, nbytes):
+        self._p, self.device, self.dtype, self.shape = ptr, dev, torch.uint8, (nbytes,)
+
+      def data_ptr(self):
+        return self._p
+
+    peer = import_destinations(descs[rank + half], kernel_device=device.index)[0]
+    dst_st = [_Peer(peer.data_ptr() + s * storage_bytes, peer.device, storage_bytes)
+              for s in range(n_st)]
+    prog = pool_reshard.PoolReshardProgram(plan, 0, srcs, dst_st)
+    n_tasks = prog.n_tasks
+    for _ in range(warmup):
+      prog.launch()
+    torch.cuda.synchronize(device)
+  dist.barrier()
+  if is_src:
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+      prog.launch()
+    e1.record()
+    torch.cuda.synchronize(device)
+    prog_ms = e0.elapsed_time(e1) / steps
+  dist.barrier()
+  t = torch.tensor([prog_ms, plan_ms], dtype=torch.float64, device=device)
+  dist.all_reduce(t, op=dist.ReduceOp.MAX)
+  prog_ms, plan_ms = float(t[0].item()), float(t[1].item())
+  if is_src:
+    prog.close()
+    plan.close()
     peer = None
     close_imports(device.index)
   dist.barrier()
@@ -430,7 +474,81 @@ def run_handoff(torch, dist, rank, world, device, steps, warmup):
                     f"token-major, {half} pairs (GPU i -> i+{half})",
           "bytes_per_pair": moved, "ms": round(ms, 3),
           "nvlink_gbs_per_pair": round(moved / (ms * 1e-3) / 1e9, 1) if ms else None,
-          "frac_of_nvlink_770": round(moved / (ms * 1e-3) / 1e9 / 770.0, 3) if ms else None}
+          "frac_of_nvlink_770": round(moved / (ms * 1e-3) / 1e9 / 770.0, 3) if ms else None,
+          "pool_plan": {"how": "pool reshard planner (span declarations -> entries) + one "
+                               "program launch per source GPU",
+                        "plan_ms_cpu": round(plan_ms, 1), "tasks": n_tasks,
+                        "ms": round(prog_ms, 3),
+                        "nvlink_gbs_per_pair": round(moved / (prog_ms * 1e-3) / 1e9, 1)
+                        if prog_ms else None,
+                        "frac_of_nvlink_770": round(moved / (prog_ms * 1e-3) / 1e9 / 770.0, 3)
+                        if prog_ms else None}}
+
+
+def run_c2_fp8(torch, rank, device, steps, warmup, max_over_ranks):
+  """C2: Llama-3-70B TP8 KV shard (80 layers x K/V, 64-token blocks of 1 head
+  x 128 bf16 = 16 KiB per storage block) on an fp8 host tier: per step 256
+  random blocks (seed 20+rank) offloaded (fused bf16 -> e4m3 + per-block
+  scale) while the previous step's 256 are reloaded (dequantised) into other
+  blocks, both directions in flight.  GB/s counts the bf16 bytes moved."""
+  from tpu_sync_b200 import KVCacheManager, workloads
+  g = workloads.C2
+  B, nblk, host_blocks = workloads.C2_BATCH, 4096, 1024
+  full = torch.empty((g.layers, g.kv, nblk, g.block_tokens, g.heads, g.head_dim),
+                     dtype=torch.bfloat16, device=device)
+  gen = torch.Generator(device=device).manual_seed(20 + rank)
+  for l in range(g.layers):
+    full[l].normal_(generator=gen)
+  storages = [full[l, k] for l in range(g.layers) for k in range(g.kv)]
+  mgr = KVCacheManager([[t] for t in storages], host_blocks_to_allocate=host_blocks, fp8=True)
+  rng = np.random.default_rng(20 + rank)
+  n = warmup + steps + 1
+  out_ids = [rng.choice(nblk // 2, B, replace=False).astype(np.int64) for _ in range(n)]
+  in_ids = [nblk // 2 + rng.choice(nblk // 2, B, replace=False).astype(np.int64) for _ in range(n)]
+  host = [((np.arange(B) + i * B) % host_blocks).astype(np.int64) for i in range(n)]
+  stream = torch.cuda.Stream(device)
+
+  def step(i):
+    f1 = mgr.d2h(out_ids[i + 1], host[i + 1], stream=stream)
+    f2 = mgr.h2d(host[i], in_ids[i], stream=stream)
+    f1.stream_wait(stream)
+    f2.stream_wait(stream)
+    return f1, f2
+
+  mgr.d2h(out_ids[0], host[0], stream=stream).Await()
+  for i in range(warmup):
+    for f in step(i):
+      f.Await()
+  torch.cuda.synchronize(device)
+  mgr.set_profiling(True)
+  mgr.kernel_stats("extract")
+  mgr.kernel_stats("insert")
+  e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+  e0.record(stream)
+  futs = []
+  for i in range(warmup, warmup + steps):
+    futs.extend(step(i))
+  e1.record(stream)
+  torch.cuda.synchronize(device)
+  for f in futs:
+    f.Await()
+  ms = max_over_ranks(e0.elapsed_time(e1)) / steps
+  ext, ins = mgr.kernel_stats("extract"), mgr.kernel_stats("insert")
+  mgr.close()
+  bf16_bytes = 2 * B * g.block_bytes
+  wire = 2 * B * mgr.host_block_pitch
+
+  def kgbs(st):
+    return round(st["bytes"] / (st["ms"] * 1e-3) / 1e9, 1) if st["ms"] > 0 else None
+
+  return {"config": "C2 Llama-3-70B TP8 KV (80 layers x K/V, 64 tok x 1 head x 128 bf16 "
+                    f"blocks), {nblk}-block pool, fp8 e4m3 host tier of {host_blocks} blocks, "
+                    f"{B} offloads + {B} reloads per step",
+          "ms_per_step": round(ms, 3),
+          "bf16_gbs": round(bf16_bytes / (ms * 1e-3) / 1e9, 2),
+          "pcie_gbs": round(wire / (ms * 1e-3) / 1e9, 2),
+          "extract_fp8_kernel_gbs": kgbs(ext), "insert_fp8_kernel_gbs": kgbs(ins),
+          "kernel_launches": ext["launches"] + ins["launches"]}
 
 
 def run_ours(args):
@@ -655,6 +773,10 @@ def run_ours(args):
   mgr.close()
   del mgr, full, storages, table
   torch.cuda.empty_cache()
+  c2 = run_c2_fp8(torch, rank, device, 5, 3, max_over_ranks)
+  torch.cuda.empty_cache()
+  if rank == 0:
+    line["c2_fp8"] = c2
   exchange = {}
   if world >= 2 and world % 2 == 0 and not args.no_exchange:
     exchange["weight_sync"] = run_weight_sync(torch, dist, rank, world, device, 3, 2)
@@ -677,6 +799,33 @@ def run_kernel_case(args):
 
   from tpu_sync_b200 import ops, workloads
   device = torch.device("cuda", 0)
+  if args.kernel_case == "pool_reshard":
+    # C3 hand-off plan for 16 of the 64 storages, destination on this GPU:
+    # 2 GiB read + 2 GiB written per launch, 4 launches.
+    from tpu_sync_b200 import pool_reshard
+    n_st, n_seqs, T, H, HB = 16, 8, 32768, 2, 256
+    rng = np.random.default_rng(30)
+    st = rng.permutation(n_seqs * T // 16).reshape(n_seqs, -1).astype(np.int32)
+    dt = rng.permutation(n_seqs * T // 64).reshape(n_seqs, -1).astype(np.int32)
+    sp, dp, ids, reg = workloads.handoff_pool_plan_inputs(n_st, st, dt, H, HB)
+    plan = pool_reshard.build_pool_reshard_plan([sp], dp, ["kv"], ids, [(0, reg)])
+    src = [torch.randint(0, 256, (n_seqs * T // 16, 16 * H * HB), dtype=torch.uint8,
+                         device=device) for _ in range(n_st)]
+    dst = [torch.empty((n_seqs * T // 64, 64 * H * HB), dtype=torch.uint8, device=device)
+           for _ in range(n_st)]
+    prog = pool_reshard.PoolReshardProgram(plan, 0, src, dst)
+    ms = []
+    for i in range(4):
+      a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+      a.record()
+      prog.launch()
+      b.record()
+      torch.cuda.synchronize()
+      ms.append(a.elapsed_time(b))
+    print(json.dumps({"kernel_case": "pool_reshard", "tasks": prog.n_tasks, "bytes": prog.bytes,
+                      "ms": [round(x, 3) for x in ms],
+                      "hbm_gbs": round(2 * prog.bytes / (min(ms) * 1e-3) / 1e9, 1)}))
+    return
   g = workloads.C1 if not args.kernel_case.endswith("fp8") else workloads.C2
   blocks = 1024 if g is workloads.C1 else 2048
   full = torch.empty((g.layers, g.kv, blocks, g.block_tokens, g.heads, g.head_dim),
