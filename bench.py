@@ -62,7 +62,7 @@ def parse():
   p.add_argument("--no-exchange", action="store_true",
                  help="skip the N>=2 weight-sync and hand-off measurements")
   p.add_argument("--kernel-case", default="",
-                 choices=["", "extract", "insert", "extract_fp8", "insert_fp8"],
+                 choices=["", "extract", "insert", "extract_fp8", "insert_fp8", "pool_reshard"],
                  help="run a few launches of one kernel on a small case (for ncu)")
   return p.parse_args()
 
