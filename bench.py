@@ -99,6 +99,12 @@ def cpu_model() -> str:
 # ---------------------------------------------------------------------------
 
 class ClockSampler:
+  """nvidia-smi clock / throttle samples (every 50 ms) around a timed region.
+
+  start() returns once the first sample has arrived, so the sampler is live
+  before the region begins; begin() / end() bracket the region; stop() waits
+  for one sample after the region and summarises those taken inside it (plus
+  that one)."""
   QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
            "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
            "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -106,34 +112,54 @@ class ClockSampler:
   def __init__(self, device_index: int):
     self.dev = device_index
     self.proc = None
-    self.lines = []
+    self.lines = []  # (monotonic time, csv line)
+    self.t0 = self.t1 = None
 
   def start(self):
     try:
       self.proc = subprocess.Popen(
           ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-           "-lms", "200", "-i", str(self.dev)], stdout=subprocess.PIPE,
+           "-lms", "50", "-i", str(self.dev)], stdout=subprocess.PIPE,
           stderr=subprocess.DEVNULL, text=True)
       self.thread = threading.Thread(target=self._read, daemon=True)
       self.thread.start()
     except OSError:
       self.proc = None
+      return
+    deadline = time.monotonic() + 10.0
+    while not self.lines and time.monotonic() < deadline and self.proc.poll() is None:
+      time.sleep(0.01)
+
+  def begin(self):
+    self.t0 = time.monotonic()
+
+  def end(self):
+    self.t1 = time.monotonic()
 
   def _read(self):
     for line in self.proc.stdout:
-      self.lines.append(line.strip())
+      self.lines.append((time.monotonic(), line.strip()))
 
   def stop(self):
     if self.proc is None:
       return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+    t1 = self.t1 if self.t1 is not None else time.monotonic()
+    t0 = self.t0 if self.t0 is not None else t1
+    deadline = time.monotonic() + 2.0
+    while (not any(t > t1 for t, _ in self.lines) and time.monotonic() < deadline
+           and self.proc.poll() is None):
+      time.sleep(0.01)
     self.proc.terminate()
     try:
       self.proc.wait(timeout=5)
     except subprocess.TimeoutExpired:
       self.proc.kill()
+    after = [t for t, _ in self.lines if t > t1]
+    t_hi = min(after) if after else t1
+    window = [l for t, l in self.lines if t0 <= t <= t_hi]
     sm, smax, reasons = [], None, set()
     names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-    for line in self.lines:
+    for line in window:
       f = [x.strip() for x in line.split(",")]
       if len(f) < 9:
         continue
@@ -622,13 +648,14 @@ def run_ours(args):
     for f in step(plans[i], bench_stream):
       f.Await()
   torch.cuda.synchronize(device)
+  clocks = ClockSampler(device.index)
+  clocks.start()  # live before the barrier, so every rank's region is sampled
   barrier()
   torch.cuda.synchronize(device)
   mgr.set_profiling(True)
   mgr.kernel_stats("extract")
   mgr.kernel_stats("insert")
-  clocks = ClockSampler(device.index)
-  clocks.start()
+  clocks.begin()
   e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
   e0.record(bench_stream)
   futs = []
@@ -636,6 +663,7 @@ def run_ours(args):
     futs.extend(step(plans[i], bench_stream))
   e1.record(bench_stream)
   torch.cuda.synchronize(device)
+  clocks.end()
   clock_info = clocks.stop()
   barrier()
   for f in futs:
