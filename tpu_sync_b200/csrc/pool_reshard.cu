@@ -79,9 +79,10 @@ struct PoolBase {
 struct ts_pool_reshard_program {
   int device = 0;
   struct Group {
-    tsb::RelTask* d_tasks = nullptr;
+    tsb::RelTask* d_tasks = nullptr;  // sorted by access width: 16-, 4-, 1-byte tasks
     tsb::PoolBase* d_pools = nullptr;
     int64_t n_tasks = 0, n_pools = 0;
+    int64_t n16 = 0, n4 = 0;          // tasks of the first two widths
   };
   std::vector<Group> groups;
   int64_t n_tasks = 0;  // tasks x pools over all groups
@@ -570,35 +571,59 @@ void push_split(std::vector<RelTask>* out, const RelTask& t) {
 }
 
 // One warp per (pool, task) item; rows and access words flattened across
-// the lanes, eight loads in flight per lane before its stores.
+// the lanes, eight loads in flight per lane before its stores.  A lane walks
+// its elements (lane, lane + 32, ...) by keeping its column and byte offset
+// and advancing 32 elements with two adds and one wrap test -- no division
+// or multiply per element; the store pass repeats the same walk.
 template <typename W>
 __device__ __forceinline__ void copy_rows(uint64_t src, uint64_t dst, const RelTask& t, int lane) {
-  const uint32_t per_row = t.bytes / uint32_t(sizeof(W));
+  constexpr int64_t kW = int64_t(sizeof(W));
+  const uint32_t per_row = t.bytes / uint32_t(kW);
   const uint32_t total = per_row * t.count;
+  const uint32_t adv_c = 32u % per_row, adv_r = 32u / per_row;
+  const int64_t s_adv = int64_t(adv_r) * t.src_stride + int64_t(adv_c) * kW;
+  const int64_t d_adv = int64_t(adv_r) * t.dst_stride + int64_t(adv_c) * kW;
+  const int64_t s_wrap = t.src_stride - int64_t(per_row) * kW;
+  const int64_t d_wrap = t.dst_stride - int64_t(per_row) * kW;
+  uint32_t col0 = uint32_t(lane) % per_row;
+  const uint32_t row0 = uint32_t(lane) / per_row;
+  int64_t s0 = int64_t(row0) * t.src_stride + int64_t(col0) * kW;
+  int64_t d0 = int64_t(row0) * t.dst_stride + int64_t(col0) * kW;
   for (uint32_t base = 0; base < total; base += 256) {
     W v[8];
+    uint32_t col = col0;
+    int64_t so = s0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const uint32_t k = base + uint32_t(lane + 32 * i);
-      if (k < total) {
-        const uint32_t row = k / per_row, col = k - row * per_row;
-        v[i] = *reinterpret_cast<const W*>(src + uint64_t(int64_t(row) * t.src_stride) +
-                                           uint64_t(col) * sizeof(W));
+      if (base + uint32_t(lane + 32 * i) < total) v[i] = *reinterpret_cast<const W*>(src + so);
+      col += adv_c;
+      so += s_adv;
+      if (col >= per_row) {
+        col -= per_row;
+        so += s_wrap;
       }
     }
+    col = col0;
+    int64_t dof = d0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const uint32_t k = base + uint32_t(lane + 32 * i);
-      if (k < total) {
-        const uint32_t row = k / per_row, col = k - row * per_row;
-        *reinterpret_cast<W*>(dst + uint64_t(int64_t(row) * t.dst_stride) +
-                              uint64_t(col) * sizeof(W)) = v[i];
+      if (base + uint32_t(lane + 32 * i) < total) *reinterpret_cast<W*>(dst + dof) = v[i];
+      col += adv_c;
+      dof += d_adv;
+      if (col >= per_row) {
+        col -= per_row;
+        dof += d_wrap;
       }
     }
+    col0 = col;
+    s0 = so;
+    d0 = dof;
   }
 }
 
-__global__ void __launch_bounds__(kThreads)
+// 16-byte path: 80 registers (3 CTAs per SM); narrower paths fit 4.
+template <typename W>
+__global__ void __launch_bounds__(kThreads, sizeof(W) == 16 ? 3 : 4)
     pool_reshard_kernel(const RelTask* __restrict__ tasks, int64_t n_tasks,
                         const PoolBase* __restrict__ pools, int64_t n_pools) {
   const int lane = threadIdx.x & 31;
@@ -609,14 +634,18 @@ __global__ void __launch_bounds__(kThreads)
     const int64_t p = i / n_tasks;
     const RelTask t = tasks[i - p * n_tasks];
     const PoolBase pb = pools[p];
-    const uint64_t src = pb.src + uint64_t(t.src_block * pb.src_stride + t.src_off);
-    const uint64_t dst = pb.dst + uint64_t(t.dst_block * pb.dst_stride + t.dst_off);
-    const uint64_t bits = src | dst | uint64_t(t.src_stride) | uint64_t(t.dst_stride) |
-                          uint64_t(t.bytes);
-    if ((bits & 15) == 0) copy_rows<int4>(src, dst, t, lane);
-    else if ((bits & 3) == 0) copy_rows<uint32_t>(src, dst, t, lane);
-    else copy_rows<uint8_t>(src, dst, t, lane);
+    copy_rows<W>(pb.src + uint64_t(t.src_block * pb.src_stride + t.src_off),
+                 pb.dst + uint64_t(t.dst_block * pb.dst_stride + t.dst_off), t, lane);
   }
+}
+
+// Widest access (16, 4 or 1 bytes) every address of `t` allows in every pool
+// of the group.
+int task_class(const RelTask& t, uint64_t pool_bits) {
+  const uint64_t bits = pool_bits | uint64_t(t.src_off) |
+                        uint64_t(t.dst_off) | uint64_t(t.src_stride) | uint64_t(t.dst_stride) |
+                        uint64_t(t.bytes);
+  return (bits & 15) == 0 ? 16 : (bits & 3) == 0 ? 4 : 1;
 }
 
 }  // namespace
@@ -788,9 +817,22 @@ extern "C" int ts_pool_reshard_program_create(const ts_pool_reshard_plan* plan, 
                        dst_storage_ptrs[dp.storage_index] + uint64_t(dp.base_offset_bytes),
                        sp.block_stride_bytes, dp.block_stride_bytes});
     }
+    // Block-0 addresses and block strides of every pool enter each task's
+    // addresses, so they bound the access width of all of the group's tasks.
+    uint64_t pool_bits = 0;
+    for (const tsb::PoolBase& pb : bases)
+      pool_bits |= pb.src | pb.dst | uint64_t(pb.src_stride) | uint64_t(pb.dst_stride);
+    std::stable_sort(tasks.begin(), tasks.end(), [&](const tsb::RelTask& a, const tsb::RelTask& b) {
+      return tsb::task_class(a, pool_bits) > tsb::task_class(b, pool_bits);
+    });
     ts_pool_reshard_program::Group g;
     g.n_tasks = int64_t(tasks.size());
     g.n_pools = int64_t(bases.size());
+    for (const tsb::RelTask& t : tasks) {
+      const int c = tsb::task_class(t, pool_bits);
+      g.n16 += c == 16;
+      g.n4 += c == 4;
+    }
     cudaError_t e = cudaMalloc(&g.d_tasks, sizeof(tsb::RelTask) * tasks.size());
     if (e == cudaSuccess) e = cudaMalloc(&g.d_pools, sizeof(tsb::PoolBase) * bases.size());
     if (e == cudaSuccess)
@@ -823,17 +865,30 @@ extern "C" int ts_pool_reshard_program_launch(ts_pool_reshard_program* prog, voi
   if (!prog) return set_error(TS_INVALID_ARGUMENT, "null program");
   tsb::DeviceGuard g(prog->device);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  int cap = tsb::sm_count(prog->device) * 4;
+  int cap = tsb::sm_count(prog->device) * 3;
   if (max_ctas > 0) cap = std::min(cap, max_ctas);
   for (const auto& grp : prog->groups) {
-    const int64_t items = grp.n_tasks * grp.n_pools;
-    if (items == 0) continue;
-    const int64_t want = (items + (tsb::kThreads / 32) - 1) / (tsb::kThreads / 32);
-    const int ctas = int(std::max<int64_t>(1, std::min<int64_t>(want, cap)));
-    tsb::pool_reshard_kernel<<<ctas, tsb::kThreads, 0, s>>>(grp.d_tasks, grp.n_tasks,
-                                                             grp.d_pools, grp.n_pools);
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return tsb::cuda_error(e, "pool reshard launch");
+    const int64_t n1 = grp.n_tasks - grp.n16 - grp.n4;
+    const tsb::RelTask* part[3] = {grp.d_tasks, grp.d_tasks + grp.n16,
+                                   grp.d_tasks + grp.n16 + grp.n4};
+    const int64_t count[3] = {grp.n16, grp.n4, n1};
+    for (int c = 0; c < 3; ++c) {
+      const int64_t items = count[c] * grp.n_pools;
+      if (items == 0) continue;
+      const int64_t want = (items + (tsb::kThreads / 32) - 1) / (tsb::kThreads / 32);
+      const int ctas = int(std::max<int64_t>(1, std::min<int64_t>(want, cap)));
+      if (c == 0)
+        tsb::pool_reshard_kernel<int4><<<ctas, tsb::kThreads, 0, s>>>(part[c], count[c],
+                                                                       grp.d_pools, grp.n_pools);
+      else if (c == 1)
+        tsb::pool_reshard_kernel<uint32_t><<<ctas, tsb::kThreads, 0, s>>>(
+            part[c], count[c], grp.d_pools, grp.n_pools);
+      else
+        tsb::pool_reshard_kernel<uint8_t><<<ctas, tsb::kThreads, 0, s>>>(
+            part[c], count[c], grp.d_pools, grp.n_pools);
+      const cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return tsb::cuda_error(e, "pool reshard launch");
+    }
   }
   return TS_OK;
 }
