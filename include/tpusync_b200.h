@@ -229,6 +229,74 @@ TS_API int ts_pool_reshard_plan_group(const ts_pool_reshard_plan* plan, int64_t 
                                       int64_t* sizes, int32_t* pool_indices, int64_t* dst_ids,
                                       int64_t* extents);
 
+/* Plans that arrive from a controller (the data fields of StartTransferRequest
+ * with its ShardPushEntryProto / PoolGroup lists,
+ * tpu_sync/rpc/raiden_service.proto).  dst_peer is an id for the entry's
+ * destination endpoint (< 0 stands for an empty address); source_rank is the
+ * entry's shard_push_schedules key. */
+typedef struct ts_received_entry {
+  int32_t source_rank;
+  int32_t dst_peer;
+  int64_t dst_shard_idx;
+  int64_t src_block_id;
+  int64_t dst_block_id;
+  int64_t src_offset_bytes;
+  int64_t dst_offset_bytes;
+  int64_t size_bytes;
+  int64_t src_stride_bytes;
+  int64_t dst_stride_bytes;
+  int32_t count;
+  int32_t pool_group;
+} ts_received_entry;
+
+typedef struct ts_received_group {
+  const int32_t* pool_indices;
+  int64_t n_pool_indices;
+  const int64_t* dst_block_ids;
+  int64_t n_dst_block_ids;
+  const int64_t* extents;            /* dst_expected_extent_bytes */
+  int64_t n_extents;
+  int32_t expected_pushes;
+  int32_t order_rank;
+} ts_received_group;
+
+typedef struct ts_received_plan {
+  const int32_t* transfer_pool_indices;
+  int64_t n_transfer_pools;
+  const char* const* pool_dtype_tags;  /* one per pool of the local table */
+  int64_t n_pool_dtype_tags;
+  const ts_received_group* groups;
+  int64_t n_groups;
+  const ts_received_entry* entries;    /* all schedules' entries */
+  int64_t n_entries;
+  int64_t n_schedules;                 /* number of shard_push_schedules keys */
+  int32_t parallelism;
+  int32_t pad_;
+} ts_received_plan;
+
+/* The executor's checks of a received plan against the local pool table:
+ * ValidatePoolReshardPlan and, for a receiver, the exact-coverage and push
+ * accounting of ValidatePoolReshardReceiverCoverage
+ * (tpu_sync/core/kv_cache_manager_with_transfer.cc:742-1150); same codes and
+ * messages.  The transport identity fields (req_id, uuid, use_block_chunks)
+ * are the control plane's and are not checked here. */
+TS_API int ts_pool_reshard_validate(const ts_received_plan* plan,
+                                    const ts_pool_spec* local_pools, int64_t n_local_pools,
+                                    int64_t num_shards, const int64_t* local_block_ids,
+                                    int64_t n_local_block_ids, int is_sender);
+/* An executable plan from a received one: runs the sender's checks against
+ * src_pools / src_block_ids and the receiver's against dst_pools /
+ * dst_block_ids (messages prefixed "sender: " / "receiver: "), so every
+ * entry of the result lies inside both sides' declared pool regions. */
+TS_API int ts_pool_reshard_plan_from_received(const ts_received_plan* plan,
+                                              const ts_pool_spec* src_pools,
+                                              const ts_pool_spec* dst_pools, int64_t n_pools,
+                                              const int64_t* src_block_ids,
+                                              int64_t n_src_block_ids,
+                                              const int64_t* dst_block_ids,
+                                              int64_t n_dst_block_ids, int64_t dst_num_shards,
+                                              ts_pool_reshard_plan** out);
+
 /* Pool reshard execution: replaces PoolReshardPush / StartPoolReshardPush /
  * OnPoolReceived + H2dPoolBlocks (D2H, TCP push, H2D;
  * tpu_sync/core/kv_cache_manager_with_transfer.cc:1152-1335, :2665-2805) by

@@ -114,3 +114,47 @@ def test_program_rejects_storages_smaller_than_pools():
   small = torch.zeros((64 * 2 * 64) - 1, dtype=torch.uint8, device=dev)
   with pytest.raises(RuntimeError, match="destination pool kv exceeds storage bytes"):
     PoolReshardProgram(plan, 0, [src], [small])
+
+
+def test_received_plan_with_repeating_entries_matches_relayout():
+  """A controller-style plan (entries with count / strides, as
+  ShardPushEntryProto carries them) validated on both ends and executed."""
+  from tpu_sync_b200.pool_reshard import plan_from_received
+  dev = gpu()
+  rng = np.random.default_rng(12)
+  n_st, n_seqs, T, H, HB = 2, 2, 256, 2, 128
+  sbps, dbps = T // 16, T // 64
+  st = rng.permutation(n_seqs * sbps).reshape(n_seqs, sbps).astype(np.int32)
+  dt = rng.permutation(n_seqs * dbps).reshape(n_seqs, dbps).astype(np.int32)
+  src_pools, dst_pools, _, _ = workloads.handoff_pool_plan_inputs(n_st, st, dt, H, HB)
+  entries = []
+  for q in range(n_seqs):
+    for p in range(sbps):
+      for h in range(H):
+        entries.append(dict(dst_peer="decode:0", dst_shard_idx=0, src_block_id=int(st[q, p]),
+                            dst_block_id=int(dt[q, p // 4]), src_offset_bytes=h * 16 * HB,
+                            dst_offset_bytes=(p % 4) * 16 * H * HB + h * HB, size_bytes=HB,
+                            src_stride_bytes=HB, dst_stride_bytes=H * HB, count=16,
+                            pool_group=0))
+  recv = {"transfer_pool_indices": list(range(n_st)), "pool_dtype_tags": [""] * n_st,
+          "parallelism": 1,
+          "pool_groups": [{"pool_indices": list(range(n_st)),
+                           "dst_device_block_ids": [int(x) for x in dt.reshape(-1)],
+                           "dst_expected_extent_bytes": [64 * H * HB] * (n_seqs * dbps),
+                           "expected_pushes": 1, "order_rank": 0}],
+          "shard_push_schedules": {0: entries}}
+  plan = plan_from_received(recv, src_pools, dst_pools, [int(x) for x in st.reshape(-1)],
+                            [int(x) for x in dt.reshape(-1)])
+  g = torch.Generator().manual_seed(3)
+  src = [torch.randint(0, 256, (n_seqs * sbps, 16 * H * HB), generator=g,
+                       dtype=torch.uint8).to(dev) for _ in range(n_st)]
+  dst = [torch.zeros((n_seqs * dbps, 64 * H * HB), dtype=torch.uint8, device=dev)
+         for _ in range(n_st)]
+  PoolReshardProgram(plan, 0, src, dst).launch()
+  torch.cuda.synchronize()
+  sg = dict(block_tokens=16, heads=H, head_bytes=HB, head_major=1)
+  dg = dict(block_tokens=64, heads=H, head_bytes=HB, head_major=0)
+  for s in range(n_st):
+    want = np.zeros((n_seqs * dbps, 64 * H * HB), np.uint8)
+    ors.relayout(src[s].cpu().numpy(), want, sg, dg, st, dt, T)
+    np.testing.assert_array_equal(dst[s].cpu().numpy(), want)

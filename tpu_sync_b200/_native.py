@@ -150,6 +150,31 @@ class ScheduleEntryC(ctypes.Structure):
               ("pad_", ctypes.c_int32)]
 
 
+class ReceivedEntryC(ctypes.Structure):
+  _fields_ = [("source_rank", ctypes.c_int32), ("dst_peer", ctypes.c_int32),
+              ("dst_shard_idx", ctypes.c_int64), ("src_block_id", ctypes.c_int64),
+              ("dst_block_id", ctypes.c_int64), ("src_offset_bytes", ctypes.c_int64),
+              ("dst_offset_bytes", ctypes.c_int64), ("size_bytes", ctypes.c_int64),
+              ("src_stride_bytes", ctypes.c_int64), ("dst_stride_bytes", ctypes.c_int64),
+              ("count", ctypes.c_int32), ("pool_group", ctypes.c_int32)]
+
+
+class ReceivedGroupC(ctypes.Structure):
+  _fields_ = [("pool_indices", c_i32_p), ("n_pool_indices", ctypes.c_int64),
+              ("dst_block_ids", c_i64_p), ("n_dst_block_ids", ctypes.c_int64),
+              ("extents", c_i64_p), ("n_extents", ctypes.c_int64),
+              ("expected_pushes", ctypes.c_int32), ("order_rank", ctypes.c_int32)]
+
+
+class ReceivedPlanC(ctypes.Structure):
+  _fields_ = [("transfer_pool_indices", c_i32_p), ("n_transfer_pools", ctypes.c_int64),
+              ("pool_dtype_tags", ctypes.POINTER(ctypes.c_char_p)),
+              ("n_pool_dtype_tags", ctypes.c_int64), ("groups", ctypes.POINTER(ReceivedGroupC)),
+              ("n_groups", ctypes.c_int64), ("entries", ctypes.POINTER(ReceivedEntryC)),
+              ("n_entries", ctypes.c_int64), ("n_schedules", ctypes.c_int64),
+              ("parallelism", ctypes.c_int32), ("pad_", ctypes.c_int32)]
+
+
 # name -> (restype, argtypes); every symbol declared in include/tpusync_b200.h
 _V = ctypes.c_void_p
 _SIGS = {
@@ -188,6 +213,16 @@ _SIGS = {
     "ts_pool_reshard_plan_units": (ctypes.c_int, [_V, c_i64_p, c_i32_p]),
     "ts_pool_reshard_plan_group": (ctypes.c_int, [_V, ctypes.c_int64, c_i64_p, c_i32_p, c_i64_p,
                                                   c_i64_p]),
+    "ts_pool_reshard_validate": (ctypes.c_int, [ctypes.POINTER(ReceivedPlanC),
+                                                ctypes.POINTER(PoolSpecC), ctypes.c_int64,
+                                                ctypes.c_int64, c_i64_p, ctypes.c_int64,
+                                                ctypes.c_int]),
+    "ts_pool_reshard_plan_from_received": (ctypes.c_int, [ctypes.POINTER(ReceivedPlanC),
+                                                          ctypes.POINTER(PoolSpecC),
+                                                          ctypes.POINTER(PoolSpecC),
+                                                          ctypes.c_int64, c_i64_p, ctypes.c_int64,
+                                                          c_i64_p, ctypes.c_int64, ctypes.c_int64,
+                                                          ctypes.POINTER(_V)]),
     "ts_pool_reshard_program_create": (ctypes.c_int, [_V, ctypes.c_int64, ctypes.c_int, c_u64_p,
                                                       c_u64_p, c_u64_p, c_u64_p, ctypes.c_int64,
                                                       ctypes.POINTER(_V)]),

@@ -41,6 +41,8 @@ struct ts_pool_reshard_plan {
   struct Entry {
     int64_t src_block, dst_block, src_off, dst_off, size;
     int32_t group;
+    int64_t src_stride = 0, dst_stride = 0;  // received plans: count repeats
+    int32_t count = 1;
   };
   struct Group {
     std::vector<int32_t> pools;
@@ -648,6 +650,297 @@ int task_class(const RelTask& t, uint64_t pool_bits) {
   return (bits & 15) == 0 ? 16 : (bits & 3) == 0 ? 4 : 1;
 }
 
+// ---------------------------------------------------------------------------
+// Plans that arrive from a controller: the executor's own checks
+// (ValidatePoolReshardPlan + ValidatePoolReshardReceiverCoverage,
+// tpu_sync/core/kv_cache_manager_with_transfer.cc:742-1150) against the local
+// pool table.  The transport identity checks (req_id, uuid,
+// use_block_chunks) belong to the control plane and are not repeated.
+// ---------------------------------------------------------------------------
+
+// StridedSpanFitsBlock / StridedSpanFitsRegions (:115-142).
+bool span_fits_block(int64_t off, int64_t stride, int64_t size, int64_t count, int64_t block) {
+  if (off < 0 || stride < 0 || size <= 0 || count <= 0 || block <= 0 || off > block ||
+      size > block - off)
+    return false;
+  if (count == 1) return true;
+  const int64_t remaining = block - off - size;
+  return stride <= remaining / (count - 1);
+}
+
+bool span_fits_regions(int64_t off, int64_t stride, int64_t size, int64_t count,
+                       const pool::Pool& p) {
+  if (!span_fits_block(off, stride, size, count, p.block_stride_bytes)) return false;
+  for (int64_t r = 0; r < count; ++r) {
+    const int64_t start = off + r * stride;
+    if (!pool::regions_cover_range(p.regions, uint64_t(start), uint64_t(start + size)))
+      return false;
+  }
+  return true;
+}
+
+int receiver_coverage(const ts_received_plan* rp, const std::vector<pool::Pool>& pools) {
+  constexpr int64_t kMaxRepeats = int64_t{1} << 20;
+  std::set<int64_t> grouped;
+  for (int64_t g = 0; g < rp->n_groups; ++g)
+    for (int64_t i = 0; i < rp->groups[g].n_pool_indices; ++i) {
+      const int32_t pi = rp->groups[g].pool_indices[i];
+      if (pi < 0 || !grouped.insert(pi).second)
+        return set_error(TS_INVALID_ARGUMENT, "group pool indices must be unique and non-negative");
+    }
+  bool partition = int64_t(grouped.size()) == rp->n_transfer_pools;
+  for (int64_t i = 0; partition && i < rp->n_transfer_pools; ++i)
+    partition = grouped.count(rp->transfer_pool_indices[i]) > 0;
+  if (!partition)
+    return set_error(TS_INVALID_ARGUMENT,
+                     "group pool indices do not partition the plan's transfer pools");
+  const int64_t par = rp->parallelism;
+  if (par <= 0)
+    return set_error(TS_INVALID_ARGUMENT,
+                     "receiver plans require positive parallelism for push accounting");
+  struct State {
+    std::vector<ts_live_segment> seg;
+    int64_t live = 0;
+    std::map<int64_t, size_t> ordinal;
+    std::vector<std::vector<std::pair<int64_t, int64_t>>> cov;
+    std::map<int32_t, std::set<std::tuple<int32_t, int64_t, int64_t>>> pairs;
+  };
+  std::vector<State> st(size_t(rp->n_groups));
+  for (int64_t g = 0; g < rp->n_groups; ++g) {
+    const ts_received_group& grp = rp->groups[g];
+    State& s = st[size_t(g)];
+    if (grp.n_pool_indices == 0)
+      return set_error(TS_INVALID_ARGUMENT, "group " + S(g) + " declares no pools");
+    for (int64_t i = 0; i < grp.n_pool_indices; ++i) {
+      const int32_t pi = grp.pool_indices[i];
+      if (pi >= int32_t(pools.size()))
+        return set_error(TS_INVALID_ARGUMENT, "group pool index out of range: " + S(pi));
+      std::vector<ts_live_segment> seg;
+      int rc = pool::live_segments(pools[size_t(pi)], &seg);
+      if (rc != TS_OK) return rc;
+      if (s.seg.empty()) {
+        s.seg = seg;
+      } else if (!same_segments(s.seg, seg)) {
+        return set_error(TS_INVALID_ARGUMENT, "group " + S(g) +
+                                                  " pools must share one live-region map; pool " +
+                                                  S(pi) + " disagrees");
+      }
+    }
+    for (const auto& x : s.seg) s.live += x.size;
+    if (s.live <= 0)
+      return set_error(TS_INVALID_ARGUMENT, "group " + S(g) + " has no live destination bytes");
+    if (grp.n_extents == 0)
+      return set_error(TS_INVALID_ARGUMENT, "receiver plans require dst_expected_extent_bytes");
+    if (grp.n_extents != grp.n_dst_block_ids)
+      return set_error(TS_INVALID_ARGUMENT, "group " + S(g) +
+                                                " extents do not match its destination block "
+                                                "count: got " + S(grp.n_extents) +
+                                                ", expected " + S(grp.n_dst_block_ids));
+    for (int64_t o = 0; o < grp.n_extents; ++o) {
+      const int64_t e = grp.extents[o];
+      if (e <= 0 || e > s.live)
+        return set_error(TS_INVALID_ARGUMENT, "extent " + S(e) + " for destination block ordinal " +
+                                                  S(o) + " of group " + S(g) +
+                                                  " is outside (0, " + S(s.live) + "]");
+      if (o != grp.n_extents - 1 && e != s.live)
+        return set_error(TS_INVALID_ARGUMENT,
+                         "extents must cover every destination block fully except the final one");
+    }
+    for (int64_t o = 0; o < grp.n_dst_block_ids; ++o) s.ordinal[grp.dst_block_ids[o]] = size_t(o);
+    s.cov.resize(size_t(grp.n_dst_block_ids));
+  }
+  int64_t repeats = 0;
+  for (int64_t i = 0; i < rp->n_entries; ++i) {
+    const ts_received_entry& e = rp->entries[i];
+    if (e.pool_group < 0 || e.pool_group >= rp->n_groups)
+      return set_error(TS_INVALID_ARGUMENT,
+                       "reshard entry declares an unknown pool group " + S(e.pool_group));
+    State& s = st[size_t(e.pool_group)];
+    auto it = s.ordinal.find(e.dst_block_id);
+    if (it == s.ordinal.end())
+      return set_error(TS_INVALID_ARGUMENT, "reshard entry targets destination block " +
+                                                S(e.dst_block_id) + " outside its group " +
+                                                S(e.pool_group) + " destination set");
+    const int64_t extent = rp->groups[e.pool_group].extents[it->second];
+    repeats += e.count;
+    if (repeats > kMaxRepeats)
+      return set_error(TS_INVALID_ARGUMENT, "receiver plan exceeds the repeat expansion bound");
+    for (int64_t r = 0; r < e.count; ++r) {
+      int64_t a = 0, b = 0;
+      if (pool::physical_to_logical(s.seg.data(), int64_t(s.seg.size()),
+                                    e.dst_offset_bytes + r * e.dst_stride_bytes, e.size_bytes, &a,
+                                    &b) != TS_OK)
+        return set_error(TS_INVALID_ARGUMENT, "reshard entry for destination block " +
+                                                  S(e.dst_block_id) +
+                                                  " crosses padding or lies outside declared live "
+                                                  "regions: " + ts_last_error());
+      if (b > extent)
+        return set_error(TS_INVALID_ARGUMENT, "reshard entry exceeds destination block " +
+                                                  S(e.dst_block_id) + " declared live tail: end=" +
+                                                  S(b) + " extent=" + S(extent));
+      s.cov[it->second].emplace_back(a, b);
+    }
+    s.pairs[e.source_rank].insert({e.dst_peer, e.src_block_id, e.dst_block_id});
+  }
+  for (int64_t g = 0; g < rp->n_groups; ++g) {
+    State& s = st[size_t(g)];
+    const ts_received_group& grp = rp->groups[g];
+    int64_t pushes = 0;
+    for (const auto& [rank, pr] : s.pairs) pushes += std::min(par, int64_t(pr.size()));
+    if (pushes != grp.expected_pushes)
+      return set_error(TS_INVALID_ARGUMENT, "expected pushes for group " + S(g) +
+                                                " do not match the received schedules: declared=" +
+                                                S(grp.expected_pushes) +
+                                                " recomputed=" + S(pushes));
+    for (int64_t o = 0; o < grp.n_dst_block_ids; ++o) {
+      auto& iv = s.cov[size_t(o)];
+      std::sort(iv.begin(), iv.end());
+      int64_t until = 0;
+      for (const auto& [a, b] : iv) {
+        if (a != until)
+          return set_error(TS_INVALID_ARGUMENT,
+                           std::string("receiver schedule has a destination coverage ") +
+                               (a < until ? "overlap" : "gap") + " for block " +
+                               S(grp.dst_block_ids[o]) + " at byte " + S(a));
+        until = b;
+      }
+      if (until != grp.extents[o])
+        return set_error(TS_INVALID_ARGUMENT,
+                         "receiver schedule does not cover the exact live bytes for destination "
+                         "block " + S(grp.dst_block_ids[o]) + ": covered=" + S(until) +
+                             " expected=" + S(grp.extents[o]));
+    }
+  }
+  return TS_OK;
+}
+
+int validate_received(const ts_received_plan* rp, const std::vector<pool::Pool>& pools,
+                      int64_t num_shards, const int64_t* local_ids, int64_t n_local,
+                      bool is_sender) {
+  if (rp->n_transfer_pools <= 0)
+    return set_error(TS_INVALID_ARGUMENT, "reshard plan must declare transfer_pool_indices");
+  if (rp->n_groups <= 0)
+    return set_error(TS_INVALID_ARGUMENT,
+                     "reshard plans must declare pool_groups (a plan is a list of groups; entries "
+                     "name their group)");
+  for (int64_t g = 0; g < rp->n_groups; ++g)
+    if (rp->groups[g].expected_pushes <= 0)
+      return set_error(TS_INVALID_ARGUMENT, "every pool group must expect a positive push count");
+  if (rp->n_pool_dtype_tags != int64_t(pools.size()))
+    return set_error(TS_INVALID_ARGUMENT, "reshard plan must declare one dtype tag per pool: plan=" +
+                                              S(rp->n_pool_dtype_tags) +
+                                              " local=" + S(int64_t(pools.size())));
+  if (n_local <= 0) return set_error(TS_INVALID_ARGUMENT, "local block ids must not be empty");
+  std::set<int64_t> local(local_ids, local_ids + n_local);
+  for (int64_t i = 0; i < n_local; ++i)
+    if (local_ids[i] < 0 || local_ids[i] > INT32_MAX)
+      return set_error(TS_INVALID_ARGUMENT, "local block ids must be non-negative and fit in int");
+  if (!is_sender) {
+    int64_t cur = 0;
+    for (int64_t g = 0; g < rp->n_groups; ++g) {
+      std::set<int64_t> ids;
+      for (int64_t i = 0; i < rp->groups[g].n_dst_block_ids; ++i) {
+        const int64_t b = rp->groups[g].dst_block_ids[i];
+        if (!ids.insert(b).second)
+          return set_error(TS_INVALID_ARGUMENT, "group destination block ids must be unique");
+        if (cur >= n_local || local_ids[cur] != b)
+          return set_error(TS_INVALID_ARGUMENT,
+                           "pool group block ids must concatenate to the plan's local block ids");
+        ++cur;
+      }
+    }
+    if (cur != n_local)
+      return set_error(TS_INVALID_ARGUMENT,
+                       "pool group block ids must cover the plan's local block ids");
+  }
+  std::set<int32_t> declared;
+  for (int64_t i = 0; i < rp->n_transfer_pools; ++i) {
+    const int32_t pi = rp->transfer_pool_indices[i];
+    if (pi < 0) return set_error(TS_INVALID_ARGUMENT, "transfer pool index must be non-negative");
+    if (!declared.insert(pi).second)
+      return set_error(TS_INVALID_ARGUMENT, "duplicate transfer pool index " + S(pi));
+    if (pi >= int32_t(pools.size()))
+      return set_error(TS_INVALID_ARGUMENT, "transfer pool index out of range: " + S(pi));
+    const pool::Pool& p = pools[size_t(pi)];
+    const char* tag = rp->pool_dtype_tags[pi] ? rp->pool_dtype_tags[pi] : "";
+    if (p.dtype_tag != tag)
+      return set_error(TS_INVALID_ARGUMENT, "plan dtype tag mismatch for pool " + S(pi) + " (" +
+                                                p.tag + "): plan=" + tag + " local=" + p.dtype_tag);
+    for (int64_t b : local)
+      if (b >= p.num_blocks)
+        return set_error(TS_INVALID_ARGUMENT, "local block id " + S(b) +
+                                                  " is out of range for pool " + S(pi));
+  }
+  if (rp->n_schedules <= 0)
+    return set_error(TS_INVALID_ARGUMENT, "reshard plan must contain shard push schedules");
+  std::set<int64_t> zero_start;
+  for (int64_t i = 0; i < rp->n_entries; ++i) {
+    const ts_received_entry& e = rp->entries[i];
+    if (e.source_rank < 0)
+      return set_error(TS_INVALID_ARGUMENT, "reshard schedule source rank must be non-negative");
+    if (e.dst_peer < 0) return set_error(TS_INVALID_ARGUMENT, "reshard entry dst_peer must be non-empty");
+    if (e.src_block_id < 0 || e.src_block_id > INT32_MAX || e.dst_block_id < 0 ||
+        e.dst_block_id > INT32_MAX || e.dst_shard_idx < 0 || e.src_offset_bytes < 0 ||
+        e.dst_offset_bytes < 0 || e.size_bytes <= 0 || e.src_stride_bytes < 0 ||
+        e.dst_stride_bytes < 0 || e.count <= 0 || e.count > (1 << 20))
+      return set_error(TS_INVALID_ARGUMENT,
+                       "reshard entry contains invalid ids, offsets, sizes, or strides");
+    if (e.count > 1 && (e.src_stride_bytes == 0 || e.dst_stride_bytes == 0))
+      return set_error(TS_INVALID_ARGUMENT, "multi-chunk reshard entries require positive strides");
+    if (!is_sender && e.dst_shard_idx >= num_shards)
+      return set_error(TS_INVALID_ARGUMENT, "destination shard index " + S(e.dst_shard_idx) +
+                                                " is out of range: receiver has " + S(num_shards) +
+                                                " shards");
+    const int64_t id = is_sender ? e.src_block_id : e.dst_block_id;
+    if (!local.count(id))
+      return set_error(TS_INVALID_ARGUMENT, std::string(is_sender ? "source" : "destination") +
+                                                " block id " + S(id) +
+                                                " is absent from the local block-id list");
+    const int64_t off = is_sender ? e.src_offset_bytes : e.dst_offset_bytes;
+    const int64_t stride = is_sender ? e.src_stride_bytes : e.dst_stride_bytes;
+    if (!is_sender && e.dst_offset_bytes == 0) zero_start.insert(e.dst_block_id);
+    if (e.pool_group < 0 || e.pool_group >= rp->n_groups)
+      return set_error(TS_INVALID_ARGUMENT,
+                       "reshard entry declares an unknown pool group " + S(e.pool_group));
+    const ts_received_group& grp = rp->groups[e.pool_group];
+    for (int64_t k = 0; k < grp.n_pool_indices; ++k) {
+      const int32_t pi = grp.pool_indices[k];
+      if (pi < 0 || pi >= int32_t(pools.size()))
+        return set_error(TS_INVALID_ARGUMENT, "group pool index out of range: " + S(pi));
+      const pool::Pool& p = pools[size_t(pi)];
+      if (!span_fits_regions(off, stride, e.size_bytes, e.count, p))
+        return set_error(TS_INVALID_ARGUMENT,
+                         std::string(is_sender ? "source" : "destination") +
+                             " span exceeds declared pool " + S(pi) + " live regions in block " +
+                             S(id) + ": offset=" + S(off) + " stride=" + S(stride) +
+                             " size=" + S(e.size_bytes) + " count=" + S(e.count) +
+                             " block_stride_bytes=" + S(p.block_stride_bytes));
+    }
+  }
+  if (rp->n_entries == 0) return set_error(TS_INVALID_ARGUMENT, "reshard plan contains no entries");
+  if (!is_sender) {
+    for (int64_t b : local)
+      if (!zero_start.count(b))
+        return set_error(TS_INVALID_ARGUMENT,
+                         "destination block " + S(b) +
+                             " has no transfer entry starting at offset 0; partial-page "
+                             "destination preservation is not implemented");
+    return receiver_coverage(rp, pools);
+  }
+  return TS_OK;
+}
+
+int pools_from_c(const ts_pool_spec* c, int64_t n, std::vector<pool::Pool>* out) {
+  out->clear();
+  for (int64_t i = 0; i < n; ++i) {
+    pool::Pool p;
+    int rc = pool::from_c(&c[i], &p);
+    if (rc != TS_OK) return rc;
+    out->push_back(std::move(p));
+  }
+  return TS_OK;
+}
+
 }  // namespace
 }  // namespace tsb
 
@@ -731,6 +1024,77 @@ extern "C" int ts_pool_reshard_plan_group(const ts_pool_reshard_plan* plan, int6
   return TS_OK;
 }
 
+extern "C" int ts_pool_reshard_validate(const ts_received_plan* plan,
+                                        const ts_pool_spec* local_pools, int64_t n_local_pools,
+                                        int64_t num_shards, const int64_t* local_block_ids,
+                                        int64_t n_local_block_ids, int is_sender) {
+  tsb::clear_error();
+  if (!plan || (n_local_pools > 0 && !local_pools) ||
+      (n_local_block_ids > 0 && !local_block_ids))
+    return set_error(TS_INVALID_ARGUMENT, "null plan, pools or block ids");
+  std::vector<tsb::pool::Pool> pools;
+  int rc = tsb::pools_from_c(local_pools, n_local_pools, &pools);
+  if (rc != TS_OK) return rc;
+  return tsb::validate_received(plan, pools, num_shards, local_block_ids, n_local_block_ids,
+                                is_sender != 0);
+}
+
+extern "C" int ts_pool_reshard_plan_from_received(
+    const ts_received_plan* plan, const ts_pool_spec* src_pools, const ts_pool_spec* dst_pools,
+    int64_t n_pools, const int64_t* src_block_ids, int64_t n_src_block_ids,
+    const int64_t* dst_block_ids, int64_t n_dst_block_ids, int64_t dst_num_shards,
+    ts_pool_reshard_plan** out) {
+  tsb::clear_error();
+  if (!plan || !out || (n_pools > 0 && (!src_pools || !dst_pools)))
+    return set_error(TS_INVALID_ARGUMENT, "null plan, pools or output");
+  *out = nullptr;
+  std::vector<tsb::pool::Pool> sp, dp;
+  int rc = tsb::pools_from_c(src_pools, n_pools, &sp);
+  if (rc == TS_OK) rc = tsb::pools_from_c(dst_pools, n_pools, &dp);
+  if (rc != TS_OK) return rc;
+  // both ends' checks: every source span inside the sender's pool regions,
+  // every destination span inside the receiver's and exactly covered
+  rc = tsb::validate_received(plan, sp, 1, src_block_ids, n_src_block_ids, true);
+  if (rc != TS_OK) return set_error(rc, std::string("sender: ") + ts_last_error());
+  rc = tsb::validate_received(plan, dp, dst_num_shards, dst_block_ids, n_dst_block_ids, false);
+  if (rc != TS_OK) return set_error(rc, std::string("receiver: ") + ts_last_error());
+  auto* p = new ts_pool_reshard_plan();
+  int64_t max_rank = 0;
+  for (int64_t i = 0; i < plan->n_entries; ++i)
+    max_rank = std::max<int64_t>(max_rank, plan->entries[i].source_rank);
+  p->n_src_units = max_rank + 1;
+  p->schedules.assign(size_t(p->n_src_units), {});
+  for (int64_t i = 0; i < plan->n_entries; ++i) {
+    const ts_received_entry& e = plan->entries[i];
+    ts_pool_reshard_plan::Entry x{e.src_block_id, e.dst_block_id, e.src_offset_bytes,
+                                  e.dst_offset_bytes, e.size_bytes, e.pool_group};
+    x.src_stride = e.src_stride_bytes;
+    x.dst_stride = e.dst_stride_bytes;
+    x.count = e.count;
+    p->schedules[size_t(e.source_rank)].push_back(x);
+  }
+  for (int64_t g = 0; g < plan->n_groups; ++g) {
+    const ts_received_group& rg = plan->groups[g];
+    ts_pool_reshard_plan::Group grp;
+    grp.pools.assign(rg.pool_indices, rg.pool_indices + rg.n_pool_indices);
+    grp.dst_ids.assign(rg.dst_block_ids, rg.dst_block_ids + rg.n_dst_block_ids);
+    grp.extents.assign(rg.extents, rg.extents + rg.n_extents);
+    grp.expected_pushes = rg.expected_pushes;
+    grp.order_rank = rg.order_rank;
+    p->groups.push_back(std::move(grp));
+  }
+  for (int64_t u = 0; u < p->n_src_units; ++u)
+    if (!p->schedules[size_t(u)].empty()) p->active_units.push_back(u);
+  p->transfer_pool_indices.assign(plan->transfer_pool_indices,
+                                  plan->transfer_pool_indices + plan->n_transfer_pools);
+  p->parallelism = plan->parallelism;
+  p->expected_block_count = n_dst_block_ids;
+  p->src_pools = std::move(sp);
+  p->dst_pools = std::move(dp);
+  *out = p;
+  return TS_OK;
+}
+
 extern "C" int ts_pool_reshard_program_create(const ts_pool_reshard_plan* plan, int64_t src_unit,
                                               int device, const uint64_t* src_storage_ptrs,
                                               const uint64_t* dst_storage_ptrs,
@@ -783,7 +1147,15 @@ extern "C" int ts_pool_reshard_program_create(const ts_pool_reshard_plan* plan, 
     std::vector<tsb::RelTask> merged;
     uint64_t group_bytes = 0;
     for (const auto* e : es) {
-      group_bytes += uint64_t(e->size);
+      group_bytes += uint64_t(e->size) * uint64_t(e->count);
+      if (e->count > 1) {  // a received entry with its own repeats
+        for (int64_t o = 0; o < e->size; o += int64_t(1) << 30)
+          merged.push_back({e->src_block, e->src_off + o, e->dst_block, e->dst_off + o,
+                            e->src_stride, e->dst_stride,
+                            uint32_t(std::min<int64_t>(e->size - o, int64_t(1) << 30)),
+                            uint32_t(e->count)});
+        continue;
+      }
       for (int64_t o = 0; o < e->size; o += int64_t(1) << 30) {
         const uint32_t n = uint32_t(std::min<int64_t>(e->size - o, int64_t(1) << 30));
         tsb::RelTask t{e->src_block, e->src_off + o, e->dst_block, e->dst_off + o, 0, 0, n, 1};

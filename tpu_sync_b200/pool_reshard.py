@@ -192,6 +192,99 @@ def build_pool_reshard_plan(
   return PoolReshardPlan(h, nu, keep)
 
 
+# -- plans that arrive from a controller ---------------------------------------
+#
+# A received plan is a dict with the data fields of StartTransferRequest
+# (tpu_sync/rpc/raiden_service.proto): "transfer_pool_indices",
+# "pool_dtype_tags", "parallelism", "pool_groups" (dicts with pool_indices,
+# dst_device_block_ids, dst_expected_extent_bytes, expected_pushes,
+# order_rank) and "shard_push_schedules" ({source rank: [entry dicts with the
+# ShardPushEntryProto fields dst_peer, dst_shard_idx, src_block_id,
+# dst_block_id, src_offset_bytes, dst_offset_bytes, size_bytes,
+# src_stride_bytes, dst_stride_bytes, count, pool_group]}).
+
+def _received_c(plan: Dict[str, Any]):
+  keep: List[Any] = []
+  i32 = lambda v: (ctypes.c_int32 * max(len(v), 1))(*[int(x) for x in v])
+  i64 = lambda v: (ctypes.c_int64 * max(len(v), 1))(*[int(x) for x in v])
+  tpi = list(plan.get("transfer_pool_indices", []))
+  tags = [str(t).encode() for t in plan.get("pool_dtype_tags", [])]
+  tag_arr = (ctypes.c_char_p * max(len(tags), 1))(*tags)
+  groups = plan.get("pool_groups", [])
+  garr = (_native.ReceivedGroupC * max(len(groups), 1))()
+  for i, g in enumerate(groups):
+    pi, ids, ext = (i32(g.get("pool_indices", [])), i64(g.get("dst_device_block_ids", [])),
+                    i64(g.get("dst_expected_extent_bytes", [])))
+    keep.append((pi, ids, ext))
+    garr[i] = _native.ReceivedGroupC(pi, len(g.get("pool_indices", [])), ids,
+                                     len(g.get("dst_device_block_ids", [])), ext,
+                                     len(g.get("dst_expected_extent_bytes", [])),
+                                     int(g.get("expected_pushes", 0)), int(g.get("order_rank", 0)))
+  peers: Dict[str, int] = {}
+  rows = []
+  scheds = plan.get("shard_push_schedules", {})
+  for rank, entries in scheds.items():
+    for e in entries:
+      peer = str(e.get("dst_peer", ""))
+      pid = -1 if not peer else peers.setdefault(peer, len(peers))
+      rows.append(_native.ReceivedEntryC(
+          int(rank), pid, int(e.get("dst_shard_idx", 0)), int(e.get("src_block_id", 0)),
+          int(e.get("dst_block_id", 0)), int(e.get("src_offset_bytes", 0)),
+          int(e.get("dst_offset_bytes", 0)), int(e.get("size_bytes", 0)),
+          int(e.get("src_stride_bytes", 0)), int(e.get("dst_stride_bytes", 0)),
+          int(e.get("count", 1)), int(e.get("pool_group", 0))))
+  earr = (_native.ReceivedEntryC * max(len(rows), 1))(*rows)
+  tarr = i32(tpi)
+  keep += [tag_arr, tags, garr, earr, tarr]
+  c = _native.ReceivedPlanC(tarr, len(tpi), tag_arr, len(tags), garr, len(groups), earr,
+                            len(rows), len(scheds), int(plan.get("parallelism", 0)), 0)
+  return c, keep
+
+
+def _pool_array(pools):
+  specs = [coerce_pool_spec(p) for p in pools]
+  cs = [_pool_c(p) for p in specs]
+  arr = (_native.PoolSpecC * max(len(cs), 1))(*[c[0] for c in cs])
+  return arr, cs
+
+
+def validate_pool_reshard_plan(plan: Dict[str, Any], local_pools: Sequence[Any],
+                               local_block_ids: Sequence[int], is_sender: bool,
+                               num_shards: int = 1) -> None:
+  """The executor's checks of a received plan; raises ValueError with the
+  reference's messages (kv_cache_manager_with_transfer.cc:742-1150)."""
+  c, keep = _received_c(plan)
+  parr, pkeep = _pool_array(local_pools)
+  ids = _native.i64_array(list(local_block_ids))
+  rc = _native.lib().ts_pool_reshard_validate(ctypes.byref(c), parr, len(pkeep), int(num_shards),
+                                              _native.i64_ptr(ids), ids.size, int(bool(is_sender)))
+  del keep
+  if rc != _native.OK:
+    raise ValueError(_native.last_error())
+
+
+def plan_from_received(plan: Dict[str, Any], src_pools: Sequence[Any], dst_pools: Sequence[Any],
+                       src_block_ids: Sequence[int], dst_block_ids: Sequence[int],
+                       dst_num_shards: int = 1) -> PoolReshardPlan:
+  """An executable plan from a received one, checked on both ends first."""
+  c, keep = _received_c(plan)
+  sarr, skeep = _pool_array(src_pools)
+  darr, dkeep = _pool_array(dst_pools)
+  if len(skeep) != len(dkeep):
+    raise ValueError("source and destination pool tables must have the same length")
+  sids = _native.i64_array(list(src_block_ids))
+  dids = _native.i64_array(list(dst_block_ids))
+  h = ctypes.c_void_p()
+  rc = _native.lib().ts_pool_reshard_plan_from_received(
+      ctypes.byref(c), sarr, darr, len(skeep), _native.i64_ptr(sids), sids.size,
+      _native.i64_ptr(dids), dids.size, int(dst_num_shards), ctypes.byref(h))
+  if rc != _native.OK:
+    raise ValueError(_native.last_error())
+  info = (ctypes.c_int64 * 8)()
+  _native.check(_native.lib().ts_pool_reshard_plan_info(h, info))
+  return PoolReshardPlan(h, info[7], [keep, skeep, dkeep])
+
+
 def _ptr(t) -> int:
   return int(t.data_ptr())
 
