@@ -198,20 +198,35 @@ struct Divider {
   }
   __device__ __forceinline__ float operator()(float x) const {
     if (use_div || fabsf(x) < 1.2621774e-29f /* 2^-96 */) return __fdiv_rn(x, scale);
+    return fast(x);
+  }
+  // Markstein only.  Exact in the e4m3 result for every x of a unit whose
+  // amax >= 2^-64 (and !use_div): x >= 2^-96 is exact as above, and for
+  // |x| < 2^-96 both the true quotient and this one are below 2^-23 in
+  // magnitude (scale >= 2^-64/448), far under half the smallest e4m3
+  // subnormal (2^-10), so both round to zero with x's sign.
+  __device__ __forceinline__ float fast(float x) const {
     const float q = __fmul_rn(x, r);
     const float e = __fmaf_rn(-q, scale, x);
     return copysignf(__fmaf_rn(e, r, q), x);  // scale > 0: sign of x (also for zeros)
   }
 };
 
-// 8 bf16 -> 8 e4m3 bytes (packed in a uint2).
+// A unit's amax from which Divider::fast is exact for all of its elements.
+constexpr float kFastAmax = 5.42101086e-20f;  // 2^-64
+
+// 8 bf16 -> 8 e4m3 bytes (packed in a uint2).  kFast: the unit allows
+// Divider::fast for every element.
+template <bool kFast>
 __device__ __forceinline__ uint2 quant8(const int4& v, const Divider& div) {
   const uint32_t w[4] = {uint32_t(v.x), uint32_t(v.y), uint32_t(v.z), uint32_t(v.w)};
   uint32_t out[2] = {0u, 0u};
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const float lo = div(bf16_bits_to_float(w[j] & 0xffffu));
-    const float hi = div(bf16_bits_to_float(w[j] >> 16));
+    const float xl = bf16_bits_to_float(w[j] & 0xffffu);
+    const float xh = bf16_bits_to_float(w[j] >> 16);
+    const float lo = kFast ? div.fast(xl) : div(xl);
+    const float hi = kFast ? div.fast(xh) : div(xh);
     const __nv_fp8x2_storage_t p =
         __nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE, __NV_E4M3);
     out[j >> 1] |= uint32_t(p) << (16 * (j & 1));
@@ -238,14 +253,32 @@ __device__ __forceinline__ int4 dequant8(uint2 q, float scale) {
   return make_int4(int(w[0]), int(w[1]), int(w[2]), int(w[3]));
 }
 
+// Units (block k, storage s) in grid-stride order, stepped without a
+// division per unit.
+struct UnitWalk {
+  int64_t k;
+  int s;
+  int step_k, step_s, n_st;
+  __device__ __forceinline__ UnitWalk(int n) : n_st(n) {
+    k = int64_t(blockIdx.x / uint32_t(n));
+    s = int(blockIdx.x - uint32_t(k) * uint32_t(n));
+    step_k = int(gridDim.x / uint32_t(n));
+    step_s = int(gridDim.x - uint32_t(step_k) * uint32_t(n));
+  }
+  __device__ __forceinline__ void next() {
+    k += step_k;
+    s += step_s;
+    if (s >= n_st) {
+      s -= n_st;
+      ++k;
+    }
+  }
+};
+
 template <typename Ids>
 __device__ __forceinline__ bool unit_addr(const ts_block_storage* __restrict__ st,
-                                          int n_st, const Ids& ids,
-                                          int64_t unit, int* err_flag, int* s_out,
-                                          int64_t* k_out, uint8_t** dev_out,
-                                          uint64_t* bb_out) {
-  const int64_t k = unit / n_st;
-  const int s = int(unit - k * n_st);
+                                          const Ids& ids, int64_t k, int s, int* err_flag,
+                                          int64_t* k_out, uint8_t** dev_out, uint64_t* bb_out) {
   const uint64_t bb = st[s].block_bytes;
   const int64_t id = ids.dev(k);
   const uint64_t dev_off = uint64_t(id) * bb;
@@ -253,7 +286,6 @@ __device__ __forceinline__ bool unit_addr(const ts_block_storage* __restrict__ s
     if (err_flag != nullptr && threadIdx.x == 0) *reinterpret_cast<volatile int*>(err_flag) = 1;
     return false;
   }
-  *s_out = s;
   *k_out = ids.stage(k);
   *dev_out = reinterpret_cast<uint8_t*>(st[s].dev_ptr) + dev_off;
   *bb_out = bb;
@@ -269,13 +301,12 @@ __global__ void __launch_bounds__(kThreads)
                        uint8_t* staging, uint64_t pitch, uint64_t scale_off,
                        int* err_flag) {
   __shared__ float red[kThreads / 32];
-  const int64_t units = n_blocks * int64_t(n_st);
-  for (int64_t unit = blockIdx.x; unit < units; unit += gridDim.x) {
-    int s;
+  for (UnitWalk u(n_st); u.k < n_blocks; u.next()) {
+    const int s = u.s;
     int64_t k;
     uint8_t* dev;
     uint64_t bb;
-    if (!unit_addr(st, n_st, ids, unit, err_flag, &s, &k, &dev, &bb)) continue;
+    if (!unit_addr(st, ids, u.k, s, err_flag, &k, &dev, &bb)) continue;
     uint8_t* stg_blk = staging + uint64_t(k) * pitch;
     uint8_t* q_out = stg_blk + st[s].stage_off;
     const int64_t nvec = int64_t(bb >> 4);  // 8 bf16 per vector
@@ -295,10 +326,18 @@ __global__ void __launch_bounds__(kThreads)
       const float amax = block_max(m, red);
       const float scale = amax == 0.f ? 1.f : __fdiv_rn(amax, 448.f);
       const Divider div(scale);
+      if (!div.use_div && amax >= kFastAmax) {  // uniform per unit
 #pragma unroll
-      for (int i = 0; i < V; ++i) {
-        const int64_t idx = threadIdx.x + int64_t(i) * kThreads;
-        if (idx < nvec) *reinterpret_cast<uint2*>(q_out + (idx << 3)) = quant8(v[i], div);
+        for (int i = 0; i < V; ++i) {
+          const int64_t idx = threadIdx.x + int64_t(i) * kThreads;
+          if (idx < nvec) *reinterpret_cast<uint2*>(q_out + (idx << 3)) = quant8<true>(v[i], div);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+          const int64_t idx = threadIdx.x + int64_t(i) * kThreads;
+          if (idx < nvec) *reinterpret_cast<uint2*>(q_out + (idx << 3)) = quant8<false>(v[i], div);
+        }
       }
       if (threadIdx.x == 0) *reinterpret_cast<float*>(stg_blk + scale_off + 4u * s) = scale;
     } else {
@@ -310,7 +349,7 @@ __global__ void __launch_bounds__(kThreads)
       const Divider div(scale);
       for (int64_t idx = threadIdx.x; idx < nvec; idx += kThreads)
         *reinterpret_cast<uint2*>(q_out + (idx << 3)) =
-            quant8(*reinterpret_cast<const int4*>(dev + (idx << 4)), div);
+            quant8<false>(*reinterpret_cast<const int4*>(dev + (idx << 4)), div);
       if (threadIdx.x == 0) *reinterpret_cast<float*>(stg_blk + scale_off + 4u * s) = scale;
     }
   }
@@ -322,13 +361,12 @@ __global__ void __launch_bounds__(kThreads)
                       const __grid_constant__ Ids ids, int64_t n_blocks,
                       const uint8_t* staging, uint64_t pitch, uint64_t scale_off,
                       int* err_flag) {
-  const int64_t units = n_blocks * int64_t(n_st);
-  for (int64_t unit = blockIdx.x; unit < units; unit += gridDim.x) {
-    int s;
+  for (UnitWalk u(n_st); u.k < n_blocks; u.next()) {
+    const int s = u.s;
     int64_t k;
     uint8_t* dev;
     uint64_t bb;
-    if (!unit_addr(st, n_st, ids, unit, err_flag, &s, &k, &dev, &bb)) continue;
+    if (!unit_addr(st, ids, u.k, s, err_flag, &k, &dev, &bb)) continue;
     const uint8_t* stg_blk = staging + uint64_t(k) * pitch;
     const uint8_t* q_in = stg_blk + st[s].stage_off;
     const float scale = *reinterpret_cast<const float*>(stg_blk + scale_off + 4u * s);
