@@ -215,6 +215,46 @@ struct Divider {
 // A unit's amax from which Divider::fast is exact for all of its elements.
 constexpr float kFastAmax = 5.42101086e-20f;  // 2^-64
 
+// Packed fp32 pairs (sm_100 .f32x2): each lane of the pair is the IEEE
+// round-to-nearest result of the scalar operation.
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+// Divider::fast on both bf16 of one 32-bit word, as a pair: q = x*r,
+// e = fma(q, -scale, x), q' = fma(e, r, q) lane by lane, then the pair's
+// e4m3 bytes.  The sign is not restored here (see quant8_fast).
+__device__ __forceinline__ uint32_t quant2_fast(uint32_t w, uint64_t r2, uint64_t ns2) {
+  const uint64_t x2 = uint64_t(w << 16) | (uint64_t(w & 0xffff0000u) << 32);
+  const uint64_t q = mul_f32x2(x2, r2);
+  const uint64_t e = fma_f32x2(q, ns2, x2);
+  const uint64_t qq = fma_f32x2(e, r2, q);
+  const float lo = __uint_as_float(uint32_t(qq)), hi = __uint_as_float(uint32_t(qq >> 32));
+  return uint32_t(__nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE, __NV_E4M3));
+}
+
+// 8 bf16 -> 8 e4m3 bytes through quant2_fast, for units that allow
+// Divider::fast for every element.  For a nonzero x the exact value of every
+// step (x*r, the residual, the corrected quotient) is nonzero with x's sign,
+// and a result that rounds to zero keeps that sign; only x = -0 comes out +0
+// (the sum of opposite zeros).  So x's sign bit is OR-ed into each e4m3 byte,
+// a no-op wherever the sign is already set.
+__device__ __forceinline__ uint2 quant8_fast(const int4& v, uint64_t r2, uint64_t ns2) {
+  const uint32_t w0 = uint32_t(v.x), w1 = uint32_t(v.y), w2 = uint32_t(v.z), w3 = uint32_t(v.w);
+  uint32_t a = quant2_fast(w0, r2, ns2) | (quant2_fast(w1, r2, ns2) << 16);
+  uint32_t b = quant2_fast(w2, r2, ns2) | (quant2_fast(w3, r2, ns2) << 16);
+  a |= __byte_perm(w0, w1, 0x7531) & 0x80808080u;  // high bytes of the four bf16
+  b |= __byte_perm(w2, w3, 0x7531) & 0x80808080u;
+  return make_uint2(a, b);
+}
+
 // 8 bf16 -> 8 e4m3 bytes (packed in a uint2).  kFast: the unit allows
 // Divider::fast for every element.
 template <bool kFast>
@@ -327,10 +367,13 @@ __global__ void __launch_bounds__(kThreads)
       const float scale = amax == 0.f ? 1.f : __fdiv_rn(amax, 448.f);
       const Divider div(scale);
       if (!div.use_div && amax >= kFastAmax) {  // uniform per unit
+        const uint32_t rb = __float_as_uint(div.r), nsb = __float_as_uint(-scale);
+        const uint64_t r2 = uint64_t(rb) | (uint64_t(rb) << 32);
+        const uint64_t ns2 = uint64_t(nsb) | (uint64_t(nsb) << 32);
 #pragma unroll
         for (int i = 0; i < V; ++i) {
           const int64_t idx = threadIdx.x + int64_t(i) * kThreads;
-          if (idx < nvec) *reinterpret_cast<uint2*>(q_out + (idx << 3)) = quant8<true>(v[i], div);
+          if (idx < nvec) *reinterpret_cast<uint2*>(q_out + (idx << 3)) = quant8_fast(v[i], r2, ns2);
         }
       } else {
 #pragma unroll
