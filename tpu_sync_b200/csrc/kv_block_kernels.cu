@@ -241,11 +241,11 @@ __device__ __forceinline__ uint32_t quant2_fast(uint32_t w, uint64_t r2, uint64_
 }
 
 // 8 bf16 -> 8 e4m3 bytes through quant2_fast, for units that allow
-// Divider::fast for every element.  For a nonzero x the exact value of every
-// step (x*r, the residual, the corrected quotient) is nonzero with x's sign,
-// and a result that rounds to zero keeps that sign; only x = -0 comes out +0
-// (the sum of opposite zeros).  So x's sign bit is OR-ed into each e4m3 byte,
-// a no-op wherever the sign is already set.
+// Divider::fast for every element.  For a nonzero x the exact corrected
+// quotient q + e*r is nonzero with x's sign (|e*r| < |q| when q != 0, and
+// e = x when x*r underflows to zero), and a result that rounds to zero keeps
+// that sign; only x = -0 comes out +0 (the sum of opposite zeros).  So x's
+// sign bit is OR-ed into each e4m3 byte, a no-op wherever it is already set.
 __device__ __forceinline__ uint2 quant8_fast(const int4& v, uint64_t r2, uint64_t ns2) {
   const uint32_t w0 = uint32_t(v.x), w1 = uint32_t(v.y), w2 = uint32_t(v.z), w3 = uint32_t(v.w);
   uint32_t a = quant2_fast(w0, r2, ns2) | (quant2_fast(w1, r2, ns2) << 16);
