@@ -334,8 +334,12 @@ __device__ __forceinline__ bool unit_addr(const ts_block_storage* __restrict__ s
 
 // V = 16-byte vectors per thread held in registers (V*4 KiB per unit); a
 // unit larger than that takes the two-pass path.
+// Resident CTAs per SM the fp8 extract is compiled for (registers <= 40 for
+// register tiles of up to 4 vectors per thread); its grid uses the same.
+constexpr int fp8_extract_ctas_per_sm(int v) { return v <= 4 ? 6 : 4; }
+
 template <typename Ids, int V>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, fp8_extract_ctas_per_sm(V))
     extract_fp8_kernel(const ts_block_storage* __restrict__ st, int n_st,
                        const __grid_constant__ Ids ids, int64_t n_blocks,
                        uint8_t* staging, uint64_t pitch, uint64_t scale_off,
@@ -512,10 +516,13 @@ int launch_extract_fp8(int device, const ts_block_storage* d_st, int n_st,
                        cudaStream_t s, uint64_t max_bb, int max_ctas = 0) {
   if (n_blocks == 0 || n_st == 0) return TS_OK;
   DeviceGuard g(device);
-  const int grid = launch_grid(device, n_blocks * int64_t(n_st), max_ctas);
   uint8_t* stg = static_cast<uint8_t*>(staging);
   // register tile sized to the largest unit (16-byte vectors per thread)
   const uint64_t vecs = (max_bb / 16 + kThreads - 1) / kThreads;
+  int64_t cap = int64_t(sm_count(device)) * fp8_extract_ctas_per_sm(vecs <= 4 ? 4 : 8);
+  if (max_ctas > 0 && max_ctas < cap) cap = max_ctas;
+  const int64_t units = n_blocks * int64_t(n_st);
+  const int grid = int(units < cap ? units : cap);
   if (vecs <= 2)
     extract_fp8_kernel<Ids, 2><<<grid, kThreads, 0, s>>>(d_st, n_st, ids, n_blocks, stg, pitch,
                                                          scale_off, err_flag);
