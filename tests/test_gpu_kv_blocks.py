@@ -104,6 +104,27 @@ def fp8_oracle(pool, ids):
   return ofp8.extract_fp8(bits, ids), bits
 
 
+def test_fp8_extract_out_of_bounds_id_sets_error_flag(cuda):
+  """16 KiB units (the bulk-copy kernel): an id past the storage flags the
+  error and is skipped; the ids around it are still extracted exactly."""
+  pool = small_pool(workloads.KVGeometry(2, 1, 64, 1, 128), 8, 4, cuda)
+  table = ops.StorageTable(pool, fp8=True)
+  ids = [1, 8, 2, 7, 0]
+  staging = table.new_staging(len(ids))
+  staging.fill_(0x5A)
+  err = torch.zeros(1, dtype=torch.int32, device=cuda)
+  ops.kv_extract(table, ids, staging, err_flag=err)
+  torch.cuda.synchronize()
+  assert int(err.item()) == 1
+  good = [0, 2, 3, 4]
+  (payload, scales), _ = fp8_oracle(pool, [ids[i] for i in good])
+  st = staging.cpu().numpy()
+  for s in range(len(pool)):
+    off = table.stage_offs[s]
+    np.testing.assert_array_equal(st[good, off:off + payload.shape[2]], payload[:, s])
+  assert (st[1] == 0x5A).all()  # the skipped block's staging row is untouched
+
+
 @pytest.mark.parametrize("block_tokens,heads,n_blocks", [(64, 1, 40), (16, 8, 9), (256, 4, 3)])
 def test_fp8_extract_insert_matches_oracle(cuda, block_tokens, heads, n_blocks):
   geom = workloads.KVGeometry(layers=3, kv=2, block_tokens=block_tokens, heads=heads,

@@ -919,6 +919,12 @@ extern "C" int ts_mgr_create(const ts_storage_desc* storages, int num_layers,
     m->max_bb = std::max(m->max_bb, s.bb);
     m->vec_ok = m->vec_ok && (s.dev_ptr % 16 == 0) && (s.bb % 16 == 0);
   }
+  if (m->fp8 && !m->vec_ok) {
+    delete m;
+    return set_error(TS_INVALID_ARGUMENT,
+                     "fp8 tier needs 16-byte aligned storages (the fused cast moves 16-byte "
+                     "vectors and bulk copies)");
+  }
   if (m->fp8) {
     m->scale_off = off;
     off += tsb::round16(uint64_t(n) * 4);
