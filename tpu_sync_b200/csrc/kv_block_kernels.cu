@@ -141,6 +141,7 @@ __global__ void __launch_bounds__(kThreads)
 // ---------------------------------------------------------------------------
 
 
+template <int T = kThreads>
 __device__ __forceinline__ float block_max(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -150,7 +151,7 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   __syncthreads();
   float r = red[0];
 #pragma unroll
-  for (int i = 1; i < kThreads / 32; ++i) r = fmaxf(r, red[i]);
+  for (int i = 1; i < T / 32; ++i) r = fmaxf(r, red[i]);
   return r;
 }
 
@@ -334,17 +335,22 @@ __device__ __forceinline__ bool unit_addr(const ts_block_storage* __restrict__ s
 
 // V = 16-byte vectors per thread held in registers (V*4 KiB per unit); a
 // unit larger than that takes the two-pass path.
-// Resident CTAs per SM the fp8 extract is compiled for (registers <= 40 for
-// register tiles of up to 4 vectors per thread); its grid uses the same.
-constexpr int fp8_extract_ctas_per_sm(int v) { return v <= 4 ? 6 : 4; }
+// Resident CTAs per SM the fp8 extract is compiled for, by threads per CTA
+// and register tile (registers per thread x threads x CTAs <= 64K); its grid
+// uses the same.  128 threads with 8 vectors each carry a 16 KiB unit with
+// half the per-unit overhead (address walk, reduction, loop) of 256 threads.
+constexpr int fp8_extract_ctas_per_sm(int v, int t) {
+  return t == 128 ? 8 : (v <= 4 ? 6 : 4);
+}
 
-template <typename Ids, int V>
-__global__ void __launch_bounds__(kThreads, fp8_extract_ctas_per_sm(V))
+template <typename Ids, int V, int T = kThreads>
+__global__ void __launch_bounds__(T, fp8_extract_ctas_per_sm(V, T))
     extract_fp8_kernel(const ts_block_storage* __restrict__ st, int n_st,
                        const __grid_constant__ Ids ids, int64_t n_blocks,
                        uint8_t* staging, uint64_t pitch, uint64_t scale_off,
                        int* err_flag) {
-  __shared__ float red[kThreads / 32];
+  constexpr int kThreads = T;
+  __shared__ float red[T / 32];
   for (UnitWalk u(n_st); u.k < n_blocks; u.next()) {
     const int s = u.s;
     int64_t k;
@@ -367,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, fp8_extract_ctas_per_sm(V))
         }
       }
       m = pair_max(mp);
-      const float amax = block_max(m, red);
+      const float amax = block_max<T>(m, red);
       const float scale = amax == 0.f ? 1.f : __fdiv_rn(amax, 448.f);
       const Divider div(scale);
       if (!div.use_div && amax >= kFastAmax) {  // uniform per unit
@@ -391,7 +397,7 @@ __global__ void __launch_bounds__(kThreads, fp8_extract_ctas_per_sm(V))
       // Large blocks: pass 1 reduces, pass 2 re-reads (L2-resident) and casts.
       for (int64_t idx = threadIdx.x; idx < nvec; idx += kThreads)
         m = amax8(ld_stream(dev + (idx << 4)), m);
-      const float amax = block_max(m, red);
+      const float amax = block_max<T>(m, red);
       const float scale = amax == 0.f ? 1.f : __fdiv_rn(amax, 448.f);
       const Divider div(scale);
       for (int64_t idx = threadIdx.x; idx < nvec; idx += kThreads)
@@ -399,166 +405,6 @@ __global__ void __launch_bounds__(kThreads, fp8_extract_ctas_per_sm(V))
             quant8<false>(*reinterpret_cast<const int4*>(dev + (idx << 4)), div);
       if (threadIdx.x == 0) *reinterpret_cast<float*>(stg_blk + scale_off + 4u * s) = scale;
     }
-  }
-}
-
-// ---------------------------------------------------------------------------
-// fp8 extract with bulk-copy double buffering.  One thread streams unit i+2
-// from HBM into a shared-memory stage (cp.async.bulk, completion counted on
-// an mbarrier; no multicast) while the CTA reduces and quantises unit i
-// from the other stage, so the HBM reads of the next units overlap the
-// arithmetic and the reduction barrier of the current one.  Units must be
-// 16-byte aligned and at most one stage (kBulkStageBytes) in size.
-// ---------------------------------------------------------------------------
-
-constexpr uint32_t kBulkStageBytes = 16 * 1024;
-constexpr int kBulkCtasPerSm = 6;
-constexpr uint32_t kWaitLimit = 1u << 22;  // try_wait polls before giving up
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-// Polls a phase; false after kWaitLimit polls (the copy never completed).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
-}
-__device__ __forceinline__ void bulk_load(void* smem, const void* gmem, uint32_t bytes,
-                                          uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-          "r"(smem_u32(smem)),
-      "l"(gmem), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// Thread 0: queue unit (k, s) into `stage`.  An out-of-range unit completes
-// the stage's phase with a plain arrive (its consumer skips it).
-template <typename Ids>
-__device__ __forceinline__ void bulk_issue(const ts_block_storage* __restrict__ st,
-                                           const Ids& ids, int64_t k, int s, uint8_t* stage,
-                                           uint64_t* bar) {
-  const uint64_t bb = st[s].block_bytes;
-  const int64_t id = ids.dev(k);
-  const uint64_t off = uint64_t(id) * bb;
-  if (id < 0 || off + bb > st[s].dev_bytes) {
-    mbar_arrive(bar);
-    return;
-  }
-  mbar_expect_tx(bar, uint32_t(bb));
-  bulk_load(stage, reinterpret_cast<const uint8_t*>(st[s].dev_ptr) + off, uint32_t(bb), bar);
-}
-
-template <typename Ids>
-__global__ void __launch_bounds__(kThreads, kBulkCtasPerSm)
-    extract_fp8_bulk_kernel(const ts_block_storage* __restrict__ st, int n_st,
-                            const __grid_constant__ Ids ids, int64_t n_blocks,
-                            uint8_t* staging, uint64_t pitch, uint64_t scale_off,
-                            int* err_flag) {
-  constexpr int V = int(kBulkStageBytes / 16 / kThreads);  // 4 vectors per thread
-  extern __shared__ __align__(128) uint8_t stages[];       // 2 x kBulkStageBytes
-  __shared__ __align__(8) uint64_t bars[2];
-  __shared__ float red[kThreads / 32];
-  if (threadIdx.x == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-  UnitWalk ahead(n_st);  // producer position (thread 0 only)
-  uint32_t queued = 0;   // thread 0: bit i = stage i holds a copy not yet consumed
-  if (threadIdx.x == 0)
-    for (int i = 0; i < 2 && ahead.k < n_blocks; ++i, ahead.next()) {
-      bulk_issue(st, ids, ahead.k, ahead.s, stages + i * kBulkStageBytes, &bars[i]);
-      queued |= 1u << i;
-    }
-  uint32_t phase = 0;  // bit i: parity to wait for on stage i
-  int64_t i = 0;
-  for (UnitWalk u(n_st); u.k < n_blocks; u.next(), ++i) {
-    const int sg = int(i & 1);
-    uint8_t* stage = stages + sg * kBulkStageBytes;
-    const bool arrived = mbar_wait(&bars[sg], (phase >> sg) & 1u);
-    phase ^= 1u << sg;
-    queued &= ~(1u << sg);
-    // abort uniformly if any thread's wait ran out
-    if (__syncthreads_or(!arrived)) {
-      if (threadIdx.x == 0) {
-        if (err_flag != nullptr) *reinterpret_cast<volatile int*>(err_flag) = 2;
-        // give the other stage's queued copy (bounded) time to land first
-        if (queued & (1u << (sg ^ 1))) mbar_wait(&bars[sg ^ 1], (phase >> (sg ^ 1)) & 1u);
-      }
-      __syncthreads();
-      return;
-    }
-    const int s = u.s;
-    int64_t k;
-    uint8_t* dev;
-    uint64_t bb;
-    const bool valid = unit_addr(st, ids, u.k, s, err_flag, &k, &dev, &bb);  // uniform
-    int4 v[V];
-    const int64_t nvec = valid ? int64_t(bb >> 4) : 0;
-    __nv_bfloat162 mp = __floats2bfloat162_rn(0.f, 0.f);
-#pragma unroll
-    for (int j = 0; j < V; ++j) {
-      const int64_t idx = threadIdx.x + int64_t(j) * kThreads;
-      if (idx < nvec) {
-        v[j] = *reinterpret_cast<const int4*>(stage + (idx << 4));
-        mp = amax8_pairs(v[j], mp);
-      }
-    }
-    // After this reduction every thread has read the stage: refill it.
-    const float amax = block_max(pair_max(mp), red);
-    if (threadIdx.x == 0 && ahead.k < n_blocks) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      bulk_issue(st, ids, ahead.k, ahead.s, stage, &bars[sg]);
-      queued |= 1u << sg;
-      ahead.next();
-    }
-    if (!valid) continue;
-    uint8_t* stg_blk = staging + uint64_t(k) * pitch;
-    uint8_t* q_out = stg_blk + st[s].stage_off;
-    const float scale = amax == 0.f ? 1.f : __fdiv_rn(amax, 448.f);
-    const Divider div(scale);
-    if (!div.use_div && amax >= kFastAmax) {  // uniform per unit
-      const uint32_t rb = __float_as_uint(div.r), nsb = __float_as_uint(-scale);
-      const uint64_t r2 = uint64_t(rb) | (uint64_t(rb) << 32);
-      const uint64_t ns2 = uint64_t(nsb) | (uint64_t(nsb) << 32);
-#pragma unroll
-      for (int j = 0; j < V; ++j) {
-        const int64_t idx = threadIdx.x + int64_t(j) * kThreads;
-        if (idx < nvec) *reinterpret_cast<uint2*>(q_out + (idx << 3)) = quant8_fast(v[j], r2, ns2);
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < V; ++j) {
-        const int64_t idx = threadIdx.x + int64_t(j) * kThreads;
-        if (idx < nvec) *reinterpret_cast<uint2*>(q_out + (idx << 3)) = quant8<false>(v[j], div);
-      }
-    }
-    if (threadIdx.x == 0) *reinterpret_cast<float*>(stg_blk + scale_off + 4u * s) = scale;
   }
 }
 
@@ -679,23 +525,14 @@ int launch_extract_fp8(int device, const ts_block_storage* d_st, int n_st,
   uint8_t* stg = static_cast<uint8_t*>(staging);
   // register tile sized to the largest unit (16-byte vectors per thread)
   const uint64_t vecs = (max_bb / 16 + kThreads - 1) / kThreads;
-  int64_t cap = int64_t(sm_count(device)) * fp8_extract_ctas_per_sm(vecs <= 4 ? 4 : 8);
+  const bool narrow = vecs <= 4;  // units <= 16 KiB: 128 threads x 8 vectors
+  int64_t cap = int64_t(sm_count(device)) *
+                (narrow ? fp8_extract_ctas_per_sm(8, 128) : fp8_extract_ctas_per_sm(8, kThreads));
   if (max_ctas > 0 && max_ctas < cap) cap = max_ctas;
   const int64_t units = n_blocks * int64_t(n_st);
   const int grid = int(units < cap ? units : cap);
-  if (max_bb <= kBulkStageBytes) {
-    // units fit a shared-memory stage (16-byte alignment is checked by the
-    // callers): bulk-copy double buffering
-    int64_t bcap = int64_t(sm_count(device)) * kBulkCtasPerSm;
-    if (max_ctas > 0 && max_ctas < bcap) bcap = max_ctas;
-    const int bgrid = int(units < bcap ? units : bcap);
-    extract_fp8_bulk_kernel<Ids><<<bgrid, kThreads, 2 * kBulkStageBytes, s>>>(
-        d_st, n_st, ids, n_blocks, stg, pitch, scale_off, err_flag);
-  } else if (vecs <= 2)
-    extract_fp8_kernel<Ids, 2><<<grid, kThreads, 0, s>>>(d_st, n_st, ids, n_blocks, stg, pitch,
-                                                         scale_off, err_flag);
-  else if (vecs <= 4)
-    extract_fp8_kernel<Ids, 4><<<grid, kThreads, 0, s>>>(d_st, n_st, ids, n_blocks, stg, pitch,
+  if (narrow)
+    extract_fp8_kernel<Ids, 8, 128><<<grid, 128, 0, s>>>(d_st, n_st, ids, n_blocks, stg, pitch,
                                                          scale_off, err_flag);
   else
     extract_fp8_kernel<Ids, 8><<<grid, kThreads, 0, s>>>(d_st, n_st, ids, n_blocks, stg, pitch,
