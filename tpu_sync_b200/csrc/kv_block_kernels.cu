@@ -408,12 +408,16 @@ __global__ void __launch_bounds__(T, fp8_extract_ctas_per_sm(V, T))
   }
 }
 
-template <typename Ids>
-__global__ void __launch_bounds__(kThreads)
+// VPT fp8 vectors (8 bytes each) per thread, T threads per CTA.  16 KiB
+// units run on 128 threads x 8 vectors: 64 bytes of loads in flight per
+// thread and 16 CTAs per SM.
+template <typename Ids, int VPT = kVecPerThread, int T = kThreads>
+__global__ void __launch_bounds__(T, T == 128 ? 16 : 8)
     insert_fp8_kernel(const ts_block_storage* __restrict__ st, int n_st,
                       const __grid_constant__ Ids ids, int64_t n_blocks,
                       const uint8_t* staging, uint64_t pitch, uint64_t scale_off,
                       int* err_flag) {
+  constexpr int kThreads = T, kVecPerThread = VPT;
   for (UnitWalk u(n_st); u.k < n_blocks; u.next()) {
     const int s = u.s;
     int64_t k;
@@ -545,13 +549,22 @@ template <typename Ids>
 int launch_insert_fp8(int device, const ts_block_storage* d_st, int n_st,
                       const Ids& ids, int64_t n_blocks, const void* staging,
                       uint64_t pitch, uint64_t scale_off, int* err_flag,
-                      cudaStream_t s, int max_ctas = 0) {
+                      cudaStream_t s, uint64_t max_bb, int max_ctas = 0) {
   if (n_blocks == 0 || n_st == 0) return TS_OK;
   DeviceGuard g(device);
-  const int grid = launch_grid(device, n_blocks * int64_t(n_st), max_ctas);
-  insert_fp8_kernel<Ids><<<grid, kThreads, 0, s>>>(
-      d_st, n_st, ids, n_blocks, static_cast<const uint8_t*>(staging), pitch,
-      scale_off, err_flag);
+  const uint8_t* stg = static_cast<const uint8_t*>(staging);
+  const int64_t units = n_blocks * int64_t(n_st);
+  if (max_bb <= 16 * 1024) {
+    int64_t cap = int64_t(sm_count(device)) * 16;
+    if (max_ctas > 0 && max_ctas < cap) cap = max_ctas;
+    const int grid = int(units < cap ? units : cap);
+    insert_fp8_kernel<Ids, 8, 128><<<grid, 128, 0, s>>>(d_st, n_st, ids, n_blocks, stg, pitch,
+                                                         scale_off, err_flag);
+  } else {
+    const int grid = launch_grid(device, units, max_ctas);
+    insert_fp8_kernel<Ids><<<grid, kThreads, 0, s>>>(d_st, n_st, ids, n_blocks, stg, pitch,
+                                                     scale_off, err_flag);
+  }
   TS_CUDA_RET(cudaGetLastError(), "insert_fp8 launch");
   return TS_OK;
 }
@@ -576,7 +589,7 @@ int mgr_insert(int device, const ts_block_storage* d_st, int n_st,
                uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas) {
   if (fp8)
     return launch_insert_fp8(device, d_st, n_st, ids, n_blocks, staging, pitch,
-                             scale_off, err_flag, s, max_ctas);
+                             scale_off, err_flag, s, max_bb, max_ctas);
   return launch_insert(device, d_st, n_st, ids, n_blocks, staging, pitch,
                        err_flag, s, vec_ok, max_bb, max_ctas);
 }
@@ -672,9 +685,10 @@ extern "C" int ts_kv_insert_fp8(int device, const ts_block_storage* d_storages,
   if (!d_storages || !d_ids || !d_staging)
     return set_error(TS_INVALID_ARGUMENT, "null pointer argument");
   tsb::DeviceGuard g(device);
-  int rc = check_fp8_table(d_storages, n_storages, stage_pitch, scale_off, d_staging, nullptr);
+  uint64_t max_bb = 0;
+  int rc = check_fp8_table(d_storages, n_storages, stage_pitch, scale_off, d_staging, &max_bb);
   if (rc != TS_OK) return rc;
   return tsb::launch_insert_fp8(device, d_storages, n_storages, tsb::DevIds{d_ids}, n_blocks,
                                 d_staging, stage_pitch, scale_off, err_flag,
-                                reinterpret_cast<cudaStream_t>(stream));
+                                reinterpret_cast<cudaStream_t>(stream), max_bb);
 }
