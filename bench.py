@@ -257,6 +257,98 @@ def cpu_offload_reload(plans, seconds: float, steps: int = 0, warmup: int = 0):
           "cpu": cpu_model()}
 
 
+def _timed_loop(fn, seconds: float, min_iters: int = 2):
+  """Runs fn() for about `seconds` (at least min_iters times); returns (iters, s)."""
+  t0 = time.perf_counter()
+  n = 0
+  while n < min_iters or time.perf_counter() - t0 < seconds:
+    fn()
+    n += 1
+  return n, time.perf_counter() - t0
+
+
+def cpu_c2_fp8(seconds: float):
+  """C2 offload on the host cores: gather + per-(block, storage) absmax scale
+  + e4m3 cast of 256 random blocks of the 80-layer x K/V shard (the C
+  restatement, all threads), from a 512-block host-resident sample pool."""
+  from oracle import cpu_ref
+  from tpu_sync_b200 import workloads
+  g = workloads.C2
+  n_st, blocks, B = g.storages, 256, workloads.C2_BATCH
+  elems = g.storage_block_bytes // 2
+  rng = np.random.default_rng(20)
+  # 40 distinct 4 MiB storages (160 MiB, more than a host L3) cycled over the
+  # 160 storage slots keeps the set-up short
+  distinct = [(rng.standard_normal((blocks, elems), np.float32).view(np.uint32) >> 16)
+              .astype(np.uint16) for _ in range(40)]
+  pool = [distinct[i % len(distinct)] for i in range(n_st)]
+  ids = rng.permutation(blocks).astype(np.int64)
+  offs = [s * elems for s in range(n_st)]  # fp8 payload: elems bytes per storage
+  scale_off = n_st * elems
+  pitch = scale_off + 4 * n_st
+  staging = np.zeros((B, pitch), np.uint8)
+  threads = cpu_ref.host_threads()
+  n, sec = _timed_loop(lambda: cpu_ref.extract_fp8(pool, ids, staging, pitch, offs, scale_off,
+                                                   threads), seconds)
+  return {"value": round(n * B * g.block_bytes / sec / 1e9, 2), "unit": "GB/s of bf16 offloaded",
+          "cores": threads, "kind": "port",
+          "sample": f"{n} offloads of 256 blocks in random order (gather + absmax scale + e4m3 "
+                    "cast, oracle/cpu_ref.c) of the C2 geometry, 160 MiB of distinct host data"}
+
+
+def cpu_c3_relayout(seconds: float):
+  """C3 permute on the host cores: one of the 8 sequences (1 GiB of the 8 GiB
+  per pair), 64 storages, head-major 16-token pages -> token-major 64-token."""
+  from oracle import cpu_ref
+  n_st, T, H, HB = 64, 32768, 2, 256
+  rng = np.random.default_rng(30)
+  st = rng.permutation(T // 16).reshape(1, -1).astype(np.int32)
+  dt = rng.permutation(T // 64).reshape(1, -1).astype(np.int32)
+  src = [rng.integers(0, 256, (T // 16) * 16 * H * HB, dtype=np.uint8) for _ in range(n_st)]
+  dst = [np.empty((T // 64) * 64 * H * HB, np.uint8) for _ in range(n_st)]
+  threads = cpu_ref.host_threads()
+  n, sec = _timed_loop(lambda: cpu_ref.relayout(src, dst, H, HB, 16, 64, st, dt, T, threads),
+                       seconds)
+  moved = n_st * T * H * HB
+  return {"value": round(n * moved / sec / 1e9, 2), "unit": "GB/s", "cores": threads,
+          "kind": "port",
+          "sample": f"{n} relayouts of one 32768-token sequence x 64 storages x 2 heads "
+                    "(1 GiB; oracle/cpu_ref.c, a 256-byte memcpy per head vector)"}
+
+
+def cpu_c4_reshard(plan, specs, seconds: float):
+  """C4 on the host cores: the planner's chunks of the first decoder layer
+  (q, k, v, o, gate, up, down, 2 norms) applied fp32 -> bf16 (RNE) with all
+  threads, source shard 0 to every destination shard."""
+  import math
+  from oracle import cpu_ref
+  from tpu_sync_b200 import reshard_plan as rp
+  chosen = [i for i, v in enumerate(specs) if v.name.startswith("layers.0.")]
+  src_sizes = {v: math.prod(rp.local_shape(rp.shard_boxes(specs[v].shape, specs[v].src_mesh)[0]))
+               for v in chosen}
+  src_off, tot = {}, 0
+  for v in chosen:
+    src_off[v], tot = tot, tot + src_sizes[v]
+  chunks, dst_off, dtot = [], {}, 0
+  for (vi, d), cs in plan.for_source(0).items():
+    if vi not in src_off:
+      continue
+    n_dst = math.prod(rp.local_shape(rp.shard_boxes(specs[vi].shape, specs[vi].dst_mesh)[d]))
+    if (vi, d) not in dst_off:
+      dst_off[(vi, d)], dtot = dtot, dtot + n_dst
+    for (so, do, size, ss, ds, cnt) in cs:
+      chunks.append((src_off[vi] + so, dst_off[(vi, d)] + do, size, ss, ds, cnt))
+  rng = np.random.default_rng(3)
+  src = (rng.standard_normal(tot, np.float32) * np.float32(0.02))
+  dst = np.empty(dtot, np.uint16)
+  threads = cpu_ref.host_threads()
+  n, sec = _timed_loop(lambda: cpu_ref.reshard_f32_bf16(src, dst, chunks, threads), seconds)
+  return {"value": round(n * 2 * dtot / sec / 1e9, 2), "unit": "GB/s of bf16 written",
+          "cores": threads, "kind": "port",
+          "sample": f"{n} pushes of decoder layer 0 ({tot / 1e6:.0f} M params, "
+                    f"{len(chunks)} chunks; oracle/cpu_ref.c fp32 -> bf16 RNE)"}
+
+
 def run_reference(args):
   rank = int(os.environ.get("RANK", "0"))
   if rank != 0:
@@ -511,7 +603,7 @@ def run_handoff(torch, dist, rank, world, device, steps, warmup):
                         if prog_ms else None}}
 
 
-def run_c2_fp8(torch, rank, device, steps, warmup, max_over_ranks):
+def run_c2_fp8(torch, rank, device, steps, warmup, max_over_ranks, cpu_seconds=0.0):
   """C2: Llama-3-70B TP8 KV shard (80 layers x K/V, 64-token blocks of 1 head
   x 128 bf16 = 16 KiB per storage block) on an fp8 host tier: per step 256
   random blocks (seed 20+rank) offloaded (fused bf16 -> e4m3 + per-block
@@ -567,9 +659,11 @@ def run_c2_fp8(torch, rank, device, steps, warmup, max_over_ranks):
   def kgbs(st):
     return round(st["bytes"] / (st["ms"] * 1e-3) / 1e9, 1) if st["ms"] > 0 else None
 
+  cpu = cpu_c2_fp8(cpu_seconds) if cpu_seconds > 0 else None
   return {"config": "C2 Llama-3-70B TP8 KV (80 layers x K/V, 64 tok x 1 head x 128 bf16 "
                     f"blocks), {nblk}-block pool, fp8 e4m3 host tier of {host_blocks} blocks, "
                     f"{B} offloads + {B} reloads per step",
+          "cpu_baseline": cpu,
           "ms_per_step": round(ms, 3),
           "bf16_gbs": round(bf16_bytes / (ms * 1e-3) / 1e9, 2),
           "pcie_gbs": round(wire / (ms * 1e-3) / 1e9, 2),
@@ -801,7 +895,9 @@ def run_ours(args):
   mgr.close()
   del mgr, full, storages, table
   torch.cuda.empty_cache()
-  c2 = run_c2_fp8(torch, rank, device, 5, 3, max_over_ranks)
+  c2 = run_c2_fp8(torch, rank, device, 5, 3, max_over_ranks,
+                  cpu_seconds=5.0 if (rank == 0 and world == 1 and not args.no_cpu_baseline)
+                  else 0.0)
   torch.cuda.empty_cache()
   if rank == 0:
     line["c2_fp8"] = c2
@@ -811,6 +907,16 @@ def run_ours(args):
     torch.cuda.empty_cache()
     exchange["handoff"] = run_handoff(torch, dist, rank, world, device, 3, 2)
     torch.cuda.empty_cache()
+    if rank == 0 and not args.no_cpu_baseline:
+      # the same exchanges on the host cores (bounded samples; the other
+      # ranks wait at the closing barrier)
+      from tpu_sync_b200 import reshard_plan as rp
+      half = world // 2
+      specs = [rp.VariableSpec(n, sh, workloads.mesh_for(sh, "fsdp", half),
+                               workloads.mesh_for(sh, split, half), layer_idx=i)
+               for i, (n, sh, split) in enumerate(workloads.llama3_8b_params())]
+      exchange["weight_sync"]["cpu_baseline"] = cpu_c4_reshard(rp.build_plan(specs), specs, 5.0)
+      exchange["handoff"]["cpu_baseline"] = cpu_c3_relayout(5.0)
   if rank == 0:
     line.update(exchange)
     print(json.dumps(line), flush=True)

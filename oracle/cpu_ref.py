@@ -29,6 +29,17 @@ def lib():
     l.oref_reshard_f32_bf16.argtypes = [ctypes.c_void_p, ctypes.c_void_p, P(ctypes.c_int64),
                                         ctypes.c_int64, ctypes.c_int]
     l.oref_reshard_f32_bf16.restype = ctypes.c_int
+    l.oref_e4m3.argtypes = [ctypes.c_float]
+    l.oref_e4m3.restype = ctypes.c_uint8
+    l.oref_extract_fp8.argtypes = [P(ctypes.c_void_p), P(ctypes.c_uint64), P(ctypes.c_uint64),
+                                   ctypes.c_int, P(ctypes.c_int64), ctypes.c_int64,
+                                   ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int]
+    l.oref_extract_fp8.restype = ctypes.c_int
+    l.oref_relayout.argtypes = [P(ctypes.c_void_p), P(ctypes.c_void_p), ctypes.c_int, ctypes.c_int,
+                                ctypes.c_uint64, ctypes.c_int64, ctypes.c_int64,
+                                P(ctypes.c_int32), P(ctypes.c_int32), ctypes.c_int64,
+                                ctypes.c_int64, ctypes.c_int]
+    l.oref_relayout.restype = ctypes.c_int
     _lib = l
   return _lib
 
@@ -59,3 +70,29 @@ def reshard_f32_bf16(src: np.ndarray, dst_bits: np.ndarray, chunks, threads: int
   lib().oref_reshard_f32_bf16(src.ctypes.data, dst_bits.ctypes.data,
                               c.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)),
                               c.shape[0], int(threads))
+
+
+def extract_fp8(storages, ids, staging, pitch, stage_offs, scale_off, threads):
+  """storages: numpy uint16 [blocks, elems] per storage (bf16 bits);
+  staging: numpy uint8 [n, pitch] (fp8 payloads + fp32 scales)."""
+  n = len(storages)
+  S = (ctypes.c_void_p * n)(*[a.ctypes.data for a in storages])
+  E = (ctypes.c_uint64 * n)(*[a.shape[1] for a in storages])
+  O = (ctypes.c_uint64 * n)(*[int(x) for x in stage_offs])
+  i = np.ascontiguousarray(ids, np.int64)
+  lib().oref_extract_fp8(S, E, O, n, i.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)), i.size,
+                         staging.ctypes.data, int(pitch), int(scale_off), int(threads))
+
+
+def relayout(src_pages, dst_pages, heads, head_bytes, st_tok, dt_tok, src_table, dst_table,
+             tokens, threads):
+  """src_pages / dst_pages: numpy uint8 arrays, one per storage."""
+  n = len(src_pages)
+  S = (ctypes.c_void_p * n)(*[a.ctypes.data for a in src_pages])
+  D = (ctypes.c_void_p * n)(*[a.ctypes.data for a in dst_pages])
+  st = np.ascontiguousarray(src_table, np.int32)
+  dt = np.ascontiguousarray(dst_table, np.int32)
+  P32 = ctypes.POINTER(ctypes.c_int32)
+  lib().oref_relayout(S, D, n, int(heads), int(head_bytes), int(st_tok), int(dt_tok),
+                      st.ctypes.data_as(P32), dt.ctypes.data_as(P32), st.shape[0], int(tokens),
+                      int(threads))

@@ -188,3 +188,62 @@ def test_normalized_plan_moves_same_elements():
     ors.apply_element_chunks(src, a, raw.chunks[key], False)
     ors.apply_element_chunks(src, b, norm.chunks[key], False)
     np.testing.assert_array_equal(a, b)
+
+
+# ---------------------------------------------------------------------------
+# C restatements used as the timed CPU baselines of C2 / C3
+# ---------------------------------------------------------------------------
+
+def test_c_e4m3_encoder_matches_oracle():
+  from oracle import cpu_ref
+  rng = np.random.default_rng(8)
+  vals = np.concatenate([
+      rng.standard_normal(20000).astype(np.float32) * np.float32(100),
+      (rng.standard_normal(20000) * 2.0 ** rng.integers(-20, 10, 20000)).astype(np.float32),
+      np.array([0.0, -0.0, 448.0, -448.0, 464.0, 465.0, 1e30, 2 ** -9, 2 ** -10, 3 * 2 ** -11,
+                2 ** -6, 2 ** -6 - 2 ** -12, np.inf, -np.inf], np.float32)])
+  want = ofp8.e4m3_encode(vals)
+  got = np.array([cpu_ref.lib().oref_e4m3(float(v)) for v in vals], np.uint8)
+  np.testing.assert_array_equal(got, want)
+
+
+def test_c_extract_fp8_matches_oracle():
+  from oracle import cpu_ref
+  bits = np.arange(1 << 16, dtype=np.uint32).astype(np.uint16)
+  finite = bits[(bits & 0x7FFF) < 0x7F80]  # every finite bf16 bit pattern
+  units = [np.zeros(8192, np.uint16) for _ in range(8)]
+  for i, chunk in enumerate(np.array_split(finite, 8)):
+    units[i][:chunk.size] = chunk
+  rng = np.random.default_rng(3)
+  for _ in range(40):
+    amax_bits = int(rng.integers(1, 0x7F80))
+    u = rng.integers(0, amax_bits + 1, 8192, dtype=np.uint32).astype(np.uint16)
+    u |= (rng.integers(0, 2, 8192, dtype=np.uint32) << 15).astype(np.uint16)
+    u[0] = amax_bits
+    units.append(u)
+  store = np.stack(units)                 # one storage, [blocks, 8192]
+  ids = list(range(store.shape[0]))[::-1]
+  payload, scales = ofp8.extract_fp8([store], ids)
+  pitch, scale_off = 8192 + 16, 8192
+  staging = np.zeros((len(ids), pitch), np.uint8)
+  cpu_ref.extract_fp8([store], ids, staging, pitch, [0], scale_off, 4)
+  np.testing.assert_array_equal(staging[:, :8192], payload[:, 0])
+  np.testing.assert_array_equal(staging[:, scale_off:scale_off + 4].copy().view(np.float32)[:, 0],
+                                scales[:, 0])
+
+
+def test_c_relayout_matches_oracle():
+  from oracle import cpu_ref
+  rng = np.random.default_rng(5)
+  n_st, n_seqs, T, H, HB = 3, 2, 256, 2, 16
+  st = rng.permutation(n_seqs * T // 16).reshape(n_seqs, -1).astype(np.int32)
+  dt = rng.permutation(n_seqs * T // 64).reshape(n_seqs, -1).astype(np.int32)
+  src = [rng.integers(0, 256, (n_seqs * T // 16, 16 * H * HB), dtype=np.uint8) for _ in range(n_st)]
+  got = [np.zeros((n_seqs * T // 64, 64 * H * HB), np.uint8) for _ in range(n_st)]
+  cpu_ref.relayout(src, got, H, HB, 16, 64, st, dt, T, 2)
+  sg = dict(block_tokens=16, heads=H, head_bytes=HB, head_major=1)
+  dg = dict(block_tokens=64, heads=H, head_bytes=HB, head_major=0)
+  for s in range(n_st):
+    want = np.zeros_like(got[s])
+    ors.relayout(src[s], want, sg, dg, st, dt, T)
+    np.testing.assert_array_equal(got[s], want)
