@@ -696,6 +696,57 @@ TS_API int ts_store_lru_op(ts_store* store, int op, const uint8_t* key, int64_t 
                            int64_t* out_val, uint8_t* out_key, int64_t out_key_cap,
                            int64_t* out_key_len);
 
+/* ---- Crash-persistent KV block metadata --------------------------------
+ * KVCacheMetadata (tpu_sync/kv_cache/kv_cache_metadata.h:19-141,
+ * kv_cache_metadata.cc:27-188) on the reference's byte layout: a 128-byte
+ * header {u64 magic "RAIDENKM", u32 version 1, u32 num_blocks, u32 entry
+ * size 128, char model_uid[64] at offset 20} and num_blocks 128-byte entries
+ * {u64 seq, u16 hash_len, u8 valid at offset 10, hash[112] at offset 16}. */
+typedef struct ts_kv_metadata ts_kv_metadata;
+/* KVCacheMetadata::RequiredSizeBytes; 0 for num_blocks <= 0. */
+TS_API uint64_t ts_kv_metadata_required_bytes(int num_blocks);
+/* KVCacheMetadataShmRegion::AttachOrFormat (kv_cache_metadata_shm.cc:29-130):
+ * attach the /dev/shm segment `key` (leading '/' added) when its table
+ * validates for (num_blocks, model_uid) -> *warm = 1, else unlink it and
+ * format a fresh one -> *warm = 0. */
+TS_API int ts_kv_metadata_open(const char* key, int num_blocks, const char* model_uid,
+                               ts_kv_metadata** out, int* warm);
+/* KVCacheMetadata::Format (attach == 0) / Attach (attach != 0) on caller
+ * memory (64-byte aligned, >= required bytes), which must outlive the handle. */
+TS_API int ts_kv_metadata_on_region(void* region, uint64_t size, int num_blocks,
+                                    const char* model_uid, int attach, ts_kv_metadata** out);
+/* KVCacheMetadata::Set / Clear. */
+TS_API int ts_kv_metadata_set(ts_kv_metadata* m, int block_id, const uint8_t* hash,
+                              int64_t len, uint64_t seq);
+TS_API int ts_kv_metadata_clear(ts_kv_metadata* m, int block_id);
+/* KVCacheMetadata::ValidEntries in block order: ids, seqs and the hashes
+ * packed into buf (hash i = buf[offs[i] .. offs[i+1])).  *n_out / *need_bytes
+ * always receive the sizes; TS_RESOURCE_EXHAUSTED (nothing written) when
+ * cap < *n_out or buf_len < *need_bytes (offs holds cap + 1 values). */
+TS_API int ts_kv_metadata_entries(ts_kv_metadata* m, int32_t* block_ids, uint64_t* seqs,
+                                  uint8_t* buf, int64_t buf_len, int64_t* offs, int64_t cap,
+                                  int64_t* n_out, int64_t* need_bytes);
+/* KVCacheMetadataShmRegion::Reformat (kv_cache_metadata_shm.cc:148-160). */
+TS_API int ts_kv_metadata_reformat(ts_kv_metadata* m);
+TS_API int ts_kv_metadata_info(ts_kv_metadata* m, int* num_blocks, int* warm);
+/* Unmaps (and, with unlink_shm, removes the segment of) an opened table. */
+TS_API int ts_kv_metadata_close(ts_kv_metadata* m, int unlink_shm);
+/* KVCacheStore::Evict (kv_cache_store.cc:1553-1570): unpinned HOST /
+ * HOST_AND_HBM entries among the keys are erased and their host blocks
+ * freed; *evicted = how many. */
+TS_API int ts_store_evict(ts_store* store, const uint8_t* keys, const int64_t* offs, int64_t n,
+                          int64_t* evicted);
+/* Attach (or with NULL detach) a table to a store: host-resident entries are
+ * recorded on insert / save / load completion and cleared on eviction and
+ * rollback (HostOffloadBackend::SetMetadataEntry / ClearMetadataEntry,
+ * host_offload_backend.cc:1224-1256).  The table must outlive the store or
+ * be detached first. */
+TS_API int ts_store_attach_metadata(ts_store* store, ts_kv_metadata* m);
+/* KVCacheStore::RecoverFromLocalManifest (kv_cache_store.cc:1541-1551,
+ * host_offload_backend.cc:559-617): rebuilds an empty store's LRU from the
+ * table's newest entry per hash, in seq order, as HOST blocks. */
+TS_API int ts_store_recover(ts_store* store, int64_t* recovered);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

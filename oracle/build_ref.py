@@ -1,14 +1,16 @@
 """Compiles reference sources into test oracle binaries.
 
-    python oracle/build_ref.py     # -> oracle/_ref/lru_ref, oracle/_ref/pool_ref
+    python oracle/build_ref.py     # -> oracle/_ref/{lru_ref, pool_ref, meta_ref}
 
 * lru_ref: oracle/ref_lru_driver.cc over the header-only LRUCache
   (tpu_sync/kv_cache/lru_cache.h);
-* pool_ref: oracle/ref_pool_driver.cc linked with tpu_sync/kv_cache/pool_layout.cc.
+* pool_ref: oracle/ref_pool_driver.cc linked with tpu_sync/kv_cache/pool_layout.cc;
+* meta_ref: oracle/ref_meta_driver.cc linked with tpu_sync/kv_cache/kv_cache_metadata.cc
+  and kv_cache_metadata_shm.cc.
 
 g++ compiles them where they lie in the reference checkout (REFERENCE_ROOT,
 default /root/reference); oracle/shim stands in for the few absl types they
-use (flat_hash_map, Status, StatusOr, StrCat, Span) and for the two proto
+use (flat_hash_map, Status, StatusOr, StrCat, Span, string_view, LOG) and for the two proto
 message classes pool_layout.h names.  Nothing is copied from the reference;
 the binaries go to oracle/_ref/ only.  Test infrastructure: tests/ use them to
 pin the product's LRU and pool geometry (and tests/golden/make_pool_golden.py
@@ -65,6 +67,27 @@ def build_pool(force: bool = False) -> Path | None:
   return POOL_OUT
 
 
+META_OUT = HERE / "_ref" / "meta_ref"
+
+
+def build_meta(force: bool = False) -> Path | None:
+  """Builds meta_ref if the reference checkout is present; returns its path."""
+  ref = reference_root()
+  kv = ref / "tpu_sync" / "kv_cache"
+  ccs = [kv / "kv_cache_metadata.cc", kv / "kv_cache_metadata_shm.cc"]
+  src = HERE / "ref_meta_driver.cc"
+  if META_OUT.exists() and not force and META_OUT.stat().st_mtime >= src.stat().st_mtime:
+    return META_OUT
+  if not all(c.exists() for c in ccs):
+    return META_OUT if META_OUT.exists() else None
+  META_OUT.parent.mkdir(parents=True, exist_ok=True)
+  cxx = shutil.which("g++") or "c++"
+  subprocess.run([cxx, "-std=c++17", "-O1", f"-I{HERE / 'shim'}", f"-I{ref}", str(src),
+                  *map(str, ccs), "-o", str(META_OUT)], check=True)
+  return META_OUT
+
+
 if __name__ == "__main__":
   print(build(force=True))
   print(build_pool(force=True))
+  print(build_meta(force=True))

@@ -1,5 +1,5 @@
 // Minimal stand-in for absl::Status used ONLY to compile the reference's
-// pool_layout.cc as a test oracle (oracle/build_ref.py).  Carries a code and
+// reference sources as test oracles (oracle/build_ref.py).  Carries a code and
 // a message; codes are absl::StatusCode's numeric values.
 #pragma once
 #include <string>
@@ -9,7 +9,7 @@ namespace absl {
 
 enum class StatusCode : int {
   kOk = 0, kInvalidArgument = 3, kNotFound = 5, kFailedPrecondition = 9,
-  kOutOfRange = 11, kInternal = 13,
+  kResourceExhausted = 8, kOutOfRange = 11, kInternal = 13,
 };
 
 class Status {
@@ -30,6 +30,7 @@ inline Status OkStatus() { return Status(); }
 inline Status InvalidArgumentError(std::string m) { return Status(StatusCode::kInvalidArgument, std::move(m)); }
 inline Status OutOfRangeError(std::string m) { return Status(StatusCode::kOutOfRange, std::move(m)); }
 inline Status InternalError(std::string m) { return Status(StatusCode::kInternal, std::move(m)); }
+inline Status ResourceExhaustedError(std::string m) { return Status(StatusCode::kResourceExhausted, std::move(m)); }
 inline Status FailedPreconditionError(std::string m) { return Status(StatusCode::kFailedPrecondition, std::move(m)); }
 
 }  // namespace absl

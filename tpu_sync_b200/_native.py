@@ -309,6 +309,25 @@ _SIGS = {
     "ts_store_lru_op": (ctypes.c_int, [_V, ctypes.c_int, ctypes.c_char_p, ctypes.c_int64,
                                        ctypes.POINTER(BlockInfo), ctypes.POINTER(BlockInfo),
                                        c_i64_p, ctypes.c_char_p, ctypes.c_int64, c_i64_p]),
+    "ts_kv_metadata_required_bytes": (ctypes.c_uint64, [ctypes.c_int]),
+    "ts_kv_metadata_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int, ctypes.c_char_p,
+                                           ctypes.POINTER(_V), ctypes.POINTER(ctypes.c_int)]),
+    "ts_kv_metadata_on_region": (ctypes.c_int, [_V, ctypes.c_uint64, ctypes.c_int,
+                                                ctypes.c_char_p, ctypes.c_int,
+                                                ctypes.POINTER(_V)]),
+    "ts_kv_metadata_set": (ctypes.c_int, [_V, ctypes.c_int, ctypes.c_char_p, ctypes.c_int64,
+                                          ctypes.c_uint64]),
+    "ts_kv_metadata_clear": (ctypes.c_int, [_V, ctypes.c_int]),
+    "ts_kv_metadata_entries": (ctypes.c_int, [_V, c_i32_p, c_u64_p, ctypes.c_char_p,
+                                              ctypes.c_int64, c_i64_p, ctypes.c_int64, c_i64_p,
+                                              c_i64_p]),
+    "ts_kv_metadata_reformat": (ctypes.c_int, [_V]),
+    "ts_kv_metadata_info": (ctypes.c_int, [_V, ctypes.POINTER(ctypes.c_int),
+                                           ctypes.POINTER(ctypes.c_int)]),
+    "ts_kv_metadata_close": (ctypes.c_int, [_V, ctypes.c_int]),
+    "ts_store_attach_metadata": (ctypes.c_int, [_V, _V]),
+    "ts_store_recover": (ctypes.c_int, [_V, c_i64_p]),
+    "ts_store_evict": (ctypes.c_int, [_V, ctypes.c_char_p, c_i64_p, ctypes.c_int64, c_i64_p]),
     "ts_event_query": (ctypes.c_int, [_V]),
     "ts_event_wait": (ctypes.c_int, [_V, ctypes.c_int64]),
     "ts_event_error": (ctypes.c_int, [_V, ctypes.c_char_p, ctypes.c_size_t]),
@@ -352,7 +371,7 @@ def lib() -> ctypes.CDLL:
 
 def last_error() -> str:
   msg = lib().ts_last_error()
-  return msg.decode() if msg else ""
+  return msg.decode(errors="replace") if msg else ""
 
 
 def check(rc: int, prefix: str = "") -> None:

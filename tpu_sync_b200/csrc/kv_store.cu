@@ -24,6 +24,7 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstring>
 #include <list>
 #include <mutex>
@@ -33,6 +34,7 @@
 #include <unordered_set>
 #include <vector>
 
+#include "kv_metadata.h"
 #include "ts_internal.h"
 
 namespace tsb {
@@ -344,10 +346,30 @@ struct ts_store {
   };
   std::vector<Op> saves, loads;
   std::vector<std::string> done_saves, failed_saves, done_loads, failed_loads;
+  // optional crash-persistent record of host-resident blocks
+  ts_kv_metadata* meta = nullptr;
+  uint64_t next_seq = 0;
 };
 
 namespace tsb {
 namespace {
+
+bool host_resident(const BlockId& b) {
+  return b.status == TS_BLOCK_HOST || b.status == TS_BLOCK_HOST_AND_HBM;
+}
+
+// SetMetadataEntry / ClearMetadataEntry
+// (tpu_sync/kv_cache/host_offload_backend.cc:1224-1256): only entries that
+// hold host bytes are recorded; a failed record is not fatal there either.
+void meta_set(ts_store* s, const std::string& hash, const BlockId& b) {
+  if (s->meta == nullptr || !host_resident(b)) return;
+  ts_kv_metadata_table(s->meta)->set(b.host_block_id, hash.data(), hash.size(), s->next_seq++);
+}
+
+void meta_clear(ts_store* s, const BlockId& b) {
+  if (s->meta == nullptr || !host_resident(b)) return;
+  ts_kv_metadata_table(s->meta)->clear(b.host_block_id);
+}
 
 // HostOffloadBackend::Lookup, local index only: every hit is found (and
 // pinned when asked) in one sweep; the answer ends at the first miss and the
@@ -396,6 +418,7 @@ int allocate_host_ids(ts_store* s, int needed, std::vector<int>* ids) {
       if (b != nullptr && s->lru.pin_count(k) == 0 &&
           (b->status == TS_BLOCK_HOST || b->status == TS_BLOCK_HOST_AND_HBM)) {
         host_ids.push_back(b->host_block_id);
+        meta_clear(s, *b);
         s->lru.erase(k);
       }
     }
@@ -433,6 +456,7 @@ void poll_locked(ts_store* s) {
         if (b != nullptr) {
           b->host_block_id = op.host_ids[k];
           b->status = TS_BLOCK_HOST_AND_HBM;
+          meta_set(s, op.hashes[k], *b);
           updated.push_back(op.hashes[k]);
         }
         s->done_saves.push_back(op.hashes[k]);
@@ -461,6 +485,7 @@ void poll_locked(ts_store* s) {
         if (b != nullptr) {
           b->device_block_id = op.dev_ids[k];
           b->status = TS_BLOCK_HOST_AND_HBM;
+          meta_set(s, op.hashes[k], *b);
           updated.push_back(op.hashes[k]);
         }
         s->done_loads.push_back(op.hashes[k]);
@@ -575,7 +600,11 @@ extern "C" int ts_store_insert(ts_store* s, const uint8_t* keys, const int64_t* 
     }
     if (int64_t(i) < n_slices) {
       tsb::BlockId* b = s->lru.peek(h[i]);
-      if (b != nullptr && b->status == TS_BLOCK_HBM) *b = slice(i);
+      if (b != nullptr && b->status == TS_BLOCK_HBM) {
+        tsb::meta_clear(s, *b);
+        *b = slice(i);
+        tsb::meta_set(s, h[i], *b);
+      }
     }
   }
   if (s->lru.available_space() < fresh.size()) {
@@ -584,14 +613,19 @@ extern "C" int ts_store_insert(ts_store* s, const uint8_t* keys, const int64_t* 
   }
   for (auto it = fresh.rbegin(); it != fresh.rend(); ++it) {
     const size_t i = *it;
+    if (const tsb::BlockId* stale = s->lru.peek_any(h[i])) tsb::meta_clear(s, *stale);
     std::string demoted;
     s->lru.put(h[i], int64_t(i) < n_slices ? slice(i) : tsb::BlockId(), &demoted);
+    if (int64_t(i) < n_slices) tsb::meta_set(s, h[i], slice(i));
   }
   for (size_t f = 0; f < fresh.size(); ++f) {
     if (!s->lru.pin(h[fresh[f]])) {
       for (size_t j = 0; j < f; ++j) s->lru.unpin(h[fresh[j]]);
       for (size_t j : existing) s->lru.unpin(h[j]);
-      for (size_t j : fresh) s->lru.erase(h[j]);
+      for (size_t j : fresh) {
+        if (const tsb::BlockId* v = s->lru.peek_any(h[j])) tsb::meta_clear(s, *v);
+        s->lru.erase(h[j]);
+      }
       return set_error(TS_RESOURCE_EXHAUSTED, refused);
     }
   }
@@ -834,4 +868,89 @@ extern "C" int ts_store_lru_op(ts_store* s, int op, const uint8_t* key, int64_t 
     case 9: *out_val = int64_t(s->lru.size()); return TS_OK;
     default: return set_error(TS_INVALID_ARGUMENT, "unknown lru op");
   }
+}
+
+// KVCacheStore::Evict / HostOffloadBackend::Evict (kv_cache_store.cc:1553-1570,
+// host_offload_backend.cc:656-686): unpinned host-resident entries among the
+// keys leave the index and their host blocks return to the allocator.
+extern "C" int ts_store_evict(ts_store* s, const uint8_t* keys, const int64_t* offs, int64_t n,
+                              int64_t* evicted) {
+  tsb::clear_error();
+  if (!s || !evicted || n < 0 || (n > 0 && (!keys || !offs)))
+    return set_error(TS_INVALID_ARGUMENT, "invalid arguments");
+  std::lock_guard<std::mutex> lock(s->mu);
+  std::vector<int> host_ids;
+  for (int64_t i = 0; i < n; ++i) {
+    const std::string k(reinterpret_cast<const char*>(keys) + offs[i], size_t(offs[i + 1] - offs[i]));
+    const tsb::BlockId* b = s->lru.peek_any(k);
+    if (b != nullptr && s->lru.pin_count(k) == 0 && tsb::host_resident(*b)) {
+      host_ids.push_back(b->host_block_id);
+      tsb::meta_clear(s, *b);
+      s->lru.erase(k);
+    }
+  }
+  if (!host_ids.empty()) s->alloc.deallocate(host_ids);
+  *evicted = int64_t(host_ids.size());
+  return TS_OK;
+}
+
+extern "C" int ts_store_attach_metadata(ts_store* s, ts_kv_metadata* meta) {
+  tsb::clear_error();
+  if (!s) return set_error(TS_INVALID_ARGUMENT, "null store");
+  std::lock_guard<std::mutex> lock(s->mu);
+  // Host block ids index the table; one the table cannot hold goes
+  // unrecorded, as a failed Set is only logged by the reference.
+  s->meta = meta;
+  return TS_OK;
+}
+
+// KVCacheStore::RecoverFromLocalManifest / HostOffloadBackend's
+// (tpu_sync/kv_cache/kv_cache_store.cc:1541-1551,
+// host_offload_backend.cc:559-617): the newest entry per hash, in recency
+// order, becomes a HOST entry of the LRU over its (now allocated) host block;
+// older duplicates are cleared from the table.
+extern "C" int ts_store_recover(ts_store* s, int64_t* recovered) {
+  tsb::clear_error();
+  if (!s || !recovered) return set_error(TS_INVALID_ARGUMENT, "null argument");
+  std::lock_guard<std::mutex> lock(s->mu);
+  *recovered = 0;
+  if (s->lru.size() != 0)
+    return set_error(TS_FAILED_PRECONDITION,
+                     "RecoverFromLocalManifest can only be called on an empty cache store");
+  if (s->meta == nullptr)
+    return set_error(TS_FAILED_PRECONDITION, "KVCacheMetadata is required for crash recovery");
+  tsb::meta::Table* t = ts_kv_metadata_table(s->meta);
+  const std::vector<tsb::meta::Record> entries = t->valid_entries();
+  if (entries.empty()) return TS_OK;
+  std::unordered_map<std::string, const tsb::meta::Record*> newest;
+  for (const auto& e : entries) {
+    auto it = newest.find(e.hash);
+    if (it == newest.end())
+      newest.emplace(e.hash, &e);
+    else if (e.seq > it->second->seq)
+      it->second = &e;
+  }
+  std::vector<const tsb::meta::Record*> keep;
+  for (const auto& [hash, e] : newest) keep.push_back(e);
+  std::sort(keep.begin(), keep.end(),
+            [](const tsb::meta::Record* a, const tsb::meta::Record* b) { return a->seq < b->seq; });
+  std::vector<int> ids;
+  for (const auto* e : keep) ids.push_back(e->block_id);
+  int rc = s->alloc.allocate_target(ids);
+  if (rc != TS_OK) return rc;
+  uint64_t max_seq = 0;
+  for (const auto* e : keep) {
+    tsb::BlockId b;
+    b.host_block_id = e->block_id;
+    b.device_block_id = -1;
+    b.status = TS_BLOCK_HOST;
+    std::string demoted;
+    s->lru.put(e->hash, b, &demoted);
+    max_seq = std::max(max_seq, e->seq);
+  }
+  s->next_seq = max_seq + 1;
+  for (const auto& e : entries)
+    if (newest.at(e.hash)->block_id != e.block_id) t->clear(e.block_id);
+  *recovered = int64_t(keep.size());
+  return TS_OK;
 }

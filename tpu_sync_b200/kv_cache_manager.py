@@ -27,6 +27,7 @@ signature compatibility and have no effect: there is no network path here.
 from __future__ import annotations
 
 import ctypes
+import os
 from typing import Any, Dict, List, Optional, Sequence, Tuple
 
 import numpy as np
@@ -170,6 +171,19 @@ class KVCacheManager:
         descs[i].dim0 = t.shape[0]
         descs[i].device = t.device.index
         i += 1
+    if not shm_name and os.environ.get("RAIDEN_SHM_KEY"):
+      # CreateHostMemoryAllocator / SharedMemoryHostMemoryAllocator
+      # (tpu_sync/core/utils.h:48-75, core/host_memory_allocator.cc:255-280):
+      # the host tier lives in /dev/shm as RAIDEN_SHM_KEY [+ "_" +
+      # RAIDEN_SHM_SERVER_NAME] + "_dev_<device>", validated against
+      # RAIDEN_SHM_MODEL_UID (default "default_model") on a warm restart.
+      shm_name = os.environ["RAIDEN_SHM_KEY"]
+      server = os.environ.get("RAIDEN_SHM_SERVER_NAME", "")
+      if server:
+        shm_name += "_" + server
+      shm_name += f"_dev_{grid[0][0].device.index}"
+      if not model_uid:
+        model_uid = os.environ.get("RAIDEN_SHM_MODEL_UID", "default_model")
     modes = {"staged": 0, "direct_d2h": 1, "direct_h2d": 2, "direct": 3}
     if mode not in modes:
       raise ValueError(f"mode must be one of {sorted(modes)}")

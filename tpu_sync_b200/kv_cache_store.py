@@ -21,6 +21,7 @@ from __future__ import annotations
 
 import ctypes
 import enum
+import logging
 from dataclasses import dataclass, field
 from typing import List, Optional, Sequence, Tuple
 
@@ -68,7 +69,8 @@ class KVCacheStore:
                raiden_id: Optional[RaidenId] = None, *, num_shards: int = 1,
                store_server_ip: str = "127.0.0.1", shard_size_bytes: int = 0,
                raiden_controller_port: int = 0, expected_worker_count: int = 0,
-               kv_pool_group: str = "", manager=None, host_blocks: Optional[int] = None):
+               kv_pool_group: str = "", manager=None, host_blocks: Optional[int] = None,
+               metadata=None):
     if num_shards < 1:
       raise ValueError("num_shards must be >= 1")
     if global_registry_address:
@@ -82,11 +84,68 @@ class KVCacheStore:
         manager._mgr if manager is not None else None, int(capacity), int(host_blocks),
         ctypes.byref(h)), "KVCacheStore: ")
     self._impl = h
+    # KVCacheStoreWrapper (kv_cache_store_wrapper.cc:111-185): with
+    # RAIDEN_SHM_KEY set, the table lives in /dev/shm beside the host tier's
+    # data segment; a table that survived a crash (warm) rebuilds the LRU, and
+    # a failed recovery falls back to a cold start over a reformatted table.
+    self._meta_region = None
+    self._metadata = None
+    self.recovered_blocks = 0
+    if metadata is None and num_shards > 0:
+      from tpu_sync_b200 import kv_metadata
+      key = kv_metadata.metadata_shm_key()
+      if key:
+        try:
+          self._meta_region = kv_metadata.KVCacheMetadataShmRegion.attach_or_format(
+              key, int(capacity), kv_metadata.model_uid_from_env())
+          metadata = self._meta_region.metadata
+        except (ValueError, RuntimeError) as e:
+          logging.warning("KV metadata table unavailable, serving without crash "
+                          "recovery: %s", e)
+    if metadata is not None:
+      self._metadata = metadata
+      _native.check(_native.lib().ts_store_attach_metadata(self._impl, metadata._h),
+                    "KVCacheStore: ")
+    if self._meta_region is not None and self._meta_region.warm:
+      try:
+        self.recovered_blocks = self.recover_from_local_manifest()
+        logging.info("Recovered %d blocks from the local KV metadata table",
+                     self.recovered_blocks)
+      except RuntimeError as e:
+        logging.warning("KV metadata recovery failed, falling back to a cold start: %s", e)
+        try:
+          self._meta_region.reformat()
+        except RuntimeError as e2:
+          logging.warning("Failed to reformat the KV metadata table: %s", e2)
 
   def close(self) -> None:
     if getattr(self, "_impl", None):
       _native.lib().ts_store_destroy(self._impl)
       self._impl = None
+    # the table outlives the store; its segment stays for the next start
+    if getattr(self, "_meta_region", None) is not None:
+      self._meta_region.close()
+      self._meta_region = None
+
+  def evict(self, block_hashes: List[bytes]) -> int:
+    """KVCacheStore::Evict (kv_cache_store.cc:1553-1570): drop unpinned
+    host-resident entries and free their host blocks; returns how many."""
+    keys, offs = _pack(block_hashes)
+    n = ctypes.c_int64()
+    _native.check(_native.lib().ts_store_evict(self._impl, keys, _native.i64_ptr(offs),
+                                               len(block_hashes), ctypes.byref(n)),
+                  "KVCacheStore evict: ")
+    return n.value
+
+  def recover_from_local_manifest(self) -> int:
+    """KVCacheStore::RecoverFromLocalManifest (kv_cache_store.cc:1541-1551):
+    rebuild an empty store's index from the metadata table's newest entry per
+    hash (HOST blocks at their recorded host block ids, LRU order by seq);
+    returns the number of recovered blocks."""
+    n = ctypes.c_int64()
+    _native.check(_native.lib().ts_store_recover(self._impl, ctypes.byref(n)),
+                  "RecoverFromLocalManifest: ")
+    return n.value
 
   def __del__(self):
     try:
