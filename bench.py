@@ -61,6 +61,12 @@ def parse():
   p.add_argument("--no-cpu-baseline", action="store_true")
   p.add_argument("--no-exchange", action="store_true",
                  help="skip the N>=2 weight-sync and hand-off measurements")
+  p.add_argument("--mode", default="staged",
+                 choices=["staged", "direct_d2h", "direct_h2d", "direct"],
+                 help="C1 manager transfer mode (staged: copy-engine DMAs through HBM "
+                      "staging; direct*: SM-driven PCIe to the mapped host tier)")
+  p.add_argument("--copy-streams", type=int, default=2)
+  p.add_argument("--chunk-blocks", type=int, default=0, help="0 = manager default")
   p.add_argument("--kernel-case", default="",
                  choices=["", "extract", "insert", "extract_fp8", "insert_fp8", "pool_reshard"],
                  help="run a few launches of one kernel on a small case (for ncu)")
@@ -715,7 +721,9 @@ def run_ours(args):
   local_ranks = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
   fit = int(0.45 * mem_available_bytes() / max(local_ranks, 1) // pitch)
   host_blocks = max(4 * B, min(want_host, fit))
-  mgr = KVCacheManager([[t] for t in storages], host_blocks_to_allocate=host_blocks)
+  mgr = KVCacheManager([[t] for t in storages], host_blocks_to_allocate=host_blocks,
+                       mode=args.mode, copy_streams=args.copy_streams,
+                       chunk_blocks=args.chunk_blocks)
 
   pcie = measure_pcie(torch, device)
 
@@ -862,6 +870,7 @@ def run_ours(args):
                       "of 512, through the tier-2 store (reference LRU + host block "
                       "allocator); steps from the middle of the trace"),
             "trace_hit_rate": trace_stats["hit_rate"],
+            "transfer_mode": args.mode, "copy_streams": args.copy_streams,
             "parallelism": f"replicas x{world}"},
         "per_gpu_gbs": round(value / world, 3),
         "pcie": {"offload_d2h_gbs": round(d2h_gbs, 2), "reload_h2d_gbs": round(h2d_gbs, 2),

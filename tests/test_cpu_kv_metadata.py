@@ -455,3 +455,22 @@ def test_crash_restart_recovers_host_index():
       assert "RECOVERED 0 []" in c.stdout, c.stdout
   finally:
     _unlink(key + "_metadata")
+
+
+def test_store_keeps_a_dropped_region_mapped():
+  """A store holding a shm table keeps it mapped after the caller dropped
+  the region object (the table handle owns the mapping)."""
+  import gc
+  key = _shm_key()
+  try:
+    reg = km.KVCacheMetadataShmRegion.attach_or_format(key, 4, "m")
+    store = KVCacheStore(4, host_blocks=4, metadata=reg.metadata)
+    del reg
+    gc.collect()
+    assert _insert_resident(store, [b"k"], [_host(2)])
+    store.close()
+    reg = km.KVCacheMetadataShmRegion.attach_or_format(key, 4, "m")
+    assert reg.warm and reg.metadata.valid_entries() == [E(2, b"k", 0)]
+    reg.close()
+  finally:
+    _unlink(key)

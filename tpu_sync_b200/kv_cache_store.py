@@ -122,10 +122,12 @@ class KVCacheStore:
     if getattr(self, "_impl", None):
       _native.lib().ts_store_destroy(self._impl)
       self._impl = None
-    # the table outlives the store; its segment stays for the next start
+    # the store is gone, so its own table can be unmapped; the segment stays
+    # in /dev/shm for the next start
     if getattr(self, "_meta_region", None) is not None:
       self._meta_region.close()
       self._meta_region = None
+    self._metadata = None
 
   def evict(self, block_hashes: List[bytes]) -> int:
     """KVCacheStore::Evict (kv_cache_store.cc:1553-1570): drop unpinned

@@ -61,11 +61,13 @@ def aligned_region(num_blocks: int) -> np.ndarray:
 
 
 class KVCacheMetadata:
-  """A non-owning view of a table (the region must outlive it)."""
+  """A table handle.  Over caller memory it keeps that buffer alive; over a
+  /dev/shm segment it owns the mapping, so a store holding the table keeps
+  it mapped even after the KVCacheMetadataShmRegion object is gone."""
 
   def __init__(self, handle, owner=None):
     self._h = handle
-    self._owner = owner  # keeps a caller buffer alive; None for shm tables
+    self._owner = owner  # the caller buffer of a region table, else None
 
   @classmethod
   def _on_region(cls, region: np.ndarray, num_blocks: int, model_uid: str, attach: bool):
@@ -126,11 +128,10 @@ class KVCacheMetadata:
       self._h = None
 
   def __del__(self):
-    if self._owner is not None:  # a view over caller memory owns only its handle
-      try:
-        self._close()
-      except Exception:
-        pass
+    try:
+      self._close()
+    except Exception:
+      pass
 
 
 class KVCacheMetadataShmRegion:
@@ -169,14 +170,10 @@ class KVCacheMetadataShmRegion:
     self._warm = False
 
   def close(self, unlink: bool = False) -> None:
-    """Unmap the segment; it stays in /dev/shm unless ``unlink``."""
+    """Unmap the segment now (no store may still use the table); it stays
+    in /dev/shm unless ``unlink``.  Without an explicit close the mapping
+    lives as long as the table object does."""
     self._meta._close(unlink)
-
-  def __del__(self):
-    try:
-      self.close()
-    except Exception:
-      pass
 
 
 def metadata_shm_key(environ=None) -> str:
