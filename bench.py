@@ -46,6 +46,10 @@ PCIE_SPEC_GBS = 64.0
 # DRAM bytes per 2 MiB block moved by the insert kernel, from
 # profiles/insert_kernel_c1_256blocks.md (mean of the two captured launches).
 INSERT_TRAFFIC_PER_BLOCK = 1019588608 / 256
+# DRAM bytes per 2 MiB block of the insert kernel pulling from the mapped host
+# tier (reload direct), from profiles/insert_direct_kernel_c1_256blocks.md
+# (HBM writes; its host reads cross PCIe, not DRAM).
+INSERT_DIRECT_TRAFFIC_PER_BLOCK = 477387264 / 256
 
 
 def parse():
@@ -61,14 +65,18 @@ def parse():
   p.add_argument("--no-cpu-baseline", action="store_true")
   p.add_argument("--no-exchange", action="store_true",
                  help="skip the N>=2 weight-sync and hand-off measurements")
-  p.add_argument("--mode", default="staged",
+  p.add_argument("--mode", default="direct_h2d",
                  choices=["staged", "direct_d2h", "direct_h2d", "direct"],
                  help="C1 manager transfer mode (staged: copy-engine DMAs through HBM "
-                      "staging; direct*: SM-driven PCIe to the mapped host tier)")
+                      "staging; direct*: SM-driven PCIe to the mapped host tier).  "
+                      "direct_h2d (reloads pulled by the insert kernel, offloads by copy "
+                      "engine) measured fastest with both directions in flight")
   p.add_argument("--copy-streams", type=int, default=2)
   p.add_argument("--chunk-blocks", type=int, default=0, help="0 = manager default")
+  p.add_argument("--max-ctas", type=int, default=0, help="kernel grid cap, 0 = default")
   p.add_argument("--kernel-case", default="",
-                 choices=["", "extract", "insert", "extract_fp8", "insert_fp8", "pool_reshard"],
+                 choices=["", "extract", "insert", "extract_fp8", "insert_fp8", "pool_reshard",
+                          "insert_direct"],
                  help="run a few launches of one kernel on a small case (for ncu)")
   return p.parse_args()
 
@@ -723,7 +731,7 @@ def run_ours(args):
   host_blocks = max(4 * B, min(want_host, fit))
   mgr = KVCacheManager([[t] for t in storages], host_blocks_to_allocate=host_blocks,
                        mode=args.mode, copy_streams=args.copy_streams,
-                       chunk_blocks=args.chunk_blocks)
+                       chunk_blocks=args.chunk_blocks, max_ctas=args.max_ctas)
 
   pcie = measure_pcie(torch, device)
 
@@ -823,13 +831,22 @@ def run_ours(args):
   if not hbm_peak:
     hbm_peak, peak_src = 6650.0, "fallback"
   kern = {}
+  direct = {"extract": args.mode in ("direct_d2h", "direct"),
+            "insert": args.mode in ("direct_h2d", "direct")}
   for name, st in (("extract", ext), ("insert", ins)):
     kern[name] = {
         "kernel": f"block_copy_vec_kernel<{'true' if name == 'extract' else 'false'}> ({name})",
+        "path": (("HBM pool -> mapped host tier over PCIe" if name == "extract" else
+                  "mapped host tier over PCIe -> HBM pool") if direct[name] else
+                 ("HBM pool -> HBM staging" if name == "extract" else
+                  "HBM staging -> HBM pool")),
         "launches": st["launches"], "total_ms": round(st["ms"], 3),
         "bytes_per_launch": int(st["bytes"] / max(st["launches"], 1)),
         "avg_launch_us": round(st["ms"] * 1e3 / max(st["launches"], 1), 2),
         "achieved_gbs": round(st["bytes"] / (st["ms"] * 1e-3) / 1e9, 1) if st["ms"] > 0 else 0.0}
+    if direct[name] and st["ms"] > 0:
+      # half of the kernel's bytes (the host side) cross the link
+      kern[name]["pcie_gbs"] = round(st["bytes"] / 2 / (st["ms"] * 1e-3) / 1e9, 2)
   tot_ms = sum(k["total_ms"] for k in kern.values()) or 1.0
   for k in kern.values():
     k["share"] = round(k["total_ms"] / tot_ms, 3)
@@ -837,9 +854,42 @@ def run_ours(args):
   # DRAM traffic per block from ncu captures of the same kernels on the
   # small kernel case (profiles/*_kernel_c1_256blocks.md), scaled to this
   # run's launches by the blocks they move.
-  traffic_per_block = {"extract": 1018413568 / 256, "insert": INSERT_TRAFFIC_PER_BLOCK}
+  traffic_per_block = {"extract": 1018413568 / 256,
+                       "insert": (INSERT_DIRECT_TRAFFIC_PER_BLOCK if direct["insert"]
+                                  else INSERT_TRAFFIC_PER_BLOCK)}
+  if direct["extract"]:
+    traffic_per_block["extract"] = None
   blocks_per_launch = kern[dom]["bytes_per_launch"] / (2 * pitch)
   tpb = traffic_per_block.get(dom)
+  if direct[dom]:
+    # a kernel that pulls (pushes) the host tier over PCIe is bound by the
+    # link, not by HBM: its roofline is the pinned-memcpy peak of that
+    # direction measured in this run
+    pdir = "h2d" if dom == "insert" else "d2h"
+    roof = {"bound": "pcie", "kernel": kern[dom]["kernel"],
+            "achieved": kern[dom]["pcie_gbs"], "peak": pcie.get(pdir), "unit": "GB/s",
+            "frac": round(kern[dom]["pcie_gbs"] / pcie[pdir], 3) if pcie.get(pdir) else None,
+            "peak_source": f"measured in this run: pinned 1 GiB cudaMemcpyAsync {pdir.upper()}",
+            "achieved_def": "host-tier bytes the kernel moved over PCIe per launch / its "
+                            "CUDA-event duration (the HBM side moves the same bytes)"}
+  else:
+    roof = {"bound": "hbm", "kernel": kern[dom]["kernel"],
+            "achieved": kern[dom]["achieved_gbs"], "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(kern[dom]["achieved_gbs"] / hbm_peak, 3), "peak_source": peak_src}
+  roof.update({
+      "traffic": int(tpb * blocks_per_launch) if tpb else None,
+      "traffic_source": "ncu DRAM read+write bytes of the small kernel case, scaled per block"
+      if tpb else None,
+      "note": ("live: launched in 64-block chunks concurrently with the other direction's "
+               "kernel and the DMAs"),
+      "kernels": kern})
+  hbm_side = [n for n in kern if not direct[n] and kern[n]["launches"]]
+  if direct[dom] and hbm_side:
+    n = max(hbm_side, key=lambda k: kern[k]["total_ms"])
+    roof["hbm_kernel"] = {"kernel": kern[n]["kernel"], "bound": "hbm",
+                          "achieved": kern[n]["achieved_gbs"], "peak": hbm_peak,
+                          "frac": round(kern[n]["achieved_gbs"] / hbm_peak, 3),
+                          "peak_source": peak_src}
   # ---- CPU baseline (rank 0, N=1) ----
   cpu = None
   if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -880,16 +930,7 @@ def run_ours(args):
                  "reload_frac_of_measured_h2d": round(h2d_gbs / pcie["h2d"], 3)
                  if pcie.get("h2d") else None,
                  "frac_of_spec_busier_dir": round(max(d2h_gbs, h2d_gbs) / PCIE_SPEC_GBS, 3)},
-        "roofline": {"bound": "hbm", "kernel": kern[dom]["kernel"],
-                     "achieved": kern[dom]["achieved_gbs"], "peak": hbm_peak, "unit": "GB/s",
-                     "frac": round(kern[dom]["achieved_gbs"] / hbm_peak, 3),
-                     "peak_source": peak_src,
-                     "traffic": int(tpb * blocks_per_launch) if tpb else None,
-                     "traffic_source": "ncu capture of the small kernel case, scaled per block"
-                     if tpb else None,
-                     "note": ("live: launched in 64-block chunks concurrently with the other "
-                              "direction's kernel and the DMAs"),
-                     "kernels": kern},
+        "roofline": roof,
         "extract_hbm_gbs_one_launch": round(extract_one_launch_gbs, 1),
         "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
                 "h2d_bytes_per_step": int(timed_h2d / args.steps),
@@ -968,6 +1009,26 @@ def run_kernel_case(args):
     print(json.dumps({"kernel_case": "pool_reshard", "tasks": prog.n_tasks, "bytes": prog.bytes,
                       "ms": [round(x, 3) for x in ms],
                       "hbm_gbs": round(2 * prog.bytes / (min(ms) * 1e-3) / 1e9, 1)}))
+    return
+  if args.kernel_case == "insert_direct":
+    # The insert kernel pulling 256 blocks (512 MiB) per launch from the
+    # manager's mapped host tier into a 1024-block C1 pool (2 GiB), 4 launches.
+    from tpu_sync_b200 import KVCacheManager
+    g = workloads.C1
+    full = torch.empty((g.layers, g.kv, 1024, g.block_tokens, g.heads, g.head_dim),
+                       dtype=torch.bfloat16, device=device)
+    full.normal_(generator=torch.Generator(device=device).manual_seed(1))
+    storages = [full[l, k] for l in range(g.layers) for k in range(g.kv)]
+    mgr = KVCacheManager([[t] for t in storages], host_blocks_to_allocate=256,
+                         mode="direct_h2d", chunk_blocks=256)
+    rng = np.random.default_rng(5)
+    mgr.d2h(list(range(256)), rng.permutation(256).tolist()).Await()
+    for i in range(4):
+      mgr.h2d(rng.permutation(256).tolist(), rng.choice(1024, 256, replace=False).tolist()).Await()
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel_case": args.kernel_case, "blocks_per_launch": 256,
+                      "bytes_per_block": g.block_bytes}))
+    mgr.close()
     return
   g = workloads.C1 if not args.kernel_case.endswith("fp8") else workloads.C2
   blocks = 1024 if g is workloads.C1 else 2048
