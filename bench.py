@@ -338,8 +338,8 @@ def cpu_c4_reshard(plan, specs, seconds: float):
   from oracle import cpu_ref
   from tpu_sync_b200 import reshard_plan as rp
   chosen = [i for i, v in enumerate(specs) if v.name.startswith("layers.0.")]
-  src_sizes = {v: math.prod(rp.local_shape(rp.shard_boxes(specs[v].shape, specs[v].src_mesh)[0]))
-               for v in chosen}
+  src_sizes = {v: math.prod(rp.local_shape(
+      rp.shard_boxes(specs[v].shape, specs[v].src_mesh)[specs[v].src_box_of(0)])) for v in chosen}
   src_off, tot = {}, 0
   for v in chosen:
     src_off[v], tot = tot, tot + src_sizes[v]
@@ -347,7 +347,8 @@ def cpu_c4_reshard(plan, specs, seconds: float):
   for (vi, d), cs in plan.for_source(0).items():
     if vi not in src_off:
       continue
-    n_dst = math.prod(rp.local_shape(rp.shard_boxes(specs[vi].shape, specs[vi].dst_mesh)[d]))
+    n_dst = math.prod(rp.local_shape(
+        rp.shard_boxes(specs[vi].shape, specs[vi].dst_mesh)[specs[vi].dst_box_of(d)]))
     if (vi, d) not in dst_off:
       dst_off[(vi, d)], dtot = dtot, dtot + n_dst
     for (so, do, size, ss, ds, cnt) in cs:
@@ -441,14 +442,13 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
   is_src = rank < half
   idx = rank if is_src else rank - half
   params = workloads.llama3_8b_params()
-  specs = [rp.VariableSpec(n, s, workloads.mesh_for(s, "fsdp", half),
-                           workloads.mesh_for(s, split, half), layer_idx=i)
-           for i, (n, s, split) in enumerate(params)]
+  specs = workloads.weight_sync_specs(half, half, params)
   plan = rp.build_plan(specs)
-  src_sizes = [[math.prod(rp.local_shape(b)) for b in rp.shard_boxes(v.shape, v.src_mesh)]
-               for v in specs]
-  dst_sizes = [[math.prod(rp.local_shape(b)) for b in rp.shard_boxes(v.shape, v.dst_mesh)]
-               for v in specs]
+  # elements each slot (rank) holds of every variable
+  src_sizes = [[math.prod(rp.local_shape(rp.shard_boxes(v.shape, v.src_mesh)[v.src_box_of(r)]))
+                for r in range(half)] for v in specs]
+  dst_sizes = [[math.prod(rp.local_shape(rp.shard_boxes(v.shape, v.dst_mesh)[v.dst_box_of(r)]))
+                for r in range(half)] for v in specs]
   src_off, src_total = _cumsum([src_sizes[v][idx] for v in range(len(specs))]) if is_src else ([], 0)
   dst_offs = [_cumsum([dst_sizes[v][d] for v in range(len(specs))]) for d in range(half)]
   if is_src:
@@ -962,9 +962,7 @@ def run_ours(args):
       # ranks wait at the closing barrier)
       from tpu_sync_b200 import reshard_plan as rp
       half = world // 2
-      specs = [rp.VariableSpec(n, sh, workloads.mesh_for(sh, "fsdp", half),
-                               workloads.mesh_for(sh, split, half), layer_idx=i)
-               for i, (n, sh, split) in enumerate(workloads.llama3_8b_params())]
+      specs = workloads.weight_sync_specs(half, half)
       exchange["weight_sync"]["cpu_baseline"] = cpu_c4_reshard(rp.build_plan(specs), specs, 5.0)
       exchange["handoff"]["cpu_baseline"] = cpu_c3_relayout(5.0)
   if rank == 0:

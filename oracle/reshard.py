@@ -162,3 +162,92 @@ def relayout(src_pages: np.ndarray, dst_pages: np.ndarray, src_geom: dict,
       do = (h * dt_ + t % dt_) if dst_geom["head_major"] else ((t % dt_) * H + h)
       cols = np.arange(hb)
       dv[dbk[:, None], do[:, None] * hb + cols] = sv[sb[:, None], so[:, None] * hb + cols]
+
+
+# ---------------------------------------------------------------------------
+# Units, replicas and de-duplication (weight sync)
+# ---------------------------------------------------------------------------
+
+def global_indices(replica_id, num_shards, logical_mesh, layout, num_hosts,
+                   sharding_spec=None, mesh_axes=None, physical_mesh=None):
+  """_get_global_indices (tpu_sync/rpc/raiden_controller.py:129-263):
+  [(local shard, global slice index)] of one unit."""
+  if num_shards == 0:
+    return []
+  if not logical_mesh:
+    return [(i, i) for i in range(num_shards)]
+  if all(d == 1 for d in logical_mesh):
+    return [(i, 0) for i in range(num_shards)]
+  m2m = list(layout)[::-1]
+  phys = [logical_mesh[d] for d in m2m]
+  host = None
+  for d, size in enumerate(logical_mesh):
+    if size == num_hosts:
+      host = d
+      break
+
+  def ravel(coords, shape):
+    g, stride = 0, 1
+    for c, s in list(zip(coords[::-1], shape[::-1])):
+      g += c * stride
+      stride *= s
+    return g
+
+  res = []
+  if host is None and sharding_spec and mesh_axes and physical_mesh:
+    for j in range(num_shards):
+      rem = replica_id * num_shards + j
+      pc = []
+      for size in physical_mesh[::-1]:
+        pc.append(rem % size)
+        rem //= size
+      pc = pc[::-1]
+      tc = []
+      for name in sharding_spec:
+        if not name:
+          tc.append(0)
+          continue
+        if "," in name:
+          v = 0
+          for sub in [x.strip() for x in name.split(",") if x.strip()]:
+            if sub in mesh_axes:
+              i = list(mesh_axes).index(sub)
+              v = v * physical_mesh[i] + pc[i]
+          tc.append(v)
+          continue
+        tc.append(pc[list(mesh_axes).index(name)] if name in mesh_axes else 0)
+      res.append((j, ravel(tc, list(logical_mesh))))
+    return res
+  non_host = [d for d in range(len(logical_mesh)) if d != host]
+  for j in range(num_shards):
+    loc, t = {}, j
+    for d in non_host[::-1]:
+      loc[d] = t % logical_mesh[d]
+      t //= logical_mesh[d]
+    full = [replica_id if d == host else loc[d] for d in range(len(logical_mesh))]
+    res.append((j, ravel([full[m] for m in m2m], phys)))
+  return res
+
+
+def plan_with_replicas(shape, src_mesh, dst_mesh, src_holders, dst_holders, itemsize=1):
+  """Schedule emission with replicated holders (raiden_controller.py:2283-2321,
+  :2392-2476): for each destination slot and each source box intersecting
+  its box, the chunks come from holder (slot index mod holders) of that
+  source box, holders in slot order.  Returns {(src slot, dst slot): chunks}."""
+  s_sl = compute_nd_shard_slices(shape, src_mesh)
+  d_sl = compute_nd_shard_slices(shape, dst_mesh)
+  by_box = {}
+  for slot, b in enumerate(src_holders):
+    by_box.setdefault(b, []).append(slot)
+  out = {}
+  for src_slot, b_s in enumerate(src_holders):
+    for dst_slot, b_d in enumerate(dst_holders):
+      inter = intersect_nd_slices(s_sl[b_s], d_sl[b_d])
+      if inter is None:
+        continue
+      cands = by_box[b_s]
+      if len(cands) > 1 and cands[dst_slot % len(cands)] != src_slot:
+        continue
+      out[(src_slot, dst_slot)] = generate_strided_copy_chunks(s_sl[b_s], d_sl[b_d], inter,
+                                                               itemsize)
+  return out

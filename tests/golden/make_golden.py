@@ -105,8 +105,56 @@ def main():
       cases.append({"param": "extra", "shape": list(shape), "src_mesh": list(sm),
                     "dst_mesh": list(dm), "itemsize": itemsize,
                     "pairs": plan(shape, sm, dm, itemsize)})
+  # unit -> slice index mapping (_get_global_indices), both branches:
+  # named-axis sharding specs over a unit mesh, and the legacy host-axis rule
+  import random
+  rng = random.Random(44)
+  index_cases = []
+  unit_meshes = [([2, 2], ["fsdp", "tp"]), ([1, 4], ["fsdp", "tp"]), ([4, 1], ["fsdp", "tp"]),
+                 ([2, 4], ["data", "model"]), ([8], ["x"]), ([2, 2, 2], ["a", "b", "c"])]
+  for _ in range(300):
+    umesh, axes = rng.choice(unit_meshes)
+    n_units = rng.choice([1, 2, 4, 8])
+    local = rng.choice([1, 1, 2])
+    rank = rng.randint(1, 3)
+    spec, vmesh = [], []
+    for _d in range(rank):
+      k = rng.random()
+      if k < 0.3:
+        spec.append("")
+        vmesh.append(1)
+      elif k < 0.8:
+        i = rng.randrange(len(axes))
+        spec.append(axes[i])
+        vmesh.append(umesh[i])
+      elif len(axes) > 1:
+        i, j = sorted(rng.sample(range(len(axes)), 2))
+        spec.append(f"{axes[i]},{axes[j]}")
+        vmesh.append(umesh[i] * umesh[j])
+      else:
+        spec.append("missing_axis")
+        vmesh.append(rng.choice([1, 2]))
+    if rng.random() < 0.2:
+      vmesh[rng.randrange(rank)] = n_units  # a dimension as large as the unit count
+    layout = list(range(rank - 1, -1, -1))
+    if rng.random() < 0.3:
+      rng.shuffle(layout)
+    with_spec = rng.random() < 0.85
+    for replica in range(n_units):
+      unit = rc.RaidenId("job", str(replica), "data")
+      got = rc._get_global_indices(unit, ["s"] * local, list(vmesh), list(layout), n_units,
+                                   sharding_spec=spec if with_spec else None,
+                                   mesh_axes=axes if with_spec else None,
+                                   physical_mesh_shape=umesh if with_spec else None)
+      index_cases.append({"replica": replica, "local": local, "var_mesh": vmesh,
+                          "layout": layout, "hosts": n_units,
+                          "spec": spec if with_spec else None,
+                          "axes": axes if with_spec else None,
+                          "unit_mesh": umesh if with_spec else None,
+                          "out": [list(x) for x in got]})
   OUT.write_text(json.dumps({"generator": "reference tpu_sync planner",
-                             "slices": slices, "plans": cases}, indent=None))
+                             "slices": slices, "plans": cases,
+                             "global_indices": index_cases}, indent=None))
   print(f"wrote {OUT} ({len(cases)} plans)")
 
 

@@ -156,6 +156,79 @@ def test_product_planner_matches_reference_goldens():
     assert pairs == case["pairs"], case["param"]
 
 
+def test_unit_shard_indices_match_reference_goldens():
+  """_get_global_indices (raiden_controller.py:129-263), both restatements,
+  against 1077 answers of the reference function itself."""
+  from tpu_sync_b200 import reshard_plan as rp
+  data = json.loads(GOLDEN.read_text())
+  assert len(data["global_indices"]) > 1000
+  for c in data["global_indices"]:
+    args = (c["replica"], c["local"], c["var_mesh"], c["layout"], c["hosts"], c["spec"],
+            c["axes"], c["unit_mesh"])
+    want = [tuple(x) for x in c["out"]]
+    assert ors.global_indices(*args) == want, c
+    assert rp.shard_index_of_units(*args) == want, c
+
+
+def test_replicated_source_dedup_matches_reference_test():
+  """raiden_controller_test.py:1868-1960: 4 trainer units on a (fsdp=1, tp=4)
+  mesh all hold layer_19.input_layernorm (2304,); 4 sampler units on a
+  (fsdp=2, tp=2) mesh hold halves.  Every destination expects exactly one
+  chunk for the layer and every destination peer gets exactly one push."""
+  from tpu_sync_b200 import reshard_plan as rp
+  sh = rp.slot_holders(4, [1], ["fsdp"], ["fsdp", "tp"], [1, 4])
+  dh = rp.slot_holders(4, [2], ["fsdp"], ["fsdp", "tp"], [2, 2])
+  assert sh == [0, 0, 0, 0] and dh == [0, 0, 1, 1]
+  v = rp.VariableSpec("layer_19.input_layernorm", (2304,), (1,), (2,), 198, sh, dh)
+  plan = rp.build_plan([v])
+  per_dst = {}
+  for (vi, s, d), cs in plan.chunks.items():
+    per_dst[d] = per_dst.get(d, 0) + len(cs)
+  assert per_dst == {0: 1, 1: 1, 2: 1, 3: 1}
+  # holder d mod 4: each source pushes to one destination
+  assert sorted((s, d) for (_, s, d) in plan.chunks) == [(0, 0), (1, 1), (2, 2), (3, 3)]
+  raw = rp.build_plan([v], normalize_runs=False)
+  want = ors.plan_with_replicas((2304,), (1,), (2,), sh, dh)
+  assert {(s, d): cs for (_, s, d), cs in raw.chunks.items()} == want
+
+
+def test_replicated_plans_product_matches_oracle():
+  from tpu_sync_b200 import reshard_plan as rp
+  rng = np.random.default_rng(21)
+  for _ in range(200):
+    rank = int(rng.integers(1, 4))
+    shape = tuple(int(x) for x in rng.integers(3, 40, rank))
+    sm = tuple(int(x) for x in rng.integers(1, 4, rank))
+    dm = tuple(int(x) for x in rng.integers(1, 4, rank))
+    ns, nd = int(np.prod(sm)), int(np.prod(dm))
+    # every box held at least once, some several times, slots shuffled
+    sh = list(range(ns)) + [int(x) for x in rng.integers(0, ns, int(rng.integers(0, 4)))]
+    dh = list(range(nd)) + [int(x) for x in rng.integers(0, nd, int(rng.integers(0, 4)))]
+    rng.shuffle(sh)
+    rng.shuffle(dh)
+    v = rp.VariableSpec("x", shape, sm, dm, 0, sh, dh)
+    got = {(s, d): cs for (_, s, d), cs in rp.build_plan([v], normalize_runs=False).chunks.items()}
+    assert got == ors.plan_with_replicas(shape, sm, dm, sh, dh)
+    # every destination slot's box is covered exactly once
+    dboxes = rp.shard_boxes(shape, dm)
+    for d, b in enumerate(dh):
+      hits = np.zeros(int(np.prod(rp.local_shape(dboxes[b]))), np.int64)
+      for (s, dd), cs in got.items():
+        if dd == d:
+          for (so, do, size, ss, ds, cnt) in cs:
+            for c in range(cnt):
+              hits[do + c * ds: do + c * ds + size] += 1
+      assert (hits == 1).all()
+
+
+def test_plan_rejects_unheld_source_box():
+  from tpu_sync_b200 import reshard_plan as rp
+  with pytest.raises(ValueError, match="no source slot holds box 1"):
+    rp.build_plan([rp.VariableSpec("x", (8,), (2,), (1,), 0, [0, 0], None)])
+  with pytest.raises(ValueError, match="dst slot holds box 3 of 2"):
+    rp.build_plan([rp.VariableSpec("x", (8,), (2,), (2,), 0, None, [0, 3])])
+
+
 def test_planner_covers_every_destination_element_once():
   from tpu_sync_b200 import reshard_plan as rp, workloads
   for name, shape, split in workloads.llama3_8b_params()[:12]:

@@ -29,37 +29,70 @@ def small_llama(hidden=256, ffn=640, vocab=1000, layers=2, kv=64):
   return out
 
 
-def run_reshard(cuda, n_src, n_dst, params, src_dtype=torch.float32, dst_dtype=torch.bfloat16):
-  g = torch.Generator().manual_seed(3)
-  specs, globals_ = [], []
-  for li, (name, shape, split) in enumerate(params):
-    specs.append(rp.VariableSpec(name, shape, workloads.mesh_for(shape, "fsdp", n_src),
-                                 workloads.mesh_for(shape, split, n_dst), layer_idx=li))
-    globals_.append((torch.randn(shape, generator=g) * 0.02).to(src_dtype))
+def execute_specs(cuda, specs, n_src_slots, n_dst_slots, src_dtype=torch.float32,
+                  dst_dtype=torch.bfloat16, seed=3):
+  """Runs the plan of `specs` on cuda:0 (source slot s = local shard s of one
+  synchronizer, destination slot d = its own tensors) and checks that every
+  destination slot holds exactly its box of every variable."""
+  g = torch.Generator().manual_seed(seed)
+  globals_ = [(torch.randn(v.shape, generator=g) * 0.02).to(src_dtype) for v in specs]
   plan = rp.build_plan(specs)
-  # trainer: one synchronizer with n_src shards per layer (all on cuda:0)
   grid = []
   for v, full in zip(specs, globals_):
     boxes = rp.shard_boxes(v.shape, v.src_mesh)
-    grid.append([full[tuple(slice(a, b) for a, b in box)].contiguous().to(cuda)
-                 for box in boxes])
+    grid.append([full[tuple(slice(a, b) for a, b in boxes[v.src_box_of(s)])].contiguous().to(cuda)
+                 for s in range(n_src_slots)])
   ws = WeightSynchronizer(grid)
   dest = {}
   for vi, v in enumerate(specs):
-    for d, box in enumerate(rp.shard_boxes(v.shape, v.dst_mesh)):
-      dest[(vi, d)] = torch.zeros(rp.local_shape(box), dtype=dst_dtype, device=cuda)
-  fut = ws.push_weights_resharded(plan, {s: s for s in range(n_src)}, dest)
+    boxes = rp.shard_boxes(v.shape, v.dst_mesh)
+    for d in range(n_dst_slots):
+      dest[(vi, d)] = torch.zeros(rp.local_shape(boxes[v.dst_box_of(d)]), dtype=dst_dtype,
+                                  device=cuda)
+  fut = ws.push_weights_resharded(plan, {s: s for s in range(n_src_slots)}, dest)
   fut.Await()
   torch.cuda.synchronize()
   for vi, v in enumerate(specs):
     want_full = globals_[vi].to(dst_dtype)
-    for d, box in enumerate(rp.shard_boxes(v.shape, v.dst_mesh)):
-      want = want_full[tuple(slice(a, b) for a, b in box)]
+    boxes = rp.shard_boxes(v.shape, v.dst_mesh)
+    for d in range(n_dst_slots):
+      want = want_full[tuple(slice(a, b) for a, b in boxes[v.dst_box_of(d)])]
       got = dest[(vi, d)].cpu()
       assert torch.equal(got.view(torch.int16) if dst_dtype == torch.bfloat16 else got,
                          want.view(torch.int16) if dst_dtype == torch.bfloat16 else want), \
           (v.name, d)
   return plan
+
+
+def run_reshard(cuda, n_src, n_dst, params, src_dtype=torch.float32, dst_dtype=torch.bfloat16):
+  specs = workloads.weight_sync_specs(n_src, n_dst, params)
+  return execute_specs(cuda, specs, n_src, n_dst, src_dtype, dst_dtype)
+
+
+def test_replicated_sources_and_destinations(cuda):
+  """Units on named meshes (the reference's sharding specs): trainer units
+  on (fsdp=2, tp=2) hold dim-0 halves replicated over tp; sampler units on
+  (fsdp=1, tp=4) hold tp quarters of dim 1, or the whole tensor for a
+  replicated norm.  Each destination slot gets its box from one holder
+  (slot mod holders), the result is exact on every slot."""
+  specs = []
+  for i, (name, shape, dst_spec, dst_mesh) in enumerate([
+      ("o_proj", (64, 96), ["", "tp"], [1, 4]),
+      ("norm", (96,), [""], [1]),
+      ("emb", (40, 24), ["tp", ""], [4, 1])]):
+    src_spec, src_mesh = (["fsdp", ""], [2, 1]) if len(shape) == 2 else (["fsdp"], [2])
+    sh = rp.slot_holders(4, src_mesh, src_spec, ["fsdp", "tp"], [2, 2])
+    dh = rp.slot_holders(4, dst_mesh, dst_spec, ["fsdp", "tp"], [1, 4])
+    specs.append(rp.VariableSpec(name, shape, tuple(src_mesh), tuple(dst_mesh), i, sh, dh))
+  assert specs[0].src_holders == [0, 0, 1, 1] and specs[1].dst_holders == [0, 0, 0, 0]
+  plan = execute_specs(cuda, specs, 4, 4)
+  # de-duplicated: a destination slot takes each source box from one holder
+  for vi in range(len(specs)):
+    pairs = [(s, d) for (v, s, d) in plan.chunks if v == vi]
+    for d in range(4):
+      srcs = [s for s, dd in pairs if dd == d]
+      boxes = [specs[vi].src_box_of(s) for s in srcs]
+      assert len(boxes) == len(set(boxes)), (vi, d, srcs)
 
 
 @pytest.mark.parametrize("n_src,n_dst", [(4, 4), (1, 1), (1, 2), (2, 4)])

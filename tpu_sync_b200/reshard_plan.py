@@ -17,6 +17,17 @@ cannot express.  `plan_bytes` gives the reference's byte form for a single
 dtype.  The TPU (8, 128) tile-aware variant (raiden_controller.py:1016-1184)
 is not needed: CUDA tensors are linear row-major.
 
+Units and replicas: a plan is keyed by SLOTS, a slot being one shard of one
+unit (a process or rank), flattened unit-major.  A slot holds one box of the
+variable; by default slot i holds box i, and `shard_index_of_units` restates
+the reference's mapping (_get_global_indices, raiden_controller.py:129-263)
+for units on a named device mesh with a per-dimension sharding spec, where
+several slots can hold the same box (replication).  Every destination slot
+receives its box; when several source slots hold a box, destination slot d
+takes it from holder d mod (number of holders), holders in slot order — the
+reference's de-duplication and load balancing (raiden_controller.py:2283-2321,
+:2460-2476).
+
 Execution: chunks of one source rank, for every destination rank, become one
 ts_reshard_copy launch (tpu_sync_b200.ops.ReshardProgram) that reads the
 local shard and stores into the destination tensors, local or on a peer GPU.
@@ -113,43 +124,159 @@ def normalize(chunks: Sequence[Chunk]) -> List[Chunk]:
   return out
 
 
+def shard_index_of_units(replica_id: int, num_local_shards: int, var_mesh: Sequence[int],
+                         layout: Sequence[int], num_physical_hosts: int,
+                         sharding_spec: Optional[Sequence[str]] = None,
+                         mesh_axes: Optional[Sequence[str]] = None,
+                         physical_mesh: Optional[Sequence[int]] = None) -> List[Tuple[int, int]]:
+  """(local shard, index of the variable's shard box it holds) for the
+  `num_local_shards` shards of unit `replica_id`.
+
+  Restates _get_global_indices (raiden_controller.py:129-263).  `layout` is
+  the variable's minor-to-major dimension order.  With a sharding spec (one
+  mesh-axis name per tensor dimension: "" = not split, "a,b" = split over the
+  product of axes a and b), the unit mesh's axis names and shape, and no
+  variable mesh dimension equal to the number of units, a shard's mesh
+  coordinates come from its global device id (replica_id * local shards +
+  local) in row-major order over the unit mesh; otherwise the legacy rule
+  puts the unit on the variable mesh dimension whose size equals the number
+  of units and its local shards, row-major, on the others.
+  """
+  n = int(num_local_shards)
+  if n == 0:
+    return []
+  var_mesh = list(var_mesh)
+  if not var_mesh:
+    return [(j, j) for j in range(n)]
+  if all(m == 1 for m in var_mesh):
+    return [(j, 0) for j in range(n)]
+  order = list(reversed(list(layout)))            # major to minor
+  phys = [var_mesh[d] for d in order]
+  host_dim = next((d for d, m in enumerate(var_mesh) if m == num_physical_hosts), None)
+
+  def flat(coords, dims):
+    idx, stride = 0, 1
+    for c, m in zip(reversed(coords), reversed(dims)):
+      idx += c * stride
+      stride *= m
+    return idx
+
+  if host_dim is None and sharding_spec and mesh_axes and physical_mesh:
+    axes, pmesh = list(mesh_axes), list(physical_mesh)
+    out = []
+    for j in range(n):
+      dev = replica_id * n + j
+      coords = [0] * len(pmesh)
+      for a in range(len(pmesh) - 1, -1, -1):
+        coords[a] = dev % pmesh[a]
+        dev //= pmesh[a]
+      tcoords = []
+      for spec in sharding_spec:
+        if not spec:
+          tcoords.append(0)
+        elif "," in spec:
+          c = 0
+          for sub in (x.strip() for x in spec.split(",")):
+            if sub and sub in axes:
+              k = axes.index(sub)
+              c = c * pmesh[k] + coords[k]
+          tcoords.append(c)
+        else:
+          tcoords.append(coords[axes.index(spec)] if spec in axes else 0)
+      out.append((j, flat(tcoords, var_mesh)))
+    return out
+  others = [d for d in range(len(var_mesh)) if d != host_dim]
+  out = []
+  for j in range(n):
+    full = [0] * len(var_mesh)
+    rest = j
+    for d in reversed(others):
+      full[d] = rest % var_mesh[d]
+      rest //= var_mesh[d]
+    if host_dim is not None:
+      full[host_dim] = replica_id
+    out.append((j, flat([full[d] for d in order], phys)))
+  return out
+
+
+def slot_holders(n_units: int, var_mesh: Sequence[int], sharding_spec: Sequence[str],
+                 mesh_axes: Sequence[str], unit_mesh: Sequence[int],
+                 shards_per_unit: int = 1) -> List[int]:
+  """Box index held by every slot (unit-major) of `n_units` units on a
+  row-major variable layout."""
+  layout = list(range(len(var_mesh) - 1, -1, -1))
+  out = []
+  for u in range(n_units):
+    out += [g for _, g in shard_index_of_units(u, shards_per_unit, var_mesh, layout, n_units,
+                                                sharding_spec, mesh_axes, unit_mesh)]
+  return out
+
+
 @dataclass
 class VariableSpec:
-  """One tensor to move: global shape, source mesh and destination mesh."""
+  """One tensor to move: global shape, source mesh and destination mesh.
+
+  src_holders / dst_holders: the box index each slot holds (None: slot i
+  holds box i, one slot per box).
+  """
   name: str
   shape: Tuple[int, ...]
   src_mesh: Tuple[int, ...]
   dst_mesh: Tuple[int, ...]
   layer_idx: int = 0
+  src_holders: Optional[List[int]] = None
+  dst_holders: Optional[List[int]] = None
+
+  def src_box_of(self, slot: int) -> int:
+    return slot if self.src_holders is None else self.src_holders[slot]
+
+  def dst_box_of(self, slot: int) -> int:
+    return slot if self.dst_holders is None else self.dst_holders[slot]
 
 
 @dataclass
 class ReshardPlan:
-  """Element-unit chunks per (variable, src shard, dst shard)."""
+  """Element-unit chunks per (variable, src slot, dst slot)."""
   variables: List[VariableSpec]
-  # (var index, src shard, dst shard) -> chunks
+  # (var index, src slot, dst slot) -> chunks
   chunks: Dict[Tuple[int, int, int], List[Chunk]] = field(default_factory=dict)
 
   def for_source(self, src_shard: int) -> Dict[Tuple[int, int], List[Chunk]]:
-    """(var index, dst shard) -> chunks of one source shard."""
+    """(var index, dst slot) -> chunks of one source slot."""
     return {(v, d): c for (v, s, d), c in self.chunks.items() if s == src_shard}
 
   def elements_to(self, dst_shard: int) -> int:
-    """Elements every source together writes into one destination shard."""
+    """Elements every source together writes into one destination slot."""
     return sum(size * max(cnt, 1) for (v, s, d), cs in self.chunks.items() if d == dst_shard
                for (_, _, size, _, _, cnt) in cs)
 
 
 def build_plan(variables: Sequence[VariableSpec], normalize_runs: bool = True) -> ReshardPlan:
+  """Chunks for every (destination slot, intersecting source box), taken
+  from one holder of that box (see the module docstring)."""
   plan = ReshardPlan(list(variables))
   for vi, v in enumerate(plan.variables):
     sboxes = shard_boxes(v.shape, v.src_mesh)
     dboxes = shard_boxes(v.shape, v.dst_mesh)
-    for si, sb in enumerate(sboxes):
-      for di, db in enumerate(dboxes):
+    src_holders = v.src_holders if v.src_holders is not None else list(range(len(sboxes)))
+    dst_holders = v.dst_holders if v.dst_holders is not None else list(range(len(dboxes)))
+    for name, hs, boxes in (("src", src_holders, sboxes), ("dst", dst_holders, dboxes)):
+      bad = [b for b in hs if not 0 <= b < len(boxes)]
+      if bad:
+        raise ValueError(f"{v.name}: {name} slot holds box {bad[0]} of {len(boxes)}")
+    holders: Dict[int, List[int]] = {}
+    for slot, b in enumerate(src_holders):
+      holders.setdefault(b, []).append(slot)
+    for di, b_d in enumerate(dst_holders):
+      db = dboxes[b_d]
+      for b_s, sb in enumerate(sboxes):
         inter = box_intersection(sb, db)
         if inter is None:
           continue
+        cands = holders.get(b_s)
+        if not cands:
+          raise ValueError(f"{v.name}: no source slot holds box {b_s}")
+        si = cands[di % len(cands)]
         cs = strided_chunks(sb, db, inter, 1)
         plan.chunks[(vi, si, di)] = normalize(cs) if normalize_runs else cs
   return plan

@@ -136,6 +136,21 @@ def mesh_for(shape, split: str, n: int) -> Tuple[int, ...]:
   return (1,) * len(shape)
 
 
+def weight_sync_specs(n_src: int, n_dst: int, params=None):
+  """C4 reshard variables: fp32 FSDP dim-0 shards on n_src trainer ranks ->
+  bf16 tensor-parallel shards on n_dst sampler ranks.  A replicated
+  parameter (the norms) is held whole by every sampler rank, so each of them
+  receives it (every trainer rank sends its FSDP slice to each)."""
+  from tpu_sync_b200 import reshard_plan as rp
+  out = []
+  for i, (name, shape, split) in enumerate(params if params is not None else
+                                           llama3_8b_params()):
+    out.append(rp.VariableSpec(name, tuple(shape), mesh_for(shape, "fsdp", n_src),
+                               mesh_for(shape, split, n_dst), layer_idx=i,
+                               dst_holders=[0] * n_dst if split == "rep" else None))
+  return out
+
+
 # ---------------------------------------------------------------------------
 # C1 access trace driving the tier-2 store
 # ---------------------------------------------------------------------------
