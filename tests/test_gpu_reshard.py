@@ -162,3 +162,89 @@ def test_relayout_round_trip(cuda):
   torch.cuda.synchronize()
   used = st.reshape(-1)
   assert torch.equal(back[used], src[used])
+
+
+# ---------------------------------------------------------------------------
+# Controller-made byte schedules (WeightSynchronizerBase::PushWeightsResharded)
+# ---------------------------------------------------------------------------
+
+def _entry(**kw):
+  e = dict(dst_peer="sampler:0", dst_shard_idx=0, src_offset_bytes=0, dst_offset_bytes=0,
+           size_bytes=0, src_stride_bytes=0, dst_stride_bytes=0, count=1, layer_idx=0)
+  e.update(kw)
+  return e
+
+
+def _byte_ws(cuda, nbytes, layers=1, fill=0xAB):
+  src = [torch.full((nbytes,), fill, dtype=torch.uint8, device=cuda) for _ in range(layers)]
+  dst = [torch.zeros(nbytes, dtype=torch.uint8, device=cuda) for _ in range(layers)]
+  ws = WeightSynchronizer([[t] for t in src], layer_names=[f"l{i}" for i in range(layers)])
+  return ws, src, {("sampler:0", i, 0): dst[i] for i in range(layers)}, dst
+
+
+def test_entries_exact_boundary_and_zero_bytes(cuda):
+  """weight_synchronizer_test.cc:184-272: a whole-slice entry copies every
+  byte; a zero-byte entry copies none."""
+  ws, _, dests, dst = _byte_ws(cuda, 16384)
+  ws.push_weights_resharded_entries({0: [_entry(size_bytes=0)]}, dests).Await()
+  assert int(dst[0].count_nonzero()) == 0
+  ws.push_weights_resharded_entries({0: [_entry(size_bytes=16384)]}, dests).Await()
+  assert bool((dst[0] == 0xAB).all())
+
+
+def test_entries_errors_match_reference(cuda):
+  """:274-360: source range past the shard, layer index past the layers,
+  an empty schedule; and the layer-name fallback (:362-460)."""
+  ws, _, dests, dst = _byte_ws(cuda, 1024, layers=2)
+  with pytest.raises(ValueError, match="^Push range out of bounds$"):
+    ws.push_weights_resharded_entries({0: [_entry(src_offset_bytes=500, size_bytes=600)]},
+                                      dests)
+  with pytest.raises(ValueError, match="^Layer index out of bounds: 2$"):
+    ws.push_weights_resharded_entries({0: [_entry(size_bytes=16, layer_idx=2)]}, dests)
+  with pytest.raises(ValueError, match="^Push range out of bounds$"):  # a late repeat
+    ws.push_weights_resharded_entries({0: [_entry(size_bytes=100, src_stride_bytes=300,
+                                                  dst_stride_bytes=100, count=5)]}, dests)
+  with pytest.raises(ValueError, match="^Push destination range out of bounds$"):
+    ws.push_weights_resharded_entries({0: [_entry(dst_offset_bytes=1000, size_bytes=64)]},
+                                      dests)
+  ws.push_weights_resharded_entries({}, dests).Await()
+  ws.push_weights_resharded_entries({0: []}, dests).Await()
+  assert int(dst[0].count_nonzero()) == 0 and int(dst[1].count_nonzero()) == 0
+  no_layer = _entry(size_bytes=32)
+  del no_layer["layer_idx"]
+  with pytest.raises(LookupError, match="Layer name not found in WeightSynchronizer: x"):
+    ws.push_weights_resharded_entries({0: [no_layer]}, dests, src_data_name="x")
+  ws.push_weights_resharded_entries({0: [no_layer]}, dests, src_data_name="l1").Await()
+  assert int(dst[1][:32].ne(0xAB).sum()) == 0 and int(dst[1][32:].count_nonzero()) == 0
+
+
+def test_entries_strided_repeats_match_oracle(cuda):
+  """Random strided entries (counts, strides, odd offsets) against the
+  oracle's entry expansion (weight_synchronizer_base.cc:606-667)."""
+  rng = np.random.default_rng(17)
+  nbytes = 1 << 16
+  g = torch.Generator().manual_seed(4)
+  src_host = torch.randint(0, 256, (nbytes,), generator=g, dtype=torch.uint8)
+  src = src_host.to(cuda)
+  dst = torch.zeros(nbytes, dtype=torch.uint8, device=cuda)
+  ws = WeightSynchronizer([[src]])
+  want = np.zeros(nbytes, np.uint8)
+  entries, used = [], np.zeros(nbytes, bool)
+  while len(entries) < 40:
+    size = int(rng.integers(1, 300))
+    count = int(rng.integers(1, 6))
+    ss = size + int(rng.integers(0, 50)) if count > 1 else 0
+    ds = size + int(rng.integers(0, 50)) if count > 1 else 0
+    so = int(rng.integers(0, nbytes - (count * max(ss, size) + size)))
+    do = int(rng.integers(0, nbytes - (count * max(ds, size) + size)))
+    span = [(do + c * (ds if count > 1 else size), size) for c in range(count)]
+    if any(used[a:a + n].any() for a, n in span):
+      continue  # destinations of one push are disjoint
+    for a, n in span:
+      used[a:a + n] = True
+    entries.append(_entry(src_offset_bytes=so, dst_offset_bytes=do, size_bytes=size,
+                          src_stride_bytes=ss, dst_stride_bytes=ds, count=count))
+    ors.apply_byte_entries(src_host.numpy(), want,
+                           [(so, do, size, ss, ds, count)])
+  ws.push_weights_resharded_entries({0: entries}, {("sampler:0", 0, 0): dst}).Await()
+  np.testing.assert_array_equal(dst.cpu().numpy(), want)

@@ -205,6 +205,101 @@ class WeightSynchronizer:
     return PushFuture(last_event, programs)
 
 
+  # -- controller-made byte schedules ------------------------------------------
+  def push_weights_resharded_entries(
+      self, shard_push_schedules: Dict[int, Sequence[Dict[str, Any]]],
+      destinations: Dict[Tuple[str, int, int], Any], src_data_name: Optional[str] = None,
+      stream: Optional[torch.cuda.Stream] = None) -> PushFuture:
+    """PushWeightsResharded for a schedule made by the controller
+    (StartTransferRequest.shard_push_schedules; weight_synchronizer_base.cc:558-700).
+
+    shard_push_schedules: local shard index -> entries, each a dict with the
+      ShardPushEntryProto fields dst_peer, dst_shard_idx, src_offset_bytes,
+      dst_offset_bytes, size_bytes, src_stride_bytes, dst_stride_bytes,
+      count and, optionally, layer_idx (absent: the layer whose name is
+      `src_data_name`, the request's first source unit's data name).
+    destinations: (dst_peer, layer_idx, dst_shard_idx) -> the tensor (or
+      PeerBuffer) of that destination layer and shard; entry offsets are bytes
+      into it.  The bytes move unchanged (the reference's push), every entry
+      with `count` repeats as one strided task of one kernel per source GPU.
+
+    Checks, in the reference's order and words (ValueError): layer index in
+    range ("Layer index out of bounds: <i>"), source range inside the
+    shard's bytes per contiguous payload or per repeat ("Push range out of
+    bounds"); a missing layer name is "Layer name not found in
+    WeightSynchronizer: <name>".  The receiver's bound becomes a check here
+    too ("Push destination range out of bounds"), so no store can leave its
+    destination.  Zero-byte entries and empty schedules push nothing.
+    """
+    fallback: List[Optional[int]] = []
+
+    def fallback_layer() -> int:
+      if not fallback:
+        if src_data_name is None:
+          raise ValueError("src_units list cannot be empty")
+        if src_data_name not in self.layer_names:
+          raise LookupError(f"Layer name not found in WeightSynchronizer: {src_data_name}")
+        fallback.append(self.layer_names.index(src_data_name))
+      return fallback[0]
+
+    def nbytes(t) -> int:
+      if isinstance(t, torch.Tensor):
+        return t.numel() * t.element_size()
+      return int(t.nbytes)
+
+    per_shard: Dict[int, List[Tuple]] = {}
+    for i in range(self.num_shards):
+      entries = shard_push_schedules.get(i)
+      if not entries:
+        continue
+      for e in entries:
+        layer = e.get("layer_idx")
+        layer = fallback_layer() if layer is None else int(layer)
+        if layer < 0 or layer >= self.num_layers:
+          raise ValueError(f"Layer index out of bounds: {layer}")
+        src = self._grid[layer][i]
+        host_size = src.numel() * src.element_size()
+        count = max(int(e.get("count", 1)), 1)
+        size = int(e.get("size_bytes", 0))
+        so, do = int(e.get("src_offset_bytes", 0)), int(e.get("dst_offset_bytes", 0))
+        ss, ds = int(e.get("src_stride_bytes", 0)), int(e.get("dst_stride_bytes", 0))
+        contiguous = count == 1 or (ss == size and ds == size)
+        if contiguous:
+          if so + count * size > host_size:
+            raise ValueError("Push range out of bounds")
+        else:
+          for c in range(count):
+            if so + c * ss + size > host_size:
+              raise ValueError("Push range out of bounds")
+        if size == 0:
+          continue
+        key = (e["dst_peer"], layer, int(e.get("dst_shard_idx", 0)))
+        if key not in destinations:
+          raise ValueError(f"No destination for peer {key[0]} layer {key[1]} shard {key[2]}")
+        dst = destinations[key]
+        dst_end = do + count * size if contiguous else do + (count - 1) * ds + size
+        if do < 0 or dst_end > nbytes(dst):
+          raise ValueError("Push destination range out of bounds")
+        if isinstance(dst, torch.Tensor) and dst.device != src.device:
+          enable_peer_access(src.device.index, dst.device.index)
+        task = (so, do, count * size, 0, 0, 1) if contiguous else (so, do, size, ss, ds, count)
+        per_shard.setdefault(i, []).append((src.data_ptr(), dst.data_ptr()) + task)
+    programs = []
+    last_event = None
+    for i, chunks in per_shard.items():
+      device = self._grid[0][i].device
+      s = stream if stream is not None else torch.cuda.current_stream(device)
+      prog = ops.ReshardProgram(chunks, torch.uint8, torch.uint8, device)
+      prog.launch(s)
+      programs.append(prog)
+      last_event = torch.cuda.Event()
+      last_event.record(s)
+    if last_event is None:
+      last_event = torch.cuda.Event()
+      last_event.record()
+    return PushFuture(last_event, programs)
+
+
 class PeerBuffer:
   """Another process's device memory, mapped for kernels on `kernel_device`.
 
@@ -220,6 +315,13 @@ class PeerBuffer:
 
   def data_ptr(self) -> int:
     return self._ptr
+
+  @property
+  def nbytes(self) -> int:
+    n = 1
+    for d in self.shape:
+      n *= int(d)
+    return n * torch.empty((), dtype=self.dtype).element_size()
 
 
 # (kernel device, handle bytes) -> mapped base address; a handle may be opened
