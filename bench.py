@@ -222,6 +222,42 @@ def c1_plans(rank: int, host_blocks: int, pool_blocks: int, batch: int, n_steps:
   return plans, stats
 
 
+def c1_host_blocks(args, world: int) -> int:
+  """Host tier blocks of the C1 configuration: as many as requested (default
+  32768 = 64 GiB), bounded by this box's RAM share per local rank."""
+  from tpu_sync_b200 import workloads
+  want = args.host_blocks or 32768
+  local_ranks = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+  fit = int(0.45 * mem_available_bytes() / max(local_ranks, 1) // workloads.C1.block_bytes)
+  return max(4 * args.batch, min(want, fit))
+
+
+def c1_config(args, host_blocks: int, plans, trace_stats, world: int) -> dict:
+  """The `config` of both arms' JSON lines (same workload, same plans)."""
+  from tpu_sync_b200 import workloads
+  g = workloads.C1
+  pitch = g.block_bytes
+  pool_bytes = args.pool_blocks * pitch
+  return {
+      "workload": ("C1 Llama-3-8B KV tier: 32 layers x K/V, 16-token blocks of "
+                   "8 heads x 128 bf16 (2 MiB per block); per step the offloads "
+                   "(misses) and reloads (hits) of consecutive 512-access batches "
+                   "of the Zipf trace until 512 reloads are pending, both "
+                   "directions in flight"),
+      "blocks_per_step": round(sum(len(p[0]) + len(p[2]) for p in plans[args.warmup:])
+                               / args.steps, 1),
+      "pool_blocks": args.pool_blocks, "pool_gib": round(pool_bytes / GIB, 1),
+      "host_tier_blocks": host_blocks,
+      "host_tier_gib": round(host_blocks * pitch / GIB, 1),
+      "batch": args.batch,
+      "l2": "inputs larger than L2 (~1 GiB of scattered 2 MiB blocks per step)",
+      "trace": ("100k accesses Zipf(1.1) over 200k prefix ids (seed 10+rank), batches "
+                "of 512, through the tier-2 store (reference LRU + host block "
+                "allocator); steps from the middle of the trace"),
+      "trace_hit_rate": trace_stats["hit_rate"],
+      "parallelism": f"replicas x{world}"}
+
+
 def cpu_offload_reload(plans, seconds: float, steps: int = 0, warmup: int = 0):
   """Times the reference host loops (restated in C) on the C1 step plans.
 
@@ -368,15 +404,17 @@ def run_reference(args):
   rank = int(os.environ.get("RANK", "0"))
   if rank != 0:
     return
-  plans, _ = c1_plans(0, 32768, args.pool_blocks, args.batch, args.warmup + args.steps)
+  world = int(os.environ.get("WORLD_SIZE", "1"))
+  host_blocks = c1_host_blocks(args, world)
+  plans, stats = c1_plans(0, host_blocks, args.pool_blocks, args.batch,
+                          args.warmup + args.steps)
   r = cpu_offload_reload(plans, 0.0, steps=args.steps, warmup=args.warmup)
   line = {"impl": "reference", "metric": METRIC, "value": r["value"], "unit": "GB/s",
           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
           "ms_per_step": round(r["ms_per_step"], 3), "higher_is_better": True,
           "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
           "data": "synthetic (host-resident pool standing in for the CPU client's device)",
-          "config": {"workload": "C1 Llama-3-8B KV tier offload/reload (CPU restatement)",
-                     "batch": args.batch},
+          "config": c1_config(args, host_blocks, plans, stats, world),
           "cpu_baseline": {"value": r["value"], "unit": "GB/s", "cores": r["cores"],
                            "kind": "port", "sample": r["sample"]},
           "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
@@ -725,10 +763,7 @@ def run_ours(args):
 
   # Host tier: as large as requested, bounded by this box's RAM share.
   pitch = g.block_bytes
-  want_host = args.host_blocks or 32768
-  local_ranks = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
-  fit = int(0.45 * mem_available_bytes() / max(local_ranks, 1) // pitch)
-  host_blocks = max(4 * B, min(want_host, fit))
+  host_blocks = c1_host_blocks(args, world)
   mgr = KVCacheManager([[t] for t in storages], host_blocks_to_allocate=host_blocks,
                        mode=args.mode, copy_streams=args.copy_streams,
                        chunk_blocks=args.chunk_blocks, max_ctas=args.max_ctas)
@@ -904,24 +939,9 @@ def run_ours(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic N(0,1) bf16 KV pool generated on device (seed 10+rank)",
-        "config": {
-            "workload": ("C1 Llama-3-8B KV tier: 32 layers x K/V, 16-token blocks of "
-                         "8 heads x 128 bf16 (2 MiB per block); per step the offloads "
-                         "(misses) and reloads (hits) of consecutive 512-access batches "
-                         "of the Zipf trace until 512 reloads are pending, both "
-                         "directions in flight"),
-            "blocks_per_step": round(sum(len(p[0]) + len(p[2]) for p in plans[args.warmup:])
-                                     / args.steps, 1),
-            "pool_blocks": pool_blocks, "pool_gib": round(full.numel() * 2 / GIB, 1),
-            "host_tier_blocks": host_blocks,
-            "host_tier_gib": round(host_blocks * pitch / GIB, 1),
-            "batch": B, "l2": "inputs larger than L2 (~1 GiB of scattered 2 MiB blocks per step)",
-            "trace": ("100k accesses Zipf(1.1) over 200k prefix ids (seed 10+rank), batches "
-                      "of 512, through the tier-2 store (reference LRU + host block "
-                      "allocator); steps from the middle of the trace"),
-            "trace_hit_rate": trace_stats["hit_rate"],
-            "transfer_mode": args.mode, "copy_streams": args.copy_streams,
-            "parallelism": f"replicas x{world}"},
+        "config": c1_config(args, host_blocks, plans, trace_stats, world),
+        "transfer": {"mode": args.mode, "copy_streams": args.copy_streams,
+                     "max_ctas": args.max_ctas or None},
         "per_gpu_gbs": round(value / world, 3),
         "pcie": {"offload_d2h_gbs": round(d2h_gbs, 2), "reload_h2d_gbs": round(h2d_gbs, 2),
                  "measured_peak": pcie, "spec_gbs_per_dir": PCIE_SPEC_GBS,
