@@ -200,3 +200,41 @@ def test_store_insert_all_or_nothing_and_drop_evict():
   got = dict((h, b) for h, b in s.lookup([H(5), H(6)], pin_found=False))
   assert sorted(b.host_block_id for b in got.values()) == [0, 1]  # ids of the evicted saves
   assert s.lookup([H(0)], pin_found=False) == []
+
+
+def test_store_concurrent_callers_keep_invariants():
+  """Threads insert, look up, release and evict their own keys through one
+  store at once (the native calls run without the GIL); afterwards no pin is
+  left, every host block is accounted for and the index holds each thread's
+  surviving keys."""
+  import threading
+  s = KVCacheStore(capacity=256, host_blocks=512)
+  errors = []
+
+  def worker(t):
+    try:
+      rng = np.random.default_rng(t)
+      for r in range(200):
+        keys = [f"t{t}-{int(k)}".encode() for k in rng.integers(0, 40, 4)]
+        keys = list(dict.fromkeys(keys))
+        hosts = [RaidenBlockId(host_block_id=t * 64 + int(rng.integers(0, 64)),
+                               status=BlockStatus.HOST) for _ in keys]
+        if s.insert(keys, hosts, on_host=True):
+          s.release(keys)
+        found = s.lookup(keys)
+        s.release([h for h, _ in found])
+        if r % 7 == 0:
+          s.evict(keys[:1])
+    except Exception as e:
+      errors.append(e)
+
+  threads = [threading.Thread(target=worker, args=(t,)) for t in range(8)]
+  for th in threads:
+    th.start()
+  for th in threads:
+    th.join()
+  assert not errors, errors
+  keys = [f"t{t}-{k}".encode() for t in range(8) for k in range(40)]
+  assert all(s.get_pin_count(k) == 0 for k in keys)
+  st = s.stats()
+  assert st["size"] <= 256 + 512 and st["available"] == 256

@@ -363,3 +363,43 @@ def test_fp8_quantizer_exact_over_bf16_domain(cuda):
   np.testing.assert_array_equal(st[:, 0:8192], payload[:, 0])
   got_scales = st[:, table.scale_off:table.scale_off + 4].copy().view(np.float32)[:, 0]
   np.testing.assert_array_equal(got_scales, scales[:, 0])
+
+
+@pytest.mark.parametrize("mode", [dict(mode="staged"), dict(mode="direct_h2d")])
+def test_manager_concurrent_callers(cuda, mode):
+  """Four host threads (ctypes releases the GIL, as the reference's bindings
+  do) offload and reload disjoint block ranges through one manager at once;
+  the result equals the model applying the same calls."""
+  import threading
+  geom = workloads.KVGeometry(layers=2, kv=2, block_tokens=16, heads=4, head_dim=128)
+  pool, mgr, model = make_pair(geom, 256, 128, 21, cuda, chunk_blocks=8, **mode)
+  plans = []
+  for t in range(4):
+    rng = np.random.default_rng(100 + t)
+    dev = list(range(t * 64, t * 64 + 32))      # offload sources of thread t
+    back = list(range(t * 64 + 32, t * 64 + 64))  # reload targets of thread t
+    host = list(range(t * 32, t * 32 + 32))
+    plans.append((list(rng.permutation(dev)), list(rng.permutation(host)), back))
+  errors = []
+
+  def worker(t):
+    try:
+      dev, host, back = plans[t]
+      for r in range(3):
+        mgr.d2h(dev, host).Await()
+        mgr.h2d(host, back).Await()
+    except Exception as e:  # surfaced below
+      errors.append(e)
+
+  threads = [threading.Thread(target=worker, args=(t,)) for t in range(4)]
+  for th in threads:
+    th.start()
+  for th in threads:
+    th.join()
+  assert not errors, errors
+  for t in range(4):
+    dev, host, back = plans[t]
+    model.d2h(dev, host)
+    model.h2d(host, back)
+  torch.cuda.synchronize()
+  assert_same(pool, mgr, model, range(128))
