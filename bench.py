@@ -76,7 +76,7 @@ def parse():
   p.add_argument("--max-ctas", type=int, default=0, help="kernel grid cap, 0 = default")
   p.add_argument("--kernel-case", default="",
                  choices=["", "extract", "insert", "extract_fp8", "insert_fp8", "pool_reshard",
-                          "insert_direct"],
+                          "insert_direct", "relayout"],
                  help="run a few launches of one kernel on a small case (for ncu)")
   return p.parse_args()
 
@@ -575,15 +575,20 @@ def run_handoff(torch, dist, rank, world, device, steps, warmup):
     storage_bytes = n_seqs * dbps * dbb
     dsts = [peer.data_ptr() + s * storage_bytes for s in range(n_st)]
     st_t, dt_t = torch.from_numpy(st_tab), torch.from_numpy(dt_tab)
+    err = torch.zeros(1, dtype=torch.int32, device=device)
     for _ in range(warmup):
-      ops.kv_relayout(srcs, dsts, sg, dg, st_t, dt_t, T, device=device)
+      ops.kv_relayout(srcs, dsts, sg, dg, st_t, dt_t, T, device=device,
+                      dst_pages=n_seqs * dbps, err=err)
     torch.cuda.synchronize(device)
+    if int(err.item()) != 0:
+      raise RuntimeError("kv_relayout: a page table entry is out of range")
   dist.barrier()
   if is_src:
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(steps):
-      ops.kv_relayout(srcs, dsts, sg, dg, st_t, dt_t, T, device=device)
+      ops.kv_relayout(srcs, dsts, sg, dg, st_t, dt_t, T, device=device,
+                      dst_pages=n_seqs * dbps, err=err)
     e1.record()
     torch.cuda.synchronize(device)
     ms = e0.elapsed_time(e1) / steps
@@ -1027,6 +1032,36 @@ def run_kernel_case(args):
     print(json.dumps({"kernel_case": "pool_reshard", "tasks": prog.n_tasks, "bytes": prog.bytes,
                       "ms": [round(x, 3) for x in ms],
                       "hbm_gbs": round(2 * prog.bytes / (min(ms) * 1e-3) / 1e9, 1)}))
+    return
+  if args.kernel_case == "relayout":
+    # The C3 relayout kernel on the pool_reshard case's geometry (16 of the 64
+    # storages, 8 x 32768 tokens, 16-token head-major -> 64-token token-major
+    # pages), destination on this GPU: 2 GiB read + 2 GiB written, 4 launches.
+    n_st, n_seqs, T, H, HB = 16, 8, 32768, 2, 256
+    rng = np.random.default_rng(30)
+    st = rng.permutation(n_seqs * T // 16).reshape(n_seqs, -1).astype(np.int32)
+    dt = rng.permutation(n_seqs * T // 64).reshape(n_seqs, -1).astype(np.int32)
+    src = [torch.randint(0, 256, (n_seqs * T // 16, 16 * H * HB), dtype=torch.uint8,
+                         device=device) for _ in range(n_st)]
+    dst = [torch.empty((n_seqs * T // 64, 64 * H * HB), dtype=torch.uint8, device=device)
+           for _ in range(n_st)]
+    sg = dict(block_tokens=16, heads=H, head_bytes=HB, head_major=1)
+    dg = dict(block_tokens=64, heads=H, head_bytes=HB, head_major=0)
+    st_t, dt_t = torch.from_numpy(st).to(device), torch.from_numpy(dt).to(device)
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+    ms = []
+    for _ in range(4):
+      a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+      a.record()
+      ops.kv_relayout(src, dst, sg, dg, st_t, dt_t, T, device=device, err=err)
+      b.record()
+      torch.cuda.synchronize()
+      ms.append(a.elapsed_time(b))
+    assert int(err.item()) == 0
+    moved = n_st * n_seqs * T * H * HB
+    print(json.dumps({"kernel_case": "relayout", "bytes": moved,
+                      "ms": [round(x, 3) for x in ms],
+                      "hbm_gbs": round(2 * moved / (min(ms) * 1e-3) / 1e9, 1)}))
     return
   if args.kernel_case == "insert_direct":
     # The insert kernel pulling 256 blocks (512 MiB) per launch from the

@@ -469,13 +469,16 @@ typedef struct ts_page_geometry {
  * src_table[q*src_table_stride + t/src.block_tokens] to destination block
  * dst_table[q*dst_table_stride + t/dst.block_tokens] in the destination order.
  * src.heads == dst.heads and src.head_bytes == dst.head_bytes are required.
- * Destination addresses may be a peer GPU's (P2P stores). */
+ * Destination addresses may be a peer GPU's (P2P stores).  Every storage
+ * holds at least src_pages (dst_pages) pages: a table entry outside
+ * [0, pages) is skipped and sets *d_err (a device int, may be NULL) to 1. */
 TS_API int ts_kv_relayout(int device, const uint64_t* d_src_bases,
                    const uint64_t* d_dst_bases, int n_storages,
                    ts_page_geometry src, ts_page_geometry dst,
                    const int32_t* d_src_table, int64_t src_table_stride,
                    const int32_t* d_dst_table, int64_t dst_table_stride,
-                   int64_t n_seqs, int64_t seq_tokens, void* stream);
+                   int64_t n_seqs, int64_t seq_tokens, int64_t src_pages,
+                   int64_t dst_pages, int* d_err, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Pinned host tier.                                                         */

@@ -137,13 +137,51 @@ def test_relayout_head_major16_to_token_major64(cuda, seq_tokens):
   srcs = [torch.from_numpy(rng.integers(0, 256, (n_src_blocks, sbb), dtype=np.uint8)).to(cuda)
           for _ in range(n_st)]
   dsts = [torch.zeros((n_dst_blocks, dbb), dtype=torch.uint8, device=cuda) for _ in range(n_st)]
-  ops.kv_relayout(srcs, dsts, GEOM_SRC, GEOM_DST, torch.from_numpy(src_table),
-                  torch.from_numpy(dst_table), seq_tokens, device=cuda)
+  err = ops.kv_relayout(srcs, dsts, GEOM_SRC, GEOM_DST, torch.from_numpy(src_table),
+                        torch.from_numpy(dst_table), seq_tokens, device=cuda)
   torch.cuda.synchronize()
+  assert int(err.item()) == 0
   for s, d in zip(srcs, dsts):
     want = np.zeros((n_dst_blocks, dbb), np.uint8)
     ors.relayout(s.cpu().numpy(), want, GEOM_SRC, GEOM_DST, src_table, dst_table, seq_tokens)
     np.testing.assert_array_equal(d.cpu().numpy(), want)
+
+
+def test_relayout_out_of_range_pages_are_skipped_and_flagged(cuda):
+  """A page id past a storage (either table) is skipped: nothing lands
+  outside the storages, the other pages still move, the flag is set."""
+  rng = np.random.default_rng(9)
+  T, n_src, n_dst = 128, 8, 2
+  st = np.arange(8, dtype=np.int32).reshape(1, 8)
+  dt = np.array([[0, 1]], np.int32)
+  src = torch.from_numpy(rng.integers(0, 256, (n_src + 1, 16 * 2 * 256), dtype=np.uint8)).to(cuda)
+  # storages are views of the first rows; the extra row is a guard band
+  dst_full = torch.zeros((n_dst + 1, 64 * 2 * 256), dtype=torch.uint8, device=cuda)
+  bad_src = st.copy()
+  bad_src[0, 5] = n_src          # one source page past the storage
+  err = ops.kv_relayout([src[:n_src]], [dst_full[:n_dst]], GEOM_SRC, GEOM_DST,
+                        torch.from_numpy(bad_src), torch.from_numpy(dt), T, device=cuda)
+  torch.cuda.synchronize()
+  assert int(err.item()) == 1
+  want = np.zeros((n_dst + 1, 64 * 2 * 256), np.uint8)
+  ors.relayout(src.cpu().numpy(), want, GEOM_SRC, GEOM_DST, st, dt, T)
+  got = dst_full.cpu().numpy()
+  # tokens 80..95 (source page 5) stay zero; everything else moved
+  page5 = np.zeros_like(want)
+  ors.relayout(np.where(np.arange(n_src + 1)[:, None] == 5, src.cpu().numpy(), 0).astype(np.uint8),
+               page5, GEOM_SRC, GEOM_DST, st, dt, T)
+  np.testing.assert_array_equal(got, np.where(page5 != 0, 0, want))
+  assert not got[n_dst].any()
+  bad_dst = dt.copy()
+  bad_dst[0, 1] = n_dst          # one destination page past the storage
+  dst_full.zero_()
+  err = ops.kv_relayout([src[:n_src]], [dst_full[:n_dst]], GEOM_SRC, GEOM_DST,
+                        torch.from_numpy(st), torch.from_numpy(bad_dst), T, device=cuda)
+  torch.cuda.synchronize()
+  assert int(err.item()) == 1
+  got = dst_full.cpu().numpy()
+  np.testing.assert_array_equal(got[0], want[0])
+  assert not got[1].any() and not got[n_dst].any()
 
 
 def test_relayout_round_trip(cuda):

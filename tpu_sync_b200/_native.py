@@ -254,7 +254,8 @@ _SIGS = {
     "ts_kv_relayout": (ctypes.c_int, [ctypes.c_int, _V, _V, ctypes.c_int,
                                       PageGeometry, PageGeometry, _V, ctypes.c_int64,
                                       _V, ctypes.c_int64, ctypes.c_int64,
-                                      ctypes.c_int64, _V]),
+                                      ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _V,
+                                      _V]),
     "ts_host_tier_create": (ctypes.c_int, [ctypes.c_uint64, ctypes.c_char_p,
                                            ctypes.c_char_p, ctypes.c_uint64,
                                            ctypes.c_int, ctypes.POINTER(_V),

@@ -155,9 +155,13 @@ __global__ void __launch_bounds__(kThreads)
                     ts_page_geometry sg, ts_page_geometry dg,
                     const int32_t* __restrict__ src_table, int64_t src_ts,
                     const int32_t* __restrict__ dst_table, int64_t dst_ts,
-                    int64_t n_seqs, int64_t seq_tokens, int64_t dst_blocks_per_seq) {
-  const int64_t vph = sg.head_bytes >> 4;          // 16-byte vectors per head vector
-  const int64_t vpt = vph * dg.heads;              // vectors per token
+                    int64_t n_seqs, int64_t seq_tokens, int64_t dst_blocks_per_seq,
+                    int64_t src_pages, int64_t dst_pages, int* err) {
+  // Token, head and vector indices fit 32 bits (checked on the host), so the
+  // per-vector divisions are 32-bit.
+  const uint32_t vph = uint32_t(sg.head_bytes >> 4);       // 16-byte vectors per head vector
+  const uint32_t vpt = vph * uint32_t(dg.heads);           // vectors per token
+  const uint32_t sbt = uint32_t(sg.block_tokens);
   const int64_t src_block_bytes = sg.block_tokens * sg.heads * sg.head_bytes;
   const int64_t dst_block_bytes = dg.block_tokens * dg.heads * dg.head_bytes;
   const int64_t items = int64_t(n_st) * n_seqs * dst_blocks_per_seq;
@@ -169,29 +173,41 @@ __global__ void __launch_bounds__(kThreads)
     const int64_t t0 = jb * dg.block_tokens;
     int64_t nt = seq_tokens - t0;
     if (nt > dg.block_tokens) nt = dg.block_tokens;
-    const int64_t nvec = nt * vpt;
+    const uint32_t nvec = uint32_t(nt) * vpt;
+    const int64_t dbi = dst_table[q * dst_ts + jb];
+    if (dbi < 0 || dbi >= dst_pages) {  // the whole destination page is skipped
+      if (err != nullptr && threadIdx.x == 0) *reinterpret_cast<volatile int*>(err) = 1;
+      continue;
+    }
     const uint8_t* sbase = reinterpret_cast<const uint8_t*>(src_bases[s]);
-    uint8_t* dbase = reinterpret_cast<uint8_t*>(dst_bases[s]);
-    uint8_t* dblk = dbase + int64_t(dst_table[q * dst_ts + jb]) * dst_block_bytes;
-    for (int64_t base = 0; base < nvec; base += int64_t(kThreads) * kRelayoutVecPerThread) {
+    uint8_t* dblk = reinterpret_cast<uint8_t*>(dst_bases[s]) + dbi * dst_block_bytes;
+    const int32_t* srow = src_table + q * src_ts;
+    for (uint32_t base = 0; base < nvec; base += uint32_t(kThreads) * kRelayoutVecPerThread) {
       int4 v[kRelayoutVecPerThread];
       uint8_t* dp[kRelayoutVecPerThread];
 #pragma unroll
       for (int i = 0; i < kRelayoutVecPerThread; ++i) {
-        const int64_t g = base + threadIdx.x + int64_t(i) * kThreads;
+        const uint32_t g = base + threadIdx.x + uint32_t(i) * kThreads;
         dp[i] = nullptr;
         if (g < nvec) {
-          const int64_t tl = g / vpt;               // token within dst block
-          const int64_t r = g - tl * vpt;
-          const int64_t h = r / vph;
-          const int64_t vv = r - h * vph;
-          const int64_t t = t0 + tl;                // token within sequence
-          const int64_t sb = src_table[q * src_ts + t / sg.block_tokens];
-          const int64_t st = t % sg.block_tokens;
-          const int64_t so = sg.head_major ? (h * sg.block_tokens + st) : (st * sg.heads + h);
-          const int64_t dpos = dg.head_major ? (h * dg.block_tokens + tl) : (tl * dg.heads + h);
-          v[i] = ld_nc(sbase + sb * src_block_bytes + so * sg.head_bytes + (vv << 4));
-          dp[i] = dblk + dpos * dg.head_bytes + (vv << 4);
+          const uint32_t tl = g / vpt;              // token within dst block
+          const uint32_t r = g - tl * vpt;
+          const uint32_t h = r / vph;
+          const uint32_t vv = r - h * vph;
+          const uint32_t t = uint32_t(t0) + tl;     // token within sequence
+          const uint32_t sbi = t / sbt;
+          const uint32_t st = t - sbi * sbt;
+          const int64_t sb = srow[sbi];
+          if (sb < 0 || sb >= src_pages) {
+            if (err != nullptr) *reinterpret_cast<volatile int*>(err) = 1;
+            continue;
+          }
+          const uint32_t so = sg.head_major ? (h * sbt + st) : (st * uint32_t(sg.heads) + h);
+          const uint32_t dpos = dg.head_major ? (h * uint32_t(dg.block_tokens) + tl)
+                                              : (tl * uint32_t(dg.heads) + h);
+          v[i] = ld_nc(sbase + sb * src_block_bytes + int64_t(so) * sg.head_bytes +
+                       (int64_t(vv) << 4));
+          dp[i] = dblk + int64_t(dpos) * dg.head_bytes + (int64_t(vv) << 4);
         }
       }
 #pragma unroll
@@ -262,9 +278,10 @@ extern "C" int ts_kv_relayout(int device, const uint64_t* d_src_bases,
                               ts_page_geometry src, ts_page_geometry dst,
                               const int32_t* d_src_table, int64_t src_table_stride,
                               const int32_t* d_dst_table, int64_t dst_table_stride,
-                              int64_t n_seqs, int64_t seq_tokens, void* stream) {
+                              int64_t n_seqs, int64_t seq_tokens, int64_t src_pages,
+                              int64_t dst_pages, int* d_err, void* stream) {
   tsb::clear_error();
-  if (n_storages < 0 || n_seqs < 0 || seq_tokens < 0)
+  if (n_storages < 0 || n_seqs < 0 || seq_tokens < 0 || src_pages < 0 || dst_pages < 0)
     return set_error(TS_INVALID_ARGUMENT, "counts must be non-negative");
   if (n_storages == 0 || n_seqs == 0 || seq_tokens == 0) return TS_OK;
   if (src.heads != dst.heads || src.head_bytes != dst.head_bytes)
@@ -274,6 +291,11 @@ extern "C" int ts_kv_relayout(int device, const uint64_t* d_src_bases,
     return set_error(TS_INVALID_ARGUMENT, "page geometry needs positive sizes and 16-byte head vectors");
   if (!d_src_bases || !d_dst_bases || !d_src_table || !d_dst_table)
     return set_error(TS_INVALID_ARGUMENT, "null pointer argument");
+  const int64_t vectors_per_block =
+      dst.block_tokens * dst.heads * (src.head_bytes >> 4);
+  if (seq_tokens > INT32_MAX || vectors_per_block > INT32_MAX ||
+      src.block_tokens > INT32_MAX || src.heads * src.block_tokens > INT32_MAX)
+    return set_error(TS_INVALID_ARGUMENT, "sequence or page too large for the relayout kernel");
   const int64_t dst_blocks_per_seq = (seq_tokens + dst.block_tokens - 1) / dst.block_tokens;
   const int64_t items = int64_t(n_storages) * n_seqs * dst_blocks_per_seq;
   tsb::DeviceGuard g(device);
@@ -281,7 +303,8 @@ extern "C" int ts_kv_relayout(int device, const uint64_t* d_src_bases,
   const int grid = int(items < cap ? items : cap);
   tsb::relayout_kernel<<<grid, tsb::kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       d_src_bases, d_dst_bases, n_storages, src, dst, d_src_table, src_table_stride,
-      d_dst_table, dst_table_stride, n_seqs, seq_tokens, dst_blocks_per_seq);
+      d_dst_table, dst_table_stride, n_seqs, seq_tokens, dst_blocks_per_seq, src_pages,
+      dst_pages, d_err);
   TS_CUDA_RET(cudaGetLastError(), "relayout launch");
   return TS_OK;
 }

@@ -166,20 +166,47 @@ class ReshardProgram:
         self.src_dtype, self.dst_dtype, _stream(stream, self.device)), "reshard: ")
 
 
+def _pages(storages, geom: dict, given: Optional[int], side: str) -> int:
+  """Pages every storage holds: `given`, else the smallest storage's bytes
+  (tensors and PeerBuffers know theirs) over the page size."""
+  if given is not None:
+    return int(given)
+  page = int(geom["block_tokens"]) * int(geom["heads"]) * int(geom["head_bytes"])
+  sizes = []
+  for x in storages:
+    if isinstance(x, torch.Tensor):
+      sizes.append(x.numel() * x.element_size())
+    elif hasattr(x, "nbytes"):
+      sizes.append(int(x.nbytes))
+    else:
+      raise ValueError(f"{side} storages given as raw addresses need {side}_pages")
+  return min(sizes) // page
+
+
 def kv_relayout(src_storages: Sequence, dst_storages: Sequence, src_geom: dict,
                 dst_geom: dict, src_table: torch.Tensor, dst_table: torch.Tensor,
                 seq_tokens: int, device=None,
-                stream: Optional[torch.cuda.Stream] = None) -> None:
+                stream: Optional[torch.cuda.Stream] = None, src_pages: Optional[int] = None,
+                dst_pages: Optional[int] = None,
+                err: Optional[torch.Tensor] = None) -> torch.Tensor:
   """Copies every token of every sequence between two page geometries.
 
-  src_storages / dst_storages: tensors or raw device addresses (destinations
-  may be peer-GPU addresses).  Geometries are dicts with block_tokens, heads,
-  head_bytes, head_major.  Tables are int32 [n_seqs, blocks_per_seq].
+  src_storages / dst_storages: tensors, PeerBuffers or raw device addresses
+  (destinations may be peer-GPU addresses; raw addresses need src_pages /
+  dst_pages, the pages each storage holds).  Geometries are dicts with
+  block_tokens, heads, head_bytes, head_major.  Tables are int32
+  [n_seqs, blocks_per_seq].  Table entries outside a storage's pages are
+  skipped and flagged: returns the device int32 flag (`err`, or a new one),
+  non-zero after the kernel ran if any entry was out of range.
   """
   device = torch.device(device) if device is not None else src_table.device
   n = len(src_storages)
   if len(dst_storages) != n:
     raise ValueError("source and destination storage counts differ")
+  sp = _pages(src_storages, src_geom, src_pages, "src")
+  dp = _pages(dst_storages, dst_geom, dst_pages, "dst")
+  if err is None:
+    err = torch.zeros(1, dtype=torch.int32, device=device)
   ptr = lambda x: x.data_ptr() if hasattr(x, "data_ptr") else int(x)
   d_src = torch.tensor([ptr(x) for x in src_storages], dtype=torch.int64,
                        device=device)
@@ -194,6 +221,7 @@ def kv_relayout(src_storages: Sequence, dst_storages: Sequence, src_geom: dict,
   _native.check(_native.lib().ts_kv_relayout(
       device.index, ctypes.c_void_p(d_src.data_ptr()), ctypes.c_void_p(d_dst.data_ptr()),
       n, sg, dg, ctypes.c_void_p(st.data_ptr()), st.shape[1],
-      ctypes.c_void_p(dt.data_ptr()), dt.shape[1], st.shape[0], int(seq_tokens),
-      _stream(stream, device)), "kv_relayout: ")
-  _keep([d_src, d_dst, st, dt], stream)
+      ctypes.c_void_p(dt.data_ptr()), dt.shape[1], st.shape[0], int(seq_tokens), sp, dp,
+      ctypes.c_void_p(err.data_ptr()), _stream(stream, device)), "kv_relayout: ")
+  _keep([d_src, d_dst, st, dt, err], stream)
+  return err
