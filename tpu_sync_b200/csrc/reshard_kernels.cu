@@ -148,8 +148,19 @@ int es_of(int dtype) {
 // ---------------------------------------------------------------------------
 
 constexpr int kRelayoutVecPerThread = 8;
+constexpr uint32_t kSkip = 0xFFFFFFFFu;  // no store (16-byte offsets never equal it)
 
-__global__ void __launch_bounds__(kThreads)
+// Index arithmetic of the relayout: 32-bit division by the page geometry, or
+// shifts and masks when every divisor is a power of two (all real KV
+// layouts: vectors per head vector, heads, tokens per page).
+template <bool kPow2>
+struct Div32 {
+  uint32_t d, shift;
+  __device__ __forceinline__ uint32_t div(uint32_t x) const { return kPow2 ? x >> shift : x / d; }
+};
+
+template <bool kPow2>
+__global__ void __launch_bounds__(kThreads, 4)
     relayout_kernel(const uint64_t* __restrict__ src_bases,
                     const uint64_t* __restrict__ dst_bases, int n_st,
                     ts_page_geometry sg, ts_page_geometry dg,
@@ -162,6 +173,9 @@ __global__ void __launch_bounds__(kThreads)
   const uint32_t vph = uint32_t(sg.head_bytes >> 4);       // 16-byte vectors per head vector
   const uint32_t vpt = vph * uint32_t(dg.heads);           // vectors per token
   const uint32_t sbt = uint32_t(sg.block_tokens);
+  const Div32<kPow2> by_vph{vph, uint32_t(__ffs(vph) - 1)};
+  const Div32<kPow2> by_vpt{vpt, uint32_t(__ffs(vpt) - 1)};
+  const Div32<kPow2> by_sbt{sbt, uint32_t(__ffs(sbt) - 1)};
   const int64_t src_block_bytes = sg.block_tokens * sg.heads * sg.head_bytes;
   const int64_t dst_block_bytes = dg.block_tokens * dg.heads * dg.head_bytes;
   const int64_t items = int64_t(n_st) * n_seqs * dst_blocks_per_seq;
@@ -184,18 +198,18 @@ __global__ void __launch_bounds__(kThreads)
     const int32_t* srow = src_table + q * src_ts;
     for (uint32_t base = 0; base < nvec; base += uint32_t(kThreads) * kRelayoutVecPerThread) {
       int4 v[kRelayoutVecPerThread];
-      uint8_t* dp[kRelayoutVecPerThread];
+      uint32_t doff[kRelayoutVecPerThread];  // byte offset in the dst page; kSkip = none
 #pragma unroll
       for (int i = 0; i < kRelayoutVecPerThread; ++i) {
         const uint32_t g = base + threadIdx.x + uint32_t(i) * kThreads;
-        dp[i] = nullptr;
+        doff[i] = kSkip;
         if (g < nvec) {
-          const uint32_t tl = g / vpt;              // token within dst block
+          const uint32_t tl = by_vpt.div(g);        // token within dst block
           const uint32_t r = g - tl * vpt;
-          const uint32_t h = r / vph;
+          const uint32_t h = by_vph.div(r);
           const uint32_t vv = r - h * vph;
           const uint32_t t = uint32_t(t0) + tl;     // token within sequence
-          const uint32_t sbi = t / sbt;
+          const uint32_t sbi = by_sbt.div(t);
           const uint32_t st = t - sbi * sbt;
           const int64_t sb = srow[sbi];
           if (sb < 0 || sb >= src_pages) {
@@ -207,12 +221,12 @@ __global__ void __launch_bounds__(kThreads)
                                               : (tl * uint32_t(dg.heads) + h);
           v[i] = ld_nc(sbase + sb * src_block_bytes + int64_t(so) * sg.head_bytes +
                        (int64_t(vv) << 4));
-          dp[i] = dblk + int64_t(dpos) * dg.head_bytes + (int64_t(vv) << 4);
+          doff[i] = dpos * uint32_t(dg.head_bytes) + (vv << 4);
         }
       }
 #pragma unroll
       for (int i = 0; i < kRelayoutVecPerThread; ++i)
-        if (dp[i] != nullptr) st_v4(dp[i], v[i]);
+        if (doff[i] != kSkip) st_v4(dblk + doff[i], v[i]);
     }
   }
 }
@@ -294,14 +308,18 @@ extern "C" int ts_kv_relayout(int device, const uint64_t* d_src_bases,
   const int64_t vectors_per_block =
       dst.block_tokens * dst.heads * (src.head_bytes >> 4);
   if (seq_tokens > INT32_MAX || vectors_per_block > INT32_MAX ||
-      src.block_tokens > INT32_MAX || src.heads * src.block_tokens > INT32_MAX)
+      src.block_tokens > INT32_MAX || src.heads * src.block_tokens > INT32_MAX ||
+      dst.block_tokens * dst.heads * dst.head_bytes > int64_t(UINT32_MAX) - 16)
     return set_error(TS_INVALID_ARGUMENT, "sequence or page too large for the relayout kernel");
   const int64_t dst_blocks_per_seq = (seq_tokens + dst.block_tokens - 1) / dst.block_tokens;
   const int64_t items = int64_t(n_storages) * n_seqs * dst_blocks_per_seq;
   tsb::DeviceGuard g(device);
   const int64_t cap = int64_t(tsb::sm_count(device)) * tsb::kCtasPerSm;
   const int grid = int(items < cap ? items : cap);
-  tsb::relayout_kernel<<<grid, tsb::kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  auto pow2 = [](int64_t v) { return v > 0 && (v & (v - 1)) == 0; };
+  const bool p2 = pow2(src.head_bytes >> 4) && pow2(src.heads) && pow2(src.block_tokens);
+  auto kernel = p2 ? tsb::relayout_kernel<true> : tsb::relayout_kernel<false>;
+  kernel<<<grid, tsb::kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       d_src_bases, d_dst_bases, n_storages, src, dst, d_src_table, src_table_stride,
       d_dst_table, dst_table_stride, n_seqs, seq_tokens, dst_blocks_per_seq, src_pages,
       dst_pages, d_err);
