@@ -147,6 +147,38 @@ def test_relayout_head_major16_to_token_major64(cuda, seq_tokens):
     np.testing.assert_array_equal(d.cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("sg,dg,seq_tokens", [
+    # power-of-two geometries (fast kernel): every head-major combination
+    ((16, 4, 128, 1), (32, 4, 128, 1), 100), ((16, 4, 128, 0), (64, 4, 128, 1), 130),
+    ((8, 8, 256, 0), (16, 8, 256, 0), 77), ((32, 1, 16, 1), (8, 1, 16, 0), 65),
+    # not powers of two (generic kernel): 3 heads, 48-byte heads, 24-token pages,
+    # a token wider than the CTA (heads x vectors > 256)
+    ((16, 3, 128, 1), (64, 3, 128, 0), 90), ((24, 2, 48, 0), (16, 2, 48, 1), 51),
+    ((16, 2, 256, 1), (24, 2, 256, 0), 70), ((4, 16, 512, 1), (8, 16, 512, 0), 19)])
+def test_relayout_geometries_match_oracle(cuda, sg, dg, seq_tokens):
+  sgd = dict(zip(("block_tokens", "heads", "head_bytes", "head_major"), sg))
+  dgd = dict(zip(("block_tokens", "heads", "head_bytes", "head_major"), dg))
+  n_seqs = 3
+  rng = np.random.default_rng(sum(sg) + sum(dg) + seq_tokens)
+  sbps = -(-seq_tokens // sg[0])
+  dbps = -(-seq_tokens // dg[0])
+  n_sb, n_db = n_seqs * sbps + 2, n_seqs * dbps + 2
+  st = rng.permutation(n_sb)[:n_seqs * sbps].reshape(n_seqs, sbps).astype(np.int32)
+  dt = rng.permutation(n_db)[:n_seqs * dbps].reshape(n_seqs, dbps).astype(np.int32)
+  sbb, dbb = sg[0] * sg[1] * sg[2], dg[0] * dg[1] * dg[2]
+  srcs = [torch.from_numpy(rng.integers(0, 256, (n_sb, sbb), dtype=np.uint8)).to(cuda)
+          for _ in range(2)]
+  dsts = [torch.zeros((n_db, dbb), dtype=torch.uint8, device=cuda) for _ in range(2)]
+  err = ops.kv_relayout(srcs, dsts, sgd, dgd, torch.from_numpy(st), torch.from_numpy(dt),
+                        seq_tokens, device=cuda)
+  torch.cuda.synchronize()
+  assert int(err.item()) == 0
+  for s, d in zip(srcs, dsts):
+    want = np.zeros((n_db, dbb), np.uint8)
+    ors.relayout(s.cpu().numpy(), want, sgd, dgd, st, dt, seq_tokens)
+    np.testing.assert_array_equal(d.cpu().numpy(), want)
+
+
 def test_relayout_out_of_range_pages_are_skipped_and_flagged(cuda):
   """A page id past a storage (either table) is skipped: nothing lands
   outside the storages, the other pages still move, the flag is set."""

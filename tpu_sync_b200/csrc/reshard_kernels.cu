@@ -231,6 +231,75 @@ __global__ void __launch_bounds__(kThreads, 4)
   }
 }
 
+// Fast path for power-of-two geometries whose token (heads x head vectors)
+// fits the CTA: a thread keeps one (head, 16-byte vector) of the token for
+// the whole page and steps through tokens, so per vector it only derives the
+// token's source page and position (shifts and masks) and issues the load.
+// lv = log2(vectors per head vector), lh = log2(heads), ls / ld = log2(tokens
+// per source / destination page).
+__global__ void __launch_bounds__(kThreads, 4)
+    relayout_pow2_kernel(const uint64_t* __restrict__ src_bases,
+                         const uint64_t* __restrict__ dst_bases, int n_st,
+                         int src_head_major, int dst_head_major, uint32_t lv, uint32_t lh,
+                         uint32_t ls, uint32_t ld,
+                         const int32_t* __restrict__ src_table, int64_t src_ts,
+                         const int32_t* __restrict__ dst_table, int64_t dst_ts,
+                         int64_t n_seqs, int64_t seq_tokens, int64_t dst_blocks_per_seq,
+                         int64_t src_pages, int64_t dst_pages, int* err) {
+  const uint32_t lhb = lv + 4;                        // log2(head bytes)
+  const uint32_t tshift = lv + lh;                    // log2(vectors per token)
+  const uint32_t tstep = uint32_t(kThreads) >> tshift;  // tokens per step of the CTA
+  const uint32_t r = threadIdx.x & ((1u << tshift) - 1);
+  const uint32_t h = r >> lv;
+  const uint32_t voff = (r & ((1u << lv) - 1)) << 4;  // byte offset in the head vector
+  const uint32_t tl0 = threadIdx.x >> tshift;
+  const int64_t src_block_bytes = int64_t(1) << (ls + lh + lhb);
+  const int64_t dst_block_bytes = int64_t(1) << (ld + lh + lhb);
+  const uint32_t dbt = 1u << ld;
+  const int64_t items = int64_t(n_st) * n_seqs * dst_blocks_per_seq;
+  for (int64_t w = blockIdx.x; w < items; w += gridDim.x) {
+    const int64_t jb = w % dst_blocks_per_seq;
+    const int64_t sq = w / dst_blocks_per_seq;
+    const int64_t q = sq % n_seqs;
+    const int s = int(sq / n_seqs);
+    const int64_t t0 = jb << ld;
+    const uint32_t nt = uint32_t(seq_tokens - t0 < int64_t(dbt) ? seq_tokens - t0 : dbt);
+    const int64_t dbi = dst_table[q * dst_ts + jb];
+    if (dbi < 0 || dbi >= dst_pages) {
+      if (err != nullptr && threadIdx.x == 0) *reinterpret_cast<volatile int*>(err) = 1;
+      continue;
+    }
+    const uint8_t* sbase = reinterpret_cast<const uint8_t*>(src_bases[s]);
+    uint8_t* dblk = reinterpret_cast<uint8_t*>(dst_bases[s]) + dbi * dst_block_bytes;
+    const int32_t* srow = src_table + q * src_ts;
+    for (uint32_t tb = tl0; tb < nt; tb += tstep * kRelayoutVecPerThread) {
+      int4 v[kRelayoutVecPerThread];
+      uint32_t doff[kRelayoutVecPerThread];
+#pragma unroll
+      for (int i = 0; i < kRelayoutVecPerThread; ++i) {
+        const uint32_t tl = tb + uint32_t(i) * tstep;  // token within the dst page
+        doff[i] = kSkip;
+        if (tl < nt) {
+          const uint32_t t = uint32_t(t0) + tl;
+          const int64_t sb = srow[t >> ls];
+          if (sb < 0 || sb >= src_pages) {
+            if (err != nullptr) *reinterpret_cast<volatile int*>(err) = 1;
+            continue;
+          }
+          const uint32_t st = t & ((1u << ls) - 1);
+          const uint32_t so = src_head_major ? ((h << ls) + st) : ((st << lh) + h);
+          const uint32_t dpos = dst_head_major ? ((h << ld) + tl) : ((tl << lh) + h);
+          v[i] = ld_nc(sbase + sb * src_block_bytes + (int64_t(so) << lhb) + voff);
+          doff[i] = (dpos << lhb) + voff;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kRelayoutVecPerThread; ++i)
+        if (doff[i] != kSkip) st_v4(dblk + doff[i], v[i]);
+    }
+  }
+}
+
 }  // namespace
 }  // namespace tsb
 
@@ -317,7 +386,17 @@ extern "C" int ts_kv_relayout(int device, const uint64_t* d_src_bases,
   const int64_t cap = int64_t(tsb::sm_count(device)) * tsb::kCtasPerSm;
   const int grid = int(items < cap ? items : cap);
   auto pow2 = [](int64_t v) { return v > 0 && (v & (v - 1)) == 0; };
+  auto lg = [](int64_t v) { uint32_t l = 0; while ((int64_t(1) << l) < v) ++l; return l; };
   const bool p2 = pow2(src.head_bytes >> 4) && pow2(src.heads) && pow2(src.block_tokens);
+  if (p2 && pow2(dst.block_tokens) && (src.head_bytes >> 4) * src.heads <= tsb::kThreads) {
+    tsb::relayout_pow2_kernel<<<grid, tsb::kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        d_src_bases, d_dst_bases, n_storages, src.head_major != 0, dst.head_major != 0,
+        lg(src.head_bytes >> 4), lg(src.heads), lg(src.block_tokens), lg(dst.block_tokens),
+        d_src_table, src_table_stride, d_dst_table, dst_table_stride, n_seqs, seq_tokens,
+        dst_blocks_per_seq, src_pages, dst_pages, d_err);
+    TS_CUDA_RET(cudaGetLastError(), "relayout launch");
+    return TS_OK;
+  }
   auto kernel = p2 ? tsb::relayout_kernel<true> : tsb::relayout_kernel<false>;
   kernel<<<grid, tsb::kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       d_src_bases, d_dst_bases, n_storages, src, dst, d_src_table, src_table_stride,
