@@ -256,6 +256,11 @@ __global__ void __launch_bounds__(kThreads, 4)
   const int64_t src_block_bytes = int64_t(1) << (ls + lh + lhb);
   const int64_t dst_block_bytes = int64_t(1) << (ld + lh + lhb);
   const uint32_t dbt = 1u << ld;
+  // Two page-id buffers used alternately: a tile's writes go to the buffer
+  // whose readers (two tiles back) all passed the previous tile's barrier,
+  // so one barrier per tile suffices.
+  __shared__ int32_t spage_buf[2][kThreads];
+  uint32_t parity = 0;
   const int64_t items = int64_t(n_st) * n_seqs * dst_blocks_per_seq;
   for (int64_t w = blockIdx.x; w < items; w += gridDim.x) {
     const int64_t jb = w % dst_blocks_per_seq;
@@ -272,16 +277,25 @@ __global__ void __launch_bounds__(kThreads, 4)
     const uint8_t* sbase = reinterpret_cast<const uint8_t*>(src_bases[s]);
     uint8_t* dblk = reinterpret_cast<uint8_t*>(dst_bases[s]) + dbi * dst_block_bytes;
     const int32_t* srow = src_table + q * src_ts;
-    for (uint32_t tb = tl0; tb < nt; tb += tstep * kRelayoutVecPerThread) {
+    const uint32_t tile = tstep * kRelayoutVecPerThread;  // tokens per step of the CTA
+    for (uint32_t tb = 0; tb < nt; tb += tile) {
+      // The tile's source page ids, loaded once into shared memory so that
+      // the data loads below do not wait on a dependent table load.
+      const uint32_t first = (uint32_t(t0) + tb) >> ls;
+      const uint32_t last = (uint32_t(t0) + min(tb + tile, nt) - 1) >> ls;
+      int32_t* spage = spage_buf[parity];
+      parity ^= 1u;
+      if (threadIdx.x <= last - first) spage[threadIdx.x] = srow[first + threadIdx.x];
+      __syncthreads();
       int4 v[kRelayoutVecPerThread];
       uint32_t doff[kRelayoutVecPerThread];
 #pragma unroll
       for (int i = 0; i < kRelayoutVecPerThread; ++i) {
-        const uint32_t tl = tb + uint32_t(i) * tstep;  // token within the dst page
+        const uint32_t tl = tb + tl0 + uint32_t(i) * tstep;  // token within the dst page
         doff[i] = kSkip;
         if (tl < nt) {
           const uint32_t t = uint32_t(t0) + tl;
-          const int64_t sb = srow[t >> ls];
+          const int64_t sb = spage[(t >> ls) - first];
           if (sb < 0 || sb >= src_pages) {
             if (err != nullptr) *reinterpret_cast<volatile int*>(err) = 1;
             continue;
@@ -388,7 +402,13 @@ extern "C" int ts_kv_relayout(int device, const uint64_t* d_src_bases,
   auto pow2 = [](int64_t v) { return v > 0 && (v & (v - 1)) == 0; };
   auto lg = [](int64_t v) { uint32_t l = 0; while ((int64_t(1) << l) < v) ++l; return l; };
   const bool p2 = pow2(src.head_bytes >> 4) && pow2(src.heads) && pow2(src.block_tokens);
-  if (p2 && pow2(dst.block_tokens) && (src.head_bytes >> 4) * src.heads <= tsb::kThreads) {
+  // the fast kernel stages a tile's source page ids in kThreads entries: a
+  // tile of (kThreads / vectors per token) * vectors-per-thread tokens spans
+  // at most tile / src.block_tokens + 2 pages
+  const int64_t vpt = (src.head_bytes >> 4) * src.heads;
+  const int64_t tile = vpt <= tsb::kThreads ? (tsb::kThreads / vpt) * tsb::kRelayoutVecPerThread : 0;
+  if (p2 && pow2(dst.block_tokens) && vpt <= tsb::kThreads &&
+      tile / src.block_tokens + 2 <= tsb::kThreads) {
     tsb::relayout_pow2_kernel<<<grid, tsb::kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         d_src_bases, d_dst_bases, n_storages, src.head_major != 0, dst.head_major != 0,
         lg(src.head_bytes >> 4), lg(src.heads), lg(src.block_tokens), lg(dst.block_tokens),
