@@ -238,3 +238,16 @@ def test_store_concurrent_callers_keep_invariants():
   assert all(s.get_pin_count(k) == 0 for k in keys)
   st = s.stats()
   assert st["size"] <= 256 + 512 and st["available"] == 256
+
+
+def test_remote_surface_refuses_without_registry():
+  """read_remote / poll_remote_read_status and the address properties exist
+  (api/torch/kv_cache_store.py:260-272, :536-596); remote reads need a global
+  registry, so they are refused."""
+  s = KVCacheStore(capacity=4, host_blocks=4)
+  assert s.raiden_controller_address == "" and s.store_server_address == ""
+  assert not s.read_remote([b"a"], [RaidenBlockId(status=BlockStatus.REMOTE)], [0])
+  assert "global registry" in s.last_error
+  assert s.poll_remote_read_status() == ([], [], [])
+  with pytest.raises(ValueError):
+    s.read_remote([b"a", b"b"], [RaidenBlockId()], [0])

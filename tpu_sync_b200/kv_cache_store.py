@@ -230,6 +230,33 @@ class KVCacheStore:
       raise ValueError(self.last_error)
     return rc == _native.OK
 
+  def read_remote(self, block_hashes: List[bytes], slices: Sequence,
+                  device_block_ids: Sequence[int]) -> bool:
+    """Reads REMOTE blocks from their owning peers (api/torch/kv_cache_store.py:536-581).
+
+    The owning peer's controller is found through the global registry, which
+    this local store does not have, so every read is refused (False, with
+    `last_error`), as the reference's store refuses without a registry."""
+    if len(slices) != len(block_hashes) or len(device_block_ids) != len(block_hashes):
+      raise ValueError("block_hashes, slices and device_block_ids must have the same length")
+    self.last_error = ("read_remote needs a global registry to reach the owning peer; "
+                       "this store is local only")
+    return False
+
+  def poll_remote_read_status(self):
+    """(done, failed, pending) of remote reads: none are ever issued."""
+    return [], [], []
+
+  @property
+  def raiden_controller_address(self) -> str:
+    """No controller endpoint: transfers are driven in-process."""
+    return ""
+
+  @property
+  def store_server_address(self) -> str:
+    """Not published to a registry ("" = undiscoverable)."""
+    return ""
+
   def _stream(self, stream):
     if self._mgr is None:
       return None
