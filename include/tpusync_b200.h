@@ -699,6 +699,58 @@ TS_API int ts_store_lru_op(ts_store* store, int op, const uint8_t* key, int64_t 
                            int64_t* out_val, uint8_t* out_key, int64_t out_key_cap,
                            int64_t* out_key_len);
 
+/* The manager's storages (layer-major, then shard): device, address, bytes,
+ * blocks (dim 0) and block bytes of storage `index`. */
+TS_API int ts_mgr_num_storages(ts_manager* mgr, int* n);
+TS_API int ts_mgr_storage(ts_manager* mgr, int index, int* device, uint64_t* dev_ptr,
+                          uint64_t* nbytes, int64_t* dim0, uint64_t* block_bytes);
+
+/* ---- Same-node block hand-off between managers (pull protocol) ---------
+ * Replaces the reference's NotifyForRead / StartRead / CompleteRead
+ * (tpu_sync/core/kv_cache_manager_with_transfer.cc:624-665, :1478-1760)
+ * and their TCP control and data planes: the producer publishes a /dev/shm
+ * mailbox (its storages' CUDA IPC handles, one entry per registered read
+ * with an interprocess event marking the blocks written); the consumer maps
+ * the storages, waits on that event on its stream and pulls every storage's
+ * bytes of each block pair with one kernel over NVLink.  Producer and
+ * consumer storages must match storage for storage (count, block bytes). */
+typedef struct ts_xfer_endpoint ts_xfer_endpoint;
+typedef struct ts_xfer_reader ts_xfer_reader;
+/* Producer: the endpoint `name` (a /dev/shm name; "ipc:" prefix accepted)
+ * with max_entries concurrent reads of up to max_blocks blocks each;
+ * unclaimed registrations time out after timeout_ms. */
+TS_API int ts_xfer_endpoint_create(ts_manager* mgr, const char* name, int max_entries,
+                                   int max_blocks, int64_t timeout_ms, ts_xfer_endpoint** out);
+TS_API int ts_xfer_endpoint_destroy(ts_xfer_endpoint* ep);
+TS_API int ts_xfer_endpoint_name(ts_xfer_endpoint* ep, char* buf, int64_t cap);
+/* NotifyForRead: the blocks are readable once the work queued on `stream`
+ * so far is done; *registered = 0 for an empty list (nothing to move). */
+TS_API int ts_xfer_register_read(ts_xfer_endpoint* ep, const char* req_id, uint64_t uuid,
+                                 const int64_t* block_ids, int64_t n, void* stream,
+                                 int* registered);
+/* Producer half of CompleteRead: req ids whose reads finished (or failed,
+ * or were never claimed before the timeout), packed into buf / offs under
+ * the capacity protocol (TS_RESOURCE_EXHAUSTED keeps them for a retry). */
+TS_API int ts_xfer_poll_sends(ts_xfer_endpoint* ep, uint8_t* buf, int64_t buf_len,
+                              int64_t* offs, int64_t offs_len, int64_t* n_out,
+                              int64_t* need_bytes);
+/* Consumer: reads into `mgr`'s storages; a read whose uuid the producer has
+ * not registered within timeout_ms fails. */
+TS_API int ts_xfer_reader_create(ts_manager* mgr, int64_t timeout_ms, ts_xfer_reader** out);
+TS_API int ts_xfer_reader_destroy(ts_xfer_reader* r);
+/* StartRead: remote block remote_ids[i] -> local block local_ids[i], queued
+ * on `stream` behind the producer's event (later work on `stream` sees the
+ * blocks).  Only blocks the producer registered under `uuid` may be read. */
+TS_API int ts_xfer_start_read(ts_xfer_reader* r, const char* req_id, uint64_t uuid,
+                              const char* endpoint, const int64_t* remote_ids,
+                              const int64_t* local_ids, int64_t n, void* stream);
+/* Consumer half of CompleteRead: which = 0 done req ids (polls first),
+ * 1 failed req ids; same packing as ts_xfer_poll_sends. */
+TS_API int ts_xfer_poll_reads(ts_xfer_reader* r, int which, uint8_t* buf, int64_t buf_len,
+                              int64_t* offs, int64_t offs_len, int64_t* n_out,
+                              int64_t* need_bytes);
+TS_API int ts_xfer_reader_pending(ts_xfer_reader* r, int64_t* n);
+
 /* ---- Crash-persistent KV block metadata --------------------------------
  * KVCacheMetadata (tpu_sync/kv_cache/kv_cache_metadata.h:19-141,
  * kv_cache_metadata.cc:27-188) on the reference's byte layout: a 128-byte

@@ -145,3 +145,25 @@ def test_pool_reshard_plan_into_peer_gpu():
     want = np.zeros((n_seqs * dbps, 64 * H * HB), np.uint8)
     ors.relayout(src[s].cpu().numpy(), want, sg, dg, st, dt, T)
     np.testing.assert_array_equal(dst[s].cpu().numpy(), want)
+
+
+def test_block_handoff_across_gpus():
+  """register_read / start_read between managers on two GPUs: in one process
+  (peer pointers) and across processes (CUDA IPC), the consumer's kernel
+  loading the producer's blocks over NVLink."""
+  two_gpus()
+  from tpu_sync_b200 import KVCacheManager
+  from test_gpu_handoff import poll_until, pool, run_cross_process
+  src, dst = pool(1, torch.device("cuda", 0)), pool(2, torch.device("cuda", 1))
+  prod = KVCacheManager([[t] for t in src], host_blocks_to_allocate=4)
+  cons = KVCacheManager([[t] for t in dst], host_blocks_to_allocate=4)
+  prod.register_read("peer", 3, [7, 8, 9])
+  cons.start_read("peer", 3, prod.get_local_endpoints(), [7, 8, 9], [60, 61, 62])
+  assert "peer" in poll_until(cons, 1, "peer")
+  torch.cuda.synchronize(1)
+  for l in range(len(src)):
+    assert torch.equal(dst[l][60:63].cpu(), src[l][7:10].cpu())
+  assert "peer" in poll_until(prod, 0, "peer")
+  prod.close()
+  cons.close()
+  run_cross_process(0, 1)

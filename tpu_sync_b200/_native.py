@@ -310,6 +310,24 @@ _SIGS = {
     "ts_store_lru_op": (ctypes.c_int, [_V, ctypes.c_int, ctypes.c_char_p, ctypes.c_int64,
                                        ctypes.POINTER(BlockInfo), ctypes.POINTER(BlockInfo),
                                        c_i64_p, ctypes.c_char_p, ctypes.c_int64, c_i64_p]),
+    "ts_mgr_num_storages": (ctypes.c_int, [_V, ctypes.POINTER(ctypes.c_int)]),
+    "ts_mgr_storage": (ctypes.c_int, [_V, ctypes.c_int, ctypes.POINTER(ctypes.c_int), c_u64_p,
+                                      c_u64_p, c_i64_p, c_u64_p]),
+    "ts_xfer_endpoint_create": (ctypes.c_int, [_V, ctypes.c_char_p, ctypes.c_int, ctypes.c_int,
+                                               ctypes.c_int64, ctypes.POINTER(_V)]),
+    "ts_xfer_endpoint_destroy": (ctypes.c_int, [_V]),
+    "ts_xfer_endpoint_name": (ctypes.c_int, [_V, ctypes.c_char_p, ctypes.c_int64]),
+    "ts_xfer_register_read": (ctypes.c_int, [_V, ctypes.c_char_p, ctypes.c_uint64, c_i64_p,
+                                             ctypes.c_int64, _V, ctypes.POINTER(ctypes.c_int)]),
+    "ts_xfer_poll_sends": (ctypes.c_int, [_V, ctypes.c_char_p, ctypes.c_int64, c_i64_p,
+                                          ctypes.c_int64, c_i64_p, c_i64_p]),
+    "ts_xfer_reader_create": (ctypes.c_int, [_V, ctypes.c_int64, ctypes.POINTER(_V)]),
+    "ts_xfer_reader_destroy": (ctypes.c_int, [_V]),
+    "ts_xfer_start_read": (ctypes.c_int, [_V, ctypes.c_char_p, ctypes.c_uint64, ctypes.c_char_p,
+                                          c_i64_p, c_i64_p, ctypes.c_int64, _V]),
+    "ts_xfer_poll_reads": (ctypes.c_int, [_V, ctypes.c_int, ctypes.c_char_p, ctypes.c_int64,
+                                          c_i64_p, ctypes.c_int64, c_i64_p, c_i64_p]),
+    "ts_xfer_reader_pending": (ctypes.c_int, [_V, c_i64_p]),
     "ts_kv_metadata_required_bytes": (ctypes.c_uint64, [ctypes.c_int]),
     "ts_kv_metadata_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int, ctypes.c_char_p,
                                            ctypes.POINTER(_V), ctypes.POINTER(ctypes.c_int)]),

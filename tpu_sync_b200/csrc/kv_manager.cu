@@ -1058,6 +1058,29 @@ extern "C" int ts_mgr_info(ts_manager* mgr, int64_t* host_blocks, uint64_t* host
   return TS_OK;
 }
 
+extern "C" int ts_mgr_storage(ts_manager* mgr, int index, int* device, uint64_t* dev_ptr,
+                              uint64_t* nbytes, int64_t* dim0, uint64_t* block_bytes) {
+  tsb::clear_error();
+  if (!mgr) return set_error(TS_INVALID_ARGUMENT, "null manager");
+  if (index < 0 || index >= int(mgr->st.size()))
+    return set_errorf(TS_OUT_OF_RANGE, "storage index %d out of range [0, %d)", index,
+                      int(mgr->st.size()));
+  const tsb::Storage& st = mgr->st[size_t(index)];
+  if (device) *device = mgr->device;
+  if (dev_ptr) *dev_ptr = st.dev_ptr;
+  if (nbytes) *nbytes = st.nbytes;
+  if (dim0) *dim0 = st.dim0;
+  if (block_bytes) *block_bytes = st.bb;
+  return TS_OK;
+}
+
+extern "C" int ts_mgr_num_storages(ts_manager* mgr, int* n) {
+  tsb::clear_error();
+  if (!mgr || !n) return set_error(TS_INVALID_ARGUMENT, "null argument");
+  *n = int(mgr->st.size());
+  return TS_OK;
+}
+
 extern "C" int ts_mgr_register_pools(ts_manager* mgr, const ts_pool_spec* pools, int64_t n) {
   tsb::clear_error();
   if (!mgr) return set_error(TS_INVALID_ARGUMENT, "null manager");
