@@ -7,16 +7,20 @@
 // Producer (ts_xfer_endpoint): publishes a mailbox named by its endpoint
 // string.  The header lists the manager's storages (IPC handle of each
 // allocation, offset, geometry); every registered read is an entry {uuid,
-// req_id, block ids, an interprocess CUDA event recorded on the producer's
-// stream when it registered, i.e. "these blocks are written"}.
+// req_id, block ids}.  Registration records an event on the producer's
+// stream; a watcher thread of the endpoint marks the entry READY once that
+// event has completed, i.e. once the blocks are written.
 //
 // Consumer (ts_xfer_reader): maps the producer's storages once per process
-// and device, claims the entry of a uuid, makes its stream wait on the
-// producer's event (a device-side wait, no spinning kernel), copies every
-// storage's bytes of each (remote block, local block) pair with one kernel
-// that loads the peer's memory over NVLink, and records its own completion.
-// Its poll reports the read done (or failed) and marks the entry consumed;
-// the producer's poll then reports the send done and recycles the entry.
+// and device, claims the READY entry of a uuid, copies every storage's bytes
+// of each (remote block, local block) pair with one kernel that loads the
+// peer's memory over NVLink, and records its own completion.  Its poll
+// reports the read done (or failed) and marks the entry consumed; the
+// producer's poll then reports the send done and recycles the entry.
+//
+// No event crosses a process or a device: a stream of one GPU waiting on an
+// interprocess event recorded on another GPU crashed the process in the
+// CUDA runtime on this platform, so readiness travels through the mailbox.
 //
 // Entry state words carry a generation (upper 24 bits) that changes every
 // time the entry is recycled, so a late consumer cannot touch an entry that
@@ -35,6 +39,11 @@
 
 #include <atomic>
 #include <cerrno>
+#include <chrono>
+#include <condition_variable>
+#include <thread>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -58,8 +67,8 @@ constexpr uint32_t kVersion = 1;
 constexpr int kReqIdBytes = 128;
 constexpr size_t kHeaderBytes = 4096;
 
-enum : uint32_t { kFree = 0, kWriting = 1, kRegistered = 2, kReading = 3, kConsumed = 4,
-                  kFailed = 5 };
+enum : uint32_t { kFree = 0, kWriting = 1, kRegistered = 2, kReady = 3, kReading = 4,
+                  kConsumed = 5, kFailed = 6 };
 
 struct alignas(64) Header {
   uint64_t magic;
@@ -90,8 +99,7 @@ struct alignas(64) Entry {
   int64_t n_blocks;
   uint64_t uuid;
   int64_t deadline_ns;         // CLOCK_MONOTONIC, the same clock in every process
-  uint8_t event_handle[64];    // cudaIpcEventHandle_t: the blocks are written
-  uint64_t event_ptr;          // the same event in the producer process
+  uint64_t reserved[9];
   char req_id[kReqIdBytes];
 };
 static_assert(std::atomic<uint32_t>::is_always_lock_free, "lock-free state word");
@@ -114,6 +122,15 @@ std::string shm_name(const std::string& endpoint) {
 }
 
 // pid 0: the consumer claimed the entry and has not written its pid yet.
+// Step trace of the consumer path on stderr when TSB_XFER_TRACE is set.
+void trace(const char* what) {
+  static const bool on = std::getenv("TSB_XFER_TRACE") != nullptr;
+  if (on) {
+    std::fprintf(stderr, "xfer: %s\n", what);
+    std::fflush(stderr);
+  }
+}
+
 bool process_alive(int pid) { return pid <= 0 || kill(pid, 0) == 0 || errno != ESRCH; }
 
 // Blocks a storage holds at its block size: the bound every block id of a
@@ -288,6 +305,10 @@ struct ts_xfer_endpoint {
   std::vector<cudaEvent_t> events;  // per entry: the "blocks written" event
   std::vector<std::string> done_sending;
   std::mutex mu;
+  std::condition_variable cv;
+  bool stop = false;
+  int pending = 0;  // entries registered whose event has not completed
+  std::thread watcher;
 };
 
 namespace {
@@ -300,10 +321,42 @@ void recycle(ts_xfer_endpoint* ep, int i, uint32_t gen) {
   ep->mb.e[i].word.store(make_word(gen + 1, kFree), std::memory_order_release);
 }
 
+// Marks registered entries READY once their event completed (FAILED if the
+// event reports an error).  Runs on the watcher thread, under ep->mu.
+void mark_ready_locked(ts_xfer_endpoint* ep) {
+  int pending = 0;
+  for (int i = 0; i < ep->mb.h->max_entries; ++i) {
+    Entry& e = ep->mb.e[i];
+    uint32_t w = e.word.load(std::memory_order_acquire);
+    if (state_of(w) != kRegistered) continue;
+    const cudaError_t q = cudaEventQuery(ep->events[size_t(i)]);
+    if (q == cudaErrorNotReady) {
+      ++pending;
+      continue;
+    }
+    e.word.compare_exchange_strong(w, make_word(gen_of(w), q == cudaSuccess ? kReady : kFailed),
+                                   std::memory_order_acq_rel);
+  }
+  ep->pending = pending;
+}
+
+void watch(ts_xfer_endpoint* ep) {
+  cudaSetDevice(ep->device);
+  std::unique_lock<std::mutex> lock(ep->mu);
+  while (!ep->stop) {
+    if (ep->pending > 0)
+      ep->cv.wait_for(lock, std::chrono::microseconds(50));
+    else
+      ep->cv.wait_for(lock, std::chrono::milliseconds(100));
+    if (ep->stop) break;
+    mark_ready_locked(ep);
+  }
+}
+
 // CompleteRead's producer half: consumed (or failed) entries are sends done;
-// registered entries past their deadline time out (done too, as the
-// reference's send entries do); a claimed entry whose consumer exited is
-// released.
+// registered entries nobody claimed before their deadline time out (done
+// too, as the reference's send entries do); a claimed entry whose consumer
+// exited is released.
 void poll_sends_locked(ts_xfer_endpoint* ep) {
   const int64_t now = now_ns();
   for (int i = 0; i < ep->mb.h->max_entries; ++i) {
@@ -313,7 +366,7 @@ void poll_sends_locked(ts_xfer_endpoint* ep) {
     bool done = false;
     if (st == kConsumed || st == kFailed) {
       done = true;
-    } else if (st == kRegistered && now > e.deadline_ns) {
+    } else if ((st == kRegistered || st == kReady) && now > e.deadline_ns) {
       done = e.word.compare_exchange_strong(w, make_word(gen, kFailed), std::memory_order_acq_rel);
     } else if (st == kReading && !process_alive(e.consumer_pid)) {
       done = e.word.compare_exchange_strong(w, make_word(gen, kFailed), std::memory_order_acq_rel);
@@ -401,12 +454,20 @@ extern "C" int ts_xfer_endpoint_create(ts_manager* mgr, const char* name, int ma
   ep->device = device;
   ep->timeout_ns = timeout_ms * 1000000;
   ep->events.assign(size_t(max_entries), nullptr);
+  ep->watcher = std::thread(watch, ep);
   *out = ep;
   return TS_OK;
 }
 
 extern "C" int ts_xfer_endpoint_destroy(ts_xfer_endpoint* ep) {
   if (!ep) return TS_OK;
+  {
+    std::lock_guard<std::mutex> lock(ep->mu);
+    ep->stop = true;
+  }
+  ep->cv.notify_all();
+  if (ep->watcher.joinable()) ep->watcher.join();
+  tsb::DeviceGuard g(ep->device);
   for (cudaEvent_t e : ep->events)
     if (e) cudaEventDestroy(e);
   ep->mb.release();
@@ -441,7 +502,7 @@ extern "C" int ts_xfer_register_read(ts_xfer_endpoint* ep, const char* req_id, u
   poll_sends_locked(ep);
   for (int i = 0; i < h->max_entries; ++i) {
     const uint32_t st = state_of(ep->mb.e[i].word.load(std::memory_order_acquire));
-    if ((st == kRegistered || st == kReading) && ep->mb.e[i].uuid == uuid)
+    if ((st == kRegistered || st == kReady || st == kReading) && ep->mb.e[i].uuid == uuid)
       return set_errorf(TS_ALREADY_EXISTS, "uuid %llu is already registered for read",
                         (unsigned long long)uuid);
   }
@@ -462,18 +523,14 @@ extern "C" int ts_xfer_register_read(ts_xfer_endpoint* ep, const char* req_id, u
   Entry& e = ep->mb.e[slot];
   tsb::DeviceGuard g(ep->device);
   cudaEvent_t ev = nullptr;
-  cudaError_t ce = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming | cudaEventInterprocess);
+  cudaError_t ce = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
   if (ce == cudaSuccess) ce = cudaEventRecord(ev, reinterpret_cast<cudaStream_t>(stream));
-  cudaIpcEventHandle_t eh;
-  if (ce == cudaSuccess) ce = cudaIpcGetEventHandle(&eh, ev);
   if (ce != cudaSuccess) {
     if (ev) cudaEventDestroy(ev);
     e.word.store(make_word(gen, kFree), std::memory_order_release);
     return tsb::cuda_error(ce, "read registration event");
   }
   ep->events[size_t(slot)] = ev;
-  std::memcpy(e.event_handle, &eh, sizeof(eh));
-  e.event_ptr = uint64_t(reinterpret_cast<uintptr_t>(ev));
   e.uuid = uuid;
   e.n_blocks = n;
   e.consumer_pid = 0;
@@ -482,6 +539,8 @@ extern "C" int ts_xfer_register_read(ts_xfer_endpoint* ep, const char* req_id, u
   std::memcpy(e.req_id, req_id, rl);
   std::memcpy(ep->mb.blocks + int64_t(slot) * h->max_blocks, block_ids, sizeof(int64_t) * size_t(n));
   e.word.store(make_word(gen, kRegistered), std::memory_order_release);
+  ep->pending += 1;
+  ep->cv.notify_all();
   *registered = 1;
   return TS_OK;
 }
@@ -531,8 +590,6 @@ struct Read {
   bool launched = false;
   int entry = -1;
   uint32_t gen = 0;
-  cudaEvent_t ready = nullptr;  // the producer's event (opened here unless same process)
-  bool own_ready = false;
   cudaEvent_t done = nullptr;
 };
 
@@ -580,6 +637,7 @@ int open_remote(ts_xfer_reader* r, const std::string& name, Remote** out) {
     close_remote(r, rem);
     r->remotes.erase(it);
   }
+  trace("open_remote: map");
   auto* rem = new Remote();
   rem->mb.name = name;
   rem->mb.fd = shm_open(name.c_str(), O_RDWR, 0600);
@@ -631,10 +689,14 @@ int open_remote(ts_xfer_reader* r, const std::string& name, Remote** out) {
     rem->dim0 = std::min(rem->dim0, blocks_of(rem->mb.st[s].nbytes, rem->mb.st[s].block_bytes));
   }
   rem->same_process = h->pid == int32_t(getpid());
+  trace(rem->same_process ? "open_remote: same process" : "open_remote: other process");
   std::vector<PeerStorage> table(size_t(h->n_storages));
   uint64_t max_bb = 0;
   int rc = TS_OK;
-  if (rem->same_process && h->device != r->device) rc = ts_enable_peer_access(r->device, h->device);
+  if (rem->same_process && h->device != r->device) {
+    trace("open_remote: enable peer access");
+    rc = ts_enable_peer_access(r->device, h->device);
+  }
   for (int s = 0; s < h->n_storages && rc == TS_OK; ++s) {
     uint64_t base = 0;
     if (rem->same_process) {
@@ -651,6 +713,7 @@ int open_remote(ts_xfer_reader* r, const std::string& name, Remote** out) {
                (table[size_t(s)].bb % 16 == 0);
     max_bb = std::max(max_bb, table[size_t(s)].bb);
   }
+  trace("open_remote: storage table");
   if (rc == TS_OK) {
     tsb::DeviceGuard g(r->device);
     cudaError_t ce = cudaMalloc(&rem->d_table, sizeof(PeerStorage) * table.size());
@@ -681,7 +744,7 @@ int try_launch(ts_xfer_reader* r, Read* x, bool* launched) {
   for (int i = 0; i < h->max_entries && slot < 0; ++i) {
     Entry& e = rem->mb.e[i];
     uint32_t w = e.word.load(std::memory_order_acquire);
-    if (state_of(w) != kRegistered || e.uuid != x->uuid) continue;
+    if (state_of(w) != kReady || e.uuid != x->uuid) continue;
     if (e.word.compare_exchange_strong(w, make_word(gen_of(w), kReading),
                                        std::memory_order_acq_rel)) {
       slot = i;
@@ -689,6 +752,7 @@ int try_launch(ts_xfer_reader* r, Read* x, bool* launched) {
     }
   }
   if (slot < 0) return TS_OK;
+  trace("try_launch: claimed");
   Entry& e = rem->mb.e[slot];
   e.consumer_pid = int32_t(getpid());
   x->entry = slot;
@@ -707,23 +771,17 @@ int try_launch(ts_xfer_reader* r, Read* x, bool* launched) {
                         (long long)x->pairs[k], (unsigned long long)x->uuid);
     }
   }
+  trace("try_launch: blocks checked");
+  // READY: the producer's writes of these blocks completed before it set
+  // the state, so the copy needs no wait on the producer's stream
   tsb::DeviceGuard g(r->device);
   cudaError_t ce = cudaSuccess;
-  if (rem->same_process) {
-    x->ready = reinterpret_cast<cudaEvent_t>(uintptr_t(e.event_ptr));
-    x->own_ready = false;
-  } else {
-    cudaIpcEventHandle_t eh;
-    std::memcpy(&eh, e.event_handle, sizeof(eh));
-    ce = cudaIpcOpenEventHandle(&x->ready, eh);
-    x->own_ready = ce == cudaSuccess;
-  }
-  if (ce == cudaSuccess) ce = cudaStreamWaitEvent(x->stream, x->ready, 0);
   void* d_pairs = nullptr;
   const size_t pbytes = sizeof(int64_t) * x->pairs.size();
   if (ce == cudaSuccess) ce = cudaMallocAsync(&d_pairs, pbytes, x->stream);
   if (ce == cudaSuccess)
     ce = cudaMemcpyAsync(d_pairs, x->pairs.data(), pbytes, cudaMemcpyHostToDevice, x->stream);
+  trace("try_launch: kernel");
   if (ce == cudaSuccess) {
     const int64_t n_pairs = int64_t(x->pairs.size() / 2);
     const int64_t units = n_pairs * h->n_storages * int64_t(rem->ppu);
@@ -741,12 +799,12 @@ int try_launch(ts_xfer_reader* r, Read* x, bool* launched) {
     const cudaError_t fe = cudaFreeAsync(d_pairs, x->stream);
     if (ce == cudaSuccess) ce = fe;
   }
+  trace("try_launch: done event");
   if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&x->done, cudaEventDisableTiming);
   if (ce == cudaSuccess) ce = cudaEventRecord(x->done, x->stream);
   if (ce != cudaSuccess) {
-    if (x->ready && x->own_ready) cudaEventDestroy(x->ready);
     if (x->done) cudaEventDestroy(x->done);
-    x->ready = x->done = nullptr;
+    x->done = nullptr;
     fail_entry();
     return tsb::cuda_error(ce, "peer block read");
   }
@@ -764,7 +822,6 @@ void finish(ts_xfer_reader* r, Read* x, bool ok) {
   }
   tsb::DeviceGuard g(r->device);
   if (x->done) cudaEventDestroy(x->done);
-  if (x->ready && x->own_ready) cudaEventDestroy(x->ready);
   (ok ? r->done_recving : r->failed_recving).push_back(x->req_id);
 }
 
@@ -858,6 +915,25 @@ extern "C" int ts_xfer_start_read(ts_xfer_reader* r, const char* req_id, uint64_
     if (remote_ids[i] < 0 || remote_ids[i] >= rem->dim0)
       return set_errorf(TS_OUT_OF_RANGE, "remote block id %lld out of range [0, %lld)",
                         (long long)remote_ids[i], (long long)rem->dim0);
+  // A registration of this uuid that does not cover the requested blocks
+  // fails the read now (and is released to its producer as failed).
+  for (int i = 0; i < rem->mb.h->max_entries; ++i) {
+    Entry& e = rem->mb.e[i];
+    uint32_t w = e.word.load(std::memory_order_acquire);
+    const uint32_t st = state_of(w);
+    if ((st != kRegistered && st != kReady) || e.uuid != uuid) continue;
+    const int64_t* reg = rem->mb.blocks + int64_t(i) * rem->mb.h->max_blocks;
+    std::unordered_set<int64_t> have(reg, reg + e.n_blocks);
+    for (int64_t k = 0; k < n; ++k) {
+      if (!have.count(remote_ids[k])) {
+        e.word.compare_exchange_strong(w, make_word(gen_of(w), kFailed), std::memory_order_acq_rel);
+        return set_errorf(TS_INVALID_ARGUMENT,
+                          "block %lld was not registered for read by uuid %llu",
+                          (long long)remote_ids[k], (unsigned long long)uuid);
+      }
+    }
+    break;
+  }
   Read x;
   x.req_id = req_id;
   x.uuid = uuid;
