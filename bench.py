@@ -540,6 +540,71 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
           "chunks_per_src": len(plan.for_source(0))}
 
 
+def run_pull(torch, dist, rank, world, device, steps, warmup):
+  """Block hand-off through the managers' pull protocol (register_read on
+  rank i, start_read on rank i + N/2): 512 C1 blocks (1 GiB) per pair and
+  step, the consumer's kernel loading the producer's pool over NVLink
+  (CUDA IPC).  Device time of the copy on the consumer's stream."""
+  from tpu_sync_b200 import KVCacheManager, workloads
+  half = world // 2
+  is_src = rank < half
+  g = workloads.C1
+  n_blocks, B = 2048, 512
+  full = torch.empty((g.layers, g.kv, n_blocks, g.block_tokens, g.heads, g.head_dim),
+                     dtype=torch.bfloat16, device=device)
+  full.normal_(generator=torch.Generator(device=device).manual_seed(50 + rank))
+  storages = [full[l, k] for l in range(g.layers) for k in range(g.kv)]
+  mgr = KVCacheManager([[t] for t in storages], host_blocks_to_allocate=4)
+  ep = mgr.get_local_endpoints() if is_src else None
+  eps = [None] * world
+  dist.all_gather_object(eps, ep)
+  rng = np.random.default_rng(60)
+  ms = []
+  for it in range(warmup + steps):
+    src_ids = rng.choice(n_blocks, B, replace=False).tolist()
+    dst_ids = rng.choice(n_blocks, B, replace=False).tolist()
+    if is_src:
+      assert mgr.register_read(f"pull-{it}", 1000 + it, src_ids)
+      t0 = time.time()
+      while mgr.read_state(1000 + it) != "ready":  # the blocks are written
+        if time.time() - t0 > 10:
+          raise RuntimeError("registered blocks never became ready")
+        time.sleep(0.0002)
+    dist.barrier()
+    if not is_src:
+      s = torch.cuda.current_stream(device)
+      e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+      e0.record(s)
+      mgr.start_read(f"pull-{it}", 1000 + it, eps[rank - half], src_ids, dst_ids)
+      e1.record(s)
+      t0 = time.time()
+      while f"pull-{it}" not in mgr.poll_stats()[1]:
+        if time.time() - t0 > 30:
+          raise RuntimeError("pull did not complete")
+      torch.cuda.synchronize(device)
+      if it >= warmup:
+        ms.append(e0.elapsed_time(e1))
+    else:
+      t0 = time.time()
+      while f"pull-{it}" not in mgr.poll_stats()[0]:
+        if time.time() - t0 > 30:
+          raise RuntimeError("pull was not consumed")
+        time.sleep(0.001)
+    dist.barrier()
+  t = torch.tensor([statistics.median(ms) if ms else 0.0], dtype=torch.float64, device=device)
+  dist.all_reduce(t, op=dist.ReduceOp.MAX)
+  step_ms = float(t.item())
+  moved = B * g.block_bytes
+  mgr.close()
+  del full, storages
+  return {"config": f"{B} C1 blocks (2 MiB each) per pair, {half} pairs (GPU i -> i+{half}), "
+                    "register_read / start_read / poll_stats over CUDA IPC",
+          "bytes_per_pair": moved, "ms": round(step_ms, 3),
+          "nvlink_gbs_per_pair": round(moved / (step_ms * 1e-3) / 1e9, 1) if step_ms else None,
+          "frac_of_nvlink_770": round(moved / (step_ms * 1e-3) / 1e9 / 770.0, 3)
+          if step_ms else None}
+
+
 def run_handoff(torch, dist, rank, world, device, steps, warmup):
   """C3: 8 sequences x 32768 tokens of Llama-3-8B KV (2 heads per GPU) move
   from rank i (16-token head-major pages) to rank i+half (64-token
@@ -981,6 +1046,8 @@ def run_ours(args):
     exchange["weight_sync"] = run_weight_sync(torch, dist, rank, world, device, 3, 2)
     torch.cuda.empty_cache()
     exchange["handoff"] = run_handoff(torch, dist, rank, world, device, 3, 2)
+    torch.cuda.empty_cache()
+    exchange["pull"] = run_pull(torch, dist, rank, world, device, 5, 2)
     torch.cuda.empty_cache()
     if rank == 0 and not args.no_cpu_baseline:
       # the same exchanges on the host cores (bounded samples; the other

@@ -723,6 +723,9 @@ TS_API int ts_xfer_endpoint_create(ts_manager* mgr, const char* name, int max_en
                                    int max_blocks, int64_t timeout_ms, ts_xfer_endpoint** out);
 TS_API int ts_xfer_endpoint_destroy(ts_xfer_endpoint* ep);
 TS_API int ts_xfer_endpoint_name(ts_xfer_endpoint* ep, char* buf, int64_t cap);
+/* State of the producer's read `uuid`: 0 none, 2 registered (blocks still
+ * being written), 3 ready, 4 being read, 5 consumed, 6 failed. */
+TS_API int ts_xfer_read_state(ts_xfer_endpoint* ep, uint64_t uuid, int* state);
 /* NotifyForRead: the blocks are readable once the work queued on `stream`
  * so far is done; *registered = 0 for an empty list (nothing to move). */
 TS_API int ts_xfer_register_read(ts_xfer_endpoint* ep, const char* req_id, uint64_t uuid,

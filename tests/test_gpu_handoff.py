@@ -180,3 +180,22 @@ def run_cross_process(producer_device, consumer_device):
 
 def test_cross_process_read_same_gpu(cuda):
   run_cross_process(0, 0)
+
+
+def test_read_state_progression(cuda):
+  src, dst = pool(9, cuda), pool(10, cuda)
+  prod = KVCacheManager([[t] for t in src], host_blocks_to_allocate=4)
+  cons = KVCacheManager([[t] for t in dst], host_blocks_to_allocate=4)
+  assert prod.read_state(5) == "none"
+  prod.register_read("req-s", 5, [0, 1])
+  t0 = time.time()
+  while prod.read_state(5) != "ready" and time.time() - t0 < 5:
+    time.sleep(0.001)
+  assert prod.read_state(5) == "ready"
+  cons.start_read("req-s", 5, prod.get_local_endpoints(), [0, 1], [2, 3])
+  assert "req-s" in poll_until(cons, 1, "req-s")
+  assert prod.read_state(5) == "consumed"
+  assert "req-s" in poll_until(prod, 0, "req-s")
+  assert prod.read_state(5) == "none"
+  prod.close()
+  cons.close()

@@ -317,6 +317,7 @@ _SIGS = {
                                                ctypes.c_int64, ctypes.POINTER(_V)]),
     "ts_xfer_endpoint_destroy": (ctypes.c_int, [_V]),
     "ts_xfer_endpoint_name": (ctypes.c_int, [_V, ctypes.c_char_p, ctypes.c_int64]),
+    "ts_xfer_read_state": (ctypes.c_int, [_V, ctypes.c_uint64, ctypes.POINTER(ctypes.c_int)]),
     "ts_xfer_register_read": (ctypes.c_int, [_V, ctypes.c_char_p, ctypes.c_uint64, c_i64_p,
                                              ctypes.c_int64, _V, ctypes.POINTER(ctypes.c_int)]),
     "ts_xfer_poll_sends": (ctypes.c_int, [_V, ctypes.c_char_p, ctypes.c_int64, c_i64_p,

@@ -555,6 +555,19 @@ extern "C" int ts_xfer_poll_sends(ts_xfer_endpoint* ep, uint8_t* buf, int64_t bu
   return pack_strings(&ep->done_sending, buf, buf_len, offs, offs_len, n_out, need_bytes);
 }
 
+extern "C" int ts_xfer_read_state(ts_xfer_endpoint* ep, uint64_t uuid, int* state) {
+  tsb::clear_error();
+  if (!ep || !state) return set_error(TS_INVALID_ARGUMENT, "null argument");
+  std::lock_guard<std::mutex> lock(ep->mu);
+  mark_ready_locked(ep);
+  *state = 0;
+  for (int i = 0; i < ep->mb.h->max_entries; ++i) {
+    const uint32_t st = state_of(ep->mb.e[i].word.load(std::memory_order_acquire));
+    if (st != kFree && st != kWriting && ep->mb.e[i].uuid == uuid) *state = int(st);
+  }
+  return TS_OK;
+}
+
 extern "C" int ts_xfer_endpoint_name(ts_xfer_endpoint* ep, char* buf, int64_t cap) {
   tsb::clear_error();
   if (!ep || !buf || cap <= int64_t(ep->mb.name.size()))

@@ -306,6 +306,17 @@ class KVCacheManager:
         _stream(stream, self.device), ctypes.byref(reg)), "register_read: ")
     return bool(reg.value)
 
+  READ_STATES = {0: "none", 2: "registered", 3: "ready", 4: "reading", 5: "consumed",
+                 6: "failed"}
+
+  def read_state(self, uuid: int) -> str:
+    """Producer: where read `uuid` stands ("ready" = its blocks are written
+    and a consumer may pull them)."""
+    st = ctypes.c_int()
+    _native.check(_native.lib().ts_xfer_read_state(self._endpoint(), int(uuid),
+                                                   ctypes.byref(st)))
+    return self.READ_STATES.get(st.value, str(st.value))
+
   def register_recv(self, uuid: int, req_id: str, expected_block_count: int) -> None:
     """Receivers need no staging here: a pool reshard program stores
     straight into this manager's HBM (PoolReshardProgram), so there is
