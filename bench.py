@@ -666,6 +666,45 @@ def run_handoff(torch, dist, rank, world, device, steps, warmup):
   ms = float(t.item())
   moved = n_st * n_seqs * T * H * HB
 
+  # The same relayout pulled by the consumer (the reference's StartRead
+  # direction): the decode GPU's kernel loads the prefill GPU's pages over
+  # NVLink and stores into its own pages.
+  src_desc = export_destinations({0: pages}) if is_src else None
+  sdescs = [None] * world
+  dist.all_gather_object(sdescs, src_desc)
+  pull_ms = 0.0
+  if not is_src:
+    peer_src = import_destinations(sdescs[rank - half], kernel_device=device.index)[0]
+    src_storage_bytes = n_seqs * sbps * sbb
+    psrcs = [peer_src.data_ptr() + s * src_storage_bytes for s in range(n_st)]
+    pdsts = [pages[s] for s in range(n_st)]
+    pst_t, pdt_t = torch.from_numpy(st_tab), torch.from_numpy(dt_tab)
+    perr = torch.zeros(1, dtype=torch.int32, device=device)
+    for _ in range(warmup):
+      ops.kv_relayout(psrcs, pdsts, sg, dg, pst_t, pdt_t, T, device=device,
+                      src_pages=n_seqs * sbps, err=perr)
+    torch.cuda.synchronize(device)
+    if int(perr.item()) != 0:
+      raise RuntimeError("kv_relayout (pull): a page table entry is out of range")
+  dist.barrier()
+  if not is_src:
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+      ops.kv_relayout(psrcs, pdsts, sg, dg, pst_t, pdt_t, T, device=device,
+                      src_pages=n_seqs * sbps, err=perr)
+    e1.record()
+    torch.cuda.synchronize(device)
+    pull_ms = e0.elapsed_time(e1) / steps
+  dist.barrier()
+  t = torch.tensor([pull_ms], dtype=torch.float64, device=device)
+  dist.all_reduce(t, op=dist.ReduceOp.MAX)
+  pull_ms = float(t.item())
+  if not is_src:
+    peer_src = psrcs = None
+    close_imports(device.index)
+  dist.barrier()
+
   # The same hand-off through the pool reshard planner: pools + span
   # declarations -> plan entries -> one program launch per source GPU.
   plan_ms = prog_ms = 0.0
@@ -718,6 +757,13 @@ def run_handoff(torch, dist, rank, world, device, steps, warmup):
           "bytes_per_pair": moved, "ms": round(ms, 3),
           "nvlink_gbs_per_pair": round(moved / (ms * 1e-3) / 1e9, 1) if ms else None,
           "frac_of_nvlink_770": round(moved / (ms * 1e-3) / 1e9 / 770.0, 3) if ms else None,
+          "pull": {"how": "the same relayout kernel launched on the consumer, loading the "
+                           "producer's pages over NVLink (CUDA IPC) and storing locally",
+                   "ms": round(pull_ms, 3),
+                   "nvlink_gbs_per_pair": round(moved / (pull_ms * 1e-3) / 1e9, 1)
+                   if pull_ms else None,
+                   "frac_of_nvlink_770": round(moved / (pull_ms * 1e-3) / 1e9 / 770.0, 3)
+                   if pull_ms else None},
           "pool_plan": {"how": "pool reshard planner (span declarations -> entries) + one "
                                "program launch per source GPU",
                         "plan_ms_cpu": round(plan_ms, 1), "tasks": n_tasks,
