@@ -752,18 +752,19 @@ def run_handoff(torch, dist, rank, world, device, steps, warmup):
     peer = None
     close_imports(device.index)
   dist.barrier()
+  def rate(t_ms):
+    return {"ms": round(t_ms, 3),
+            "nvlink_gbs_per_pair": round(moved / (t_ms * 1e-3) / 1e9, 1) if t_ms else None,
+            "frac_of_nvlink_770": round(moved / (t_ms * 1e-3) / 1e9 / 770.0, 3) if t_ms else None}
+
   return {"config": "C3 8 seqs x 32768 tok, 2 KV heads/GPU, 16-tok head-major -> 64-tok "
                     f"token-major, {half} pairs (GPU i -> i+{half})",
-          "bytes_per_pair": moved, "ms": round(ms, 3),
-          "nvlink_gbs_per_pair": round(moved / (ms * 1e-3) / 1e9, 1) if ms else None,
-          "frac_of_nvlink_770": round(moved / (ms * 1e-3) / 1e9 / 770.0, 3) if ms else None,
-          "pull": {"how": "the same relayout kernel launched on the consumer, loading the "
-                           "producer's pages over NVLink (CUDA IPC) and storing locally",
-                   "ms": round(pull_ms, 3),
-                   "nvlink_gbs_per_pair": round(moved / (pull_ms * 1e-3) / 1e9, 1)
-                   if pull_ms else None,
-                   "frac_of_nvlink_770": round(moved / (pull_ms * 1e-3) / 1e9 / 770.0, 3)
-                   if pull_ms else None},
+          "bytes_per_pair": moved,
+          "how": ("relayout kernel on the consumer (the reference's pull direction): loads "
+                  "the producer's pages over NVLink (CUDA IPC), stores its own pages"),
+          **rate(pull_ms),
+          "push": dict(how="the same kernel on the producer, storing into the consumer's "
+                           "pages over NVLink", **rate(ms)),
           "pool_plan": {"how": "pool reshard planner (span declarations -> entries) + one "
                                "program launch per source GPU",
                         "plan_ms_cpu": round(plan_ms, 1), "tasks": n_tasks,
