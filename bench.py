@@ -752,6 +752,52 @@ def run_handoff(torch, dist, rank, world, device, steps, warmup):
     peer = None
     close_imports(device.index)
   dist.barrier()
+
+  # The planner's program pulled: launched on the consumer, its tasks load
+  # the producer's pages over NVLink.
+  pull_prog_ms = 0.0
+  if not is_src:
+    from tpu_sync_b200 import pool_reshard, workloads
+    src_pools, dst_pools, dst_ids, reg = workloads.handoff_pool_plan_inputs(
+        n_st, st_tab, dt_tab, H, HB)
+    plan = pool_reshard.build_pool_reshard_plan([src_pools], dst_pools, ["kv"], dst_ids,
+                                                [(0, reg)])
+
+    class _Remote:  # one source storage inside the imported mapping
+      def __init__(self, ptr, dev, nbytes):
+        self._p, self.device, self.dtype, self.shape = ptr, dev, torch.uint8, (nbytes,)
+
+      def data_ptr(self):
+        return self._p
+
+    peer_src = import_destinations(sdescs[rank - half], kernel_device=device.index)[0]
+    src_storage_bytes = n_seqs * sbps * sbb
+    src_st = [_Remote(peer_src.data_ptr() + s * src_storage_bytes, peer_src.device,
+                      src_storage_bytes) for s in range(n_st)]
+    prog = pool_reshard.PoolReshardProgram(plan, 0, src_st, [pages[s] for s in range(n_st)],
+                                           device=device.index)
+    for _ in range(warmup):
+      prog.launch()
+    torch.cuda.synchronize(device)
+  dist.barrier()
+  if not is_src:
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+      prog.launch()
+    e1.record()
+    torch.cuda.synchronize(device)
+    pull_prog_ms = e0.elapsed_time(e1) / steps
+  dist.barrier()
+  t = torch.tensor([pull_prog_ms], dtype=torch.float64, device=device)
+  dist.all_reduce(t, op=dist.ReduceOp.MAX)
+  pull_prog_ms = float(t.item())
+  if not is_src:
+    prog.close()
+    plan.close()
+    peer_src = src_st = None
+    close_imports(device.index)
+  dist.barrier()
   def rate(t_ms):
     return {"ms": round(t_ms, 3),
             "nvlink_gbs_per_pair": round(moved / (t_ms * 1e-3) / 1e9, 1) if t_ms else None,
@@ -772,7 +818,9 @@ def run_handoff(torch, dist, rank, world, device, steps, warmup):
                         "nvlink_gbs_per_pair": round(moved / (prog_ms * 1e-3) / 1e9, 1)
                         if prog_ms else None,
                         "frac_of_nvlink_770": round(moved / (prog_ms * 1e-3) / 1e9 / 770.0, 3)
-                        if prog_ms else None}}
+                        if prog_ms else None,
+                        "pull": dict(how="the same program launched on the consumer",
+                                     **rate(pull_prog_ms))}}
 
 
 def run_c2_fp8(torch, rank, device, steps, warmup, max_over_ranks, cpu_seconds=0.0):

@@ -299,12 +299,13 @@ def _nbytes(t) -> int:
 
 
 class PoolReshardProgram:
-  """One source unit's share of a plan, ready to launch on its GPU.
+  """One source unit's share of a plan, ready to launch on a GPU.
 
-  src_storages / dst_storages are indexed by pool storage_index: the source
-  unit's device storages, and the destination's as this GPU reaches them
-  (tensors on this or a peer GPU, or PeerBuffer mappings of another
-  process's memory).
+  src_storages / dst_storages are indexed by pool storage_index, each as the
+  launching GPU reaches it: tensors on this or a peer GPU, or PeerBuffer
+  mappings of another process's memory.  The program runs on the source
+  unit's GPU by default (stores cross NVLink); with `device` set to the
+  destination's GPU it pulls instead (loads cross NVLink).
   """
 
   def __init__(self, plan: PoolReshardPlan, src_unit: int, src_storages: Sequence[Any],
@@ -313,7 +314,7 @@ class PoolReshardProgram:
     if len(src_storages) != len(dst_storages):
       raise ValueError("src_storages and dst_storages must have the same length")
     dev = src_storages[0].device.index if device is None else int(device)
-    for t in dst_storages:
+    for t in list(src_storages) + list(dst_storages):
       if isinstance(t, torch.Tensor) and t.device.index != dev:
         from tpu_sync_b200.weight_synchronizer import enable_peer_access
         enable_peer_access(dev, t.device.index)
