@@ -439,8 +439,9 @@ TS_API int ts_enable_peer_access(int device, int peer);
  * into this process FOR KERNELS RUNNING ON `device`: the handle is opened
  * with `device` current and lazy peer access, so `device`'s kernels can
  * store into the peer GPU's memory over NVLink.  Replaces the TCP push of
- * the reference's cross-host transfers on one NVSwitch box.  A handle may be
- * opened once per device per process; ts_ipc_close unmaps it. */
+ * the reference's cross-host transfers on one NVSwitch box.  Mappings are
+ * shared per (device, handle) in a process and reference-counted: every
+ * ts_ipc_open is paired with a ts_ipc_close, the last one unmaps. */
 TS_API int ts_ipc_open(int device, const void* handle_bytes, void** base_out);
 /* The exporting side: the 64-byte handle of the allocation holding dev_ptr and
  * dev_ptr's byte offset inside it (cudaMalloc'ed memory, e.g. torch's default

@@ -1,6 +1,8 @@
 """GPU parity of the weight-sync reshard executor and the KV hand-off relayout
 kernel against the CPU oracle (bit-exact, fp32 -> bf16 round-to-nearest-even)."""
 
+import textwrap
+
 import numpy as np
 import pytest
 import torch
@@ -318,3 +320,78 @@ def test_entries_strided_repeats_match_oracle(cuda):
                            [(so, do, size, ss, ds, count)])
   ws.push_weights_resharded_entries({0: entries}, {("sampler:0", 0, 0): dst}).Await()
   np.testing.assert_array_equal(dst.cpu().numpy(), want)
+
+
+# ---------------------------------------------------------------------------
+# push_weights to "ipc:" endpoints (PushWeights, weight_synchronizer_base.cc:541-556)
+# ---------------------------------------------------------------------------
+
+def _grid(cuda, seed, fill=None):
+  g = torch.Generator().manual_seed(seed)
+  shapes = [[(64, 33), (64, 33)], [(17,), (17,)], [(8, 4, 2), (8, 4, 2)]]
+  out = []
+  for layer in shapes:
+    row = []
+    for shp in layer:
+      t = torch.randn(shp, generator=g).to(torch.bfloat16)
+      row.append((t if fill is None else torch.full(shp, fill, dtype=torch.bfloat16)).to(cuda))
+    out.append(row)
+  return out
+
+
+def test_push_weights_to_ipc_endpoint_same_process(cuda):
+  src_grid, dst_grid = _grid(cuda, 1), _grid(cuda, 2, fill=0.0)
+  src, dst = WeightSynchronizer(src_grid), WeightSynchronizer(dst_grid)
+  ep = dst.get_local_endpoint()
+  assert ep.startswith("ipc:") and dst.get_local_endpoint() == ep
+  src.push_weights([ep])
+  for a, b in zip(src_grid, dst_grid):
+    for x, y in zip(a, b):
+      assert torch.equal(x, y)
+  with pytest.raises(ValueError, match="only same-node 'ipc:' endpoints"):
+    src.push_weights(["10.0.0.1:8000"])
+  other = WeightSynchronizer([[t[:32] for t in src_grid[0]]])
+  with pytest.raises(RuntimeError, match="is torch.bfloat16 \\(64, 33\\)"):
+    other.push_weights([ep])
+  dst.close()
+  with pytest.raises(RuntimeError, match="no weight synchronizer endpoint"):
+    src.push_weights([ep])
+
+
+_RECEIVER = textwrap.dedent("""
+    import sys
+    sys.path.insert(0, {root!r})
+    sys.path.insert(0, {tests!r})
+    import torch
+    from test_gpu_reshard import _grid
+    from tpu_sync_b200.weight_synchronizer import WeightSynchronizer
+    dev = torch.device("cuda", 0)
+    grid = _grid(dev, 2, fill=0.0)
+    ws = WeightSynchronizer(grid)
+    print(ws.get_local_endpoint(), flush=True)
+    sys.stdin.readline()          # the pusher is done
+    want = _grid(dev, 1)
+    ok = all(torch.equal(x, y) for a, b in zip(grid, want) for x, y in zip(a, b))
+    print("MATCH" if ok else "DIFF", flush=True)
+    ws.close()
+""")
+
+
+def test_push_weights_to_ipc_endpoint_other_process(cuda):
+  import subprocess, sys
+  from pathlib import Path
+  here = Path(__file__).resolve().parent
+  p = subprocess.Popen([sys.executable, "-c", _RECEIVER.format(root=str(here.parent),
+                                                               tests=str(here))],
+                       stdin=subprocess.PIPE, stdout=subprocess.PIPE, stderr=subprocess.PIPE,
+                       text=True)
+  try:
+    ep = p.stdout.readline().strip()
+    assert ep.startswith("ipc:"), p.stderr.read()[-3000:]
+    WeightSynchronizer(_grid(cuda, 1)).push_weights([ep])
+    out, err = p.communicate("done\n", timeout=120)
+    assert "MATCH" in out, (out, err[-3000:])
+  finally:
+    if p.poll() is None:
+      p.kill()
+      p.wait()

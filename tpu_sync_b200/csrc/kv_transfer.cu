@@ -180,44 +180,6 @@ int manager_geometry(ts_manager* mgr, int* device, std::vector<Geo>* out) {
   return TS_OK;
 }
 
-// Process-wide IPC mappings, (device, handle) -> base; a handle can be opened
-// only once per device in a process.
-struct IpcKey {
-  int device;
-  std::string handle;
-  bool operator<(const IpcKey& o) const {
-    return device != o.device ? device < o.device : handle < o.handle;
-  }
-};
-std::mutex g_ipc_mu;
-std::map<IpcKey, std::pair<void*, int>> g_ipc;  // base, references
-
-int ipc_acquire(int device, const uint8_t* handle, void** base) {
-  std::lock_guard<std::mutex> lock(g_ipc_mu);
-  IpcKey k{device, std::string(reinterpret_cast<const char*>(handle), 64)};
-  auto it = g_ipc.find(k);
-  if (it != g_ipc.end()) {
-    ++it->second.second;
-    *base = it->second.first;
-    return TS_OK;
-  }
-  int rc = ts_ipc_open(device, handle, base);
-  if (rc != TS_OK) return rc;
-  g_ipc.emplace(k, std::make_pair(*base, 1));
-  return TS_OK;
-}
-
-void ipc_release(int device, const uint8_t* handle) {
-  std::lock_guard<std::mutex> lock(g_ipc_mu);
-  IpcKey k{device, std::string(reinterpret_cast<const char*>(handle), 64)};
-  auto it = g_ipc.find(k);
-  if (it == g_ipc.end()) return;
-  if (--it->second.second == 0) {
-    ts_ipc_close(device, it->second.first);
-    g_ipc.erase(it);
-  }
-}
-
 // Packs strings into (buf, offs) under the capacity protocol of the C ABI.
 int pack_strings(std::vector<std::string>* items, uint8_t* buf, int64_t buf_len, int64_t* offs,
                  int64_t offs_len, int64_t* n_out, int64_t* need_bytes) {
@@ -586,7 +548,7 @@ struct Remote {
   Mailbox mb;
   uint64_t nonce = 0;
   bool same_process = false;
-  std::vector<uint8_t> opened;      // handles opened through the IPC cache (64 bytes each)
+  std::vector<void*> opened;        // IPC mappings taken (ts_ipc_open), released on close
   PeerStorage* d_table = nullptr;   // device table of (src, dst, bb) per storage
   bool vec = true;
   uint32_t ppu = 1;
@@ -625,7 +587,7 @@ void close_remote(ts_xfer_reader* r, Remote* rem) {
     tsb::DeviceGuard g(r->device);
     cudaFree(rem->d_table);
   }
-  for (size_t i = 0; i + 64 <= rem->opened.size(); i += 64) ipc_release(r->device, &rem->opened[i]);
+  for (void* base : rem->opened) ts_ipc_close(r->device, base);
   rem->mb.release();
   delete rem;
 }
@@ -716,9 +678,9 @@ int open_remote(ts_xfer_reader* r, const std::string& name, Remote** out) {
       base = rem->mb.st[s].dev_ptr;
     } else {
       void* b = nullptr;
-      rc = ipc_acquire(r->device, rem->mb.st[s].handle, &b);
+      rc = ts_ipc_open(r->device, rem->mb.st[s].handle, &b);
       if (rc != TS_OK) break;
-      rem->opened.insert(rem->opened.end(), rem->mb.st[s].handle, rem->mb.st[s].handle + 64);
+      rem->opened.push_back(b);
       base = uint64_t(reinterpret_cast<uintptr_t>(b)) + rem->mb.st[s].offset;
     }
     table[size_t(s)] = {base, r->local[size_t(s)].ptr, r->local[size_t(s)].bb};

@@ -11,6 +11,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -127,24 +128,47 @@ extern "C" int ts_enable_peer_access(int device, int peer) {
   return TS_OK;
 }
 
+namespace {
+// Process-wide IPC mappings by (device, handle): CUDA opens a handle once per
+// device in a process, so every user shares one mapping, reference-counted.
+std::mutex g_ipc_mu;
+std::map<std::pair<int, std::string>, std::pair<void*, int>> g_ipc;  // base, references
+}  // namespace
+
 extern "C" int ts_ipc_open(int device, const void* handle_bytes, void** base_out) {
   tsb::clear_error();
   if (!handle_bytes || !base_out) return tsb::set_error(TS_INVALID_ARGUMENT, "null pointer argument");
   cudaIpcMemHandle_t h;
   static_assert(sizeof(h) == 64, "cudaIpcMemHandle_t is 64 bytes");
   std::memcpy(&h, handle_bytes, sizeof(h));
+  const auto key = std::make_pair(device, std::string(static_cast<const char*>(handle_bytes), 64));
+  std::lock_guard<std::mutex> lock(g_ipc_mu);
+  auto it = g_ipc.find(key);
+  if (it != g_ipc.end()) {
+    ++it->second.second;
+    *base_out = it->second.first;
+    return TS_OK;
+  }
   tsb::DeviceGuard g(device);
   void* p = nullptr;
   TS_CUDA_RET(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+  g_ipc.emplace(key, std::make_pair(p, 1));
   *base_out = p;
   return TS_OK;
 }
 
 extern "C" int ts_ipc_close(int device, void* base) {
   tsb::clear_error();
-  tsb::DeviceGuard g(device);
-  TS_CUDA_RET(cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle");
-  return TS_OK;
+  std::lock_guard<std::mutex> lock(g_ipc_mu);
+  for (auto it = g_ipc.begin(); it != g_ipc.end(); ++it) {
+    if (it->first.first != device || it->second.first != base) continue;
+    if (--it->second.second > 0) return TS_OK;
+    g_ipc.erase(it);
+    tsb::DeviceGuard g(device);
+    TS_CUDA_RET(cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle");
+    return TS_OK;
+  }
+  return tsb::set_error(TS_NOT_FOUND, "no such IPC mapping on this device");
 }
 
 extern "C" int ts_ipc_export(const void* dev_ptr, void* handle_out, uint64_t* offset_out) {

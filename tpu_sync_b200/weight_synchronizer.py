@@ -20,6 +20,8 @@ multi-process job the sampler ranks export theirs with
 from __future__ import annotations
 
 import ctypes
+import os
+import pickle
 from typing import Any, Dict, List, Optional, Sequence, Tuple
 
 import torch
@@ -144,16 +146,88 @@ class WeightSynchronizer:
       raise RuntimeError("layer or shard index out of range")
     return self._host_buf(layer_idx, shard_idx)
 
-  def push_weights(self, peers: Sequence[Any]) -> None:
-    """Whole-buffer push to peer synchronizers with the same layout.
+  def get_local_endpoint(self) -> str:
+    """"ipc:<name>": this synchronizer's [layer][shard] buffers, published for
+    peers' push_weights on the same node (CUDA IPC descriptors in /dev/shm).
+    The buffers stay valid while this synchronizer lives; close() withdraws
+    the endpoint."""
+    if getattr(self, "_endpoint", None) is None:
+      desc = export_destinations({(l, s): t for l, layer in enumerate(self._grid)
+                                  for s, t in enumerate(layer)})
+      local = {k: (t.data_ptr(), t.device.index) for k, t in
+               ((k, self._grid[k[0]][k[1]]) for k in desc)}
+      name = f"tsb_ws_{os.getpid()}_{id(self) & 0xffffffff:x}"
+      with open(os.path.join("/dev/shm", name), "wb") as f:
+        pickle.dump({"pid": os.getpid(), "desc": desc, "local": local}, f)
+      self._endpoint = "ipc:" + name
+    return self._endpoint
 
-    ``peers`` are WeightSynchronizer objects (or [layers][shards] tensor
-    grids) of identical shapes; replaces PushWeights' D2H + TCP push of every
-    host buffer (weight_synchronizer_base.cc:541-556) with device copies.
+  def close(self) -> None:
+    ep = getattr(self, "_endpoint", None)
+    if ep is not None:
+      try:
+        os.unlink(os.path.join("/dev/shm", ep[4:]))
+      except FileNotFoundError:
+        pass
+      self._endpoint = None
+
+  def __del__(self):
+    try:
+      self.close()
+    except Exception:
+      pass
+
+  def _push_to_endpoint(self, endpoint: str) -> None:
+    """Byte copy of every (layer, shard) buffer into the peer's, one kernel
+    per source GPU storing over NVLink."""
+    try:
+      with open(os.path.join("/dev/shm", endpoint[4:]), "rb") as f:
+        info = pickle.load(f)
+    except FileNotFoundError:
+      raise RuntimeError(f"no weight synchronizer endpoint {endpoint}") from None
+    desc = info["desc"]
+    by_dev: Dict[int, List] = {}
+    for l, layer in enumerate(self._grid):
+      for s, t in enumerate(layer):
+        if (l, s) not in desc:
+          raise RuntimeError(f"peer {endpoint} has no buffer for layer {l} shard {s}")
+        peer_dev, _, _, dtype, shape = desc[(l, s)]
+        if dtype != t.dtype or tuple(shape) != tuple(t.shape):
+          raise RuntimeError(f"peer {endpoint} layer {l} shard {s} is {dtype} {tuple(shape)}, "
+                             f"this synchronizer's {t.dtype} {tuple(t.shape)}")
+        dev = t.device.index
+        if info["pid"] == os.getpid():  # the same process: plain peer pointers
+          ptr = info["local"][(l, s)][0]
+          enable_peer_access(dev, peer_dev)
+        else:
+          ptr = import_destinations({0: desc[(l, s)]}, kernel_device=dev)[0].data_ptr()
+        n = t.numel() * t.element_size()
+        by_dev.setdefault(dev, []).append((t.data_ptr(), ptr, 0, 0, n, 0, 0, 1))
+    for dev, chunks in by_dev.items():
+      device = torch.device("cuda", dev)
+      prog = ops.ReshardProgram(chunks, torch.uint8, torch.uint8, device)
+      prog.launch(torch.cuda.current_stream(device))
+      torch.cuda.current_stream(device).synchronize()
+
+  def push_weights(self, peers: Sequence[Any]) -> None:
+    """Whole-buffer push to peer synchronizers with the same layout
+    (PushWeights, weight_synchronizer_base.cc:541-556: D2H, then a TCP push
+    of every host buffer), here straight between device buffers.
+
+    ``peers``: "ipc:<name>" endpoints of synchronizers in other processes of
+    this node (get_local_endpoint()), WeightSynchronizer objects, or
+    [layers][shards] tensor grids, all with this synchronizer's shapes.
+    Returns when every byte has landed.
     """
     if not peers:
       raise RuntimeError("Peer list cannot be empty for trainer weights sync")
     for p in peers:
+      if isinstance(p, str):
+        if not p.startswith("ipc:"):
+          raise ValueError(f"peer {p!r}: only same-node 'ipc:' endpoints are supported "
+                           "(get_local_endpoint()); there is no TCP transport")
+        self._push_to_endpoint(p)
+        continue
       grid = p._grid if isinstance(p, WeightSynchronizer) else p
       for l, layer in enumerate(self._grid):
         for s, t in enumerate(layer):
