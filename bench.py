@@ -74,6 +74,8 @@ def parse():
   p.add_argument("--copy-streams", type=int, default=2)
   p.add_argument("--chunk-blocks", type=int, default=0, help="0 = manager default")
   p.add_argument("--max-ctas", type=int, default=0, help="kernel grid cap, 0 = default")
+  p.add_argument("--reload-staged-every", type=int, default=0,
+                 help="direct reloads: every n-th chunk through the copy engines (0 = none)")
   p.add_argument("--kernel-case", default="",
                  choices=["", "extract", "insert", "extract_fp8", "insert_fp8", "pool_reshard",
                           "insert_direct", "relayout"],
@@ -934,7 +936,8 @@ def run_ours(args):
   host_blocks = c1_host_blocks(args, world)
   mgr = KVCacheManager([[t] for t in storages], host_blocks_to_allocate=host_blocks,
                        mode=args.mode, copy_streams=args.copy_streams,
-                       chunk_blocks=args.chunk_blocks, max_ctas=args.max_ctas)
+                       chunk_blocks=args.chunk_blocks, max_ctas=args.max_ctas,
+                       reload_staged_every=args.reload_staged_every)
 
   pcie = measure_pcie(torch, device)
 
@@ -1109,7 +1112,8 @@ def run_ours(args):
         "data": "synthetic N(0,1) bf16 KV pool generated on device (seed 10+rank)",
         "config": c1_config(args, host_blocks, plans, trace_stats, world),
         "transfer": {"mode": args.mode, "copy_streams": args.copy_streams,
-                     "max_ctas": args.max_ctas or None},
+                     "max_ctas": args.max_ctas or None,
+                     "reload_staged_every": args.reload_staged_every or None},
         "per_gpu_gbs": round(value / world, 3),
         "pcie": {"offload_d2h_gbs": round(d2h_gbs, 2), "reload_h2d_gbs": round(h2d_gbs, 2),
                  "measured_peak": pcie, "spec_gbs_per_dir": PCIE_SPEC_GBS,

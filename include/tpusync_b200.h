@@ -530,6 +530,10 @@ typedef struct ts_manager_opts {
                                   PCIe themselves */
   int32_t copy_streams;        /* staged mode: copy streams per direction (1..4) */
   int32_t max_ctas;            /* grid cap of the kernels (0 = every SM) */
+  int32_t reload_staged_every; /* direct reloads only: every n-th chunk goes through
+                                  the copy engines instead (0 = none), so both
+                                  H2D mechanisms run at once */
+  int32_t pad_;
 } ts_manager_opts;
 
 /* Creates a manager over num_layers x num_shards storages (row-major

@@ -163,7 +163,7 @@ def test_fp8_extract_insert_matches_oracle(cuda, block_tokens, heads, n_blocks):
 
 MODES = [dict(mode="staged", copy_streams=1), dict(mode="staged", copy_streams=2),
          dict(mode="direct", max_ctas=64), dict(mode="direct_d2h", max_ctas=148),
-         dict(mode="direct_h2d")]
+         dict(mode="direct_h2d"), dict(mode="direct_h2d", reload_staged_every=2)]
 
 
 def make_pair(geom, blocks, host_blocks, seed, cuda, chunk_blocks=0, **kw):

@@ -78,7 +78,8 @@ class ManagerOpts(ctypes.Structure):
   _fields_ = [("host_blocks", ctypes.c_int64), ("chunk_blocks", ctypes.c_int64),
               ("shm_name", ctypes.c_char_p), ("model_uid", ctypes.c_char_p),
               ("fp8", ctypes.c_int32), ("mode", ctypes.c_int32),
-              ("copy_streams", ctypes.c_int32), ("max_ctas", ctypes.c_int32)]
+              ("copy_streams", ctypes.c_int32), ("max_ctas", ctypes.c_int32),
+              ("reload_staged_every", ctypes.c_int32), ("pad_", ctypes.c_int32)]
 
 
 class BlockInfo(ctypes.Structure):

@@ -114,6 +114,7 @@ struct ts_manager {
   int mode = 0;       // bit 0: offload direct, bit 1: reload direct (else staged)
   int ncs = 2;        // copy streams per direction (staged)
   int max_ctas = 0;   // grid cap of the kernels
+  int reload_staged_every = 0;  // direct reloads: every n-th chunk staged (0 = none)
   uint8_t* host_dev = nullptr;  // device address of the mapped host tier
 
   cudaStream_t s_out_kernel = nullptr, s_in_kernel = nullptr;
@@ -456,9 +457,11 @@ int enqueue_transfer(ts_manager* m, bool to_host, const Plan& p, void* user_stre
   cudaStream_t ks = to_host ? m->s_out_kernel : m->s_in_kernel;
   cudaStream_t* cs = to_host ? m->out_cs : m->in_cs;
   const bool direct = is_direct(m, to_host) && p.whole;
+  // direct reloads may route every n-th chunk through the copy engines
+  const int staged_every = to_host ? 0 : m->reload_staged_every;
   const cudaStream_t last = last_stream(m, to_host);
   std::vector<cudaStream_t> streams{ks};
-  if (!is_direct(m, to_host))
+  if (!is_direct(m, to_host) || staged_every > 0)
     for (int i = 0; i < m->ncs; ++i) streams.push_back(cs[i]);
   int* err_dev = nullptr;
   TS_CUDA_RET(cudaHostGetDevicePointer(reinterpret_cast<void**>(&err_dev), ev->err_word, 0),
@@ -544,34 +547,30 @@ int enqueue_transfer(ts_manager* m, bool to_host, const Plan& p, void* user_stre
     for (int64_t k = 0; k < cn; ++k) x = std::max(x, need_o[size_t(c0 + k)]);
     return x;
   };
-  if (direct) {
-    for (int64_t c0 = 0; c0 < nblk; c0 += m->chunk_blocks) {
-      const int64_t cn = std::min<int64_t>(m->chunk_blocks, nblk - c0);
-      int rc = wait_upto(chunk_need(c0, cn));
-      if (rc != TS_OK) return rc;
+  std::vector<Slot>& slots = to_host ? m->out_slots : m->in_slots;
+  int& next = to_host ? m->next_out : m->next_in;
+  int chunk = 0;  // staged chunks issued (copy stream rotation)
+  int64_t ci = 0;
+  for (int64_t c0 = 0; c0 < nblk; c0 += m->chunk_blocks, ++ci) {
+    const int64_t cn = std::min<int64_t>(m->chunk_blocks, nblk - c0);
+    int rc0 = wait_upto(chunk_need(c0, cn));
+    if (rc0 != TS_OK) return rc0;
+    if (direct && !(staged_every > 0 && ci % staged_every == staged_every - 1)) {
+      // the kernel moves the chunk over PCIe itself (mapped host tier)
       ParamIds ids;
       ids.direct = 1;
       for (int64_t k = 0; k < cn; ++k) {
         ids.v[k] = dev_ids[size_t(c0 + k)];
         ids.s[k] = host_ids[size_t(c0 + k)];
       }
-      rc = launch_chunk(m, to_host, ids, cn, m->host_dev, err_dev, ks);
+      int rc = launch_chunk(m, to_host, ids, cn, m->host_dev, err_dev, ks);
       if (rc != TS_OK) return rc;
+      continue;
     }
-    TS_CUDA_RET(cudaEventRecord(ev->done, ks), "event record");
-    return TS_OK;
-  }
-
-  std::vector<Slot>& slots = to_host ? m->out_slots : m->in_slots;
-  int& next = to_host ? m->next_out : m->next_in;
-  int chunk = 0;
-  for (int64_t c0 = 0; c0 < nblk; c0 += m->chunk_blocks, ++chunk) {
-    const int64_t cn = std::min<int64_t>(m->chunk_blocks, nblk - c0);
-    int rc0 = wait_upto(chunk_need(c0, cn));
-    if (rc0 != TS_OK) return rc0;
+    ++chunk;
     Slot& slot = slots[size_t(next)];
     next = (next + 1) % int(slots.size());
-    cudaStream_t cc = cs[chunk % m->ncs];
+    cudaStream_t cc = cs[(chunk - 1) % m->ncs];
     ParamIds ids;
     ids.direct = 0;
     for (int64_t k = 0; k < cn; ++k) ids.v[k] = dev_ids[size_t(c0 + k)];
@@ -883,6 +882,8 @@ extern "C" int ts_mgr_create(const ts_storage_desc* storages, int num_layers,
   }
   m->ncs = opts && opts->copy_streams > 0 ? std::min(opts->copy_streams, tsb::kMaxCopyStreams) : 2;
   m->max_ctas = opts && opts->max_ctas > 0 ? opts->max_ctas : 0;
+  m->reload_staged_every = opts && opts->reload_staged_every > 0 && (m->mode & 2)
+                               ? opts->reload_staged_every : 0;
   const int n = num_layers * num_shards;
   m->st.resize(size_t(n));
   // reference: slice_byte_size from layer 0, shard 0 (GetMajorSliceByteSize)
@@ -977,7 +978,7 @@ extern "C" int ts_mgr_create(const ts_storage_desc* storages, int num_layers,
   if (e != cudaSuccess) return fail(tsb::cuda_error(e, "event create"));
   const size_t slot_bytes = size_t(m->chunk_blocks) * m->host_pitch;
   for (int dir = 0; dir < 2; ++dir) {
-    if (tsb::is_direct(m, dir == 0)) continue;
+    if (tsb::is_direct(m, dir == 0) && !(dir == 1 && m->reload_staged_every > 0)) continue;
     std::vector<tsb::Slot>& slots = dir == 0 ? m->out_slots : m->in_slots;
     slots.resize(size_t(2 * m->ncs));
     for (tsb::Slot& sl : slots) {

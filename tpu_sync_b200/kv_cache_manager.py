@@ -154,6 +154,7 @@ class KVCacheManager:
       mode: str = "staged",
       copy_streams: int = 2,
       max_ctas: int = 0,
+      reload_staged_every: int = 0,
   ):
     if host_blocks_to_allocate is None:
       if max_blocks is None or num_slots is None:
@@ -196,7 +197,7 @@ class KVCacheManager:
         host_blocks=int(host_blocks_to_allocate), chunk_blocks=int(chunk_blocks),
         shm_name=shm_name.encode(), model_uid=model_uid.encode(), fp8=int(fp8),
         mode=modes[mode], copy_streams=int(copy_streams),
-        max_ctas=int(max_ctas))
+        max_ctas=int(max_ctas), reload_staged_every=int(reload_staged_every))
     handle = ctypes.c_void_p()
     rc = _native.lib().ts_mgr_create(descs, self.num_layers, self.num_shards,
                                      ctypes.byref(opts), ctypes.byref(handle))
