@@ -511,26 +511,37 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
       for (so, do, size, ss, ds, cnt) in cs:
         chunks.append((sp, dp, so, do, size, ss, ds, cnt))
     prog = ops.ReshardProgram(chunks, torch.float32, torch.bfloat16, device)
+    prog_ce = ops.ReshardCopyEngineProgram(chunks, torch.float32, torch.bfloat16, device)
     for _ in range(warmup):
       prog.launch()
+      prog_ce.launch()
     torch.cuda.synchronize(device)
   dist.barrier()
+  ce_ms = 0.0
   if is_src:
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-      prog.launch()
-    e1.record()
-    torch.cuda.synchronize(device)
-    per_push_ms = e0.elapsed_time(e1) / steps
+    for which in ("sm", "copy"):
+      p_ = prog if which == "sm" else prog_ce
+      e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+      e0.record()
+      for _ in range(steps):
+        p_.launch()
+      e1.record()
+      torch.cuda.synchronize(device)
+      if which == "sm":
+        per_push_ms = e0.elapsed_time(e1) / steps
+      else:
+        ce_ms = e0.elapsed_time(e1) / steps
   dist.barrier()
-  t = torch.tensor([per_push_ms], dtype=torch.float64, device=device)
+  t = torch.tensor([per_push_ms, ce_ms], dtype=torch.float64, device=device)
   dist.all_reduce(t, op=dist.ReduceOp.MAX)
-  push_s = float(t.item()) / 1e3
+  sm_s, ce_s = float(t[0].item()) / 1e3, float(t[1].item()) / 1e3
+  push_s = min(sm_s, ce_s) if ce_s > 0 else sm_s
+  engine = "copy" if push_s == ce_s and ce_s > 0 else "sm"
   recv_bytes = max(2 * plan.elements_to(d) for d in range(half))
   total_params = sum(math.prod(v.shape) for v in specs)
   del prog
   if is_src:
+    prog_ce.close()
     dsts = None
     close_imports(device.index)
   dist.barrier()
@@ -539,6 +550,12 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
           "bytes_per_dst_gpu": recv_bytes,
           "nvlink_gbs_per_dst_gpu": round(recv_bytes / push_s / 1e9, 1) if push_s else None,
           "frac_of_nvlink_770": round(recv_bytes / push_s / 1e9 / 770.0, 3) if push_s else None,
+          "engine": engine,
+          "engines": {"sm": {"how": "one kernel per trainer GPU casting and storing into the "
+                                    "samplers' memory over NVLink", "seconds": round(sm_s, 5)},
+                      "copy": {"how": "the kernel casts into local staging, the copy engines "
+                                      "move each chunk (cudaMemcpy2DAsync), 16 pipelined groups",
+                               "seconds": round(ce_s, 5)}},
           "chunks_per_src": len(plan.for_source(0))}
 
 

@@ -449,6 +449,23 @@ TS_API int ts_ipc_open(int device, const void* handle_bytes, void** base_out);
 TS_API int ts_ipc_export(const void* dev_ptr, void* handle_out, uint64_t* offset_out);
 TS_API int ts_ipc_close(int device, void* base);
 
+/* Weight-sync reshard pushed by the copy engines: the chunks' fp32 -> bf16
+ * cast goes to a local staging buffer (rows packed), and every staged chunk
+ * moves to its (local or peer) destination with one cudaMemcpy2DAsync;
+ * groups of chunks pipeline the cast against the copies.  Same-dtype chunks
+ * are copied from the source directly.  Launches are ordered on `stream`
+ * (after its earlier work, before its later work).  Replaces, like
+ * ts_reshard_copy, PushWeightsResharded's D2H + TCP push + H2D
+ * (weight_synchronizer_base.cc:558-760). */
+typedef struct ts_reshard_ce ts_reshard_ce;
+TS_API int ts_reshard_ce_create(int device, const ts_reshard_chunk* chunks, int64_t n,
+                                int src_dtype, int dst_dtype, int n_groups,
+                                ts_reshard_ce** out);
+TS_API int ts_reshard_ce_launch(ts_reshard_ce* program, void* stream);
+TS_API int ts_reshard_ce_info(ts_reshard_ce* program, int64_t* groups,
+                              uint64_t* staging_bytes, int64_t* copies);
+TS_API int ts_reshard_ce_destroy(ts_reshard_ce* program);
+
 /* ------------------------------------------------------------------------ */
 /* Paged KV relayout (disaggregated prefill -> decode hand-off).             */
 /* ------------------------------------------------------------------------ */

@@ -32,7 +32,7 @@ def small_llama(hidden=256, ffn=640, vocab=1000, layers=2, kv=64):
 
 
 def execute_specs(cuda, specs, n_src_slots, n_dst_slots, src_dtype=torch.float32,
-                  dst_dtype=torch.bfloat16, seed=3):
+                  dst_dtype=torch.bfloat16, seed=3, engine="sm"):
   """Runs the plan of `specs` on cuda:0 (source slot s = local shard s of one
   synchronizer, destination slot d = its own tensors) and checks that every
   destination slot holds exactly its box of every variable."""
@@ -51,7 +51,7 @@ def execute_specs(cuda, specs, n_src_slots, n_dst_slots, src_dtype=torch.float32
     for d in range(n_dst_slots):
       dest[(vi, d)] = torch.zeros(rp.local_shape(boxes[v.dst_box_of(d)]), dtype=dst_dtype,
                                   device=cuda)
-  fut = ws.push_weights_resharded(plan, {s: s for s in range(n_src_slots)}, dest)
+  fut = ws.push_weights_resharded(plan, {s: s for s in range(n_src_slots)}, dest, engine=engine)
   fut.Await()
   torch.cuda.synchronize()
   for vi, v in enumerate(specs):
@@ -66,9 +66,10 @@ def execute_specs(cuda, specs, n_src_slots, n_dst_slots, src_dtype=torch.float32
   return plan
 
 
-def run_reshard(cuda, n_src, n_dst, params, src_dtype=torch.float32, dst_dtype=torch.bfloat16):
+def run_reshard(cuda, n_src, n_dst, params, src_dtype=torch.float32, dst_dtype=torch.bfloat16,
+                engine="sm"):
   specs = workloads.weight_sync_specs(n_src, n_dst, params)
-  return execute_specs(cuda, specs, n_src, n_dst, src_dtype, dst_dtype)
+  return execute_specs(cuda, specs, n_src, n_dst, src_dtype, dst_dtype, engine=engine)
 
 
 def test_replicated_sources_and_destinations(cuda):
@@ -97,9 +98,42 @@ def test_replicated_sources_and_destinations(cuda):
       assert len(boxes) == len(set(boxes)), (vi, d, srcs)
 
 
+@pytest.mark.parametrize("engine", ["sm", "copy"])
 @pytest.mark.parametrize("n_src,n_dst", [(4, 4), (1, 1), (1, 2), (2, 4)])
-def test_llama_shaped_reshard_fp32_to_bf16(cuda, n_src, n_dst):
-  run_reshard(cuda, n_src, n_dst, small_llama())
+def test_llama_shaped_reshard_fp32_to_bf16(cuda, n_src, n_dst, engine):
+  run_reshard(cuda, n_src, n_dst, small_llama(), engine=engine)
+
+
+def test_copy_engine_program_relaunch_and_identity(cuda):
+  """Relaunching reuses the staging only after the previous launch's copies
+  left it; same-dtype chunks copy straight from the source; the result is
+  exact after every launch."""
+  from tpu_sync_b200 import ops
+  g = torch.Generator().manual_seed(11)
+  src = (torch.randn(512, 96, generator=g) * 0.02).to(cuda)
+  dst = torch.zeros(96, 512, dtype=torch.bfloat16, device=cuda)
+  # even source rows written transposed: 96 one-element rows at stride 512
+  chunks = [(src, dst, r * 96, r, 1, 1, 512, 96) for r in range(0, 512, 2)]
+  chunks += [(src, dst, 96, 1, 32, 192, 1024, 0)]  # count 0: nothing
+  prog = ops.ReshardCopyEngineProgram(chunks, torch.float32, torch.bfloat16, cuda, groups=5)
+  assert prog.groups >= 5 and prog.staging_bytes == 256 * 96 * 2
+  want = torch.zeros(96, 512, dtype=torch.bfloat16)
+  want[:, 0::2] = src[0::2].cpu().t().to(torch.bfloat16)
+  for _ in range(3):
+    dst.zero_()
+    prog.launch()
+    torch.cuda.synchronize()
+    assert torch.equal(dst.cpu().view(torch.int16), want.view(torch.int16))
+  b_src = torch.randint(0, 256, (4096,), dtype=torch.uint8, device=cuda)
+  b_dst = torch.zeros(8192, dtype=torch.uint8, device=cuda)
+  ident = ops.ReshardCopyEngineProgram([(b_src, b_dst, 7, 100, 33, 64, 1000, 20)],
+                                       torch.uint8, torch.uint8, cuda)
+  assert ident.staging_bytes == 0
+  ident.launch()
+  torch.cuda.synchronize()
+  want = np.zeros(8192, np.uint8)
+  ors.apply_byte_entries(b_src.cpu().numpy(), want, [(7, 100, 33, 64, 1000, 20)])
+  np.testing.assert_array_equal(b_dst.cpu().numpy(), want)
 
 
 def test_reshard_identity_dtype_odd_shapes(cuda):

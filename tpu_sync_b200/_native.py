@@ -330,6 +330,11 @@ _SIGS = {
     "ts_xfer_poll_reads": (ctypes.c_int, [_V, ctypes.c_int, ctypes.c_char_p, ctypes.c_int64,
                                           c_i64_p, ctypes.c_int64, c_i64_p, c_i64_p]),
     "ts_xfer_reader_pending": (ctypes.c_int, [_V, c_i64_p]),
+    "ts_reshard_ce_create": (ctypes.c_int, [ctypes.c_int, _V, ctypes.c_int64, ctypes.c_int,
+                                            ctypes.c_int, ctypes.c_int, ctypes.POINTER(_V)]),
+    "ts_reshard_ce_launch": (ctypes.c_int, [_V, _V]),
+    "ts_reshard_ce_info": (ctypes.c_int, [_V, c_i64_p, c_u64_p, c_i64_p]),
+    "ts_reshard_ce_destroy": (ctypes.c_int, [_V]),
     "ts_kv_metadata_required_bytes": (ctypes.c_uint64, [ctypes.c_int]),
     "ts_kv_metadata_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int, ctypes.c_char_p,
                                            ctypes.POINTER(_V), ctypes.POINTER(ctypes.c_int)]),

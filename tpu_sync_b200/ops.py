@@ -183,6 +183,48 @@ def _pages(storages, geom: dict, given: Optional[int], side: str) -> int:
   return min(sizes) // page
 
 
+class ReshardCopyEngineProgram:
+  """The same chunks as ReshardProgram, pushed by the copy engines: the cast
+  to the destination dtype goes to a local staging buffer and each staged
+  chunk moves with one cudaMemcpy2DAsync, `groups` groups pipelining the
+  cast against the copies (ts_reshard_ce_*)."""
+
+  def __init__(self, chunks, src_dtype: torch.dtype, dst_dtype: torch.dtype,
+               device: torch.device, groups: int = 16):
+    self.device = torch.device(device)
+    chunks = list(chunks)
+    arr = (_native.ReshardChunk * max(len(chunks), 1))()
+    for i, (sp, dp, so, do, size, ss, ds, cnt) in enumerate(chunks):
+      arr[i].src_ptr = sp.data_ptr() if hasattr(sp, "data_ptr") else int(sp)
+      arr[i].dst_ptr = dp.data_ptr() if hasattr(dp, "data_ptr") else int(dp)
+      arr[i].src_off, arr[i].dst_off, arr[i].size = int(so), int(do), int(size)
+      arr[i].src_stride, arr[i].dst_stride, arr[i].count = int(ss), int(ds), int(cnt)
+    h = ctypes.c_void_p()
+    _native.check(_native.lib().ts_reshard_ce_create(
+        self.device.index, arr, len(chunks), _TORCH_TO_TS[src_dtype], _TORCH_TO_TS[dst_dtype],
+        int(groups), ctypes.byref(h)), "reshard (copy engines): ")
+    self._h = h
+    g, b, c = ctypes.c_int64(), ctypes.c_uint64(), ctypes.c_int64()
+    _native.check(_native.lib().ts_reshard_ce_info(h, ctypes.byref(g), ctypes.byref(b),
+                                                   ctypes.byref(c)))
+    self.groups, self.staging_bytes, self.copies = g.value, b.value, c.value
+
+  def launch(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+    _native.check(_native.lib().ts_reshard_ce_launch(self._h, _stream(stream, self.device)),
+                  "reshard (copy engines): ")
+
+  def close(self) -> None:
+    if getattr(self, "_h", None):
+      _native.lib().ts_reshard_ce_destroy(self._h)
+      self._h = None
+
+  def __del__(self):
+    try:
+      self.close()
+    except Exception:
+      pass
+
+
 def kv_relayout(src_storages: Sequence, dst_storages: Sequence, src_geom: dict,
                 dst_geom: dict, src_table: torch.Tensor, dst_table: torch.Tensor,
                 seq_tokens: int, device=None,

@@ -237,8 +237,13 @@ class WeightSynchronizer:
   # -- resharded push -------------------------------------------------------
   def push_weights_resharded(self, plan: ReshardPlan, src_shards: Dict[int, int],
                              destinations: Dict[Tuple[int, int], torch.Tensor],
-                             stream: Optional[torch.cuda.Stream] = None) -> PushFuture:
+                             stream: Optional[torch.cuda.Stream] = None,
+                             engine: str = "sm") -> PushFuture:
     """Executes every chunk of `plan` whose source shard lives here.
+
+    engine: "sm" — one kernel per source GPU casts and stores into the
+    destinations; "copy" — the kernel casts into local staging and the copy
+    engines move the chunks (ops.ReshardCopyEngineProgram).
 
     src_shards: local shard index -> plan source shard index.
     destinations: (var index, plan dst shard) -> destination tensor (local or
@@ -267,7 +272,12 @@ class WeightSynchronizer:
         continue
       s = stream if stream is not None else torch.cuda.current_stream(device)
       for (sd, dd), chunk_list in by_kind.items():
-        prog = ops.ReshardProgram(chunk_list, sd, dd, device)
+        if engine == "copy":
+          prog = ops.ReshardCopyEngineProgram(chunk_list, sd, dd, device)
+        elif engine == "sm":
+          prog = ops.ReshardProgram(chunk_list, sd, dd, device)
+        else:
+          raise ValueError(f"engine must be 'sm' or 'copy', got {engine!r}")
         prog.launch(s)
         programs.append(prog)
       ev = torch.cuda.Event()
