@@ -126,14 +126,20 @@ def test_copy_engine_program_relaunch_and_identity(cuda):
     assert torch.equal(dst.cpu().view(torch.int16), want.view(torch.int16))
   b_src = torch.randint(0, 256, (4096,), dtype=torch.uint8, device=cuda)
   b_dst = torch.zeros(8192, dtype=torch.uint8, device=cuda)
-  ident = ops.ReshardCopyEngineProgram([(b_src, b_dst, 7, 100, 33, 64, 1000, 20)],
+  ident = ops.ReshardCopyEngineProgram([(b_src, b_dst, 7, 100, 33, 64, 200, 20)],
                                        torch.uint8, torch.uint8, cuda)
   assert ident.staging_bytes == 0
   ident.launch()
   torch.cuda.synchronize()
   want = np.zeros(8192, np.uint8)
-  ors.apply_byte_entries(b_src.cpu().numpy(), want, [(7, 100, 33, 64, 1000, 20)])
+  ors.apply_byte_entries(b_src.cpu().numpy(), want, [(7, 100, 33, 64, 200, 20)])
   np.testing.assert_array_equal(b_dst.cpu().numpy(), want)
+  # a chunk that would end past its destination is refused before any launch
+  with pytest.raises(ValueError, match="chunk 0 ends past its destination"):
+    ops.ReshardCopyEngineProgram([(b_src, b_dst, 7, 100, 33, 64, 1000, 20)],
+                                 torch.uint8, torch.uint8, cuda)
+  with pytest.raises(ValueError, match="chunk 0 ends past its source"):
+    ops.ReshardProgram([(b_src, b_dst, 4000, 0, 200, 0, 0, 1)], torch.uint8, torch.uint8, cuda)
 
 
 def test_reshard_identity_dtype_odd_shapes(cuda):

@@ -129,6 +129,34 @@ _TORCH_TO_TS = {torch.uint8: _native.DTYPE_U8, torch.bfloat16: _native.DTYPE_BF1
                 torch.float32: _native.DTYPE_F32, torch.float16: _native.DTYPE_F16}
 
 
+def _extent_bytes(x) -> Optional[int]:
+  """Bytes a chunk endpoint holds when it knows its size (a tensor or a
+  PeerBuffer), else None (a raw address)."""
+  if isinstance(x, torch.Tensor):
+    return x.numel() * x.element_size()
+  if isinstance(x, (int, np.integer)):
+    return None
+  if hasattr(x, "nbytes"):
+    return int(x.nbytes)
+  return None
+
+
+def _check_chunks(chunks, src_es: int, dst_es: int) -> None:
+  """Every chunk stays inside its source and destination where their sizes
+  are known: (offset + (count - 1) * stride + size) elements."""
+  for i, (sp, dp, so, do, size, ss, ds, cnt) in enumerate(chunks):
+    if size <= 0 or cnt <= 0:
+      continue
+    for name, obj, off, stride, es in (("source", sp, so, ss, src_es),
+                                       ("destination", dp, do, ds, dst_es)):
+      n = _extent_bytes(obj)
+      if n is None:
+        continue
+      end = (off + (cnt - 1) * stride + size) * es if cnt > 1 else (off + size * cnt) * es
+      if off < 0 or end > n:
+        raise ValueError(f"chunk {i} ends past its {name}: byte {end} of {n}")
+
+
 class ReshardProgram:
   """A list of strided chunks compiled for one launch of ts_reshard_copy.
 
@@ -143,6 +171,8 @@ class ReshardProgram:
     self.src_dtype = _TORCH_TO_TS[src_dtype]
     self.dst_dtype = _TORCH_TO_TS[dst_dtype]
     chunks = list(chunks)
+    _check_chunks(chunks, torch.empty((), dtype=src_dtype).element_size(),
+                  torch.empty((), dtype=dst_dtype).element_size())
     n = len(chunks)
     arr = (_native.ReshardChunk * max(n, 1))()
     for i, (sp, dp, so, do, size, ss, ds, cnt) in enumerate(chunks):
@@ -193,6 +223,8 @@ class ReshardCopyEngineProgram:
                device: torch.device, groups: int = 16):
     self.device = torch.device(device)
     chunks = list(chunks)
+    _check_chunks(chunks, torch.empty((), dtype=src_dtype).element_size(),
+                  torch.empty((), dtype=dst_dtype).element_size())
     arr = (_native.ReshardChunk * max(len(chunks), 1))()
     for i, (sp, dp, so, do, size, ss, ds, cnt) in enumerate(chunks):
       arr[i].src_ptr = sp.data_ptr() if hasattr(sp, "data_ptr") else int(sp)
