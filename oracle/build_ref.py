@@ -9,7 +9,7 @@
   and kv_cache_metadata_shm.cc.
 
 g++ compiles them where they lie in the reference checkout (REFERENCE_ROOT,
-default /root/reference); oracle/shim stands in for the few absl types they
+else BASELINE.json's reference_path); oracle/shim stands in for the few absl types they
 use (flat_hash_map, Status, StatusOr, StrCat, Span, string_view, LOG) and for the two proto
 message classes pool_layout.h names.  Nothing is copied from the reference;
 the binaries go to oracle/_ref/ only.  Test infrastructure: tests/ use them to
@@ -29,7 +29,15 @@ OUT = HERE / "_ref" / "lru_ref"
 
 
 def reference_root() -> Path:
-  return Path(os.environ.get("REFERENCE_ROOT", "/root/reference"))
+  """The reference checkout: $REFERENCE_ROOT, else BASELINE.json's reference_path."""
+  env = os.environ.get("REFERENCE_ROOT")
+  if env:
+    return Path(env)
+  try:
+    import json
+    return Path(json.loads((HERE.parent / "BASELINE.json").read_text())["reference_path"])
+  except (OSError, KeyError, ValueError):
+    return HERE / "_no_reference_checkout"
 
 
 def build(force: bool = False) -> Path | None:

@@ -1,7 +1,7 @@
 """Generates the golden reshard-plan fixtures by running the REFERENCE planner.
 
 Run in a container that has the reference checkout (read-only) at
-REFERENCE_ROOT (default /root/reference):
+REFERENCE_ROOT (else BASELINE.json's reference_path):
 
     python tests/golden/make_golden.py
 
@@ -21,7 +21,10 @@ import sys
 import types
 from pathlib import Path
 
-REF = os.environ.get("REFERENCE_ROOT", "/root/reference")
+sys.path.insert(0, str(Path(__file__).resolve().parents[2]))
+from oracle.build_ref import reference_root  # noqa: E402
+
+REF = str(reference_root())
 OUT = Path(__file__).resolve().parent / "reshard_plans.json"
 sys.path.insert(0, str(Path(__file__).resolve().parents[2]))
 

@@ -1,7 +1,7 @@
 """Generates tests/golden/kv_metadata.json: KV metadata table fixtures.
 
 Run in a container that has the reference checkout (read-only) at
-REFERENCE_ROOT (default /root/reference):
+REFERENCE_ROOT (else BASELINE.json's reference_path):
 
     python tests/golden/make_kv_metadata_golden.py
 

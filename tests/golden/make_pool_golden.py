@@ -1,7 +1,7 @@
 """Generates tests/golden/pool_layout.json: pool-geometry fixtures.
 
 Run in a container that has the reference checkout (read-only) at
-REFERENCE_ROOT (default /root/reference):
+REFERENCE_ROOT (else BASELINE.json's reference_path):
 
     python tests/golden/make_pool_golden.py
 
