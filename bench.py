@@ -500,7 +500,7 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
     desc = export_destinations({0: flat})
   descs = [None] * world
   dist.all_gather_object(descs, desc)
-  per_push_ms, prog = 0.0, None
+  per_push_ms, prog, prog_ce, ce_error = 0.0, None, None, ""
   if is_src:
     dsts = {d: import_destinations(descs[half + d], kernel_device=device.index)[0]
             for d in range(half)}
@@ -511,15 +511,26 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
       for (so, do, size, ss, ds, cnt) in cs:
         chunks.append((sp, dp, so, do, size, ss, ds, cnt))
     prog = ops.ReshardProgram(chunks, torch.float32, torch.bfloat16, device)
-    prog_ce = ops.ReshardCopyEngineProgram(chunks, torch.float32, torch.bfloat16, device)
     for _ in range(warmup):
       prog.launch()
-      prog_ce.launch()
+    # the copy-engine leg is a comparison: a launch error there is reported
+    # in the line instead of ending the run
+    try:
+      prog_ce = ops.ReshardCopyEngineProgram(chunks, torch.float32, torch.bfloat16, device)
+      for _ in range(warmup):
+        prog_ce.launch()
+    except RuntimeError as e:
+      ce_error = str(e).splitlines()[0][:200]
+      prog_ce = None
     torch.cuda.synchronize(device)
+  ok = torch.tensor([0 if ce_error else 1], dtype=torch.int32, device=device)
+  dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+  if not int(ok.item()) and not ce_error:
+    ce_error = "failed on another trainer rank"
   dist.barrier()
   ce_ms = 0.0
   if is_src:
-    for which in ("sm", "copy"):
+    for which in (("sm", "copy") if not ce_error else ("sm",)):
       p_ = prog if which == "sm" else prog_ce
       e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
       e0.record()
@@ -540,8 +551,9 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
   recv_bytes = max(2 * plan.elements_to(d) for d in range(half))
   total_params = sum(math.prod(v.shape) for v in specs)
   del prog
-  if is_src:
+  if prog_ce is not None:
     prog_ce.close()
+  if is_src:
     dsts = None
     close_imports(device.index)
   dist.barrier()
@@ -555,7 +567,8 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
                                     "samplers' memory over NVLink", "seconds": round(sm_s, 5)},
                       "copy": {"how": "the kernel casts into local staging, the copy engines "
                                       "move each chunk (cudaMemcpy2DAsync), 16 pipelined groups",
-                               "seconds": round(ce_s, 5)}},
+                               "seconds": round(ce_s, 5) if not ce_error else None,
+                               **({"error": ce_error} if ce_error else {})}},
           "chunks_per_src": len(plan.for_source(0))}
 
 
@@ -578,7 +591,7 @@ def run_pull(torch, dist, rank, world, device, steps, warmup):
   eps = [None] * world
   dist.all_gather_object(eps, ep)
   rng = np.random.default_rng(60)
-  ms = []
+  ms, host_ms = [], []
   for it in range(warmup + steps):
     src_ids = rng.choice(n_blocks, B, replace=False).tolist()
     dst_ids = rng.choice(n_blocks, B, replace=False).tolist()
@@ -593,11 +606,14 @@ def run_pull(torch, dist, rank, world, device, steps, warmup):
     if not is_src:
       s = torch.cuda.current_stream(device)
       e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-      # a fixed ~1 ms of GPU sleep ahead of e0 keeps the host's start_read
-      # (checks, pair upload, launch) out of the timed window
-      torch.cuda._sleep(2_000_000)
+      # ~5 ms of GPU sleep ahead of e0 keeps the host's start_read (checks,
+      # pair upload, launch; its wall time is reported as host_ms) out of the
+      # timed window
+      torch.cuda._sleep(10_000_000)
       e0.record(s)
+      h0 = time.perf_counter()
       mgr.start_read(f"pull-{it}", 1000 + it, eps[rank - half], src_ids, dst_ids)
+      h1 = time.perf_counter()
       e1.record(s)
       t0 = time.time()
       while f"pull-{it}" not in mgr.poll_stats()[1]:
@@ -606,6 +622,7 @@ def run_pull(torch, dist, rank, world, device, steps, warmup):
       torch.cuda.synchronize(device)
       if it >= warmup:
         ms.append(e0.elapsed_time(e1))
+        host_ms.append((h1 - h0) * 1e3)
     else:
       t0 = time.time()
       while f"pull-{it}" not in mgr.poll_stats()[0]:
@@ -613,15 +630,18 @@ def run_pull(torch, dist, rank, world, device, steps, warmup):
           raise RuntimeError("pull was not consumed")
         time.sleep(0.001)
     dist.barrier()
-  t = torch.tensor([statistics.median(ms) if ms else 0.0], dtype=torch.float64, device=device)
+  t = torch.tensor([statistics.median(ms) if ms else 0.0,
+                    statistics.median(host_ms) if host_ms else 0.0],
+                   dtype=torch.float64, device=device)
   dist.all_reduce(t, op=dist.ReduceOp.MAX)
-  step_ms = float(t.item())
+  step_ms, start_read_ms = float(t[0].item()), float(t[1].item())
   moved = B * g.block_bytes
   mgr.close()
   del full, storages
   return {"config": f"{B} C1 blocks (2 MiB each) per pair, {half} pairs (GPU i -> i+{half}), "
                     "register_read / start_read / poll_stats over CUDA IPC",
           "bytes_per_pair": moved, "ms": round(step_ms, 3),
+          "start_read_host_ms": round(start_read_ms, 3),
           "nvlink_gbs_per_pair": round(moved / (step_ms * 1e-3) / 1e9, 1) if step_ms else None,
           "frac_of_nvlink_770": round(moved / (step_ms * 1e-3) / 1e9 / 770.0, 3)
           if step_ms else None}
