@@ -180,7 +180,7 @@ typedef struct ts_pool_reshard_request {  /* PlanRequest (data-plane fields) */
   const ts_pool_spec* dst_pools;          /* the destination unit's manifest */
   int64_t n_dst_pools;
   const int32_t* transfer_ranks;          /* per unit (NULL: unit index) */
-  const int32_t* transfer_parallelism;    /* per unit (NULL: 1) */
+  const int32_t* transfer_parallelism;    /* per unit (NULL: the number of units) */
   int32_t parallelism;                    /* 0: the units' admitted value */
   int32_t pad_;
   const char* const* tags;                /* transfer_pool_tags */

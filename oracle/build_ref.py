@@ -1,20 +1,23 @@
 """Compiles reference sources into test oracle binaries.
 
-    python oracle/build_ref.py     # -> oracle/_ref/{lru_ref, pool_ref, meta_ref}
+    python oracle/build_ref.py     # -> oracle/_ref/{lru_ref, pool_ref, meta_ref, plan_ref}
 
 * lru_ref: oracle/ref_lru_driver.cc over the header-only LRUCache
   (tpu_sync/kv_cache/lru_cache.h);
 * pool_ref: oracle/ref_pool_driver.cc linked with tpu_sync/kv_cache/pool_layout.cc;
 * meta_ref: oracle/ref_meta_driver.cc linked with tpu_sync/kv_cache/kv_cache_metadata.cc
-  and kv_cache_metadata_shm.cc.
+  and kv_cache_metadata_shm.cc;
+* plan_ref: oracle/ref_pool_reshard_driver.cc linked with tpu_sync/kv_cache/pool_layout.cc
+  and reshard/{declaration_types, work_unit_directory, request_block_registry,
+  pool_reshard_planner}.cc.
 
 g++ compiles them where they lie in the reference checkout (REFERENCE_ROOT,
 else BASELINE.json's reference_path); oracle/shim stands in for the few absl types they
-use (flat_hash_map, Status, StatusOr, StrCat, Span, string_view, LOG) and for the two proto
-message classes pool_layout.h names.  Nothing is copied from the reference;
+use (flat_hash_map, Status, StatusOr, StrCat, StrJoin, Span, string_view, LOG, Mutex,
+HashOf, thread annotations) and for the proto message classes those sources name.  Nothing is copied from the reference;
 the binaries go to oracle/_ref/ only.  Test infrastructure: tests/ use them to
-pin the product's LRU and pool geometry (and tests/golden/make_pool_golden.py
-records pool_ref's answers as fixtures).
+pin the product's LRU, pool geometry, metadata table and pool reshard planner
+(tests/golden/make_*_golden.py record the binaries' answers as fixtures).
 """
 
 from __future__ import annotations
@@ -95,7 +98,30 @@ def build_meta(force: bool = False) -> Path | None:
   return META_OUT
 
 
+PLAN_OUT = HERE / "_ref" / "plan_ref"
+
+
+def build_plan(force: bool = False) -> Path | None:
+  """Builds plan_ref if the reference checkout is present; returns its path."""
+  ref = reference_root()
+  kv = ref / "tpu_sync" / "kv_cache"
+  ccs = [kv / "pool_layout.cc"] + [kv / "reshard" / f"{n}.cc" for n in (
+      "declaration_types", "work_unit_directory", "request_block_registry",
+      "pool_reshard_planner")]
+  src = HERE / "ref_pool_reshard_driver.cc"
+  if PLAN_OUT.exists() and not force and PLAN_OUT.stat().st_mtime >= src.stat().st_mtime:
+    return PLAN_OUT
+  if not all(c.exists() for c in ccs):
+    return PLAN_OUT if PLAN_OUT.exists() else None
+  PLAN_OUT.parent.mkdir(parents=True, exist_ok=True)
+  cxx = shutil.which("g++") or "c++"
+  subprocess.run([cxx, "-std=c++17", "-O1", f"-I{HERE / 'shim'}", f"-I{ref}", str(src),
+                  *map(str, ccs), "-o", str(PLAN_OUT)], check=True)
+  return PLAN_OUT
+
+
 if __name__ == "__main__":
   print(build(force=True))
   print(build_pool(force=True))
   print(build_meta(force=True))
+  print(build_plan(force=True))

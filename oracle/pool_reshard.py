@@ -10,10 +10,13 @@ block, tpu_sync/kv_cache/kv_cache_manager_base.cc:2400-2510; every pool of
 the entry's group gets the bytes).
 
 Parity pinning: the known answers of the reference's planner tests
-(tpu_sync/kv_cache/reshard/reshard_service_test.cc:288-487) are checked in
-tests/test_cpu_pool_reshard.py.  The planner itself is not compiled here: it
-needs the request registry and several generated proto messages beyond the
-pool geometry (which is pinned separately, see oracle/pool_layout.py).
+(tpu_sync/kv_cache/reshard/reshard_service_test.cc:288-487) and 300 seeded
+requests answered by the reference's own planning flow -- its
+pool_layout.cc, work_unit_directory.cc, request_block_registry.cc and
+pool_reshard_planner.cc compiled here (oracle/build_ref.py -> plan_ref),
+recorded in tests/golden/pool_reshard_plans.json -- are checked in
+tests/test_cpu_pool_reshard.py.  The registration checks the reference makes
+before planning (unit and byte-span registration) come first here too.
 
 Pools are dicts as in oracle/pool_layout.py; a declaration is
 (unit, {"tag", "block_ids", "spans": [span dicts], "declared_bytes",
@@ -44,21 +47,107 @@ def _sig(p):
                  r["num_units"], r["units_per_stride"]) for r in p["regions"]))
 
 
+MAX_SPAN_COUNT = 1 << 20
+
+
+def check_unit_registrations(src_pools, dst_pools, ranks, unit_parallelism):
+  """WorkUnitDirectory::Validate (kv_cache/reshard/work_unit_directory.cc:66-86)
+  for every source unit in order, then the destination.  A unit without an
+  explicit transfer_parallelism declares the number of source units, without
+  a rank its index."""
+  nu = len(src_pools)
+  for u in range(nu):
+    if not src_pools[u]:
+      raise PlanError("pool_manifest must not be empty")
+    par = unit_parallelism[u] if unit_parallelism else nu
+    rank = ranks[u] if ranks else u
+    if par <= 0:
+      raise PlanError("transfer_parallelism must be positive")
+    if rank < 0:
+      raise PlanError("transfer_rank must be non-negative")
+    if rank >= par:
+      raise PlanError("transfer_rank must be less than transfer_parallelism")
+  if not dst_pools:
+    raise PlanError("pool_manifest must not be empty")
+
+
+def check_span_registrations(src_pools, decls, name):
+  """RequestBlockRegistry::Register (kv_cache/reshard/request_block_registry.cc:142-245)
+  for every source unit in order: its declarations, in the order given,
+  against the live bytes of its manifest's pools per tag."""
+  for u in range(len(src_pools)):
+    mine = [d for uu, d in decls if uu == u]
+    if not mine:
+      continue
+    live_by_tag = {}
+    for p in src_pools[u]:
+      try:
+        live = sum(x[2] for x in opl.live_segments(p))
+      except opl.PoolError as e:
+        raise PlanError(e.message) from None
+      if live_by_tag.setdefault(p["tag"], live) != live:
+        raise PlanError(f"pools tagged {p['tag']} disagree on live bytes for {name(u)}; "
+                        "byte-span registration requires one geometry per tag")
+    seen = set()
+    for d in mine:
+      tag = d["tag"]
+      if not tag:
+        raise PlanError("pool span registration tag must not be empty")
+      if tag in seen:
+        raise PlanError(f"duplicate pool span registration tag: {tag}")
+      seen.add(tag)
+      if tag not in live_by_tag:
+        raise PlanError(f"pool span registration {tag} does not match any registered pool for "
+                        f"{name(u)}")
+      live = live_by_tag[tag]
+      ids = list(d["block_ids"])
+      if any(b < 0 for b in ids):
+        raise PlanError(f"pool span registration {tag} block_ids must be non-negative")
+      if len(set(ids)) != len(ids):
+        raise PlanError(f"pool span registration {tag} block_ids must not contain duplicates")
+      total = 0
+      for sp in d["spans"]:
+        if sp["size_bytes"] <= 0:
+          raise PlanError(f"byte span size_bytes must be positive ({tag})")
+        if sp["count"] <= 0:
+          raise PlanError(f"byte span count must be positive ({tag})")
+        if sp["count"] > MAX_SPAN_COUNT:
+          raise PlanError(f"byte span count {sp['count']} exceeds the expansion bound ({tag})")
+        if min(sp["src_offset_bytes"], sp["dst_offset_bytes"], sp["src_stride_bytes"],
+               sp["dst_stride_bytes"], sp["dst_block_index"]) < 0:
+          raise PlanError(f"byte span fields must be non-negative ({tag})")
+        o = sp["src_block_ordinal"]
+        if o < 0 or o >= len(ids):
+          raise PlanError(f"byte span ordinal {o} is outside the registration's {len(ids)} "
+                          f"block ids ({tag})")
+        end = sp["src_offset_bytes"] + (sp["count"] - 1) * sp["src_stride_bytes"] + sp["size_bytes"]
+        if end > live:
+          raise PlanError(f"byte span exceeds its source block live bytes ({tag}): end={end}, "
+                          f"live={live}")
+        total += sp["size_bytes"] * sp["count"]
+      if d["declared_bytes"] != total:
+        raise PlanError(f"pool span registration {tag} declared_bytes {d['declared_bytes']} "
+                        f"disagrees with the span sum {total}")
+
+
 def build_plan(src_pools, dst_pools, tags, dst_ids, decls, dst_block_counts=None,
-               dst_skip_bytes=None, parallelism=None, ranks=None, unit_parallelism=None):
+               dst_skip_bytes=None, parallelism=None, ranks=None, unit_parallelism=None,
+               unit_names=None):
   """Returns {"schedules": {unit: [entry tuples]}, "groups": [...], "src_units": [...]}.
 
   entry tuple = (src_block, dst_block, src_off, dst_off, size, group).
-  Raises PlanError(message) with the planner's messages.
+  Raises PlanError(message) with the reference's messages: the registration
+  checks first (check_unit_registrations, check_span_registrations), then
+  the planner's.
   """
   nu = len(src_pools)
-  name = lambda u: f"src unit {u}"
+  name = (lambda u: unit_names[u]) if unit_names else (lambda u: f"src unit {u}")
+  check_unit_registrations(src_pools, dst_pools, ranks, unit_parallelism)
+  check_span_registrations(src_pools, decls, name)
   if not dst_ids:
     raise PlanError("dst_device_block_ids must not be empty")
   if any(b < 0 for b in dst_ids):
     raise PlanError("dst_device_block_ids must be non-negative")
-  if not dst_pools:
-    raise PlanError("Destination pool manifest must not be empty")
   for u in range(nu):
     if not src_pools[u]:
       raise PlanError(f"Missing explicit pool manifest for {name(u)}")
@@ -104,7 +193,7 @@ def build_plan(src_pools, dst_pools, tags, dst_ids, decls, dst_block_counts=None
   for t in tags:
     if t not in avail:
       raise PlanError(f"transfer_pool_tags do not match any registered pool: [{_q(t)}]")
-  par = {(unit_parallelism[u] if unit_parallelism else 1) for u in range(nu)}
+  par = {(unit_parallelism[u] if unit_parallelism else nu) for u in range(nu)}
   rank_of = {(ranks[u] if ranks else u): u for u in range(nu)}
   if len(par) != 1 or min(par) <= 0:
     raise PlanError("All source ranks must declare one consistent positive transfer_parallelism")

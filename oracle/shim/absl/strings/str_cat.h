@@ -1,5 +1,5 @@
-// Minimal stand-in for absl::StrCat used ONLY to compile the reference's
-// pool_layout.cc as a test oracle (oracle/build_ref.py): decimal integers,
+// Minimal stand-in for absl::StrCat / StrAppend used ONLY to compile
+// reference sources as test oracles (oracle/build_ref.py): decimal integers,
 // strings and C strings concatenated.
 #pragma once
 #include <sstream>
@@ -12,6 +12,11 @@ std::string StrCat(const Args&... args) {
   std::ostringstream os;
   (os << ... << args);
   return os.str();
+}
+
+template <typename... Args>
+void StrAppend(std::string* out, const Args&... args) {
+  out->append(StrCat(args...));
 }
 
 }  // namespace absl

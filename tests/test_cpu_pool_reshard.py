@@ -4,13 +4,20 @@
   (tpu_sync/kv_cache/reshard/reshard_service_test.cc:288-487), for both the
   product planner (tpu_sync_b200.pool_reshard, C ABI) and the oracle
   (oracle/pool_reshard.py);
+* 300 seeded requests answered by the reference's own planning flow
+  (tests/golden/pool_reshard_plans.json, made by
+  tests/golden/make_pool_reshard_golden.py from the compiled reference):
+  product and oracle give the same plan, or the same error message at the
+  same step (unit registration, span registration, planning);
 * product vs oracle on seeded random requests -- valid ones (entries,
   groups, active units equal) and broken ones (same error message);
 * the C3 hand-off written as pool span declarations, applied by the oracle,
   equals the oracle's head-major -> token-major relayout.
 """
 
+import json
 import random
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -18,7 +25,7 @@ import pytest
 from oracle import pool_reshard as opr
 from oracle import reshard as ors
 from tpu_sync_b200 import workloads
-from tpu_sync_b200.pool_layout import PoolSpec, RegionSpec
+from tpu_sync_b200.pool_layout import PoolSpec, RegionSpec, coerce_pool_spec
 from tpu_sync_b200.pool_reshard import (PoolByteSpan, PoolSpanRegistration,
                                         build_pool_reshard_plan)
 
@@ -63,7 +70,8 @@ def both(src_pools, dst_pools, tags, dst_ids, decls, **kw):
                        dst_block_counts=kw.get("dst_block_counts"),
                        dst_skip_bytes=kw.get("dst_skip_bytes"),
                        parallelism=kw.get("parallelism"), ranks=kw.get("transfer_ranks"),
-                       unit_parallelism=kw.get("transfer_parallelism"))
+                       unit_parallelism=kw.get("transfer_parallelism"),
+                       unit_names=kw.get("unit_names"))
   except opr.PlanError as e:
     o = {"error": str(e)}
   return prod, o
@@ -243,3 +251,68 @@ def test_c3_handoff_as_pool_spans_equals_relayout():
     want = np.zeros_like(got[s]).reshape(-1, dbb)
     ors.relayout(src[s].reshape(-1, sbb), want, sg, dg, st, dt, T)
     np.testing.assert_array_equal(got[s], want.reshape(-1))
+
+
+GOLDEN = Path(__file__).resolve().parent / "golden" / "pool_reshard_plans.json"
+
+
+def _golden_case(case, keys):
+  pk, rk = keys
+  pool = lambda c: coerce_pool_spec(dict(zip(pk, c[:-1]),
+                                         regions=[dict(zip(rk, r)) for r in c[-1]]))
+  r = case["request"]
+  nu = r["n_units"]
+  src = [[pool(p) for p in r["src_pools"]] for _ in range(nu)]
+  dst = [pool(p) for p in r["dst_pools"]]
+  decls = [(u, PoolSpanRegistration(d["tag"], d["block_ids"], [PoolByteSpan(*sp) for sp in d["spans"]],
+                                    d["declared_bytes"], d["dst_space_version"]))
+           for u, d in r["decls"]]
+  # the reference's units are RaidenId("src", "<u>", "kv", 0): messages name them so
+  names = [f"RaidenId(job_name='src', job_replica_id='{u}', data_name='kv', data_replica_idx=0)"
+           for u in range(nu)]
+  kw = dict(dst_block_counts=r["dst_block_counts"], dst_skip_bytes=r["dst_skip_bytes"],
+            parallelism=r["parallelism"], transfer_ranks=r["transfer_ranks"],
+            transfer_parallelism=r["transfer_parallelism"], unit_names=names)
+  return src, dst, r["tags"], r["dst_ids"], decls, kw
+
+
+def test_reference_planning_flow_golden():
+  g = json.loads(GOLDEN.read_text())
+  keys = (g["pool_keys"], g["region_keys"])
+  stages = {}
+  for i, case in enumerate(g["cases"]):
+    ref = case["reference"]
+    src, dst, tags, ids, decls, kw = _golden_case(case, keys)
+    prod, orc = both(src, dst, tags, ids, decls, **kw)
+    assert prod == orc, (i, prod, orc)
+    if not ref["ok"]:
+      assert prod == {"error": ref["message"]}, (i, ref, prod)
+      stages[ref["stage"]] = stages.get(ref["stage"], 0) + 1
+      continue
+    assert "error" not in prod, (i, prod)
+    assert prod["src_units"] == ref["src_units"], i
+    assert list(prod["transfer_pool_indices"]) == ref["transfer_pool_indices"], i
+    assert {str(u): [list(e) for e in es] for u, es in prod["schedules"].items()} == \
+        ref["schedules"], i
+    assert [dict(g_, pool_indices=list(g_["pool_indices"]),
+                 dst_device_block_ids=list(g_["dst_device_block_ids"]),
+                 dst_expected_extent_bytes=list(g_["dst_expected_extent_bytes"]))
+            for g_ in prod["groups"]] == ref["groups"], i
+    p = build_pool_reshard_plan(src, dst, tags, ids, decls, **kw)
+    assert (p.expected_block_count, p.parallelism, p.expected_pushes_per_pool) == \
+        (ref["expected_block_count"], ref["parallelism"], ref["expected_pushes_per_pool"]), i
+  # every step of the reference's flow rejects some requests
+  assert set(stages) == {"register_unit", "register_spans", "plan"}, stages
+  assert sum(c["reference"]["ok"] for c in g["cases"]) > 150
+
+
+def test_default_parallelism_is_the_unit_count():
+  """Units without explicit transfer_parallelism / ranks register as ranks
+  0..n-1 of n (a registration the reference accepts)."""
+  p = build_pool_reshard_plan([P1024, P1024], P1024, ["fa"], [7, 9],
+                              [(0, reg([3], [(0, 0, 0, 0, 1024)])),
+                               (1, reg([5], [(0, 0, 1, 0, 512)]))])
+  assert p.parallelism == 2 and p.pool_groups[0].expected_pushes == 2
+  with pytest.raises(ValueError, match="transfer_rank must be less than transfer_parallelism"):
+    build_pool_reshard_plan([P1024, P1024], P1024, ["fa"], [7, 9],
+                            [(0, reg([3], [(0, 0, 0, 0, 1024)]))], transfer_parallelism=[1, 1])

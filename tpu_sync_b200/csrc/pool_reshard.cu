@@ -9,7 +9,12 @@
 // destination block (:624-719), emission of (src block, dst block, src
 // offset, dst offset, size) entries through TranslateLiveCopy in
 // (dst block index, dst offset) order (:721-781) and the expected push
-// counts.  The registry claim, the units' network endpoints and the layout
+// counts.  Before planning it makes the checks the reference makes when the
+// units and their byte-span declarations are registered
+// (WorkUnitDirectory::Validate, kv_cache/reshard/work_unit_directory.cc:66-86;
+// RequestBlockRegistry::Register, kv_cache/reshard/request_block_registry.cc:142-245),
+// so a request fails with the message the reference gives at whichever step
+// rejects it.  The registry claim, the units' network endpoints and the layout
 // fingerprints are control plane and have no counterpart here; a source unit
 // is named by its index (or a caller-given name) in messages.
 //
@@ -139,6 +144,118 @@ bool same_segments(const std::vector<ts_live_segment>& a, const std::vector<ts_l
   return true;
 }
 
+std::string S128(__int128 v) {
+  if (v >= INT64_MIN && v <= INT64_MAX) return S(int64_t(v));
+  const bool neg = v < 0;
+  unsigned __int128 m = neg ? (unsigned __int128)(-(v + 1)) + 1 : (unsigned __int128)v;
+  std::string d;
+  while (m) {
+    d.insert(d.begin(), char('0' + int(m % 10)));
+    m /= 10;
+  }
+  return neg ? "-" + d : d;
+}
+
+// Unit registration (WorkUnitDirectory::Validate,
+// kv_cache/reshard/work_unit_directory.cc:66-86): every source unit in
+// order, then the destination.  A unit without an explicit
+// transfer_parallelism declares the number of source units, without a rank
+// its index.
+int validate_unit_registrations(const ts_pool_reshard_request* rq, int64_t nu) {
+  for (int64_t u = 0; u < nu; ++u) {
+    if (rq->n_src_pools[u] <= 0)
+      return set_error(TS_INVALID_ARGUMENT, "pool_manifest must not be empty");
+    const int64_t par = rq->transfer_parallelism ? rq->transfer_parallelism[u] : nu;
+    const int64_t rank = rq->transfer_ranks ? rq->transfer_ranks[u] : u;
+    if (par <= 0) return set_error(TS_INVALID_ARGUMENT, "transfer_parallelism must be positive");
+    if (rank < 0) return set_error(TS_INVALID_ARGUMENT, "transfer_rank must be non-negative");
+    if (rank >= par)
+      return set_error(TS_INVALID_ARGUMENT, "transfer_rank must be less than transfer_parallelism");
+  }
+  if (rq->n_dst_pools <= 0) return set_error(TS_INVALID_ARGUMENT, "pool_manifest must not be empty");
+  return TS_OK;
+}
+
+// Byte-span registration (RequestBlockRegistry::Register,
+// kv_cache/reshard/request_block_registry.cc:142-245): per source unit, in
+// unit order, its declarations in the order given, against the live bytes of
+// its manifest's pools per tag.  Arithmetic is widened so no overflow can
+// let a span through.
+template <typename UnitName>
+int validate_span_registrations(const ts_pool_reshard_request* rq,
+                                const std::vector<std::vector<pool::Pool>>& src,
+                                const UnitName& unit_name) {
+  constexpr int64_t kMaxSpanCount = int64_t{1} << 20;
+  for (int64_t u = 0; u < int64_t(src.size()); ++u) {
+    std::vector<const ts_span_decl*> mine;
+    for (int64_t d = 0; d < rq->n_decls; ++d)
+      if (rq->decls[d].src_unit == u) mine.push_back(&rq->decls[d]);
+    if (mine.empty()) continue;
+    std::map<std::string, int64_t> live_by_tag;
+    for (const pool::Pool& p : src[size_t(u)]) {
+      std::vector<ts_live_segment> seg;
+      const int rc = pool::live_segments(p, &seg);
+      if (rc != TS_OK) return rc;
+      int64_t live = 0;
+      for (const ts_live_segment& g : seg) live += g.size;
+      auto [it, inserted] = live_by_tag.emplace(p.tag, live);
+      if (!inserted && it->second != live)
+        return set_error(TS_INVALID_ARGUMENT, "pools tagged " + p.tag + " disagree on live bytes for " +
+                                                  unit_name(u) +
+                                                  "; byte-span registration requires one geometry per tag");
+    }
+    std::set<std::string> seen;
+    for (const ts_span_decl* sd : mine) {
+      const std::string tag = sd->tag ? sd->tag : "";
+      if (tag.empty()) return set_error(TS_INVALID_ARGUMENT, "pool span registration tag must not be empty");
+      if (!seen.insert(tag).second)
+        return set_error(TS_INVALID_ARGUMENT, "duplicate pool span registration tag: " + tag);
+      auto live_it = live_by_tag.find(tag);
+      if (live_it == live_by_tag.end())
+        return set_error(TS_INVALID_ARGUMENT, "pool span registration " + tag +
+                                                  " does not match any registered pool for " + unit_name(u));
+      const int64_t live = live_it->second;
+      const int64_t n_ids = sd->n_block_ids > 0 ? sd->n_block_ids : 0;
+      for (int64_t i = 0; i < n_ids; ++i)
+        if (sd->block_ids[i] < 0)
+          return set_error(TS_INVALID_ARGUMENT, "pool span registration " + tag +
+                                                    " block_ids must be non-negative");
+      if (int64_t(std::set<int64_t>(sd->block_ids, sd->block_ids + n_ids).size()) != n_ids)
+        return set_error(TS_INVALID_ARGUMENT, "pool span registration " + tag +
+                                                  " block_ids must not contain duplicates");
+      __int128 span_bytes = 0;
+      for (int64_t k = 0; k < (sd->n_spans > 0 ? sd->n_spans : 0); ++k) {
+        const ts_byte_span& sp = sd->spans[k];
+        if (sp.size_bytes <= 0)
+          return set_error(TS_INVALID_ARGUMENT, "byte span size_bytes must be positive (" + tag + ")");
+        if (sp.count <= 0)
+          return set_error(TS_INVALID_ARGUMENT, "byte span count must be positive (" + tag + ")");
+        if (sp.count > kMaxSpanCount)
+          return set_error(TS_INVALID_ARGUMENT, "byte span count " + S(sp.count) +
+                                                    " exceeds the expansion bound (" + tag + ")");
+        if (sp.src_offset_bytes < 0 || sp.dst_offset_bytes < 0 || sp.src_stride_bytes < 0 ||
+            sp.dst_stride_bytes < 0 || sp.dst_block_index < 0)
+          return set_error(TS_INVALID_ARGUMENT, "byte span fields must be non-negative (" + tag + ")");
+        if (sp.src_block_ordinal < 0 || sp.src_block_ordinal >= n_ids)
+          return set_error(TS_INVALID_ARGUMENT, "byte span ordinal " + S(sp.src_block_ordinal) +
+                                                    " is outside the registration's " + S(n_ids) +
+                                                    " block ids (" + tag + ")");
+        const __int128 src_end = __int128(sp.src_offset_bytes) +
+                                 __int128(sp.count - 1) * sp.src_stride_bytes + sp.size_bytes;
+        if (src_end > live)
+          return set_error(TS_INVALID_ARGUMENT, "byte span exceeds its source block live bytes (" + tag +
+                                                    "): end=" + S128(src_end) + ", live=" + S(live));
+        span_bytes += __int128(sp.size_bytes) * sp.count;
+      }
+      if (__int128(sd->declared_bytes) != span_bytes)
+        return set_error(TS_INVALID_ARGUMENT, "pool span registration " + tag + " declared_bytes " +
+                                                  S(sd->declared_bytes) + " disagrees with the span sum " +
+                                                  S128(span_bytes));
+    }
+  }
+  return TS_OK;
+}
+
 int build(const ts_pool_reshard_request* rq, Plan* plan) {
   const int64_t nu = rq->n_src_units;
   if (nu <= 0) return set_error(TS_INVALID_ARGUMENT, "src_units must not be empty");
@@ -146,12 +263,9 @@ int build(const ts_pool_reshard_request* rq, Plan* plan) {
     return rq->unit_names && rq->unit_names[u] ? std::string(rq->unit_names[u])
                                                : "src unit " + S(u);
   };
-  std::vector<int64_t> dst_ids(rq->dst_block_ids, rq->dst_block_ids + rq->n_dst_block_ids);
-  if (dst_ids.empty()) return set_error(TS_INVALID_ARGUMENT, "dst_device_block_ids must not be empty");
-  for (int64_t b : dst_ids)
-    if (b < 0) return set_error(TS_INVALID_ARGUMENT, "dst_device_block_ids must be non-negative");
+  // registration-time checks first, as in the reference's flow
+  if (int rc = validate_unit_registrations(rq, nu); rc != TS_OK) return rc;
   const int64_t np_dst = rq->n_dst_pools;
-  if (np_dst <= 0) return set_error(TS_INVALID_ARGUMENT, "Destination pool manifest must not be empty");
   std::vector<std::vector<pool::Pool>> src(static_cast<size_t>(nu));
   for (int64_t u = 0; u < nu; ++u) {
     if (rq->n_src_pools[u] <= 0)
@@ -170,6 +284,12 @@ int build(const ts_pool_reshard_request* rq, Plan* plan) {
     if (rc != TS_OK) return rc;
     dst.push_back(std::move(p));
   }
+  if (int rc = validate_span_registrations(rq, src, unit_name); rc != TS_OK) return rc;
+  // BuildPoolReshardPlan proper
+  std::vector<int64_t> dst_ids(rq->dst_block_ids, rq->dst_block_ids + rq->n_dst_block_ids);
+  if (dst_ids.empty()) return set_error(TS_INVALID_ARGUMENT, "dst_device_block_ids must not be empty");
+  for (int64_t b : dst_ids)
+    if (b < 0) return set_error(TS_INVALID_ARGUMENT, "dst_device_block_ids must be non-negative");
   // canonical (tag, dtype_tag) manifests agree; source geometry agrees
   for (int64_t u = 0; u < nu; ++u) {
     bool same = src[size_t(u)].size() == dst.size();
@@ -244,7 +364,7 @@ int build(const ts_pool_reshard_request* rq, Plan* plan) {
   std::set<int64_t> par;
   std::map<int64_t, int64_t> ranks;  // rank -> unit
   for (int64_t u = 0; u < nu; ++u) {
-    par.insert(rq->transfer_parallelism ? rq->transfer_parallelism[u] : 1);
+    par.insert(rq->transfer_parallelism ? rq->transfer_parallelism[u] : nu);
     ranks[rq->transfer_ranks ? rq->transfer_ranks[u] : u] = u;
   }
   if (par.size() != 1 || *par.begin() <= 0)

@@ -140,7 +140,11 @@ def build_pool_reshard_plan(
 
   src_pools[u]: source unit u's pool manifest; dst_pools: the destination's.
   declarations: (source unit index, PoolSpanRegistration) pairs.
-  Raises ValueError with the reference planner's messages.
+  transfer_parallelism / transfer_ranks: each unit's registration (default:
+  the number of units / the unit's index).
+  Raises ValueError with the reference's messages: the checks its unit and
+  span registration make (work_unit_directory.cc:66-86,
+  request_block_registry.cc:142-245), then the planner's.
   """
   nu = len(src_pools)
   src = [[coerce_pool_spec(p) for p in unit] for unit in src_pools]
