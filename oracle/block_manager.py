@@ -5,7 +5,9 @@ as written: Allocate scans every block, takes free ids in increasing order,
 then evictable (allocated, unlocked) ids sorted by (last_access_counter, id);
 one access-counter tick per Allocate / AllocateTarget / AccessBlock call.
 Used to check the product allocator's order, which reaches the same result
-from ordered sets instead of a full scan.
+from ordered sets instead of a full scan.  Pinned, with the product, to the
+answers of the reference's own logical_block_manager.cc (compiled by
+oracle/build_ref.py; tests/golden/block_manager.json).
 """
 
 from __future__ import annotations

@@ -1,6 +1,6 @@
 """Compiles reference sources into test oracle binaries.
 
-    python oracle/build_ref.py     # -> oracle/_ref/{lru_ref, pool_ref, meta_ref, plan_ref}
+    python oracle/build_ref.py     # -> oracle/_ref/{lru_ref, pool_ref, meta_ref, plan_ref, bm_ref}
 
 * lru_ref: oracle/ref_lru_driver.cc over the header-only LRUCache
   (tpu_sync/kv_cache/lru_cache.h);
@@ -9,7 +9,8 @@
   and kv_cache_metadata_shm.cc;
 * plan_ref: oracle/ref_pool_reshard_driver.cc linked with tpu_sync/kv_cache/pool_layout.cc
   and reshard/{declaration_types, work_unit_directory, request_block_registry,
-  pool_reshard_planner}.cc.
+  pool_reshard_planner}.cc;
+* bm_ref: oracle/ref_bm_driver.cc linked with tpu_sync/kv_cache/logical_block_manager.cc.
 
 g++ compiles them where they lie in the reference checkout (REFERENCE_ROOT,
 else BASELINE.json's reference_path); oracle/shim stands in for the few absl types they
@@ -120,8 +121,28 @@ def build_plan(force: bool = False) -> Path | None:
   return PLAN_OUT
 
 
+BM_OUT = HERE / "_ref" / "bm_ref"
+
+
+def build_bm(force: bool = False) -> Path | None:
+  """Builds bm_ref if the reference checkout is present; returns its path."""
+  ref = reference_root()
+  cc = ref / "tpu_sync" / "kv_cache" / "logical_block_manager.cc"
+  src = HERE / "ref_bm_driver.cc"
+  if BM_OUT.exists() and not force and BM_OUT.stat().st_mtime >= src.stat().st_mtime:
+    return BM_OUT
+  if not cc.exists():
+    return BM_OUT if BM_OUT.exists() else None
+  BM_OUT.parent.mkdir(parents=True, exist_ok=True)
+  cxx = shutil.which("g++") or "c++"
+  subprocess.run([cxx, "-std=c++17", "-O1", f"-I{HERE / 'shim'}", f"-I{ref}", str(src), str(cc),
+                  "-o", str(BM_OUT)], check=True)
+  return BM_OUT
+
+
 if __name__ == "__main__":
   print(build(force=True))
   print(build_pool(force=True))
   print(build_meta(force=True))
   print(build_plan(force=True))
+  print(build_bm(force=True))

@@ -1,11 +1,15 @@
 """CPU tests of the tier-2 store: its LRU index replayed against the
 reference's own LRUCache (compiled by oracle/build_ref.py), its host block
-allocator against the LogicalBlockManager restatement and the reference's
-allocator test expectations, and the local Lookup / Insert / Save / Load /
-Poll state machine (host-only mode: transfers complete at issue)."""
+allocator against the reference's own LogicalBlockManager (operation scripts
+it answered, tests/golden/block_manager.json), the LogicalBlockManager
+restatement and the reference's allocator test expectations, and the local
+Lookup / Insert / Save / Load / Poll state machine (host-only mode:
+transfers complete at issue)."""
 
 import ctypes
+import json
 import subprocess
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -112,6 +116,39 @@ def test_allocator_reference_expectations():
   assert host_op(s, 1, [1]) == _native.FAILED_PRECONDITION
   assert host_op(s, 1, [2, 2]) == _native.INVALID_ARGUMENT
   assert host_op(s, 0, [1, 3]) == 0 and s.stats()["host_free"] == 5
+
+
+def test_allocator_replays_reference_scripts():
+  """Every answer the reference's LogicalBlockManager gave (status code,
+  allocated ids in order, state counts), from the product and the oracle."""
+  g = json.loads((Path(__file__).resolve().parent / "golden" / "block_manager.json").read_text())
+  ops_code = {"dealloc": 0, "target": 1, "unlock": 2, "access": 3}
+  n_ops = 0
+  for sc in g["scripts"]:
+    n = sc["blocks"]
+    s = KVCacheStore(capacity=4, host_blocks=n)
+    o = obm.LogicalBlockManager(n)
+    for line, want in sc["ops"]:
+      op, *args = line.split()
+      vals = [int(a) for a in args]
+      if op == "alloc":
+        rc, ids = alloc(s, vals[0], bool(vals[1]))
+        got = f"{rc} " + (" ".join(str(int(i)) for i in ids) if rc == 0 else "-")
+        code, oids = o.allocate(vals[0], bool(vals[1]))
+        ogot = f"{code} " + (" ".join(map(str, oids)) if code == 0 else "-")
+      elif op == "stats":
+        st = s.stats()
+        got = f"{st['host_free']} {n - st['host_free']} {st['host_locked']}"
+        ogot = f"{o.num_free()} {n - o.num_free()} {o.num_locked()}"
+      else:
+        got = str(host_op(s, ops_code[op], vals))
+        fn = {"dealloc": o.deallocate, "target": o.allocate_target, "unlock": o.unlock,
+              "access": lambda v: o.access(v[0])}[op]
+        ogot = str(fn(vals))
+      assert got == want, (line, got, want)
+      assert ogot == want, (line, ogot, want)
+      n_ops += 1
+  assert n_ops >= 3000
 
 
 @pytest.mark.parametrize("seed", range(5))
