@@ -462,14 +462,6 @@ def measure_pcie(torch, device, nbytes=GIB):
   return out
 
 
-def _cumsum(sizes):
-  out, acc = [], 0
-  for n in sizes:
-    out.append(acc)
-    acc += n
-  return out, acc
-
-
 def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
   """C4: Llama-3-8B fp32 FSDP shards on ranks [0, half) -> TP bf16 shards on
   ranks [half, 2*half), one reshard kernel per trainer rank storing straight
@@ -484,13 +476,9 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
   params = workloads.llama3_8b_params()
   specs = workloads.weight_sync_specs(half, half, params)
   plan = rp.build_plan(specs)
-  # elements each slot (rank) holds of every variable
-  src_sizes = [[math.prod(rp.local_shape(rp.shard_boxes(v.shape, v.src_mesh)[v.src_box_of(r)]))
-                for r in range(half)] for v in specs]
-  dst_sizes = [[math.prod(rp.local_shape(rp.shard_boxes(v.shape, v.dst_mesh)[v.dst_box_of(r)]))
-                for r in range(half)] for v in specs]
-  src_off, src_total = _cumsum([src_sizes[v][idx] for v in range(len(specs))]) if is_src else ([], 0)
-  dst_offs = [_cumsum([dst_sizes[v][d] for v in range(len(specs))]) for d in range(half)]
+  layout = workloads.weight_sync_layout(specs, half, half)
+  src_total = layout[0][idx][1] if is_src else 0
+  dst_offs = layout[1]
   if is_src:
     flat = torch.empty(src_total, dtype=torch.float32, device=device)
     flat.normal_(0.0, 0.02, generator=torch.Generator(device=device).manual_seed(3 + idx))
@@ -504,12 +492,8 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
   if is_src:
     dsts = {d: import_destinations(descs[half + d], kernel_device=device.index)[0]
             for d in range(half)}
-    chunks = []
-    for (vi, d), cs in plan.for_source(idx).items():
-      sp = flat.data_ptr() + 4 * src_off[vi]
-      dp = dsts[d].data_ptr() + 2 * dst_offs[d][0][vi]
-      for (so, do, size, ss, ds, cnt) in cs:
-        chunks.append((sp, dp, so, do, size, ss, ds, cnt))
+    chunks = workloads.weight_sync_chunks(plan, layout, idx, flat.data_ptr(),
+                                          {d: dsts[d].data_ptr() for d in range(half)})
     prog = ops.ReshardProgram(chunks, torch.float32, torch.bfloat16, device)
     for _ in range(warmup):
       prog.launch()

@@ -151,6 +151,45 @@ def weight_sync_specs(n_src: int, n_dst: int, params=None):
   return out
 
 
+def _cumsum(sizes):
+  out, acc = [], 0
+  for n in sizes:
+    out.append(acc)
+    acc += int(n)
+  return out, acc
+
+
+def weight_sync_layout(specs, n_src: int, n_dst: int):
+  """Flat-buffer layout of a weight sync: every trainer slot holds its
+  source boxes of all variables back to back (variable order), every
+  sampler slot its destination boxes.  Returns (src, dst): per slot a pair
+  (element offset of each variable, total elements)."""
+  import math
+
+  from tpu_sync_b200 import reshard_plan as rp
+  src_sizes = [[math.prod(rp.local_shape(rp.shard_boxes(v.shape, v.src_mesh)[v.src_box_of(r)]))
+                for v in specs] for r in range(n_src)]
+  dst_sizes = [[math.prod(rp.local_shape(rp.shard_boxes(v.shape, v.dst_mesh)[v.dst_box_of(r)]))
+                for v in specs] for r in range(n_dst)]
+  return [_cumsum(x) for x in src_sizes], [_cumsum(x) for x in dst_sizes]
+
+
+def weight_sync_chunks(plan, layout, src_slot: int, src_base: int, dst_bases,
+                       src_itemsize: int = 4, dst_itemsize: int = 2):
+  """One trainer slot's chunks over the flat buffers, in the form of
+  ops.ReshardProgram: (src address, dst address, src element offset, dst
+  element offset, size, src stride, dst stride, count), addresses being each
+  variable's start (`src_base` / `dst_bases[d]` plus its byte offset)."""
+  src, dst = layout
+  out = []
+  for (vi, d), cs in plan.for_source(src_slot).items():
+    sp = src_base + src_itemsize * src[src_slot][0][vi]
+    dp = dst_bases[d] + dst_itemsize * dst[d][0][vi]
+    for (so, do, size, ss, ds, cnt) in cs:
+      out.append((sp, dp, so, do, size, ss, ds, cnt))
+  return out
+
+
 # ---------------------------------------------------------------------------
 # C1 access trace driving the tier-2 store
 # ---------------------------------------------------------------------------
