@@ -318,6 +318,41 @@ class KVCacheManager:
                                                    ctypes.byref(st)))
     return self.READ_STATES.get(st.value, str(st.value))
 
+  # -- reference entry points with no counterpart on one node -----------------
+  @classmethod
+  def create_host_only_for_testing(cls, *, num_layers: int, num_shards: int = 1,
+                                   slice_byte_size: int, node_id: int,
+                                   local_port: Optional[int] = None, host_blocks: int,
+                                   parallelism: int = 4) -> "KVCacheManager":
+    """The reference's CPU-only manager over host memory
+    (tpu_sync/api/torch/kv_cache_manager.py:137-160).  Blocks live in HBM
+    here and nothing runs on a CPU path, so there is none: CPU tests use the
+    oracle's byte model of the manager."""
+    raise NotImplementedError(
+        "create_host_only_for_testing: this build has no host-only manager (blocks live "
+        "in HBM); construct KVCacheManager over device tensors")
+
+  def register_active_plan(self, uuid: int, request, is_sender: bool) -> None:
+    """Registers a serialized StartTransferRequest for a strided TCP push in
+    the reference (tpu_sync/api/torch/kv_cache_manager.py:196-204).  The TCP
+    transport is not part of this build: on one node a planned hand-off runs
+    as a PoolReshardProgram or push_weights_resharded_entries over NVLink."""
+    raise NotImplementedError(
+        "register_active_plan: strided TCP push plans are not supported; use "
+        "pool_reshard.PoolReshardProgram or WeightSynchronizer.push_weights_resharded_entries")
+
+  def unregister_active_plan(self, uuid: int) -> None:
+    """See register_active_plan (tpu_sync/api/torch/kv_cache_manager.py:206-208)."""
+    raise NotImplementedError("unregister_active_plan: strided TCP push plans are not supported")
+
+  def push_registered_plan(self, uuid: int, peer: str, src_block_ids: Sequence[int],
+                           dst_block_ids: Sequence[int], layer_idx: int = -1,
+                           parallelism: int = 1) -> None:
+    """See register_active_plan (tpu_sync/api/torch/kv_cache_manager.py:210-227)."""
+    raise NotImplementedError(
+        "push_registered_plan: strided TCP push plans are not supported; use "
+        "pool_reshard.PoolReshardProgram or WeightSynchronizer.push_weights_resharded_entries")
+
   def register_recv(self, uuid: int, req_id: str, expected_block_count: int) -> None:
     """Receivers need no staging here: a pool reshard program stores
     straight into this manager's HBM (PoolReshardProgram), so there is

@@ -40,18 +40,46 @@ class BlockStatus(enum.IntEnum):
 
 @dataclass(frozen=True)
 class RaidenId:
+  """RaidenId (tpu_sync/api/torch/kv_cache_store.py:38-86): a value type here
+  (no native object behind it), so `impl`, the reference's handle to one,
+  is accepted and ignored."""
   job_name: str = ""
   job_replica_id: str = ""
   data_name: str = ""
   data_replica_idx: int = 0
+  impl: object = field(default=None, repr=False, compare=False)
 
 
 @dataclass
 class RaidenBlockId:
-  raiden_id: RaidenId = field(default_factory=RaidenId)
+  """RaidenBlockId (tpu_sync/api/torch/kv_cache_store.py:89-151), with the
+  reference's positional order (raiden_id, host_block_id, status,
+  device_block_id) and its accessors of the owning RaidenId's fields."""
+  raiden_id: Optional[RaidenId] = None  # None: an empty RaidenId, as in the reference
   host_block_id: int = -1
-  device_block_id: int = -1
   status: BlockStatus = BlockStatus.INIT
+  device_block_id: int = -1
+  impl: object = field(default=None, repr=False, compare=False)
+
+  def __post_init__(self):
+    if self.raiden_id is None:
+      self.raiden_id = RaidenId()
+
+  @property
+  def job_name(self) -> str:
+    return self.raiden_id.job_name
+
+  @property
+  def job_replica_id(self) -> str:
+    return self.raiden_id.job_replica_id
+
+  @property
+  def data_name(self) -> str:
+    return self.raiden_id.data_name
+
+  @property
+  def data_replica_idx(self) -> int:
+    return self.raiden_id.data_replica_idx
 
 
 def _pack(hashes: Sequence[bytes]):
@@ -75,7 +103,7 @@ class KVCacheStore:
       raise ValueError("num_shards must be >= 1")
     if global_registry_address:
       raise ValueError("the global registry is not supported (local store only)")
-    self.raiden_id = raiden_id or RaidenId()
+    self._raiden_id = raiden_id or RaidenId()
     self._mgr = manager
     if host_blocks is None:
       host_blocks = manager.host_blocks if manager is not None else capacity
@@ -117,6 +145,11 @@ class KVCacheStore:
           self._meta_region.reformat()
         except RuntimeError as e2:
           logging.warning("Failed to reformat the KV metadata table: %s", e2)
+
+  @property
+  def raiden_id(self) -> RaidenId:
+    """The RaidenId of this store (tpu_sync/api/torch/kv_cache_store.py:260-263)."""
+    return self._raiden_id
 
   def close(self) -> None:
     if getattr(self, "_impl", None):
@@ -165,8 +198,9 @@ class KVCacheStore:
                                                 len(block_hashes), int(pin_found), out,
                                                 ctypes.byref(n)), "KVCacheStore lookup: ")
     return [(bytes(block_hashes[i]),
-             RaidenBlockId(self.raiden_id, out[i].host_block_id, out[i].device_block_id,
-                           BlockStatus(out[i].status))) for i in range(n.value)]
+             RaidenBlockId(raiden_id=self.raiden_id, host_block_id=out[i].host_block_id,
+                           device_block_id=out[i].device_block_id,
+                           status=BlockStatus(out[i].status))) for i in range(n.value)]
 
   def insert(self, block_hashes: List[bytes], slices: Sequence, on_host: bool = False) -> bool:
     infos = (_native.BlockInfo * max(len(slices), 1))()
