@@ -104,19 +104,15 @@ def random_request(rng: random.Random):
           if take % 8 == 0 and take >= 16 and rng.random() < 0.4:
             # two interleaved row sets: rows of `row` bytes, even rows from
             # one span, odd rows from the other (strided on both sides)
+            # the source rows interleave the same way, inside [base, base + take)
             row = rng.choice([r for r in (4, 8) if take % (2 * r) == 0])
             rows = take // row
-            sstride = 2 * row
-            base = rng.randrange(0, s_live - ((rows - 1) * row + row) + 1)
+            base = rng.randrange(0, s_live - take + 1)
             ev, od = (rows + 1) // 2, rows // 2
-            spans.append(span(ordinal, base, page, inp, row, sstride, 2 * row, ev))
+            spans.append(span(ordinal, base, page, inp, row, 2 * row, 2 * row, ev))
             if od:
-              spans.append(span(ordinal, base + row, page, inp + row, row, sstride,
-                                2 * row, od))
-            # the source rows interleave too: keep them inside the live bytes
-            if base + (rows - 1) * row + row > s_live:
-              spans = spans[:-2 if od else -1]
-              spans.append(span(ordinal, 0, page, inp, take))
+              spans.append(span(ordinal, base + row, page, inp + row, row, 2 * row, 2 * row,
+                                od))
           else:
             spans.append(span(ordinal, rng.randrange(0, s_live - take + 1), page, inp,
                               take))
