@@ -75,6 +75,9 @@ def check_span_registrations(src_pools, decls, name):
   """RequestBlockRegistry::Register (kv_cache/reshard/request_block_registry.cc:142-245)
   for every source unit in order: its declarations, in the order given,
   against the live bytes of its manifest's pools per tag."""
+  for uu, _ in decls:
+    if uu < 0 or uu >= len(src_pools):
+      raise PlanError(f"Work unit is not registered: src unit {uu}")
   for u in range(len(src_pools)):
     mine = [d for uu, d in decls if uu == u]
     if not mine:

@@ -316,3 +316,12 @@ def test_default_parallelism_is_the_unit_count():
   with pytest.raises(ValueError, match="transfer_rank must be less than transfer_parallelism"):
     build_pool_reshard_plan([P1024, P1024], P1024, ["fa"], [7, 9],
                             [(0, reg([3], [(0, 0, 0, 0, 1024)]))], transfer_parallelism=[1, 1])
+
+
+@pytest.mark.parametrize("unit", [-1, 2])
+def test_declaration_of_an_unknown_unit_is_rejected(unit):
+  """Register for a unit the request does not have fails in the reference
+  ("Work unit is not registered", request_block_registry.cc:266-268)."""
+  prod, orc = both([P1024, P1024], P1024, ["fa"], [7, 9],
+                   [(0, reg([3], [(0, 0, 0, 0, 1024)])), (unit, reg([5], [(0, 0, 1, 0, 1024)]))])
+  assert prod == orc == {"error": f"Work unit is not registered: src unit {unit}"}

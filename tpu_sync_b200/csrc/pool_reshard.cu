@@ -186,6 +186,11 @@ int validate_span_registrations(const ts_pool_reshard_request* rq,
                                 const std::vector<std::vector<pool::Pool>>& src,
                                 const UnitName& unit_name) {
   constexpr int64_t kMaxSpanCount = int64_t{1} << 20;
+  // a declaration of a unit the request does not have was never registered
+  for (int64_t d = 0; d < rq->n_decls; ++d)
+    if (rq->decls[d].src_unit < 0 || rq->decls[d].src_unit >= int64_t(src.size()))
+      return set_error(TS_INVALID_ARGUMENT,
+                       "Work unit is not registered: src unit " + S(rq->decls[d].src_unit));
   for (int64_t u = 0; u < int64_t(src.size()); ++u) {
     std::vector<const ts_span_decl*> mine;
     for (int64_t d = 0; d < rq->n_decls; ++d)
