@@ -42,6 +42,12 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "KV offload/reload GB/s per GPU vs PCIe peak; extract HBM GB/s; 8B weight-sync s"
 GIB = 1 << 30
+# C1 geometry (Llama-3-8B KV): 32 layers x K/V storages of 16-token blocks of
+# 8 heads x 128 bf16.  Stated here so the CPU reference arm needs nothing from
+# the product package; the GPU arm checks the package's C1 against it.
+C1_STORAGES = 32 * 2
+C1_STORAGE_BLOCK_BYTES = 16 * 8 * 128 * 2     # 32 KiB
+C1_BLOCK_BYTES = C1_STORAGES * C1_STORAGE_BLOCK_BYTES  # 2 MiB
 PCIE_SPEC_GBS = 64.0
 # DRAM bytes per 2 MiB block moved by the insert kernel, from
 # profiles/insert_kernel_c1_256blocks.md (mean of the two captured launches).
@@ -195,12 +201,23 @@ class ClockSampler:
 # CPU arms (oracle restatement of the reference host loops)
 # ---------------------------------------------------------------------------
 
-def c1_plans(rank: int, host_blocks: int, pool_blocks: int, batch: int, n_steps: int):
+def c1_plans(rank: int, host_blocks: int, pool_blocks: int, batch: int, n_steps: int,
+             source: str = "product"):
   """Step plans of the C1 trace (see run_ours): per step (offload device ids,
-  offload host ids, reload host ids, reload device ids)."""
-  from tpu_sync_b200 import workloads
-  trace = workloads.zipf_trace(seed=10 + rank)
-  batches, stats = workloads.store_transfer_streams(trace, host_blocks, pool_blocks, batch)
+  offload host ids, reload host ids, reload device ids).
+
+  source "product": the trace runs through the product's tier-2 store;
+  "reference": through the reference's own LRU and block allocator compiled
+  from source (oracle/_ref/store_trace_ref), which imports nothing from the
+  product.  Both give the same plans (tests/test_cpu_store.py)."""
+  if source == "reference":
+    from oracle import store_trace
+    trace = store_trace.zipf_trace(seed=10 + rank)
+    batches, stats = store_trace.transfer_streams(trace, host_blocks, pool_blocks, batch)
+  else:
+    from tpu_sync_b200 import workloads
+    trace = workloads.zipf_trace(seed=10 + rank)
+    batches, stats = workloads.store_transfer_streams(trace, host_blocks, pool_blocks, batch)
   half_pool = pool_blocks // 2
   # A step gathers consecutive access batches, in trace order, until `batch`
   # reloads (or offloads) are pending: its offloads and reloads go out
@@ -227,18 +244,15 @@ def c1_plans(rank: int, host_blocks: int, pool_blocks: int, batch: int, n_steps:
 def c1_host_blocks(args, world: int) -> int:
   """Host tier blocks of the C1 configuration: as many as requested (default
   32768 = 64 GiB), bounded by this box's RAM share per local rank."""
-  from tpu_sync_b200 import workloads
   want = args.host_blocks or 32768
   local_ranks = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
-  fit = int(0.45 * mem_available_bytes() / max(local_ranks, 1) // workloads.C1.block_bytes)
+  fit = int(0.45 * mem_available_bytes() / max(local_ranks, 1) // C1_BLOCK_BYTES)
   return max(4 * args.batch, min(want, fit))
 
 
 def c1_config(args, host_blocks: int, plans, trace_stats, world: int) -> dict:
   """The `config` of both arms' JSON lines (same workload, same plans)."""
-  from tpu_sync_b200 import workloads
-  g = workloads.C1
-  pitch = g.block_bytes
+  pitch = C1_BLOCK_BYTES
   pool_bytes = args.pool_blocks * pitch
   return {
       "workload": ("C1 Llama-3-8B KV tier: 32 layers x K/V, 16-token blocks of "
@@ -269,9 +283,7 @@ def cpu_offload_reload(plans, seconds: float, steps: int = 0, warmup: int = 0):
   per storage, as in the real layout).
   """
   from oracle import cpu_ref
-  from tpu_sync_b200 import workloads
-  g = workloads.C1
-  S, bb = g.storages, g.storage_block_bytes
+  S, bb = C1_STORAGES, C1_STORAGE_BLOCK_BYTES
   nb = 2048
   threads = cpu_ref.host_threads()
   dev = [np.empty(nb * bb, np.uint8) for _ in range(S)]
@@ -297,7 +309,7 @@ def cpu_offload_reload(plans, seconds: float, steps: int = 0, warmup: int = 0):
     t0 = time.perf_counter()
     one_step(p)
     times.append(time.perf_counter() - t0)
-    moved += (len(p[0]) + len(p[2])) * g.block_bytes
+    moved += (len(p[0]) + len(p[2])) * C1_BLOCK_BYTES
     i += 1
   total = sum(times)
   return {"value": round(moved / total / 1e9, 3), "unit": "GB/s", "cores": threads,
@@ -408,8 +420,13 @@ def run_reference(args):
     return
   world = int(os.environ.get("WORLD_SIZE", "1"))
   host_blocks = c1_host_blocks(args, world)
-  plans, stats = c1_plans(0, host_blocks, args.pool_blocks, args.batch,
-                          args.warmup + args.steps)
+  try:
+    plans, stats = c1_plans(0, host_blocks, args.pool_blocks, args.batch,
+                            args.warmup + args.steps, source="reference")
+  except (OSError, RuntimeError) as e:
+    print(json.dumps({"impl": "reference",
+                      "unavailable": f"reference store trace driver unavailable: {e}"}))
+    return
   r = cpu_offload_reload(plans, 0.0, steps=args.steps, warmup=args.warmup)
   line = {"impl": "reference", "metric": METRIC, "value": r["value"], "unit": "GB/s",
           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -942,6 +959,8 @@ def run_ours(args):
     return float(t.item())
 
   g = workloads.C1
+  if (g.storages, g.storage_block_bytes) != (C1_STORAGES, C1_STORAGE_BLOCK_BYTES):
+    raise RuntimeError("workloads.C1 does not match the C1 geometry stated in bench.py")
   B = args.batch
   pool_blocks = args.pool_blocks
   # Pool: [layers, K/V, blocks, 16, 8, 128] bf16, N(0,1) generated on device.
@@ -970,6 +989,17 @@ def run_ours(args):
   # from its middle (tier full, evicting).  Device ids: offloads read the
   # first half of the pool, reloads write the second half.
   plans, trace_stats = c1_plans(rank, host_blocks, pool_blocks, B, args.warmup + args.steps)
+  # The CPU reference arm takes its plans from the reference's own LRU and
+  # allocator; the two must agree for its number to be comparable.
+  plans_match = None
+  if rank == 0:
+    try:
+      ref_plans, _ = c1_plans(rank, host_blocks, pool_blocks, B, args.warmup + args.steps,
+                              source="reference")
+      plans_match = all(all(np.array_equal(a, b) for a, b in zip(p, q))
+                        for p, q in zip(plans, ref_plans))
+    except (OSError, RuntimeError):
+      plans_match = None
   plan_bytes = [(len(p[0]) + len(p[2])) * pitch for p in plans]
   bench_stream = torch.cuda.Stream(device)
 
@@ -1131,7 +1161,8 @@ def run_ours(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic N(0,1) bf16 KV pool generated on device (seed 10+rank)",
-        "config": c1_config(args, host_blocks, plans, trace_stats, world),
+        "config": dict(c1_config(args, host_blocks, plans, trace_stats, world),
+                       plans_match_reference_store=plans_match),
         "transfer": {"mode": args.mode, "copy_streams": args.copy_streams,
                      "max_ctas": args.max_ctas or None,
                      "reload_staged_every": args.reload_staged_every or None},

@@ -1,6 +1,7 @@
 """Compiles reference sources into test oracle binaries.
 
-    python oracle/build_ref.py     # -> oracle/_ref/{lru_ref, pool_ref, meta_ref, plan_ref, bm_ref}
+    python oracle/build_ref.py     # -> oracle/_ref/{lru_ref, pool_ref, meta_ref, plan_ref, bm_ref,
+                                   #                 store_trace_ref}
 
 * lru_ref: oracle/ref_lru_driver.cc over the header-only LRUCache
   (tpu_sync/kv_cache/lru_cache.h);
@@ -10,7 +11,10 @@
 * plan_ref: oracle/ref_pool_reshard_driver.cc linked with tpu_sync/kv_cache/pool_layout.cc
   and reshard/{declaration_types, work_unit_directory, request_block_registry,
   pool_reshard_planner}.cc;
-* bm_ref: oracle/ref_bm_driver.cc linked with tpu_sync/kv_cache/logical_block_manager.cc.
+* bm_ref: oracle/ref_bm_driver.cc linked with tpu_sync/kv_cache/logical_block_manager.cc;
+* store_trace_ref: oracle/ref_store_trace_driver.cc over lru_cache.h, linked with
+  tpu_sync/kv_cache/logical_block_manager.cc (the C1 access trace through the
+  reference's index and allocator).
 
 g++ compiles them where they lie in the reference checkout (REFERENCE_ROOT,
 else BASELINE.json's reference_path); oracle/shim stands in for the few absl types they
@@ -140,9 +144,30 @@ def build_bm(force: bool = False) -> Path | None:
   return BM_OUT
 
 
+STORE_OUT = HERE / "_ref" / "store_trace_ref"
+
+
+def build_store_trace(force: bool = False) -> Path | None:
+  """Builds store_trace_ref if the reference checkout is present; returns its path."""
+  ref = reference_root()
+  cc = ref / "tpu_sync" / "kv_cache" / "logical_block_manager.cc"
+  header = ref / "tpu_sync" / "kv_cache" / "lru_cache.h"
+  src = HERE / "ref_store_trace_driver.cc"
+  if STORE_OUT.exists() and not force and STORE_OUT.stat().st_mtime >= src.stat().st_mtime:
+    return STORE_OUT
+  if not (cc.exists() and header.exists()):
+    return STORE_OUT if STORE_OUT.exists() else None
+  STORE_OUT.parent.mkdir(parents=True, exist_ok=True)
+  cxx = shutil.which("g++") or "c++"
+  subprocess.run([cxx, "-std=c++17", "-O2", f"-I{HERE / 'shim'}", f"-I{ref}", str(src), str(cc),
+                  "-o", str(STORE_OUT)], check=True)
+  return STORE_OUT
+
+
 if __name__ == "__main__":
   print(build(force=True))
   print(build_pool(force=True))
   print(build_meta(force=True))
   print(build_plan(force=True))
   print(build_bm(force=True))
+  print(build_store_trace(force=True))

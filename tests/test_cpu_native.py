@@ -30,28 +30,6 @@ def test_library_exports_every_declared_symbol():
   assert b"sm_100a" in lib.ts_version()
 
 
-def test_integration_guide_maps_every_symbol():
-  """INTEGRATION.md's entry-point table names every declared symbol (rows
-  may abbreviate a family as `ts_x_create` / `_launch` / ...)."""
-  text = (HEADER.parents[1] / "INTEGRATION.md").read_text()
-  names = set(declared_in_header())
-  named = set(re.findall(r"`(ts_\w+)`", text))
-  for row in text.splitlines():
-    if not row.startswith("| `ts_"):
-      continue
-    base = None
-    for tok in re.findall(r"`(\w+)`", row.split("|")[1]):
-      if tok.startswith("ts_"):
-        base = tok
-      elif tok.startswith("_") and base:
-        parts = base.split("_")
-        for k in range(len(parts) - 1, 1, -1):
-          if "_".join(parts[:k]) + tok in names:
-            named.add("_".join(parts[:k]) + tok)
-            break
-  assert sorted(names - named) == []
-
-
 def validate(src, dst, sizes):
   s, d, z = (_native.i64_array(x) for x in (src, dst, sizes))
   rc = _native.lib().ts_validate_copy_spec(_native.i64_ptr(s), s.size, _native.i64_ptr(d),

@@ -288,3 +288,48 @@ def test_remote_surface_refuses_without_registry():
   assert s.poll_remote_read_status() == ([], [], [])
   with pytest.raises(ValueError):
     s.read_remote([b"a", b"b"], [RaidenBlockId()], [0])
+
+
+def _same_streams(ref, prod):
+  assert len(ref) == len(prod)
+  for i, ((rs, rl), (ps, pl)) in enumerate(zip(ref, prod)):
+    assert rs == [tuple(x) for x in ps], f"saves of access batch {i} differ"
+    assert rl == [tuple(x) for x in pl], f"loads of access batch {i} differ"
+
+
+def test_c1_trace_decisions_match_reference_store():
+  """The whole C1 access trace (bench seed 10, 32768-block tier and pool,
+  512-access batches): every save's (device, host) ids and every load's
+  (host, device) ids equal those of the reference's LRUCache and
+  LogicalBlockManager composed as KVCacheStore's local paths
+  (oracle/_ref/store_trace_ref).  bench.py's CPU reference arm takes its
+  block lists from that binary, the product arm from the product store."""
+  from oracle import store_trace as ost
+  from tpu_sync_b200 import workloads
+  if build_ref.build_store_trace() is None:
+    pytest.skip("reference checkout not available to build the store trace oracle")
+  trace = ost.zipf_trace(seed=10)
+  assert np.array_equal(trace, workloads.zipf_trace(seed=10))
+  ref, ref_stats = ost.transfer_streams(trace, 32768, 32768, 512)
+  prod, prod_stats = workloads.store_transfer_streams(trace, 32768, 32768, 512)
+  assert ref_stats == prod_stats
+  _same_streams(ref, prod)
+
+
+@pytest.mark.parametrize("seed,host_blocks,pool,batch,n", [
+    (10, 4096, 32768, 512, 100_000), (11, 1024, 2048, 256, 30_000),
+    (12, 300, 512, 128, 20_000), (13, 2000, 1000, 512, 30_000)])
+def test_trace_decisions_under_eviction_match_reference_store(seed, host_blocks, pool, batch, n):
+  """Tiers smaller than the trace's working set: saves drop-evict unpinned
+  host entries (candidates first, then the LRU end) and reuse their ids in
+  the allocator's order; loads pinned by lookup survive the same batch's
+  saves, and completions only take effect when polled."""
+  from oracle import store_trace as ost
+  from tpu_sync_b200 import workloads
+  if build_ref.build_store_trace() is None:
+    pytest.skip("reference checkout not available to build the store trace oracle")
+  trace = ost.zipf_trace(n_access=n, seed=seed)
+  ref, ref_stats = ost.transfer_streams(trace, host_blocks, pool, batch)
+  prod, prod_stats = workloads.store_transfer_streams(trace, host_blocks, pool, batch)
+  assert ref_stats == prod_stats
+  _same_streams(ref, prod)

@@ -654,8 +654,10 @@ extern "C" int ts_store_save(ts_store* s, const uint8_t* keys, const int64_t* of
   tsb::clear_error();
   if (!s || (n > 0 && (!keys || !offs))) return set_error(TS_INVALID_ARGUMENT, "null pointer argument");
   std::vector<std::string> h = tsb::unpack_keys(keys, offs, n);
+  // SaveLocal processes no completions: finished transfers update the index
+  // only when polled (kv_cache_store.cc:977-1058), so a load finished but
+  // not yet polled still holds its pin here.
   std::lock_guard<std::mutex> lock(s->mu);
-  tsb::poll_locked(s);
   std::vector<tsb::BlockId> found;
   const int64_t nf = tsb::lookup_locked(s, h, false, &found);
   if (nf < n) return set_errorf(TS_NOT_FOUND, "Block hash not found: %s", tsb::hex(h[size_t(nf)]).c_str());
@@ -703,8 +705,7 @@ extern "C" int ts_store_load(ts_store* s, const uint8_t* keys, const int64_t* of
     return set_error(TS_INVALID_ARGUMENT, "block_hashes and device_block_ids size mismatch");
   if (n == 0) return TS_OK;
   std::vector<std::string> h = tsb::unpack_keys(keys, offs, n);
-  std::lock_guard<std::mutex> lock(s->mu);
-  tsb::poll_locked(s);
+  std::lock_guard<std::mutex> lock(s->mu);  // no completions processed (as Load)
   std::vector<tsb::BlockId> found;
   const int64_t nf = tsb::lookup_locked(s, h, false, &found);
   if (nf < n) return set_errorf(TS_NOT_FOUND, "Block hash not found: %s", tsb::hex(h[size_t(nf)]).c_str());
