@@ -80,6 +80,9 @@ def parse():
   p.add_argument("--copy-streams", type=int, default=2)
   p.add_argument("--chunk-blocks", type=int, default=0, help="0 = manager default")
   p.add_argument("--max-ctas", type=int, default=0, help="kernel grid cap, 0 = default")
+  p.add_argument("--sched", default="offload_priority,reload_per_piece",
+                 help="comma-separated manager sched flags: offload_priority, "
+                      "reload_per_piece, reload_overlap ('' = none)")
   p.add_argument("--reload-staged-every", type=int, default=0,
                  help="direct reloads: every n-th chunk through the copy engines (0 = none)")
   p.add_argument("--kernel-case", default="",
@@ -977,7 +980,8 @@ def run_ours(args):
   mgr = KVCacheManager([[t] for t in storages], host_blocks_to_allocate=host_blocks,
                        mode=args.mode, copy_streams=args.copy_streams,
                        chunk_blocks=args.chunk_blocks, max_ctas=args.max_ctas,
-                       reload_staged_every=args.reload_staged_every)
+                       reload_staged_every=args.reload_staged_every,
+                       sched=tuple(f for f in args.sched.split(",") if f))
 
   pcie = measure_pcie(torch, device)
 
@@ -1165,7 +1169,8 @@ def run_ours(args):
                        plans_match_reference_store=plans_match),
         "transfer": {"mode": args.mode, "copy_streams": args.copy_streams,
                      "max_ctas": args.max_ctas or None,
-                     "reload_staged_every": args.reload_staged_every or None},
+                     "reload_staged_every": args.reload_staged_every or None,
+                     "sched": [f for f in args.sched.split(",") if f]},
         "per_gpu_gbs": round(value / world, 3),
         "pcie": {"offload_d2h_gbs": round(d2h_gbs, 2), "reload_h2d_gbs": round(h2d_gbs, 2),
                  "measured_peak": pcie, "spec_gbs_per_dir": PCIE_SPEC_GBS,

@@ -550,8 +550,23 @@ typedef struct ts_manager_opts {
   int32_t reload_staged_every; /* direct reloads only: every n-th chunk goes through
                                   the copy engines instead (0 = none), so both
                                   H2D mechanisms run at once */
-  int32_t pad_;
+  int32_t sched;               /* SM scheduling of the two directions, a sum of
+                                  TS_SCHED_* flags (0 = neither) */
 } ts_manager_opts;
+
+/* ts_manager_opts.sched flags. */
+enum {
+  /* offload kernels run on a stream of the device's highest priority, so the
+   * gather takes SM slots ahead of a long-running reload kernel */
+  TS_SCHED_OFFLOAD_PRIORITY = 1,
+  /* direct reloads launch one CTA per 16 KiB piece instead of a persistent
+   * grid, so their CTAs retire (and free SM slots) as each piece lands */
+  TS_SCHED_RELOAD_PER_PIECE = 2,
+  /* consecutive direct reload chunks alternate between two kernel streams,
+   * so one chunk's last wave overlaps the next chunk's first (not used when
+   * a destination block repeats inside the call) */
+  TS_SCHED_RELOAD_OVERLAP = 4,
+};
 
 /* Creates a manager over num_layers x num_shards storages (row-major
  * [layer][shard]).  Replaces the device-backed KVCacheManagerBase constructor
@@ -621,8 +636,10 @@ TS_API int ts_mgr_pool_block_ref(ts_manager* mgr, int64_t pool_idx, int64_t shar
 
 /* Per-launch timing of the manager's kernels (CUDA events around every
  * extract / insert launch on its kernel streams).  ts_mgr_kernel_stats
- * returns and resets the launches, their summed device time and their
- * algorithmic HBM bytes (read + write) for which = 0 (extract) or 1 (insert).
+ * returns and resets the launches, their device time (the union of the
+ * launches' intervals: launches that overlap on two streams count once) and
+ * their algorithmic HBM bytes (read + write) for which = 0 (extract) or
+ * 1 (insert).
  * Plays the role of the reference's per-op duration telemetry
  * (JoinAndRecordTelemetry, tpu_sync/kv_cache/kv_cache_manager_base.cc:205-219). */
 TS_API int ts_mgr_set_profiling(ts_manager* mgr, int on);

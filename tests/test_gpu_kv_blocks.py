@@ -163,7 +163,12 @@ def test_fp8_extract_insert_matches_oracle(cuda, block_tokens, heads, n_blocks):
 
 MODES = [dict(mode="staged", copy_streams=1), dict(mode="staged", copy_streams=2),
          dict(mode="direct", max_ctas=64), dict(mode="direct_d2h", max_ctas=148),
-         dict(mode="direct_h2d"), dict(mode="direct_h2d", reload_staged_every=2)]
+         dict(mode="direct_h2d"), dict(mode="direct_h2d", reload_staged_every=2),
+         dict(mode="direct_h2d", sched=("offload_priority", "reload_per_piece")),
+         dict(mode="direct_h2d", sched=("offload_priority", "reload_per_piece",
+                                        "reload_overlap")),
+         dict(mode="direct", sched=("reload_per_piece", "reload_overlap")),
+         dict(mode="staged", sched=("offload_priority",))]
 
 
 def make_pair(geom, blocks, host_blocks, seed, cuda, chunk_blocks=0, **kw):
@@ -208,6 +213,28 @@ def test_manager_offload_reload_matches_model(cuda, chunk_blocks, mode):
     g.Await()
   torch.cuda.synchronize()
   assert_same(pool, mgr, model, range(96))
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_manager_repeated_destination_last_copy_wins(cuda, mode):
+  """A destination block named twice in one call ends with the later copy's
+  bytes, as the reference's in-order per-run copies leave it
+  (kv_cache_manager_base.cc:1945-2124), also when the two copies fall into
+  different pipelined chunks."""
+  geom = workloads.KVGeometry(layers=2, kv=2, block_tokens=16, heads=2, head_dim=128)
+  pool, mgr, model = make_pair(geom, 48, 48, 21, cuda, chunk_blocks=3, **mode)
+  mgr.d2h(list(range(20)), list(range(20))).Await()
+  model.d2h(list(range(20)), list(range(20)))
+  hs = [0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11]
+  ds = [30, 31, 32, 33, 30, 34, 31, 35, 36, 30, 37, 31]
+  mgr.h2d(hs, ds).Await()
+  assert model.h2d(hs, ds) == (ref.OK, "")
+  src = [40, 41, 42, 43, 44, 45, 46, 47]
+  dst = [25, 26, 25, 27, 28, 26, 29, 25]
+  mgr.d2h(src, dst).Await()
+  assert model.d2h(src, dst) == (ref.OK, "")
+  torch.cuda.synchronize()
+  assert_same(pool, mgr, model, range(48))
 
 
 @pytest.mark.parametrize("mode", MODES)

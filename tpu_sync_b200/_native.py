@@ -33,6 +33,11 @@ INTERNAL = 13
 UNAVAILABLE = 14
 PENDING = 100
 
+# ts_manager_opts.sched flags (TS_SCHED_*)
+SCHED_OFFLOAD_PRIORITY = 1
+SCHED_RELOAD_PER_PIECE = 2
+SCHED_RELOAD_OVERLAP = 4
+
 STATUS_NAMES = {
     OK: "OK", CANCELLED: "CANCELLED", UNKNOWN: "UNKNOWN",
     INVALID_ARGUMENT: "INVALID_ARGUMENT", DEADLINE_EXCEEDED: "DEADLINE_EXCEEDED",
@@ -79,7 +84,7 @@ class ManagerOpts(ctypes.Structure):
               ("shm_name", ctypes.c_char_p), ("model_uid", ctypes.c_char_p),
               ("fp8", ctypes.c_int32), ("mode", ctypes.c_int32),
               ("copy_streams", ctypes.c_int32), ("max_ctas", ctypes.c_int32),
-              ("reload_staged_every", ctypes.c_int32), ("pad_", ctypes.c_int32)]
+              ("reload_staged_every", ctypes.c_int32), ("sched", ctypes.c_int32)]
 
 
 class BlockInfo(ctypes.Structure):

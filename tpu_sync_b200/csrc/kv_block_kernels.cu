@@ -446,9 +446,12 @@ __global__ void __launch_bounds__(T, T == 128 ? 16 : 8)
 
 bool aligned16(uint64_t v) { return (v & 15u) == 0; }
 
+// max_ctas > 0 caps the persistent grid; max_ctas < 0 asks for one CTA per
+// item (CTAs retire as their piece lands instead of grid-striding).
 int launch_grid(int device, int64_t items, int max_ctas = 0) {
   int64_t cap = int64_t(sm_count(device)) * kCtasPerSm;
   if (max_ctas > 0 && max_ctas < cap) cap = max_ctas;
+  if (max_ctas < 0) cap = INT32_MAX;
   return int(items < cap ? items : cap);
 }
 

@@ -69,10 +69,13 @@ struct Slot {
   cudaEvent_t free = nullptr;
 };
 
-// Completion record of one call, kept so later calls can wait on it.
+// Completion record of one call, kept so later calls can wait on it: the
+// whole call, and each pipelined chunk of a whole-block call (chunk_ev[c]
+// completes once chunk c's blocks have been read and written).
 struct CallRec {
   uint64_t seq = 0;
   cudaEvent_t done = nullptr;
+  std::vector<cudaEvent_t> chunk_ev;
 };
 
 }  // namespace
@@ -115,9 +118,12 @@ struct ts_manager {
   int ncs = 2;        // copy streams per direction (staged)
   int max_ctas = 0;   // grid cap of the kernels
   int reload_staged_every = 0;  // direct reloads: every n-th chunk staged (0 = none)
+  int sched = 0;                // TS_SCHED_* flags
   uint8_t* host_dev = nullptr;  // device address of the mapped host tier
 
   cudaStream_t s_out_kernel = nullptr, s_in_kernel = nullptr;
+  cudaStream_t s_in_kernel2 = nullptr;  // second reload kernel stream (overlap)
+  cudaEvent_t in_join = nullptr;
   cudaStream_t out_cs[tsb::kMaxCopyStreams] = {};
   cudaStream_t in_cs[tsb::kMaxCopyStreams] = {};
   cudaEvent_t out_join[tsb::kMaxCopyStreams] = {};
@@ -128,6 +134,8 @@ struct ts_manager {
   // hazard tracking: sequence numbers of the last offload (d2h) / reload
   // (h2d) call touching each host block and device block.
   std::vector<uint64_t> host_d2h_seq, host_h2d_seq, dev_d2h_seq, dev_h2d_seq;
+  // ... and the chunk of that call which moved the block (-1: not chunked)
+  std::vector<int32_t> host_d2h_chunk, host_h2d_chunk, dev_d2h_chunk, dev_h2d_chunk;
   uint64_t d2h_seq = 0, h2d_seq = 0;
   tsb::CallRec d2h_ring[tsb::kEventRing];
   tsb::CallRec h2d_ring[tsb::kEventRing];
@@ -433,13 +441,17 @@ int launch_chunk(ts_manager* m, bool to_host, const ParamIds& ids, int64_t cn,
     e1 = prof_event(m);
     TS_CUDA_RET(cudaEventRecord(e0, ks), "event record");
   }
+  // A direct reload waits on PCIe for its whole chunk; launched one CTA per
+  // piece its CTAs retire as pieces land, so other kernels get SM slots.
+  const int ctas = !to_host && ids.direct && (m->sched & TS_SCHED_RELOAD_PER_PIECE) != 0
+                       ? -1 : m->max_ctas;
   int rc = to_host
                ? mgr_extract(m->device, m->d_table, int(m->st.size()), ids, cn, staging,
                              m->host_pitch, err_dev, ks, m->vec_ok, m->max_bb, m->fp8,
                              m->scale_off, m->max_ctas)
                : mgr_insert(m->device, m->d_table, int(m->st.size()), ids, cn, staging,
                             m->host_pitch, err_dev, ks, m->vec_ok, m->max_bb, m->fp8,
-                            m->scale_off, m->max_ctas);
+                            m->scale_off, ctas);
   if (rc != TS_OK) return rc;
   if (m->profiling) {
     TS_CUDA_RET(cudaEventRecord(e1, ks), "event record");
@@ -451,8 +463,10 @@ int launch_chunk(ts_manager* m, bool to_host, const ParamIds& ids, int64_t cn,
   return TS_OK;
 }
 
+// `seq` is the sequence number this call will get; chunk_of[i] receives the
+// pipelined chunk that moves block i of the plan (-1 when not chunked).
 int enqueue_transfer(ts_manager* m, bool to_host, const Plan& p, void* user_stream,
-                     ts_event* ev) {
+                     ts_event* ev, uint64_t seq, std::vector<int32_t>* chunk_of) {
   cudaStream_t user = reinterpret_cast<cudaStream_t>(user_stream);
   cudaStream_t ks = to_host ? m->s_out_kernel : m->s_in_kernel;
   cudaStream_t* cs = to_host ? m->out_cs : m->in_cs;
@@ -463,6 +477,8 @@ int enqueue_transfer(ts_manager* m, bool to_host, const Plan& p, void* user_stre
   std::vector<cudaStream_t> streams{ks};
   if (!is_direct(m, to_host) || staged_every > 0)
     for (int i = 0; i < m->ncs; ++i) streams.push_back(cs[i]);
+  cudaStream_t ks2 = !to_host && direct ? m->s_in_kernel2 : nullptr;
+  if (ks2 != nullptr) streams.push_back(ks2);
   int* err_dev = nullptr;
   TS_CUDA_RET(cudaHostGetDevicePointer(reinterpret_cast<void**>(&err_dev), ev->err_word, 0),
               "error word mapping");
@@ -479,7 +495,20 @@ int enqueue_transfer(ts_manager* m, bool to_host, const Plan& p, void* user_stre
   // blocks need, so a few conflicting blocks do not hold back the rest.
   CallRec* ring = to_host ? m->h2d_ring : m->d2h_ring;
   const size_t nb = p.src.size();
+  chunk_of->assign(nb, -1);
+  // This call's own record: its previous user (kEventRing calls ago) is
+  // drained first, and until this call is recorded nothing may name it.
+  CallRec& own = (to_host ? m->d2h_ring : m->h2d_ring)[seq % kEventRing];
+  if (own.seq != 0 && own.done != nullptr)
+    TS_CUDA_RET(cudaEventSynchronize(own.done), "event ring recycle");
+  own.seq = 0;
   std::vector<uint64_t> need(nb, 0);
+  // the (call, chunk) pairs each block waits for (seq 0 = none)
+  struct Dep {
+    uint64_t seq = 0;
+    int32_t chunk = -1;
+  };
+  std::vector<Dep> dep_a(nb), dep_b(nb);
   std::unordered_map<uint64_t, bool> finished;
   auto still_running = [&](uint64_t seq) {
     if (seq == 0) return false;
@@ -491,10 +520,12 @@ int enqueue_transfer(ts_manager* m, bool to_host, const Plan& p, void* user_stre
     return !done;
   };
   for (size_t i = 0; i < nb; ++i) {
-    const uint64_t a = to_host ? m->dev_h2d_seq[size_t(p.src[i])] : m->host_d2h_seq[size_t(p.src[i])];
-    const uint64_t b = to_host ? m->host_h2d_seq[size_t(p.dst[i])] : m->dev_d2h_seq[size_t(p.dst[i])];
-    const uint64_t x = std::max(still_running(a) ? a : 0, still_running(b) ? b : 0);
-    need[i] = x;
+    const size_t si = size_t(p.src[i]), di = size_t(p.dst[i]);
+    const uint64_t a = to_host ? m->dev_h2d_seq[si] : m->host_d2h_seq[si];
+    const uint64_t b = to_host ? m->host_h2d_seq[di] : m->dev_d2h_seq[di];
+    if (still_running(a)) dep_a[i] = {a, to_host ? m->dev_h2d_chunk[si] : m->host_d2h_chunk[si]};
+    if (still_running(b)) dep_b[i] = {b, to_host ? m->host_h2d_chunk[di] : m->dev_d2h_chunk[di]};
+    need[i] = std::max(dep_a[i].seq, dep_b[i].seq);
   }
   cudaGetLastError();  // cudaEventQuery's "not ready" is not an error
   std::vector<size_t> order(nb);
@@ -535,25 +566,55 @@ int enqueue_transfer(ts_manager* m, bool to_host, const Plan& p, void* user_stre
 
   const int64_t nblk = int64_t(nb);
   std::vector<int64_t> dev_ids(nb), host_ids(nb);
-  std::vector<uint64_t> need_o(nb);
   for (size_t k = 0; k < nb; ++k) {
     const size_t i = order[k];
     dev_ids[k] = to_host ? p.src[i] : p.dst[i];
     host_ids[k] = to_host ? p.dst[i] : p.src[i];
-    need_o[k] = need[i];
+    (*chunk_of)[i] = int32_t(int64_t(k) / m->chunk_blocks);
   }
-  auto chunk_need = [&](int64_t c0, int64_t cn) {
-    uint64_t x = 0;
-    for (int64_t k = 0; k < cn; ++k) x = std::max(x, need_o[size_t(c0 + k)]);
-    return x;
+  // A chunk waits for the chunks of other calls that moved its blocks (or
+  // for a whole call when that call was not chunked).
+  std::set<std::pair<uint64_t, int32_t>> waited_chunks;
+  auto wait_chunk_deps = [&](int64_t c0, int64_t cn) -> int {
+    for (int64_t k = c0; k < c0 + cn; ++k) {
+      for (const Dep& d : {dep_a[order[size_t(k)]], dep_b[order[size_t(k)]]}) {
+        if (d.seq == 0 || d.seq <= waited) continue;
+        const CallRec& r = ring[d.seq % kEventRing];
+        if (r.seq != d.seq) continue;  // recycled => long done
+        if (d.chunk < 0 || size_t(d.chunk) >= r.chunk_ev.size()) {
+          int rc = wait_upto(d.seq);
+          if (rc != TS_OK) return rc;
+          continue;
+        }
+        if (!waited_chunks.insert({d.seq, d.chunk}).second) continue;
+        for (cudaStream_t s : streams)
+          TS_CUDA_RET(cudaStreamWaitEvent(s, r.chunk_ev[size_t(d.chunk)], 0),
+                      "cross-direction ordering");
+      }
+    }
+    return TS_OK;
+  };
+  auto record_chunk = [&](int64_t ci, cudaStream_t s) -> int {
+    while (own.chunk_ev.size() <= size_t(ci)) {
+      cudaEvent_t e = nullptr;
+      TS_CUDA_RET(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event create");
+      own.chunk_ev.push_back(e);
+    }
+    TS_CUDA_RET(cudaEventRecord(own.chunk_ev[size_t(ci)], s), "event record");
+    return TS_OK;
   };
   std::vector<Slot>& slots = to_host ? m->out_slots : m->in_slots;
   int& next = to_host ? m->next_out : m->next_in;
   int chunk = 0;  // staged chunks issued (copy stream rotation)
   int64_t ci = 0;
+  // Direct reload chunks alternate between two kernel streams (their
+  // destinations are distinct, so they may run concurrently).
+  const bool overlap = ks2 != nullptr && !dup_dst;
+  int n_direct = 0;
+  bool used_ks2 = false;
   for (int64_t c0 = 0; c0 < nblk; c0 += m->chunk_blocks, ++ci) {
     const int64_t cn = std::min<int64_t>(m->chunk_blocks, nblk - c0);
-    int rc0 = wait_upto(chunk_need(c0, cn));
+    int rc0 = wait_chunk_deps(c0, cn);
     if (rc0 != TS_OK) return rc0;
     if (direct && !(staged_every > 0 && ci % staged_every == staged_every - 1)) {
       // the kernel moves the chunk over PCIe itself (mapped host tier)
@@ -563,14 +624,19 @@ int enqueue_transfer(ts_manager* m, bool to_host, const Plan& p, void* user_stre
         ids.v[k] = dev_ids[size_t(c0 + k)];
         ids.s[k] = host_ids[size_t(c0 + k)];
       }
-      int rc = launch_chunk(m, to_host, ids, cn, m->host_dev, err_dev, ks);
+      cudaStream_t kc = overlap && (n_direct++ & 1) ? ks2 : ks;
+      used_ks2 = used_ks2 || kc == ks2;
+      int rc = launch_chunk(m, to_host, ids, cn, m->host_dev, err_dev, kc);
+      if (rc == TS_OK) rc = record_chunk(ci, kc);
       if (rc != TS_OK) return rc;
       continue;
     }
     ++chunk;
     Slot& slot = slots[size_t(next)];
     next = (next + 1) % int(slots.size());
-    cudaStream_t cc = cs[(chunk - 1) % m->ncs];
+    // a repeated destination keeps every DMA on one copy stream, so the
+    // later copy lands last
+    cudaStream_t cc = dup_dst ? cs[0] : cs[(chunk - 1) % m->ncs];
     ParamIds ids;
     ids.direct = 0;
     for (int64_t k = 0; k < cn; ++k) ids.v[k] = dev_ids[size_t(c0 + k)];
@@ -600,12 +666,16 @@ int enqueue_transfer(ts_manager* m, bool to_host, const Plan& p, void* user_stre
     }
     if (to_host) {
       TS_CUDA_RET(cudaEventRecord(slot.free, cc), "event record");
+      int rc = record_chunk(ci, cc);
+      if (rc != TS_OK) return rc;
     } else {
       TS_CUDA_RET(cudaEventRecord(slot.ready, cc), "event record");
       TS_CUDA_RET(cudaStreamWaitEvent(ks, slot.ready, 0), "stream wait");
       int rc = launch_chunk(m, false, ids, cn, slot.buf, err_dev, ks);
       if (rc != TS_OK) return rc;
       TS_CUDA_RET(cudaEventRecord(slot.free, ks), "event record");
+      rc = record_chunk(ci, ks);
+      if (rc != TS_OK) return rc;
     }
   }
   if (to_host) {  // join the other copy streams into the completing one
@@ -614,12 +684,16 @@ int enqueue_transfer(ts_manager* m, bool to_host, const Plan& p, void* user_stre
       TS_CUDA_RET(cudaStreamWaitEvent(last, m->out_join[i], 0), "stream wait");
     }
   }
+  if (used_ks2) {
+    TS_CUDA_RET(cudaEventRecord(m->in_join, ks2), "event record");
+    TS_CUDA_RET(cudaStreamWaitEvent(last, m->in_join, 0), "stream wait");
+  }
   TS_CUDA_RET(cudaEventRecord(ev->done, last), "event record");
   return TS_OK;
 }
 
 void sync_all(ts_manager* m) {
-  for (cudaStream_t s : {m->s_out_kernel, m->s_in_kernel})
+  for (cudaStream_t s : {m->s_out_kernel, m->s_in_kernel, m->s_in_kernel2})
     if (s) cudaStreamSynchronize(s);
   for (int i = 0; i < kMaxCopyStreams; ++i) {
     if (m->out_cs[i]) cudaStreamSynchronize(m->out_cs[i]);
@@ -651,7 +725,9 @@ int submit_locked(ts_manager* m, bool to_host, const Plan& p, void* stream, ts_e
   ts_event* ev = nullptr;
   int rc = make_event(m, &ev);
   if (rc != TS_OK) return rc;
-  rc = enqueue_transfer(m, to_host, p, stream, ev);
+  const uint64_t seq = (to_host ? m->d2h_seq : m->h2d_seq) + 1;
+  std::vector<int32_t> chunk_of;
+  rc = enqueue_transfer(m, to_host, p, stream, ev, seq, &chunk_of);
   if (rc != TS_OK) {
     // Work already queued stays ordered on the manager's streams; drain it so
     // the error word can be recycled safely.
@@ -661,7 +737,7 @@ int submit_locked(ts_manager* m, bool to_host, const Plan& p, void* stream, ts_e
     return set_error(rc, msg);
   }
   cudaStream_t last = last_stream(m, to_host);
-  const uint64_t seq = to_host ? ++m->d2h_seq : ++m->h2d_seq;
+  (to_host ? m->d2h_seq : m->h2d_seq) = seq;
   rc = record_call(to_host ? m->d2h_ring : m->h2d_ring, seq, last);
   if (rc != TS_OK) {
     cudaEventSynchronize(ev->done);
@@ -669,12 +745,15 @@ int submit_locked(ts_manager* m, bool to_host, const Plan& p, void* stream, ts_e
     return rc;
   }
   for (size_t i = 0; i < p.src.size(); ++i) {
+    const size_t si = size_t(p.src[i]), di = size_t(p.dst[i]);
     if (to_host) {
-      m->dev_d2h_seq[size_t(p.src[i])] = seq;
-      m->host_d2h_seq[size_t(p.dst[i])] = seq;
+      m->dev_d2h_seq[si] = seq;
+      m->host_d2h_seq[di] = seq;
+      m->dev_d2h_chunk[si] = m->host_d2h_chunk[di] = chunk_of[i];
     } else {
-      m->host_h2d_seq[size_t(p.src[i])] = seq;
-      m->dev_h2d_seq[size_t(p.dst[i])] = seq;
+      m->host_h2d_seq[si] = seq;
+      m->dev_h2d_seq[di] = seq;
+      m->host_h2d_chunk[si] = m->dev_h2d_chunk[di] = chunk_of[i];
     }
   }
   *out = ev;
@@ -829,10 +908,13 @@ void destroy_resources(ts_manager* m) {
       if (sl.free) cudaEventDestroy(sl.free);
     }
   for (CallRec* ring : {m->d2h_ring, m->h2d_ring})
-    for (int i = 0; i < kEventRing; ++i)
+    for (int i = 0; i < kEventRing; ++i) {
       if (ring[i].done) cudaEventDestroy(ring[i].done);
-  for (cudaStream_t s : {m->s_out_kernel, m->s_in_kernel})
+      for (cudaEvent_t e : ring[i].chunk_ev) cudaEventDestroy(e);
+    }
+  for (cudaStream_t s : {m->s_out_kernel, m->s_in_kernel, m->s_in_kernel2})
     if (s) cudaStreamDestroy(s);
+  if (m->in_join) cudaEventDestroy(m->in_join);
   for (int i = 0; i < kMaxCopyStreams; ++i) {
     if (m->out_cs[i]) cudaStreamDestroy(m->out_cs[i]);
     if (m->in_cs[i]) cudaStreamDestroy(m->in_cs[i]);
@@ -884,6 +966,12 @@ extern "C" int ts_mgr_create(const ts_storage_desc* storages, int num_layers,
   m->max_ctas = opts && opts->max_ctas > 0 ? opts->max_ctas : 0;
   m->reload_staged_every = opts && opts->reload_staged_every > 0 && (m->mode & 2)
                                ? opts->reload_staged_every : 0;
+  m->sched = opts ? opts->sched : 0;
+  if (m->sched < 0 || m->sched > (TS_SCHED_OFFLOAD_PRIORITY | TS_SCHED_RELOAD_PER_PIECE |
+                                  TS_SCHED_RELOAD_OVERLAP)) {
+    delete m;
+    return set_error(TS_INVALID_ARGUMENT, "sched must be a sum of TS_SCHED_* flags");
+  }
   const int n = num_layers * num_shards;
   m->st.resize(size_t(n));
   // reference: slice_byte_size from layer 0, shard 0 (GetMajorSliceByteSize)
@@ -964,10 +1052,17 @@ extern "C" int ts_mgr_create(const ts_storage_desc* storages, int num_layers,
                    cudaMemcpyHostToDevice);
   if (e != cudaSuccess) return fail(tsb::cuda_error(e, "storage table upload"));
 
-  for (cudaStream_t* s : {&m->s_out_kernel, &m->s_in_kernel}) {
-    e = cudaStreamCreateWithFlags(s, cudaStreamNonBlocking);
-    if (e != cudaSuccess) return fail(tsb::cuda_error(e, "stream create"));
+  int prio_least = 0, prio_greatest = 0;
+  e = cudaDeviceGetStreamPriorityRange(&prio_least, &prio_greatest);
+  if (e != cudaSuccess) return fail(tsb::cuda_error(e, "stream priority range"));
+  const int out_prio = (m->sched & TS_SCHED_OFFLOAD_PRIORITY) ? prio_greatest : prio_least;
+  e = cudaStreamCreateWithPriority(&m->s_out_kernel, cudaStreamNonBlocking, out_prio);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&m->s_in_kernel, cudaStreamNonBlocking);
+  if (e == cudaSuccess && (m->sched & TS_SCHED_RELOAD_OVERLAP)) {
+    e = cudaStreamCreateWithFlags(&m->s_in_kernel2, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&m->in_join, cudaEventDisableTiming);
   }
+  if (e != cudaSuccess) return fail(tsb::cuda_error(e, "stream create"));
   for (int i = 0; i < m->ncs; ++i) {
     e = cudaStreamCreateWithFlags(&m->out_cs[i], cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&m->in_cs[i], cudaStreamNonBlocking);
@@ -998,6 +1093,10 @@ extern "C" int ts_mgr_create(const ts_storage_desc* storages, int num_layers,
   m->host_h2d_seq.assign(size_t(m->host_blocks), 0);
   m->dev_d2h_seq.assign(size_t(max_dev_blocks), 0);
   m->dev_h2d_seq.assign(size_t(max_dev_blocks), 0);
+  m->host_d2h_chunk.assign(size_t(m->host_blocks), -1);
+  m->host_h2d_chunk.assign(size_t(m->host_blocks), -1);
+  m->dev_d2h_chunk.assign(size_t(max_dev_blocks), -1);
+  m->dev_h2d_chunk.assign(size_t(max_dev_blocks), -1);
   *out = m;
   return TS_OK;
 }
@@ -1215,12 +1314,28 @@ extern "C" int ts_mgr_kernel_stats(ts_manager* mgr, int which, int64_t* launches
   double ms = 0;
   uint64_t b = 0;
   std::vector<cudaEvent_t>& ev = mgr->prof_ev[which];
+  // Launch intervals relative to the first launch's start; their union is
+  // the time the kernels ran (launches on two streams may overlap).
+  std::vector<std::pair<double, double>> iv;
   for (size_t i = 0; i + 1 < ev.size(); i += 2) {
     TS_CUDA_RET(cudaEventSynchronize(ev[i + 1]), "profiling event");
-    float t = 0;
-    TS_CUDA_RET(cudaEventElapsedTime(&t, ev[i], ev[i + 1]), "profiling event");
-    ms += t;
+    float t0 = 0, t1 = 0;
+    if (i > 0) TS_CUDA_RET(cudaEventElapsedTime(&t0, ev[0], ev[i]), "profiling event");
+    TS_CUDA_RET(cudaEventElapsedTime(&t1, ev[0], ev[i + 1]), "profiling event");
+    iv.emplace_back(double(t0), double(t1));
   }
+  std::sort(iv.begin(), iv.end());
+  double cur0 = 0, cur1 = -1;
+  for (const auto& x : iv) {
+    if (x.first > cur1) {
+      if (cur1 > cur0) ms += cur1 - cur0;
+      cur0 = x.first;
+      cur1 = x.second;
+    } else if (x.second > cur1) {
+      cur1 = x.second;
+    }
+  }
+  if (cur1 > cur0) ms += cur1 - cur0;
   for (uint64_t x : mgr->prof_bytes[which]) b += x;
   if (launches) *launches = int64_t(ev.size() / 2);
   if (total_ms) *total_ms = ms;

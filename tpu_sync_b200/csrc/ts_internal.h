@@ -39,7 +39,8 @@ struct ParamIds {
 };
 
 // Chunk launchers of kv_block_kernels.cu used by the manager.  max_ctas caps
-// the grid (0 = a full wave of every SM).
+// the grid (0 = a full wave of every SM); max_ctas < 0 launches one CTA per
+// work item (16 KiB piece) instead of a persistent grid (plain copies only).
 int mgr_extract(int device, const ts_block_storage* d_st, int n_st,
                 const ParamIds& ids, int64_t n_blocks, void* staging,
                 uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,

@@ -155,6 +155,7 @@ class KVCacheManager:
       copy_streams: int = 2,
       max_ctas: int = 0,
       reload_staged_every: int = 0,
+      sched: Sequence[str] = (),
   ):
     if host_blocks_to_allocate is None:
       if max_blocks is None or num_slots is None:
@@ -193,11 +194,20 @@ class KVCacheManager:
     modes = {"staged": 0, "direct_d2h": 1, "direct_h2d": 2, "direct": 3}
     if mode not in modes:
       raise ValueError(f"mode must be one of {sorted(modes)}")
+    flags = {"offload_priority": _native.SCHED_OFFLOAD_PRIORITY,
+             "reload_per_piece": _native.SCHED_RELOAD_PER_PIECE,
+             "reload_overlap": _native.SCHED_RELOAD_OVERLAP}
+    if isinstance(sched, str):
+      sched = (sched,)
+    unknown = [f for f in sched if f not in flags]
+    if unknown:
+      raise ValueError(f"sched flags must be among {sorted(flags)}, got {unknown}")
     opts = _native.ManagerOpts(
         host_blocks=int(host_blocks_to_allocate), chunk_blocks=int(chunk_blocks),
         shm_name=shm_name.encode(), model_uid=model_uid.encode(), fp8=int(fp8),
         mode=modes[mode], copy_streams=int(copy_streams),
-        max_ctas=int(max_ctas), reload_staged_every=int(reload_staged_every))
+        max_ctas=int(max_ctas), reload_staged_every=int(reload_staged_every),
+        sched=sum(flags[f] for f in set(sched)))
     handle = ctypes.c_void_p()
     rc = _native.lib().ts_mgr_create(descs, self.num_layers, self.num_shards,
                                      ctypes.byref(opts), ctypes.byref(handle))
