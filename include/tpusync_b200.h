@@ -344,7 +344,10 @@ typedef struct ts_block_storage {
  * Replaces the per-(storage, run) DMA loop of DispatchD2hWork
  * (tpu_sync/kv_cache/kv_cache_manager_base.cc:2036-2124) on the device side.
  * `err_flag` (device or host-mapped int, may be 0) receives 1 when an id is
- * out of the storage's bounds (that block is skipped). */
+ * out of the storage's bounds (that block is skipped).  The table is read on
+ * the device only (the kernel scans it for block sizes and alignment), so
+ * the call queues its kernel on `stream` and returns without waiting for the
+ * device. */
 TS_API int ts_kv_extract(int device, const ts_block_storage* d_storages, int n_storages,
                   const int64_t* d_ids, int64_t n_blocks, void* d_staging,
                   uint64_t stage_pitch, int* err_flag, void* stream);
@@ -359,7 +362,11 @@ TS_API int ts_kv_insert(int device, const ts_block_storage* d_storages, int n_st
  * storage) one fp32 scale = absmax/448 (1 if absmax is 0) is written to
  * staging[k*stage_pitch + scale_off + 4*s] and the payload
  * e4m3_rn_satfinite(x / scale) to staging[k*stage_pitch + st[s].stage_off ...]
- * (block_bytes/2 bytes).  No reference counterpart (new in this build). */
+ * (block_bytes/2 bytes).  No reference counterpart (new in this build).
+ * pitch, staging and scale_off alignment is checked on the host
+ * (TS_INVALID_ARGUMENT); a storage whose address, block bytes or stage offset
+ * is not a multiple of 16 is found by the kernel, which then sets *err_flag
+ * to 2 and moves nothing. */
 TS_API int ts_kv_extract_fp8(int device, const ts_block_storage* d_storages,
                       int n_storages, const int64_t* d_ids, int64_t n_blocks,
                       void* d_staging, uint64_t stage_pitch, uint64_t scale_off,
@@ -378,14 +385,20 @@ TS_API int ts_kv_insert_fp8(int device, const ts_block_storage* d_storages,
  * No counterpart in the reference.  For k < n_blocks and every storage s:
  *   host_dst[dst_ids[k]*host_pitch + st[s].stage_off + b] = storage s block
  *   src_ids[k], byte b
- * (the block-major layout of the manager's host tier).  src_ids / dst_ids are
- * HOST arrays; host_dst is pinned (or registered) host memory of host_blocks
- * blocks.  Staging is a file-scope device array of 64 MiB: host_pitch above
- * that is rejected (TS_OUT_OF_RANGE).  Allocates nothing; everything is
- * queued on `stream` (synchronise it to know the copy landed).  The first
- * call on a device looks up the array's device address (make it before any
- * stream capture); calls that overlap on the GPU race on the shared array. */
-TS_API int ts_kv_offload_noalloc(int device, const ts_block_storage* d_storages,
+ * (the block-major layout of the manager's host tier; bytes of a host block
+ * that no storage slot covers are written as zeros).  `storages` is a HOST
+ * array of at most 512 entries (passed to the gather kernel by value), and
+ * src_ids / dst_ids are HOST arrays: every check (slots inside the pitch, ids
+ * against the storages and host_blocks) is made on the host before anything
+ * is queued, and nothing is read back from the device, so the call returns
+ * without waiting for it.  host_dst is pinned (or registered) host memory of
+ * host_blocks blocks.  Staging is a file-scope device array of 64 MiB: a
+ * host_pitch above that is rejected (TS_OUT_OF_RANGE).  Allocates nothing;
+ * everything is queued on `stream` (synchronise it to know the copy landed).
+ * Each call looks up the array's device address (the first lookup on a device
+ * also loads this library's device code there); the array is shared, so
+ * calls that overlap on the GPU (other streams) race on it. */
+TS_API int ts_kv_offload_noalloc(int device, const ts_block_storage* storages,
                                  int n_storages, const int64_t* src_ids,
                                  const int64_t* dst_ids, int64_t n_blocks,
                                  void* host_dst, uint64_t host_pitch,

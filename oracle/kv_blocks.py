@@ -218,10 +218,12 @@ def staging_layout(block_bytes: Sequence[int], fp8: bool = False):
   return offs, scale_off, (off + 15) // 16 * 16
 
 
-def extract_to_padded_staging(storages, ids) -> np.ndarray:
-  """extract_to_staging with the kernel's 16-byte aligned slot layout."""
+def extract_to_padded_staging(storages, ids, offs=None, pitch=None) -> np.ndarray:
+  """extract_to_staging with the kernel's 16-byte aligned slot layout, or
+  with the given slot offsets and pitch; bytes no slot covers are zero."""
   bbs = [st.reshape(st.shape[0], -1).shape[1] for st in storages]
-  offs, _, pitch = staging_layout(bbs)
+  if offs is None:
+    offs, _, pitch = staging_layout(bbs)
   out = np.zeros((len(ids), pitch), np.uint8)
   ids = np.asarray(ids, dtype=np.int64)
   for st, off, bb in zip(storages, offs, bbs):

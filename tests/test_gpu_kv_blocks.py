@@ -94,6 +94,76 @@ def test_out_of_bounds_id_sets_error_flag(cuda):
                                 ref.extract_to_padded_staging([u8(t) for t in pool], [1])[0])
 
 
+def test_manager_free_calls_queue_without_blocking(cuda):
+  """ts_kv_extract / ts_kv_insert and their fp8 variants read nothing back
+  from the device: queued behind ~0.5 s of GPU work on their stream, two
+  calls of each return at once, and the copies land exactly once the stream
+  drains."""
+  geom = workloads.KVGeometry(layers=2, kv=2, block_tokens=16, heads=8, head_dim=128)
+  pool = small_pool(geom, 48, 17, cuda)
+  host_pool = [u8(t) for t in pool]
+  ids_a = torch.tensor([3, 40, 7, 0], dtype=torch.int64, device=cuda)
+  ids_b = torch.tensor([11, 12, 47], dtype=torch.int64, device=cuda)
+  table = ops.StorageTable(pool)
+  ftable = ops.StorageTable(pool, fp8=True)
+  sa, sb = table.new_staging(4), table.new_staging(3)
+  fa, fb = ftable.new_staging(4), ftable.new_staging(3)
+  err = torch.zeros(1, dtype=torch.int32, device=cuda)
+  dst = [torch.empty_like(t) for t in pool]
+  dtable = ops.StorageTable(dst)
+  stream = torch.cuda.Stream(cuda)
+  torch.cuda.synchronize()
+  with torch.cuda.stream(stream):
+    torch.cuda._sleep(1_000_000_000)  # ~0.5 s at the B200's clocks
+  import time
+  t0 = time.perf_counter()
+  for ids, stg, fstg in ((ids_a, sa, fa), (ids_b, sb, fb)):
+    ops.kv_extract(table, ids, stg, err_flag=err, stream=stream)
+    ops.kv_extract(ftable, ids, fstg, err_flag=err, stream=stream)
+    ops.kv_insert(dtable, ids, stg, err_flag=err, stream=stream)
+  host_s = time.perf_counter() - t0
+  assert stream.query() is False  # the sleep is still running
+  assert host_s < 0.1, f"calls blocked the host for {host_s:.3f} s"
+  stream.synchronize()
+  assert int(err.item()) == 0
+  for ids, stg, fstg in ((ids_a, sa, fa), (ids_b, sb, fb)):
+    idl = ids.tolist()
+    np.testing.assert_array_equal(stg.cpu().numpy(), ref.extract_to_padded_staging(host_pool, idl))
+    (payload, _), _ = fp8_oracle(pool, idl)
+    fs = fstg.cpu().numpy()
+    for k in range(len(pool)):
+      off = ftable.stage_offs[k]
+      np.testing.assert_array_equal(fs[:, off:off + payload.shape[2]], payload[:, k])
+    for t, d in zip(pool, dst):
+      for i in idl:
+        assert torch.equal(t[i], d[i])
+
+
+def test_fp8_misaligned_table_sets_error_flag(cuda):
+  """A storage whose address is not 16-byte aligned cannot take the fp8
+  kernels' 16-byte vectors: the kernel reports it as *err_flag = 2 and moves
+  nothing (the table is checked on the device, not read back)."""
+  geom = workloads.KVGeometry(layers=1, kv=2, block_tokens=64, heads=1, head_dim=128)
+  good = small_pool(geom, 8, 5, cuda)
+  raw = torch.zeros(8 * 64 * 128 + 1, dtype=torch.bfloat16, device=cuda)
+  bad = raw[1:].view(8, 64, 1, 128)  # address 2 bytes past an aligned one
+  bad.copy_(good[1])
+  table = ops.StorageTable([good[0], bad], fp8=True)
+  staging = table.new_staging(2)
+  staging.fill_(0x33)
+  err = torch.zeros(1, dtype=torch.int32, device=cuda)
+  ops.kv_extract(table, [1, 4], staging, err_flag=err)
+  torch.cuda.synchronize()
+  assert int(err.item()) == 2
+  assert (staging.cpu().numpy() == 0x33).all()
+  err.zero_()
+  before = [t.clone() for t in (good[0], bad)]
+  ops.kv_insert(table, [1, 4], staging, err_flag=err)
+  torch.cuda.synchronize()
+  assert int(err.item()) == 2
+  assert torch.equal(before[0], good[0]) and torch.equal(before[1], bad)
+
+
 # ---------------------------------------------------------------------------
 # fp8 fused cast
 # ---------------------------------------------------------------------------

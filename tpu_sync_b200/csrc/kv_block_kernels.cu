@@ -134,6 +134,85 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 // ---------------------------------------------------------------------------
+// Manager-free entry points with a device-resident storage table: every CTA
+// first scans the (small, L2-resident) table for the largest block and for
+// 16-byte alignment, so the host never reads the table back (no blocking
+// copy on the launch path).
+// ---------------------------------------------------------------------------
+
+struct TableScan {
+  uint64_t max_bb;
+  bool aligned;  // every dev_ptr, block_bytes, stage_off (and pitch, staging) % 16 == 0
+};
+
+__device__ __forceinline__ TableScan scan_table(const ts_block_storage* __restrict__ st,
+                                                int n_st, uint64_t extra_align) {
+  __shared__ unsigned long long s_max;
+  __shared__ int s_bad;
+  if (threadIdx.x == 0) {
+    s_max = 0;
+    s_bad = (extra_align & 15u) != 0;
+  }
+  __syncthreads();
+  unsigned long long m = 0;
+  int bad = 0;
+  for (int i = threadIdx.x; i < n_st; i += blockDim.x) {
+    const ts_block_storage e = st[i];
+    m = e.block_bytes > m ? e.block_bytes : m;
+    bad |= ((e.dev_ptr | e.block_bytes | e.stage_off) & 15u) != 0;
+  }
+  if (m) atomicMax(&s_max, m);
+  if (bad) atomicOr(&s_bad, 1);
+  __syncthreads();
+  return TableScan{s_max, s_bad == 0};
+}
+
+template <bool kToStaging>
+__global__ void __launch_bounds__(kThreads)
+    block_copy_scan_kernel(const ts_block_storage* __restrict__ st, int n_st,
+                           const int64_t* __restrict__ d_ids, int64_t n_blocks,
+                           uint8_t* staging, uint64_t pitch, int* err_flag) {
+  const TableScan t = scan_table(st, n_st, pitch | reinterpret_cast<uint64_t>(staging));
+  const uint32_t ppu = uint32_t((t.max_bb + kPieceBytes - 1) / kPieceBytes);
+  const int64_t items = n_blocks * int64_t(n_st) * ppu;
+  const DevIds ids{d_ids};
+  for (int64_t w = blockIdx.x; w < items; w += gridDim.x) {
+    Unit u;
+    if (!resolve(st, n_st, ids, staging, pitch, ppu, w, err_flag, &u)) continue;
+    const uint8_t* src = kToStaging ? u.dev : u.stg;
+    uint8_t* dst = kToStaging ? u.stg : u.dev;
+    if (t.aligned) {  // uniform per CTA
+      const int nvec = int(u.nbytes >> 4);
+      int4 v[kVecPerThread];
+#pragma unroll
+      for (int i = 0; i < kVecPerThread; ++i) {
+        const int idx = threadIdx.x + i * kThreads;
+        if (idx < nvec) v[i] = ld_stream(src + (uint64_t(idx) << 4));
+      }
+#pragma unroll
+      for (int i = 0; i < kVecPerThread; ++i) {
+        const int idx = threadIdx.x + i * kThreads;
+        if (idx < nvec) st_vec(dst + (uint64_t(idx) << 4), v[i]);
+      }
+    } else {
+      for (uint64_t b = threadIdx.x; b < u.nbytes; b += kThreads) dst[b] = src[b];
+    }
+  }
+}
+
+// The fp8 kernels of the manager-free entry points check the table before
+// touching anything: a storage that is not 16-byte aligned sets *err_flag to
+// 2 (first CTA) and no CTA moves a byte.
+__device__ __forceinline__ bool fp8_table_ok(const ts_block_storage* __restrict__ st, int n_st,
+                                             int check, int* err_flag) {
+  if (!check) return true;
+  const TableScan t = scan_table(st, n_st, 0);
+  if (!t.aligned && blockIdx.x == 0 && threadIdx.x == 0 && err_flag != nullptr)
+    *reinterpret_cast<volatile int*>(err_flag) = 2;
+  return t.aligned;
+}
+
+// ---------------------------------------------------------------------------
 // fp8 e4m3 fused cast.  One CTA per (block, storage) unit of bf16 values.
 // scale = amax / 448 (IEEE round-to-nearest division; 1 when amax == 0),
 // q = cvt.rn.satfinite.e4m3(x / scale) with x / scale an IEEE RN division,
@@ -348,9 +427,10 @@ __global__ void __launch_bounds__(T, fp8_extract_ctas_per_sm(V, T))
     extract_fp8_kernel(const ts_block_storage* __restrict__ st, int n_st,
                        const __grid_constant__ Ids ids, int64_t n_blocks,
                        uint8_t* staging, uint64_t pitch, uint64_t scale_off,
-                       int* err_flag) {
+                       int* err_flag, int check) {
   constexpr int kThreads = T;
   __shared__ float red[T / 32];
+  if (!fp8_table_ok(st, n_st, check, err_flag)) return;
   for (UnitWalk u(n_st); u.k < n_blocks; u.next()) {
     const int s = u.s;
     int64_t k;
@@ -416,8 +496,9 @@ __global__ void __launch_bounds__(T, T == 128 ? 16 : 8)
     insert_fp8_kernel(const ts_block_storage* __restrict__ st, int n_st,
                       const __grid_constant__ Ids ids, int64_t n_blocks,
                       const uint8_t* staging, uint64_t pitch, uint64_t scale_off,
-                      int* err_flag) {
+                      int* err_flag, int check) {
   constexpr int kThreads = T, kVecPerThread = VPT;
+  if (!fp8_table_ok(st, n_st, check, err_flag)) return;
   for (UnitWalk u(n_st); u.k < n_blocks; u.next()) {
     const int s = u.s;
     int64_t k;
@@ -455,6 +536,8 @@ int launch_grid(int device, int64_t items, int max_ctas = 0) {
   return int(items < cap ? items : cap);
 }
 
+// Manager chunks: storage table inspected on the host when the manager was
+// created (vec_ok, max_block_bytes).
 template <bool kToStaging, typename Ids>
 int block_copy(int device, const ts_block_storage* d_st, int n_st,
                const Ids& d_ids, int64_t n_blocks, uint8_t* staging,
@@ -478,55 +561,29 @@ int block_copy(int device, const ts_block_storage* d_st, int n_st,
   return TS_OK;
 }
 
-// Reads the device storage table back to decide alignment and piece count.
-int inspect_storages(const ts_block_storage* d_st, int n_st, uint64_t pitch,
-                     const void* staging, bool* vec_ok, uint64_t* max_bb) {
-  if (n_st < 0) return set_error(TS_INVALID_ARGUMENT, "n_storages must be >= 0");
-  ts_block_storage h[512];
-  *vec_ok = aligned16(pitch) && aligned16(reinterpret_cast<uint64_t>(staging));
-  *max_bb = 0;
-  for (int base = 0; base < n_st; base += 512) {
-    const int n = n_st - base < 512 ? n_st - base : 512;
-    TS_CUDA_RET(cudaMemcpy(h, d_st + base, sizeof(ts_block_storage) * n,
-                           cudaMemcpyDeviceToHost),
-                "read storage table");
-    for (int i = 0; i < n; ++i) {
-      *vec_ok = *vec_ok && aligned16(h[i].dev_ptr) && aligned16(h[i].block_bytes) &&
-                aligned16(h[i].stage_off);
-      if (h[i].block_bytes > *max_bb) *max_bb = h[i].block_bytes;
-    }
-  }
+// Device-table entry points: the kernel scans the table itself.  The grid
+// is a full wave, or 8 CTAs per (block, storage) unit when that is fewer.
+template <bool kToStaging>
+int block_copy_scan(int device, const ts_block_storage* d_st, int n_st, const int64_t* d_ids,
+                    int64_t n_blocks, uint8_t* staging, uint64_t pitch, int* err_flag,
+                    cudaStream_t s) {
+  DeviceGuard g(device);
+  const int grid = launch_grid(device, n_blocks * int64_t(n_st) * 8);
+  block_copy_scan_kernel<kToStaging><<<grid, kThreads, 0, s>>>(d_st, n_st, d_ids, n_blocks,
+                                                               staging, pitch, err_flag);
+  TS_CUDA_RET(cudaGetLastError(), "block copy launch");
   return TS_OK;
 }
 
-
-// Launchers used by the manager and the C entry points (storage table
-// already inspected on the host).
-template <typename Ids>
-int launch_extract(int device, const ts_block_storage* d_st, int n_st,
-                   const Ids& ids, int64_t n_blocks, void* staging,
-                   uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
-                   uint64_t max_bb, int max_ctas = 0) {
-  return block_copy<true>(device, d_st, n_st, ids, n_blocks,
-                          static_cast<uint8_t*>(staging), pitch, err_flag, s,
-                          vec_ok, max_bb, max_ctas);
-}
-
-template <typename Ids>
-int launch_insert(int device, const ts_block_storage* d_st, int n_st,
-                  const Ids& ids, int64_t n_blocks, const void* staging,
-                  uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
-                  uint64_t max_bb, int max_ctas = 0) {
-  return block_copy<false>(device, d_st, n_st, ids, n_blocks,
-                           static_cast<uint8_t*>(const_cast<void*>(staging)),
-                           pitch, err_flag, s, vec_ok, max_bb, max_ctas);
-}
-
+// fp8 launchers.  max_bb picks the kernel shape only (units <= 16 KiB run on
+// 128-thread CTAs); every shape handles every unit size.  check = 1 makes
+// the kernel validate the table's alignment first (device-table entry
+// points; the manager validated its table when it was created).
 template <typename Ids>
 int launch_extract_fp8(int device, const ts_block_storage* d_st, int n_st,
                        const Ids& ids, int64_t n_blocks, void* staging,
                        uint64_t pitch, uint64_t scale_off, int* err_flag,
-                       cudaStream_t s, uint64_t max_bb, int max_ctas = 0) {
+                       cudaStream_t s, uint64_t max_bb, int max_ctas, int check) {
   if (n_blocks == 0 || n_st == 0) return TS_OK;
   DeviceGuard g(device);
   uint8_t* stg = static_cast<uint8_t*>(staging);
@@ -540,10 +597,10 @@ int launch_extract_fp8(int device, const ts_block_storage* d_st, int n_st,
   const int grid = int(units < cap ? units : cap);
   if (narrow)
     extract_fp8_kernel<Ids, 8, 128><<<grid, 128, 0, s>>>(d_st, n_st, ids, n_blocks, stg, pitch,
-                                                         scale_off, err_flag);
+                                                         scale_off, err_flag, check);
   else
     extract_fp8_kernel<Ids, 8><<<grid, kThreads, 0, s>>>(d_st, n_st, ids, n_blocks, stg, pitch,
-                                                         scale_off, err_flag);
+                                                         scale_off, err_flag, check);
   TS_CUDA_RET(cudaGetLastError(), "extract_fp8 launch");
   return TS_OK;
 }
@@ -552,7 +609,7 @@ template <typename Ids>
 int launch_insert_fp8(int device, const ts_block_storage* d_st, int n_st,
                       const Ids& ids, int64_t n_blocks, const void* staging,
                       uint64_t pitch, uint64_t scale_off, int* err_flag,
-                      cudaStream_t s, uint64_t max_bb, int max_ctas = 0) {
+                      cudaStream_t s, uint64_t max_bb, int max_ctas, int check) {
   if (n_blocks == 0 || n_st == 0) return TS_OK;
   DeviceGuard g(device);
   const uint8_t* stg = static_cast<const uint8_t*>(staging);
@@ -562,14 +619,22 @@ int launch_insert_fp8(int device, const ts_block_storage* d_st, int n_st,
     if (max_ctas > 0 && max_ctas < cap) cap = max_ctas;
     const int grid = int(units < cap ? units : cap);
     insert_fp8_kernel<Ids, 8, 128><<<grid, 128, 0, s>>>(d_st, n_st, ids, n_blocks, stg, pitch,
-                                                         scale_off, err_flag);
+                                                         scale_off, err_flag, check);
   } else {
     const int grid = launch_grid(device, units, max_ctas);
     insert_fp8_kernel<Ids><<<grid, kThreads, 0, s>>>(d_st, n_st, ids, n_blocks, stg, pitch,
-                                                     scale_off, err_flag);
+                                                     scale_off, err_flag, check);
   }
   TS_CUDA_RET(cudaGetLastError(), "insert_fp8 launch");
   return TS_OK;
+}
+
+// Block bytes of an fp8 table's storages, estimated from its staging pitch
+// (sum of 16-byte-rounded halves plus the scale words): exact for equal
+// storages, and used only to pick a kernel shape.
+uint64_t fp8_block_bytes_hint(int n_st, uint64_t pitch, uint64_t scale_off) {
+  const uint64_t payload = scale_off < pitch ? scale_off : pitch;
+  return n_st > 0 ? 2 * (payload / uint64_t(n_st)) : 0;
 }
 
 }  // namespace
@@ -581,9 +646,9 @@ int mgr_extract(int device, const ts_block_storage* d_st, int n_st,
                 uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas) {
   if (fp8)
     return launch_extract_fp8(device, d_st, n_st, ids, n_blocks, staging, pitch,
-                              scale_off, err_flag, s, max_bb, max_ctas);
-  return launch_extract(device, d_st, n_st, ids, n_blocks, staging, pitch,
-                        err_flag, s, vec_ok, max_bb, max_ctas);
+                              scale_off, err_flag, s, max_bb, max_ctas, 0);
+  return block_copy<true>(device, d_st, n_st, ids, n_blocks, static_cast<uint8_t*>(staging),
+                          pitch, err_flag, s, vec_ok, max_bb, max_ctas);
 }
 
 int mgr_insert(int device, const ts_block_storage* d_st, int n_st,
@@ -592,65 +657,30 @@ int mgr_insert(int device, const ts_block_storage* d_st, int n_st,
                uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas) {
   if (fp8)
     return launch_insert_fp8(device, d_st, n_st, ids, n_blocks, staging, pitch,
-                             scale_off, err_flag, s, max_bb, max_ctas);
-  return launch_insert(device, d_st, n_st, ids, n_blocks, staging, pitch,
-                       err_flag, s, vec_ok, max_bb, max_ctas);
+                             scale_off, err_flag, s, max_bb, max_ctas, 0);
+  return block_copy<false>(device, d_st, n_st, ids, n_blocks,
+                           static_cast<uint8_t*>(const_cast<void*>(staging)), pitch, err_flag,
+                           s, vec_ok, max_bb, max_ctas);
 }
 
 }  // namespace tsb
 
 using tsb::set_error;
 
-extern "C" int ts_kv_extract(int device, const ts_block_storage* d_storages,
-                             int n_storages, const int64_t* d_ids,
-                             int64_t n_blocks, void* d_staging,
-                             uint64_t stage_pitch, int* err_flag, void* stream) {
-  tsb::clear_error();
-  if (n_blocks < 0) return set_error(TS_INVALID_ARGUMENT, "n_blocks must be >= 0");
-  if (n_blocks == 0 || n_storages == 0) return TS_OK;
-  if (!d_storages || !d_ids || !d_staging)
-    return set_error(TS_INVALID_ARGUMENT, "null pointer argument");
-  bool vec_ok;
-  uint64_t max_bb;
-  tsb::DeviceGuard g(device);
-  int rc = tsb::inspect_storages(d_storages, n_storages, stage_pitch, d_staging,
-                                 &vec_ok, &max_bb);
-  if (rc != TS_OK) return rc;
-  return tsb::launch_extract(device, d_storages, n_storages, tsb::DevIds{d_ids}, n_blocks,
-                             d_staging, stage_pitch, err_flag,
-                             reinterpret_cast<cudaStream_t>(stream), vec_ok, max_bb);
-}
-
-extern "C" int ts_kv_insert(int device, const ts_block_storage* d_storages,
-                            int n_storages, const int64_t* d_ids,
-                            int64_t n_blocks, const void* d_staging,
-                            uint64_t stage_pitch, int* err_flag, void* stream) {
-  tsb::clear_error();
-  if (n_blocks < 0) return set_error(TS_INVALID_ARGUMENT, "n_blocks must be >= 0");
-  if (n_blocks == 0 || n_storages == 0) return TS_OK;
-  if (!d_storages || !d_ids || !d_staging)
-    return set_error(TS_INVALID_ARGUMENT, "null pointer argument");
-  bool vec_ok;
-  uint64_t max_bb;
-  tsb::DeviceGuard g(device);
-  int rc = tsb::inspect_storages(d_storages, n_storages, stage_pitch, d_staging,
-                                 &vec_ok, &max_bb);
-  if (rc != TS_OK) return rc;
-  return tsb::launch_insert(device, d_storages, n_storages, tsb::DevIds{d_ids}, n_blocks,
-                            d_staging, stage_pitch, err_flag,
-                            reinterpret_cast<cudaStream_t>(stream), vec_ok, max_bb);
-}
-
 namespace {
-int check_fp8_table(const ts_block_storage* d_st, int n_st, uint64_t pitch,
-                    uint64_t scale_off, const void* staging, uint64_t* max_bb_out) {
-  bool vec_ok;
-  uint64_t max_bb;
-  int rc = tsb::inspect_storages(d_st, n_st, pitch, staging, &vec_ok, &max_bb);
-  if (max_bb_out) *max_bb_out = max_bb;
-  if (rc != TS_OK) return rc;
+int check_args(int64_t n_blocks, int n_storages, const void* d_storages, const void* d_ids,
+               const void* d_staging) {
+  if (n_blocks < 0) return set_error(TS_INVALID_ARGUMENT, "n_blocks must be >= 0");
+  if (n_storages < 0) return set_error(TS_INVALID_ARGUMENT, "n_storages must be >= 0");
+  if (n_blocks > 0 && n_storages > 0 && (!d_storages || !d_ids || !d_staging))
+    return set_error(TS_INVALID_ARGUMENT, "null pointer argument");
+  return TS_OK;
+}
+
+int check_fp8_args(uint64_t pitch, uint64_t scale_off, const void* staging) {
   // The fp8 kernels move 16 B of bf16 / 8 B of fp8 per vector.
-  if (!vec_ok || (scale_off & 3u) != 0)
+  if (!tsb::aligned16(pitch) || !tsb::aligned16(reinterpret_cast<uint64_t>(staging)) ||
+      (scale_off & 3u) != 0)
     return set_error(TS_INVALID_ARGUMENT,
                      "fp8 path needs 16-byte aligned storages, block sizes, "
                      "stage offsets and pitch, and a 4-byte aligned scale offset");
@@ -658,23 +688,46 @@ int check_fp8_table(const ts_block_storage* d_st, int n_st, uint64_t pitch,
 }
 }  // namespace
 
+extern "C" int ts_kv_extract(int device, const ts_block_storage* d_storages,
+                             int n_storages, const int64_t* d_ids,
+                             int64_t n_blocks, void* d_staging,
+                             uint64_t stage_pitch, int* err_flag, void* stream) {
+  tsb::clear_error();
+  int rc = check_args(n_blocks, n_storages, d_storages, d_ids, d_staging);
+  if (rc != TS_OK || n_blocks == 0 || n_storages == 0) return rc;
+  return tsb::block_copy_scan<true>(device, d_storages, n_storages, d_ids, n_blocks,
+                                    static_cast<uint8_t*>(d_staging), stage_pitch, err_flag,
+                                    reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ts_kv_insert(int device, const ts_block_storage* d_storages,
+                            int n_storages, const int64_t* d_ids,
+                            int64_t n_blocks, const void* d_staging,
+                            uint64_t stage_pitch, int* err_flag, void* stream) {
+  tsb::clear_error();
+  int rc = check_args(n_blocks, n_storages, d_storages, d_ids, d_staging);
+  if (rc != TS_OK || n_blocks == 0 || n_storages == 0) return rc;
+  return tsb::block_copy_scan<false>(device, d_storages, n_storages, d_ids, n_blocks,
+                                     static_cast<uint8_t*>(const_cast<void*>(d_staging)),
+                                     stage_pitch, err_flag,
+                                     reinterpret_cast<cudaStream_t>(stream));
+}
+
 extern "C" int ts_kv_extract_fp8(int device, const ts_block_storage* d_storages,
                                  int n_storages, const int64_t* d_ids,
                                  int64_t n_blocks, void* d_staging,
                                  uint64_t stage_pitch, uint64_t scale_off,
                                  int* err_flag, void* stream) {
   tsb::clear_error();
-  if (n_blocks < 0) return set_error(TS_INVALID_ARGUMENT, "n_blocks must be >= 0");
-  if (n_blocks == 0 || n_storages == 0) return TS_OK;
-  if (!d_storages || !d_ids || !d_staging)
-    return set_error(TS_INVALID_ARGUMENT, "null pointer argument");
-  tsb::DeviceGuard g(device);
-  uint64_t max_bb = 0;
-  int rc = check_fp8_table(d_storages, n_storages, stage_pitch, scale_off, d_staging, &max_bb);
+  int rc = check_args(n_blocks, n_storages, d_storages, d_ids, d_staging);
+  if (rc != TS_OK || n_blocks == 0 || n_storages == 0) return rc;
+  rc = check_fp8_args(stage_pitch, scale_off, d_staging);
   if (rc != TS_OK) return rc;
   return tsb::launch_extract_fp8(device, d_storages, n_storages, tsb::DevIds{d_ids}, n_blocks,
                                  d_staging, stage_pitch, scale_off, err_flag,
-                                 reinterpret_cast<cudaStream_t>(stream), max_bb);
+                                 reinterpret_cast<cudaStream_t>(stream),
+                                 tsb::fp8_block_bytes_hint(n_storages, stage_pitch, scale_off),
+                                 0, 1);
 }
 
 extern "C" int ts_kv_insert_fp8(int device, const ts_block_storage* d_storages,
@@ -683,15 +736,13 @@ extern "C" int ts_kv_insert_fp8(int device, const ts_block_storage* d_storages,
                                 uint64_t stage_pitch, uint64_t scale_off,
                                 int* err_flag, void* stream) {
   tsb::clear_error();
-  if (n_blocks < 0) return set_error(TS_INVALID_ARGUMENT, "n_blocks must be >= 0");
-  if (n_blocks == 0 || n_storages == 0) return TS_OK;
-  if (!d_storages || !d_ids || !d_staging)
-    return set_error(TS_INVALID_ARGUMENT, "null pointer argument");
-  tsb::DeviceGuard g(device);
-  uint64_t max_bb = 0;
-  int rc = check_fp8_table(d_storages, n_storages, stage_pitch, scale_off, d_staging, &max_bb);
+  int rc = check_args(n_blocks, n_storages, d_storages, d_ids, d_staging);
+  if (rc != TS_OK || n_blocks == 0 || n_storages == 0) return rc;
+  rc = check_fp8_args(stage_pitch, scale_off, d_staging);
   if (rc != TS_OK) return rc;
   return tsb::launch_insert_fp8(device, d_storages, n_storages, tsb::DevIds{d_ids}, n_blocks,
                                 d_staging, stage_pitch, scale_off, err_flag,
-                                reinterpret_cast<cudaStream_t>(stream), max_bb);
+                                reinterpret_cast<cudaStream_t>(stream),
+                                tsb::fp8_block_bytes_hint(n_storages, stage_pitch, scale_off),
+                                0, 1);
 }
