@@ -480,6 +480,88 @@ TS_API int ts_reshard_ce_info(ts_reshard_ce* program, int64_t* groups,
 TS_API int ts_reshard_ce_destroy(ts_reshard_ce* program);
 
 /* ------------------------------------------------------------------------ */
+/* Weight synchronizer (resharded push of controller-made schedules).        */
+/* ------------------------------------------------------------------------ */
+
+/* Replaces WeightSynchronizerBase's resharded push
+ * (tpu_sync/weight_sync/weight_synchronizer_base.cc:558-760): the trainer's
+ * [layer][shard] buffers, a registered plan of ShardPushEntry lists, and its
+ * execution as one strided-copy kernel per source GPU storing straight into
+ * the destinations (no D2H, TCP push, receiver H2D). */
+typedef struct ts_wsync ts_wsync;
+
+/* One [layer][shard] buffer of the synchronizer (the reference's host mirror
+ * of that buffer is not needed: the kernel reads the device buffer). */
+typedef struct ts_wsync_buffer {
+  uint64_t dev_ptr;  /* device address */
+  uint64_t nbytes;   /* its size (the reference's GetHostSize) */
+  int32_t device;    /* CUDA device ordinal */
+  int32_t pad_;
+} ts_wsync_buffer;
+
+/* ShardPushEntryProto (tpu_sync/rpc/raiden_service.proto:105-131) plus the
+ * map key it sits under in StartTransferRequest.shard_push_schedules. */
+typedef struct ts_shard_push_entry {
+  int32_t src_shard_idx;  /* local shard whose schedule holds the entry */
+  int32_t has_layer_idx;  /* 0: the layer named by the request's first source unit */
+  int32_t layer_idx;
+  int32_t pad_;
+  const char* dst_peer;
+  int64_t dst_shard_idx;
+  uint64_t src_offset_bytes;
+  uint64_t dst_offset_bytes;
+  uint64_t size_bytes;
+  uint64_t src_stride_bytes;
+  uint64_t dst_stride_bytes;
+  int64_t count;          /* <= 0 means 1, as in the reference */
+} ts_shard_push_entry;
+
+/* Where the bytes of (peer, layer, destination shard) go, as the source's
+ * kernels address them: its own memory, a peer GPU's memory (device >= 0:
+ * peer access is enabled by the registration), or a CUDA IPC mapping opened
+ * for the source device (device = -1). */
+typedef struct ts_wsync_dest {
+  const char* peer;
+  int64_t layer_idx;
+  int64_t dst_shard_idx;
+  uint64_t dst_ptr;
+  uint64_t nbytes;
+  int32_t device;
+  int32_t pad_;
+} ts_wsync_dest;
+
+/* num_layers x num_shards buffers, row-major [layer][shard]; layer_names may
+ * be NULL (names "0", "1", ...), as WeightSynchronizerBase's layer names. */
+TS_API int ts_wsync_create(const ts_wsync_buffer* buffers, int num_layers, int num_shards,
+                           const char* const* layer_names, ts_wsync** out);
+/* Checks every entry, in the reference's order and words (per local shard in
+ * order, its entries in order: layer index or the fallback layer named
+ * src_data_name, NULL = no source units -> "src_units list cannot be empty",
+ * unknown -> TS_NOT_FOUND "Layer name not found in WeightSynchronizer: <name>";
+ * "Layer index out of bounds: <i>"; "Push range out of bounds" per contiguous
+ * payload or per repeat), then that its destination is registered and holds
+ * its range ("No destination for peer ...", "Push destination range out of
+ * bounds"), and replaces the registered plan only if all pass.  Uploads the
+ * plan's task tables (device allocations owned by the object; a push still
+ * running on the previous plan is waited for first). */
+TS_API int ts_wsync_register_plan(ts_wsync* w, const ts_shard_push_entry* entries,
+                                  int64_t n_entries, const char* src_data_name,
+                                  const ts_wsync_dest* dests, int64_t n_dests);
+/* Queues the registered plan, ordered after the work already queued on
+ * `stream` (any device of this process; 0 = the current device's default
+ * stream): one kernel per source GPU on the object's own streams. */
+TS_API int ts_wsync_push(ts_wsync* w, void* stream);
+/* TS_OK when the last push has landed, TS_PENDING before. */
+TS_API int ts_wsync_query(ts_wsync* w);
+/* Waits for the last push (timeout_ms < 0: no limit; TS_DEADLINE_EXCEEDED). */
+TS_API int ts_wsync_wait(ts_wsync* w, int64_t timeout_ms);
+/* Makes `stream` wait on the device for the last push. */
+TS_API int ts_wsync_stream_wait(ts_wsync* w, void* stream);
+/* Tasks (one per non-empty entry) and bytes of the registered plan. */
+TS_API int ts_wsync_info(ts_wsync* w, int64_t* n_tasks, uint64_t* bytes);
+TS_API void ts_wsync_destroy(ts_wsync* w);
+
+/* ------------------------------------------------------------------------ */
 /* Paged KV relayout (disaggregated prefill -> decode hand-off).             */
 /* ------------------------------------------------------------------------ */
 

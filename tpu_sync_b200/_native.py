@@ -60,6 +60,27 @@ class BlockStorage(ctypes.Structure):
               ("dev_bytes", ctypes.c_uint64), ("stage_off", ctypes.c_uint64)]
 
 
+class WsyncBuffer(ctypes.Structure):
+  _fields_ = [("dev_ptr", ctypes.c_uint64), ("nbytes", ctypes.c_uint64),
+              ("device", ctypes.c_int32), ("pad_", ctypes.c_int32)]
+
+
+class ShardPushEntry(ctypes.Structure):
+  _fields_ = [("src_shard_idx", ctypes.c_int32), ("has_layer_idx", ctypes.c_int32),
+              ("layer_idx", ctypes.c_int32), ("pad_", ctypes.c_int32),
+              ("dst_peer", ctypes.c_char_p), ("dst_shard_idx", ctypes.c_int64),
+              ("src_offset_bytes", ctypes.c_uint64), ("dst_offset_bytes", ctypes.c_uint64),
+              ("size_bytes", ctypes.c_uint64), ("src_stride_bytes", ctypes.c_uint64),
+              ("dst_stride_bytes", ctypes.c_uint64), ("count", ctypes.c_int64)]
+
+
+class WsyncDest(ctypes.Structure):
+  _fields_ = [("peer", ctypes.c_char_p), ("layer_idx", ctypes.c_int64),
+              ("dst_shard_idx", ctypes.c_int64), ("dst_ptr", ctypes.c_uint64),
+              ("nbytes", ctypes.c_uint64), ("device", ctypes.c_int32),
+              ("pad_", ctypes.c_int32)]
+
+
 class ReshardChunk(ctypes.Structure):
   _fields_ = [("src_ptr", ctypes.c_uint64), ("dst_ptr", ctypes.c_uint64),
               ("src_off", ctypes.c_int64), ("dst_off", ctypes.c_int64),
@@ -253,6 +274,17 @@ _SIGS = {
                                              ctypes.c_int, c_i64_p]),
     "ts_reshard_copy": (ctypes.c_int, [ctypes.c_int, _V, _V, ctypes.c_int64,
                                        ctypes.c_int64, ctypes.c_int, ctypes.c_int, _V]),
+    "ts_wsync_create": (ctypes.c_int, [ctypes.POINTER(WsyncBuffer), ctypes.c_int, ctypes.c_int,
+                                       ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(_V)]),
+    "ts_wsync_register_plan": (ctypes.c_int, [_V, ctypes.POINTER(ShardPushEntry),
+                                              ctypes.c_int64, ctypes.c_char_p,
+                                              ctypes.POINTER(WsyncDest), ctypes.c_int64]),
+    "ts_wsync_push": (ctypes.c_int, [_V, _V]),
+    "ts_wsync_query": (ctypes.c_int, [_V]),
+    "ts_wsync_wait": (ctypes.c_int, [_V, ctypes.c_int64]),
+    "ts_wsync_stream_wait": (ctypes.c_int, [_V, _V]),
+    "ts_wsync_info": (ctypes.c_int, [_V, c_i64_p, c_u64_p]),
+    "ts_wsync_destroy": (None, [_V]),
     "ts_enable_peer_access": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
     "ts_ipc_open": (ctypes.c_int, [ctypes.c_int, ctypes.c_char_p, ctypes.POINTER(_V)]),
     "ts_ipc_close": (ctypes.c_int, [ctypes.c_int, _V]),

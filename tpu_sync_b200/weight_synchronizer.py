@@ -86,6 +86,7 @@ class WeightSynchronizer:
     self.layer_names = list(layer_names) if layer_names else [str(i) for i in range(len(grid))]
     self._host: Dict[Tuple[int, int], torch.Tensor] = {}
     self.auto_h2d = auto_h2d
+    self._wsync = None  # native ts_wsync of the resharded push, made on first use
 
   # -- reference properties --------------------------------------------------
   @property
@@ -163,6 +164,10 @@ class WeightSynchronizer:
     return self._endpoint
 
   def close(self) -> None:
+    w = getattr(self, "_wsync", None)
+    if w is not None:
+      _native.lib().ts_wsync_destroy(w)  # waits for a push still running
+      self._wsync = None
     ep = getattr(self, "_endpoint", None)
     if ep is not None:
       try:
@@ -290,12 +295,30 @@ class WeightSynchronizer:
 
 
   # -- controller-made byte schedules ------------------------------------------
+  def _native_wsync(self):
+    """The native synchronizer over this object's [layer][shard] buffers."""
+    if self._wsync is None:
+      L, S = self.num_layers, self.num_shards
+      bufs = (_native.WsyncBuffer * (L * S))()
+      for l, layer in enumerate(self._grid):
+        for s, t in enumerate(layer):
+          b = bufs[l * S + s]
+          b.dev_ptr, b.nbytes, b.device = t.data_ptr(), t.numel() * t.element_size(), \
+              t.device.index
+      names = (ctypes.c_char_p * L)(*[n.encode() for n in self.layer_names])
+      h = ctypes.c_void_p()
+      _native.check(_native.lib().ts_wsync_create(bufs, L, S, names, ctypes.byref(h)),
+                    "weight synchronizer: ")
+      self._wsync = h
+    return self._wsync
+
   def push_weights_resharded_entries(
       self, shard_push_schedules: Dict[int, Sequence[Dict[str, Any]]],
       destinations: Dict[Tuple[str, int, int], Any], src_data_name: Optional[str] = None,
-      stream: Optional[torch.cuda.Stream] = None) -> PushFuture:
+      stream: Optional[torch.cuda.Stream] = None) -> "EntriesPushFuture":
     """PushWeightsResharded for a schedule made by the controller
-    (StartTransferRequest.shard_push_schedules; weight_synchronizer_base.cc:558-700).
+    (StartTransferRequest.shard_push_schedules; weight_synchronizer_base.cc:558-760),
+    executed by the native synchronizer (ts_wsync_register_plan / ts_wsync_push).
 
     shard_push_schedules: local shard index -> entries, each a dict with the
       ShardPushEntryProto fields dst_peer, dst_shard_idx, src_offset_bytes,
@@ -307,81 +330,81 @@ class WeightSynchronizer:
       into it.  The bytes move unchanged (the reference's push), every entry
       with `count` repeats as one strided task of one kernel per source GPU.
 
-    Checks, in the reference's order and words (ValueError): layer index in
-    range ("Layer index out of bounds: <i>"), source range inside the
-    shard's bytes per contiguous payload or per repeat ("Push range out of
-    bounds"); a missing layer name is "Layer name not found in
-    WeightSynchronizer: <name>".  The receiver's bound becomes a check here
-    too ("Push destination range out of bounds"), so no store can leave its
-    destination.  Zero-byte entries and empty schedules push nothing.
+    The native checks keep the reference's order and words: ValueError for
+    "Layer index out of bounds: <i>", "Push range out of bounds" (source
+    range per contiguous payload or per repeat), "src_units list cannot be
+    empty", and this build's destination checks ("No destination for ...",
+    "Push destination range out of bounds"); LookupError for "Layer name not
+    found in WeightSynchronizer: <name>".  Zero-byte entries and empty
+    schedules push nothing.  A later call waits for this push before it
+    replaces the plan.
     """
-    fallback: List[Optional[int]] = []
-
-    def fallback_layer() -> int:
-      if not fallback:
-        if src_data_name is None:
-          raise ValueError("src_units list cannot be empty")
-        if src_data_name not in self.layer_names:
-          raise LookupError(f"Layer name not found in WeightSynchronizer: {src_data_name}")
-        fallback.append(self.layer_names.index(src_data_name))
-      return fallback[0]
-
-    def nbytes(t) -> int:
-      if isinstance(t, torch.Tensor):
-        return t.numel() * t.element_size()
-      return int(t.nbytes)
-
-    per_shard: Dict[int, List[Tuple]] = {}
-    for i in range(self.num_shards):
-      entries = shard_push_schedules.get(i)
-      if not entries:
-        continue
-      for e in entries:
+    entries, keep = [], []
+    for i, lst in shard_push_schedules.items():
+      for e in lst or ():
+        peer = str(e["dst_peer"]).encode()
+        keep.append(peer)
         layer = e.get("layer_idx")
-        layer = fallback_layer() if layer is None else int(layer)
-        if layer < 0 or layer >= self.num_layers:
-          raise ValueError(f"Layer index out of bounds: {layer}")
-        src = self._grid[layer][i]
-        host_size = src.numel() * src.element_size()
-        count = max(int(e.get("count", 1)), 1)
-        size = int(e.get("size_bytes", 0))
-        so, do = int(e.get("src_offset_bytes", 0)), int(e.get("dst_offset_bytes", 0))
-        ss, ds = int(e.get("src_stride_bytes", 0)), int(e.get("dst_stride_bytes", 0))
-        contiguous = count == 1 or (ss == size and ds == size)
-        if contiguous:
-          if so + count * size > host_size:
-            raise ValueError("Push range out of bounds")
-        else:
-          for c in range(count):
-            if so + c * ss + size > host_size:
-              raise ValueError("Push range out of bounds")
-        if size == 0:
-          continue
-        key = (e["dst_peer"], layer, int(e.get("dst_shard_idx", 0)))
-        if key not in destinations:
-          raise ValueError(f"No destination for peer {key[0]} layer {key[1]} shard {key[2]}")
-        dst = destinations[key]
-        dst_end = do + count * size if contiguous else do + (count - 1) * ds + size
-        if do < 0 or dst_end > nbytes(dst):
-          raise ValueError("Push destination range out of bounds")
-        if isinstance(dst, torch.Tensor) and dst.device != src.device:
-          enable_peer_access(src.device.index, dst.device.index)
-        task = (so, do, count * size, 0, 0, 1) if contiguous else (so, do, size, ss, ds, count)
-        per_shard.setdefault(i, []).append((src.data_ptr(), dst.data_ptr()) + task)
-    programs = []
-    last_event = None
-    for i, chunks in per_shard.items():
-      device = self._grid[0][i].device
-      s = stream if stream is not None else torch.cuda.current_stream(device)
-      prog = ops.ReshardProgram(chunks, torch.uint8, torch.uint8, device)
-      prog.launch(s)
-      programs.append(prog)
-      last_event = torch.cuda.Event()
-      last_event.record(s)
-    if last_event is None:
-      last_event = torch.cuda.Event()
-      last_event.record()
-    return PushFuture(last_event, programs)
+        entries.append(_native.ShardPushEntry(
+            src_shard_idx=int(i), has_layer_idx=int(layer is not None),
+            layer_idx=int(layer) if layer is not None else 0, dst_peer=peer,
+            dst_shard_idx=int(e.get("dst_shard_idx", 0)),
+            src_offset_bytes=int(e.get("src_offset_bytes", 0)),
+            dst_offset_bytes=int(e.get("dst_offset_bytes", 0)),
+            size_bytes=int(e.get("size_bytes", 0)),
+            src_stride_bytes=int(e.get("src_stride_bytes", 0)),
+            dst_stride_bytes=int(e.get("dst_stride_bytes", 0)),
+            count=int(e.get("count", 1))))
+    dests = []
+    for (peer, layer, shard), t in destinations.items():
+      pb = str(peer).encode()
+      keep.append(pb)
+      if isinstance(t, torch.Tensor):
+        nbytes, device = t.numel() * t.element_size(), t.device.index
+      else:  # PeerBuffer: an IPC mapping already opened for the source device
+        nbytes, device = int(t.nbytes), -1
+      dests.append(_native.WsyncDest(peer=pb, layer_idx=int(layer), dst_shard_idx=int(shard),
+                                     dst_ptr=t.data_ptr(), nbytes=nbytes, device=device))
+    e_arr = (_native.ShardPushEntry * max(len(entries), 1))(*entries)
+    d_arr = (_native.WsyncDest * max(len(dests), 1))(*dests)
+    w = self._native_wsync()
+    name = src_data_name.encode() if src_data_name is not None else None
+    rc = _native.lib().ts_wsync_register_plan(w, e_arr, len(entries), name, d_arr, len(dests))
+    if rc != _native.OK:
+      msg = _native.last_error()
+      if rc == _native.NOT_FOUND:
+        raise LookupError(msg)
+      if rc == _native.INVALID_ARGUMENT:
+        raise ValueError(msg)
+      raise RuntimeError(msg)
+    s = stream if stream is not None else torch.cuda.current_stream(self._grid[0][0].device)
+    _native.check(_native.lib().ts_wsync_push(w, ctypes.c_void_p(s.cuda_stream)),
+                  "weight push: ")
+    del keep
+    return EntriesPushFuture(w)
+
+
+class EntriesPushFuture:
+  """Completion of a push of the native synchronizer (its latest push)."""
+
+  def __init__(self, wsync):
+    self._w = wsync
+
+  def is_ready(self) -> bool:
+    rc = _native.lib().ts_wsync_query(self._w)
+    if rc not in (_native.OK, _native.PENDING):
+      raise RuntimeError(_native.last_error())
+    return rc == _native.OK
+
+  def Await(self, timeout_ms: int = -1) -> None:
+    _native.check(_native.lib().ts_wsync_wait(self._w, int(timeout_ms)), "weight push: ")
+
+  wait = Await
+
+  def stream_wait(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+    s = stream or torch.cuda.current_stream()
+    _native.check(_native.lib().ts_wsync_stream_wait(self._w, ctypes.c_void_p(s.cuda_stream)),
+                  "weight push: ")
 
 
 class PeerBuffer:
