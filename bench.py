@@ -482,6 +482,47 @@ def measure_pcie(torch, device, nbytes=GIB):
   return out
 
 
+def c4_shards_exact(torch, device, params, half, d, flat):
+  """Sampler d's bf16 TP shards against their definition, recomputed with
+  torch on this GPU (no product planner or kernel): each trainer t's fp32
+  FSDP buffer is regenerated from its seed (3 + t; the same CUDA generator
+  stream the trainer drew), every parameter's global tensor is reassembled
+  from the trainers' dim-0 slices, and sampler d's shard is the dim-0
+  (column-parallel, vocab) or dim-1 (row-parallel) slice d of `half`, or the
+  whole tensor (replicated norms), cast to bf16 round-to-nearest-even.
+  Returns the names of the parameters whose bytes differ."""
+  import math
+  sizes = [math.prod(shape) // half for _, shape, _ in params]
+  total = sum(sizes)
+  trainers = []
+  for t in range(half):
+    x = torch.empty(total, dtype=torch.float32, device=device)
+    x.normal_(0.0, 0.02, generator=torch.Generator(device=device).manual_seed(3 + t))
+    trainers.append(x)
+  bad, soff, doff = [], 0, 0
+  for (name, shape, split), n in zip(params, sizes):
+    rows = shape[0] // half
+    full = torch.cat([trainers[t][soff:soff + n].view((rows,) + tuple(shape[1:]))
+                      for t in range(half)])
+    if split in ("col", "vocab"):
+      want = full[d * (shape[0] // half):(d + 1) * (shape[0] // half)]
+    elif split == "row":
+      want = full[:, d * (shape[1] // half):(d + 1) * (shape[1] // half)]
+    else:
+      want = full
+    want = want.to(torch.bfloat16).contiguous()
+    got = flat[doff:doff + want.numel()].view(want.shape)
+    if not torch.equal(got.view(torch.int16), want.view(torch.int16)):
+      bad.append(name)
+    soff += n
+    doff += want.numel()
+  if doff != flat.numel():
+    bad.append(f"<layout: {doff} of {flat.numel()} elements>")
+  del trainers
+  torch.cuda.empty_cache()
+  return bad
+
+
 def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
   """C4: Llama-3-8B fp32 FSDP shards on ranks [0, half) -> TP bf16 shards on
   ranks [half, 2*half), one reshard kernel per trainer rank storing straight
@@ -533,8 +574,9 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
     ce_error = "failed on another trainer rank"
   dist.barrier()
   ce_ms = 0.0
-  if is_src:
-    for which in (("sm", "copy") if not ce_error else ("sm",)):
+  mismatched = {}
+  for which in (("sm", "copy") if not ce_error else ("sm",)):
+    if is_src:
       p_ = prog if which == "sm" else prog_ce
       e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
       e0.record()
@@ -546,7 +588,16 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
         per_push_ms = e0.elapsed_time(e1) / steps
       else:
         ce_ms = e0.elapsed_time(e1) / steps
-  dist.barrier()
+    dist.barrier()
+    # after each engine's pushes the samplers check every byte they received,
+    # then clear their buffers for the next engine
+    if not is_src:
+      mismatched[which] = c4_shards_exact(torch, device, params, half, idx, flat)
+      flat.zero_()
+      torch.cuda.synchronize(device)
+    dist.barrier()
+  exact = torch.tensor([0 if any(mismatched.values()) else 1], dtype=torch.int32, device=device)
+  dist.all_reduce(exact, op=dist.ReduceOp.MIN)
   t = torch.tensor([per_push_ms, ce_ms], dtype=torch.float64, device=device)
   dist.all_reduce(t, op=dist.ReduceOp.MAX)
   sm_s, ce_s = float(t[0].item()) / 1e3, float(t[1].item()) / 1e3
@@ -573,7 +624,12 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
                                       "move each chunk (cudaMemcpy2DAsync), 16 pipelined groups",
                                "seconds": round(ce_s, 5) if not ce_error else None,
                                **({"error": ce_error} if ce_error else {})}},
-          "chunks_per_src": len(plan.for_source(0))}
+          "chunks_per_src": len(plan.for_source(0)),
+          "exact": bool(int(exact.item())),
+          "exact_how": ("every sampler's bf16 TP shards of all parameters, after each "
+                        "engine's pushes, equal their definition recomputed with torch "
+                        "(global tensors from the trainers' seeded fp32 shards, TP slice, "
+                        "RNE cast)")}
 
 
 def run_pull(torch, dist, rank, world, device, steps, warmup):
@@ -641,14 +697,48 @@ def run_pull(torch, dist, rank, world, device, steps, warmup):
   step_ms, start_read_ms = float(t[0].item()), float(t[1].item())
   moved = B * g.block_bytes
   mgr.close()
+  # The last read's destination blocks hold the producer's source blocks,
+  # the producer's pool regenerated here from its seed (50 + its rank).
+  exact = True
+  if not is_src:
+    prod = torch.empty_like(full)
+    prod.normal_(generator=torch.Generator(device=device).manual_seed(50 + rank - half))
+    si = torch.tensor(src_ids, dtype=torch.int64, device=device)
+    di = torch.tensor(dst_ids, dtype=torch.int64, device=device)
+    exact = bool(torch.equal(full[:, :, di].view(torch.int16), prod[:, :, si].view(torch.int16)))
+    del prod
+  ok = torch.tensor([1 if exact else 0], dtype=torch.int32, device=device)
+  dist.all_reduce(ok, op=dist.ReduceOp.MIN)
   del full, storages
   return {"config": f"{B} C1 blocks (2 MiB each) per pair, {half} pairs (GPU i -> i+{half}), "
                     "register_read / start_read / poll_stats over CUDA IPC",
           "bytes_per_pair": moved, "ms": round(step_ms, 3),
+          "exact": bool(int(ok.item())),
+          "exact_how": "the last read's 512 destination blocks equal the producer's source "
+                       "blocks, its pool regenerated from its seed",
           "start_read_host_ms": round(start_read_ms, 3),
           "nvlink_gbs_per_pair": round(moved / (step_ms * 1e-3) / 1e9, 1) if step_ms else None,
           "frac_of_nvlink_770": round(moved / (step_ms * 1e-3) / 1e9 / 770.0, 3)
           if step_ms else None}
+
+
+def c3_expected_pages(torch, device, src_rank, n_st, n_seqs, sbps, dbps, H, HB, st_tab, dt_tab):
+  """The consumer's pages after the hand-off, recomputed with torch (no
+  product kernel or planner): the producer's pages regenerated from its seed
+  (40 + its rank), each sequence's 16-token head-major source pages gathered
+  in order by its source page table, laid out token-major ([token][head]),
+  four to a 64-token page, and scattered by the destination page table."""
+  E = HB // 2  # bf16 elements of one head vector
+  src = torch.empty((n_st, n_seqs * sbps, 16 * H * E), dtype=torch.bfloat16, device=device)
+  src.normal_(generator=torch.Generator(device=device).manual_seed(40 + src_rank))
+  sidx = torch.from_numpy(st_tab.reshape(-1).astype(np.int64)).to(device)
+  didx = torch.from_numpy(dt_tab.reshape(-1).astype(np.int64)).to(device)
+  g = src[:, sidx].view(n_st, n_seqs, sbps, H, 16, E)       # [st][seq][page][head][tok]
+  g = g.permute(0, 1, 2, 4, 3, 5).reshape(n_st, n_seqs * dbps, 64 * H * E)
+  del src
+  out = torch.zeros((n_st, n_seqs * dbps, 64 * H * E), dtype=torch.bfloat16, device=device)
+  out[:, didx] = g
+  return out
 
 
 def run_handoff(torch, dist, rank, world, device, steps, warmup):
@@ -708,6 +798,21 @@ def run_handoff(torch, dist, rank, world, device, steps, warmup):
   dist.all_reduce(t, op=dist.ReduceOp.MAX)
   ms = float(t.item())
   moved = n_st * n_seqs * T * H * HB
+  # After each variant the consumer compares every page with the pages
+  # recomputed from their definition, then clears them for the next one.
+  expected = (c3_expected_pages(torch, device, rank - half, n_st, n_seqs, sbps, dbps, H, HB,
+                                st_tab, dt_tab) if not is_src else None)
+  exact = {}
+
+  def check(label):
+    if not is_src:
+      torch.cuda.synchronize(device)
+      exact[label] = bool(torch.equal(pages.view(torch.int16), expected.view(torch.int16)))
+      pages.zero_()
+      torch.cuda.synchronize(device)
+    dist.barrier()
+
+  check("push")
 
   # The same relayout pulled by the consumer (the reference's StartRead
   # direction): the decode GPU's kernel loads the prefill GPU's pages over
@@ -743,6 +848,7 @@ def run_handoff(torch, dist, rank, world, device, steps, warmup):
   t = torch.tensor([pull_ms], dtype=torch.float64, device=device)
   dist.all_reduce(t, op=dist.ReduceOp.MAX)
   pull_ms = float(t.item())
+  check("pull")
   if not is_src:
     peer_src = psrcs = None
     close_imports(device.index)
@@ -789,6 +895,7 @@ def run_handoff(torch, dist, rank, world, device, steps, warmup):
   t = torch.tensor([prog_ms, plan_ms], dtype=torch.float64, device=device)
   dist.all_reduce(t, op=dist.ReduceOp.MAX)
   prog_ms, plan_ms = float(t[0].item()), float(t[1].item())
+  check("pool_plan")
   if is_src:
     prog.close()
     plan.close()
@@ -835,6 +942,11 @@ def run_handoff(torch, dist, rank, world, device, steps, warmup):
   t = torch.tensor([pull_prog_ms], dtype=torch.float64, device=device)
   dist.all_reduce(t, op=dist.ReduceOp.MAX)
   pull_prog_ms = float(t.item())
+  check("pool_plan_pull")
+  ok = torch.tensor([1 if all(exact.values()) else 0], dtype=torch.int32, device=device)
+  dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+  expected = None
+  torch.cuda.empty_cache()
   if not is_src:
     prog.close()
     plan.close()
@@ -849,6 +961,10 @@ def run_handoff(torch, dist, rank, world, device, steps, warmup):
   return {"config": "C3 8 seqs x 32768 tok, 2 KV heads/GPU, 16-tok head-major -> 64-tok "
                     f"token-major, {half} pairs (GPU i -> i+{half})",
           "bytes_per_pair": moved,
+          "exact": bool(int(ok.item())),
+          "exact_how": ("after each of the four variants every consumer's 8 GiB of pages "
+                        "equal the producer's regenerated pages relaid out by torch indexing "
+                        "(page tables applied by definition)"),
           "how": ("relayout kernel on the consumer (the reference's pull direction): loads "
                   "the producer's pages over NVLink (CUDA IPC), stores its own pages"),
           **rate(pull_ms),
@@ -916,6 +1032,21 @@ def run_c2_fp8(torch, rank, device, steps, warmup, max_over_ranks, cpu_seconds=0
   ms = max_over_ranks(e0.elapsed_time(e1)) / steps
   ext, ins = mgr.kernel_stats("extract"), mgr.kernel_stats("insert")
   mgr.close()
+  # The last step reloaded into in_ids[last] what the step before offloaded
+  # from out_ids[last]: the fp8 round trip of those blocks, recomputed here
+  # with torch from its definition (per (layer, K/V, block) scale =
+  # amax / 448, q = e4m3 RN of x / scale, x' = bf16 RN of q * scale).
+  last = warmup + steps - 1
+  sid = torch.from_numpy(out_ids[last]).to(device)
+  did = torch.from_numpy(in_ids[last]).to(device)
+  x = full[:, :, sid].float()
+  amax = x.abs().amax(dim=(3, 4, 5), keepdim=True)
+  # a tensor divisor keeps torch's true (round-to-nearest) division on the
+  # GPU; a Python-scalar divisor would be applied as a reciprocal multiply
+  scale = torch.where(amax == 0, torch.ones_like(amax), amax / torch.full_like(amax, 448.0))
+  want = ((x / scale).to(torch.float8_e4m3fn).float() * scale).to(torch.bfloat16)
+  exact = bool(torch.equal(full[:, :, did].view(torch.int16), want.view(torch.int16)))
+  del x, amax, scale, want
   bf16_bytes = 2 * B * g.block_bytes
   wire = 2 * B * mgr.host_block_pitch
 
@@ -931,7 +1062,10 @@ def run_c2_fp8(torch, rank, device, steps, warmup, max_over_ranks, cpu_seconds=0
           "bf16_gbs": round(bf16_bytes / (ms * 1e-3) / 1e9, 2),
           "pcie_gbs": round(wire / (ms * 1e-3) / 1e9, 2),
           "extract_fp8_kernel_gbs": kgbs(ext), "insert_fp8_kernel_gbs": kgbs(ins),
-          "kernel_launches": ext["launches"] + ins["launches"]}
+          "kernel_launches": ext["launches"] + ins["launches"],
+          "exact": exact,
+          "exact_how": ("the last step's 256 reloaded blocks (all 160 storages) equal the fp8 "
+                        "round trip of the blocks offloaded before them, recomputed with torch")}
 
 
 def noalloc_offload_figure(torch, device, storages, table, id_sets, n, pitch):
@@ -1233,6 +1367,11 @@ def run_ours(args):
                   cpu_seconds=5.0 if (rank == 0 and world == 1 and not args.no_cpu_baseline)
                   else 0.0)
   torch.cuda.empty_cache()
+  if world > 1:  # every rank's check must hold
+    ok = torch.tensor([1 if c2["exact"] else 0], dtype=torch.int32, device=device)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    c2["exact"] = bool(int(ok.item()))
+  c2["gpus_concurrent"] = world
   if rank == 0:
     line["c2_fp8"] = c2
   exchange = {}

@@ -201,3 +201,296 @@ def test_pool_registration_and_block_ref_errors():
   with pytest.raises(RuntimeError, match="not supported on an fp8 host tier"):
     m3.register_pools([PoolSpec("x", 0, 0, 2048, 8, (RegionSpec("k", 0, 2048, 2048, 1),))])
   m3.close()
+
+
+# ---------------------------------------------------------------------------
+# The reference's manager pool tests (tpu_sync/kv_cache/kv_cache_manager_test.cc
+# :120-556), one counterpart per TEST, on device-backed managers.  The
+# reference's TestKVCacheManager(num_layers, num_shards, slice_byte_size,
+# host_blocks) holds storages of host_blocks x slice bytes; here those are
+# device tensors of [host_blocks, slice] bytes (or [dim0, slice] where the
+# reference sets a device physical size).  Host addresses: byte x of storage
+# s lives at host block x // bb of that storage's slot, offset x % bb (the
+# block-major tier); with one storage that is the reference's base + x.
+# ---------------------------------------------------------------------------
+
+import ctypes
+
+from tpu_sync_b200 import _native
+
+
+def ref_manager(num_layers, slice_bytes, host_blocks, dim0=None, num_shards=1):
+  dev = gpu()
+  dim0 = host_blocks if dim0 is None else dim0
+  grid = [[torch.zeros((dim0, slice_bytes), dtype=torch.uint8, device=dev)
+           for _ in range(num_shards)] for _ in range(num_layers)]
+  return grid, KVCacheManager(grid, host_blocks_to_allocate=host_blocks)
+
+
+def dense_pool(tag, storage_index, base, stride, num_blocks, dtype_tag="dtype_a"):
+  """DensePool (kv_cache_manager_test.cc:89-115): one region covering the block."""
+  return PoolSpec(tag, storage_index, base, stride, num_blocks,
+                  (RegionSpec("block", 0, stride, stride, 1),), dtype_tag=dtype_tag)
+
+
+def strided_pool(tag, storage_index, base, stride, num_blocks):
+  """StridedPool (:68-87): live [0, 32) and [64, 96) of every block."""
+  return PoolSpec(tag, storage_index, base, stride, num_blocks,
+                  (RegionSpec("payload", 0, 64, 32, 2),), dtype_tag="dtype_a")
+
+
+def host_addr(mgr, layer, x, shard=0):
+  rc, ptr, _ = mgr._host_block(layer, x // mgr.block_bytes(layer), shard)
+  assert rc == _native.OK
+  return ptr + x % mgr.block_bytes(layer)
+
+
+def block_ref_rc(mgr, pool_idx, shard_idx, block_id):
+  ptr = ctypes.c_uint64()
+  rc = _native.lib().ts_mgr_pool_block_ref(mgr._mgr, pool_idx, shard_idx, block_id,
+                                           ctypes.byref(ptr))
+  return rc, ptr.value
+
+
+def host_bytes(mgr, layer, x, n):
+  return np.frombuffer(mgr.read_storage_bytes(layer, x, n), np.uint8)
+
+
+def test_register_pools_validates_against_storage():
+  """RegisterPoolsValidatesAgainstStorage (:120-153)."""
+  _, mgr = ref_manager(2, 128, 2)
+  mgr.register_pools([dense_pool("kind_a", 0, 0, 128, 2), strided_pool("kind_b", 0, 0, 128, 2),
+                      dense_pool("kind_a", 1, 64, 64, 3)])  # overlapping pools are allowed
+  assert mgr.has_explicit_pools() and mgr.num_pools() == 3
+  with pytest.raises(ValueError, match="storage_index"):
+    mgr.register_pools([dense_pool("kind_a", 5, 0, 128, 2)])
+  with pytest.raises(RuntimeError, match="exceeds storage bytes"):  # 64 + 2 x 128 > 256
+    mgr.register_pools([dense_pool("kind_a", 0, 64, 128, 2)])
+  # the device's physical size, not the host mirror's, bounds a pool
+  _, dev_backed = ref_manager(1, 128, 2, dim0=1)
+  dev_backed.register_pools([dense_pool("kind_a", 0, 0, 128, 1)])
+  with pytest.raises(RuntimeError, match="exceeds storage bytes"):
+    dev_backed.register_pools([dense_pool("kind_a", 0, 0, 128, 2)])
+  mgr.close()
+  dev_backed.close()
+
+
+def test_get_pool_block_ref_pointer_math():
+  """GetPoolBlockRefPointerMath (:155-195), and the same pools on the second
+  storage of a two-storage tier (addresses restated for the block-major
+  layout)."""
+  _, mgr = ref_manager(1, 128, 4)
+  mgr.register_pools([dense_pool("kind_a", 0, 0, 128, 2), dense_pool("kind_b", 0, 256, 64, 4)])
+  base = host_addr(mgr, 0, 0)
+  r = mgr.get_block_ref(0, 1)
+  assert r["ptr"] == base + 128 and r["block_stride_bytes"] == 128
+  assert r["tag"] == "kind_a" and r["pool_idx"] == 0 and r["block_id"] == 1
+  assert mgr.get_block_ref(1, 0)["ptr"] == base + 256
+  assert mgr.get_block_ref(1, 3)["ptr"] == base + 256 + 3 * 64
+  for pool, shard, block in ((0, 0, 2), (1, 0, 4), (2, 0, 0), (0, 1, 0)):
+    assert block_ref_rc(mgr, pool, shard, block)[0] == _native.OUT_OF_RANGE
+  mgr.close()
+  _, two = ref_manager(2, 128, 4)
+  two.register_pools([dense_pool("kind_a", 1, 0, 128, 2), dense_pool("kind_b", 1, 256, 64, 4)])
+  assert two.get_block_ref(0, 1)["ptr"] == host_addr(two, 1, 128)
+  assert two.get_block_ref(1, 3)["ptr"] == host_addr(two, 1, 256 + 3 * 64)
+  assert host_addr(two, 1, 128) - host_addr(two, 1, 0) == two.host_block_pitch
+  two.close()
+
+
+def test_register_pools_grows_device_backed_host_mirror():
+  """RegisterPoolsGrowsDeviceBackedHostMirror (:197-225).  The tier here is
+  one block-major allocation of host_blocks x the sum of the storages'
+  block bytes, sized at creation: where it already mirrors the storage the
+  pool is admitted and its last block sits at base + 3 x 64, as in the
+  reference after it grew; a pool reaching past the bytes the tier mirrors
+  is refused (FAILED_PRECONDITION) instead of regrowing the tier, and the
+  bytes already there are kept."""
+  _, mgr = ref_manager(1, 256, 1, dim0=1)
+  mgr.write_block_bytes(0, 0, bytes(range(64)))
+  mgr.register_pools([dense_pool("kind_a", 0, 0, 64, 4)])
+  assert mgr.get_block_ref(0, 3)["ptr"] == host_addr(mgr, 0, 0) + 3 * 64
+  assert mgr.read_block_bytes(0, 0)[:64] == bytes(range(64))
+  mgr.close()
+  _, short = ref_manager(1, 64, 1, dim0=4)  # 256 device bytes, the tier mirrors 64
+  short.write_block_bytes(0, 0, bytes(range(64)))
+  rc = _native.lib().ts_mgr_register_pools(short._mgr, *_pools_c([dense_pool("kind_a", 0, 0,
+                                                                              64, 4)]))
+  assert rc == _native.FAILED_PRECONDITION
+  assert "tier mirrors 64 bytes of storage 0" in _native.last_error()
+  assert short.read_block_bytes(0, 0) == bytes(range(64))
+  short.close()
+
+
+def _pools_c(pools):
+  from tpu_sync_b200 import pool_layout
+  arr, keep = pool_layout.pools_c(tuple(pools))
+  _pools_c.keep = keep
+  return arr, len(pools)
+
+
+def test_register_pools_fails_after_active_plan_registered():
+  """RegisterPoolsFailsAfterActivePlanRegistered (:227-243).  Active plans
+  are the TCP push protocol's state, which this build does not have
+  (register_active_plan names the on-node alternatives), so nothing
+  freezes the pool table: a later registration replaces it."""
+  _, mgr = ref_manager(1, 128, 1)
+  with pytest.raises(NotImplementedError, match="PoolReshardProgram"):
+    mgr.register_active_plan(445566, None, True)
+  mgr.register_pools([dense_pool("kind_a", 0, 0, 128, 1)])
+  mgr.register_pools([dense_pool("kind_b", 0, 0, 64, 2)])
+  assert mgr.num_pools() == 1 and mgr.pool_spec(0)["tag"] == "kind_b"
+  mgr.close()
+
+
+def test_pool_indices_with_tag():
+  """PoolIndicesWithTag (:245-263)."""
+  _, mgr = ref_manager(2, 128, 2)
+  mgr.register_pools([dense_pool("kind_a", 0, 0, 128, 2),
+                      dense_pool("kind_b", 1, 0, 128, 2, dtype_tag="dtype_b"),
+                      strided_pool("kind_a", 1, 0, 128, 2)])
+  assert mgr.pool_ids_with_tag("kind_a") == [0, 2]
+  assert mgr.pool_ids_with_tag("kind_b") == [1]
+  assert mgr.pool_ids_with_tag("missing") == []
+  mgr.close()
+
+
+def test_register_active_plan_checks_pool_dtype_tags():
+  """RegisterActivePlanChecksPoolDtypeTags (:265-297).  The dtype tags are
+  kept per pool (pool_spec) for the on-node hand-off; the TCP plan
+  registration that compares them against a request is not built."""
+  _, mgr = ref_manager(2, 128, 2)
+  mgr.register_pools([dense_pool("kind_a", 0, 0, 128, 2),
+                      dense_pool("kind_b", 1, 0, 128, 2, dtype_tag="dtype_b"),
+                      strided_pool("kind_a", 1, 0, 128, 2)])
+  assert [mgr.pool_spec(i)["dtype_tag"] for i in range(3)] == ["dtype_a", "dtype_b", "dtype_a"]
+  with pytest.raises(NotImplementedError):
+    mgr.register_active_plan(777, None, True)
+  mgr.close()
+
+
+def test_explicit_pool_addressing_uses_pool_base_and_stride():
+  """ExplicitPoolAddressingUsesPoolBaseAndStride (:299-324): pool 0 on
+  storage 1 at base 128, stride 64; block 2 lives at storage byte 256.  The
+  reference's GetBlockChunks (TCP chunking) has no counterpart; the pool's
+  blocks 0, 2, 3 move between device and host at those addresses and
+  nothing else does."""
+  grid, mgr = ref_manager(2, 128, 4)
+  mgr.register_pools([dense_pool("kind_a", 1, 128, 64, 4)])
+  assert mgr.get_block_ref(0, 2)["ptr"] == host_addr(mgr, 1, 128 + 2 * 64)
+  pattern = torch.arange(512, dtype=torch.int32).remainder(251).to(torch.uint8)
+  grid[1][0].view(-1).copy_(pattern.to(grid[1][0].device))
+  mgr.d2h_pool_blocks(0, [0, 2, 3]).Await()
+  want = np.zeros(512, np.uint8)
+  p = pattern.numpy()
+  for b in (0, 2, 3):
+    want[128 + 64 * b:192 + 64 * b] = p[128 + 64 * b:192 + 64 * b]
+  np.testing.assert_array_equal(host_bytes(mgr, 1, 0, 512), want)
+  assert not host_bytes(mgr, 0, 0, 512).any()
+  mgr.close()
+
+
+def test_explicit_pool_transport_uses_backing_storage_base_and_pool_stride():
+  """ExplicitPoolTransportUsesBackingStorageBaseAndPoolStride (:326-392):
+  pool 0 on storage 1 at base 64, stride 128, 2 blocks.  A pattern written
+  at the pool's block 0 (storage 1 bytes [64, 192) of the host tier) reaches
+  the device at storage 1 bytes
+  [64, 192) and storage 0 stays zero; block 2 lies outside the pool (though
+  inside storage 1), so a copy of it is refused and its bytes, host and
+  device, stay as they were."""
+  grid, mgr = ref_manager(2, 64, 8)
+  mgr.register_pools([dense_pool("kind_a", 1, 64, 128, 2)])
+  pattern = bytes((i * 17 + 3) % 251 for i in range(128))
+  # the 128-byte pool block spans two 64-byte host blocks, which are not
+  # adjacent on the block-major tier: no single host pointer covers it
+  with pytest.raises(RuntimeError, match="spans several host blocks"):
+    mgr.get_block_ref(0, 0)
+  for i in range(0, 128, 64):
+    ctypes.memmove(host_addr(mgr, 1, 64 + i), pattern[i:i + 64], 64)
+  mgr.h2d_pool_blocks(0, [0]).Await()
+  dev1 = grid[1][0].view(-1).cpu().numpy()
+  assert dev1[64:192].tobytes() == pattern
+  assert not dev1[:64].any() and not dev1[192:].any()
+  assert not grid[0][0].any()
+  grid[1][0].view(-1)[64 + 2 * 128:64 + 3 * 128].fill_(0xD4)
+  with pytest.raises(RuntimeError, match="out of range"):
+    mgr.d2h_pool_blocks(0, [2])
+  with pytest.raises(RuntimeError, match="out of range"):
+    mgr.h2d_pool_blocks(0, [2])
+  torch.cuda.synchronize()
+  assert not host_bytes(mgr, 1, 64 + 2 * 128, 128).any()
+  assert (grid[1][0].view(-1)[64 + 2 * 128:64 + 3 * 128] == 0xD4).all()
+  mgr.close()
+
+
+def test_aliased_pool_transport_copies_only_live_regions_and_preserves_padding():
+  """AliasedPoolTransportCopiesOnlyLiveRegionsAndPreservesPadding (:394-440):
+  strided pool at base 32, stride 128, 2 blocks on a 256-byte storage.  Its
+  logical end (288) passes the storage but its last live byte is 256, so it
+  is admitted and block 1 sits at byte 160.  Copying block 1 moves the live
+  [160, 192) and [224, 256) and leaves the padding [192, 224) alone."""
+  grid, mgr = ref_manager(1, 128, 2)
+  mgr.register_pools([strided_pool("aliased", 0, 32, 128, 2)])
+  assert mgr.get_block_ref(0, 1)["ptr"] == host_addr(mgr, 0, 160)
+  dev = grid[0][0].view(-1)
+  dev.fill_(0xA5)
+  dev[160:192].fill_(0x11)
+  dev[224:256].fill_(0x22)
+  tier = mgr.host_tier_view()
+  tier[:] = 0xEE
+  mgr.d2h_pool_blocks(0, [1]).Await()
+  h = host_bytes(mgr, 0, 0, 256)
+  assert (h[160:192] == 0x11).all() and (h[192:224] == 0xEE).all() and (h[224:256] == 0x22).all()
+  assert (h[:160] == 0xEE).all()
+  dev.zero_()
+  mgr.h2d_pool_blocks(0, [1]).Await()
+  torch.cuda.synchronize()
+  d = dev.cpu().numpy()
+  assert (d[160:192] == 0x11).all() and (d[224:256] == 0x22).all()
+  assert not d[:160].any() and not d[192:224].any()
+  mgr.close()
+
+
+def test_explicit_pool_transport_enumerates_all_pools():
+  """ExplicitPoolTransportEnumeratesAllPools (:442-520): two pools on one
+  storage (kind_a at 0, kind_b at 256, 64-byte blocks); each pool's copy of
+  its block 1 moves that pool's bytes only, both ways."""
+  grid, mgr = ref_manager(1, 64, 8)
+  mgr.register_pools([dense_pool("kind_a", 0, 0, 64, 2), dense_pool("kind_b", 0, 256, 64, 2)])
+  assert mgr.num_pools() == 2
+  dev = grid[0][0].view(-1)
+  dev[64:128].fill_(0xA1)
+  dev[256 + 64:256 + 128].fill_(0xB2)
+  mgr.d2h_pool_blocks(0, [1]).Await()
+  h = host_bytes(mgr, 0, 0, 512)
+  assert (h[64:128] == 0xA1).all() and not h[256:].any()
+  mgr.d2h_pool_blocks(1, [1]).Await()
+  h = host_bytes(mgr, 0, 0, 512)
+  assert (h[320:384] == 0xB2).all() and not h[:64].any() and not h[128:320].any()
+  dev.zero_()
+  mgr.h2d_pool_blocks(0, [1]).Await()
+  mgr.h2d_pool_blocks(1, [1]).Await()
+  torch.cuda.synchronize()
+  d = dev.cpu().numpy()
+  assert (d[64:128] == 0xA1).all() and (d[320:384] == 0xB2).all()
+  assert not d[:64].any() and not d[128:320].any() and not d[384:].any()
+  mgr.close()
+
+
+def test_pool_block_copies_reject_host_only_manager():
+  """PoolBlockCopiesRejectHostOnlyManager (:522-538): this build has no
+  host-only manager to refuse (blocks live in HBM); asking for one says so."""
+  with pytest.raises(NotImplementedError, match="no host-only manager"):
+    KVCacheManager.create_host_only_for_testing(num_layers=1, slice_byte_size=64, node_id=0,
+                                                host_blocks=2)
+
+
+def test_implicit_pools_mirror_storages():
+  """ImplicitPoolsMirrorStorages (:540-556)."""
+  _, mgr = ref_manager(2, 128, 2)
+  assert not mgr.has_explicit_pools() and mgr.num_pools() == 2
+  p = mgr.pool_spec(0)
+  assert (p["tag"], p["storage_index"], p["base_offset_bytes"], p["block_stride_bytes"],
+          p["num_blocks"]) == ("opaque", 0, 0, 128, 2)
+  assert mgr.get_block_ref(1, 1)["ptr"] == host_addr(mgr, 1, 128)
+  mgr.close()
