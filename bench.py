@@ -246,11 +246,47 @@ def c1_plans(rank: int, host_blocks: int, pool_blocks: int, batch: int, n_steps:
 
 def c1_host_blocks(args, world: int) -> int:
   """Host tier blocks of the C1 configuration: as many as requested (default
-  32768 = 64 GiB), bounded by this box's RAM share per local rank."""
+  32768 = 64 GiB), bounded by this box's RAM share per local rank: 45 % of
+  the available RAM for one rank, 30 % in total when ranks share the host
+  (with eight ranks pinning 45 % of a 1 TB host, later pinned allocations
+  of the run were refused)."""
   want = args.host_blocks or 32768
   local_ranks = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
-  fit = int(0.45 * mem_available_bytes() / max(local_ranks, 1) // C1_BLOCK_BYTES)
+  share = 0.45 if local_ranks <= 1 else 0.30
+  fit = int(share * mem_available_bytes() / max(local_ranks, 1) // C1_BLOCK_BYTES)
   return max(4 * args.batch, min(want, fit))
+
+
+def host_memory_state() -> dict:
+  """Host memory figures that bound pinned allocations (GiB)."""
+  out = {}
+  try:
+    for line in open("/proc/meminfo"):
+      k, v = line.split(":", 1)
+      if k in ("MemTotal", "MemAvailable", "Mlocked", "Unevictable"):
+        out[k] = round(int(v.split()[0]) / 2**20, 1)
+  except OSError:
+    pass
+  for name in ("memory.current", "memory.max"):
+    try:
+      v = open(f"/sys/fs/cgroup/{name}").read().strip()
+      out[name] = v if v == "max" else round(int(v) / 2**30, 1)
+    except (OSError, ValueError):
+      pass
+  return out
+
+
+def make_manager(KVCacheManager, grid, attempts: int = 6, **kw):
+  """A manager whose pinned host tier may be refused for a moment right after
+  another leg freed a large one (seen with eight ranks on one host): retries
+  a few times, and on the last failure reports the host memory state."""
+  for i in range(attempts):
+    try:
+      return KVCacheManager(grid, **kw)
+    except RuntimeError as e:
+      if "cudaHostAlloc" not in str(e) or i == attempts - 1:
+        raise RuntimeError(f"{e} (host memory: {host_memory_state()})") from e
+      time.sleep(2.0)
 
 
 def c1_config(args, host_blocks: int, plans, trace_stats, world: int) -> dict:
@@ -646,7 +682,7 @@ def run_pull(torch, dist, rank, world, device, steps, warmup):
                      dtype=torch.bfloat16, device=device)
   full.normal_(generator=torch.Generator(device=device).manual_seed(50 + rank))
   storages = [full[l, k] for l in range(g.layers) for k in range(g.kv)]
-  mgr = KVCacheManager([[t] for t in storages], host_blocks_to_allocate=4)
+  mgr = make_manager(KVCacheManager, [[t] for t in storages], host_blocks_to_allocate=4)
   ep = mgr.get_local_endpoints() if is_src else None
   eps = [None] * world
   dist.all_gather_object(eps, ep)
@@ -997,7 +1033,8 @@ def run_c2_fp8(torch, rank, device, steps, warmup, max_over_ranks, cpu_seconds=0
   for l in range(g.layers):
     full[l].normal_(generator=gen)
   storages = [full[l, k] for l in range(g.layers) for k in range(g.kv)]
-  mgr = KVCacheManager([[t] for t in storages], host_blocks_to_allocate=host_blocks, fp8=True)
+  mgr = make_manager(KVCacheManager, [[t] for t in storages], host_blocks_to_allocate=host_blocks,
+                     fp8=True)
   rng = np.random.default_rng(20 + rank)
   n = warmup + steps + 1
   out_ids = [rng.choice(nblk // 2, B, replace=False).astype(np.int64) for _ in range(n)]
@@ -1144,11 +1181,11 @@ def run_ours(args):
   # Host tier: as large as requested, bounded by this box's RAM share.
   pitch = g.block_bytes
   host_blocks = c1_host_blocks(args, world)
-  mgr = KVCacheManager([[t] for t in storages], host_blocks_to_allocate=host_blocks,
-                       mode=args.mode, copy_streams=args.copy_streams,
-                       chunk_blocks=args.chunk_blocks, max_ctas=args.max_ctas,
-                       reload_staged_every=args.reload_staged_every,
-                       sched=tuple(f for f in args.sched.split(",") if f))
+  mgr = make_manager(KVCacheManager, [[t] for t in storages], host_blocks_to_allocate=host_blocks,
+                     mode=args.mode, copy_streams=args.copy_streams,
+                     chunk_blocks=args.chunk_blocks, max_ctas=args.max_ctas,
+                     reload_staged_every=args.reload_staged_every,
+                     sched=tuple(f for f in args.sched.split(",") if f))
 
   pcie = measure_pcie(torch, device)
 
@@ -1360,9 +1397,14 @@ def run_ours(args):
             "value": cpu["value"], "unit": "GB/s", "cores": cpu["cores"], "kind": "port",
             "sample": cpu["sample"], "cpu": cpu["cpu"]},
     }
+  host_after_c1 = host_memory_state()
   mgr.close()
   del mgr, full, storages, table
   torch.cuda.empty_cache()
+  if hasattr(torch._C, "_host_emptyCache"):  # torch's cached pinned buffers
+    torch._C._host_emptyCache()
+  if rank == 0:
+    line["host_memory"] = {"during_c1": host_after_c1, "after_c1": host_memory_state()}
   c2 = run_c2_fp8(torch, rank, device, 5, 3, max_over_ranks,
                   cpu_seconds=5.0 if (rank == 0 and world == 1 and not args.no_cpu_baseline)
                   else 0.0)
