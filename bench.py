@@ -80,14 +80,15 @@ def parse():
   p.add_argument("--copy-streams", type=int, default=2)
   p.add_argument("--chunk-blocks", type=int, default=0, help="0 = manager default")
   p.add_argument("--max-ctas", type=int, default=0, help="kernel grid cap, 0 = default")
-  p.add_argument("--sched", default="offload_priority,reload_per_piece",
+  p.add_argument("--sched", default="offload_priority,reload_per_piece,bulk_copy",
                  help="comma-separated manager sched flags: offload_priority, "
-                      "reload_per_piece, reload_overlap ('' = none)")
+                      "reload_per_piece, reload_overlap, bulk_copy ('' = none)")
   p.add_argument("--reload-staged-every", type=int, default=0,
                  help="direct reloads: every n-th chunk through the copy engines (0 = none)")
   p.add_argument("--kernel-case", default="",
                  choices=["", "extract", "insert", "extract_fp8", "insert_fp8", "pool_reshard",
-                          "insert_direct", "relayout"],
+                          "insert_direct", "relayout", "manager_extract",
+                          "manager_insert"],
                  help="run a few launches of one kernel on a small case (for ncu)")
   return p.parse_args()
 
@@ -1524,6 +1525,38 @@ def run_kernel_case(args):
     print(json.dumps({"kernel_case": args.kernel_case, "blocks_per_launch": 256,
                       "bytes_per_block": g.block_bytes}))
     mgr.close()
+    return
+  if args.kernel_case in ("manager_extract", "manager_insert"):
+    # The manager's staged extract (HBM pool -> HBM staging) or insert kernel,
+    # 256 random C1 blocks (512 MiB each way) per launch on a 1024-block pool,
+    # with the kernel the --sched flags select (bulk_copy: the bulk-copy
+    # kernel); CUDA-event device time of each launch from the manager.
+    from tpu_sync_b200 import KVCacheManager
+    g = workloads.C1
+    full = torch.empty((g.layers, g.kv, 1024, g.block_tokens, g.heads, g.head_dim),
+                       dtype=torch.bfloat16, device=device)
+    full.normal_(generator=torch.Generator(device=device).manual_seed(1))
+    storages = [full[l, k] for l in range(g.layers) for k in range(g.kv)]
+    mgr = KVCacheManager([[t] for t in storages], host_blocks_to_allocate=256, mode="staged",
+                         chunk_blocks=256, sched=tuple(f for f in args.sched.split(",") if f))
+    rng = np.random.default_rng(5)
+    extract = args.kernel_case == "manager_extract"
+    if not extract:
+      mgr.d2h(list(range(256)), list(range(256))).Await()
+    for i in range(8):
+      if i == 3:
+        mgr.set_profiling(True)
+        mgr.kernel_stats("extract")
+        mgr.kernel_stats("insert")
+      ids = rng.choice(1024, 256, replace=False).tolist()
+      (mgr.d2h(ids, rng.permutation(256).tolist()) if extract
+       else mgr.h2d(rng.permutation(256).tolist(), ids)).Await()
+    st = mgr.kernel_stats("extract" if extract else "insert")
+    mgr.close()
+    print(json.dumps({"kernel_case": args.kernel_case, "sched": args.sched,
+                      "launches": st["launches"],
+                      "us_per_launch": round(st["ms"] * 1e3 / max(st["launches"], 1), 1),
+                      "hbm_gbs": round(st["bytes"] / (st["ms"] * 1e-3) / 1e9, 1)}))
     return
   g = workloads.C1 if not args.kernel_case.endswith("fp8") else workloads.C2
   blocks = 1024 if g is workloads.C1 else 2048

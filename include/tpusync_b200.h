@@ -661,6 +661,11 @@ enum {
    * so one chunk's last wave overlaps the next chunk's first (not used when
    * a destination block repeats inside the call) */
   TS_SCHED_RELOAD_OVERLAP = 4,
+  /* staged (HBM -> HBM) extract and insert kernels move 16 KiB pieces with
+   * bulk copies through shared memory: one CTA of 6 warps per SM instead of
+   * a full-SM grid of vector loads (plain copies of 16-byte aligned tables;
+   * fp8 and direct-mode kernels are unchanged) */
+  TS_SCHED_BULK_COPY = 8,
 };
 
 /* Creates a manager over num_layers x num_shards storages (row-major

@@ -77,7 +77,9 @@ __device__ __forceinline__ bool resolve(const ts_block_storage* __restrict__ st,
   const int64_t id = ids.dev(k);
   const uint64_t dev_off = uint64_t(id) * bb;
   if (id < 0 || dev_off + bb > st[s].dev_bytes) {
-    if (err_flag != nullptr && threadIdx.x == 0) *reinterpret_cast<volatile int*>(err_flag) = 1;
+    // lane 0 of every warp: the bulk kernel resolves pieces on lane 0 only
+    if (err_flag != nullptr && (threadIdx.x & 31) == 0)
+      *reinterpret_cast<volatile int*>(err_flag) = 1;
     return false;
   }
   u->dev = reinterpret_cast<uint8_t*>(st[s].dev_ptr) + dev_off + off;
@@ -131,6 +133,125 @@ __global__ void __launch_bounds__(kThreads)
     uint8_t* dst = kToStaging ? u.stg : u.dev;
     for (uint64_t b = threadIdx.x; b < u.nbytes; b += kThreads) dst[b] = src[b];
   }
+}
+
+// ---------------------------------------------------------------------------
+// Bulk-copy variant (HBM -> HBM only): each warp's lane 0 moves 16 KiB pieces
+// with the Blackwell bulk-copy engine, global -> shared (completion counted
+// on an mbarrier) then shared -> global (bulk async-group), two shared-memory
+// buffers per warp so the next piece's load overlaps the current piece's
+// store.  Six warps per CTA and one CTA per SM keep up to twelve 16 KiB loads
+// in flight per SM in 192 KiB of shared memory while occupying 6 of the SM's
+// 64 warp slots, so the gather can run beside another kernel that holds most
+// of the SM.  Plain (non-multicast) copies of this GPU's own memory only;
+// every address and size is a multiple of 16 (the caller checks vec_ok).
+// Each wait on a load is bounded: past ~2^32 cycles the warp stops, records
+// 3 in err_flag, waits for its issued stores and leaves.
+// ---------------------------------------------------------------------------
+
+constexpr int kBulkWarps = 6;
+constexpr int kBulkBufs = 2;
+constexpr uint32_t kBulkSmem = uint32_t(kBulkWarps) * kBulkBufs * uint32_t(kPieceBytes);
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void bulk_load(uint32_t dst_smem, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n\t"
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%2], [%3], %1, [%0];"
+      ::"r"(bar), "r"(bytes), "r"(dst_smem), "l"(src)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_store(void* dst, uint32_t src_smem, uint32_t bytes) {
+  asm volatile(
+      "cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n\t"
+      "cp.async.bulk.commit_group;"
+      ::"l"(dst), "r"(src_smem), "r"(bytes)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_reads_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// True once the mbarrier's phase `parity` completed; false after ~2^32 cycles.
+__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
+  const long long t0 = clock64();
+  for (;;) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (clock64() - t0 > (1ll << 32)) return false;
+  }
+}
+
+template <bool kToStaging, typename Ids>
+__global__ void __launch_bounds__(kBulkWarps * 32, 1)
+    block_copy_bulk_kernel(const ts_block_storage* __restrict__ st, int n_st,
+                           const __grid_constant__ Ids ids, int64_t n_blocks,
+                           uint8_t* staging, uint64_t pitch, uint32_t ppu, int* err_flag) {
+  extern __shared__ __align__(128) uint8_t bulk_smem[];
+  __shared__ __align__(8) uint64_t bars[kBulkWarps][kBulkBufs];
+  const int warp = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) != 0) return;  // one issuing lane per warp
+  uint32_t bar[kBulkBufs], buf[kBulkBufs], phase[kBulkBufs];
+  for (int b = 0; b < kBulkBufs; ++b) {
+    bar[b] = smem_u32(&bars[warp][b]);
+    buf[b] = smem_u32(bulk_smem + (size_t(warp) * kBulkBufs + b) * kPieceBytes);
+    phase[b] = 0;
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar[b]) : "memory");
+  }
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  const int64_t items = n_blocks * int64_t(n_st) * ppu;
+  const int64_t stride = int64_t(gridDim.x) * kBulkWarps;
+  int64_t w = int64_t(blockIdx.x) * kBulkWarps + warp;
+  // next valid piece at or after w (pieces past a block's end and blocks
+  // whose id is out of range are skipped, the latter flagged by resolve)
+  auto next = [&](Unit* u) {
+    while (w < items) {
+      const bool ok = resolve(st, n_st, ids, staging, pitch, ppu, w, err_flag, u);
+      w += stride;
+      if (ok) return true;
+    }
+    return false;
+  };
+  Unit cur, nxt;
+  if (!next(&cur)) return;
+  int b = 0;
+  bulk_load(buf[b], kToStaging ? cur.dev : cur.stg, uint32_t(cur.nbytes), bar[b]);
+  for (;;) {
+    const bool more = next(&nxt);
+    if (more) {
+      // the other buffer's last store must have read it out of shared memory
+      bulk_wait_reads_all();
+      bulk_load(buf[b ^ 1], kToStaging ? nxt.dev : nxt.stg, uint32_t(nxt.nbytes), bar[b ^ 1]);
+    }
+    if (!bar_wait(bar[b], phase[b])) {
+      if (err_flag != nullptr) *reinterpret_cast<volatile int*>(err_flag) = 3;
+      if (more) bar_wait(bar[b ^ 1], phase[b ^ 1]);  // the next piece's load (bounded)
+      break;
+    }
+    phase[b] ^= 1;
+    bulk_store(kToStaging ? cur.stg : cur.dev, buf[b], uint32_t(cur.nbytes));
+    if (!more) break;
+    cur = nxt;
+    b ^= 1;
+  }
+  bulk_wait_all();
 }
 
 // ---------------------------------------------------------------------------
@@ -537,12 +658,13 @@ int launch_grid(int device, int64_t items, int max_ctas = 0) {
 }
 
 // Manager chunks: storage table inspected on the host when the manager was
-// created (vec_ok, max_block_bytes).
+// created (vec_ok, max_block_bytes).  bulk: the bulk-copy kernel (one CTA per
+// SM), for 16-byte aligned tables whose both sides are device memory.
 template <bool kToStaging, typename Ids>
 int block_copy(int device, const ts_block_storage* d_st, int n_st,
                const Ids& d_ids, int64_t n_blocks, uint8_t* staging,
                uint64_t pitch, int* err_flag, void* stream, bool vec_ok,
-               uint64_t max_block_bytes, int max_ctas = 0) {
+               uint64_t max_block_bytes, int max_ctas = 0, bool bulk = false) {
   if (n_blocks == 0 || n_st == 0) return TS_OK;
   const uint32_t ppu = uint32_t((max_block_bytes + kPieceBytes - 1) / kPieceBytes);
   if (ppu == 0) return TS_OK;
@@ -550,7 +672,19 @@ int block_copy(int device, const ts_block_storage* d_st, int n_st,
   DeviceGuard g(device);
   const int grid = launch_grid(device, items, max_ctas);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (vec_ok) {
+  if (bulk && vec_ok) {
+    // opt in to 192 KiB of dynamic shared memory (per device: set each launch)
+    TS_CUDA_RET(cudaFuncSetAttribute(block_copy_bulk_kernel<kToStaging, Ids>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     int(kBulkSmem)),
+                "bulk copy shared memory attribute");
+    const int64_t ctas = (items + kBulkWarps - 1) / kBulkWarps;
+    int bgrid = sm_count(device);
+    if (max_ctas > 0 && max_ctas < bgrid) bgrid = max_ctas;
+    if (ctas < bgrid) bgrid = int(ctas);
+    block_copy_bulk_kernel<kToStaging, Ids><<<bgrid, kBulkWarps * 32, kBulkSmem, s>>>(
+        d_st, n_st, d_ids, n_blocks, staging, pitch, ppu, err_flag);
+  } else if (vec_ok) {
     block_copy_vec_kernel<kToStaging, Ids><<<grid, kThreads, 0, s>>>(
         d_st, n_st, d_ids, n_blocks, staging, pitch, ppu, err_flag);
   } else {
@@ -643,24 +777,24 @@ uint64_t fp8_block_bytes_hint(int n_st, uint64_t pitch, uint64_t scale_off) {
 int mgr_extract(int device, const ts_block_storage* d_st, int n_st,
                 const ParamIds& ids, int64_t n_blocks, void* staging,
                 uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
-                uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas) {
+                uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas, bool bulk) {
   if (fp8)
     return launch_extract_fp8(device, d_st, n_st, ids, n_blocks, staging, pitch,
                               scale_off, err_flag, s, max_bb, max_ctas, 0);
   return block_copy<true>(device, d_st, n_st, ids, n_blocks, static_cast<uint8_t*>(staging),
-                          pitch, err_flag, s, vec_ok, max_bb, max_ctas);
+                          pitch, err_flag, s, vec_ok, max_bb, max_ctas, bulk);
 }
 
 int mgr_insert(int device, const ts_block_storage* d_st, int n_st,
                const ParamIds& ids, int64_t n_blocks, const void* staging,
                uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
-               uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas) {
+               uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas, bool bulk) {
   if (fp8)
     return launch_insert_fp8(device, d_st, n_st, ids, n_blocks, staging, pitch,
                              scale_off, err_flag, s, max_bb, max_ctas, 0);
   return block_copy<false>(device, d_st, n_st, ids, n_blocks,
                            static_cast<uint8_t*>(const_cast<void*>(staging)), pitch, err_flag,
-                           s, vec_ok, max_bb, max_ctas);
+                           s, vec_ok, max_bb, max_ctas, bulk);
 }
 
 }  // namespace tsb

@@ -445,13 +445,15 @@ int launch_chunk(ts_manager* m, bool to_host, const ParamIds& ids, int64_t cn,
   // piece its CTAs retire as pieces land, so other kernels get SM slots.
   const int ctas = !to_host && ids.direct && (m->sched & TS_SCHED_RELOAD_PER_PIECE) != 0
                        ? -1 : m->max_ctas;
+  // bulk copies only between device buffers (staged chunks)
+  const bool bulk = !ids.direct && (m->sched & TS_SCHED_BULK_COPY) != 0;
   int rc = to_host
                ? mgr_extract(m->device, m->d_table, int(m->st.size()), ids, cn, staging,
                              m->host_pitch, err_dev, ks, m->vec_ok, m->max_bb, m->fp8,
-                             m->scale_off, m->max_ctas)
+                             m->scale_off, m->max_ctas, bulk)
                : mgr_insert(m->device, m->d_table, int(m->st.size()), ids, cn, staging,
                             m->host_pitch, err_dev, ks, m->vec_ok, m->max_bb, m->fp8,
-                            m->scale_off, ctas);
+                            m->scale_off, ctas, bulk);
   if (rc != TS_OK) return rc;
   if (m->profiling) {
     TS_CUDA_RET(cudaEventRecord(e1, ks), "event record");
@@ -968,7 +970,7 @@ extern "C" int ts_mgr_create(const ts_storage_desc* storages, int num_layers,
                                ? opts->reload_staged_every : 0;
   m->sched = opts ? opts->sched : 0;
   if (m->sched < 0 || m->sched > (TS_SCHED_OFFLOAD_PRIORITY | TS_SCHED_RELOAD_PER_PIECE |
-                                  TS_SCHED_RELOAD_OVERLAP)) {
+                                  TS_SCHED_RELOAD_OVERLAP | TS_SCHED_BULK_COPY)) {
     delete m;
     return set_error(TS_INVALID_ARGUMENT, "sched must be a sum of TS_SCHED_* flags");
   }

@@ -41,14 +41,16 @@ struct ParamIds {
 // Chunk launchers of kv_block_kernels.cu used by the manager.  max_ctas caps
 // the grid (0 = a full wave of every SM); max_ctas < 0 launches one CTA per
 // work item (16 KiB piece) instead of a persistent grid (plain copies only).
+// bulk selects the bulk-copy kernel for plain copies whose both sides are
+// device memory (ignored for fp8 and for unaligned tables).
 int mgr_extract(int device, const ts_block_storage* d_st, int n_st,
                 const ParamIds& ids, int64_t n_blocks, void* staging,
                 uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
-                uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas);
+                uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas, bool bulk);
 int mgr_insert(int device, const ts_block_storage* d_st, int n_st,
                const ParamIds& ids, int64_t n_blocks, const void* staging,
                uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
-               uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas);
+               uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas, bool bulk);
 
 // Strided byte runs for seg_copy (seg_copy.cu): row r of `count` rows of
 // `bytes` bytes goes from src + r*src_stride to dst + r*dst_stride.  src / dst

@@ -196,7 +196,8 @@ class KVCacheManager:
       raise ValueError(f"mode must be one of {sorted(modes)}")
     flags = {"offload_priority": _native.SCHED_OFFLOAD_PRIORITY,
              "reload_per_piece": _native.SCHED_RELOAD_PER_PIECE,
-             "reload_overlap": _native.SCHED_RELOAD_OVERLAP}
+             "reload_overlap": _native.SCHED_RELOAD_OVERLAP,
+             "bulk_copy": _native.SCHED_BULK_COPY}
     if isinstance(sched, str):
       sched = (sched,)
     unknown = [f for f in sched if f not in flags]
