@@ -9,14 +9,18 @@ in flight together.  A block is 2 MiB (32 layers x K/V x 16 tokens x 8 heads x
 
   value      offload + reload bytes of all ranks / device time (CUDA events,
              max over ranks), through the C ABI manager with the pool resident
-             in HBM and block lists prepared before the timed region
+             in HBM and block lists prepared before the timed region; the K
+             steps are issued back to back (the manager orders dependent
+             blocks), and `step_synchronous` times them one at a time
   e2e        the same through the Python KVCacheManager.d2h/h2d API from
              Python lists, Await() on each step, host wall clock
-  roofline   the extract kernel (dominant kernel): algorithmic bytes
-             (read + write of every moved block) / its device time, timed live
-             with CUDA events around every launch in the timed region
+  roofline   the kernel with the most live device time (the reload's insert
+             kernel pulling the mapped host tier): host-tier bytes it moved /
+             its device time, CUDA events around every launch in the timed
+             region, against the pinned-memcpy peak of its direction
   pcie       achieved D2H / H2D GB/s of the step against pinned-memcpy peaks
-             measured in this run and the Gen5 x16 spec (64 GB/s)
+             measured in this run (at N > 1 with all ranks copying at once)
+             and the Gen5 x16 spec (64 GB/s)
   cpu_baseline  the reference's host copy loops restated in C (oracle/cpu_ref.c)
              on this box's host cores, on a bounded sample of the workload
 
@@ -485,8 +489,12 @@ def run_reference(args):
 # GPU arm
 # ---------------------------------------------------------------------------
 
-def measure_pcie(torch, device, nbytes=GIB):
-  """Best-of-3 pinned cudaMemcpyAsync D2H, H2D and both at once (GB/s)."""
+def measure_pcie(torch, device, nbytes=GIB, barrier=None):
+  """Best-of-3 pinned cudaMemcpyAsync D2H, H2D and both at once (GB/s).
+
+  With `barrier` (N > 1) every trial starts on all ranks together, so the
+  figures are per-GPU peaks with all N GPUs copying at once: the host link
+  and host memory they share are part of the measured peak."""
   d = torch.empty(nbytes, dtype=torch.uint8, device=device)
   d2 = torch.empty(nbytes, dtype=torch.uint8, device=device)
   h = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
@@ -497,6 +505,8 @@ def measure_pcie(torch, device, nbytes=GIB):
     best = 0.0
     for _ in range(3):
       torch.cuda.synchronize(device)
+      if barrier is not None:
+        barrier()
       e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
       e2 = torch.cuda.Event(enable_timing=True)
       e0.record(s1)
@@ -1188,7 +1198,8 @@ def run_ours(args):
                      reload_staged_every=args.reload_staged_every,
                      sched=tuple(f for f in args.sched.split(",") if f))
 
-  pcie = measure_pcie(torch, device)
+  pcie = measure_pcie(torch, device, barrier=barrier if world > 1 else None)
+  pcie["gpus_copying_at_once"] = world
 
   # Step plans from the C1 access trace: 100k accesses Zipf(1.1) over 200k
   # prefix ids, in batches of 512, run through the tier-2 store (LRU index +
@@ -1232,11 +1243,20 @@ def run_ours(args):
   mgr.kernel_stats("extract")
   mgr.kernel_stats("insert")
   clocks.begin()
+  # The K steps are issued back to back, as an engine issues its batches:
+  # no step waits for the previous one on the host or on the stream; the
+  # manager orders each block after the calls it depends on (a reload of a
+  # host block an earlier offload writes, an offload over a block an earlier
+  # reload still reads).  The end event waits for every step's completion.
   e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
   e0.record(bench_stream)
   futs = []
   for i in range(args.warmup, args.warmup + args.steps):
-    futs.extend(step(plans[i], bench_stream))
+    p_ = plans[i]
+    futs.append(mgr.d2h(p_[0], p_[1], stream=bench_stream))
+    futs.append(mgr.h2d(p_[2], p_[3], stream=bench_stream))
+  for f in futs:
+    f.stream_wait(bench_stream)
   e1.record(bench_stream)
   torch.cuda.synchronize(device)
   clocks.end()
@@ -1249,6 +1269,21 @@ def run_ours(args):
   ext = mgr.kernel_stats("extract")
   ins = mgr.kernel_stats("insert")
   max_ms = max_over_ranks(dev_ms)
+
+  # The same steps one at a time: each step's work starts only after the
+  # previous step completed (reported beside the value).
+  torch.cuda.synchronize(device)
+  barrier()
+  s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+  s0.record(bench_stream)
+  sfuts = []
+  for i in range(args.warmup, args.warmup + args.steps):
+    sfuts.extend(step(plans[i], bench_stream))
+  s1.record(bench_stream)
+  torch.cuda.synchronize(device)
+  for f in sfuts:
+    f.Await()
+  stepwise_ms = max_over_ranks(s0.elapsed_time(s1))
   ms_per_step = max_ms / args.steps
   timed_bytes = sum(plan_bytes[args.warmup:])
   timed_d2h = sum(len(p[0]) for p in plans[args.warmup:]) * pitch
@@ -1300,9 +1335,12 @@ def run_ours(args):
   kern = {}
   direct = {"extract": args.mode in ("direct_d2h", "direct"),
             "insert": args.mode in ("direct_h2d", "direct")}
+  bulk = "bulk_copy" in args.sched.split(",")
   for name, st in (("extract", ext), ("insert", ins)):
+    # the manager runs HBM -> HBM chunks on the bulk-copy kernel when asked
+    kname = "block_copy_bulk_kernel" if bulk and not direct[name] else "block_copy_vec_kernel"
     kern[name] = {
-        "kernel": f"block_copy_vec_kernel<{'true' if name == 'extract' else 'false'}> ({name})",
+        "kernel": f"{kname}<{'true' if name == 'extract' else 'false'}> ({name})",
         "path": (("HBM pool -> mapped host tier over PCIe" if name == "extract" else
                   "mapped host tier over PCIe -> HBM pool") if direct[name] else
                  ("HBM pool -> HBM staging" if name == "extract" else
@@ -1378,6 +1416,11 @@ def run_ours(args):
                      "reload_staged_every": args.reload_staged_every or None,
                      "sched": [f for f in args.sched.split(",") if f]},
         "per_gpu_gbs": round(value / world, 3),
+        "step_synchronous": {
+            "value": round(world * timed_bytes / (stepwise_ms * 1e-3) / 1e9, 3),
+            "ms_per_step": round(stepwise_ms / args.steps, 3),
+            "how": "the same K steps, each started only after the previous one completed "
+                   "(its futures waited on the stream)"},
         "pcie": {"offload_d2h_gbs": round(d2h_gbs, 2), "reload_h2d_gbs": round(h2d_gbs, 2),
                  "measured_peak": pcie, "spec_gbs_per_dir": PCIE_SPEC_GBS,
                  "frac_of_measured_duplex": round((d2h_gbs + h2d_gbs) / pcie["duplex"], 3)

@@ -143,7 +143,7 @@ __global__ void __launch_bounds__(kThreads)
 // store.  Six warps per CTA and one CTA per SM keep up to twelve 16 KiB loads
 // in flight per SM in 192 KiB of shared memory while occupying 6 of the SM's
 // 64 warp slots, so the gather can run beside another kernel that holds most
-// of the SM.  Plain (non-multicast) copies of this GPU's own memory only;
+// of the SM.  Plain single-CTA copies of this GPU's own memory only;
 // every address and size is a multiple of 16 (the caller checks vec_ok).
 // Each wait on a load is bounded: past ~2^32 cycles the warp stops, records
 // 3 in err_flag, waits for its issued stores and leaves.
