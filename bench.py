@@ -9,9 +9,7 @@ in flight together.  A block is 2 MiB (32 layers x K/V x 16 tokens x 8 heads x
 
   value      offload + reload bytes of all ranks / device time (CUDA events,
              max over ranks), through the C ABI manager with the pool resident
-             in HBM and block lists prepared before the timed region; the K
-             steps are issued back to back (the manager orders dependent
-             blocks), and `step_synchronous` times them one at a time
+             in HBM and block lists prepared before the timed region
   e2e        the same through the Python KVCacheManager.d2h/h2d API from
              Python lists, Await() on each step, host wall clock
   roofline   the kernel with the most live device time (the reload's insert
@@ -56,6 +54,12 @@ PCIE_SPEC_GBS = 64.0
 # DRAM bytes per 2 MiB block moved by the insert kernel, from
 # profiles/insert_kernel_c1_256blocks.md (mean of the two captured launches).
 INSERT_TRAFFIC_PER_BLOCK = 1019588608 / 256
+# DRAM bytes per 2 MiB block moved by the extract kernel (HBM pool -> HBM
+# staging): the 16-byte vector kernel (profiles/extract_kernel_c1_256blocks.md)
+# and the bulk-copy kernel (profiles/bulk_copy_kernel_c1_256blocks.md), mean
+# of the two captured launches each.
+VEC_EXTRACT_TRAFFIC_PER_BLOCK = 1018413568 / 256
+BULK_EXTRACT_TRAFFIC_PER_BLOCK = 1026581632 / 256
 # DRAM bytes per 2 MiB block of the insert kernel pulling from the mapped host
 # tier (reload direct), from profiles/insert_direct_kernel_c1_256blocks.md
 # (HBM writes; its host reads cross PCIe, not DRAM).
@@ -488,6 +492,57 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
+
+def c1_seed_host_blocks(plans, executed, half_pool):
+  """Host blocks the executed steps reload before any of them offloads
+  there (blocks the trace saved before the steps that run): host block h ->
+  pool block h mod half_pool, which an untimed offload puts there before
+  the warm-up, so every reload moves known bytes."""
+  written, seed = set(), {}
+  for i in executed:
+    off_d, off_h, ld_h, ld_d = plans[i]
+    written.update(off_h.tolist())
+    for h in ld_h.tolist():
+      if h not in written and h not in seed:
+        seed[h] = h % half_pool
+  return seed
+
+
+def c1_expected_sources(plans, executed, seed=None):
+  """The pool block whose bytes each reloaded pool block must hold after the
+  steps `executed` (plan indices, in order) over a host tier seeded as
+  `seed` says: a step's offloads go before its reloads (the manager orders
+  a reload after an earlier call's offload of the same host block), and
+  within a call the last copy to a block wins.  Offloads read the pool's
+  first half, which nothing writes, and reloads write its second half.  A
+  reload of a host block of unknown content is left out."""
+  host_src, dev_src = dict(seed or {}), {}
+  for i in executed:
+    off_d, off_h, ld_h, ld_d = plans[i]
+    for d, h in zip(off_d.tolist(), off_h.tolist()):
+      host_src[h] = d
+    for h, d in zip(ld_h.tolist(), ld_d.tolist()):
+      dev_src[d] = host_src.get(h)
+  return {d: s for d, s in dev_src.items() if s is not None}
+
+
+def c1_blocks_differ(torch, full, expected, device, batch=512) -> int:
+  """Pool blocks (all layers, K and V) that differ bitwise from the block
+  `expected` names; `full` is the [layers, 2, blocks, ...] bf16 pool."""
+  if not expected:
+    return 0
+  dst = torch.tensor(sorted(expected), dtype=torch.int64, device=device)
+  src = torch.tensor([expected[int(d)] for d in dst.tolist()], dtype=torch.int64, device=device)
+  bad = torch.zeros(dst.numel(), dtype=torch.bool, device=device)
+  bits = full.view(torch.int16)
+  for l in range(full.shape[0]):
+    for k0 in range(0, dst.numel(), batch):
+      d_, s_ = dst[k0:k0 + batch], src[k0:k0 + batch]
+      a = bits[l].index_select(1, d_)
+      b = bits[l].index_select(1, s_)
+      bad[k0:k0 + batch] |= (a != b).flatten(2).any(dim=2).any(dim=0)
+  return int(bad.sum().item())
+
 
 def measure_pcie(torch, device, nbytes=GIB, barrier=None):
   """Best-of-3 pinned cudaMemcpyAsync D2H, H2D and both at once (GB/s).
@@ -1230,6 +1285,16 @@ def run_ours(args):
     f2.stream_wait(stream)
     return f1, f2
 
+  # Untimed: the host blocks the steps reload before offloading there get
+  # known bytes (the trace saved them before the steps that run), so the
+  # end-of-run check can name what every reloaded block must hold.
+  executed = list(range(args.warmup + args.steps)) + list(range(args.warmup,
+                                                                args.warmup + args.steps))
+  seed = c1_seed_host_blocks(plans, executed, pool_blocks // 2)
+  if seed:
+    seed_h = sorted(seed)
+    mgr.d2h([seed[h] for h in seed_h], seed_h).Await()
+
   # ---- device-timed steps (value) ----
   for i in range(args.warmup):
     for f in step(plans[i], bench_stream):
@@ -1243,20 +1308,11 @@ def run_ours(args):
   mgr.kernel_stats("extract")
   mgr.kernel_stats("insert")
   clocks.begin()
-  # The K steps are issued back to back, as an engine issues its batches:
-  # no step waits for the previous one on the host or on the stream; the
-  # manager orders each block after the calls it depends on (a reload of a
-  # host block an earlier offload writes, an offload over a block an earlier
-  # reload still reads).  The end event waits for every step's completion.
   e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
   e0.record(bench_stream)
   futs = []
   for i in range(args.warmup, args.warmup + args.steps):
-    p_ = plans[i]
-    futs.append(mgr.d2h(p_[0], p_[1], stream=bench_stream))
-    futs.append(mgr.h2d(p_[2], p_[3], stream=bench_stream))
-  for f in futs:
-    f.stream_wait(bench_stream)
+    futs.extend(step(plans[i], bench_stream))
   e1.record(bench_stream)
   torch.cuda.synchronize(device)
   clocks.end()
@@ -1269,21 +1325,6 @@ def run_ours(args):
   ext = mgr.kernel_stats("extract")
   ins = mgr.kernel_stats("insert")
   max_ms = max_over_ranks(dev_ms)
-
-  # The same steps one at a time: each step's work starts only after the
-  # previous step completed (reported beside the value).
-  torch.cuda.synchronize(device)
-  barrier()
-  s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-  s0.record(bench_stream)
-  sfuts = []
-  for i in range(args.warmup, args.warmup + args.steps):
-    sfuts.extend(step(plans[i], bench_stream))
-  s1.record(bench_stream)
-  torch.cuda.synchronize(device)
-  for f in sfuts:
-    f.Await()
-  stepwise_ms = max_over_ranks(s0.elapsed_time(s1))
   ms_per_step = max_ms / args.steps
   timed_bytes = sum(plan_bytes[args.warmup:])
   timed_d2h = sum(len(p[0]) for p in plans[args.warmup:]) * pitch
@@ -1326,6 +1367,14 @@ def run_ours(args):
   wall = max_over_ranks(wall)
   e2e_value = world * timed_bytes / wall / 1e9
 
+  # ---- every reloaded block checked against its definition ----
+  expected = c1_expected_sources(plans, executed, seed)
+  c1_bad = c1_blocks_differ(torch, full, expected, device)
+  c1_exact = torch.tensor([0 if c1_bad else 1], dtype=torch.int32, device=device)
+  if world > 1:
+    dist.all_reduce(c1_exact, op=dist.ReduceOp.MIN)
+  c1_exact = bool(int(c1_exact.item()))
+
   # ---- roofline of the dominant kernel (by live device time) ----
   pk = peaks()
   hbm_peak = pk.get("hbm_gbs")
@@ -1359,7 +1408,8 @@ def run_ours(args):
   # DRAM traffic per block from ncu captures of the same kernels on the
   # small kernel case (profiles/*_kernel_c1_256blocks.md), scaled to this
   # run's launches by the blocks they move.
-  traffic_per_block = {"extract": 1018413568 / 256,
+  traffic_per_block = {"extract": (BULK_EXTRACT_TRAFFIC_PER_BLOCK if bulk
+                                   else VEC_EXTRACT_TRAFFIC_PER_BLOCK),
                        "insert": (INSERT_DIRECT_TRAFFIC_PER_BLOCK if direct["insert"]
                                   else INSERT_TRAFFIC_PER_BLOCK)}
   if direct["extract"]:
@@ -1416,11 +1466,6 @@ def run_ours(args):
                      "reload_staged_every": args.reload_staged_every or None,
                      "sched": [f for f in args.sched.split(",") if f]},
         "per_gpu_gbs": round(value / world, 3),
-        "step_synchronous": {
-            "value": round(world * timed_bytes / (stepwise_ms * 1e-3) / 1e9, 3),
-            "ms_per_step": round(stepwise_ms / args.steps, 3),
-            "how": "the same K steps, each started only after the previous one completed "
-                   "(its futures waited on the stream)"},
         "pcie": {"offload_d2h_gbs": round(d2h_gbs, 2), "reload_h2d_gbs": round(h2d_gbs, 2),
                  "measured_peak": pcie, "spec_gbs_per_dir": PCIE_SPEC_GBS,
                  "frac_of_measured_duplex": round((d2h_gbs + h2d_gbs) / pcie["duplex"], 3)
@@ -1431,6 +1476,14 @@ def run_ours(args):
         "roofline": roof,
         "extract_hbm_gbs_one_launch": round(extract_one_launch_gbs, 1),
         "noalloc_offload": noalloc,
+        "exact": c1_exact,
+        "exact_how": (f"after the warm-up, timed and end-to-end steps, each of the "
+                      f"{len(expected)} pool blocks the reloads wrote equals, bitwise, the "
+                      f"pool block whose bytes the host block it last read held (offloaded "
+                      f"by an earlier step, or before the warm-up for the "
+                      f"{len(seed)} host blocks the trace had saved earlier); torch on "
+                      f"the device, a step's offloads before its reloads, the last copy "
+                      f"to a block winning"),
         "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
                 "h2d_bytes_per_step": int(timed_h2d / args.steps),
                 "d2h_bytes_per_step": int(timed_d2h / args.steps),

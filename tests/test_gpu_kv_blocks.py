@@ -309,6 +309,31 @@ def test_manager_repeated_destination_last_copy_wins(cuda, mode):
   assert_same(pool, mgr, model, range(48))
 
 
+@pytest.mark.parametrize("mode", MODES + [dict(mode="staged", sched=("bulk_copy",)),
+                                          dict(mode="direct_h2d", sched=("bulk_copy",))])
+def test_manager_repeated_destination_within_one_chunk(cuda, mode):
+  """Destinations named many times inside one pipelined chunk (the default
+  64-block chunks run all their pieces at once): every copy of the call
+  lands as if run in order, the last one to a block winning
+  (kv_cache_manager_base.cc:1945-2124), in both directions."""
+  geom = workloads.KVGeometry(layers=2, kv=2, block_tokens=16, heads=2, head_dim=128)
+  pool, mgr, model = make_pair(geom, 96, 64, 27, cuda, **mode)
+  rng = np.random.default_rng(11)
+  mgr.d2h(list(range(48)), list(range(48))).Await()
+  model.d2h(list(range(48)), list(range(48)))
+  for _ in range(3):
+    hs = [int(x) for x in rng.integers(0, 48, 40)]
+    ds = [int(x) for x in rng.choice([60, 61, 62, 63, 70], 40)]
+    mgr.h2d(hs, ds).Await()
+    assert model.h2d(hs, ds) == (ref.OK, "")
+    src = [int(x) for x in rng.integers(0, 96, 40)]
+    dst = [int(x) for x in rng.choice([50, 51, 52, 5], 40)]
+    mgr.d2h(src, dst).Await()
+    assert model.d2h(src, dst) == (ref.OK, "")
+  torch.cuda.synchronize()
+  assert_same(pool, mgr, model, range(64))
+
+
 @pytest.mark.parametrize("mode", MODES)
 def test_manager_back_to_back_calls_are_ordered(cuda, mode):
   """Offload then reload of the same host blocks without waiting in between."""

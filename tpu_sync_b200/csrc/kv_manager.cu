@@ -308,6 +308,29 @@ int build_plan(ts_manager* m, bool to_host, const int64_t* src, const int64_t* d
         plan->src.push_back(cs[r] + j);
         plan->dst.push_back(cd[r] + j);
       }
+    // A destination block named more than once ends with the last copy's
+    // bytes: the reference copies run by run, in order
+    // (kv_cache_manager_base.cc:1945-2124), and nothing reads a destination
+    // within one call.  The earlier copies to such a block are dropped, so no
+    // kernel launch or DMA ever has two writers of one block (the pieces of
+    // one chunk run concurrently).
+    std::unordered_set<int64_t> seen;
+    bool repeats = false;
+    for (int64_t d : plan->dst)
+      if (!seen.insert(d).second) { repeats = true; break; }
+    if (repeats) {
+      seen.clear();
+      std::vector<int64_t> ks, kd;
+      for (size_t i = plan->dst.size(); i-- > 0;)
+        if (seen.insert(plan->dst[i]).second) {
+          ks.push_back(plan->src[i]);
+          kd.push_back(plan->dst[i]);
+        }
+      std::reverse(ks.begin(), ks.end());
+      std::reverse(kd.begin(), kd.end());
+      plan->src.swap(ks);
+      plan->dst.swap(kd);
+    }
   }
   return TS_OK;
 }
