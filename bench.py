@@ -698,13 +698,81 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
       flat.zero_()
       torch.cuda.synchronize(device)
     dist.barrier()
+  # Staged pull: each trainer casts into its bf16 staging group by group and
+  # publishes the groups in a /dev/shm mailbox; each sampler's kernels read
+  # the staging over NVLink as the groups appear.  Timed per rank from one
+  # barrier over `steps` back-to-back pushes (a trainer's next stage waits
+  # for every sampler to finish the previous pull), max over ranks.
+  pull_ms, pull_error = 0.0, ""
+  token = [f"{os.getpid()}_{int(time.time() * 1e3) % 10**9}" if rank == 0 else None]
+  dist.broadcast_object_list(token, src=0)
+  names = [f"tsb_bench_wpull_{token[0]}_{t_}" for t_ in range(half)]
+  sender = receiver = None
+  try:
+    if is_src:
+      sender = ops.PullSender(names[idx], flat, groups=16)
+  except RuntimeError as e:
+    pull_error = str(e).splitlines()[0][:200]
+  ok = torch.tensor([0 if pull_error else 1], dtype=torch.int32, device=device)
+  dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+  if int(ok.item()):
+    try:
+      if not is_src:
+        receiver = ops.PullReceiver(
+            names, workloads.weight_sync_pull_chunks(plan, layout, idx, flat.data_ptr(), half),
+            device)
+    except RuntimeError as e:
+      pull_error = str(e).splitlines()[0][:200]
+    ok = torch.tensor([0 if pull_error else 1], dtype=torch.int32, device=device)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+  if int(ok.item()):
+    def one_pull():
+      if is_src:
+        sender.stage(timeout_ms=60000)
+      else:
+        receiver.pull(timeout_ms=60000)
+    try:
+      for _ in range(warmup):
+        one_pull()
+      torch.cuda.synchronize(device)
+      dist.barrier()
+      e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+      e0.record()
+      for _ in range(steps):
+        one_pull()
+      e1.record()
+      torch.cuda.synchronize(device)
+      pull_ms = e0.elapsed_time(e1) / steps
+    except RuntimeError as e:
+      pull_error = str(e).splitlines()[0][:200]
+      torch.cuda.synchronize(device)
+    ok = torch.tensor([0 if pull_error else 1], dtype=torch.int32, device=device)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if not int(ok.item()) and not pull_error:
+      pull_error = "failed on another rank"
+    dist.barrier()
+    if not is_src and not pull_error:
+      mismatched["pull"] = c4_shards_exact(torch, device, params, half, idx, flat)
+      flat.zero_()
+      torch.cuda.synchronize(device)
+  elif not pull_error:
+    pull_error = "failed on another rank"
+  if pull_error:
+    pull_ms = 0.0
+  if receiver is not None:
+    receiver.close()  # the samplers' mappings go before the trainers' staging
+  dist.barrier()
+  if sender is not None:
+    sender.close()
   exact = torch.tensor([0 if any(mismatched.values()) else 1], dtype=torch.int32, device=device)
   dist.all_reduce(exact, op=dist.ReduceOp.MIN)
-  t = torch.tensor([per_push_ms, ce_ms], dtype=torch.float64, device=device)
+  t = torch.tensor([per_push_ms, ce_ms, pull_ms], dtype=torch.float64, device=device)
   dist.all_reduce(t, op=dist.ReduceOp.MAX)
-  sm_s, ce_s = float(t[0].item()) / 1e3, float(t[1].item()) / 1e3
-  push_s = min(sm_s, ce_s) if ce_s > 0 else sm_s
-  engine = "copy" if push_s == ce_s and ce_s > 0 else "sm"
+  sm_s, ce_s, pull_s = (float(t[0].item()) / 1e3, float(t[1].item()) / 1e3,
+                        float(t[2].item()) / 1e3)
+  runs = {"sm": sm_s, "copy": ce_s, "pull": pull_s}
+  engine = min((k for k, v in runs.items() if v > 0), key=lambda k: runs[k])
+  push_s = runs[engine]
   recv_bytes = max(2 * plan.elements_to(d) for d in range(half))
   total_params = sum(math.prod(v.shape) for v in specs)
   del prog
@@ -725,7 +793,14 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
                       "copy": {"how": "the kernel casts into local staging, the copy engines "
                                       "move each chunk (cudaMemcpy2DAsync), 16 pipelined groups",
                                "seconds": round(ce_s, 5) if not ce_error else None,
-                               **({"error": ce_error} if ce_error else {})}},
+                               **({"error": ce_error} if ce_error else {})},
+                      "pull": {"how": "each trainer casts into local bf16 staging in 16 groups "
+                                      "published through a /dev/shm mailbox; each sampler's "
+                                      "kernels load the staging over NVLink as groups appear "
+                                      "(back-to-back pushes, each waiting for the previous "
+                                      "pull to finish)",
+                               "seconds": round(pull_s, 5) if not pull_error else None,
+                               **({"error": pull_error} if pull_error else {})}},
           "chunks_per_src": len(plan.for_source(0)),
           "exact": bool(int(exact.item())),
           "exact_how": ("every sampler's bf16 TP shards of all parameters, after each "

@@ -479,6 +479,58 @@ TS_API int ts_reshard_ce_info(ts_reshard_ce* program, int64_t* groups,
                               uint64_t* staging_bytes, int64_t* copies);
 TS_API int ts_reshard_ce_destroy(ts_reshard_ce* program);
 
+/* Weight-sync reshard pulled by the receivers ("staged pull").  On this
+ * platform a GPU's NVLink loads of a peer's memory run at the peer-copy
+ * rate while its stores into a peer stop near 0.92 of it, so this variant
+ * moves the bytes with loads: the sender casts its fp32 shard into a local
+ * bf16 staging buffer of the same element layout, group by group, and
+ * publishes each group's readiness in a /dev/shm mailbox; every receiver
+ * maps the staging (CUDA IPC) and, as groups become ready, launches the
+ * strided copies of its chunks that need nothing beyond them.  No kernel
+ * waits on another GPU: readiness travels through host memory.  Replaces,
+ * like ts_reshard_copy, PushWeightsResharded's D2H + TCP push + H2D
+ * (weight_synchronizer_base.cc:558-760), with the direction of the data
+ * plane's requests reversed (the receiver reads).
+ *
+ * Sender: `name` is the mailbox (a /dev/shm name; the creator owns and
+ * unlinks it).  `src` holds n_elems fp32 values (the shard, as the
+ * receivers' chunks address it); n_groups (1..64) equal element ranges,
+ * each a multiple of 8 elements except the last.  stage() casts every group
+ * on the sender's stream ordered after `stream`'s queued work (the caller's
+ * stream then waits for the staging to be written) and publishes group g as
+ * soon as it is written; before overwriting the staging it waits, at most
+ * `timeout_ms`, until every receiver that attached has finished pulling the
+ * previous generation (TS_DEADLINE_EXCEEDED otherwise, nothing queued).
+ * wait() returns once every group of the last stage() is published. */
+typedef struct ts_wpull_src ts_wpull_src;
+TS_API int ts_wpull_src_create(int device, const char* name, const void* src_f32,
+                               int64_t n_elems, int n_groups, ts_wpull_src** out);
+TS_API int ts_wpull_src_stage(ts_wpull_src* src, void* stream, int64_t timeout_ms);
+TS_API int ts_wpull_src_wait(ts_wpull_src* src, int64_t timeout_ms);
+TS_API int ts_wpull_src_info(ts_wpull_src* src, int64_t* generation, int64_t* groups,
+                             uint64_t* staging_bytes, int64_t* receivers);
+TS_API int ts_wpull_src_destroy(ts_wpull_src* src);
+
+/* Receiver: attaches to the mailboxes `names[0..n_src)`.  Each chunk's
+ * src_ptr is the INDEX of its sender in `names` (not an address); src_off,
+ * strides and size count bf16 elements of that sender's staging; dst_ptr /
+ * dst_off / dst_stride address this GPU's bf16 destination.  Every chunk is
+ * checked against its sender's staging before anything is created.  pull()
+ * is one generation: it launches, on `stream` and in group order, the
+ * copies of every chunk as soon as each sender has published the groups the
+ * chunk reads (the host thread waits on the mailboxes, at most timeout_ms in
+ * all; TS_DEADLINE_EXCEEDED leaves the copies already queued in place), then
+ * tells the senders when the copies have finished, so their next stage()
+ * may overwrite the staging.  Later work on `stream` sees the bytes. */
+typedef struct ts_wpull_dst ts_wpull_dst;
+TS_API int ts_wpull_dst_create(int device, const char* const* names, int n_src,
+                               const ts_reshard_chunk* chunks, int64_t n_chunks,
+                               ts_wpull_dst** out);
+TS_API int ts_wpull_dst_pull(ts_wpull_dst* dst, void* stream, int64_t timeout_ms);
+TS_API int ts_wpull_dst_info(ts_wpull_dst* dst, int64_t* generation, int64_t* launches,
+                             uint64_t* bytes);
+TS_API int ts_wpull_dst_destroy(ts_wpull_dst* dst);
+
 /* ------------------------------------------------------------------------ */
 /* Weight synchronizer (resharded push of controller-made schedules).        */
 /* ------------------------------------------------------------------------ */

@@ -373,6 +373,18 @@ _SIGS = {
     "ts_reshard_ce_launch": (ctypes.c_int, [_V, _V]),
     "ts_reshard_ce_info": (ctypes.c_int, [_V, c_i64_p, c_u64_p, c_i64_p]),
     "ts_reshard_ce_destroy": (ctypes.c_int, [_V]),
+    "ts_wpull_src_create": (ctypes.c_int, [ctypes.c_int, ctypes.c_char_p, _V, ctypes.c_int64,
+                                           ctypes.c_int, ctypes.POINTER(_V)]),
+    "ts_wpull_src_stage": (ctypes.c_int, [_V, _V, ctypes.c_int64]),
+    "ts_wpull_src_wait": (ctypes.c_int, [_V, ctypes.c_int64]),
+    "ts_wpull_src_info": (ctypes.c_int, [_V, c_i64_p, c_i64_p, c_u64_p, c_i64_p]),
+    "ts_wpull_src_destroy": (ctypes.c_int, [_V]),
+    "ts_wpull_dst_create": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_char_p),
+                                           ctypes.c_int, _V, ctypes.c_int64,
+                                           ctypes.POINTER(_V)]),
+    "ts_wpull_dst_pull": (ctypes.c_int, [_V, _V, ctypes.c_int64]),
+    "ts_wpull_dst_info": (ctypes.c_int, [_V, c_i64_p, c_i64_p, c_u64_p]),
+    "ts_wpull_dst_destroy": (ctypes.c_int, [_V]),
     "ts_kv_metadata_required_bytes": (ctypes.c_uint64, [ctypes.c_int]),
     "ts_kv_metadata_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int, ctypes.c_char_p,
                                            ctypes.POINTER(_V), ctypes.POINTER(ctypes.c_int)]),

@@ -257,6 +257,103 @@ class ReshardCopyEngineProgram:
       pass
 
 
+class PullSender:
+  """Sender side of the staged-pull weight sync (ts_wpull_src_*): casts the
+  fp32 `src` (a 1-D CUDA tensor, the shard as the receivers' chunks address
+  it) into a bf16 staging of the same element layout in `groups` groups, and
+  publishes each group in the /dev/shm mailbox `name` as soon as it is
+  written.  `stage()` is one generation; it first waits until every attached
+  receiver has pulled the previous one."""
+
+  def __init__(self, name: str, src: torch.Tensor, groups: int = 16):
+    if src.dtype != torch.float32 or not src.is_cuda or not src.is_contiguous():
+      raise ValueError("PullSender needs a contiguous fp32 CUDA tensor")
+    self.device = src.device
+    self.name = name
+    self._src = src  # kept alive: the cast kernels read it
+    h = ctypes.c_void_p()
+    _native.check(_native.lib().ts_wpull_src_create(
+        self.device.index, name.encode(), ctypes.c_void_p(src.data_ptr()), src.numel(),
+        int(groups), ctypes.byref(h)), "weight pull sender: ")
+    self._h = h
+    g, b = ctypes.c_int64(), ctypes.c_uint64()
+    _native.check(_native.lib().ts_wpull_src_info(h, None, ctypes.byref(g), ctypes.byref(b), None))
+    self.groups, self.staging_bytes = g.value, b.value
+
+  def stage(self, stream: Optional[torch.cuda.Stream] = None, timeout_ms: int = 30000) -> None:
+    _native.check(_native.lib().ts_wpull_src_stage(self._h, _stream(stream, self.device),
+                                                   int(timeout_ms)), "weight pull sender: ")
+
+  def wait(self, timeout_ms: int = 30000) -> None:
+    _native.check(_native.lib().ts_wpull_src_wait(self._h, int(timeout_ms)),
+                  "weight pull sender: ")
+
+  @property
+  def receivers(self) -> int:
+    n = ctypes.c_int64()
+    _native.check(_native.lib().ts_wpull_src_info(self._h, None, None, None, ctypes.byref(n)))
+    return n.value
+
+  def close(self) -> None:
+    if getattr(self, "_h", None):
+      _native.lib().ts_wpull_src_destroy(self._h)
+      self._h = None
+
+  def __del__(self):
+    try:
+      self.close()
+    except Exception:
+      pass
+
+
+class PullReceiver:
+  """Receiver side of the staged-pull weight sync (ts_wpull_dst_*).
+
+  names: the senders' mailboxes.  chunks: iterables (sender_index,
+  dst_tensor_or_ptr, src_off, dst_off, size, src_stride, dst_stride, count)
+  in bf16 elements; the source is the sender's staging (its fp32 shard's
+  element layout).  `pull()` launches every chunk's copy on `stream` as soon
+  as the groups it reads are published, and returns once all are queued."""
+
+  def __init__(self, names: Sequence[str], chunks, device: torch.device):
+    self.device = torch.device(device)
+    chunks = list(chunks)
+    _check_chunks([(None,) + tuple(c[1:]) for c in chunks], 2, 2)
+    arr = (_native.ReshardChunk * max(len(chunks), 1))()
+    self._keep = []
+    for i, (t, dp, so, do, size, ss, ds, cnt) in enumerate(chunks):
+      arr[i].src_ptr = int(t)
+      arr[i].dst_ptr = dp.data_ptr() if hasattr(dp, "data_ptr") else int(dp)
+      if hasattr(dp, "data_ptr"):
+        self._keep.append(dp)
+      arr[i].src_off, arr[i].dst_off, arr[i].size = int(so), int(do), int(size)
+      arr[i].src_stride, arr[i].dst_stride, arr[i].count = int(ss), int(ds), int(cnt)
+    cnames = (ctypes.c_char_p * len(names))(*[n.encode() for n in names])
+    h = ctypes.c_void_p()
+    _native.check(_native.lib().ts_wpull_dst_create(
+        self.device.index, cnames, len(names), arr, len(chunks), ctypes.byref(h)),
+        "weight pull receiver: ")
+    self._h = h
+    lc, b = ctypes.c_int64(), ctypes.c_uint64()
+    _native.check(_native.lib().ts_wpull_dst_info(h, None, ctypes.byref(lc), ctypes.byref(b)))
+    self.launches, self.bytes = lc.value, b.value
+
+  def pull(self, stream: Optional[torch.cuda.Stream] = None, timeout_ms: int = 30000) -> None:
+    _native.check(_native.lib().ts_wpull_dst_pull(self._h, _stream(stream, self.device),
+                                                  int(timeout_ms)), "weight pull receiver: ")
+
+  def close(self) -> None:
+    if getattr(self, "_h", None):
+      _native.lib().ts_wpull_dst_destroy(self._h)
+      self._h = None
+
+  def __del__(self):
+    try:
+      self.close()
+    except Exception:
+      pass
+
+
 def kv_relayout(src_storages: Sequence, dst_storages: Sequence, src_geom: dict,
                 dst_geom: dict, src_table: torch.Tensor, dst_table: torch.Tensor,
                 seq_tokens: int, device=None,

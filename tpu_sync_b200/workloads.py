@@ -190,6 +190,23 @@ def weight_sync_chunks(plan, layout, src_slot: int, src_base: int, dst_bases,
   return out
 
 
+def weight_sync_pull_chunks(plan, layout, dst_slot: int, dst_base: int, n_src: int,
+                            dst_itemsize: int = 2):
+  """One sampler slot's chunks for the staged pull (ops.PullReceiver):
+  (trainer slot, dst address, src element offset in that trainer's flat
+  buffer, dst element offset, size, src stride, dst stride, count)."""
+  src, dst = layout
+  out = []
+  for s in range(n_src):
+    for (vi, d), cs in plan.for_source(s).items():
+      if d != dst_slot:
+        continue
+      dp = dst_base + dst_itemsize * dst[d][0][vi]
+      for (so, do, size, ss, ds, cnt) in cs:
+        out.append((s, dp, src[s][0][vi] + so, do, size, ss, ds, cnt))
+  return out
+
+
 # ---------------------------------------------------------------------------
 # C1 access trace driving the tier-2 store
 # ---------------------------------------------------------------------------
