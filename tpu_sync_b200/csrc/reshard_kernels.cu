@@ -8,9 +8,11 @@
 // the chunks execute as one kernel that reads the local shard in HBM and
 // stores straight into the destination tensor, which may live on a peer GPU
 // (P2P stores over NVLink through a peer-mapped pointer).  Work is flattened
-// over (chunk, row, 8-element vector); per CTA work item 256 threads x 2
-// vectors.  Loads use 16-byte vectors when the chunk's rows are 16-byte
-// aligned on both sides, else a scalar path.  Bound: NVLink (peer) or HBM.
+// over (chunk, row, 8-element vector); per CTA work item 256 threads x 4
+// vectors, all four loads of a thread issued before its stores, on a
+// persistent grid of as many CTAs as fit on the SMs at once.  Loads use
+// 16-byte vectors when the chunk's rows are 16-byte aligned on both sides,
+// else a scalar path.  Bound: NVLink (peer) or HBM.
 //
 // Relayout: destination-block-centric copy of 16-byte vectors of head
 // vectors between two page geometries (tokens per block, head-major or
@@ -28,7 +30,7 @@ namespace tsb {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kVecPerThread = 2;
+constexpr int kVecPerThread = 4;
 constexpr int kCtasPerSm = 8;
 
 __device__ __forceinline__ int4 ld_nc(const void* p) {
@@ -52,11 +54,15 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 }
 
 // Element transfer policies.  VEC elements per vector step.
+// Element transfer policies: load() one vector of VEC elements into
+// registers, store() it (converted) to the destination.
 struct CopyBytes {  // raw bytes: 16 per vector
   static constexpr int VEC = 16;
   static constexpr int SRC_ES = 1;
   static constexpr int DST_ES = 1;
-  __device__ static void vec(const uint8_t* s, uint8_t* d) { st_v4(d, ld_nc(s)); }
+  using Reg = int4;
+  __device__ static Reg load(const uint8_t* s) { return ld_nc(s); }
+  __device__ static void store(uint8_t* d, const Reg& v) { st_v4(d, v); }
   __device__ static void one(const uint8_t* s, uint8_t* d) { *d = *s; }
 };
 
@@ -64,14 +70,16 @@ struct F32ToBf16 {  // 8 floats (32 B) -> 8 bf16 (16 B)
   static constexpr int VEC = 8;
   static constexpr int SRC_ES = 4;
   static constexpr int DST_ES = 2;
-  __device__ static void vec(const uint8_t* s, uint8_t* d) {
-    const int4 a = ld_nc(s);
-    const int4 b = ld_nc(s + 16);
+  struct Reg {
+    int4 a, b;
+  };
+  __device__ static Reg load(const uint8_t* s) { return Reg{ld_nc(s), ld_nc(s + 16)}; }
+  __device__ static void store(uint8_t* d, const Reg& v) {
     int4 o;
-    o.x = int(pack_bf16x2(__int_as_float(a.x), __int_as_float(a.y)));
-    o.y = int(pack_bf16x2(__int_as_float(a.z), __int_as_float(a.w)));
-    o.z = int(pack_bf16x2(__int_as_float(b.x), __int_as_float(b.y)));
-    o.w = int(pack_bf16x2(__int_as_float(b.z), __int_as_float(b.w)));
+    o.x = int(pack_bf16x2(__int_as_float(v.a.x), __int_as_float(v.a.y)));
+    o.y = int(pack_bf16x2(__int_as_float(v.a.z), __int_as_float(v.a.w)));
+    o.z = int(pack_bf16x2(__int_as_float(v.b.x), __int_as_float(v.b.y)));
+    o.w = int(pack_bf16x2(__int_as_float(v.b.z), __int_as_float(v.b.w)));
     st_v4(d, o);
   }
   __device__ static void one(const uint8_t* s, uint8_t* d) {
@@ -107,21 +115,31 @@ __global__ void __launch_bounds__(kThreads)
     const bool aligned = ((a_src | (uint64_t(src_stride) * P::SRC_ES)) & 15u) == 0 &&
                          ((a_dst | (uint64_t(dst_stride) * P::DST_ES)) & 15u) == 0;
     const int64_t g0 = (w - prefix[lo]) * int64_t(kThreads) * kVecPerThread;
+    // every vector load of the thread is issued before its first store
+    // (kVecPerThread loads in flight: what hides NVLink latency when the
+    // source is a peer's memory)
+    typename P::Reg v[kVecPerThread];
+    uint8_t* dv[kVecPerThread];
 #pragma unroll
     for (int i = 0; i < kVecPerThread; ++i) {
+      dv[i] = nullptr;
       const int64_t g = g0 + threadIdx.x + int64_t(i) * kThreads;
-      if (g >= total) break;
+      if (g >= total) continue;
       const int64_t row = g / vpr;
       const int64_t e0 = (g - row * vpr) * P::VEC;
       const int64_t n = size - e0 < P::VEC ? size - e0 : P::VEC;
       const uint8_t* s = src + (src_off + row * src_stride + e0) * P::SRC_ES;
       uint8_t* d = dst + (dst_off + row * dst_stride + e0) * P::DST_ES;
       if (aligned && n == P::VEC) {
-        P::vec(s, d);
+        v[i] = P::load(s);
+        dv[i] = d;
       } else {
         for (int64_t e = 0; e < n; ++e) P::one(s + e * P::SRC_ES, d + e * P::DST_ES);
       }
     }
+#pragma unroll
+    for (int i = 0; i < kVecPerThread; ++i)
+      if (dv[i] != nullptr) P::store(dv[i], v[i]);
   }
 }
 
@@ -354,13 +372,23 @@ extern "C" int ts_reshard_copy(int device, const ts_reshard_chunk* d_chunks,
   if (es == 0 || tsb::es_of(dst_dtype) == 0) return set_error(TS_INVALID_ARGUMENT, "unknown dtype");
   tsb::DeviceGuard g(device);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const int64_t cap = int64_t(tsb::sm_count(device)) * tsb::kCtasPerSm;
-  const int grid = int(n_items < cap ? n_items : cap);
+  // a persistent grid: the CTAs that fit on the SMs at once
+  auto grid_for = [&](const void* fn) {
+    static int per_sm[2] = {0, 0};
+    int& occ = per_sm[fn == reinterpret_cast<const void*>(tsb::reshard_kernel<tsb::CopyBytes>)];
+    if (occ == 0 && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, tsb::kThreads, 0) !=
+                        cudaSuccess)
+      occ = 4;
+    const int64_t cap = int64_t(tsb::sm_count(device)) * (occ > 0 ? occ : 1);
+    return int(n_items < cap ? n_items : cap);
+  };
   if (src_dtype == dst_dtype) {
     // Identity copies run as raw bytes: chunk element units scaled by es.
+    const int grid = grid_for(reinterpret_cast<const void*>(tsb::reshard_kernel<tsb::CopyBytes>));
     tsb::reshard_kernel<tsb::CopyBytes><<<grid, tsb::kThreads, 0, s>>>(
         d_chunks, d_item_prefix, n_chunks, n_items, es);
   } else if (src_dtype == TS_DTYPE_F32 && dst_dtype == TS_DTYPE_BF16) {
+    const int grid = grid_for(reinterpret_cast<const void*>(tsb::reshard_kernel<tsb::F32ToBf16>));
     tsb::reshard_kernel<tsb::F32ToBf16><<<grid, tsb::kThreads, 0, s>>>(
         d_chunks, d_item_prefix, n_chunks, n_items, 1);
   } else {
