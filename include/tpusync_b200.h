@@ -494,8 +494,9 @@ TS_API int ts_reshard_ce_destroy(ts_reshard_ce* program);
  *
  * Sender: `name` is the mailbox (a /dev/shm name; the creator owns and
  * unlinks it).  `src` holds n_elems fp32 values (the shard, as the
- * receivers' chunks address it); n_groups (1..64) equal element ranges,
- * each a multiple of 8 elements except the last.  stage() casts every group
+ * receivers' chunks address it).  n_groups (1..61) sets the group size,
+ * n_elems / n_groups rounded up to 8 elements; the first three groups are
+ * 1/8, 1/4 and 1/2 of it, so receivers can start early.  stage() casts every group
  * on the sender's stream ordered after `stream`'s queued work (the caller's
  * stream then waits for the staging to be written) and publishes group g as
  * soon as it is written; before overwriting the staging it waits, at most

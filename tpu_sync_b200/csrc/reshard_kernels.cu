@@ -95,12 +95,17 @@ __global__ void __launch_bounds__(kThreads)
     reshard_kernel(const ts_reshard_chunk* __restrict__ chunks,
                    const int64_t* __restrict__ prefix, int64_t n_chunks,
                    int64_t n_items, int64_t scale) {
+  int64_t lo = 0;  // chunk of this CTA's previous item (prefix[lo] <= w)
   for (int64_t w = blockIdx.x; w < n_items; w += gridDim.x) {
-    // chunk c with prefix[c] <= w < prefix[c+1]
-    int64_t lo = 0, hi = n_chunks;
-    while (hi - lo > 1) {
-      const int64_t mid = (lo + hi) >> 1;
-      if (prefix[mid] <= w) lo = mid; else hi = mid;
+    // chunk c with prefix[c] <= w < prefix[c+1]: the previous item's chunk,
+    // or a binary search over the chunks after it (a CTA's items grow)
+    if (prefix[lo + 1] <= w) {
+      int64_t hi = n_chunks;
+      ++lo;
+      while (hi - lo > 1) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (prefix[mid] <= w) lo = mid; else hi = mid;
+      }
     }
     const ts_reshard_chunk c = chunks[lo];
     const int64_t size = c.size * scale;

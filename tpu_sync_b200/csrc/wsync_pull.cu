@@ -53,8 +53,9 @@ namespace wpull {
 namespace {
 
 constexpr uint64_t kMagic = 0x314c4c5550575354ull;  // "TSWPULL1" little-endian
-constexpr uint32_t kVersion = 1;
-constexpr int kMaxGroups = 64;
+constexpr uint32_t kVersion = 2;
+constexpr int kMaxGroups = 64;   // groups per staging (n_groups + 3 at most)
+constexpr int kMaxGroupArg = kMaxGroups - 3;
 constexpr int kMaxReceivers = 16;
 constexpr uint64_t kDetached = ~uint64_t(0);  // a receiver slot nobody waits for
 constexpr size_t kBoxBytes = 4096;
@@ -66,7 +67,7 @@ struct alignas(64) Box {
   int32_t pid;         // the sender process
   int32_t n_groups;
   uint64_t n_elems;      // bf16 elements of the staging
-  uint64_t group_elems;  // elements per group (the last may be shorter)
+  uint64_t group_elems;  // the full group size (elements)
   uint64_t dev_ptr;      // the staging's address in the sender's process
   uint8_t handle[64];    // cudaIpcMemHandle_t of the staging allocation
   uint64_t offset;       // the staging's byte offset in that allocation
@@ -74,6 +75,7 @@ struct alignas(64) Box {
   std::atomic<int32_t> n_receivers;   // receiver slots claimed
   alignas(64) std::atomic<uint64_t> ready[kMaxGroups];     // generation published per group
   alignas(64) std::atomic<uint64_t> done[kMaxReceivers];   // generation pulled per receiver
+  uint64_t bounds[kMaxGroups + 1];  // group g = staging elements [bounds[g], bounds[g + 1])
 };
 static_assert(sizeof(Box) <= kBoxBytes, "mailbox layout");
 static_assert(std::atomic<uint64_t>::is_always_lock_free, "lock-free mailbox words");
@@ -200,18 +202,29 @@ extern "C" int ts_wpull_src_create(int device, const char* name, const void* src
   if (!out || !name || !src_f32 || n_elems <= 0)
     return set_error(TS_INVALID_ARGUMENT, "invalid arguments");
   *out = nullptr;
-  if (n_groups < 1 || n_groups > kMaxGroups)
-    return set_errorf(TS_INVALID_ARGUMENT, "n_groups must be in [1, %d]", kMaxGroups);
+  if (n_groups < 1 || n_groups > kMaxGroupArg)
+    return set_errorf(TS_INVALID_ARGUMENT, "n_groups must be in [1, %d]", kMaxGroupArg);
   if (reinterpret_cast<uintptr_t>(src_f32) % 16 != 0)
     return set_error(TS_INVALID_ARGUMENT, "the fp32 source must be 16-byte aligned");
   auto* p = new ts_wpull_src();
   p->device = device;
   p->path = shm_path(name);
   p->n_elems = uint64_t(n_elems);
-  // groups of a multiple of 8 elements (whole 16-byte bf16 vectors)
+  // Group size ge = n_elems / n_groups, a multiple of 8 elements (whole
+  // 16-byte bf16 vectors).  The first three groups are ge/8, ge/4 and ge/2:
+  // receivers can start after a short first cast, and the cast of each next
+  // group still finishes before the receivers have read the previous one
+  // (the cast moves 6 bytes of HBM per element, a receiver 2 of NVLink).
   uint64_t ge = (uint64_t(n_elems) + uint64_t(n_groups) - 1) / uint64_t(n_groups);
   ge = (ge + 7) / 8 * 8;
-  const int groups = int((uint64_t(n_elems) + ge - 1) / ge);
+  std::vector<uint64_t> bounds{0};
+  while (bounds.back() < uint64_t(n_elems)) {
+    const int k = int(bounds.size()) - 1;
+    uint64_t sz = k < 3 ? (ge >> (3 - k)) : ge;
+    sz = std::max<uint64_t>(8, (sz + 7) / 8 * 8);
+    bounds.push_back(std::min<uint64_t>(bounds.back() + sz, uint64_t(n_elems)));
+  }
+  const int groups = int(bounds.size()) - 1;
   tsb::DeviceGuard g(device);
   cudaError_t ce = cudaMalloc(&p->staging, uint64_t(n_elems) * 2);
   if (ce != cudaSuccess) {
@@ -219,7 +232,7 @@ extern "C" int ts_wpull_src_create(int device, const char* name, const void* src
     return tsb::cuda_error(ce, "pull staging");
   }
   for (int k = 0; k < groups; ++k) {
-    const uint64_t a = uint64_t(k) * ge, b = std::min<uint64_t>(a + ge, uint64_t(n_elems));
+    const uint64_t a = bounds[size_t(k)], b = bounds[size_t(k) + 1];
     ts_reshard_chunk c{};
     c.src_ptr = reinterpret_cast<uint64_t>(src_f32);
     c.dst_ptr = reinterpret_cast<uint64_t>(p->staging);
@@ -285,6 +298,7 @@ extern "C" int ts_wpull_src_create(int device, const char* name, const void* src
   box->n_groups = groups;
   box->n_elems = uint64_t(n_elems);
   box->group_elems = ge;
+  for (int k = 0; k <= groups; ++k) box->bounds[k] = bounds[size_t(k)];
   box->dev_ptr = reinterpret_cast<uint64_t>(p->staging);
   std::memcpy(box->handle, handle, 64);
   box->offset = offset;
@@ -403,6 +417,8 @@ struct ts_wpull_dst {
   int device = 0;
   std::vector<Sender> senders;
   std::vector<Batch> batches;  // in group order
+  cudaStream_t side = nullptr;  // every other batch: a batch's drain overlaps the next
+  cudaEvent_t start = nullptr, side_done = nullptr;
   cudaEvent_t done = nullptr;
   std::thread acker;           // acknowledges the last pull once it finished
   uint64_t pulls = 0;
@@ -417,8 +433,12 @@ void dst_release(ts_wpull_dst* p) {
   if (p->acker.joinable()) p->acker.join();
   tsb::DeviceGuard g(p->device);
   if (p->done) cudaEventSynchronize(p->done);
+  if (p->side) cudaStreamSynchronize(p->side);
   for (auto& b : p->batches) free_launch(&b.launch);
   if (p->done) cudaEventDestroy(p->done);
+  if (p->start) cudaEventDestroy(p->start);
+  if (p->side_done) cudaEventDestroy(p->side_done);
+  if (p->side) cudaStreamDestroy(p->side);
   for (auto& s : p->senders) {
     if (s.box && s.slot >= 0) s.box->done[s.slot].store(kDetached, std::memory_order_release);
     if (s.ipc_base) ts_ipc_close(p->device, s.ipc_base);
@@ -522,8 +542,10 @@ extern "C" int ts_wpull_dst_create(int device, const char* const* names, int n_s
                         (long long)i, (unsigned long long)n, (long long)t);
     }
     const uint64_t end = uint64_t(c.src_off) + rows * uint64_t(c.src_stride) + uint64_t(c.size);
-    const int group = int(std::min<uint64_t>((end - 1) / box->group_elems,
-                                             uint64_t(box->n_groups - 1)));
+    // the group holding the last element read
+    const uint64_t* gb = box->bounds;
+    const int group =
+        int(std::upper_bound(gb + 1, gb + box->n_groups + 1, end - 1) - (gb + 1));
     c.src_ptr = p->senders[size_t(t)].staging;
     by_group[size_t(group)].push_back(c);
     auto& nd = need[size_t(group)];
@@ -544,10 +566,12 @@ extern "C" int ts_wpull_dst_create(int device, const char* const* names, int n_s
   }
   tsb::DeviceGuard g(device);
   cudaError_t ce = cudaEventCreateWithFlags(&p->done, cudaEventDisableTiming);
+  if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&p->start, cudaEventDisableTiming);
+  if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&p->side_done, cudaEventDisableTiming);
+  if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&p->side, cudaStreamNonBlocking);
   if (ce != cudaSuccess) {
-    p->done = nullptr;
     dst_release(p);
-    return tsb::cuda_error(ce, "pull event");
+    return tsb::cuda_error(ce, "pull events");
   }
   *out = p;
   return TS_OK;
@@ -562,6 +586,12 @@ extern "C" int ts_wpull_dst_pull(ts_wpull_dst* p, void* stream, int64_t timeout_
   const uint64_t k = ++p->pulls;
   tsb::DeviceGuard g(p->device);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // Batches alternate between the caller's stream and a side stream ordered
+  // after it (their destinations are disjoint): one batch's last CTAs drain
+  // while the next batch's start.
+  TS_CUDA_RET(cudaEventRecord(p->start, s), "event record");
+  TS_CUDA_RET(cudaStreamWaitEvent(p->side, p->start, 0), "stream wait");
+  size_t nb = 0;
   for (const auto& b : p->batches) {
     const bool ready = wait_until(
         [&] {
@@ -578,10 +608,13 @@ extern "C" int ts_wpull_dst_pull(ts_wpull_dst* p, void* stream, int64_t timeout_
                         "group %d of generation %llu not published within the timeout",
                         b.group, (unsigned long long)k);
     int rc = ts_reshard_copy(p->device, b.launch.d_chunks, b.launch.d_prefix, b.launch.n_chunks,
-                             b.launch.n_items, TS_DTYPE_BF16, TS_DTYPE_BF16, s);
+                             b.launch.n_items, TS_DTYPE_BF16, TS_DTYPE_BF16,
+                             (nb++ & 1) ? p->side : s);
     if (rc != TS_OK) return rc;
     ++p->launches;
   }
+  TS_CUDA_RET(cudaEventRecord(p->side_done, p->side), "event record");
+  TS_CUDA_RET(cudaStreamWaitEvent(s, p->side_done, 0), "stream wait");
   TS_CUDA_RET(cudaEventRecord(p->done, s), "event record");
   p->acker = std::thread([p, k] {
     cudaSetDevice(p->device);
