@@ -96,7 +96,7 @@ def parse():
   p.add_argument("--kernel-case", default="",
                  choices=["", "extract", "insert", "extract_fp8", "insert_fp8", "pool_reshard",
                           "insert_direct", "relayout", "manager_extract",
-                          "manager_insert"],
+                          "manager_insert", "reshard_cast", "reshard_copy"],
                  help="run a few launches of one kernel on a small case (for ncu)")
   return p.parse_args()
 
@@ -1676,6 +1676,42 @@ def run_kernel_case(args):
     print(json.dumps({"kernel_case": "relayout", "bytes": moved,
                       "ms": [round(x, 3) for x in ms],
                       "hbm_gbs": round(2 * moved / (min(ms) * 1e-3) / 1e9, 1)}))
+    return
+  if args.kernel_case in ("reshard_cast", "reshard_copy"):
+    # The weight-sync reshard kernel on trainer 0's chunks of the C4 4 -> 4
+    # plan for decoder layers 0-7 of Llama-3-8B (a 436 M-parameter FSDP
+    # slice of their 1.74 G), every destination on this GPU:
+    # reshard_cast = fp32 -> bf16 (the push kernel's arithmetic and the
+    # staged pull's sender cast), reshard_copy = bf16 -> bf16 (the staged
+    # pull's receiver copy).  4 launches, CUDA events.
+    from tpu_sync_b200 import reshard_plan as rp
+    params = [p for p in workloads.llama3_8b_params()
+              if p[0].startswith(tuple(f"layers.{i}." for i in range(8)))]
+    specs = workloads.weight_sync_specs(4, 4, params)
+    plan = rp.build_plan(specs)
+    layout = workloads.weight_sync_layout(specs, 4, 4)
+    cast = args.kernel_case == "reshard_cast"
+    sdt = torch.float32 if cast else torch.bfloat16
+    src = torch.empty(layout[0][0][1], dtype=sdt, device=device).normal_(0.0, 0.02)
+    dsts = {d: torch.empty(layout[1][d][1], dtype=torch.bfloat16, device=device)
+            for d in range(4)}
+    chunks = workloads.weight_sync_chunks(plan, layout, 0, src.data_ptr(),
+                                          {d: dsts[d].data_ptr() for d in range(4)},
+                                          src_itemsize=src.element_size())
+    prog = ops.ReshardProgram(chunks, sdt, torch.bfloat16, device)
+    elems = sum(c[4] * c[7] for c in chunks)
+    ms = []
+    for _ in range(4):
+      a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+      a.record()
+      prog.launch()
+      b.record()
+      torch.cuda.synchronize()
+      ms.append(a.elapsed_time(b))
+    moved = elems * (src.element_size() + 2)
+    print(json.dumps({"kernel_case": args.kernel_case, "chunks": len(chunks), "elements": elems,
+                      "bytes": moved, "ms": [round(x, 3) for x in ms],
+                      "hbm_gbs": round(moved / (min(ms) * 1e-3) / 1e9, 1)}))
     return
   if args.kernel_case == "insert_direct":
     # The insert kernel pulling 256 blocks (512 MiB) per launch from the
