@@ -128,3 +128,37 @@ def test_weight_sync_across_ranks(world):
   assert not alive, "ranks did not finish"
   assert not msgs, msgs
   assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+
+
+@pytest.mark.parametrize("n_src,n_dst", [(1, 1), (1, 2), (2, 1), (2, 2), (4, 4), (2, 4)])
+def test_staged_pull_chunks_cover_each_sampler_exactly_once(n_src, n_dst):
+  """The staged pull's receiver chunk lists (workloads.weight_sync_pull_chunks,
+  what bench.py hands to ops.PullReceiver): applied by the oracle from the
+  trainers' flat fp32 buffers (the staging holds their bf16 casts in the same
+  element layout), every element of a sampler's buffer is written exactly
+  once and equals its TP shards of the global tensors."""
+  specs = workloads.weight_sync_specs(n_src, n_dst, PARAMS)
+  plan = rp.build_plan(specs)
+  layout = workloads.weight_sync_layout(specs, n_src, n_dst)
+  full = _global_tensors()
+  flats = [torch.cat([_box(full[vi], rp.shard_boxes(v.shape, v.src_mesh)[v.src_box_of(s)])
+                      .reshape(-1) for vi, v in enumerate(specs)]).numpy()
+           for s in range(n_src)]
+  for d in range(n_dst):
+    chunks = workloads.weight_sync_pull_chunks(plan, layout, d, 0, n_src)
+    n = layout[1][d][1]
+    out = np.zeros(n, np.uint16)
+    cover = np.zeros(n, np.int64)
+    for s in range(n_src):
+      mine = [(so, dp // 2 + do, size, ss, ds, cnt)
+              for (t, dp, so, do, size, ss, ds, cnt) in chunks if t == s]
+      for (so, _, size, ss, _, cnt) in mine:  # inside the sender's staging
+        assert so + (cnt - 1) * ss + size <= layout[0][s][1]
+      ors.apply_element_chunks(flats[s], out, mine, cast_bf16=True)
+      for (_, do, size, _, ds, cnt) in mine:
+        for c in range(max(cnt, 1)):
+          cover[do + c * ds: do + c * ds + size] += 1
+    assert (cover == 1).all(), (d, np.unique(cover))
+    want = torch.cat([_box(full[vi], rp.shard_boxes(v.shape, v.dst_mesh)[v.dst_box_of(d)])
+                      .reshape(-1) for vi, v in enumerate(specs)]).to(torch.bfloat16)
+    np.testing.assert_array_equal(out, want.view(torch.int16).numpy().view(np.uint16))
