@@ -196,3 +196,108 @@ def test_block_handoff_across_gpus():
   prod.close()
   cons.close()
   run_cross_process(0, 1)
+
+
+def _pull_case(n_src, n_dst):
+  specs = workloads.weight_sync_specs(n_src, n_dst, small_params())
+  plan = rp.build_plan(specs)
+  layout = workloads.weight_sync_layout(specs, n_src, n_dst)
+  return specs, plan, layout
+
+
+def _pull_expected(plan, layout, flats, d, n_src):
+  out = np.zeros(layout[1][d][1], np.uint16)
+  chunks = workloads.weight_sync_pull_chunks(plan, layout, d, 0, n_src)
+  for s in range(n_src):
+    ors.apply_element_chunks(flats[s], out, [(so, dp // 2 + do, size, ss, ds, cnt)
+                                             for (t, dp, so, do, size, ss, ds, cnt) in chunks
+                                             if t == s], cast_bf16=True)
+  return out
+
+
+def test_staged_pull_across_gpus_in_process():
+  """Trainers' staging on cuda:0, samplers on cuda:1 reading it over NVLink
+  (peer pointers in one process), two generations, oracle-exact."""
+  two_gpus()
+  import os
+  specs, plan, layout = _pull_case(2, 2)
+  srcs = [torch.empty(layout[0][s][1], dtype=torch.float32, device="cuda:0") for s in range(2)]
+  senders = [ops.PullSender(f"tsb_multi_pull_{os.getpid()}_{s}", srcs[s], groups=4)
+             for s in range(2)]
+  dsts = [torch.zeros(layout[1][d][1], dtype=torch.bfloat16, device="cuda:1") for d in range(2)]
+  recv = [ops.PullReceiver([x.name for x in senders],
+                           workloads.weight_sync_pull_chunks(plan, layout, d, dsts[d].data_ptr(), 2),
+                           torch.device("cuda:1")) for d in range(2)]
+  try:
+    for gen in range(2):
+      g = torch.Generator().manual_seed(40 + gen)
+      flats = [(torch.randn(layout[0][s][1], generator=g) * 0.02).float() for s in range(2)]
+      for s in range(2):
+        srcs[s].copy_(flats[s])
+        senders[s].stage(torch.cuda.current_stream(0))
+      for r in recv:
+        r.pull(torch.cuda.current_stream(1))
+      torch.cuda.synchronize(0)
+      torch.cuda.synchronize(1)
+      for d in range(2):
+        got = dsts[d].view(torch.int16).cpu().numpy().view(np.uint16)
+        np.testing.assert_array_equal(got, _pull_expected(plan, layout,
+                                                          [f.numpy() for f in flats], d, 2))
+  finally:
+    for r in recv:
+      r.close()
+    for x in senders:
+      x.close()
+
+
+def _pull_sender_proc(mailbox, n, seed, q_ready, q_go):
+  import torch as t
+  from tpu_sync_b200 import ops as o
+  t.cuda.set_device(0)
+  g = t.Generator().manual_seed(seed)
+  src = (t.randn(n, generator=g) * 0.02).float().to("cuda:0")
+  snd = o.PullSender(mailbox, src, groups=5)
+  q_ready.put("READY")
+  assert q_go.get(timeout=120) == "GO"
+  snd.stage()
+  snd.wait()
+  q_ready.put("STAGED")
+  assert q_go.get(timeout=120) == "EXIT"
+  snd.close()
+  q_ready.put("BYE")
+
+
+def test_staged_pull_from_a_sender_process_on_the_other_gpu():
+  """Trainer process on cuda:0, sampler (this process) on cuda:1: the
+  staging crosses processes by CUDA IPC and GPUs over NVLink."""
+  two_gpus()
+  import os
+  specs, plan, layout = _pull_case(1, 1)
+  n = layout[0][0][1]
+  mailbox = f"tsb_multi_pullx_{os.getpid()}"
+  ctx = mp.get_context("spawn")
+  q_ready, q_go = ctx.Queue(), ctx.Queue()
+  p = ctx.Process(target=_pull_sender_proc, args=(mailbox, n, 91, q_ready, q_go))
+  p.start()
+  try:
+    assert q_ready.get(timeout=180) == "READY"
+    dst = torch.zeros(layout[1][0][1], dtype=torch.bfloat16, device="cuda:1")
+    rcv = ops.PullReceiver([mailbox], workloads.weight_sync_pull_chunks(plan, layout, 0,
+                                                                        dst.data_ptr(), 1),
+                           torch.device("cuda:1"))
+    q_go.put("GO")
+    rcv.pull(torch.cuda.current_stream(1), timeout_ms=60000)
+    torch.cuda.synchronize(1)
+    assert q_ready.get(timeout=120) == "STAGED"
+    g = torch.Generator().manual_seed(91)
+    flat = (torch.randn(n, generator=g) * 0.02).float().numpy()
+    np.testing.assert_array_equal(dst.view(torch.int16).cpu().numpy().view(np.uint16),
+                                  _pull_expected(plan, layout, [flat], 0, 1))
+    rcv.close()
+    q_go.put("EXIT")
+    assert q_ready.get(timeout=120) == "BYE"
+    p.join(timeout=60)
+  finally:
+    if p.is_alive():
+      p.kill()
+      p.join()
