@@ -1519,7 +1519,11 @@ def run_ours(args):
     roof["hbm_kernel"] = {"kernel": kern[n]["kernel"], "bound": "hbm",
                           "achieved": kern[n]["achieved_gbs"], "peak": hbm_peak,
                           "frac": round(kern[n]["achieved_gbs"] / hbm_peak, 3),
-                          "peak_source": peak_src}
+                          "peak_source": peak_src,
+                          "note": ("live, each launch timed from its start event: the "
+                                   "gather waits for SM slots that the reload's CTAs hold "
+                                   "while they wait on PCIe; the extract_hbm_gbs_one_launch "
+                                   "figure is a 512-block extract alone")}
   # ---- CPU baseline (rank 0, N=1) ----
   cpu = None
   if rank == 0 and world == 1 and not args.no_cpu_baseline:
