@@ -719,6 +719,10 @@ enum {
    * a full-SM grid of vector loads (plain copies of 16-byte aligned tables;
    * fp8 and direct-mode kernels are unchanged) */
   TS_SCHED_BULK_COPY = 8,
+  /* direct reloads read the mapped host tier with 32-byte (256-bit) vector
+   * loads instead of 16-byte ones (tables whose storages, slots and tier are
+   * all 32-byte aligned; others keep 16-byte vectors) */
+  TS_SCHED_WIDE_LOADS = 16,
 };
 
 /* Creates a manager over num_layers x num_shards storages (row-major

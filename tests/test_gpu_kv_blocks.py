@@ -238,6 +238,9 @@ MODES = [dict(mode="staged", copy_streams=1), dict(mode="staged", copy_streams=2
          dict(mode="direct_h2d", sched=("offload_priority", "reload_per_piece",
                                         "reload_overlap")),
          dict(mode="direct", sched=("reload_per_piece", "reload_overlap")),
+         dict(mode="direct", sched=("wide_loads",)),
+         dict(mode="direct_h2d", sched=("offload_priority", "reload_per_piece", "bulk_copy",
+                                        "wide_loads")),
          dict(mode="staged", sched=("offload_priority",)),
          dict(mode="staged", copy_streams=1, sched=("bulk_copy",)),
          dict(mode="direct_h2d", sched=("offload_priority", "reload_per_piece", "bulk_copy"))]

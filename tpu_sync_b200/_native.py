@@ -38,6 +38,7 @@ SCHED_OFFLOAD_PRIORITY = 1
 SCHED_RELOAD_PER_PIECE = 2
 SCHED_RELOAD_OVERLAP = 4
 SCHED_BULK_COPY = 8
+SCHED_WIDE_LOADS = 16
 
 STATUS_NAMES = {
     OK: "OK", CANCELLED: "CANCELLED", UNKNOWN: "UNKNOWN",

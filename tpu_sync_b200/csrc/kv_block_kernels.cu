@@ -135,6 +135,53 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// 32-byte vector path (sm_100 256-bit loads and stores): every address,
+// block size, slot offset and pitch is a multiple of 32 (checked on the host
+// before choosing this kernel); each thread moves two 32-byte vectors of a
+// 16 KiB piece, both loads before its stores.  Used for the direct reload,
+// whose loads read the mapped host tier over PCIe.
+__device__ __forceinline__ void ld_wide(const void* p, uint32_t (&r)[8]) {
+  asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "l"(p));
+}
+
+__device__ __forceinline__ void st_wide(void* p, const uint32_t (&r)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
+constexpr int kWidePerThread = int(kPieceBytes / 32 / kThreads);  // 2
+
+template <bool kToStaging, typename Ids>
+__global__ void __launch_bounds__(kThreads)
+    block_copy_wide_kernel(const ts_block_storage* __restrict__ st, int n_st,
+                           const __grid_constant__ Ids ids, int64_t n_blocks,
+                           uint8_t* staging, uint64_t pitch, uint32_t ppu,
+                           int* err_flag) {
+  const int64_t items = n_blocks * int64_t(n_st) * ppu;
+  for (int64_t w = blockIdx.x; w < items; w += gridDim.x) {
+    Unit u;
+    if (!resolve(st, n_st, ids, staging, pitch, ppu, w, err_flag, &u)) continue;
+    const uint8_t* src = kToStaging ? u.dev : u.stg;
+    uint8_t* dst = kToStaging ? u.stg : u.dev;
+    const int nvec = int(u.nbytes >> 5);
+    uint32_t v[kWidePerThread][8];
+#pragma unroll
+    for (int i = 0; i < kWidePerThread; ++i) {
+      const int idx = threadIdx.x + i * kThreads;
+      if (idx < nvec) ld_wide(src + (uint64_t(idx) << 5), v[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < kWidePerThread; ++i) {
+      const int idx = threadIdx.x + i * kThreads;
+      if (idx < nvec) st_wide(dst + (uint64_t(idx) << 5), v[i]);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Bulk-copy variant (HBM -> HBM only): each warp's lane 0 moves 16 KiB pieces
 // with the Blackwell bulk-copy engine, global -> shared (completion counted
@@ -664,7 +711,7 @@ template <bool kToStaging, typename Ids>
 int block_copy(int device, const ts_block_storage* d_st, int n_st,
                const Ids& d_ids, int64_t n_blocks, uint8_t* staging,
                uint64_t pitch, int* err_flag, void* stream, bool vec_ok,
-               uint64_t max_block_bytes, int max_ctas = 0, bool bulk = false) {
+               uint64_t max_block_bytes, int max_ctas = 0, int variant = kCopyVec) {
   if (n_blocks == 0 || n_st == 0) return TS_OK;
   const uint32_t ppu = uint32_t((max_block_bytes + kPieceBytes - 1) / kPieceBytes);
   if (ppu == 0) return TS_OK;
@@ -672,7 +719,7 @@ int block_copy(int device, const ts_block_storage* d_st, int n_st,
   DeviceGuard g(device);
   const int grid = launch_grid(device, items, max_ctas);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (bulk && vec_ok) {
+  if (variant == kCopyBulk && vec_ok) {
     // opt in to 192 KiB of dynamic shared memory (per device: set each launch)
     TS_CUDA_RET(cudaFuncSetAttribute(block_copy_bulk_kernel<kToStaging, Ids>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -683,6 +730,9 @@ int block_copy(int device, const ts_block_storage* d_st, int n_st,
     if (max_ctas > 0 && max_ctas < bgrid) bgrid = max_ctas;
     if (ctas < bgrid) bgrid = int(ctas);
     block_copy_bulk_kernel<kToStaging, Ids><<<bgrid, kBulkWarps * 32, kBulkSmem, s>>>(
+        d_st, n_st, d_ids, n_blocks, staging, pitch, ppu, err_flag);
+  } else if (variant == kCopyWide && vec_ok) {
+    block_copy_wide_kernel<kToStaging, Ids><<<grid, kThreads, 0, s>>>(
         d_st, n_st, d_ids, n_blocks, staging, pitch, ppu, err_flag);
   } else if (vec_ok) {
     block_copy_vec_kernel<kToStaging, Ids><<<grid, kThreads, 0, s>>>(
@@ -777,24 +827,24 @@ uint64_t fp8_block_bytes_hint(int n_st, uint64_t pitch, uint64_t scale_off) {
 int mgr_extract(int device, const ts_block_storage* d_st, int n_st,
                 const ParamIds& ids, int64_t n_blocks, void* staging,
                 uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
-                uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas, bool bulk) {
+                uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas, int variant) {
   if (fp8)
     return launch_extract_fp8(device, d_st, n_st, ids, n_blocks, staging, pitch,
                               scale_off, err_flag, s, max_bb, max_ctas, 0);
   return block_copy<true>(device, d_st, n_st, ids, n_blocks, static_cast<uint8_t*>(staging),
-                          pitch, err_flag, s, vec_ok, max_bb, max_ctas, bulk);
+                          pitch, err_flag, s, vec_ok, max_bb, max_ctas, variant);
 }
 
 int mgr_insert(int device, const ts_block_storage* d_st, int n_st,
                const ParamIds& ids, int64_t n_blocks, const void* staging,
                uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
-               uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas, bool bulk) {
+               uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas, int variant) {
   if (fp8)
     return launch_insert_fp8(device, d_st, n_st, ids, n_blocks, staging, pitch,
                              scale_off, err_flag, s, max_bb, max_ctas, 0);
   return block_copy<false>(device, d_st, n_st, ids, n_blocks,
                            static_cast<uint8_t*>(const_cast<void*>(staging)), pitch, err_flag,
-                           s, vec_ok, max_bb, max_ctas, bulk);
+                           s, vec_ok, max_bb, max_ctas, variant);
 }
 
 }  // namespace tsb

@@ -111,6 +111,7 @@ struct ts_manager {
 
   ts_block_storage* d_table = nullptr;
   bool vec_ok = true;
+  bool wide_ok = false;  // every storage, slot and the host tier 32-byte aligned
   uint64_t max_bb = 0;
   int64_t chunk_blocks = 64;
 
@@ -469,14 +470,16 @@ int launch_chunk(ts_manager* m, bool to_host, const ParamIds& ids, int64_t cn,
   const int ctas = !to_host && ids.direct && (m->sched & TS_SCHED_RELOAD_PER_PIECE) != 0
                        ? -1 : m->max_ctas;
   // bulk copies only between device buffers (staged chunks)
-  const bool bulk = !ids.direct && (m->sched & TS_SCHED_BULK_COPY) != 0;
+  const int variant = !ids.direct && (m->sched & TS_SCHED_BULK_COPY) != 0 ? kCopyBulk
+                      : ids.direct && m->wide_ok && (m->sched & TS_SCHED_WIDE_LOADS) != 0
+                          ? kCopyWide : kCopyVec;
   int rc = to_host
                ? mgr_extract(m->device, m->d_table, int(m->st.size()), ids, cn, staging,
                              m->host_pitch, err_dev, ks, m->vec_ok, m->max_bb, m->fp8,
-                             m->scale_off, m->max_ctas, bulk)
+                             m->scale_off, m->max_ctas, variant)
                : mgr_insert(m->device, m->d_table, int(m->st.size()), ids, cn, staging,
                             m->host_pitch, err_dev, ks, m->vec_ok, m->max_bb, m->fp8,
-                            m->scale_off, ctas, bulk);
+                            m->scale_off, ctas, variant);
   if (rc != TS_OK) return rc;
   if (m->profiling) {
     TS_CUDA_RET(cudaEventRecord(e1, ks), "event record");
@@ -993,7 +996,8 @@ extern "C" int ts_mgr_create(const ts_storage_desc* storages, int num_layers,
                                ? opts->reload_staged_every : 0;
   m->sched = opts ? opts->sched : 0;
   if (m->sched < 0 || m->sched > (TS_SCHED_OFFLOAD_PRIORITY | TS_SCHED_RELOAD_PER_PIECE |
-                                  TS_SCHED_RELOAD_OVERLAP | TS_SCHED_BULK_COPY)) {
+                                  TS_SCHED_RELOAD_OVERLAP | TS_SCHED_BULK_COPY |
+                                  TS_SCHED_WIDE_LOADS)) {
     delete m;
     return set_error(TS_INVALID_ARGUMENT, "sched must be a sum of TS_SCHED_* flags");
   }
@@ -1110,6 +1114,12 @@ extern "C" int ts_mgr_create(const ts_storage_desc* storages, int num_layers,
   }
   e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&m->host_dev), m->host, 0);
   if (e != cudaSuccess) return fail(tsb::cuda_error(e, "host tier mapping"));
+  // 32-byte vectors need every storage, slot, block size, the pitch and the
+  // mapped tier 32-byte aligned
+  m->wide_ok = m->vec_ok && !m->fp8 && m->host_pitch % 32 == 0 &&
+               reinterpret_cast<uintptr_t>(m->host_dev) % 32 == 0;
+  for (const auto& st : m->st)
+    m->wide_ok = m->wide_ok && st.dev_ptr % 32 == 0 && st.bb % 32 == 0 && st.host_off % 32 == 0;
   e = cudaHostAlloc(reinterpret_cast<void**>(&m->err_host), sizeof(int) * tsb::kErrWords,
                     cudaHostAllocMapped | cudaHostAllocPortable);
   if (e != cudaSuccess) return fail(tsb::cuda_error(e, "error words"));

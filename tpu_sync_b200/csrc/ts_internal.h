@@ -41,16 +41,19 @@ struct ParamIds {
 // Chunk launchers of kv_block_kernels.cu used by the manager.  max_ctas caps
 // the grid (0 = a full wave of every SM); max_ctas < 0 launches one CTA per
 // work item (16 KiB piece) instead of a persistent grid (plain copies only).
-// bulk selects the bulk-copy kernel for plain copies whose both sides are
-// device memory (ignored for fp8 and for unaligned tables).
+// variant picks the plain-copy kernel: kCopyVec (16-byte vectors), kCopyBulk
+// (the bulk-copy kernel, both sides device memory) or kCopyWide (32-byte
+// vectors, every address and size a multiple of 32); ignored for fp8, and
+// the byte kernel runs for tables that are not 16-byte aligned.
+enum CopyVariant : int { kCopyVec = 0, kCopyBulk = 1, kCopyWide = 2 };
 int mgr_extract(int device, const ts_block_storage* d_st, int n_st,
                 const ParamIds& ids, int64_t n_blocks, void* staging,
                 uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
-                uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas, bool bulk);
+                uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas, int variant);
 int mgr_insert(int device, const ts_block_storage* d_st, int n_st,
                const ParamIds& ids, int64_t n_blocks, const void* staging,
                uint64_t pitch, int* err_flag, cudaStream_t s, bool vec_ok,
-               uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas, bool bulk);
+               uint64_t max_bb, bool fp8, uint64_t scale_off, int max_ctas, int variant);
 
 // Strided byte runs for seg_copy (seg_copy.cu): row r of `count` rows of
 // `bytes` bytes goes from src + r*src_stride to dst + r*dst_stride.  src / dst

@@ -197,7 +197,8 @@ class KVCacheManager:
     flags = {"offload_priority": _native.SCHED_OFFLOAD_PRIORITY,
              "reload_per_piece": _native.SCHED_RELOAD_PER_PIECE,
              "reload_overlap": _native.SCHED_RELOAD_OVERLAP,
-             "bulk_copy": _native.SCHED_BULK_COPY}
+             "bulk_copy": _native.SCHED_BULK_COPY,
+             "wide_loads": _native.SCHED_WIDE_LOADS}
     if isinstance(sched, str):
       sched = (sched,)
     unknown = [f for f in sched if f not in flags]
