@@ -162,3 +162,43 @@ def test_staged_pull_chunks_cover_each_sampler_exactly_once(n_src, n_dst):
     want = torch.cat([_box(full[vi], rp.shard_boxes(v.shape, v.dst_mesh)[v.dst_box_of(d)])
                       .reshape(-1) for vi, v in enumerate(specs)]).to(torch.bfloat16)
     np.testing.assert_array_equal(out, want.view(torch.int16).numpy().view(np.uint16))
+
+
+@pytest.mark.parametrize("n", [2, 4])
+def test_hybrid_split_covers_each_sampler_exactly_once(n):
+  """The hybrid weight sync of bench.py (n -> n): sampler d pulls only what
+  trainer d holds for it (weight_sync_pull_chunks with src_slots={d}), and
+  every other trainer pushes its slices for d (weight_sync_chunks with
+  dst_slots={d}).  Together they write every element of d's buffer exactly
+  once, equal to its TP shards."""
+  specs = workloads.weight_sync_specs(n, n, PARAMS)
+  plan = rp.build_plan(specs)
+  layout = workloads.weight_sync_layout(specs, n, n)
+  full = _global_tensors()
+  flats = [torch.cat([_box(full[vi], rp.shard_boxes(v.shape, v.src_mesh)[v.src_box_of(s)])
+                      .reshape(-1) for vi, v in enumerate(specs)]).numpy() for s in range(n)]
+  for d in range(n):
+    size = layout[1][d][1]
+    out = np.zeros(size, np.uint16)
+    cover = np.zeros(size, np.int64)
+    parts = []
+    for (t, dp, so, do, sz, ss, ds, cnt) in workloads.weight_sync_pull_chunks(
+        plan, layout, d, 0, n, src_slots={d}):
+      assert t == d
+      parts.append((t, (so, dp // 2 + do, sz, ss, ds, cnt)))
+    for t in range(n):
+      if t == d:
+        continue
+      for (sp, dp, so, do, sz, ss, ds, cnt) in workloads.weight_sync_chunks(
+          plan, layout, t, 0, {e: e * DST_BASE for e in range(n)}, dst_slots={d}):
+        assert dp // DST_BASE == d
+        parts.append((t, (sp // 4 + so, (dp - d * DST_BASE) // 2 + do, sz, ss, ds, cnt)))
+    for t, c in parts:
+      ors.apply_element_chunks(flats[t], out, [c], cast_bf16=True)
+      so, do, sz, ss, ds, cnt = c
+      for r in range(max(cnt, 1)):
+        cover[do + r * ds: do + r * ds + sz] += 1
+    assert (cover == 1).all(), (d, np.unique(cover))
+    want = torch.cat([_box(full[vi], rp.shard_boxes(v.shape, v.dst_mesh)[v.dst_box_of(d)])
+                      .reshape(-1) for vi, v in enumerate(specs)]).to(torch.bfloat16)
+    np.testing.assert_array_equal(out, want.view(torch.int16).numpy().view(np.uint16))

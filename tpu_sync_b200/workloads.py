@@ -175,14 +175,17 @@ def weight_sync_layout(specs, n_src: int, n_dst: int):
 
 
 def weight_sync_chunks(plan, layout, src_slot: int, src_base: int, dst_bases,
-                       src_itemsize: int = 4, dst_itemsize: int = 2):
+                       src_itemsize: int = 4, dst_itemsize: int = 2, dst_slots=None):
   """One trainer slot's chunks over the flat buffers, in the form of
   ops.ReshardProgram: (src address, dst address, src element offset, dst
   element offset, size, src stride, dst stride, count), addresses being each
-  variable's start (`src_base` / `dst_bases[d]` plus its byte offset)."""
+  variable's start (`src_base` / `dst_bases[d]` plus its byte offset).
+  dst_slots: only the chunks into these sampler slots (None: all)."""
   src, dst = layout
   out = []
   for (vi, d), cs in plan.for_source(src_slot).items():
+    if dst_slots is not None and d not in dst_slots:
+      continue
     sp = src_base + src_itemsize * src[src_slot][0][vi]
     dp = dst_bases[d] + dst_itemsize * dst[d][0][vi]
     for (so, do, size, ss, ds, cnt) in cs:
@@ -191,13 +194,16 @@ def weight_sync_chunks(plan, layout, src_slot: int, src_base: int, dst_bases,
 
 
 def weight_sync_pull_chunks(plan, layout, dst_slot: int, dst_base: int, n_src: int,
-                            dst_itemsize: int = 2):
+                            dst_itemsize: int = 2, src_slots=None):
   """One sampler slot's chunks for the staged pull (ops.PullReceiver):
   (trainer slot, dst address, src element offset in that trainer's flat
-  buffer, dst element offset, size, src stride, dst stride, count)."""
+  buffer, dst element offset, size, src stride, dst stride, count).
+  src_slots: only the chunks from these trainer slots (None: all)."""
   src, dst = layout
   out = []
   for s in range(n_src):
+    if src_slots is not None and s not in src_slots:
+      continue
     for (vi, d), cs in plan.for_source(s).items():
       if d != dst_slot:
         continue
