@@ -700,77 +700,108 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
     dist.barrier()
   # Staged pull: each trainer casts into its bf16 staging group by group and
   # publishes the groups in a /dev/shm mailbox; each sampler's kernels read
-  # the staging over NVLink as the groups appear.  Timed per rank from one
-  # barrier over `steps` back-to-back pushes (a trainer's next stage waits
-  # for every sampler to finish the previous pull), max over ranks.
-  pull_ms, pull_error = 0.0, ""
+  # the staging over NVLink as the groups appear.  Hybrid (N >= 4): each
+  # sampler pulls only from its own-index trainer, and each trainer pushes
+  # its slices for the other samplers (the SM push kernel) while it casts, so
+  # every trainer has one reader and every sampler one source to read.
+  # Timed per rank from one barrier over `steps` back-to-back pushes (a
+  # trainer's next stage waits for its readers to finish the previous pull),
+  # max over ranks.
   token = [f"{os.getpid()}_{int(time.time() * 1e3) % 10**9}" if rank == 0 else None]
   dist.broadcast_object_list(token, src=0)
-  names = [f"tsb_bench_wpull_{token[0]}_{t_}" for t_ in range(half)]
-  sender = receiver = None
-  try:
-    if is_src:
-      sender = ops.PullSender(names[idx], flat, groups=16)
-  except RuntimeError as e:
-    pull_error = str(e).splitlines()[0][:200]
-  ok = torch.tensor([0 if pull_error else 1], dtype=torch.int32, device=device)
-  dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-  if int(ok.item()):
+
+  def staged_engine(kind):
+    names = [f"tsb_bench_w{kind}_{token[0]}_{t_}" for t_ in range(half)]
+    sender = receiver = cross = None
+    err, ms = "", 0.0
+    side = torch.cuda.Stream(device)
     try:
-      if not is_src:
-        receiver = ops.PullReceiver(
-            names, workloads.weight_sync_pull_chunks(plan, layout, idx, flat.data_ptr(), half),
-            device)
-    except RuntimeError as e:
-      pull_error = str(e).splitlines()[0][:200]
-    ok = torch.tensor([0 if pull_error else 1], dtype=torch.int32, device=device)
-    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-  if int(ok.item()):
-    def one_pull():
       if is_src:
-        sender.stage(timeout_ms=60000)
-      else:
-        receiver.pull(timeout_ms=60000)
-    try:
-      for _ in range(warmup):
-        one_pull()
-      torch.cuda.synchronize(device)
-      dist.barrier()
-      e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-      e0.record()
-      for _ in range(steps):
-        one_pull()
-      e1.record()
-      torch.cuda.synchronize(device)
-      pull_ms = e0.elapsed_time(e1) / steps
+        sender = ops.PullSender(names[idx], flat, groups=16)
+        if kind == "hybrid":
+          cross = ops.ReshardProgram(
+              workloads.weight_sync_chunks(plan, layout, idx, flat.data_ptr(),
+                                           {d: dsts[d].data_ptr() for d in range(half)},
+                                           dst_slots=set(range(half)) - {idx}),
+              torch.float32, torch.bfloat16, device)
     except RuntimeError as e:
-      pull_error = str(e).splitlines()[0][:200]
-      torch.cuda.synchronize(device)
-    ok = torch.tensor([0 if pull_error else 1], dtype=torch.int32, device=device)
-    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-    if not int(ok.item()) and not pull_error:
-      pull_error = "failed on another rank"
+      err = str(e).splitlines()[0][:200]
+    ok_ = torch.tensor([0 if err else 1], dtype=torch.int32, device=device)
+    dist.all_reduce(ok_, op=dist.ReduceOp.MIN)
+    if int(ok_.item()):
+      try:
+        if not is_src:
+          srcs_ = {idx} if kind == "hybrid" else None
+          pulls = workloads.weight_sync_pull_chunks(plan, layout, idx, flat.data_ptr(), half,
+                                                    src_slots=srcs_)
+          if kind == "hybrid":
+            receiver = ops.PullReceiver([names[idx]], [(0,) + tuple(c[1:]) for c in pulls],
+                                        device)
+          else:
+            receiver = ops.PullReceiver(names, pulls, device)
+      except RuntimeError as e:
+        err = str(e).splitlines()[0][:200]
+      ok_ = torch.tensor([0 if err else 1], dtype=torch.int32, device=device)
+      dist.all_reduce(ok_, op=dist.ReduceOp.MIN)
+    if int(ok_.item()):
+      def one_push():
+        if is_src:
+          if cross is not None:  # the cross slices go out while the trainer casts
+            side.wait_stream(torch.cuda.current_stream(device))
+            cross.launch(side)
+          sender.stage(timeout_ms=60000)
+          if cross is not None:
+            torch.cuda.current_stream(device).wait_stream(side)
+        else:
+          receiver.pull(timeout_ms=60000)
+      def pushes(n):
+        try:
+          for _ in range(n):
+            one_push()
+          torch.cuda.synchronize(device)
+          return ""
+        except RuntimeError as e:
+          torch.cuda.synchronize(device)
+          return str(e).splitlines()[0][:200]
+
+      # every rank takes the same collective steps, failed or not
+      err = pushes(warmup)
+      ok_ = torch.tensor([0 if err else 1], dtype=torch.int32, device=device)
+      dist.all_reduce(ok_, op=dist.ReduceOp.MIN)
+      if int(ok_.item()):
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        err = pushes(steps)
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1) / steps
+        ok_ = torch.tensor([0 if err else 1], dtype=torch.int32, device=device)
+        dist.all_reduce(ok_, op=dist.ReduceOp.MIN)
+      if not int(ok_.item()) and not err:
+        err = "failed on another rank"
+      dist.barrier()
+      if not is_src and not err:
+        mismatched[kind] = c4_shards_exact(torch, device, params, half, idx, flat)
+        flat.zero_()
+        torch.cuda.synchronize(device)
+    elif not err:
+      err = "failed on another rank"
+    if receiver is not None:
+      receiver.close()  # the samplers' mappings go before the trainers' staging
     dist.barrier()
-    if not is_src and not pull_error:
-      mismatched["pull"] = c4_shards_exact(torch, device, params, half, idx, flat)
-      flat.zero_()
-      torch.cuda.synchronize(device)
-  elif not pull_error:
-    pull_error = "failed on another rank"
-  if pull_error:
-    pull_ms = 0.0
-  if receiver is not None:
-    receiver.close()  # the samplers' mappings go before the trainers' staging
-  dist.barrier()
-  if sender is not None:
-    sender.close()
+    if sender is not None:
+      sender.close()
+    return (0.0 if err else ms), err
+
+  pull_ms, pull_error = staged_engine("pull")
+  hyb_ms, hyb_error = staged_engine("hybrid") if half >= 2 else (0.0, "")
   exact = torch.tensor([0 if any(mismatched.values()) else 1], dtype=torch.int32, device=device)
   dist.all_reduce(exact, op=dist.ReduceOp.MIN)
-  t = torch.tensor([per_push_ms, ce_ms, pull_ms], dtype=torch.float64, device=device)
+  t = torch.tensor([per_push_ms, ce_ms, pull_ms, hyb_ms], dtype=torch.float64, device=device)
   dist.all_reduce(t, op=dist.ReduceOp.MAX)
-  sm_s, ce_s, pull_s = (float(t[0].item()) / 1e3, float(t[1].item()) / 1e3,
-                        float(t[2].item()) / 1e3)
-  runs = {"sm": sm_s, "copy": ce_s, "pull": pull_s}
+  sm_s, ce_s, pull_s, hyb_s = (float(t[k].item()) / 1e3 for k in range(4))
+  runs = {"sm": sm_s, "copy": ce_s, "pull": pull_s, "hybrid": hyb_s}
   engine = min((k for k, v in runs.items() if v > 0), key=lambda k: runs[k])
   push_s = runs[engine]
   recv_bytes = max(2 * plan.elements_to(d) for d in range(half))
@@ -800,7 +831,13 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
                                       "(back-to-back pushes, each waiting for the previous "
                                       "pull to finish)",
                                "seconds": round(pull_s, 5) if not pull_error else None,
-                               **({"error": pull_error} if pull_error else {})}},
+                               **({"error": pull_error} if pull_error else {})},
+                      **({"hybrid": {
+                          "how": "each sampler pulls from its own-index trainer's staging "
+                                 "(as pull); each trainer pushes its slices for the other "
+                                 "samplers with the SM kernel while it casts",
+                          "seconds": round(hyb_s, 5) if not hyb_error else None,
+                          **({"error": hyb_error} if hyb_error else {})}} if half >= 2 else {})},
           "chunks_per_src": len(plan.for_source(0)),
           "exact": bool(int(exact.item())),
           "exact_how": ("every sampler's bf16 TP shards of all parameters, after each "

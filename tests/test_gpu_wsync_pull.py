@@ -233,3 +233,48 @@ def test_pull_from_a_sender_in_another_process(cuda):
     if p.poll() is None:
       p.kill()
       p.wait()
+
+
+def test_hybrid_pull_own_trainer_and_push_the_rest(cuda):
+  """bench.py's hybrid weight sync (2 -> 2) on one GPU: sampler d pulls only
+  from trainer d's staging, trainer t pushes its slices for the other
+  sampler with the SM kernel (fp32 -> bf16) while it casts; exact against
+  the oracle over two generations."""
+  n = 2
+  specs = workloads.weight_sync_specs(n, n, small_params())
+  plan = rp.build_plan(specs)
+  layout = workloads.weight_sync_layout(specs, n, n)
+  srcs = [torch.empty(layout[0][s][1], dtype=torch.float32, device=cuda) for s in range(n)]
+  dsts = [torch.zeros(layout[1][d][1], dtype=torch.bfloat16, device=cuda) for d in range(n)]
+  senders = [ops.PullSender(name("hyb", s), srcs[s], groups=6) for s in range(n)]
+  recv = [ops.PullReceiver([senders[d].name],
+                           [(0,) + tuple(c[1:]) for c in workloads.weight_sync_pull_chunks(
+                               plan, layout, d, dsts[d].data_ptr(), n, src_slots={d})], cuda)
+          for d in range(n)]
+  cross = [ops.ReshardProgram(workloads.weight_sync_chunks(
+      plan, layout, t, srcs[t].data_ptr(), {d: dsts[d].data_ptr() for d in range(n)},
+      dst_slots=set(range(n)) - {t}), torch.float32, torch.bfloat16, cuda) for t in range(n)]
+  side = torch.cuda.Stream(cuda)
+  try:
+    for gen in range(2):
+      flats = [trainer_flat(layout[0][s][1], 300 + 10 * gen + s) for s in range(n)]
+      for d in range(n):
+        dsts[d].zero_()
+      for t in range(n):
+        srcs[t].copy_(flats[t])
+        side.wait_stream(torch.cuda.current_stream(cuda))
+        cross[t].launch(side)
+        senders[t].stage()
+        torch.cuda.current_stream(cuda).wait_stream(side)
+      for r in recv:
+        r.pull()
+      torch.cuda.synchronize()
+      for d in range(n):
+        want = expected(plan, layout, [f.numpy() for f in flats], d, n)
+        got = dsts[d].view(torch.int16).cpu().numpy().view(np.uint16)
+        np.testing.assert_array_equal(got, want, err_msg=f"generation {gen}, sampler {d}")
+  finally:
+    for r in recv:
+      r.close()
+    for snd in senders:
+      snd.close()
