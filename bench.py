@@ -724,7 +724,7 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
                                            {d: dsts[d].data_ptr() for d in range(half)},
                                            dst_slots=set(range(half)) - {idx}),
               torch.float32, torch.bfloat16, device)
-    except RuntimeError as e:
+    except Exception as e:  # reported in the line, never ends the run
       err = str(e).splitlines()[0][:200]
     ok_ = torch.tensor([0 if err else 1], dtype=torch.int32, device=device)
     dist.all_reduce(ok_, op=dist.ReduceOp.MIN)
@@ -739,7 +739,7 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
                                         device)
           else:
             receiver = ops.PullReceiver(names, pulls, device)
-      except RuntimeError as e:
+      except Exception as e:  # reported in the line, never ends the run
         err = str(e).splitlines()[0][:200]
       ok_ = torch.tensor([0 if err else 1], dtype=torch.int32, device=device)
       dist.all_reduce(ok_, op=dist.ReduceOp.MIN)
@@ -760,7 +760,7 @@ def run_weight_sync(torch, dist, rank, world, device, steps, warmup):
             one_push()
           torch.cuda.synchronize(device)
           return ""
-        except RuntimeError as e:
+        except Exception as e:  # reported in the line, never ends the run
           torch.cuda.synchronize(device)
           return str(e).splitlines()[0][:200]
 
