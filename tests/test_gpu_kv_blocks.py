@@ -112,6 +112,14 @@ def test_manager_free_calls_queue_without_blocking(cuda):
   dst = [torch.empty_like(t) for t in pool]
   dtable = ops.StorageTable(dst)
   stream = torch.cuda.Stream(cuda)
+  # warm-up: the first launch of each kernel (the sleep kernel too) in a
+  # fresh process loads it (lazy module loading), which must not fall inside
+  # the window the sleep covers
+  ops.kv_extract(table, ids_a, sa, err_flag=err, stream=stream)
+  ops.kv_extract(ftable, ids_a, fa, err_flag=err, stream=stream)
+  ops.kv_insert(dtable, ids_a, sa, err_flag=err, stream=stream)
+  with torch.cuda.stream(stream):
+    torch.cuda._sleep(1000)
   torch.cuda.synchronize()
   with torch.cuda.stream(stream):
     torch.cuda._sleep(1_000_000_000)  # ~0.5 s at the B200's clocks

@@ -216,6 +216,11 @@ def test_push_queues_without_blocking(cuda):
   w = Wsync(src)
   assert w.register([entry(size=1 << 20)], [dest(dst[0][0])]) == _native.OK
   s = torch.cuda.Stream(cuda)
+  # warm-up (kernel loading in a fresh process), outside the slept window
+  assert w.push(s) == _native.OK and w.wait() == _native.OK
+  with torch.cuda.stream(s):
+    torch.cuda._sleep(1000)
+  dst[0][0].zero_()
   torch.cuda.synchronize()
   with torch.cuda.stream(s):
     torch.cuda._sleep(1_000_000_000)

@@ -200,7 +200,13 @@ def test_noalloc_offload_returns_without_waiting_for_the_device(cuda):
   table = host_table(pool, offs)
   stream = torch.cuda.Stream(cuda)
   src, dst = np.arange(40)[::-1].copy(), np.arange(40)
+  # warm-up (kernel loading in a fresh process), outside the slept window
+  rc = noalloc_offload(cuda, table, src, dst, host_buf, 4 * 4096, 64, stream)
+  assert rc == _native.OK, _native.last_error()
+  with torch.cuda.stream(stream):
+    torch.cuda._sleep(1000)
   torch.cuda.synchronize()
+  host_buf.zero_()
   with torch.cuda.stream(stream):
     torch.cuda._sleep(1_000_000_000)
   t0 = time.perf_counter()

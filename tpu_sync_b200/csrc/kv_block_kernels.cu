@@ -138,10 +138,11 @@ __global__ void __launch_bounds__(kThreads)
 // 32-byte vector path (sm_100 256-bit loads and stores): every address,
 // block size, slot offset and pitch is a multiple of 32 (checked on the host
 // before choosing this kernel); each thread moves two 32-byte vectors of a
-// 16 KiB piece, both loads before its stores.  Used for the direct reload,
-// whose loads read the mapped host tier over PCIe.
+// 16 KiB piece, both loads before its stores, the loads asking L2 to fetch
+// 256-byte spans (.L2::256B).  Used for the direct reload, whose loads read
+// the mapped host tier over PCIe.
 __device__ __forceinline__ void ld_wide(const void* p, uint32_t (&r)[8]) {
-  asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
                  "=r"(r[6]), "=r"(r[7])
                : "l"(p));
