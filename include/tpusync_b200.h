@@ -700,6 +700,12 @@ typedef struct ts_manager_opts {
                                   H2D mechanisms run at once */
   int32_t sched;               /* SM scheduling of the two directions, a sum of
                                   TS_SCHED_* flags (0 = neither) */
+  int32_t numa_node;           /* NUMA node of the host tier's pages: 0 = the
+                                  node of the device's PCI function (the
+                                  reference's DetectAndAssignNumaNode), n > 0 =
+                                  node n - 1 (its assigned_numa_node_override),
+                                  -1 = no placement.  Applied on hosts with
+                                  more than one node. */
 } ts_manager_opts;
 
 /* ts_manager_opts.sched flags. */
@@ -755,6 +761,16 @@ TS_API int ts_h2d(ts_manager* mgr, const int64_t* src, const int64_t* dst,
 TS_API int ts_mgr_host_block_ptr(ts_manager* mgr, int64_t layer_idx, int64_t shard_idx,
                           int64_t block_id, uint64_t* ptr_out,
                           uint64_t* bytes_out);
+/* RaidenManagerBase::assigned_numa_node (tpu_sync/core/raiden_manager_base.h:102):
+ * the node assigned to the manager (-1 = none known) and whether the host
+ * tier's pages were placed on it (0 on single-node hosts, or when the kernel
+ * refused the memory policy). */
+TS_API int ts_mgr_numa_node(ts_manager* mgr, int* node, int* placed);
+/* The NUMA node sysfs lists for a PCI bus id ("0000:1b:00.0" or CUDA's
+ * 8-digit-domain form), -1 when unknown; sysfs_root NULL = "/sys".  Host
+ * logic of GetPjRtDeviceNumaNode's role in DetectAndAssignNumaNode
+ * (tpu_sync/core/raiden_manager_base.cc:47-78); no CUDA call. */
+TS_API int ts_pci_numa_node(const char* bus_id, const char* sysfs_root, int* node);
 TS_API int ts_mgr_info(ts_manager* mgr, int64_t* host_blocks, uint64_t* host_block_pitch,
                 int64_t* major_dim, uint64_t* bytes_per_block);
 

@@ -115,3 +115,32 @@ def test_host_tier_anonymous_and_shm(tmp_path):
                                         ctypes.byref(warm)))
   assert warm.value == 0
   lib.ts_host_tier_destroy(t, 1)
+
+
+def test_pci_numa_node_reads_sysfs(tmp_path):
+  """ts_pci_numa_node: the node sysfs lists for a PCI function, from CUDA's
+  8-digit-domain bus id or sysfs's own form, case-insensitive; -1 when the
+  device, or its node, is unknown (DetectAndAssignNumaNode keeps no node
+  then, raiden_manager_base.cc:47-78)."""
+  import ctypes
+  dev = tmp_path / "bus" / "pci" / "devices"
+  for bus, node in (("0000:1b:00.0", "1\n"), ("0000:9a:00.0", "-1\n"), ("0000:c3:00.0", "0")):
+    (dev / bus).mkdir(parents=True)
+    (dev / bus / "numa_node").write_text(node)
+  root = str(tmp_path).encode()
+  out = ctypes.c_int(7)
+  for bus, want in ((b"00000000:1B:00.0", 1), (b"0000:1b:00.0", 1), (b"0000:9A:00.0", -1),
+                    (b"00000000:C3:00.0", 0), (b"0000:ff:00.0", -1)):
+    assert _native.lib().ts_pci_numa_node(bus, root, ctypes.byref(out)) == _native.OK
+    assert out.value == want, bus
+  assert _native.lib().ts_pci_numa_node(None, root, ctypes.byref(out)) == _native.INVALID_ARGUMENT
+
+
+def test_numa_option_of_the_manager():
+  from tpu_sync_b200.kv_cache_manager import _numa_opt
+  assert _numa_opt(None) == 0 and _numa_opt("none") == -1
+  assert _numa_opt(0) == 1 and _numa_opt(3) == 4
+  with pytest.raises(ValueError):
+    _numa_opt(-2)
+  with pytest.raises(ValueError):
+    _numa_opt("local")

@@ -345,6 +345,29 @@ def test_manager_repeated_destination_within_one_chunk(cuda, mode):
   assert_same(pool, mgr, model, range(64))
 
 
+@pytest.mark.parametrize("numa", [None, 0, "none"])
+def test_manager_numa_node_option(cuda, numa):
+  """The manager's NUMA node: the device's own by default (the reference's
+  DetectAndAssignNumaNode), a caller's override, or none; the host tier is
+  allocated under that placement and the round trip stays exact."""
+  geom = workloads.KVGeometry(layers=2, kv=2, block_tokens=16, heads=2, head_dim=128)
+  pool, mgr, model = make_pair(geom, 32, 16, 41, cuda, numa_node=numa)
+  if numa == 0:
+    assert mgr.assigned_numa_node == 0
+  elif numa == "none":
+    assert mgr.assigned_numa_node is None and not mgr.host_tier_numa_placed
+  else:
+    assert mgr.assigned_numa_node is None or mgr.assigned_numa_node >= 0
+  assert isinstance(mgr.host_tier_numa_placed, bool)
+  mgr.d2h(list(range(10)), list(range(10))).Await()
+  model.d2h(list(range(10)), list(range(10)))
+  mgr.h2d(list(range(10)), list(range(20, 30))).Await()
+  model.h2d(list(range(10)), list(range(20, 30)))
+  torch.cuda.synchronize()
+  assert_same(pool, mgr, model, range(16))
+  mgr.close()
+
+
 @pytest.mark.parametrize("mode", MODES)
 def test_manager_back_to_back_calls_are_ordered(cuda, mode):
   """Offload then reload of the same host blocks without waiting in between."""

@@ -107,7 +107,8 @@ class ManagerOpts(ctypes.Structure):
               ("shm_name", ctypes.c_char_p), ("model_uid", ctypes.c_char_p),
               ("fp8", ctypes.c_int32), ("mode", ctypes.c_int32),
               ("copy_streams", ctypes.c_int32), ("max_ctas", ctypes.c_int32),
-              ("reload_staged_every", ctypes.c_int32), ("sched", ctypes.c_int32)]
+              ("reload_staged_every", ctypes.c_int32), ("sched", ctypes.c_int32),
+              ("numa_node", ctypes.c_int32)]
 
 
 class BlockInfo(ctypes.Structure):
@@ -374,6 +375,10 @@ _SIGS = {
     "ts_reshard_ce_launch": (ctypes.c_int, [_V, _V]),
     "ts_reshard_ce_info": (ctypes.c_int, [_V, c_i64_p, c_u64_p, c_i64_p]),
     "ts_reshard_ce_destroy": (ctypes.c_int, [_V]),
+    "ts_mgr_numa_node": (ctypes.c_int, [_V, ctypes.POINTER(ctypes.c_int),
+                                        ctypes.POINTER(ctypes.c_int)]),
+    "ts_pci_numa_node": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p,
+                                        ctypes.POINTER(ctypes.c_int)]),
     "ts_wpull_src_create": (ctypes.c_int, [ctypes.c_int, ctypes.c_char_p, _V, ctypes.c_int64,
                                            ctypes.c_int, ctypes.POINTER(_V)]),
     "ts_wpull_src_stage": (ctypes.c_int, [_V, _V, ctypes.c_int64]),

@@ -112,6 +112,8 @@ struct ts_manager {
   ts_block_storage* d_table = nullptr;
   bool vec_ok = true;
   bool wide_ok = false;  // every storage, slot and the host tier 32-byte aligned
+  int numa_node = -1;    // assigned NUMA node (-1: none known)
+  bool numa_placed = false;
   uint64_t max_bb = 0;
   int64_t chunk_blocks = 64;
 
@@ -1060,8 +1062,20 @@ extern "C" int ts_mgr_create(const ts_storage_desc* storages, int num_layers,
   const char* uid = opts && opts->model_uid ? opts->model_uid : "";
   uint64_t geometry = m->host_pitch * 1000003ull ^ uint64_t(n) * 7919ull ^ (m->fp8 ? 1 : 0);
   int warm = 0;
-  rc = ts_host_tier_create(uint64_t(m->host_blocks) * m->host_pitch, shm, uid, geometry, 1,
-                           &m->tier, &warm);
+  // NUMA node of the host tier: the device's own (DetectAndAssignNumaNode,
+  // raiden_manager_base.cc:47-78) unless the caller overrides it
+  // (kv_cache_manager_base.cc:231-249); pages are placed there while the
+  // tier is allocated and pinned, on hosts with more than one node.
+  const int numa_opt = opts ? opts->numa_node : 0;
+  m->numa_node = numa_opt > 0 ? numa_opt - 1 : numa_opt == 0 ? tsb::device_numa_node(m->device)
+                                                             : -1;
+  {
+    const bool place = m->numa_node >= 0 && tsb::numa_node_count(nullptr) > 1;
+    tsb::ScopedPreferredNode policy(place ? m->numa_node : -1);
+    m->numa_placed = policy.applied();
+    rc = ts_host_tier_create(uint64_t(m->host_blocks) * m->host_pitch, shm, uid, geometry, 1,
+                             &m->tier, &warm);
+  }
   if (rc != TS_OK) return fail(rc);
   m->host = static_cast<uint8_t*>(ts_host_tier_ptr(m->tier));
   if (!warm && (shm == nullptr || shm[0] == '\0')) {
@@ -1179,6 +1193,14 @@ extern "C" int ts_mgr_host_block_ptr(ts_manager* mgr, int64_t layer_idx, int64_t
     *ptr_out = reinterpret_cast<uint64_t>(mgr->host + uint64_t(block_id) * mgr->host_pitch +
                                           s.host_off);
   if (bytes_out) *bytes_out = s.host_bytes;
+  return TS_OK;
+}
+
+extern "C" int ts_mgr_numa_node(ts_manager* mgr, int* node, int* placed) {
+  tsb::clear_error();
+  if (!mgr) return set_error(TS_INVALID_ARGUMENT, "null manager");
+  if (node) *node = mgr->numa_node;
+  if (placed) *placed = mgr->numa_placed ? 1 : 0;
   return TS_OK;
 }
 

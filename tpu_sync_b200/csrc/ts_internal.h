@@ -70,6 +70,32 @@ struct SegTask {
 constexpr int kMaxSegTasks = 512;  // tasks per launch (kernel parameters)
 int seg_copy(int device, const SegTask* tasks, int64_t n, cudaStream_t s, int max_ctas);
 
+// NUMA placement (numa.cu).  pci_numa_node: the node sysfs lists for a PCI
+// bus id (CUDA's "00000000:1b:00.0" or "0000:1b:00.0"), -1 when unknown;
+// sysfs_root NULL = "/sys".  numa_node_count: nodes under
+// <root>/devices/system/node (1 when unreadable).  device_numa_node: the
+// node of a CUDA device's PCI function.
+int pci_numa_node(const char* bus_id, const char* sysfs_root);
+int numa_node_count(const char* sysfs_root);
+int device_numa_node(int device);
+
+// While alive, the calling thread's memory policy prefers `node` (pages it
+// faults in, including those a cudaHostAlloc / cudaHostRegister pins, come
+// from that node when it has room); the previous policy is restored after.
+// applied() is false when the kernel refused the policy.
+class ScopedPreferredNode {
+ public:
+  explicit ScopedPreferredNode(int node);
+  ~ScopedPreferredNode();
+  bool applied() const { return applied_; }
+
+ private:
+  static constexpr int kMaskWords = 16;
+  bool applied_ = false;
+  int prev_mode_ = 0;
+  unsigned long prev_mask_[kMaskWords] = {0};
+};
+
 // Scoped switch of the current CUDA device.
 class DeviceGuard {
  public:

@@ -41,6 +41,21 @@ def _stream(stream: Optional["torch.cuda.Stream"], device) -> ctypes.c_void_p:
   return ctypes.c_void_p(s.cuda_stream)
 
 
+def _numa_opt(numa_node) -> int:
+  """ts_manager_opts.numa_node from the Python argument: None = the device's
+  own node (the reference's detection), an int n >= 0 = node n (its
+  assigned_numa_node_override), "none" = no placement."""
+  if numa_node is None:
+    return 0
+  if isinstance(numa_node, str):
+    if numa_node != "none":
+      raise ValueError(f"numa_node must be None, a node number or 'none', got {numa_node!r}")
+    return -1
+  if int(numa_node) < 0:
+    raise ValueError(f"numa_node must be >= 0, got {numa_node}")
+  return int(numa_node) + 1
+
+
 def _storage_grid(kv_caches) -> List[List[torch.Tensor]]:
   if isinstance(kv_caches, torch.Tensor):
     raise TypeError("kv_caches must be a list of tensors or a list of lists")
@@ -156,6 +171,7 @@ class KVCacheManager:
       max_ctas: int = 0,
       reload_staged_every: int = 0,
       sched: Sequence[str] = (),
+      numa_node: Any = None,
   ):
     if host_blocks_to_allocate is None:
       if max_blocks is None or num_slots is None:
@@ -209,7 +225,7 @@ class KVCacheManager:
         shm_name=shm_name.encode(), model_uid=model_uid.encode(), fp8=int(fp8),
         mode=modes[mode], copy_streams=int(copy_streams),
         max_ctas=int(max_ctas), reload_staged_every=int(reload_staged_every),
-        sched=sum(flags[f] for f in set(sched)))
+        sched=sum(flags[f] for f in set(sched)), numa_node=_numa_opt(numa_node))
     handle = ctypes.c_void_p()
     rc = _native.lib().ts_mgr_create(descs, self.num_layers, self.num_shards,
                                      ctypes.byref(opts), ctypes.byref(handle))
@@ -233,6 +249,26 @@ class KVCacheManager:
   @property
   def node_id(self) -> int:
     return self._node_id
+
+  @property
+  def assigned_numa_node(self) -> Optional[int]:
+    """The NUMA node assigned to this manager (RaidenManagerBase::
+    assigned_numa_node, raiden_manager_base.h:102): the device's own unless
+    `numa_node` overrode it; None when unknown."""
+    node, _ = self._numa()
+    return None if node < 0 else node
+
+  @property
+  def host_tier_numa_placed(self) -> bool:
+    """Whether the host tier's pages were placed on the assigned node
+    (False on single-node hosts, or when the kernel refused the policy)."""
+    return self._numa()[1]
+
+  def _numa(self):
+    node, placed = ctypes.c_int(), ctypes.c_int()
+    _native.check(_native.lib().ts_mgr_numa_node(self._mgr, ctypes.byref(node),
+                                                  ctypes.byref(placed)))
+    return node.value, bool(placed.value)
 
   @property
   def local_port(self) -> Optional[int]:
