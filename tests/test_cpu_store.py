@@ -333,3 +333,40 @@ def test_trace_decisions_under_eviction_match_reference_store(seed, host_blocks,
   prod, prod_stats = workloads.store_transfer_streams(trace, host_blocks, pool, batch)
   assert ref_stats == prod_stats
   _same_streams(ref, prod)
+
+
+def test_bench_c1_exactness_model_matches_an_in_order_replay():
+  """bench.py's full-size C1 check names, for every reloaded pool block, the
+  pool block whose bytes it must hold (c1_seed_host_blocks /
+  c1_expected_sources).  Replayed here call by call on a toy pool whose
+  blocks hold their own ids (offloads of a step before its reloads, the
+  last copy to a block winning, as the manager orders them), the same
+  steps leave exactly those ids."""
+  import sys
+  from pathlib import Path
+  sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+  import bench
+  rng = np.random.default_rng(4)
+  half, host_blocks, steps = 64, 96, 9
+  plans = []
+  for _ in range(steps):
+    n_off, n_ld = int(rng.integers(0, 20)), int(rng.integers(1, 30))
+    plans.append((rng.integers(0, half, n_off), rng.choice(host_blocks, n_off, replace=False),
+                   rng.integers(0, host_blocks, n_ld), half + rng.integers(0, half, n_ld)))
+  executed = list(range(steps)) + list(range(3, steps))
+  seed = bench.c1_seed_host_blocks(plans, executed, half)
+  dev = np.arange(2 * half)              # block d holds the bytes of block d
+  host = np.full(host_blocks, -1)        # unknown content
+  for h, d in seed.items():              # the untimed seeding offload
+    host[h] = dev[d]
+  for i in executed:
+    off_d, off_h, ld_h, ld_d = plans[i]
+    for d, h in zip(off_d, off_h):
+      host[h] = dev[d]
+    for h, d in zip(ld_h, ld_d):
+      dev[d] = host[h]
+  expected = bench.c1_expected_sources(plans, executed, seed)
+  reloaded = {int(d) for i in executed for d in plans[i][3]}
+  assert set(expected) == reloaded       # seeding leaves no reload unknown
+  for d, s in expected.items():
+    assert dev[d] == s, (d, s, dev[d])
