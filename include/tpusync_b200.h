@@ -502,7 +502,9 @@ TS_API int ts_reshard_ce_destroy(ts_reshard_ce* program);
  * soon as it is written; before overwriting the staging it waits, at most
  * `timeout_ms`, until every receiver that attached has finished pulling the
  * previous generation (TS_DEADLINE_EXCEEDED otherwise, nothing queued).
- * wait() returns once every group of the last stage() is published. */
+ * wait() returns once every group of the last stage() is published.
+ * destroy() waits up to 2 s for attached receivers to detach before it
+ * frees the staging; destroy the receivers first. */
 typedef struct ts_wpull_src ts_wpull_src;
 TS_API int ts_wpull_src_create(int device, const char* name, const void* src_f32,
                                int64_t n_elems, int n_groups, ts_wpull_src** out);

@@ -176,6 +176,21 @@ void src_join(ts_wpull_src* p) {
 
 void src_release(ts_wpull_src* p) {
   src_join(p);
+  if (p->box) {
+    // Receivers in other processes map the staging: give them a moment to
+    // detach (ts_wpull_dst_destroy) before it is freed.
+    tsb::wpull::Box* box = p->box;
+    tsb::wpull::wait_until(
+        [&] {
+          const int n = std::min(box->n_receivers.load(std::memory_order_acquire),
+                                 tsb::wpull::kMaxReceivers);
+          for (int r = 0; r < n; ++r)
+            if (box->done[r].load(std::memory_order_acquire) != tsb::wpull::kDetached)
+              return false;
+          return true;
+        },
+        tsb::wpull::deadline_in(2000));
+  }
   {
     tsb::DeviceGuard g(p->device);
     if (p->stream) cudaStreamSynchronize(p->stream);
